@@ -1,0 +1,458 @@
+// extern "C" entry points of libdp_gbdt (declared in include/dp_gbdt.h).
+#include "../../include/dp_gbdt.h"
+
+#include <cuda_runtime.h>
+
+#include <cstring>
+#include <fstream>
+#include <memory>
+#include <sstream>
+#include <string>
+#include <vector>
+
+#include "booster.h"
+#include "comm.h"
+#include "dmatrix.h"
+#include "json.h"
+#include "kernels.h"
+#include "quantile.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+#define DP_API_BEGIN() try {
+#define DP_API_END()                         \
+  }                                          \
+  catch (const std::exception& e) {          \
+    g_last_error = e.what();                 \
+    return -1;                               \
+  }                                          \
+  catch (...) {                              \
+    g_last_error = "unknown error";          \
+    return -1;                               \
+  }                                          \
+  return 0;
+
+using dp::need;
+
+struct ArrayInterface {
+  std::uintptr_t ptr = 0;
+  std::vector<dp::u64> shape;
+  std::vector<dp::i64> strides;  // bytes; empty = C-contiguous
+  std::string typestr;
+};
+
+ArrayInterface parse_array(const char* text) {
+  need(text != nullptr, "array interface string is null");
+  dp::json::Value v = dp::json::parse(text);
+  if (v.is_array()) {
+    need(v.size() == 1, "only one array interface (one column batch) is supported");
+    v = dp::json::Value(v[0]);
+  }
+  need(v.is_object(), "array interface must be a JSON object");
+  ArrayInterface a;
+  const auto& data = v.at("data");
+  need(data.is_array() && data.size() >= 1, "array interface data must be [pointer, read_only]");
+  a.ptr = std::uintptr_t(data[0].as_uint());
+  for (const auto& s : v.at("shape").items()) a.shape.push_back(s.as_uint());
+  if (const auto* st = v.find("strides"))
+    if (!st->is_null())
+      for (const auto& s : st->items()) a.strides.push_back(s.as_int());
+  a.typestr = v.at("typestr").as_string();
+  if (const auto* m = v.find("mask")) need(m->is_null(), "masked arrays are not supported");
+  return a;
+}
+
+int pointer_device(const void* p, bool allow_host) {
+  cudaPointerAttributes attr{};
+  dp::cuda_check(cudaPointerGetAttributes(&attr, p), "cudaPointerGetAttributes");
+  if (attr.type == cudaMemoryTypeDevice || attr.type == cudaMemoryTypeManaged) return attr.device;
+  need(allow_host, "array memory must be CUDA device memory");
+  int dev = 0;
+  dp::cuda_check(cudaGetDevice(&dev), "cudaGetDevice");
+  return dev;
+}
+
+dp::DMatrix* as_dmatrix(void* h) {
+  need(h != nullptr, "DMatrix handle is null");
+  return static_cast<dp::DMatrix*>(h);
+}
+dp::Booster* as_booster(void* h) {
+  need(h != nullptr, "Booster handle is null");
+  return static_cast<dp::Booster*>(h);
+}
+
+std::string read_file(const char* path) {
+  std::ifstream f(path, std::ios::binary);
+  need(bool(f), std::string("cannot read ") + path);
+  std::ostringstream s;
+  s << f.rdbuf();
+  return s.str();
+}
+
+bool ends_with(const std::string& s, const std::string& suf) {
+  return s.size() >= suf.size() && s.compare(s.size() - suf.size(), suf.size(), suf) == 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+void XGBoostVersion(int* major, int* minor, int* patch) {
+  if (major) *major = 3;
+  if (minor) *minor = 4;
+  if (patch) *patch = 1;
+}
+
+int XGBuildInfo(const char** out) {
+  static const char* info =
+      "{\"USE_CUDA\":true,\"USE_NCCL\":true,\"USE_OPENMP\":false,\"CUDA_VERSION\":[12,9],"
+      "\"GPU_ARCH\":\"sm_100a\",\"DP_B200_GBDT\":true}";
+  if (out) *out = info;
+  return 0;
+}
+
+const char* XGBGetLastError(void) { return g_last_error.c_str(); }
+
+int XGDMatrixCreateFromCudaArrayInterface(const char* data, const char* config, DMatrixHandle* out) {
+  DP_API_BEGIN();
+  need(out != nullptr, "output handle pointer is null");
+  const ArrayInterface a = parse_array(data);
+  need(a.typestr == "<f4", "only little-endian float32 (<f4) matrices are supported");
+  need(a.shape.size() == 2, "matrix array interface must be two-dimensional");
+  const dp::u64 rows = a.shape[0], cols = a.shape[1];
+  need(cols > 0 && cols <= 0x7fffffffULL, "matrix column count out of range");
+  dp::u64 stride = cols;
+  if (!a.strides.empty()) {
+    need(a.strides.size() == 2 && a.strides[1] == 4 && a.strides[0] > 0 && a.strides[0] % 4 == 0,
+         "matrix strides must be row-major with 4-byte elements");
+    stride = dp::u64(a.strides[0]) / 4;
+  }
+  bool has_mv = false;
+  float mv = 0.f;
+  if (config && *config) {
+    const dp::json::Value c = dp::json::parse(config);
+    if (const auto* m = c.find("missing")) {
+      const double d = m->as_double();
+      if (!std::isnan(d)) { has_mv = true; mv = float(d); }
+    }
+  }
+  need(rows == 0 || a.ptr != 0, "matrix data pointer is null");
+  const int dev = rows ? pointer_device(reinterpret_cast<const void*>(a.ptr), false) : 0;
+  {
+    dp::DeviceGuard g(dev);
+    // the producer may still be writing on its own stream
+    dp::cuda_check(cudaDeviceSynchronize(), "synchronise producer");
+  }
+  auto d = std::make_unique<dp::DMatrix>(reinterpret_cast<const float*>(a.ptr), rows, dp::u32(cols), stride, dev,
+                                         has_mv, mv);
+  *out = d.release();
+  DP_API_END();
+}
+
+int XGDMatrixSetInfoFromInterface(DMatrixHandle handle, const char* field, const char* data) {
+  DP_API_BEGIN();
+  dp::DMatrix* d = as_dmatrix(handle);
+  need(field != nullptr && std::string(field) == "label", "only the \"label\" field is supported");
+  const ArrayInterface a = parse_array(data);
+  need(a.typestr == "<f4", "labels must be little-endian float32 (<f4)");
+  need(a.shape.size() == 1 || (a.shape.size() == 2 && a.shape[1] == 1), "labels must be a vector");
+  need(a.strides.empty() || a.strides.back() == 4, "labels must be contiguous");
+  need(a.shape[0] == 0 || a.ptr != 0, "label pointer is null");
+  {
+    dp::DeviceGuard g(d->device());
+    dp::cuda_check(cudaDeviceSynchronize(), "synchronise producer");
+  }
+  d->set_labels_device(reinterpret_cast<const float*>(a.ptr), a.shape[0]);
+  DP_API_END();
+}
+
+int XGDMatrixSetFloatInfo(DMatrixHandle handle, const char* field, const float* data, bst_ulong len) {
+  DP_API_BEGIN();
+  dp::DMatrix* d = as_dmatrix(handle);
+  need(field != nullptr && std::string(field) == "label", "only the \"label\" field is supported");
+  need(len == 0 || data != nullptr, "label pointer is null");
+  d->set_labels_host(data, len);
+  DP_API_END();
+}
+
+int XGDMatrixNumRow(DMatrixHandle handle, bst_ulong* out) {
+  DP_API_BEGIN();
+  *out = as_dmatrix(handle)->rows();
+  DP_API_END();
+}
+
+int XGDMatrixNumCol(DMatrixHandle handle, bst_ulong* out) {
+  DP_API_BEGIN();
+  *out = as_dmatrix(handle)->cols();
+  DP_API_END();
+}
+
+int XGDMatrixFree(DMatrixHandle handle) {
+  DP_API_BEGIN();
+  delete static_cast<dp::DMatrix*>(handle);
+  DP_API_END();
+}
+
+int XGBoosterCreate(const DMatrixHandle dmats[], bst_ulong len, BoosterHandle* out) {
+  DP_API_BEGIN();
+  need(out != nullptr, "output handle pointer is null");
+  need(len == 0 || dmats != nullptr, "matrix list is null");
+  for (bst_ulong i = 0; i < len; ++i) need(dmats[i] != nullptr, "matrix handle is null");
+  *out = new dp::Booster();
+  DP_API_END();
+}
+
+int XGBoosterFree(BoosterHandle handle) {
+  DP_API_BEGIN();
+  delete static_cast<dp::Booster*>(handle);
+  DP_API_END();
+}
+
+int XGBoosterSetParam(BoosterHandle handle, const char* name, const char* value) {
+  DP_API_BEGIN();
+  need(name != nullptr && value != nullptr, "parameter name / value is null");
+  as_booster(handle)->set_param(name, value);
+  DP_API_END();
+}
+
+int XGBoosterUpdateOneIter(BoosterHandle handle, int iter, DMatrixHandle dtrain) {
+  DP_API_BEGIN();
+  as_booster(handle)->update_one_iter(iter, as_dmatrix(dtrain));
+  DP_API_END();
+}
+
+int XGBoosterBoostedRounds(BoosterHandle handle, int* out) {
+  DP_API_BEGIN();
+  need(out != nullptr, "output pointer is null");
+  *out = as_booster(handle)->boosted_rounds();
+  DP_API_END();
+}
+
+int XGBoosterSaveJsonConfig(BoosterHandle handle, bst_ulong* out_len, const char** out) {
+  DP_API_BEGIN();
+  const std::string& s = as_booster(handle)->save_config_json();
+  *out_len = s.size();
+  *out = s.c_str();
+  DP_API_END();
+}
+
+int XGBoosterSaveModel(BoosterHandle handle, const char* fname) {
+  DP_API_BEGIN();
+  need(fname != nullptr, "file name is null");
+  const std::string path(fname);
+  need(ends_with(path, ".json"), "only JSON models (a .json file name) are supported");
+  const std::string& s = as_booster(handle)->save_model_json();
+  std::ofstream f(path, std::ios::binary | std::ios::trunc);
+  need(bool(f), "cannot write " + path);
+  f.write(s.data(), std::streamsize(s.size()));
+  f.flush();
+  need(bool(f), "cannot write " + path);
+  DP_API_END();
+}
+
+int XGBoosterSaveModelToBuffer(BoosterHandle handle, const char* config, bst_ulong* out_len, const char** out) {
+  DP_API_BEGIN();
+  need(config != nullptr, "config is null");
+  const dp::json::Value c = dp::json::parse(config);
+  need(c.at("format").as_string() == "json", "only {\"format\":\"json\"} is supported");
+  const std::string& s = as_booster(handle)->save_model_json();
+  *out_len = s.size();
+  *out = s.c_str();
+  DP_API_END();
+}
+
+int XGBoosterLoadModelFromBuffer(BoosterHandle handle, const void* buf, bst_ulong len) {
+  DP_API_BEGIN();
+  need(buf != nullptr && len > 0, "model buffer is empty");
+  as_booster(handle)->load_model_json(std::string(static_cast<const char*>(buf), len));
+  DP_API_END();
+}
+
+int XGBoosterLoadModel(BoosterHandle handle, const char* fname) {
+  DP_API_BEGIN();
+  need(fname != nullptr, "file name is null");
+  as_booster(handle)->load_model_json(read_file(fname));
+  DP_API_END();
+}
+
+int XGBoosterSlice(BoosterHandle handle, int begin_layer, int end_layer, int step, BoosterHandle* out) {
+  DP_API_BEGIN();
+  need(out != nullptr, "output handle pointer is null");
+  *out = as_booster(handle)->slice(begin_layer, end_layer, step).release();
+  DP_API_END();
+}
+
+int XGBoosterGetNumFeature(BoosterHandle handle, bst_ulong* out) {
+  DP_API_BEGIN();
+  *out = bst_ulong(as_booster(handle)->model.num_feature);
+  DP_API_END();
+}
+
+// ---- extensions --------------------------------------------------------------
+int dp_comm_unique_id(void* out128) {
+  DP_API_BEGIN();
+  need(out128 != nullptr, "output pointer is null");
+  dp::nccl_unique_id(out128);
+  DP_API_END();
+}
+
+int dp_comm_create(const void* unique_id128, int nranks, int rank, int device, void** out) {
+  DP_API_BEGIN();
+  need(unique_id128 != nullptr && out != nullptr, "null argument");
+  *out = dp::make_nccl_comm(unique_id128, nranks, rank, device);
+  DP_API_END();
+}
+
+int dp_comm_free(void* comm) {
+  DP_API_BEGIN();
+  delete static_cast<dp::Comm*>(comm);
+  DP_API_END();
+}
+
+int dp_booster_set_comm(BoosterHandle handle, void* comm) {
+  DP_API_BEGIN();
+  dp::Booster* b = as_booster(handle);
+  need(b->boosted_rounds() == 0, "the communicator must be attached before the first round");
+  b->comm = static_cast<dp::Comm*>(comm);
+  DP_API_END();
+}
+
+int dp_booster_set_profiling(BoosterHandle handle, int on) {
+  DP_API_BEGIN();
+  dp::Booster* b = as_booster(handle);
+  b->profiling = on != 0;
+  if (b->engine()) {
+    b->engine()->profiler().enable(b->profiling);
+    if (b->profiling) b->engine()->profiler().reset();
+  }
+  DP_API_END();
+}
+
+int dp_booster_profile(BoosterHandle handle, const char** out_json) {
+  DP_API_BEGIN();
+  dp::Booster* b = as_booster(handle);
+  b->profile_buf = b->engine() ? b->engine()->profiler().json() : std::string("{}");
+  *out_json = b->profile_buf.c_str();
+  DP_API_END();
+}
+
+int dp_booster_margins(BoosterHandle handle, float* out, bst_ulong len) {
+  DP_API_BEGIN();
+  dp::Booster* b = as_booster(handle);
+  need(b->engine() != nullptr, "the booster has not been trained on a matrix");
+  const std::vector<float> m = b->engine()->margins();
+  need(len == m.size(), "margin buffer size differs from rows * outputs");
+  std::memcpy(out, m.data(), m.size() * sizeof(float));
+  DP_API_END();
+}
+
+uint64_t dp_launch_count(void) { return dp::launch_counter().load(); }
+
+int dp_quantile_cuts(const float* x, uint64_t rows, uint32_t features, uint64_t row_stride, int max_bin,
+                     float* cut, uint16_t* nbins, uint8_t* has_missing, void* stream) {
+  DP_API_BEGIN();
+  dp::CutsDevice cd{cut, nbins, has_missing};
+  dp::compute_cuts(x, rows, features, row_stride, max_bin, false, 0.f, rows, nullptr, cd,
+                   static_cast<cudaStream_t>(stream));
+  DP_API_END();
+}
+
+int dp_bin_matrix(const float* x, uint64_t rows, uint32_t features, uint64_t row_stride, const float* cut,
+                  const uint16_t* nbins, uint8_t* bins, uint64_t bin_stride, void* stream) {
+  DP_API_BEGIN();
+  need(bin_stride >= features && bin_stride % 16 == 0, "bin_stride must cover the features and be a multiple of 16");
+  dp::CutsDevice cd{const_cast<float*>(cut), const_cast<uint16_t*>(nbins), nullptr};
+  dp::launch_bin_matrix(x, rows, features, row_stride, false, 0.f, cd, bins, bin_stride,
+                        static_cast<cudaStream_t>(stream));
+  DP_API_END();
+}
+
+int dp_gradients(int objective, int num_class, const float* margin, const float* label, uint64_t rows, float* gh,
+                 float* scales, void* stream) {
+  DP_API_BEGIN();
+  need(objective >= 0 && objective <= 3, "objective id must be 0..3");
+  const int K = (objective >= 2) ? num_class : 1;
+  need(K >= 1, "num_class must be at least 1");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  dp::DevBuf<dp::u32> mx(2 * size_t(K));
+  dp::cuda_check(cudaMemsetAsync(mx.get(), 0, 2 * K * sizeof(dp::u32), s), "memset");
+  dp::launch_gradients(objective, K, margin, label, rows, reinterpret_cast<float2*>(gh), mx.get(), mx.get() + K, s);
+  dp::launch_scales(K, mx.get(), mx.get() + K, reinterpret_cast<dp::Scales*>(scales), s);
+  dp::cuda_check(cudaStreamSynchronize(s), "gradients");
+  DP_API_END();
+}
+
+int dp_hist_build(const uint8_t* bins, uint64_t bin_stride, uint32_t features, const float* gh, const uint32_t* ridx,
+                  const int64_t* seg_begin, const int64_t* seg_end, int32_t nseg, float sg, float sh, int64_t* hist,
+                  void* stream) {
+  DP_API_BEGIN();
+  need(nseg >= 0 && (nseg == 0 || (seg_begin && seg_end)), "invalid segments");
+  need(bin_stride % 16 == 0 && bin_stride >= features, "bin_stride must cover the features and be a multiple of 16");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const dp::u64 slot = dp::u64(features) * dp::kMaxBins * 2;
+  std::vector<dp::HistTask> tasks;
+  const dp::u32 ftiles = (features + dp::kHistFeatureTile - 1) / dp::kHistFeatureTile;
+  for (int32_t i = 0; i < nseg; ++i) {
+    need(seg_begin[i] >= 0 && seg_end[i] >= seg_begin[i], "invalid segment bounds");
+    for (dp::u32 ft = 0; ft < ftiles; ++ft)
+      for (int64_t b = seg_begin[i]; b < seg_end[i]; b += dp::kWindowRows)
+        tasks.push_back(dp::HistTask{dp::u32(i), ft * dp::kHistFeatureTile, 0, 0, b,
+                                     std::min<int64_t>(seg_end[i], b + dp::kWindowRows)});
+  }
+  dp::DevBuf<dp::HistTask> dt(std::max<size_t>(tasks.size(), 1));
+  dp::DevBuf<dp::TreeArrays> ta(1);
+  dp::DevBuf<dp::Scales> sc(1);
+  const dp::TreeArrays th{const_cast<uint32_t*>(ridx), reinterpret_cast<float2*>(const_cast<float*>(gh))};
+  const dp::Scales sh_{sg, sh};
+  dp::cuda_check(cudaMemcpyAsync(ta.get(), &th, sizeof th, cudaMemcpyHostToDevice, s), "upload");
+  dp::cuda_check(cudaMemcpyAsync(sc.get(), &sh_, sizeof sh_, cudaMemcpyHostToDevice, s), "upload");
+  if (!tasks.empty())
+    dp::cuda_check(cudaMemcpyAsync(dt.get(), tasks.data(), tasks.size() * sizeof(dp::HistTask),
+                                   cudaMemcpyHostToDevice, s),
+                   "upload");
+  if (nseg) dp::cuda_check(cudaMemsetAsync(hist, 0, dp::u64(nseg) * slot * sizeof(int64_t), s), "memset");
+  dp::launch_histograms(bins, bin_stride, features, ta.get(), sc.get(), dt.get(), dp::u32(tasks.size()), hist, s);
+  dp::cuda_check(cudaStreamSynchronize(s), "histograms");
+  DP_API_END();
+}
+
+int dp_eval_splits(const int64_t* hist, int32_t nnodes, uint32_t features, const uint16_t* nbins,
+                   const uint8_t* has_missing, const int64_t* totals, float sg, float sh, double lambda, double alpha,
+                   double gamma, double min_child_weight, int32_t* out_i, double* out_gain, int64_t* out_left) {
+  DP_API_BEGIN();
+  need(nnodes >= 0, "invalid node count");
+  if (nnodes == 0) return 0;
+  std::vector<dp::EvalNode> en(nnodes);
+  for (int32_t n = 0; n < nnodes; ++n) en[n] = dp::EvalNode{dp::u32(n), 0, totals[2 * n], totals[2 * n + 1]};
+  const dp::u32 nchunks = (features + dp::kEvalFeatureChunk - 1) / dp::kEvalFeatureChunk;
+  dp::DevBuf<dp::EvalNode> de(nnodes);
+  dp::DevBuf<dp::SplitCand> cand(size_t(nnodes) * nchunks), best(nnodes);
+  dp::DevBuf<dp::Scales> sc(1);
+  const dp::Scales s{sg, sh};
+  dp::cuda_check(cudaMemcpy(de.get(), en.data(), en.size() * sizeof(dp::EvalNode), cudaMemcpyHostToDevice), "upload");
+  dp::cuda_check(cudaMemcpy(sc.get(), &s, sizeof s, cudaMemcpyHostToDevice), "upload");
+  dp::SplitParams p;
+  p.lambda = lambda;
+  p.alpha = alpha;
+  p.gamma = gamma;
+  p.min_child_weight = min_child_weight;
+  dp::launch_eval_splits(hist, features, nbins, has_missing, de.get(), dp::u32(nnodes), sc.get(), p, cand.get(),
+                         best.get(), nullptr);
+  std::vector<dp::SplitCand> b(nnodes);
+  dp::cuda_check(cudaMemcpy(b.data(), best.get(), b.size() * sizeof(dp::SplitCand), cudaMemcpyDeviceToHost),
+                 "download");
+  for (int32_t n = 0; n < nnodes; ++n) {
+    out_i[4 * n] = b[n].feature;
+    out_i[4 * n + 1] = b[n].bin;
+    out_i[4 * n + 2] = b[n].default_left;
+    out_i[4 * n + 3] = b[n].feature >= 0;
+    out_gain[n] = b[n].gain;
+    out_left[2 * n] = b[n].gl;
+    out_left[2 * n + 1] = b[n].hl;
+  }
+  DP_API_END();
+}
+
+}  // extern "C"

@@ -1,0 +1,108 @@
+// NCCL communicator for row-sharded training: one process per GPU, sums of
+// integer histograms / counts and maxima of gradient magnitudes over NVLink.
+// libnccl.so.2 is opened with dlopen on first use, so the library has no
+// link-time NCCL dependency and a process that already loaded NCCL (for
+// example through torch.distributed) shares that copy.
+#include <dlfcn.h>
+#include <nccl.h>
+
+#include <cstring>
+#include <mutex>
+
+#include "comm.h"
+#include "common.h"
+
+namespace dp {
+
+namespace {
+
+struct NcclApi {
+  ncclResult_t (*get_unique_id)(ncclUniqueId*) = nullptr;
+  ncclResult_t (*comm_init_rank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*all_reduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                             cudaStream_t) = nullptr;
+  ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
+  const char* (*error_string)(ncclResult_t) = nullptr;
+};
+
+const NcclApi& nccl() {
+  static NcclApi api;
+  static std::once_flag once;
+  static std::string error;
+  std::call_once(once, [] {
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) { error = std::string("cannot load NCCL: ") + dlerror(); return; }
+    api.get_unique_id = reinterpret_cast<decltype(api.get_unique_id)>(dlsym(h, "ncclGetUniqueId"));
+    api.comm_init_rank = reinterpret_cast<decltype(api.comm_init_rank)>(dlsym(h, "ncclCommInitRank"));
+    api.all_reduce = reinterpret_cast<decltype(api.all_reduce)>(dlsym(h, "ncclAllReduce"));
+    api.comm_destroy = reinterpret_cast<decltype(api.comm_destroy)>(dlsym(h, "ncclCommDestroy"));
+    api.error_string = reinterpret_cast<decltype(api.error_string)>(dlsym(h, "ncclGetErrorString"));
+    if (!api.get_unique_id || !api.comm_init_rank || !api.all_reduce || !api.comm_destroy || !api.error_string) {
+      error = "NCCL library lacks a required symbol";
+      api = NcclApi{};
+    }
+  });
+  need(api.all_reduce != nullptr, error.empty() ? "NCCL unavailable" : error);
+  return api;
+}
+
+void check(ncclResult_t r, const char* what) {
+  if (r != ncclSuccess) fail(std::string(what) + ": " + nccl().error_string(r));
+}
+
+class NcclComm final : public Comm {
+ public:
+  NcclComm(const void* id, int nranks, int rank, int device) : rank_(rank), size_(nranks), device_(device) {
+    need(nranks >= 1 && rank >= 0 && rank < nranks, "invalid NCCL rank / size");
+    ncclUniqueId uid;
+    static_assert(sizeof(uid) == 128, "ncclUniqueId is 128 bytes");
+    std::memcpy(&uid, id, sizeof uid);
+    DeviceGuard g(device_);
+    check(nccl().comm_init_rank(&comm_, nranks, uid, rank), "ncclCommInitRank");
+    DP_CUDA(cudaMalloc(&scratch_, sizeof(u64)));
+  }
+  ~NcclComm() override {
+    DeviceGuard g(device_);
+    if (scratch_) cudaFree(scratch_);
+    if (comm_) nccl().comm_destroy(comm_);
+  }
+  int rank() const override { return rank_; }
+  int size() const override { return size_; }
+  void sum_u32(u32* d, size_t n, cudaStream_t s) override {
+    if (n) check(nccl().all_reduce(d, d, n, ncclUint32, ncclSum, comm_, s), "ncclAllReduce(u32 sum)");
+  }
+  void sum_i64(i64* d, size_t n, cudaStream_t s) override {
+    if (n) check(nccl().all_reduce(d, d, n, ncclInt64, ncclSum, comm_, s), "ncclAllReduce(i64 sum)");
+  }
+  void max_u32(u32* d, size_t n, cudaStream_t s) override {
+    if (n) check(nccl().all_reduce(d, d, n, ncclUint32, ncclMax, comm_, s), "ncclAllReduce(u32 max)");
+  }
+  u64 sum_host_u64(u64 v, cudaStream_t s) override {
+    DP_CUDA(cudaMemcpyAsync(scratch_, &v, sizeof v, cudaMemcpyHostToDevice, s));
+    check(nccl().all_reduce(scratch_, scratch_, 1, ncclUint64, ncclSum, comm_, s), "ncclAllReduce(u64 sum)");
+    u64 out = 0;
+    DP_CUDA(cudaMemcpyAsync(&out, scratch_, sizeof out, cudaMemcpyDeviceToHost, s));
+    DP_CUDA(cudaStreamSynchronize(s));
+    return out;
+  }
+
+ private:
+  ncclComm_t comm_ = nullptr;
+  int rank_, size_, device_;
+  u64* scratch_ = nullptr;
+};
+
+}  // namespace
+
+Comm* make_nccl_comm(const void* unique_id, int nranks, int rank, int device) {
+  return new NcclComm(unique_id, nranks, rank, device);
+}
+
+void nccl_unique_id(void* out128) {
+  ncclUniqueId uid;
+  check(nccl().get_unique_id(&uid), "ncclGetUniqueId");
+  std::memcpy(out128, &uid, sizeof uid);
+}
+
+}  // namespace dp

@@ -1,0 +1,59 @@
+// Training matrix handed over by XGDMatrixCreateFromCudaArrayInterface: a
+// borrowed dense fp32 device matrix (NaN = missing) plus owned labels, and the
+// cached quantile cuts / uint8 bin matrix built at the first boosting round.
+// Mirrors the reference's use: a borrowed CUDA pointer that must stay valid
+// while the DMatrix lives (native/class_native_training.cuh:49-53,
+// native/class_study_oof.cu:532-534).
+#pragma once
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "comm.h"
+#include "common.h"
+#include "kernels.h"
+
+namespace dp {
+
+struct Quantized {
+  int max_bin = 0;
+  u64 bin_stride = 0;       // bytes per row of `bins` (multiple of 16)
+  DevBuf<float> cut;        // [F][256]
+  DevBuf<u16> nbins;        // [F]
+  DevBuf<u8> has_missing;   // [F]
+  DevBuf<u8> bins;          // [R][bin_stride]
+  std::vector<float> cut_h;
+  std::vector<u16> nbins_h;
+  std::vector<u8> has_missing_h;
+  u64 rows_total = 0;       // over all ranks
+};
+
+class DMatrix {
+ public:
+  DMatrix(const float* x, u64 rows, u32 cols, u64 stride, int device, bool has_mv, float mv);
+
+  void set_labels_device(const float* y, u64 n);
+  void set_labels_host(const float* y, u64 n);
+
+  // Cuts and bins for `max_bin` over all ranks of `comm` (built once).
+  const Quantized& quantized(int max_bin, Comm* comm, cudaStream_t s);
+
+  u64 rows() const { return rows_; }
+  u32 cols() const { return cols_; }
+  int device() const { return device_; }
+  const float* labels() const { return labels_.get(); }
+  bool has_labels() const { return labels_n_ == rows_; }
+
+ private:
+  const float* x_ = nullptr;
+  u64 rows_ = 0, stride_ = 0;
+  u32 cols_ = 0;
+  int device_ = 0;
+  bool has_mv_ = false;
+  float mv_ = 0.f;
+  DevBuf<float> labels_;
+  u64 labels_n_ = 0;
+  std::unique_ptr<Quantized> q_;
+};
+
+}  // namespace dp

@@ -1,0 +1,166 @@
+// Objective gradients, quantiser scales, leaf/margin update and input checks.
+//
+// Gradients (per row, double precision, then rounded to float):
+//   reg:squarederror          g = m - y,            h = 1
+//   binary:logistic           p = 1/(1+e^-m),       g = p - y,  h = max(p(1-p), 1e-16)
+//   multi:softprob / softmax  p_k = softmax(m)_k,   g_k = p_k - [y==k],
+//                                                   h_k = max(2 p_k (1-p_k), 1e-16)
+// These are the objectives the reference configures or that its drop-in
+// callers need (native/class_native_training.cuh:60 hard-codes
+// multi:softmax; BASELINE configs add binary:logistic and reg:squarederror).
+#include "kernels.h"
+
+namespace dp {
+
+namespace {
+
+__device__ __forceinline__ void warp_max_to(u32* dst, float v) {
+  u32 b = __float_as_uint(v);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) b = max(b, __shfl_xor_sync(0xffffffffu, b, o));
+  if ((threadIdx.x & 31) == 0 && b) atomicMax(dst, b);
+}
+
+__global__ void __launch_bounds__(256) k_gradients(int objective, int K, const float* __restrict__ margin,
+                                                    const float* __restrict__ label, u64 R, float2* __restrict__ gh,
+                                                    u32* gmax, u32* hmax) {
+  const u64 step = u64(gridDim.x) * blockDim.x;
+  for (u64 base = u64(blockIdx.x) * blockDim.x; base < R; base += step) {
+    const u64 r = base + threadIdx.x;
+    const bool valid = r < R;
+    const double y = valid ? double(label[r]) : 0.0;
+    if (objective == kSquaredError || objective == kLogistic) {
+      float g = 0.f, h = 0.f;
+      if (valid) {
+        const double m = double(margin[r]);
+        if (objective == kSquaredError) {
+          g = float(m - y);
+          h = 1.0f;
+        } else {
+          const double p = 1.0 / (1.0 + dp_exp(-m));
+          g = float(p - y);
+          h = float(fmax(p * (1.0 - p), 1e-16));
+        }
+        gh[r] = make_float2(g, h);
+      }
+      warp_max_to(gmax, fabsf(g));
+      warp_max_to(hmax, h);
+    } else {
+      double mx = 0.0, s = 0.0;
+      const float* m = margin + (valid ? r : 0) * u64(K);
+      if (valid) {
+        mx = double(m[0]);
+        for (int k = 1; k < K; ++k) mx = fmax(mx, double(m[k]));
+        for (int k = 0; k < K; ++k) s = s + dp_exp(double(m[k]) - mx);
+      }
+      for (int k = 0; k < K; ++k) {
+        float g = 0.f, h = 0.f;
+        if (valid) {
+          const double pk = dp_exp(double(m[k]) - mx) / s;
+          g = float(pk - (double(k) == y ? 1.0 : 0.0));
+          h = float(fmax(2.0 * pk * (1.0 - pk), 1e-16));
+          gh[u64(k) * R + r] = make_float2(g, h);
+        }
+        warp_max_to(gmax + k, fabsf(g));
+        warp_max_to(hmax + k, h);
+      }
+    }
+  }
+}
+
+__global__ void k_scales(int K, const u32* gmax, const u32* hmax, Scales* scales) {
+  const int k = blockIdx.x * blockDim.x + threadIdx.x;
+  if (k < K) {
+    scales[k].sg = quant_scale(__uint_as_float(gmax[k]), kGradBits);
+    scales[k].sh = quant_scale(__uint_as_float(hmax[k]), kHessBits);
+  }
+}
+
+// One block per leaf task; rows of a leaf are updated in place.
+__global__ void __launch_bounds__(256) k_leaf_update(const LeafTask* __restrict__ tasks, float* margin, u32 K) {
+  const LeafTask t = tasks[blockIdx.x];
+  for (i64 i = t.begin + threadIdx.x; i < t.end; i += blockDim.x) {
+    const u32 r = t.ridx[i];
+    float* m = margin + u64(r) * K + t.klass;
+    *m = *m + t.value;
+  }
+}
+
+__global__ void k_iota(u32* p, u64 n) {
+  for (u64 i = u64(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += u64(gridDim.x) * blockDim.x) p[i] = u32(i);
+}
+
+__global__ void k_check_finite(const float* __restrict__ x, u64 R, u32 F, u64 stride, u32* bad) {
+  const u64 n = R * F;
+  bool any = false;
+  for (u64 i = u64(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += u64(gridDim.x) * blockDim.x) {
+    const u64 r = i / F, f = i - r * F;
+    any |= isinf(x[r * stride + f]);
+  }
+  if (__any_sync(0xffffffffu, any) && (threadIdx.x & 31) == 0) atomicOr(bad, 1u);
+}
+
+__global__ void k_check_labels(const float* __restrict__ y, u64 R, int objective, int K, u32* bad) {
+  bool any = false;
+  for (u64 i = u64(blockIdx.x) * blockDim.x + threadIdx.x; i < R; i += u64(gridDim.x) * blockDim.x) {
+    const float v = y[i];
+    if (!isfinite(v)) any = true;
+    else if (objective == kLogistic) any |= (v < 0.f || v > 1.f);
+    else if (objective == kSoftprob || objective == kSoftmax) any |= (v < 0.f || v >= float(K) || v != floorf(v));
+  }
+  if (__any_sync(0xffffffffu, any) && (threadIdx.x & 31) == 0) atomicOr(bad, 1u);
+}
+
+int grid_for(u64 n, int block) {
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const u64 want = (n + block - 1) / block;
+  const u64 cap = u64(sms) * 8;
+  return int(want < cap ? (want ? want : 1) : cap);
+}
+
+}  // namespace
+
+void launch_gradients(int objective, int K, const float* margin, const float* label, u64 R, float2* gh,
+                      u32* gmax_bits, u32* hmax_bits, cudaStream_t s) {
+  if (R == 0) return;
+  k_gradients<<<grid_for(R, 256), 256, 0, s>>>(objective, K, margin, label, R, gh, gmax_bits, hmax_bits);
+  after_launch("gradients");
+}
+
+void launch_scales(int K, const u32* gmax_bits, const u32* hmax_bits, Scales* scales, cudaStream_t s) {
+  k_scales<<<(K + 127) / 128, 128, 0, s>>>(K, gmax_bits, hmax_bits, scales);
+  after_launch("scales");
+}
+
+void launch_leaf_update(const LeafTask* tasks, u32 ntasks, float* margin, u32 K, cudaStream_t s) {
+  if (!ntasks) return;
+  k_leaf_update<<<ntasks, 256, 0, s>>>(tasks, margin, K);
+  after_launch("leaf_update");
+}
+
+void launch_iota(u32* p, u64 n, cudaStream_t s) {
+  if (!n) return;
+  k_iota<<<grid_for(n, 256), 256, 0, s>>>(p, n);
+  after_launch("iota");
+}
+
+void launch_check_finite(const float* x, u64 R, u32 F, u64 stride, u32* bad, cudaStream_t s) {
+  if (!R || !F) return;
+  k_check_finite<<<grid_for(R * F, 256), 256, 0, s>>>(x, R, F, stride, bad);
+  after_launch("check_finite");
+}
+
+void launch_check_labels(const float* y, u64 R, int objective, int K, u32* bad, cudaStream_t s) {
+  if (!R) return;
+  k_check_labels<<<grid_for(R, 256), 256, 0, s>>>(y, R, objective, K, bad);
+  after_launch("check_labels");
+}
+
+std::atomic<u64>& launch_counter() {
+  static std::atomic<u64> n{0};
+  return n;
+}
+
+}  // namespace dp

@@ -1,0 +1,152 @@
+// Split evaluation: for every open node, the best (feature, bin, missing
+// direction) by second-order gain (Chen & Guestrin 2016):
+//   gain = 0.5 * (s(GL,HL) + s(GR,HR) - s(G,H)) - gamma,  s(G,H) = T(G)^2/(H+lambda)
+// A warp scans one feature: lane l owns bins [8l, 8l+8) and the warp-level
+// exclusive scan of the lanes' int64 sums gives every prefix exactly.  Ties
+// resolve to the lowest (feature, bin, default_left), i.e. the first maximum
+// in scan order, at every reduction level.
+#include "kernels.h"
+
+namespace dp {
+
+namespace {
+
+constexpr int kEvalThreads = 256;
+
+struct Best {
+  double gain;
+  i64 gl, hl;
+  i32 f, b, d;
+};
+
+__device__ __forceinline__ bool better(const Best& a, const Best& c) {
+  if (a.gain > c.gain) return true;
+  if (!(a.gain == c.gain)) return false;
+  if (a.f != c.f) return a.f < c.f;
+  if (a.b != c.b) return a.b < c.b;
+  return a.d < c.d;
+}
+
+__device__ __forceinline__ Best shfl_best(const Best& v, int src) {
+  Best o;
+  o.gain = __shfl_sync(0xffffffffu, v.gain, src);
+  o.gl = __shfl_sync(0xffffffffu, v.gl, src);
+  o.hl = __shfl_sync(0xffffffffu, v.hl, src);
+  o.f = __shfl_sync(0xffffffffu, v.f, src);
+  o.b = __shfl_sync(0xffffffffu, v.b, src);
+  o.d = __shfl_sync(0xffffffffu, v.d, src);
+  return o;
+}
+
+__global__ void __launch_bounds__(kEvalThreads) k_eval(const i64* __restrict__ hist, u32 F,
+                                                       const u16* __restrict__ nbins,
+                                                       const u8* __restrict__ has_missing,
+                                                       const EvalNode* __restrict__ nodes,
+                                                       const Scales* __restrict__ scales, SplitParams p, u32 nchunks,
+                                                       SplitCand* __restrict__ cand) {
+  __shared__ Best wbest[kEvalThreads / 32];
+  const u32 node = blockIdx.x / nchunks, chunk = blockIdx.x % nchunks;
+  const EvalNode nd = nodes[node];
+  const Scales sc = scales[nd.tree];
+  const double isg = 1.0 / double(sc.sg), ish = 1.0 / double(sc.sh);
+  const double G = double(nd.gq) * isg, H = double(nd.hq) * ish;
+  const double sp = node_score(G, H, p);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  Best best{-HUGE_VAL, 0, 0, -1, -1, 0};
+  const u32 f_end = min(F, (chunk + 1) * kEvalFeatureChunk);
+  for (u32 f = chunk * kEvalFeatureChunk + warp; f < f_end; f += kEvalThreads / 32) {
+    const int nb = nbins[f];
+    if (nb < 2) continue;
+    const bool hm = has_missing[f] != 0;
+    const i64* hf = hist + (u64(nd.slot) * F + f) * (2 * kMaxBins);
+    const i64 gm = hm ? hf[2 * kMissingBin] : 0, hmq = hm ? hf[2 * kMissingBin + 1] : 0;
+    i64 g[8], h[8];
+    const longlong2* v = reinterpret_cast<const longlong2*>(hf) + 8 * lane;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const longlong2 x = v[j];
+      const bool value_bin = 8 * lane + j < nb;  // missing bin and empty tail excluded
+      g[j] = value_bin ? x.x : 0;
+      h[j] = value_bin ? x.y : 0;
+    }
+    i64 sg_l = 0, sh_l = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) { sg_l += g[j]; sh_l += h[j]; }
+    // exclusive warp scan of the lane sums
+    i64 eg = sg_l, eh = sh_l;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const i64 ug = __shfl_up_sync(0xffffffffu, eg, o), uh = __shfl_up_sync(0xffffffffu, eh, o);
+      if (lane >= o) { eg += ug; eh += uh; }
+    }
+    eg -= sg_l;
+    eh -= sh_l;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      eg += g[j];
+      eh += h[j];
+      const int b = 8 * lane + j;
+      if (b > nb - 2) continue;
+#pragma unroll
+      for (int d = 0; d < 2; ++d) {
+        if (d == 1 && !hm) break;
+        const i64 glq = eg + (d ? gm : 0), hlq = eh + (d ? hmq : 0);
+        const i64 grq = nd.gq - glq, hrq = nd.hq - hlq;
+        const double gain = split_gain(double(glq) * isg, double(hlq) * ish, double(grq) * isg,
+                                       double(hrq) * ish, sp, p);
+        const Best c{gain, glq, hlq, i32(f), b, d};
+        if (better(c, best)) best = c;
+      }
+    }
+  }
+  // warp reduction, then block reduction; `better` breaks ties by index
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const Best other = shfl_best(best, lane ^ o);
+    if (better(other, best)) best = other;
+  }
+  if (lane == 0) wbest[warp] = best;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    Best b = wbest[0];
+    for (int w = 1; w < kEvalThreads / 32; ++w)
+      if (better(wbest[w], b)) b = wbest[w];
+    SplitCand out;
+    out.gain = b.gain;
+    out.gl = b.gl;
+    out.hl = b.hl;
+    out.feature = b.f;
+    out.bin = b.b;
+    out.default_left = b.d;
+    out.pad = 0;
+    cand[blockIdx.x] = out;
+  }
+}
+
+__global__ void k_reduce_cands(const SplitCand* __restrict__ cand, u32 nnodes, u32 nchunks,
+                               SplitCand* __restrict__ best) {
+  const u32 n = blockIdx.x * blockDim.x + threadIdx.x;
+  if (n >= nnodes) return;
+  SplitCand b = cand[u64(n) * nchunks];
+  for (u32 c = 1; c < nchunks; ++c) {
+    const SplitCand x = cand[u64(n) * nchunks + c];
+    // chunks hold increasing features, so on equal gain the earlier one wins
+    if (x.gain > b.gain) b = x;
+  }
+  best[n] = b;
+}
+
+}  // namespace
+
+void launch_eval_splits(const i64* hist, u32 F, const u16* nbins, const u8* has_missing, const EvalNode* nodes,
+                        u32 nnodes, const Scales* scales, SplitParams p, SplitCand* cand, SplitCand* best,
+                        cudaStream_t s) {
+  if (!nnodes) return;
+  const u32 nchunks = (F + kEvalFeatureChunk - 1) / kEvalFeatureChunk;
+  k_eval<<<nnodes * nchunks, kEvalThreads, 0, s>>>(hist, F, nbins, has_missing, nodes, scales, p, nchunks, cand);
+  after_launch("eval_splits");
+  k_reduce_cands<<<(nnodes + 127) / 128, 128, 0, s>>>(cand, nnodes, nchunks, best);
+  after_launch("reduce_splits");
+}
+
+}  // namespace dp

@@ -1,0 +1,132 @@
+// Host launchers of the sm_100a kernels of the GBDT-training path.  All
+// pointers are device pointers unless named *_host; every launcher enqueues on
+// `stream` and never synchronises.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "common.h"
+#include "dp_math.cuh"
+
+namespace dp {
+
+// One unit of histogram work: rows at positions [begin, end) of a node's
+// segment (end - begin <= kWindowRows), accumulated into histogram slot
+// `slot` for features [f0, f0 + feature tile).
+struct HistTask {
+  u32 slot;
+  u32 f0;
+  u32 tree;   // selects the (g,h) / row-index arrays of this tree
+  u32 pad;
+  i64 begin;
+  i64 end;
+};
+
+// Per-tree position-ordered arrays used by the histogram and partition kernels.
+struct TreeArrays {
+  u32* ridx;    // [positions] row index
+  float2* gh;   // [positions] (g, h)
+};
+
+// Quantiser scales of one tree: s_g, s_h.
+struct Scales {
+  float sg, sh;
+};
+
+// Best split candidate.  gain = -inf when no valid candidate exists.
+struct SplitCand {
+  double gain;
+  i64 gl, hl;  // left quantised sums (missing bin included when default_left)
+  i32 feature;
+  i32 bin;
+  i32 default_left;
+  i32 pad;
+};
+
+// Open node handed to split evaluation.
+struct EvalNode {
+  u32 slot;   // histogram slot
+  u32 tree;
+  i64 gq, hq; // quantised totals
+};
+
+// ---- binning (quantile cuts by exact radix selection) ---------------------
+struct CutState;  // defined in k_quantile.cu
+struct CutsDevice {
+  float* cut = nullptr;      // [F][256] boundaries
+  u16* nbins = nullptr;      // [F] value bins
+  u8* has_missing = nullptr; // [F]
+};
+
+// ---- gradients --------------------------------------------------------------
+enum Objective : int { kSquaredError = 0, kLogistic = 1, kSoftprob = 2, kSoftmax = 3 };
+
+// gh[k][r] from margins [R][K] and labels; maxima of |g| and h per class are
+// atomically maxed into gmax[k], hmax[k] (float bits as u32; must be zeroed).
+void launch_gradients(int objective, int K, const float* margin, const float* label, u64 R, float2* gh,
+                      u32* gmax_bits, u32* hmax_bits, cudaStream_t s);
+// scales[k] from the maxima.
+void launch_scales(int K, const u32* gmax_bits, const u32* hmax_bits, Scales* scales, cudaStream_t s);
+
+// ---- histograms -------------------------------------------------------------
+// hist[slot][F][256][2] (int64) must be zeroed for every slot the tasks touch.
+void launch_histograms(const u8* bins, u64 bin_stride, u32 F, const TreeArrays* trees, const Scales* scales,
+                       const HistTask* tasks, u32 ntasks, i64* hist, cudaStream_t s);
+constexpr u32 kHistFeatureTile = 32;
+
+// hist[dst] = parent_hist[par] - hist[src] for each (par, src, dst) slot triple.
+void launch_subtract(i64* hist, const i64* parent_hist, u64 slot_elems, const u32* triples, u32 n, cudaStream_t s);
+
+// ---- split evaluation --------------------------------------------------------
+// Per (node, feature chunk) candidate into cand[node][chunk]; then the best per
+// node into best[node].
+void launch_eval_splits(const i64* hist, u32 F, const u16* nbins, const u8* has_missing, const EvalNode* nodes,
+                        u32 nnodes, const Scales* scales, SplitParams p, SplitCand* cand, SplitCand* best,
+                        cudaStream_t s);
+constexpr u32 kEvalFeatureChunk = 16;
+
+// ---- partition ----------------------------------------------------------------
+struct PartTask {
+  u32 node;      // index into PartNode
+  u32 pad;
+  i64 begin;     // positions [begin, end)
+  i64 end;
+};
+struct PartNode {
+  u32 tree;
+  i32 feature;
+  i32 bin;
+  i32 default_left;
+  i32 missing_is_bin;  // has_missing[feature]
+  i32 pad;
+  i64 begin;       // segment start
+  i64 nleft;       // filled by the host between count and scatter
+};
+// Counts left-going rows per task (left[task]) and stores decision bits.
+void launch_partition_count(const u8* bins, u64 bin_stride, const TreeArrays* trees, const PartNode* nodes,
+                            const PartTask* tasks, u32 ntasks, u32* flags, u32* left, cudaStream_t s);
+// Scatters rows into the other buffer: left_off[task] / right_off[task] are
+// the exclusive offsets of the task's rows within its node's left / right part.
+void launch_partition_scatter(const TreeArrays* src, const TreeArrays* dst, const PartNode* nodes,
+                              const PartTask* tasks, u32 ntasks, const u32* flags, const i64* left_off,
+                              const i64* right_off, cudaStream_t s);
+constexpr u32 kPartChunk = 4096;
+
+// ---- leaves -------------------------------------------------------------------
+struct LeafTask {
+  const u32* ridx;
+  i64 begin, end;
+  float value;
+  u32 klass;
+};
+void launch_leaf_update(const LeafTask* tasks, u32 ntasks, float* margin, u32 K, cudaStream_t s);
+
+// ---- misc ---------------------------------------------------------------------
+void launch_iota(u32* p, u64 n, cudaStream_t s);
+// Flags (atomicOr into bad[0]) any +-inf in x[r*stride + f].
+void launch_check_finite(const float* x, u64 R, u32 F, u64 stride, u32* bad, cudaStream_t s);
+// Labels: flags values that are not valid for the objective.
+void launch_check_labels(const float* y, u64 R, int objective, int K, u32* bad, cudaStream_t s);
+
+}  // namespace dp

@@ -1,0 +1,293 @@
+"""ctypes binding of libdp_gbdt (include/dp_gbdt.h).
+
+Mirrors the call sequence the reference trainer issues through the XGBoost C
+API (native/class_native_training.cuh:47-70): a DMatrix over borrowed CUDA
+fp32 memory, a Booster configured with XGBoosterSetParam, one
+XGBoosterUpdateOneIter per round, then the JSON configuration and model.
+Device memory is supplied by the caller (here: torch CUDA tensors or raw
+pointers); the library itself has no CPU training path and raises if its
+shared object is missing.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import json
+import math
+import pathlib
+from typing import Iterable
+
+HERE = pathlib.Path(__file__).resolve().parent
+LIB_PATH = HERE / "libdp_gbdt.so"
+
+EXPORTED = [
+    "XGBoostVersion", "XGBuildInfo", "XGBGetLastError", "XGDMatrixCreateFromCudaArrayInterface",
+    "XGDMatrixSetInfoFromInterface", "XGDMatrixSetFloatInfo", "XGDMatrixNumRow", "XGDMatrixNumCol",
+    "XGDMatrixFree", "XGBoosterCreate", "XGBoosterFree", "XGBoosterSetParam", "XGBoosterUpdateOneIter",
+    "XGBoosterBoostedRounds", "XGBoosterSaveJsonConfig", "XGBoosterSaveModel", "XGBoosterSaveModelToBuffer",
+    "XGBoosterLoadModelFromBuffer", "XGBoosterLoadModel", "XGBoosterSlice", "XGBoosterGetNumFeature",
+    "dp_comm_unique_id", "dp_comm_create", "dp_comm_free", "dp_booster_set_comm", "dp_booster_set_profiling",
+    "dp_booster_profile", "dp_booster_margins", "dp_launch_count", "dp_quantile_cuts", "dp_bin_matrix",
+    "dp_gradients", "dp_hist_build", "dp_eval_splits",
+]
+
+OBJECTIVE_IDS = {"reg:squarederror": 0, "binary:logistic": 1, "multi:softprob": 2, "multi:softmax": 3}
+
+
+class DPError(RuntimeError):
+    pass
+
+
+_lib = None
+
+
+def lib() -> C.CDLL:
+    """Loads libdp_gbdt.so (built by `make -C decision-programs_b200`)."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise DPError(f"libdp_gbdt.so is missing at {LIB_PATH}; build it with __graft_entry__.build()")
+        L = C.CDLL(str(LIB_PATH))
+        P, u64, i32, f32, f64 = C.c_void_p, C.c_uint64, C.c_int, C.c_float, C.c_double
+        L.XGBoostVersion.restype = None
+        L.XGBoostVersion.argtypes = [C.POINTER(i32)] * 3
+        L.XGBuildInfo.argtypes = [C.POINTER(C.c_char_p)]
+        L.XGBGetLastError.restype = C.c_char_p
+        L.XGDMatrixCreateFromCudaArrayInterface.argtypes = [C.c_char_p, C.c_char_p, C.POINTER(P)]
+        L.XGDMatrixSetInfoFromInterface.argtypes = [P, C.c_char_p, C.c_char_p]
+        L.XGDMatrixSetFloatInfo.argtypes = [P, C.c_char_p, P, u64]
+        L.XGDMatrixNumRow.argtypes = [P, C.POINTER(u64)]
+        L.XGDMatrixNumCol.argtypes = [P, C.POINTER(u64)]
+        L.XGDMatrixFree.argtypes = [P]
+        L.XGBoosterCreate.argtypes = [C.POINTER(P), u64, C.POINTER(P)]
+        L.XGBoosterFree.argtypes = [P]
+        L.XGBoosterSetParam.argtypes = [P, C.c_char_p, C.c_char_p]
+        L.XGBoosterUpdateOneIter.argtypes = [P, i32, P]
+        L.XGBoosterBoostedRounds.argtypes = [P, C.POINTER(i32)]
+        L.XGBoosterSaveJsonConfig.argtypes = [P, C.POINTER(u64), C.POINTER(C.c_char_p)]
+        L.XGBoosterSaveModel.argtypes = [P, C.c_char_p]
+        L.XGBoosterSaveModelToBuffer.argtypes = [P, C.c_char_p, C.POINTER(u64), C.POINTER(C.c_void_p)]
+        L.XGBoosterLoadModelFromBuffer.argtypes = [P, C.c_char_p, u64]
+        L.XGBoosterLoadModel.argtypes = [P, C.c_char_p]
+        L.XGBoosterSlice.argtypes = [P, i32, i32, i32, C.POINTER(P)]
+        L.XGBoosterGetNumFeature.argtypes = [P, C.POINTER(u64)]
+        L.dp_comm_unique_id.argtypes = [P]
+        L.dp_comm_create.argtypes = [P, i32, i32, i32, C.POINTER(P)]
+        L.dp_comm_free.argtypes = [P]
+        L.dp_booster_set_comm.argtypes = [P, P]
+        L.dp_booster_set_profiling.argtypes = [P, i32]
+        L.dp_booster_profile.argtypes = [P, C.POINTER(C.c_char_p)]
+        L.dp_booster_margins.argtypes = [P, P, u64]
+        L.dp_launch_count.restype = u64
+        L.dp_launch_count.argtypes = []
+        L.dp_quantile_cuts.argtypes = [P, u64, C.c_uint32, u64, i32, P, P, P, P]
+        L.dp_bin_matrix.argtypes = [P, u64, C.c_uint32, u64, P, P, P, u64, P]
+        L.dp_gradients.argtypes = [i32, i32, P, P, u64, P, P, P]
+        L.dp_hist_build.argtypes = [P, u64, C.c_uint32, P, P, P, P, C.c_int32, f32, f32, P, P]
+        L.dp_eval_splits.argtypes = [P, C.c_int32, C.c_uint32, P, P, P, f32, f32, f64, f64, f64, f64, P, P, P]
+        _lib = L
+    return _lib
+
+
+def check(rc: int) -> None:
+    if rc != 0:
+        raise DPError(lib().XGBGetLastError().decode())
+
+
+def version() -> tuple[int, int, int]:
+    a, b, c = C.c_int(), C.c_int(), C.c_int()
+    lib().XGBoostVersion(C.byref(a), C.byref(b), C.byref(c))
+    return a.value, b.value, c.value
+
+
+def build_info() -> dict:
+    p = C.c_char_p()
+    check(lib().XGBuildInfo(C.byref(p)))
+    return json.loads(p.value.decode())
+
+
+def launch_count() -> int:
+    return int(lib().dp_launch_count())
+
+
+def array_interface(ptr: int, shape: Iterable[int], typestr: str = "<f4", strides=None) -> str:
+    """__cuda_array_interface__ JSON as the reference builds it
+    (native/class_model_native_adapter.cuh:26)."""
+    return json.dumps({"data": [int(ptr), True], "shape": list(shape), "strides": strides, "typestr": typestr,
+                       "version": 3, "stream": 1}, separators=(",", ":"))
+
+
+class DMatrix:
+    """Borrowed dense fp32 CUDA matrix [R][F] (NaN = missing)."""
+
+    def __init__(self, data_ptr: int, rows: int, cols: int, label_ptr: int | None = None, row_stride: int | None = None,
+                 missing: float = math.nan, keepalive=None):
+        self.handle = C.c_void_p()
+        strides = None if row_stride is None else [int(row_stride) * 4, 4]
+        cfg = '{"missing":NaN,"nthread":2}' if math.isnan(missing) else json.dumps({"missing": missing, "nthread": 2})
+        check(lib().XGDMatrixCreateFromCudaArrayInterface(array_interface(data_ptr, [rows, cols], strides=strides)
+                                                          .encode(), cfg.encode(), C.byref(self.handle)))
+        self._keep = keepalive
+        if label_ptr is not None:
+            self.set_label_ptr(label_ptr, rows)
+
+    @classmethod
+    def from_torch(cls, x, y=None, missing: float = math.nan) -> "DMatrix":
+        """x: CUDA float32 tensor [R, F] (row stride allowed); y: CUDA float32 [R]."""
+        assert x.is_cuda and x.dtype.is_floating_point and x.element_size() == 4 and x.dim() == 2
+        assert x.stride(1) == 1
+        d = cls(x.data_ptr(), x.shape[0], x.shape[1], row_stride=x.stride(0) if x.stride(0) != x.shape[1] else None,
+                missing=missing, keepalive=(x, y))
+        if y is not None:
+            y = y.contiguous()
+            d._keep = (x, y)
+            d.set_label_ptr(y.data_ptr(), y.shape[0])
+        return d
+
+    def set_label_ptr(self, ptr: int, n: int) -> None:
+        check(lib().XGDMatrixSetInfoFromInterface(self.handle, b"label", array_interface(ptr, [n]).encode()))
+
+    def set_label_host(self, y) -> None:
+        import numpy as np
+        y = np.ascontiguousarray(y, dtype=np.float32)
+        check(lib().XGDMatrixSetFloatInfo(self.handle, b"label", y.ctypes.data, y.size))
+
+    def num_row(self) -> int:
+        n = C.c_uint64()
+        check(lib().XGDMatrixNumRow(self.handle, C.byref(n)))
+        return n.value
+
+    def num_col(self) -> int:
+        n = C.c_uint64()
+        check(lib().XGDMatrixNumCol(self.handle, C.byref(n)))
+        return n.value
+
+    def free(self) -> None:
+        if self.handle:
+            check(lib().XGDMatrixFree(self.handle))
+            self.handle = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+class Booster:
+    def __init__(self, params: dict | None = None, cache: list[DMatrix] | None = None, handle=None):
+        if handle is not None:
+            self.handle = handle
+        else:
+            self.handle = C.c_void_p()
+            cache = cache or []
+            arr = (C.c_void_p * max(1, len(cache)))(*[d.handle for d in cache])
+            check(lib().XGBoosterCreate(arr, len(cache), C.byref(self.handle)))
+        for k, v in (params or {}).items():
+            self.set_param(k, v)
+
+    def set_param(self, key: str, value) -> None:
+        if isinstance(value, (list, tuple)):
+            value = json.dumps(list(value))
+        elif isinstance(value, bool):
+            value = "1" if value else "0"
+        check(lib().XGBoosterSetParam(self.handle, key.encode(), str(value).encode()))
+
+    def update(self, dtrain: DMatrix, iteration: int) -> None:
+        check(lib().XGBoosterUpdateOneIter(self.handle, iteration, dtrain.handle))
+
+    def boosted_rounds(self) -> int:
+        n = C.c_int()
+        check(lib().XGBoosterBoostedRounds(self.handle, C.byref(n)))
+        return n.value
+
+    def save_config(self) -> dict:
+        n = C.c_uint64()
+        p = C.c_char_p()
+        check(lib().XGBoosterSaveJsonConfig(self.handle, C.byref(n), C.byref(p)))
+        return json.loads(C.string_at(p, n.value).decode())
+
+    def save_raw(self) -> bytes:
+        n = C.c_uint64()
+        p = C.c_void_p()
+        check(lib().XGBoosterSaveModelToBuffer(self.handle, b'{"format":"json"}', C.byref(n), C.byref(p)))
+        return C.string_at(p, n.value)
+
+    def save_model(self, path: str) -> None:
+        check(lib().XGBoosterSaveModel(self.handle, str(path).encode()))
+
+    def load_raw(self, raw: bytes) -> None:
+        check(lib().XGBoosterLoadModelFromBuffer(self.handle, raw, len(raw)))
+
+    def load_model(self, path: str) -> None:
+        check(lib().XGBoosterLoadModel(self.handle, str(path).encode()))
+
+    def slice(self, begin: int, end: int, step: int = 1) -> "Booster":
+        out = C.c_void_p()
+        check(lib().XGBoosterSlice(self.handle, begin, end, step, C.byref(out)))
+        return Booster(handle=out)
+
+    def num_features(self) -> int:
+        n = C.c_uint64()
+        check(lib().XGBoosterGetNumFeature(self.handle, C.byref(n)))
+        return n.value
+
+    def set_comm(self, comm: "Comm") -> None:
+        check(lib().dp_booster_set_comm(self.handle, comm.handle))
+
+    def set_profiling(self, on: bool) -> None:
+        check(lib().dp_booster_set_profiling(self.handle, int(on)))
+
+    def profile(self) -> dict:
+        p = C.c_char_p()
+        check(lib().dp_booster_profile(self.handle, C.byref(p)))
+        return json.loads(p.value.decode())
+
+    def margins(self, rows: int, outputs: int):
+        import numpy as np
+        out = np.zeros((rows, outputs), np.float32)
+        check(lib().dp_booster_margins(self.handle, out.ctypes.data, out.size))
+        return out
+
+    def trees(self) -> list[dict]:
+        return json.loads(self.save_raw())["learner"]["gradient_booster"]["model"]["trees"]
+
+    def free(self) -> None:
+        if self.handle:
+            check(lib().XGBoosterFree(self.handle))
+            self.handle = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+class Comm:
+    """NCCL communicator for row-sharded training (one process per GPU)."""
+
+    @staticmethod
+    def unique_id() -> bytes:
+        buf = C.create_string_buffer(128)
+        check(lib().dp_comm_unique_id(buf))
+        return buf.raw
+
+    def __init__(self, unique_id: bytes, nranks: int, rank: int, device: int):
+        assert len(unique_id) == 128
+        self.handle = C.c_void_p()
+        check(lib().dp_comm_create(unique_id, nranks, rank, device, C.byref(self.handle)))
+
+    def free(self) -> None:
+        if self.handle:
+            check(lib().dp_comm_free(self.handle))
+            self.handle = C.c_void_p()
+
+
+def train(params: dict, dtrain: DMatrix, rounds: int, comm: Comm | None = None) -> Booster:
+    """The reference's sequence: create, set params, one UpdateOneIter per round."""
+    b = Booster(params, [dtrain])
+    if comm is not None:
+        b.set_comm(comm)
+    for i in range(rounds):
+        b.update(dtrain, i)
+    return b

@@ -1,0 +1,157 @@
+/* libdp_gbdt -- B200 (sm_100a) gradient-boosted-tree training behind the
+ * XGBoost 3.4.1 C-API subset that the decision-programs trainer binds with
+ * dlopen/dlsym (native/class_model_native_adapter.cuh:20-31).
+ *
+ * Conventions (as the reference expects them):
+ *  - every int-returning call returns 0 on success and -1 on failure; the
+ *    message is then available from XGBGetLastError() (thread-local)
+ *    (native/class_model_native_adapter.cuh:23);
+ *  - handles are opaque; string / array outputs are borrowed and stay valid
+ *    until the next call on the same handle (native/class_study_train.hpp:63-64);
+ *  - matrices borrow the caller's CUDA fp32 memory, which must outlive the
+ *    DMatrix (native/class_study_oof.cu:532-534);
+ *  - training runs on the device that holds the matrix; there is no CPU path.
+ */
+#ifndef DP_GBDT_H_
+#define DP_GBDT_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DP_API __attribute__((visibility("default")))
+
+typedef void* DMatrixHandle;
+typedef void* BoosterHandle;
+typedef uint64_t bst_ulong;
+
+/* ---- XGBoost C-API subset ------------------------------------------------ */
+
+/* Reports 3,4,1 for ABI compatibility; the reference refuses any other
+ * version (native/class_model_native_adapter.cuh:24). */
+DP_API void XGBoostVersion(int* major, int* minor, int* patch);
+
+/* JSON with "USE_CUDA":true (checked at native/class_model_native_adapter.cuh:24)
+ * and "DP_B200_GBDT":true identifying this implementation. */
+DP_API int XGBuildInfo(const char** out);
+
+/* Thread-local message of the last failure (native/class_model_native_adapter.cuh:21,23). */
+DP_API const char* XGBGetLastError(void);
+
+/* Dense fp32 CUDA matrix from a __cuda_array_interface__ JSON object
+ * {"data":[ptr,ro],"shape":[R,F],"strides":null|[bytes,4],"typestr":"<f4",...}
+ * and config {"missing":NaN|value,"nthread":n}.  Rejects +-inf.
+ * Replaces native/class_native_training.cuh:51 (array JSON built at
+ * native/class_model_native_adapter.cuh:26). */
+DP_API int XGDMatrixCreateFromCudaArrayInterface(const char* data, const char* config, DMatrixHandle* out);
+
+/* field "label": f32 [R] array interface (device or host memory); copied.
+ * Replaces native/class_native_training.cuh:52. */
+DP_API int XGDMatrixSetInfoFromInterface(DMatrixHandle handle, const char* field, const char* data);
+
+/* field "label" from host memory (XGBoost C API; used by host-side callers). */
+DP_API int XGDMatrixSetFloatInfo(DMatrixHandle handle, const char* field, const float* data, bst_ulong len);
+
+DP_API int XGDMatrixNumRow(DMatrixHandle handle, bst_ulong* out);
+DP_API int XGDMatrixNumCol(DMatrixHandle handle, bst_ulong* out);
+
+/* Replaces the free calls at native/class_model_native_adapter.cuh:21,25. */
+DP_API int XGDMatrixFree(DMatrixHandle handle);
+
+/* native/class_native_training.cuh:56 (with the training matrix) and
+ * native/class_study_train.cu:98 (with nullptr, 0). */
+DP_API int XGBoosterCreate(const DMatrixHandle dmats[], bst_ulong len, BoosterHandle* out);
+DP_API int XGBoosterFree(BoosterHandle handle);
+
+/* Parameters as the reference sets them (native/class_native_training.cuh:57-65,
+ * native/class_model_native_adapter.cuh:27): objective in {multi:softmax,
+ * multi:softprob, binary:logistic, reg:squarederror}, num_class, max_depth,
+ * max_bin, eta, lambda, alpha, gamma, min_child_weight, subsample,
+ * colsample_*, base_score (scalar or JSON array), seed, device "cuda:N",
+ * tree_method "hist"; bookkeeping keys (nthread, verbosity, ...) are accepted. */
+DP_API int XGBoosterSetParam(BoosterHandle handle, const char* name, const char* value);
+
+/* One boosting round (K trees for K-class objectives); synchronous.
+ * The hot path: replaces native/class_native_training.cuh:67. */
+DP_API int XGBoosterUpdateOneIter(BoosterHandle handle, int iter, DMatrixHandle dtrain);
+
+/* native/class_model_train.cu:49, native/class_study_train.cu:104,127,328. */
+DP_API int XGBoosterBoostedRounds(BoosterHandle handle, int* out);
+
+/* Configuration JSON; learner.generic_param.device == "cuda:N" and
+ * learner.gradient_booster.updater[0].name == "grow_gpu_hist" as checked at
+ * native/class_model_train.cu:48 and native/class_study_train.cu:327.
+ * Replaces native/class_native_training.cuh:68. */
+DP_API int XGBoosterSaveJsonConfig(BoosterHandle handle, bst_ulong* out_len, const char** out);
+
+/* XGBoost-3.4.1-schema JSON model (".json" paths only).
+ * Replaces native/class_native_training.cuh:69. */
+DP_API int XGBoosterSaveModel(BoosterHandle handle, const char* fname);
+
+/* config {"format":"json"}; replaces native/class_study_train.cu:329,363. */
+DP_API int XGBoosterSaveModelToBuffer(BoosterHandle handle, const char* config, bst_ulong* out_len,
+                                      const char** out);
+
+/* native/class_study_train.cu:101 and native/class_model_native_adapter.cuh:29. */
+DP_API int XGBoosterLoadModelFromBuffer(BoosterHandle handle, const void* buf, bst_ulong len);
+DP_API int XGBoosterLoadModel(BoosterHandle handle, const char* fname);
+
+/* Rounds [begin, end) with step; end == 0 means all rounds.
+ * native/class_study_train.cu:130,355. */
+DP_API int XGBoosterSlice(BoosterHandle handle, int begin_layer, int end_layer, int step, BoosterHandle* out);
+
+/* native/class_model_convert.cpp:112. */
+DP_API int XGBoosterGetNumFeature(BoosterHandle handle, bst_ulong* out);
+
+/* ---- extensions (no counterpart in the reference, which is single-GPU) --- */
+
+/* Multi-GPU: rank 0 creates a 128-byte NCCL unique id, every rank creates a
+ * communicator with it and attaches it to its booster before the first
+ * round.  Rows are sharded across ranks; trees are identical on every rank. */
+DP_API int dp_comm_unique_id(void* out128);
+DP_API int dp_comm_create(const void* unique_id128, int nranks, int rank, int device, void** out);
+DP_API int dp_comm_free(void* comm);
+DP_API int dp_booster_set_comm(BoosterHandle handle, void* comm);
+
+/* Per-kernel CUDA-event timings of the training rounds ({"name":{"launches",
+ * "ms","alg_bytes"}}), collected on the launching stream while enabled. */
+DP_API int dp_booster_set_profiling(BoosterHandle handle, int on);
+DP_API int dp_booster_profile(BoosterHandle handle, const char** out_json);
+
+/* Training margins [R][K] of the booster's training matrix (host copy). */
+DP_API int dp_booster_margins(BoosterHandle handle, float* out, bst_ulong len);
+
+/* Number of CUDA kernels this library has launched in the process. */
+DP_API uint64_t dp_launch_count(void);
+
+/* ---- kernel-level entry points (device pointers; stream may be NULL) ----- */
+
+/* Exact quantile cuts: cut[F][256], nbins[F], has_missing[F]. */
+DP_API int dp_quantile_cuts(const float* x, uint64_t rows, uint32_t features, uint64_t row_stride, int max_bin,
+                            float* cut, uint16_t* nbins, uint8_t* has_missing, void* stream);
+/* bins[R][bin_stride] (bin_stride >= features, multiple of 16). */
+DP_API int dp_bin_matrix(const float* x, uint64_t rows, uint32_t features, uint64_t row_stride, const float* cut,
+                         const uint16_t* nbins, uint8_t* bins, uint64_t bin_stride, void* stream);
+/* gh[K][R][2] and per-class quantiser scales scales[K][2] (sg, sh; device). */
+DP_API int dp_gradients(int objective, int num_class, const float* margin, const float* label, uint64_t rows,
+                        float* gh, float* scales, void* stream);
+/* hist[nseg][F][256][2] (int64, overwritten) of position segments
+ * [seg_begin[i], seg_end[i]) (host arrays) of (ridx, gh) in position order. */
+DP_API int dp_hist_build(const uint8_t* bins, uint64_t bin_stride, uint32_t features, const float* gh,
+                         const uint32_t* ridx, const int64_t* seg_begin, const int64_t* seg_end, int32_t nseg,
+                         float sg, float sh, int64_t* hist, void* stream);
+/* Best split per node from hist[N][F][256][2] (device) and quantised totals
+ * totals[N][2] (host); outputs on the host: out_i[N][4] = feature, bin,
+ * default_left, valid; out_gain[N]; out_left[N][2]. */
+DP_API int dp_eval_splits(const int64_t* hist, int32_t nnodes, uint32_t features, const uint16_t* nbins,
+                          const uint8_t* has_missing, const int64_t* totals, float sg, float sh, double lambda,
+                          double alpha, double gamma, double min_child_weight, int32_t* out_i, double* out_gain,
+                          int64_t* out_left);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DP_GBDT_H_ */

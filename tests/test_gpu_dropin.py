@@ -1,0 +1,71 @@
+"""Drop-in check: the reference's own FIT-only trainer (native/class_model_train.cu,
+compiled unmodified from the reference sources into oracle/_ref/) binds
+libdp_gbdt.so through its plan's native_library_path, trains, and its own
+checks pass: the CUDA updater and device (native/class_model_train.cu:48),
+the completed round count (:49), the saved objective and shape (:50-51).  The
+model it writes must equal the oracle's trees for the same inputs."""
+import hashlib
+import json
+import pathlib
+import subprocess
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+ROOT = pathlib.Path(__file__).resolve().parents[1]
+TRAINER = ROOT / "oracle" / "_ref" / "class_model_train"
+LIB = ROOT / "decision-programs_b200" / "libdp_gbdt.so"
+
+
+def sha(p: pathlib.Path) -> str:
+    return hashlib.sha256(p.read_bytes()).hexdigest()
+
+
+@pytest.mark.skipif(not TRAINER.exists(), reason="reference trainer not built (needs the reference sources)")
+def test_reference_trainer_runs_on_libdp_gbdt(orc, tmp_path):
+    rng = np.random.default_rng(21)
+    R, F, K = 3000, 6, 3
+    x = rng.standard_normal((R, F)).astype(np.float32)
+    x[rng.random((R, F)) < 0.05] = np.nan
+    y = np.argmax(np.nan_to_num(x[:, :3]) + 0.3 * rng.standard_normal((R, 3)), 1).astype(np.uint32)
+    values, labels = tmp_path / "values.fp32", tmp_path / "labels.u32"
+    values.write_bytes(x.astype("<f4").tobytes())
+    labels.write_bytes(y.astype("<u4").tobytes())
+    manifest = json.loads(subprocess.run([str(TRAINER), "source-manifest"], check=True, capture_output=True,
+                                         text=True).stdout)
+    hp = {"rounds": 4, "max_depth": 3, "eta": 0.3, "max_bin": 256, "lambda": 1.0, "min_child_weight": 1.0}
+    plan = {
+        "format": "class-model-training-plan-1", "TEST_read": False, "VALID_read": False,
+        "selection_performed": False, "training_performed": True,
+        "dataset": {"format": "dense-fp32-u32-class-labels-1", "TEST_read": False, "features": F, "classes": K,
+                    "rows": R, "row_stride": F, "FIT_rows": R, "VALID_rows": 0, "preprocessing": "seeded synthetic",
+                    "values_path": str(values), "labels_path": str(labels), "values_sha256": sha(values),
+                    "labels_sha256": sha(labels)},
+        "hyperparameters": hp,
+        "native_library_path": str(LIB), "native_library_sha256": sha(LIB),
+        "executable_sha256": sha(TRAINER), "source_manifest_sha256": manifest["sha256"],
+    }
+    plan_path = tmp_path / "plan.json"
+    plan_path.write_text(json.dumps(plan))
+    out = tmp_path / "out"
+    r = subprocess.run([str(TRAINER), "fit", str(plan_path), sha(plan_path), str(out)], capture_output=True,
+                       text=True, timeout=300)
+    assert r.returncode == 0, r.stderr + r.stdout
+    result = json.loads((out / "result.json").read_text())
+    assert result["complete"] and result["CUDA_executed"] and result["native_objective"] == "multi:softmax"
+    cfg = json.loads((out / "configuration.json").read_text())
+    assert cfg["learner"]["gradient_booster"]["updater"][0]["name"] == "grow_gpu_hist"
+    model = json.loads((out / "model.json").read_text())
+    trees = model["learner"]["gradient_booster"]["model"]["trees"]
+    o = orc.Model(x, y.astype(np.float32), "multi:softmax", num_class=K, max_depth=3, max_bin=256, eta=0.3,
+                  rounds=4, threads=4)
+    assert len(trees) == o.num_trees() == 4 * K
+    for i, t in enumerate(trees):
+        ot = o.tree(i)
+        for f in ["left_children", "right_children", "split_indices"]:
+            np.testing.assert_array_equal(np.array(t[f]), ot[f])
+        np.testing.assert_array_equal(np.array(t["default_left"], np.uint8), ot["default_left"])
+        np.testing.assert_array_equal(np.array(t["split_conditions"], np.float32).view(np.uint32),
+                                      ot["split_conditions"].view(np.uint32))

@@ -1,0 +1,146 @@
+"""End-to-end parity: trees grown through the XGBoost C-API subset
+(XGBoosterUpdateOneIter, the call at native/class_native_training.cuh:67)
+against the CPU oracle on the same seeded inputs.  Trees must be identical
+field by field (structure, split features, fp32 thresholds, default
+directions, leaf values, gains, hessian sums) and so must the training
+margins."""
+import json
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+FIELDS_EXACT = ["left_children", "right_children", "split_indices", "default_left"]
+FIELDS_F32 = ["split_conditions", "base_weights", "loss_changes", "sum_hessian"]
+
+
+def cuda(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def compare_models(b, o, K):
+    trees = b.trees()
+    assert len(trees) == o.num_trees()
+    for i, t in enumerate(trees):
+        ot = o.tree(i)
+        for f in FIELDS_EXACT:
+            np.testing.assert_array_equal(np.array(t[f], np.int64), ot[f].astype(np.int64), err_msg=f"tree {i} {f}")
+        for f in FIELDS_F32:
+            got = np.array(t[f], np.float32)
+            np.testing.assert_array_equal(got.view(np.uint32), ot[f].view(np.uint32), err_msg=f"tree {i} {f}")
+    return trees
+
+
+def run(dp, orc, x, y, objective, rounds, K=1, **hp):
+    params = {"objective": objective, "tree_method": "hist", "device": "cuda:0", "max_depth": hp.get("max_depth", 6),
+              "max_bin": hp.get("max_bin", 256), "eta": hp.get("eta", 0.3), "lambda": hp.get("reg_lambda", 1.0),
+              "alpha": hp.get("alpha", 0.0), "gamma": hp.get("gamma", 0.0),
+              "min_child_weight": hp.get("min_child_weight", 1.0)}
+    if objective.startswith("multi:"):
+        params["num_class"] = K
+    d = dp.DMatrix.from_torch(cuda(x), cuda(y))
+    b = dp.train(params, d, rounds)
+    assert b.boosted_rounds() == rounds
+    o = orc.Model(x, y, objective, num_class=K, max_depth=params["max_depth"], max_bin=params["max_bin"],
+                  eta=params["eta"], reg_lambda=params["lambda"], alpha=params["alpha"], gamma=params["gamma"],
+                  min_child_weight=params["min_child_weight"], rounds=rounds, threads=8)
+    trees = compare_models(b, o, K)
+    R = x.shape[0]
+    np.testing.assert_array_equal(b.margins(R, K).view(np.uint32), o.margins().view(np.uint32))
+    return b, o, trees
+
+
+def c1_data(R=20000, seed=0):
+    """x ~ N(0,1) 16 features; y = 1[x0 + 0.5 x1 x2 + N(0, 0.3) > 0]."""
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((R, 16), dtype=np.float32)
+    y = (x[:, 0] + 0.5 * x[:, 1] * x[:, 2] + rng.normal(0, 0.3, R) > 0).astype(np.float32)
+    return x, y
+
+
+def test_config1_binary_logistic_full_size(dp, orc):
+    x, y = c1_data()
+    b, o, trees = run(dp, orc, x, y, "binary:logistic", 20, max_depth=4)
+    assert len(trees) == 20 and all(len(t["left_children"]) <= 31 for t in trees)
+    m = b.margins(len(y), 1)[:, 0]
+    assert ((m > 0) == (y > 0.5)).mean() > 0.85
+
+
+def test_squared_error_with_missing_values(dp, orc):
+    rng = np.random.default_rng(3)
+    R, F = 6000, 10
+    x = rng.standard_normal((R, F)).astype(np.float32)
+    y = (np.sin(x[:, 0]) + x[:, 1] ** 2 + 0.1 * rng.standard_normal(R)).astype(np.float32)
+    x[rng.random((R, F)) < 0.2] = np.nan
+    run(dp, orc, x, y, "reg:squarederror", 6, max_depth=5)
+
+
+@pytest.mark.parametrize("objective", ["multi:softprob", "multi:softmax"])
+def test_multiclass(dp, orc, objective):
+    rng = np.random.default_rng(4)
+    R, F, K = 4000, 30, 5
+    x = rng.standard_normal((R, F)).astype(np.float32)
+    w = rng.standard_normal((F, K))
+    y = np.argmax(x @ w, 1).astype(np.float32)
+    b, o, trees = run(dp, orc, x, y, objective, 3, K=K, max_depth=4)
+    assert [t["id"] for t in trees] == list(range(15))
+    doc = json.loads(b.save_raw())
+    assert doc["learner"]["gradient_booster"]["model"]["tree_info"] == [0, 1, 2, 3, 4] * 3
+    assert doc["learner"]["gradient_booster"]["model"]["iteration_indptr"] == [0, 5, 10, 15]
+
+
+def test_config3_shape_uint8_sparse_multiclass(dp, orc):
+    """BASELINE config 3 shape, scaled down: 784 uint8 features, 80% zeros, 10 classes."""
+    rng = np.random.default_rng(5)
+    R, F, K = 3000, 784, 10
+    x = np.where(rng.random((R, F)) < 0.8, 0, rng.integers(1, 256, (R, F))).astype(np.float32)
+    y = np.argmax(x @ rng.standard_normal((F, K)), 1).astype(np.float32)
+    run(dp, orc, x, y, "multi:softprob", 2, K=K, max_depth=3)
+
+
+@pytest.mark.parametrize("hp", [dict(alpha=0.5, gamma=1.0, min_child_weight=5.0, reg_lambda=2.0),
+                                dict(max_bin=16, max_depth=7), dict(eta=1.0, reg_lambda=0.0, min_child_weight=0.0),
+                                dict(max_depth=10)])
+def test_regularisation_and_shapes(dp, orc, hp):
+    x, y = c1_data(8000, seed=9)
+    run(dp, orc, x, y, "binary:logistic", 4, **hp)
+
+
+@pytest.mark.parametrize("R", [1, 2, 7, 33])
+def test_tiny_inputs(dp, orc, R):
+    rng = np.random.default_rng(R)
+    x = rng.standard_normal((R, 3)).astype(np.float32)
+    y = rng.standard_normal(R).astype(np.float32)
+    run(dp, orc, x, y, "reg:squarederror", 3, max_depth=4, min_child_weight=0.0)
+
+
+def test_config_reports_cuda_updater_and_model_reloads(dp, orc, tmp_path):
+    x, y = c1_data(3000, seed=2)
+    b, o, _ = run(dp, orc, x, y, "binary:logistic", 3, max_depth=3)
+    cfg = b.save_config()
+    assert cfg["learner"]["generic_param"]["device"] == "cuda:0"
+    assert cfg["learner"]["gradient_booster"]["updater"][0]["name"] == "grow_gpu_hist"
+    p = tmp_path / "model.json"
+    b.save_model(str(p))
+    raw = p.read_bytes()
+    assert raw == b.save_raw()
+    c = dp.Booster()
+    c.load_model(str(p))
+    assert c.save_raw() == raw
+    s = b.slice(0, 2)
+    assert s.boosted_rounds() == 2 and s.trees() == b.trees()[:2]
+
+
+def test_bad_labels_and_inf_are_refused(dp):
+    x = np.zeros((10, 2), np.float32)
+    y = np.full(10, 2.0, np.float32)
+    d = dp.DMatrix.from_torch(cuda(x), cuda(y))
+    b = dp.Booster({"objective": "binary:logistic"})
+    with pytest.raises(dp.DPError, match="label"):
+        b.update(d, 0)
+    x[3, 1] = np.inf
+    with pytest.raises(dp.DPError, match="inf"):
+        dp.DMatrix.from_torch(cuda(x), cuda(y))
