@@ -1,0 +1,401 @@
+"""Benchmark of the GBDT-training hot path (BASELINE config 4 as the step).
+
+A step is one boosting round of squared-error regression (one depth-10 tree)
+over 10,000,000 rows x 128 fp32 features binned to 256 uint8 bins, rows
+sharded over the ranks (strong scaling: the total row count is fixed).  The
+target is a seeded random depth-6, 20-tree ensemble plus N(0, 0.1) noise.
+Data is synthetic (seeded) with BASELINE's shapes and distributions.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+value    rows*trees/s of the timed rounds, inputs resident in HBM (device
+         events around the rounds, max over ranks).
+e2e      the same metric through the C-ABI with host inputs: pinned-host
+         fp32 matrix and labels copied to the device, DMatrix creation (cuts
+         and bins), W+K rounds, the model read back as JSON.
+roofline histogram kernel: algorithmic bytes rows*(F + 12) + slots*F*256*16
+         per launch over its CUDA-event duration on the library stream.
+The reference arm (--impl reference) times the CPU oracle: the reference
+repository trains only through an external GPU library that is absent here,
+so the restatement of the same algorithm is the CPU implementation of the path.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import pathlib
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = pathlib.Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "decision-programs_b200"))
+
+ROWS = 10_000_000
+FEATURES = 128
+DEPTH = 10
+CHUNK = 250_000           # generation unit; the dataset does not depend on the rank count
+SEED = 20240601
+PARAMS = {"objective": "reg:squarederror", "tree_method": "hist", "max_depth": DEPTH, "max_bin": 256, "eta": 0.3,
+          "lambda": 1.0, "min_child_weight": 1.0}
+WORKLOAD = "config4: reg:squarederror 10M x 128 fp32 -> 256 uint8 bins, depth 10, one tree per step"
+
+
+def measured_peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return json.loads(p.read_text())
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "fallback": True}
+
+
+# --------------------------------------------------------------------------- data
+def teacher(seed: int = SEED):
+    """Random depth-6 x 20-tree ensemble: feature, threshold per internal node,
+    value per leaf."""
+    rs = np.random.RandomState(seed)
+    feats = rs.randint(0, FEATURES, (20, 63))
+    thr = rs.normal(0.0, 0.7, (20, 63)).astype(np.float32)
+    leaf = rs.normal(0.0, 1.0, (20, 64)).astype(np.float32)
+    return feats, thr, leaf
+
+
+def make_chunk(torch, c: int, device):
+    g = torch.Generator(device=device)
+    g.manual_seed(SEED * 1000 + c)
+    x = torch.randn((CHUNK, FEATURES), device=device, generator=g, dtype=torch.float32)
+    feats, thr, leaf = (torch.from_numpy(a).to(device) for a in teacher())
+    y = torch.zeros(CHUNK, device=device)
+    for t in range(20):
+        idx = torch.zeros(CHUNK, dtype=torch.long, device=device)
+        for _ in range(6):
+            f = feats[t][idx]
+            go = (x.gather(1, f[:, None])[:, 0] >= thr[t][idx]).long()
+            idx = 2 * idx + 1 + go
+        y += leaf[t][idx - 63]
+    y += 0.1 * torch.randn(CHUNK, device=device, generator=g)
+    return x, y
+
+
+def shard(torch, rank: int, world: int, device):
+    nchunks = ROWS // CHUNK
+    mine = [c for c in range(nchunks) if c * world // nchunks == rank]
+    xs, ys = zip(*(make_chunk(torch, c, device) for c in mine))
+    return torch.cat(xs).contiguous(), torch.cat(ys).contiguous()
+
+
+# --------------------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.dev = device_index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.dev), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# --------------------------------------------------------------------------- reference / CPU arm
+def cpu_oracle_run(rows: int, trees: int, threads: int) -> dict:
+    """Oracle (CPU restatement) on the first `rows` rows of the workload."""
+    import torch
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import oracle
+    nchunks = (rows + CHUNK - 1) // CHUNK
+    xs, ys = zip(*(make_chunk(torch, c, "cpu") for c in range(nchunks)))
+    x = torch.cat(xs)[:rows].numpy()
+    y = torch.cat(ys)[:rows].numpy()
+    m = oracle.Model(x, y, "reg:squarederror", max_depth=DEPTH, max_bin=256, eta=0.3, rounds=0, threads=threads)
+    t0 = time.perf_counter()
+    m.train_more(trees)
+    dt = time.perf_counter() - t0
+    return {"value": rows * trees / dt, "seconds": dt, "rows": rows, "trees": trees}
+
+
+def reference_arm(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = len(os.sched_getaffinity(0))
+    rows = 1_000_000
+    steps = []
+    for _ in range(args.warmup):
+        cpu_oracle_run(rows, 1, threads)
+    for _ in range(args.steps):
+        steps.append(cpu_oracle_run(rows, 1, threads)["value"])
+    value = statistics.median(steps)
+    line = {
+        "impl": "reference", "metric": "boosting rows*trees/s (config 4 step, 1 tree)", "value": value,
+        "unit": "rows*trees/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "u8 bins / int64 sums",
+        "data": "synthetic (seeded)", "config": {"workload": WORKLOAD, "rows": ROWS, "features": FEATURES},
+        "cpu_baseline": {"value": value, "unit": "rows*trees/s", "cores": threads, "kind": "port",
+                         "sample": f"first {rows} rows of the config-4 data, one depth-10 tree per step "
+                                   f"(C++ oracle, {threads} threads)"},
+        "e2e": {"value": value, "unit": "rows*trees/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------------------- histogram sweep (config 5)
+def hist_sweep(torch, dp, device, peak_gbs: float) -> list[dict]:
+    R, F = 100_000_000, 32
+    out = []
+    g = torch.Generator(device=device)
+    g.manual_seed(SEED + 5)
+    gh = torch.stack([torch.randn(R, device=device, generator=g), torch.rand(R, device=device, generator=g)],
+                     1).contiguous()
+    for B in (16, 64, 256):
+        bins = torch.randint(0, B, (R, F), dtype=torch.uint8, device=device, generator=g)
+        for N in (1, 8, 64, 1024):
+            node = torch.randint(0, N, (R,), device=device, generator=g)
+            ridx = torch.argsort(node, stable=True).to(torch.int32)
+            ghp = gh[ridx.long()].contiguous()
+            counts = torch.bincount(node, minlength=N).cpu().numpy()
+            del node
+            edges = np.concatenate([[0], np.cumsum(counts)]).astype(np.int64)
+            sb, se = np.ascontiguousarray(edges[:-1]), np.ascontiguousarray(edges[1:])
+            hist = torch.empty((N, F, 256, 2), dtype=torch.int64, device=device)
+            plan = dp.ctypes_void_p()
+            dp.check(dp.lib().dp_hist_prepare(bins.data_ptr(), F, F, B, ghp.data_ptr(), ridx.data_ptr(), sb.ctypes.data,
+                                              se.ctypes.data, N, 2.0 ** 15, 2.0 ** 16, hist.data_ptr(),
+                                              dp.C.byref(plan)))
+            stream = torch.cuda.current_stream()
+            for _ in range(3):
+                dp.check(dp.lib().dp_hist_run(plan, stream.cuda_stream))
+            ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            reps = 5
+            torch.cuda.synchronize()
+            ev0.record()
+            for _ in range(reps):
+                dp.check(dp.lib().dp_hist_run(plan, stream.cuda_stream))
+            ev1.record()
+            torch.cuda.synchronize()
+            ms = ev0.elapsed_time(ev1) / reps
+            dp.check(dp.lib().dp_hist_free(plan))
+            alg = R * (F + 12) + N * F * 256 * 16
+            out.append({"bins": B, "nodes": N, "ms": round(ms, 4), "GB/s": round(alg / ms / 1e6, 1),
+                        "frac_hbm": round(alg / ms / 1e6 / peak_gbs, 3),
+                        "rows_features_per_s": R * F / (ms / 1e3)})
+            del ridx, ghp, hist
+        del bins
+    del gh
+    torch.cuda.empty_cache()
+    return out
+
+
+# --------------------------------------------------------------------------- main GPU arm
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200")
+    ap.add_argument("--no-sweep", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        reference_arm(args)
+        return
+    assert args.warmup >= 3, "at least 3 warm-up rounds"
+
+    import torch
+    import torch.distributed as dist
+
+    import dp_gbdt as dp
+    import ctypes
+    dp.C = ctypes
+    dp.ctypes_void_p = ctypes.c_void_p
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    assert world == args.gpus, f"--gpus {args.gpus} but WORLD_SIZE={world}"
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=device)
+    peaks = measured_peaks()
+    peak_gbs = float(peaks["hbm_gbs"])
+
+    x, y = shard(torch, rank, world, device)
+    rows_local = x.shape[0]
+    comm = None
+    if world > 1:
+        uid = torch.zeros(128, dtype=torch.uint8, device=device)
+        if rank == 0:
+            uid.copy_(torch.frombuffer(bytearray(dp.Comm.unique_id()), dtype=torch.uint8))
+        dist.broadcast(uid, 0)
+        comm = dp.Comm(bytes(uid.cpu().numpy().tobytes()), world, rank, local)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- device-resident timing
+    d = dp.DMatrix.from_torch(x, y)
+    b = dp.Booster(PARAMS | {"device": f"cuda:{local}"}, [d])
+    if comm is not None:
+        b.set_comm(comm)
+    for i in range(args.warmup):
+        b.update(d, i)
+    b.set_profiling(True)
+    clocks = ClockSampler(local)
+    barrier()
+    launches0 = dp.launch_count()
+    clocks.start()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for i in range(args.steps):
+        b.update(d, args.warmup + i)
+    ev1.record()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    launches = dp.launch_count() - launches0
+    ms_local = ev0.elapsed_time(ev1)
+    barrier()
+    ms = max_over_ranks(ms_local)
+    prof = b.profile()
+    value = ROWS * args.steps / (ms / 1e3)
+    hist = prof.get("histograms", {"launches": 0, "ms": 0.0, "alg_bytes": 0.0})
+    hist_ms_per_launch = hist["ms"] / max(1, hist["launches"])
+    achieved = hist["alg_bytes"] / max(1, hist["launches"]) / (hist_ms_per_launch / 1e3) / 1e9 if hist["ms"] else 0.0
+    traffic = None
+    tfile = ROOT / "profiles" / "hist_traffic.json"
+    if tfile.exists():
+        traffic = json.loads(tfile.read_text()).get("bytes_per_launch_config4")
+    model_bytes = len(b.save_raw())
+    b.free()
+    d.free()
+
+    # ---- end to end through the C-ABI with host buffers
+    xh = torch.empty_like(x, device="cpu").pin_memory()
+    yh = torch.empty_like(y, device="cpu").pin_memory()
+    xh.copy_(x)
+    yh.copy_(y)
+    xd, yd = torch.empty_like(x), torch.empty_like(y)
+    del x, y
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    xd.copy_(xh, non_blocking=True)
+    yd.copy_(yh, non_blocking=True)
+    torch.cuda.synchronize()
+    d2 = dp.DMatrix.from_torch(xd, yd)
+    b2 = dp.Booster(PARAMS | {"device": f"cuda:{local}"}, [d2])
+    if comm is not None:
+        b2.set_comm(comm)
+    rounds_e2e = args.warmup + args.steps
+    for i in range(rounds_e2e):
+        b2.update(d2, i)
+    raw = b2.save_raw()
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1))
+    e2e_value = ROWS * rounds_e2e / (e2e_ms / 1e3)
+    b2.free()
+    d2.free()
+    del xd, yd, xh, yh
+    torch.cuda.empty_cache()
+
+    sweep = None
+    cpu = None
+    if rank == 0 and world == 1:
+        if not args.no_sweep:
+            sweep = hist_sweep(torch, dp, device, peak_gbs)
+        if not args.no_cpu:
+            threads = len(os.sched_getaffinity(0))
+            r = cpu_oracle_run(500_000, 1, threads)
+            cpu = {"value": r["value"], "unit": "rows*trees/s", "cores": threads, "kind": "port",
+                   "sample": f"first 500000 rows of the config-4 data, one depth-10 tree "
+                             f"(C++ oracle, {threads} threads, {r['seconds']:.1f} s)"}
+    if comm is not None:
+        comm.free()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    line = {
+        "metric": "boosting rows*trees/s (config 4 step, 1 tree)", "value": value, "unit": "rows*trees/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "u8 bins / int64 sums",
+        "data": "synthetic (seeded), inputs larger than L2",
+        "config": {"workload": WORKLOAD, "rows": ROWS, "features": FEATURES, "max_depth": DEPTH, "max_bin": 256,
+                   "parallelism": f"rows sharded over {world} GPU(s)", "l2": "inputs (1.28 GB bins) exceed L2"},
+        "e2e": {"value": e2e_value, "unit": "rows*trees/s",
+                "h2d_bytes_per_step": int(ROWS * (FEATURES + 1) * 4 / rounds_e2e),
+                "d2h_bytes_per_step": int(len(raw) * world / rounds_e2e),
+                "note": f"host fp32 inputs -> DMatrix (cuts+bins) -> {rounds_e2e} rounds -> JSON model"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak_gbs, "unit": "GB/s",
+                     "frac": achieved / peak_gbs, "traffic": traffic, "kernel": "k_hist",
+                     "peak_source": "measured" if not peaks.get("fallback") else "fallback",
+                     "launches": hist["launches"], "ms_per_launch": hist_ms_per_launch},
+        "gpu_launches": launches,
+        "clocks": clk,
+        "kernel_profile": prof,
+        "model_bytes": model_bytes,
+    }
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    if sweep is not None:
+        line["hist_sweep"] = sweep
+    print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

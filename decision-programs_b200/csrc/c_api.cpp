@@ -384,37 +384,116 @@ int dp_gradients(int objective, int num_class, const float* margin, const float*
   DP_API_END();
 }
 
-int dp_hist_build(const uint8_t* bins, uint64_t bin_stride, uint32_t features, const float* gh, const uint32_t* ridx,
-                  const int64_t* seg_begin, const int64_t* seg_end, int32_t nseg, float sg, float sh, int64_t* hist,
-                  void* stream) {
-  DP_API_BEGIN();
+}  // extern "C"
+
+namespace {
+
+// Task list and device descriptors of one histogram build.
+struct HistPlan {
+  const uint8_t* bins = nullptr;
+  uint64_t bin_stride = 0;
+  uint32_t features = 0;
+  int num_bins = 256;
+  int64_t* hist = nullptr;
+  int32_t nseg = 0;
+  dp::u32 ntasks = 0;
+  dp::DevBuf<dp::HistTask> tasks;
+  dp::DevBuf<dp::TreeArrays> trees;
+  dp::DevBuf<dp::Scales> scales;
+  int device = 0;
+};
+
+HistPlan* make_hist_plan(const uint8_t* bins, uint64_t bin_stride, uint32_t features, int32_t num_bins,
+                         const float* gh, const uint32_t* ridx, const int64_t* seg_begin, const int64_t* seg_end,
+                         int32_t nseg, float sg, float sh, int64_t* hist) {
   need(nseg >= 0 && (nseg == 0 || (seg_begin && seg_end)), "invalid segments");
+  need(num_bins >= 1 && num_bins <= 256, "num_bins must be in [1, 256]");
   need(bin_stride % 16 == 0 && bin_stride >= features, "bin_stride must cover the features and be a multiple of 16");
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const dp::u64 slot = dp::u64(features) * dp::kMaxBins * 2;
+  auto p = std::make_unique<HistPlan>();
+  dp::cuda_check(cudaGetDevice(&p->device), "cudaGetDevice");
+  p->bins = bins;
+  p->bin_stride = bin_stride;
+  p->features = features;
+  p->num_bins = num_bins;
+  p->hist = hist;
+  p->nseg = nseg;
   std::vector<dp::HistTask> tasks;
   const dp::u32 ftiles = (features + dp::kHistFeatureTile - 1) / dp::kHistFeatureTile;
+  dp::u64 total = 0;
   for (int32_t i = 0; i < nseg; ++i) {
     need(seg_begin[i] >= 0 && seg_end[i] >= seg_begin[i], "invalid segment bounds");
-    for (dp::u32 ft = 0; ft < ftiles; ++ft)
-      for (int64_t b = seg_begin[i]; b < seg_end[i]; b += dp::kWindowRows)
-        tasks.push_back(dp::HistTask{dp::u32(i), ft * dp::kHistFeatureTile, 0, 0, b,
-                                     std::min<int64_t>(seg_end[i], b + dp::kWindowRows)});
+    total += dp::u64(seg_end[i] - seg_begin[i]);
   }
-  dp::DevBuf<dp::HistTask> dt(std::max<size_t>(tasks.size(), 1));
-  dp::DevBuf<dp::TreeArrays> ta(1);
-  dp::DevBuf<dp::Scales> sc(1);
+  const int64_t chunk = int64_t(dp::hist_chunk_rows(total * ftiles));
+  for (int32_t i = 0; i < nseg; ++i) {
+    const int64_t n = seg_end[i] - seg_begin[i];
+    if (n == 0) continue;
+    const int64_t pieces = (n + chunk - 1) / chunk, piece = (n + pieces - 1) / pieces;
+    for (dp::u32 ft = 0; ft < ftiles; ++ft)
+      for (int64_t b = seg_begin[i]; b < seg_end[i]; b += piece)
+        tasks.push_back(dp::HistTask{dp::u32(i), ft * dp::kHistFeatureTile, 0, 0, b,
+                                     std::min<int64_t>(seg_end[i], b + piece)});
+  }
+  p->ntasks = dp::u32(tasks.size());
+  p->tasks.resize(std::max<size_t>(tasks.size(), 1));
+  p->trees.resize(1);
+  p->scales.resize(1);
   const dp::TreeArrays th{const_cast<uint32_t*>(ridx), reinterpret_cast<float2*>(const_cast<float*>(gh))};
-  const dp::Scales sh_{sg, sh};
-  dp::cuda_check(cudaMemcpyAsync(ta.get(), &th, sizeof th, cudaMemcpyHostToDevice, s), "upload");
-  dp::cuda_check(cudaMemcpyAsync(sc.get(), &sh_, sizeof sh_, cudaMemcpyHostToDevice, s), "upload");
+  const dp::Scales sc{sg, sh};
+  dp::cuda_check(cudaMemcpy(p->trees.get(), &th, sizeof th, cudaMemcpyHostToDevice), "upload");
+  dp::cuda_check(cudaMemcpy(p->scales.get(), &sc, sizeof sc, cudaMemcpyHostToDevice), "upload");
   if (!tasks.empty())
-    dp::cuda_check(cudaMemcpyAsync(dt.get(), tasks.data(), tasks.size() * sizeof(dp::HistTask),
-                                   cudaMemcpyHostToDevice, s),
+    dp::cuda_check(cudaMemcpy(p->tasks.get(), tasks.data(), tasks.size() * sizeof(dp::HistTask),
+                              cudaMemcpyHostToDevice),
                    "upload");
-  if (nseg) dp::cuda_check(cudaMemsetAsync(hist, 0, dp::u64(nseg) * slot * sizeof(int64_t), s), "memset");
-  dp::launch_histograms(bins, bin_stride, features, ta.get(), sc.get(), dt.get(), dp::u32(tasks.size()), hist, s);
+  return p.release();
+}
+
+void run_hist_plan(const HistPlan& p, cudaStream_t s) {
+  const dp::u64 slot = dp::u64(p.features) * dp::kMaxBins * 2;
+  if (p.nseg) dp::cuda_check(cudaMemsetAsync(p.hist, 0, dp::u64(p.nseg) * slot * sizeof(int64_t), s), "memset");
+  dp::launch_histograms(p.bins, p.bin_stride, p.features, p.num_bins, p.trees.get(), p.scales.get(), p.tasks.get(),
+                        p.ntasks, p.hist, s);
+}
+
+}  // namespace
+
+extern "C" {
+
+int dp_hist_build(const uint8_t* bins, uint64_t bin_stride, uint32_t features, int32_t num_bins, const float* gh,
+                  const uint32_t* ridx, const int64_t* seg_begin, const int64_t* seg_end, int32_t nseg, float sg,
+                  float sh, int64_t* hist, void* stream) {
+  DP_API_BEGIN();
+  std::unique_ptr<HistPlan> p(
+      make_hist_plan(bins, bin_stride, features, num_bins, gh, ridx, seg_begin, seg_end, nseg, sg, sh, hist));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  run_hist_plan(*p, s);
   dp::cuda_check(cudaStreamSynchronize(s), "histograms");
+  DP_API_END();
+}
+
+int dp_hist_prepare(const uint8_t* bins, uint64_t bin_stride, uint32_t features, int32_t num_bins, const float* gh,
+                    const uint32_t* ridx, const int64_t* seg_begin, const int64_t* seg_end, int32_t nseg, float sg,
+                    float sh, int64_t* hist, void** out_plan) {
+  DP_API_BEGIN();
+  need(out_plan != nullptr, "output pointer is null");
+  *out_plan =
+      make_hist_plan(bins, bin_stride, features, num_bins, gh, ridx, seg_begin, seg_end, nseg, sg, sh, hist);
+  DP_API_END();
+}
+
+int dp_hist_run(void* plan, void* stream) {
+  DP_API_BEGIN();
+  need(plan != nullptr, "plan is null");
+  const HistPlan& p = *static_cast<HistPlan*>(plan);
+  dp::DeviceGuard g(p.device);
+  run_hist_plan(p, static_cast<cudaStream_t>(stream));
+  DP_API_END();
+}
+
+int dp_hist_free(void* plan) {
+  DP_API_BEGIN();
+  delete static_cast<HistPlan*>(plan);
   DP_API_END();
 }
 

@@ -75,6 +75,11 @@ Engine::Engine(DMatrix& d, const TrainParams& p, Comm* comm) : d_(d), p_(p), com
   need(R_ < (u64(1) << 32), "row count exceeds the 32-bit row index");
   q_ = &d_.quantized(p_.max_bin, comm_, stream_);
   slot_elems_ = u64(F_) * kMaxBins * 2;
+  max_bins_ = 0;
+  for (u32 f = 0; f < F_; ++f) {
+    max_bins_ = std::max<int>(max_bins_, q_->nbins_h[f]);
+    if (q_->has_missing_h[f]) max_bins_ = kMaxBins;
+  }
   // label validation for the objective
   {
     DevBuf<u32> bad(1);
@@ -219,18 +224,22 @@ void Engine::boost_round(Model& m) {
     DP_CUDA(cudaMemsetAsync(hist, 0, nbuild * slot_elems_ * sizeof(i64), stream_));
     std::vector<HistTask> tasks;
     double rows_built = 0;
+    for (auto& b : build) rows_built += double(open[b.second].count);
+    const i64 chunk = i64(hist_chunk_rows(u64(rows_built) * ftiles));
     for (auto& b : build) {
       const Open& o = open[b.second];
-      rows_built += double(o.count);
+      if (o.count == 0) continue;
+      const i64 pieces = (o.count + chunk - 1) / chunk;
+      const i64 piece = (o.count + pieces - 1) / pieces;
       for (u32 ft = 0; ft < ftiles; ++ft)
-        for (i64 s = o.begin; s < o.begin + o.count; s += kWindowRows)
+        for (i64 s = o.begin; s < o.begin + o.count; s += piece)
           tasks.push_back(HistTask{u32(b.first), ft * kFT, u32(o.tree), 0, s,
-                                   std::min<i64>(o.begin + o.count, s + kWindowRows)});
+                                   std::min<i64>(o.begin + o.count, s + piece)});
     }
     upload(hist_tasks_, tasks);
     prof_.begin(stream_, "histograms", rows_built * (double(F) + 12.0) + double(nbuild) * slot_elems_ * 8.0);
-    launch_histograms(q_->bins.get(), q_->bin_stride, F, tarr_[set].get(), scales_.get(), hist_tasks_.get(),
-                      u32(tasks.size()), hist, stream_);
+    launch_histograms(q_->bins.get(), q_->bin_stride, F, max_bins_, tarr_[set].get(), scales_.get(),
+                      hist_tasks_.get(), u32(tasks.size()), hist, stream_);
     prof_.end(stream_);
     if (comm_) comm_->sum_i64(hist, nbuild * slot_elems_, stream_);
     if (!triples.empty()) {

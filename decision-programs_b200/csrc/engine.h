@@ -81,6 +81,7 @@ class Engine {
   u64 R_ = 0;
   u32 F_ = 0;
   int K_ = 1;
+  int max_bins_ = kMaxBins;  // bin codes are < max_bins_ (missing code 255 included)
   u64 slot_elems_ = 0;
 
   DevBuf<float> margin_;

@@ -122,6 +122,8 @@ std::string format_double(double v) {
 std::string format_float(float v) {
   if (std::isnan(v)) return "NaN";
   if (std::isinf(v)) return v > 0 ? "Infinity" : "-Infinity";
+  // "-0" would read back as the integer 0; keep the sign with a float token
+  if (v == 0.0f) return std::signbit(v) ? "-0.0" : "0";
   char buf[64];
   auto r = std::to_chars(buf, buf + sizeof buf, v);
   std::string s(buf, r.ptr);

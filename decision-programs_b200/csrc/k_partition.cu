@@ -31,14 +31,25 @@ __global__ void __launch_bounds__(kPartThreads) k_part_count(const u8* __restric
   u32* fl = flags + u64(blockIdx.x) * kWordsPerTask;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   u32 cnt = 0;
-  for (i64 base = t.begin; base < t.end; base += kPartThreads) {
-    const i64 i = base + threadIdx.x;
-    bool go = false;
-    if (i < t.end) go = goes_left(__ldg(col + u64(__ldg(ridx + i)) * bstride), nd);
-    const u32 ballot = __ballot_sync(0xffffffffu, go);
-    const i64 w0 = base + warp * 32;
-    if (lane == 0 && w0 < t.end) fl[(w0 - t.begin) / 32] = ballot;
-    cnt += go;
+  constexpr int kIlp = 4;  // independent row gathers in flight per thread
+  for (i64 base = t.begin; base < t.end; base += kPartThreads * kIlp) {
+    u32 r[kIlp];
+#pragma unroll
+    for (int u = 0; u < kIlp; ++u) {
+      const i64 i = base + u * kPartThreads + threadIdx.x;
+      r[u] = i < t.end ? __ldg(ridx + i) : 0xffffffffu;
+    }
+    u8 b[kIlp];
+#pragma unroll
+    for (int u = 0; u < kIlp; ++u) b[u] = r[u] != 0xffffffffu ? __ldg(col + u64(r[u]) * bstride) : u8(0);
+#pragma unroll
+    for (int u = 0; u < kIlp; ++u) {
+      const bool go = r[u] != 0xffffffffu && goes_left(b[u], nd);
+      const u32 ballot = __ballot_sync(0xffffffffu, go);
+      const i64 w0 = base + u * kPartThreads + warp * 32;
+      if (lane == 0 && w0 < t.end) fl[(w0 - t.begin) / 32] = ballot;
+      cnt += go;
+    }
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, o);

@@ -12,8 +12,8 @@
 namespace dp {
 
 // One unit of histogram work: rows at positions [begin, end) of a node's
-// segment (end - begin <= kWindowRows), accumulated into histogram slot
-// `slot` for features [f0, f0 + feature tile).
+// segment, accumulated into histogram slot `slot` for features
+// [f0, f0 + feature tile).
 struct HistTask {
   u32 slot;
   u32 f0;
@@ -71,9 +71,13 @@ void launch_scales(int K, const u32* gmax_bits, const u32* hmax_bits, Scales* sc
 
 // ---- histograms -------------------------------------------------------------
 // hist[slot][F][256][2] (int64) must be zeroed for every slot the tasks touch.
-void launch_histograms(const u8* bins, u64 bin_stride, u32 F, const TreeArrays* trees, const Scales* scales,
-                       const HistTask* tasks, u32 ntasks, i64* hist, cudaStream_t s);
+// Every bin value must be < max_bins (<= 64 selects a smaller tile).
+void launch_histograms(const u8* bins, u64 bin_stride, u32 F, int max_bins, const TreeArrays* trees,
+                       const Scales* scales, const HistTask* tasks, u32 ntasks, i64* hist, cudaStream_t s);
 constexpr u32 kHistFeatureTile = 32;
+// Rows per histogram task for a launch over `total_rows` row-tiles: about two
+// tasks per SM, a multiple of the accumulation window.
+u64 hist_chunk_rows(u64 total_rows);
 
 // hist[dst] = parent_hist[par] - hist[src] for each (par, src, dst) slot triple.
 void launch_subtract(i64* hist, const i64* parent_hist, u64 slot_elems, const u32* triples, u32 n, cudaStream_t s);

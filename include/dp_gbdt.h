@@ -138,10 +138,20 @@ DP_API int dp_bin_matrix(const float* x, uint64_t rows, uint32_t features, uint6
 DP_API int dp_gradients(int objective, int num_class, const float* margin, const float* label, uint64_t rows,
                         float* gh, float* scales, void* stream);
 /* hist[nseg][F][256][2] (int64, overwritten) of position segments
- * [seg_begin[i], seg_end[i]) (host arrays) of (ridx, gh) in position order. */
-DP_API int dp_hist_build(const uint8_t* bins, uint64_t bin_stride, uint32_t features, const float* gh,
-                         const uint32_t* ridx, const int64_t* seg_begin, const int64_t* seg_end, int32_t nseg,
-                         float sg, float sh, int64_t* hist, void* stream);
+ * [seg_begin[i], seg_end[i]) (host arrays) of (ridx, gh) in position order.
+ * Every bin code must be < num_bins (1..256); codes at or above it are skipped. */
+DP_API int dp_hist_build(const uint8_t* bins, uint64_t bin_stride, uint32_t features, int32_t num_bins,
+                         const float* gh, const uint32_t* ridx, const int64_t* seg_begin, const int64_t* seg_end,
+                         int32_t nseg, float sg, float sh, int64_t* hist, void* stream);
+/* The same histogram build with its task list prepared once: dp_hist_prepare
+ * uploads the tasks of the segments; dp_hist_run zeroes `hist` and enqueues
+ * the kernel on `stream` without synchronising (for timing loops). */
+DP_API int dp_hist_prepare(const uint8_t* bins, uint64_t bin_stride, uint32_t features, int32_t num_bins,
+                           const float* gh, const uint32_t* ridx, const int64_t* seg_begin, const int64_t* seg_end,
+                           int32_t nseg, float sg, float sh, int64_t* hist, void** out_plan);
+DP_API int dp_hist_run(void* plan, void* stream);
+DP_API int dp_hist_free(void* plan);
+
 /* Best split per node from hist[N][F][256][2] (device) and quantised totals
  * totals[N][2] (host); outputs on the host: out_i[N][4] = feature, bin,
  * default_left, valid; out_gain[N]; out_left[N][2]. */

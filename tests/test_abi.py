@@ -118,7 +118,7 @@ def test_float_format_round_trips_through_double(dp, tmp_path):
     import numpy as np
     rng = np.random.default_rng(7)
     vals = np.concatenate([rng.standard_normal(2000).astype(np.float32),
-                           np.array([1e-38, 3.4028235e38, -0.0, 0.1, 1 / 3], np.float32)])
+                           np.array([1e-38, 3.4028235e38, -0.0, 0.0, 0.1, 1 / 3], np.float32)])
     m = _model()
     m["learner"]["gradient_booster"]["model"]["trees"][0]["split_conditions"] = [float(vals[0]), -1.0, 1.0]
     b = dp.Booster()
@@ -126,4 +126,5 @@ def test_float_format_round_trips_through_double(dp, tmp_path):
         m["learner"]["gradient_booster"]["model"]["trees"][0]["split_conditions"][0] = float(v)
         b.load_raw(json.dumps(m).encode())
         out = json.loads(b.save_raw())["learner"]["gradient_booster"]["model"]["trees"][0]["split_conditions"][0]
-        assert np.float32(out) == v  # double parse then narrow, as native/class_io.hpp:180 does
+        # double parse then narrow, as native/class_io.hpp:180 does; the sign of zero survives
+        assert np.float32(out).view(np.uint32) == v.view(np.uint32)

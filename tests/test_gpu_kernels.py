@@ -11,12 +11,27 @@ pytestmark = pytest.mark.gpu
 torch = pytest.importorskip("torch")
 
 
+_alive = []
+
+
 def cuda(a):
-    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    """Device copy kept alive for the rest of the test session: the C-ABI
+    receives raw pointers, so a temporary must not return to torch's caching
+    allocator before the call has finished."""
+    t = torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    _alive.append(t)
+    return t
 
 
 def ptr(t):
     return t.data_ptr()
+
+
+@pytest.fixture(autouse=True)
+def _release_buffers():
+    yield
+    torch.cuda.synchronize()
+    _alive.clear()
 
 
 def special_matrix(R, F, seed, nan_frac=0.0):
@@ -107,12 +122,14 @@ def test_gradients_and_scales_match_oracle(dp, orc, objective, K):
         assert tuple(scales[k]) == orc.quantizer(ogh[k])
 
 
-@pytest.mark.parametrize("F,nodes,seed", [(32, 1, 0), (16, 3, 1), (64, 5, 2), (100, 2, 3), (784, 2, 4)])
-def test_histograms_match_oracle(dp, orc, F, nodes, seed):
+@pytest.mark.parametrize("F,nodes,seed,nbins,R", [(32, 1, 0, 256, 40000), (16, 3, 1, 256, 40000),
+                                                 (64, 5, 2, 256, 40000), (100, 2, 3, 256, 40000),
+                                                 (784, 2, 4, 256, 40000), (32, 1, 5, 64, 200000),
+                                                 (40, 4, 6, 16, 100000), (32, 2, 7, 256, 600000)])
+def test_histograms_match_oracle(dp, orc, F, nodes, seed, nbins, R):
     rng = np.random.default_rng(seed)
-    R = 40000
     stride = (F + 15) // 16 * 16
-    bins = rng.integers(0, 256, (R, stride)).astype(np.uint8)
+    bins = rng.integers(0, nbins, (R, stride)).astype(np.uint8)
     bins[:, F:] = 0
     gh = np.stack([rng.standard_normal(R), rng.random(R)], 1).astype(np.float32)
     ridx = rng.permutation(R).astype(np.uint32)
@@ -125,7 +142,7 @@ def test_histograms_match_oracle(dp, orc, F, nodes, seed):
     hist = torch.zeros((len(sb), F, 256, 2), dtype=torch.int64, device="cuda")
     sbn = np.array(sb, np.int64)
     sen = np.array(se, np.int64)
-    dp.check(dp.lib().dp_hist_build(ptr(cuda(bins)), stride, F, ptr(cuda(gh)), ptr(cuda(ridx)), sbn.ctypes.data,
+    dp.check(dp.lib().dp_hist_build(ptr(cuda(bins)), stride, F, nbins, ptr(cuda(gh)), ptr(cuda(ridx)), sbn.ctypes.data,
                                     sen.ctypes.data, len(sb), sg, sh, ptr(hist), None))
     ohist = orc.histograms(bins, F, gh, ridx, sb, se, sg, sh, threads=4)
     np.testing.assert_array_equal(hist.cpu().numpy(), ohist)

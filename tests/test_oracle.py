@@ -1,0 +1,106 @@
+"""CPU checks of the oracle (test infrastructure): hand-computed known answers
+and the golden fixtures produced by tests/golden/make_golden.py, an
+independent pure-Python restatement of the same rules.  XGBoost 3.4.1 (where
+the reference's arithmetic lives) is absent, so these pin the oracle to its
+written semantics, not to XGBoost."""
+import json
+import math
+import pathlib
+
+import numpy as np
+import pytest
+
+GOLDEN = pathlib.Path(__file__).resolve().parent / "golden"
+CASES = sorted(p.stem for p in GOLDEN.glob("*.json"))
+
+
+def load_case(name):
+    d = json.loads((GOLDEN / f"{name}.json").read_text())
+    x = np.array([[np.nan if v is None else v for v in r] for r in d["x"]], np.float32)
+    return d, x, np.array(d["y"], np.float32)
+
+
+def test_exp_is_accurate(orc):
+    xs = np.concatenate([np.linspace(-700, 700, 20001), np.linspace(-2, 2, 20001), [0.0, 1e-300, -1e-300]])
+    for x in xs:
+        e = orc.dp_exp(float(x))
+        ref = math.exp(x)
+        assert abs(e - ref) <= 4e-16 * ref, (x, e, ref)
+    assert orc.dp_exp(710.0) == math.inf and orc.dp_exp(-800.0) == 0.0
+
+
+def test_hand_computed_stump(orc):
+    # x = 1..4, y = 1,1,3,3, squared error, lambda 0, eta 1, mcw 0: g = -y, h = 1.
+    # Candidates (x < 2, 3, 4) give gains 2/3, 2, 2/3 -> split x < 3, leaves 1 and 3.
+    x = np.array([[1.0], [2.0], [3.0], [4.0]], np.float32)
+    y = np.array([1, 1, 3, 3], np.float32)
+    m = orc.Model(x, y, "reg:squarederror", max_depth=1, eta=1.0, reg_lambda=0.0, min_child_weight=0.0, rounds=1)
+    t = m.tree(0)
+    assert t["left_children"].tolist() == [1, -1, -1] and t["right_children"].tolist() == [2, -1, -1]
+    assert t["split_conditions"].tolist() == [3.0, 1.0, 3.0]
+    assert t["loss_changes"][0] == np.float32(2.0)
+    assert t["sum_hessian"].tolist() == [4.0, 2.0, 2.0]
+    np.testing.assert_array_equal(m.margins()[:, 0], [1, 1, 3, 3])
+
+
+def test_quantile_boundaries_by_hand(orc):
+    # 10 distinct values, max_bin 4: ranks floor(k*10/4) = 2, 5, 7 -> values 20, 50, 70
+    x = (np.arange(10, dtype=np.float32) * 10)[::-1].reshape(-1, 1).copy()
+    cut, nb, hm = orc.cuts(x, 4)
+    assert nb[0] == 4 and hm[0] == 0
+    assert cut[0, :3].tolist() == [20.0, 50.0, 70.0]
+    bins = orc.bin_matrix(x, cut, nb, hm)[:, 0]
+    assert bins[::-1].tolist() == [0, 0, 1, 1, 1, 2, 2, 3, 3, 3]
+
+
+def test_missing_values_take_the_reserved_code(orc):
+    x = np.array([[np.nan], [1.0], [2.0], [-0.0], [0.0]], np.float32)
+    cut, nb, hm = orc.cuts(x, 256)
+    assert hm[0] == 1 and nb[0] == 3  # distinct {0, 1, 2}; -0.0 folds into 0.0
+    assert cut[0, :2].tolist() == [1.0, 2.0]
+    assert orc.bin_matrix(x, cut, nb, hm)[:, 0].tolist() == [255, 1, 2, 0, 0]
+
+
+def test_quantiser_scale(orc):
+    gh = np.array([[0.75, 0.25], [-3.0, 0.1]], np.float32)
+    sg, sh = orc.quantizer(gh)
+    assert sg == 2.0 ** 15 and sh == 2.0 ** 19  # |g| < 4 -> 2^(17-2); h < 0.5 -> 2^(18-(-1))
+    assert orc.quantizer(np.zeros((3, 2), np.float32)) == (1.0, 1.0)
+
+
+@pytest.mark.parametrize("name", CASES)
+def test_oracle_matches_golden_restatement(orc, name):
+    d, x, y = load_case(name)
+    p = d["params"]
+    exp = d["expected"]
+    cut, nb, hm = orc.cuts(x, p["max_bin"])
+    assert nb.tolist() == exp["nbins"] and hm.tolist() == exp["has_missing"]
+    for f, b in enumerate(exp["bounds"]):
+        np.testing.assert_array_equal(cut[f, : len(b)], np.array(b, np.float32))
+    np.testing.assert_array_equal(orc.bin_matrix(x, cut, nb, hm)[:, : x.shape[1]], np.array(exp["bins"]))
+    m = orc.Model(x, y, d["objective"], num_class=d["num_class"], max_depth=p["max_depth"], max_bin=p["max_bin"],
+                  eta=p["eta"], reg_lambda=p["lambda"], alpha=p["alpha"], gamma=p["gamma"],
+                  min_child_weight=p["mcw"], rounds=d["rounds"])
+    assert m.num_trees() == len(exp["trees"])
+    for i, t in enumerate(exp["trees"]):
+        ot = m.tree(i)
+        assert ot["left_children"].tolist() == t["left"]
+        assert ot["right_children"].tolist() == t["right"]
+        assert ot["split_indices"].tolist() == t["feature"]
+        assert ot["default_left"].tolist() == t["dleft"]
+        np.testing.assert_array_equal(ot["split_conditions"].view(np.uint32),
+                                      np.array(t["cond"], np.float32).view(np.uint32))
+    np.testing.assert_array_equal(m.margins().view(np.uint32), np.array(exp["margin"], np.float32).view(np.uint32))
+
+
+def test_threads_and_subtraction_do_not_change_trees(orc):
+    d, x, y = load_case("logistic_nan")
+    rng = np.random.default_rng(3)
+    x = rng.standard_normal((5000, 12)).astype(np.float32)
+    x[rng.random(x.shape) < 0.1] = np.nan
+    y = (np.nan_to_num(x[:, 0]) > 0).astype(np.float32)
+    a = orc.Model(x, y, "binary:logistic", max_depth=6, rounds=3, threads=1, subtract=False)
+    b = orc.Model(x, y, "binary:logistic", max_depth=6, rounds=3, threads=8, subtract=True)
+    for i in range(3):
+        for k, v in a.tree(i).items():
+            np.testing.assert_array_equal(v, b.tree(i)[k])
