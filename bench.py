@@ -26,7 +26,6 @@ import json
 import os
 import pathlib
 import statistics
-import subprocess
 import sys
 import threading
 import time
@@ -90,53 +89,69 @@ def shard(torch, rank: int, world: int, device):
 
 # --------------------------------------------------------------------------- clocks
 class ClockSampler:
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    """SM clock and clock-event reasons of one GPU, sampled every 100 ms from a
+    background thread through NVML in this process (spawning nvidia-smi inside
+    the timed region stalls the driver).  Falls back to nvidia-smi when NVML is
+    unavailable."""
 
-    def __init__(self, device_index: int):
+    def __init__(self, torch, device_index: int):
+        self.torch = torch
         self.dev = device_index
-        self.proc = None
-        self.lines: list[str] = []
+        self.samples: list[tuple[float, float, int]] = []
+        self._stop = threading.Event()
+        self.nvml = None
+        self.handle = None
+
+    def _open(self):
+        import pynvml
+        pynvml.nvmlInit()
+        props = self.torch.cuda.get_device_properties(self.dev)
+        handle = None
+        try:
+            bus = f"{props.pci_domain_id:08X}:{props.pci_bus_id:02X}:{props.pci_device_id:02X}.0"
+            handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            handle = pynvml.nvmlDeviceGetHandleByIndex(self.dev)
+        self.nvml, self.handle = pynvml, handle
+
+    def _run(self):
+        nv, h = self.nvml, self.handle
+        mx = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+        while not self._stop.is_set():
+            try:
+                self.samples.append((float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)), mx,
+                                     int(nv.nvmlDeviceGetCurrentClocksEventReasons(h))))
+            except Exception:
+                pass
+            self._stop.wait(0.1)
 
     def start(self):
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.dev), f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
-                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
-            self.t.start()
-        except OSError:
-            self.proc = None
-
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            self._open()
+        except Exception:
+            self.nvml = None
+            return
+        self.t = threading.Thread(target=self._run, daemon=True)
+        self.t.start()
+        t0 = time.time()
+        while not self.samples and time.time() - t0 < 2.0:
+            time.sleep(0.01)
 
     def stop(self) -> dict:
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
-        sm, mx, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.lines:
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                mx.append(float(parts[2]))
-            except ValueError:
-                continue
-            for n, v in zip(names, parts[5:9]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        if self.nvml is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["NVML unavailable"], "samples": 0}
+        self._stop.set()
+        self.t.join(timeout=2)
+        nv = self.nvml
+        names = {"hw_slowdown": nv.nvmlClocksEventReasonHwSlowdown,
+                 "hw_thermal_slowdown": nv.nvmlClocksEventReasonHwThermalSlowdown,
+                 "sw_thermal_slowdown": nv.nvmlClocksEventReasonSwThermalSlowdown,
+                 "sw_power_cap": nv.nvmlClocksEventReasonSwPowerCap}
+        reasons = sorted({n for _, _, r in self.samples for n, bit in names.items() if r & bit})
+        sm = [c for c, _, _ in self.samples]
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(m for _, m, _ in self.samples) if self.samples else None,
+                "reasons": reasons, "samples": len(sm), "source": "NVML, 100 ms"}
 
 
 # --------------------------------------------------------------------------- reference / CPU arm
@@ -195,13 +210,14 @@ def hist_sweep(torch, dp, device, peak_gbs: float) -> list[dict]:
             node = torch.randint(0, N, (R,), device=device, generator=g)
             ridx = torch.argsort(node, stable=True).to(torch.int32)
             ghp = gh[ridx.long()].contiguous()
+            dp.check(dp.lib().dp_quantize_gh(ghp.data_ptr(), R, 2.0 ** 15, 2.0 ** 16, None))
             counts = torch.bincount(node, minlength=N).cpu().numpy()
             del node
             edges = np.concatenate([[0], np.cumsum(counts)]).astype(np.int64)
             sb, se = np.ascontiguousarray(edges[:-1]), np.ascontiguousarray(edges[1:])
             hist = torch.empty((N, F, 256, 2), dtype=torch.int64, device=device)
             plan = dp.ctypes_void_p()
-            dp.check(dp.lib().dp_hist_prepare(bins.data_ptr(), F, F, B, ghp.data_ptr(), ridx.data_ptr(), sb.ctypes.data,
+            dp.check(dp.lib().dp_hist_prepare(bins.data_ptr(), F, F, B, 1, ghp.data_ptr(), ridx.data_ptr(), sb.ctypes.data,
                                               se.ctypes.data, N, 2.0 ** 15, 2.0 ** 16, hist.data_ptr(),
                                               dp.C.byref(plan)))
             stream = torch.cuda.current_stream()
@@ -294,10 +310,10 @@ def main() -> None:
     for i in range(args.warmup):
         b.update(d, i)
     b.set_profiling(True)
-    clocks = ClockSampler(local)
+    clocks = ClockSampler(torch, local)
+    clocks.start()
     barrier()
     launches0 = dp.launch_count()
-    clocks.start()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev0.record()
     for i in range(args.steps):

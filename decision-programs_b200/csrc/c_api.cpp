@@ -394,18 +394,20 @@ struct HistPlan {
   uint64_t bin_stride = 0;
   uint32_t features = 0;
   int num_bins = 256;
+  bool quantized = false;
   int64_t* hist = nullptr;
   int32_t nseg = 0;
   dp::u32 ntasks = 0;
   dp::DevBuf<dp::HistTask> tasks;
   dp::DevBuf<dp::TreeArrays> trees;
   dp::DevBuf<dp::Scales> scales;
+  dp::DevBuf<dp::u32> counter;
   int device = 0;
 };
 
 HistPlan* make_hist_plan(const uint8_t* bins, uint64_t bin_stride, uint32_t features, int32_t num_bins,
-                         const float* gh, const uint32_t* ridx, const int64_t* seg_begin, const int64_t* seg_end,
-                         int32_t nseg, float sg, float sh, int64_t* hist) {
+                         bool quantized, const void* gh, const uint32_t* ridx, const int64_t* seg_begin,
+                         const int64_t* seg_end, int32_t nseg, float sg, float sh, int64_t* hist) {
   need(nseg >= 0 && (nseg == 0 || (seg_begin && seg_end)), "invalid segments");
   need(num_bins >= 1 && num_bins <= 256, "num_bins must be in [1, 256]");
   need(bin_stride % 16 == 0 && bin_stride >= features, "bin_stride must cover the features and be a multiple of 16");
@@ -415,13 +417,15 @@ HistPlan* make_hist_plan(const uint8_t* bins, uint64_t bin_stride, uint32_t feat
   p->bin_stride = bin_stride;
   p->features = features;
   p->num_bins = num_bins;
+  p->quantized = quantized;
   p->hist = hist;
   p->nseg = nseg;
   std::vector<dp::HistTask> tasks;
   const dp::u32 ftiles = (features + dp::kHistFeatureTile - 1) / dp::kHistFeatureTile;
   dp::u64 total = 0;
   for (int32_t i = 0; i < nseg; ++i) {
-    need(seg_begin[i] >= 0 && seg_end[i] >= seg_begin[i], "invalid segment bounds");
+    need(seg_begin[i] >= 0 && seg_end[i] >= seg_begin[i] && seg_end[i] < (int64_t(1) << 31),
+         "invalid segment bounds (positions must be below 2^31)");
     total += dp::u64(seg_end[i] - seg_begin[i]);
   }
   const int64_t chunk = int64_t(dp::hist_chunk_rows(total * ftiles));
@@ -438,7 +442,8 @@ HistPlan* make_hist_plan(const uint8_t* bins, uint64_t bin_stride, uint32_t feat
   p->tasks.resize(std::max<size_t>(tasks.size(), 1));
   p->trees.resize(1);
   p->scales.resize(1);
-  const dp::TreeArrays th{const_cast<uint32_t*>(ridx), reinterpret_cast<float2*>(const_cast<float*>(gh))};
+  p->counter.resize(1);
+  const dp::TreeArrays th{const_cast<uint32_t*>(ridx), reinterpret_cast<float2*>(const_cast<void*>(gh))};
   const dp::Scales sc{sg, sh};
   dp::cuda_check(cudaMemcpy(p->trees.get(), &th, sizeof th, cudaMemcpyHostToDevice), "upload");
   dp::cuda_check(cudaMemcpy(p->scales.get(), &sc, sizeof sc, cudaMemcpyHostToDevice), "upload");
@@ -452,8 +457,8 @@ HistPlan* make_hist_plan(const uint8_t* bins, uint64_t bin_stride, uint32_t feat
 void run_hist_plan(const HistPlan& p, cudaStream_t s) {
   const dp::u64 slot = dp::u64(p.features) * dp::kMaxBins * 2;
   if (p.nseg) dp::cuda_check(cudaMemsetAsync(p.hist, 0, dp::u64(p.nseg) * slot * sizeof(int64_t), s), "memset");
-  dp::launch_histograms(p.bins, p.bin_stride, p.features, p.num_bins, p.trees.get(), p.scales.get(), p.tasks.get(),
-                        p.ntasks, p.hist, s);
+  dp::launch_histograms(p.bins, p.bin_stride, p.features, p.num_bins, p.quantized, p.trees.get(), p.scales.get(),
+                        p.tasks.get(), p.ntasks, p.counter.get(), p.hist, s);
 }
 
 }  // namespace
@@ -464,21 +469,22 @@ int dp_hist_build(const uint8_t* bins, uint64_t bin_stride, uint32_t features, i
                   const uint32_t* ridx, const int64_t* seg_begin, const int64_t* seg_end, int32_t nseg, float sg,
                   float sh, int64_t* hist, void* stream) {
   DP_API_BEGIN();
-  std::unique_ptr<HistPlan> p(
-      make_hist_plan(bins, bin_stride, features, num_bins, gh, ridx, seg_begin, seg_end, nseg, sg, sh, hist));
+  std::unique_ptr<HistPlan> p(make_hist_plan(bins, bin_stride, features, num_bins, false, gh, ridx, seg_begin,
+                                             seg_end, nseg, sg, sh, hist));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   run_hist_plan(*p, s);
   dp::cuda_check(cudaStreamSynchronize(s), "histograms");
   DP_API_END();
 }
 
-int dp_hist_prepare(const uint8_t* bins, uint64_t bin_stride, uint32_t features, int32_t num_bins, const float* gh,
-                    const uint32_t* ridx, const int64_t* seg_begin, const int64_t* seg_end, int32_t nseg, float sg,
-                    float sh, int64_t* hist, void** out_plan) {
+int dp_hist_prepare(const uint8_t* bins, uint64_t bin_stride, uint32_t features, int32_t num_bins, int32_t gh_kind,
+                    const void* gh, const uint32_t* ridx, const int64_t* seg_begin, const int64_t* seg_end,
+                    int32_t nseg, float sg, float sh, int64_t* hist, void** out_plan) {
   DP_API_BEGIN();
   need(out_plan != nullptr, "output pointer is null");
-  *out_plan =
-      make_hist_plan(bins, bin_stride, features, num_bins, gh, ridx, seg_begin, seg_end, nseg, sg, sh, hist);
+  need(gh_kind == 0 || gh_kind == 1, "gh_kind must be 0 (fp32 pairs) or 1 (quantised int32 pairs)");
+  *out_plan = make_hist_plan(bins, bin_stride, features, num_bins, gh_kind == 1, gh, ridx, seg_begin, seg_end,
+                             nseg, sg, sh, hist);
   DP_API_END();
 }
 
@@ -494,6 +500,17 @@ int dp_hist_run(void* plan, void* stream) {
 int dp_hist_free(void* plan) {
   DP_API_BEGIN();
   delete static_cast<HistPlan*>(plan);
+  DP_API_END();
+}
+
+int dp_quantize_gh(float* gh, uint64_t n, float sg, float sh, void* stream) {
+  DP_API_BEGIN();
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  dp::DevBuf<dp::Scales> sc(1);
+  const dp::Scales h{sg, sh};
+  dp::cuda_check(cudaMemcpyAsync(sc.get(), &h, sizeof h, cudaMemcpyHostToDevice, s), "upload");
+  dp::launch_quantize_gh(reinterpret_cast<float2*>(gh), n, 1, sc.get(), s);
+  dp::cuda_check(cudaStreamSynchronize(s), "quantize");
   DP_API_END();
 }
 

@@ -19,11 +19,11 @@ constexpr int kMissingBin = 255;
 constexpr int kMaxBins = 256;
 // Quantised gradient ranges: |q_g| <= 2^17 and 0 <= q_h <= 2^18.  With at most
 // kWindowRows rows per shared-memory accumulation window, window sums satisfy
-// |sum q_g| < 2^31 and sum q_h < 2^32, so one 64-bit word holds both:
-// packed = sum_g * 2^32 + sum_h.
+// |sum q_g| <= 16383 * 2^17 < 2^31 and sum q_h <= 16383 * 2^18 < 2^32, so
+// 32-bit shared-memory counters are exact within a window.
 constexpr int kGradBits = 17;
 constexpr int kHessBits = 18;
-constexpr int kWindowRows = 8192;
+constexpr int kWindowRows = 16383;
 
 // e^x: Cody & Waite (1980) argument reduction x = k ln2 + r with ln2 split
 // into a 24-bit head and a tail, the Taylor series of e^r to degree 13

@@ -72,7 +72,7 @@ Engine::Engine(DMatrix& d, const TrainParams& p, Comm* comm) : d_(d), p_(p), com
   need(K_ >= 1, "num_class must be set for multi-class objectives");
   R_ = d_.rows();
   F_ = d_.cols();
-  need(R_ < (u64(1) << 32), "row count exceeds the 32-bit row index");
+  need(R_ < (u64(1) << 31), "row count per device exceeds 2^31");
   q_ = &d_.quantized(p_.max_bin, comm_, stream_);
   slot_elems_ = u64(F_) * kMaxBins * 2;
   max_bins_ = 0;
@@ -112,6 +112,7 @@ Engine::Engine(DMatrix& d, const TrainParams& p, Comm* comm) : d_(d), p_(p), com
   gmax_.resize(K_);
   hmax_.resize(K_);
   scales_.resize(K_);
+  hist_counter_.resize(1);
   arena_.reserve(size_t(8) << 20);
 }
 
@@ -194,6 +195,8 @@ void Engine::boost_round(Model& m) {
     comm_->max_u32(hmax_.get(), K, stream_);
   }
   launch_scales(K, gmax_.get(), hmax_.get(), scales_.get(), stream_);
+  // (g, h) become exact int32 pairs once per round; every later pass reads them
+  launch_quantize_gh(gh_[0].get(), R, K, scales_.get(), stream_);
   for (int k = 0; k < K; ++k) launch_iota(ridx_[0].get() + u64(k) * R, R, stream_);
   const Scales* sc_h = download(scales_.get(), K);
 
@@ -238,8 +241,8 @@ void Engine::boost_round(Model& m) {
     }
     upload(hist_tasks_, tasks);
     prof_.begin(stream_, "histograms", rows_built * (double(F) + 12.0) + double(nbuild) * slot_elems_ * 8.0);
-    launch_histograms(q_->bins.get(), q_->bin_stride, F, max_bins_, tarr_[set].get(), scales_.get(),
-                      hist_tasks_.get(), u32(tasks.size()), hist, stream_);
+    launch_histograms(q_->bins.get(), q_->bin_stride, F, max_bins_, true, tarr_[set].get(), scales_.get(),
+                      hist_tasks_.get(), u32(tasks.size()), hist_counter_.get(), hist, stream_);
     prof_.end(stream_);
     if (comm_) comm_->sum_i64(hist, nbuild * slot_elems_, stream_);
     if (!triples.empty()) {
@@ -288,33 +291,28 @@ void Engine::boost_round(Model& m) {
     // ---- partition
     std::vector<PartNode> pn(split.size());
     std::vector<PartTask> pt;
-    std::vector<u32> task_node;
     for (size_t j = 0; j < split.size(); ++j) {
       const Open& o = open[split[j]];
       const SplitCand& c = best[split[j]];
-      pn[j] = PartNode{u32(o.tree), c.feature, c.bin, c.default_left, i32(hm[c.feature]), 0, o.begin, 0};
+      pn[j] = PartNode{u32(o.tree), c.feature, c.bin, c.default_left, i32(hm[c.feature]), 0, o.begin,
+                       o.begin + o.count};
       for (i64 s = o.begin; s < o.begin + o.count; s += kPartChunk)
         pt.push_back(PartTask{u32(j), 0, s, std::min<i64>(o.begin + o.count, s + kPartChunk)});
     }
     upload(part_nodes_, pn);
     upload(part_tasks_, pt);
-    flags_.reserve(std::max<size_t>(pt.size(), 1) * (kPartChunk / 32));
-    left_.reserve(std::max<size_t>(pt.size(), 1));
-    prof_.begin(stream_, "partition_count", 0.0);
-    launch_partition_count(q_->bins.get(), q_->bin_stride, tarr_[set].get(), part_nodes_.get(), part_tasks_.get(),
-                           u32(pt.size()), flags_.get(), left_.get(), stream_);
+    cursors_.reserve(2 * split.size());
+    DP_CUDA(cudaMemsetAsync(cursors_.get(), 0, 2 * split.size() * sizeof(u32), stream_));
+    prof_.begin(stream_, "partition", 0.0);
+    launch_partition(q_->bins.get(), q_->bin_stride, tarr_[set].get(), tarr_[1 - set].get(), part_nodes_.get(),
+                     part_tasks_.get(), u32(pt.size()), cursors_.get(), stream_);
     prof_.end(stream_);
-    const u32* left_h = download(left_.get(), std::max<size_t>(pt.size(), 1));
+    const u32* cur_h = download(cursors_.get(), 2 * split.size());
     sync();
-    std::vector<u32> left(left_h, left_h + pt.size());
-    std::vector<i64> loff(pt.size()), roff(pt.size());
-    std::vector<i64> nleft(split.size(), 0), seen(split.size(), 0);
-    for (size_t t = 0; t < pt.size(); ++t) {
-      const u32 j = pt[t].node;
-      loff[t] = nleft[j];
-      roff[t] = seen[j] - nleft[j];
-      nleft[j] += left[t];
-      seen[j] += pt[t].end - pt[t].begin;
+    std::vector<i64> nleft(split.size());
+    for (size_t j = 0; j < split.size(); ++j) {
+      nleft[j] = cur_h[2 * j];
+      need(i64(cur_h[2 * j]) + i64(cur_h[2 * j + 1]) == open[split[j]].count, "partition lost rows");
     }
     std::vector<i64> gleft(nleft);
     if (comm_) {
@@ -325,14 +323,6 @@ void Engine::boost_round(Model& m) {
       sync();
       gleft.assign(g_h, g_h + split.size());
     }
-    for (size_t j = 0; j < split.size(); ++j) pn[j].nleft = nleft[j];
-    upload(part_nodes_, pn);
-    upload(left_off_, loff);
-    upload(right_off_, roff);
-    prof_.begin(stream_, "partition_scatter", 0.0);
-    launch_partition_scatter(tarr_[set].get(), tarr_[1 - set].get(), part_nodes_.get(), part_tasks_.get(),
-                             u32(pt.size()), flags_.get(), left_off_.get(), right_off_.get(), stream_);
-    prof_.end(stream_);
 
     // ---- children
     std::vector<Open> next;

@@ -92,13 +92,14 @@ class Engine {
   DevBuf<Scales> scales_;
   DevBuf<i64> hist_[2];
   DevBuf<HistTask> hist_tasks_;
+  DevBuf<u32> hist_counter_;
   DevBuf<u32> triples_;
   DevBuf<EvalNode> eval_nodes_;
   DevBuf<SplitCand> cand_, best_;
   DevBuf<PartNode> part_nodes_;
   DevBuf<PartTask> part_tasks_;
-  DevBuf<u32> flags_, left_;
-  DevBuf<i64> left_off_, right_off_, counts_;
+  DevBuf<u32> cursors_;
+  DevBuf<i64> counts_;
   DevBuf<LeafTask> leaf_tasks_;
 
   PinnedBuf<u8> arena_;

@@ -3,19 +3,24 @@
 // hist[slot][f][bin] (int64 pairs).
 //
 // Design (HBM- and shared-atomic-bound, no tensor cores):
+//  * persistent blocks (one 1024-thread block per SM for 256 bins) pull tasks
+//    from an atomic counter; consecutive tasks of the same (node, tile) keep
+//    accumulating, so a block drains to global memory only when the node or
+//    tile changes and the tail of the launch stays balanced;
 //  * two u32 planes in shared memory, g and h, laid out [bin][column]: one
 //    32-bit shared atomic per (row, feature) and plane.  The quantiser bounds
-//    (|q_g| <= 2^17, q_h <= 2^18) keep the sums of an 8192-row window inside
-//    int32 / uint32, so after every window the planes are folded into int64
-//    planes in shared memory; a block can therefore own an arbitrarily long
-//    row range and drains to global memory once;
-//  * a warp reads 4 rows x 32 features per step: lane (s, q) loads the 32-bit
-//    word holding features 4q..4q+3 of row s.  In atomic step j the lane
-//    updates feature 4q + ((j + s) & 3), whose column is ((j+s)&3)*8 + q, so
-//    the 32 lanes of a step hit 32 distinct banks whatever the bins are;
+//    keep the sums of a kWindowRows window inside int32 / uint32, so every
+//    window is folded into int64 planes in shared memory; the final drain uses
+//    64-bit global atomics (integer: the result does not depend on order);
+//  * a warp reads 16 rows x 32 features per step with 16-byte loads: lane
+//    (s, h) holds bytes 16h..16h+15 of row s, rotated by s bytes once, so that
+//    in atomic step j it updates feature 16h + ((j + s) & 15).  The 32 lanes
+//    of a step then address 32 distinct feature columns -- 32 distinct banks
+//    of the [bin][feature] planes whatever the bins are -- while every byte
+//    extraction uses a compile-time position;
 //  * rows are gathered through the node's row-index segment; (g, h) is read
-//    in position order (the partition kernel moves it with the row index);
-//  * the final drain uses 64-bit global atomics (integer: order-independent).
+//    in position order, already quantised to int32 pairs by the training
+//    engine (the kernel-level entry point may pass fp32 pairs instead).
 #include "kernels.h"
 
 namespace dp {
@@ -23,115 +28,194 @@ namespace dp {
 namespace {
 
 constexpr int kFT = kHistFeatureTile;  // 32 features per tile
-constexpr int kQPR = kFT / 4;          // 32-bit words per row tile
-constexpr int kRPW = 32 / kQPR;        // rows per warp step
-constexpr int kUnroll = 8;             // row steps in flight per warp
+constexpr int kRPW = 16;               // rows per warp step (two lanes per row)
+#ifndef DP_HIST_UNROLL
+#define DP_HIST_UNROLL 4
+#endif
+#ifndef DP_HIST_THREADS
+#define DP_HIST_THREADS 1024
+#endif
+constexpr int kUnroll = DP_HIST_UNROLL;  // row steps in flight per warp
+constexpr u32 kNoRow = 0xffffffffu;
 
-template <int MB, int THREADS>
-__global__ void __launch_bounds__(THREADS) k_hist(const u8* __restrict__ bins, u64 bstride, u32 F,
-                                                  const TreeArrays* __restrict__ trees,
-                                                  const Scales* __restrict__ scales,
-                                                  const HistTask* __restrict__ tasks, i64* __restrict__ hist) {
-  extern __shared__ __align__(16) unsigned char smem[];
-  constexpr int kCells = MB * kFT;
-  u32* Lg = reinterpret_cast<u32*>(smem);
-  u32* Lh = Lg + kCells;
-  long long* Wg = reinterpret_cast<long long*>(Lh + kCells);
-  long long* Wh = Wg + kCells;
-  const HistTask t = tasks[blockIdx.x];
-  const bool multi = t.end - t.begin > kWindowRows;
-  for (int i = threadIdx.x; i < kCells; i += THREADS) {
-    Lg[i] = 0u;
-    Lh[i] = 0u;
-    if (multi) { Wg[i] = 0; Wh[i] = 0; }
-  }
-  __syncthreads();
+struct HistArgs {
+  const u8* bins;
+  u64 bstride;
+  u32 F;
+  u32 ntasks;
+  const TreeArrays* trees;
+  const Scales* scales;
+  const HistTask* tasks;
+  u32* counter;
+  i64* hist;
+};
 
-  const TreeArrays ta = trees[t.tree];
-  const Scales sc = scales[t.tree];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  constexpr int kWarps = THREADS / 32;
-  const int s = lane / kQPR, q = lane % kQPR;
-  // words past the row's bin_stride (last tile of a row) are never read
-  const bool qvalid = u64(t.f0) + 4u * q < bstride;
-  const u8* base = bins + t.f0 + 4 * q;
-  constexpr i64 kStep = i64(kWarps) * kRPW;
-
-  for (i64 w0 = t.begin; w0 < t.end; w0 += kWindowRows) {
-    const i64 w1 = (t.end - w0) < kWindowRows ? t.end : w0 + kWindowRows;
-    for (i64 i0 = w0 + i64(warp) * kRPW + s; i0 < w1; i0 += kStep * kUnroll) {
-      u32 row[kUnroll];
-#pragma unroll
-      for (int u = 0; u < kUnroll; ++u) {
-        const i64 i = i0 + u * kStep;
-        row[u] = i < w1 ? __ldg(ta.ridx + i) : 0xffffffffu;
-      }
-      u32 word[kUnroll];
-      float2 g[kUnroll];
-#pragma unroll
-      for (int u = 0; u < kUnroll; ++u) {
-        word[u] = 0u;
-        g[u] = make_float2(0.f, 0.f);
-        if (row[u] != 0xffffffffu && qvalid) {
-          word[u] = __ldg(reinterpret_cast<const u32*>(base + u64(row[u]) * bstride));
-          g[u] = __ldg(ta.gh + (i0 + u * kStep));
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < kUnroll; ++u) {
-        if (row[u] == 0xffffffffu || !qvalid) continue;
-        const u32 gq = static_cast<u32>(quantize(g[u].x, sc.sg));
-        const u32 hq = static_cast<u32>(quantize(g[u].y, sc.sh));
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int jj = (j + s) & 3;
-          const u32 b = (word[u] >> (8 * jj)) & 0xffu;
-          if (MB < 256 && b >= u32(MB)) continue;
-          const int cell = int(b) * kFT + jj * kQPR + q;
-          atomicAdd(Lg + cell, gq);
-          atomicAdd(Lh + cell, hq);
-        }
-      }
-    }
-    if (multi) {
-      __syncthreads();
-      for (int i = threadIdx.x; i < kCells; i += THREADS) {
-        Wg[i] += static_cast<long long>(static_cast<int>(Lg[i]));
-        Wh[i] += static_cast<long long>(Lh[i]);
-        Lg[i] = 0u;
-        Lh[i] = 0u;
-      }
-      __syncthreads();
-    }
-  }
-  __syncthreads();
-
-  i64* out = hist + u64(t.slot) * F * (2 * kMaxBins);
-  for (int idx = threadIdx.x; idx < kCells; idx += THREADS) {
-    const long long gs = multi ? Wg[idx] : static_cast<long long>(static_cast<int>(Lg[idx]));
-    const long long hs = multi ? Wh[idx] : static_cast<long long>(Lh[idx]);
-    if (!(gs | hs)) continue;
-    const int b = idx / kFT, col = idx % kFT;
-    const u32 f = t.f0 + 4 * (col % kQPR) + col / kQPR;
-    if (f >= F) continue;
-    unsigned long long* cell = reinterpret_cast<unsigned long long*>(out + (u64(f) * kMaxBins + b) * 2);
-    atomicAdd(cell, static_cast<unsigned long long>(gs));
-    atomicAdd(cell + 1, static_cast<unsigned long long>(hs));
+template <bool QUANT>
+__device__ __forceinline__ void load_q(const TreeArrays& ta, const Scales& sc, u32 i, u32& gq, u32& hq) {
+  if (QUANT) {
+    const int2 v = __ldg(reinterpret_cast<const int2*>(ta.gh) + i);
+    gq = u32(v.x);
+    hq = u32(v.y);
+  } else {
+    const float2 v = __ldg(ta.gh + i);
+    gq = u32(quantize(v.x, sc.sg));
+    hq = u32(quantize(v.y, sc.sh));
   }
 }
 
-template <int MB, int THREADS>
-void launch_hist_variant(const u8* bins, u64 bin_stride, u32 F, const TreeArrays* trees, const Scales* scales,
-                         const HistTask* tasks, u32 ntasks, i64* hist, cudaStream_t s) {
-  constexpr int kSmem = MB * kFT * (4 + 4 + 8 + 8);
+template <int MB, int THREADS, bool QUANT>
+__global__ void __launch_bounds__(THREADS) k_hist(HistArgs a) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  __shared__ u32 s_task;
+  constexpr int kCells = MB * kFT;          // u32 planes: [bin][feature]
+  constexpr int kWRow = MB + 1;              // int64 planes: [feature][bin], rows padded
+  constexpr int kWCells = kFT * kWRow;
+  constexpr int kWarps = THREADS / 32;
+  constexpr u32 kStep = u32(kWarps) * kRPW;
+  u32* Lg = reinterpret_cast<u32*>(smem);
+  u32* Lh = Lg + kCells;
+  long long* Wg = reinterpret_cast<long long*>(Lh + kCells);
+  long long* Wh = Wg + kWCells;
+  for (int i = threadIdx.x; i < kCells; i += THREADS) {
+    Lg[i] = 0u;
+    Lh[i] = 0u;
+  }
+  for (int i = threadIdx.x; i < kWCells; i += THREADS) {
+    Wg[i] = 0;
+    Wh[i] = 0;
+  }
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const u32 s = u32(lane) >> 1, h16 = u32(lane & 1) * 16u;  // row slot, feature half
+  const bool rot8 = (s & 8u) != 0, rot4 = (s & 4u) != 0;   // word rotation by s >> 2
+  const u32 rsh = 8u * (s & 3u);                           // byte rotation by s & 3
+  // column of atomic step j: feature 16h + ((s + j) & 15) of the tile
+  u32 colj[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) colj[j] = h16 + ((s + u32(j)) & 15u);
+  u32 key_slot = kNoRow, key_f0 = 0, key_tree = 0;  // current accumulation target (block-uniform)
+  u32 in_window = 0;                                // rows in the u32 planes since the last fold
+
+  auto fold = [&]() {
+    for (int i = threadIdx.x; i < kCells; i += THREADS) {
+      const int b = i / kFT, f = i % kFT;
+      Wg[f * kWRow + b] += static_cast<long long>(static_cast<int>(Lg[i]));
+      Wh[f * kWRow + b] += static_cast<long long>(Lh[i]);
+      Lg[i] = 0u;
+      Lh[i] = 0u;
+    }
+  };
+
+  for (;;) {
+    if (threadIdx.x == 0) s_task = atomicAdd(a.counter, 1u);
+    __syncthreads();  // also: every warp has finished the previous task
+    const u32 ti = s_task;
+    const bool done = ti >= a.ntasks;
+    HistTask t{};
+    if (!done) t = a.tasks[ti];
+    const bool same = !done && t.slot == key_slot && t.f0 == key_f0 && t.tree == key_tree;
+    if (!same && key_slot != kNoRow) {
+      fold();
+      __syncthreads();
+      // consecutive threads take consecutive bins of one feature: the global
+      // atomics of a warp cover one contiguous 512-byte run
+      i64* out = a.hist + u64(key_slot) * a.F * (2 * kMaxBins);
+      for (int idx = threadIdx.x; idx < kCells; idx += THREADS) {
+        const int f = idx / MB, b = idx % MB;
+        const long long gs = Wg[f * kWRow + b], hs = Wh[f * kWRow + b];
+        Wg[f * kWRow + b] = 0;
+        Wh[f * kWRow + b] = 0;
+        if (!(gs | hs) || key_f0 + u32(f) >= a.F) continue;
+        unsigned long long* cell = reinterpret_cast<unsigned long long*>(out + (u64(key_f0 + f) * kMaxBins + b) * 2);
+        atomicAdd(cell, static_cast<unsigned long long>(gs));
+        atomicAdd(cell + 1, static_cast<unsigned long long>(hs));
+      }
+      key_slot = kNoRow;
+      in_window = 0;
+    }
+    if (done) break;
+    __syncthreads();  // s_task is read by all before thread 0 rewrites it
+    key_slot = t.slot;
+    key_f0 = t.f0;
+    key_tree = t.tree;
+    const TreeArrays ta = a.trees[t.tree];
+    Scales sc{1.f, 1.f};
+    if (!QUANT) sc = a.scales[t.tree];
+    // halves past the row's bin_stride (last tile of a row) are never read
+    const bool qvalid = u64(t.f0) + h16 < a.bstride;
+    const u8* base = a.bins + t.f0 + h16;
+    u32 pos = u32(t.begin);
+    const u32 tend = u32(t.end);
+    while (pos < tend) {
+      const u32 room = u32(kWindowRows) - in_window;
+      const u32 end = (tend - pos) < room ? tend : pos + room;
+      for (u32 i0 = pos + u32(warp) * kRPW + s; i0 < end; i0 += kStep * kUnroll) {
+        u32 row[kUnroll];
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+          const u32 i = i0 + u * kStep;
+          row[u] = (i < end && qvalid) ? __ldg(ta.ridx + i) : kNoRow;
+        }
+        uint4 v[kUnroll];
+        u32 gq[kUnroll], hq[kUnroll];
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+          v[u] = make_uint4(0u, 0u, 0u, 0u);
+          gq[u] = 0u;
+          hq[u] = 0u;
+          if (row[u] != kNoRow) {
+            v[u] = __ldg(reinterpret_cast<const uint4*>(base + u64(row[u]) * a.bstride));
+            load_q<QUANT>(ta, sc, i0 + u * kStep, gq[u], hq[u]);
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+          if (row[u] == kNoRow) continue;
+          // rotate the 16 bytes right by s: byte j of w becomes byte (j + s) & 15 of the row half
+          u32 t0 = rot8 ? v[u].z : v[u].x, t1 = rot8 ? v[u].w : v[u].y;
+          u32 t2 = rot8 ? v[u].x : v[u].z, t3 = rot8 ? v[u].y : v[u].w;
+          const u32 x0 = rot4 ? t1 : t0, x1 = rot4 ? t2 : t1, x2 = rot4 ? t3 : t2, x3 = rot4 ? t0 : t3;
+          const u32 w[4] = {__funnelshift_r(x0, x1, rsh), __funnelshift_r(x1, x2, rsh),
+                            __funnelshift_r(x2, x3, rsh), __funnelshift_r(x3, x0, rsh)};
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const u32 b = (w[j >> 2] >> (8 * (j & 3))) & 0xffu;
+            if (MB < 256 && b >= u32(MB)) continue;
+            const u32 cell = b * kFT + colj[j];
+            atomicAdd(Lg + cell, gq[u]);
+            atomicAdd(Lh + cell, hq[u]);
+          }
+        }
+      }
+      in_window += end - pos;
+      pos = end;
+      if (in_window == u32(kWindowRows)) {
+        __syncthreads();
+        fold();
+        __syncthreads();
+        in_window = 0;
+      }
+    }
+  }
+}
+
+template <int MB, int THREADS, bool QUANT>
+void launch_hist_variant(const HistArgs& a, cudaStream_t s) {
+  constexpr int kSmem = MB * kFT * (4 + 4) + kFT * (MB + 1) * (8 + 8);
   static thread_local int configured_device = -1;
+  static thread_local int grid_cap = 0;
   int dev = 0;
   DP_CUDA(cudaGetDevice(&dev));
   if (configured_device != dev) {
-    DP_CUDA(cudaFuncSetAttribute(k_hist<MB, THREADS>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem));
+    DP_CUDA(cudaFuncSetAttribute(k_hist<MB, THREADS, QUANT>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem));
+    int sms = 0, per_sm = 0;
+    DP_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    DP_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_hist<MB, THREADS, QUANT>, THREADS, kSmem));
+    grid_cap = sms * (per_sm > 0 ? per_sm : 1);
     configured_device = dev;
   }
-  k_hist<MB, THREADS><<<ntasks, THREADS, kSmem, s>>>(bins, bin_stride, F, trees, scales, tasks, hist);
+  const u32 grid = a.ntasks < u32(grid_cap) ? a.ntasks : u32(grid_cap);
+  DP_CUDA(cudaMemsetAsync(a.counter, 0, sizeof(u32), s));
+  k_hist<MB, THREADS, QUANT><<<grid, THREADS, kSmem, s>>>(a);
 }
 
 // hist[dst] = parent[par] - hist[src]; one block handles 2048 int64 of one triple.
@@ -151,13 +235,18 @@ __global__ void __launch_bounds__(256) k_subtract(i64* hist, const i64* __restri
 
 }  // namespace
 
-void launch_histograms(const u8* bins, u64 bin_stride, u32 F, int max_bins, const TreeArrays* trees,
-                       const Scales* scales, const HistTask* tasks, u32 ntasks, i64* hist, cudaStream_t s) {
+void launch_histograms(const u8* bins, u64 bin_stride, u32 F, int max_bins, bool quantized_gh,
+                       const TreeArrays* trees, const Scales* scales, const HistTask* tasks, u32 ntasks,
+                       u32* counter, i64* hist, cudaStream_t s) {
   if (!ntasks) return;
-  if (max_bins <= 64)
-    launch_hist_variant<64, 512>(bins, bin_stride, F, trees, scales, tasks, ntasks, hist, s);
-  else
-    launch_hist_variant<256, 1024>(bins, bin_stride, F, trees, scales, tasks, ntasks, hist, s);
+  const HistArgs a{bins, bin_stride, F, ntasks, trees, scales, tasks, counter, hist};
+  if (max_bins <= 64) {
+    if (quantized_gh) launch_hist_variant<64, 512, true>(a, s);
+    else launch_hist_variant<64, 512, false>(a, s);
+  } else {
+    if (quantized_gh) launch_hist_variant<256, DP_HIST_THREADS, true>(a, s);
+    else launch_hist_variant<256, DP_HIST_THREADS, false>(a, s);
+  }
   after_launch("histograms");
 }
 
@@ -165,10 +254,9 @@ u64 hist_chunk_rows(u64 total_rows) {
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const u64 target = u64(sms) * 2;  // about two blocks per SM over the launch
-  u64 chunk = (total_rows + target - 1) / target;
-  chunk = (chunk + kWindowRows - 1) / kWindowRows * kWindowRows;
-  return chunk < u64(kWindowRows) ? u64(kWindowRows) : chunk;
+  const u64 target = u64(sms) * 4;  // about four tasks per SM, balanced by the task queue
+  const u64 chunk = (total_rows + target - 1) / target;
+  return chunk < 2048 ? 2048 : chunk;
 }
 
 void launch_subtract(i64* hist, const i64* parent_hist, u64 slot_elems, const u32* triples, u32 n, cudaStream_t s) {

@@ -14,24 +14,34 @@ namespace dp {
 
 namespace {
 
-__device__ __forceinline__ void warp_max_to(u32* dst, float v) {
-  u32 b = __float_as_uint(v);
+constexpr int kSharedClasses = 64;
+
+__device__ __forceinline__ u32 warp_max(u32 b) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) b = max(b, __shfl_xor_sync(0xffffffffu, b, o));
-  if ((threadIdx.x & 31) == 0 && b) atomicMax(dst, b);
+  return b;
 }
 
+// Maxima of |g| and h per class (float bits compare as unsigned for
+// non-negative values): per-thread registers for one class, per-block shared
+// counters for up to kSharedClasses classes, then one global atomic per
+// block and class.
 __global__ void __launch_bounds__(256) k_gradients(int objective, int K, const float* __restrict__ margin,
                                                     const float* __restrict__ label, u64 R, float2* __restrict__ gh,
                                                     u32* gmax, u32* hmax) {
+  __shared__ u32 smg[kSharedClasses], smh[kSharedClasses];
+  const bool shared_max = K <= kSharedClasses;
+  for (int k = threadIdx.x; k < kSharedClasses; k += blockDim.x) { smg[k] = 0u; smh[k] = 0u; }
+  __syncthreads();
+  u32 lg = 0u, lh = 0u;  // this thread's maxima when K == 1
   const u64 step = u64(gridDim.x) * blockDim.x;
   for (u64 base = u64(blockIdx.x) * blockDim.x; base < R; base += step) {
     const u64 r = base + threadIdx.x;
     const bool valid = r < R;
     const double y = valid ? double(label[r]) : 0.0;
     if (objective == kSquaredError || objective == kLogistic) {
-      float g = 0.f, h = 0.f;
       if (valid) {
+        float g, h;
         const double m = double(margin[r]);
         if (objective == kSquaredError) {
           g = float(m - y);
@@ -42,9 +52,9 @@ __global__ void __launch_bounds__(256) k_gradients(int objective, int K, const f
           h = float(fmax(p * (1.0 - p), 1e-16));
         }
         gh[r] = make_float2(g, h);
+        lg = max(lg, __float_as_uint(fabsf(g)));
+        lh = max(lh, __float_as_uint(h));
       }
-      warp_max_to(gmax, fabsf(g));
-      warp_max_to(hmax, h);
     } else {
       double mx = 0.0, s = 0.0;
       const float* m = margin + (valid ? r : 0) * u64(K);
@@ -61,10 +71,33 @@ __global__ void __launch_bounds__(256) k_gradients(int objective, int K, const f
           h = float(fmax(2.0 * pk * (1.0 - pk), 1e-16));
           gh[u64(k) * R + r] = make_float2(g, h);
         }
-        warp_max_to(gmax + k, fabsf(g));
-        warp_max_to(hmax + k, h);
+        const u32 wg = warp_max(__float_as_uint(fabsf(g))), wh = warp_max(__float_as_uint(h));
+        if ((threadIdx.x & 31) == 0 && (wg | wh)) {
+          if (shared_max) { atomicMax(smg + k, wg); atomicMax(smh + k, wh); }
+          else { atomicMax(gmax + k, wg); atomicMax(hmax + k, wh); }
+        }
       }
     }
+  }
+  if (objective == kSquaredError || objective == kLogistic) {
+    lg = warp_max(lg);
+    lh = warp_max(lh);
+    if ((threadIdx.x & 31) == 0) { atomicMax(smg, lg); atomicMax(smh, lh); }
+  }
+  __syncthreads();
+  if (shared_max)
+    for (int k = threadIdx.x; k < K; k += blockDim.x) {
+      if (smg[k]) atomicMax(gmax + k, smg[k]);
+      if (smh[k]) atomicMax(hmax + k, smh[k]);
+    }
+}
+
+__global__ void __launch_bounds__(256) k_quantize_gh(float2* gh, u64 R, int K, const Scales* __restrict__ sc) {
+  const u64 n = R * u64(K);
+  for (u64 i = u64(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += u64(gridDim.x) * blockDim.x) {
+    const Scales s = sc[i / R];
+    const float2 v = gh[i];
+    reinterpret_cast<int2*>(gh)[i] = make_int2(quantize(v.x, s.sg), quantize(v.y, s.sh));
   }
 }
 
@@ -132,6 +165,12 @@ void launch_gradients(int objective, int K, const float* margin, const float* la
 void launch_scales(int K, const u32* gmax_bits, const u32* hmax_bits, Scales* scales, cudaStream_t s) {
   k_scales<<<(K + 127) / 128, 128, 0, s>>>(K, gmax_bits, hmax_bits, scales);
   after_launch("scales");
+}
+
+void launch_quantize_gh(float2* gh, u64 R, int K, const Scales* scales, cudaStream_t s) {
+  if (!R) return;
+  k_quantize_gh<<<grid_for(R * u64(K), 256), 256, 0, s>>>(gh, R, K, scales);
+  after_launch("quantize_gh");
 }
 
 void launch_leaf_update(const LeafTask* tasks, u32 ntasks, float* margin, u32 K, cudaStream_t s) {

@@ -1,9 +1,16 @@
-// Row partition: stable split of every split node's position segment into
-// [left rows][right rows], moving the row index and the (g, h) pair together
-// so that the next histogram pass reads (g, h) contiguously.
+// Row partition: every split node's position segment becomes
+// [left rows][right rows]; the row index and the quantised (g, h) pair move
+// together so that the next histogram pass reads (g, h) contiguously.
 // Routing: bin <= split bin goes left (equivalent to x < split_condition);
 // the missing code follows default_left (native/class_tree_runtime_compare.cu:47,
 // native/class_runtime.cu:128).
+//
+// One pass: a block decides its task's rows (decision bits kept in shared
+// memory), reserves space in its node's left and right parts with one atomic
+// add on each of the node's cursors, then scatters: left rows upward from the
+// segment start, right rows downward from the segment end.  Row order inside a
+// segment depends on block scheduling, but nothing computed from a segment
+// does: histogram sums are integer and every row gets exactly one leaf.
 #include "kernels.h"
 
 namespace dp {
@@ -11,33 +18,40 @@ namespace dp {
 namespace {
 
 constexpr int kPartThreads = 256;
+constexpr int kIlp = 4;  // independent row gathers in flight per thread
 constexpr int kWordsPerTask = kPartChunk / 32;
+static_assert(kPartChunk % (kPartThreads * kIlp) == 0, "task rows are whole gather rounds");
 
 __device__ __forceinline__ bool goes_left(u8 b, const PartNode& nd) {
   if (nd.missing_is_bin && b == kMissingBin) return nd.default_left != 0;
   return int(b) <= nd.bin;
 }
 
-__global__ void __launch_bounds__(kPartThreads) k_part_count(const u8* __restrict__ bins, u64 bstride,
-                                                             const TreeArrays* __restrict__ trees,
-                                                             const PartNode* __restrict__ nodes,
-                                                             const PartTask* __restrict__ tasks, u32* __restrict__ flags,
-                                                             u32* __restrict__ left) {
+__global__ void __launch_bounds__(kPartThreads) k_partition(const u8* __restrict__ bins, u64 bstride,
+                                                            const TreeArrays* __restrict__ src,
+                                                            const TreeArrays* __restrict__ dst,
+                                                            const PartNode* __restrict__ nodes,
+                                                            const PartTask* __restrict__ tasks,
+                                                            u32* __restrict__ cursors) {
+  __shared__ u32 ballots[kWordsPerTask];
   __shared__ u32 wsum[kPartThreads / 32];
+  __shared__ u32 base_lr[2];
   const PartTask t = tasks[blockIdx.x];
   const PartNode nd = nodes[t.node];
-  const u32* ridx = trees[nd.tree].ridx;
+  const TreeArrays s = src[nd.tree];
+  const TreeArrays d = dst[nd.tree];
   const u8* col = bins + nd.feature;
-  u32* fl = flags + u64(blockIdx.x) * kWordsPerTask;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const u32 n = u32(t.end - t.begin);
+
+  // decisions
   u32 cnt = 0;
-  constexpr int kIlp = 4;  // independent row gathers in flight per thread
-  for (i64 base = t.begin; base < t.end; base += kPartThreads * kIlp) {
+  for (u32 base = 0; base < n; base += kPartThreads * kIlp) {
     u32 r[kIlp];
 #pragma unroll
     for (int u = 0; u < kIlp; ++u) {
-      const i64 i = base + u * kPartThreads + threadIdx.x;
-      r[u] = i < t.end ? __ldg(ridx + i) : 0xffffffffu;
+      const u32 i = base + u * kPartThreads + threadIdx.x;
+      r[u] = i < n ? __ldg(s.ridx + t.begin + i) : 0xffffffffu;
     }
     u8 b[kIlp];
 #pragma unroll
@@ -46,8 +60,7 @@ __global__ void __launch_bounds__(kPartThreads) k_part_count(const u8* __restric
     for (int u = 0; u < kIlp; ++u) {
       const bool go = r[u] != 0xffffffffu && goes_left(b[u], nd);
       const u32 ballot = __ballot_sync(0xffffffffu, go);
-      const i64 w0 = base + u * kPartThreads + warp * 32;
-      if (lane == 0 && w0 < t.end) fl[(w0 - t.begin) / 32] = ballot;
+      if (lane == 0) ballots[(base + u * kPartThreads) / 32 + warp] = ballot;
       cnt += go;
     }
   }
@@ -56,72 +69,46 @@ __global__ void __launch_bounds__(kPartThreads) k_part_count(const u8* __restric
   if (lane == 0) wsum[warp] = cnt;
   __syncthreads();
   if (threadIdx.x == 0) {
-    u32 s = 0;
-    for (int w = 0; w < kPartThreads / 32; ++w) s += wsum[w];
-    left[blockIdx.x] = s;
+    u32 left = 0;
+    for (int w = 0; w < kPartThreads / 32; ++w) left += wsum[w];
+    base_lr[0] = atomicAdd(cursors + 2 * t.node, left);
+    base_lr[1] = atomicAdd(cursors + 2 * t.node + 1, n - left);
   }
-}
+  __syncthreads();
 
-__global__ void __launch_bounds__(kPartThreads) k_part_scatter(const TreeArrays* __restrict__ src,
-                                                               const TreeArrays* __restrict__ dst,
-                                                               const PartNode* __restrict__ nodes,
-                                                               const PartTask* __restrict__ tasks,
-                                                               const u32* __restrict__ flags,
-                                                               const i64* __restrict__ left_off,
-                                                               const i64* __restrict__ right_off) {
-  __shared__ u32 wl[kPartThreads / 32];
-  const PartTask t = tasks[blockIdx.x];
-  const PartNode nd = nodes[t.node];
-  const TreeArrays s = src[nd.tree];
-  const TreeArrays d = dst[nd.tree];
-  const u32* fl = flags + u64(blockIdx.x) * kWordsPerTask;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  i64 lpos = nd.begin + left_off[blockIdx.x];
-  i64 rpos = nd.begin + nd.nleft + right_off[blockIdx.x];
-  for (i64 base = t.begin; base < t.end; base += kPartThreads) {
-    const i64 w0 = base + warp * 32;
-    const u32 ballot = w0 < t.end ? fl[(w0 - t.begin) / 32] : 0u;
-    if (lane == 0) wl[warp] = __popc(ballot);
-    __syncthreads();
-    u32 lbefore = 0, ltotal = 0;
+  // scatter, 256 positions per step; ranks from the stored ballots
+  u32 run_left = 0;
+  const i64 lbase = nd.begin + base_lr[0];
+  const i64 rtop = nd.end - 1 - i64(base_lr[1]);
+  for (u32 base = 0; base < n; base += kPartThreads) {
+    const u32 wi = base / 32 + warp;
+    const u32 ballot = base + warp * 32 < n ? ballots[wi] : 0u;
+    u32 before = 0, step_left = 0;
+#pragma unroll
     for (int w = 0; w < kPartThreads / 32; ++w) {
-      const u32 c = wl[w];
-      if (w < warp) lbefore += c;
-      ltotal += c;
+      const u32 c = (base + w * 32 < n) ? __popc(ballots[base / 32 + w]) : 0u;
+      if (w < warp) before += c;
+      step_left += c;
     }
-    const i64 rows_before = i64(warp) * 32;  // valid rows in earlier warps of this step
-    const i64 step_rows = (t.end - base) < kPartThreads ? (t.end - base) : i64(kPartThreads);
-    const i64 i = base + threadIdx.x;
-    if (i < t.end) {
-      const u32 lt = (1u << lane) - 1u;
+    const u32 i = base + threadIdx.x;
+    if (i < n) {
       const bool go = (ballot >> lane) & 1u;
-      const u32 lrank = lbefore + __popc(ballot & lt);
-      const i64 dstpos = go ? lpos + lrank
-                            : rpos + (rows_before + lane - i64(lrank));
-      d.ridx[dstpos] = s.ridx[i];
-      d.gh[dstpos] = s.gh[i];
+      const u32 lrank = run_left + before + __popc(ballot & ((1u << lane) - 1u));
+      const i64 to = go ? lbase + lrank : rtop - i64(i - lrank);
+      d.ridx[to] = s.ridx[t.begin + i];
+      d.gh[to] = s.gh[t.begin + i];
     }
-    lpos += ltotal;
-    rpos += step_rows - ltotal;
-    __syncthreads();
+    run_left += step_left;
   }
 }
 
 }  // namespace
 
-void launch_partition_count(const u8* bins, u64 bin_stride, const TreeArrays* trees, const PartNode* nodes,
-                            const PartTask* tasks, u32 ntasks, u32* flags, u32* left, cudaStream_t s) {
+void launch_partition(const u8* bins, u64 bin_stride, const TreeArrays* src, const TreeArrays* dst,
+                      const PartNode* nodes, const PartTask* tasks, u32 ntasks, u32* cursors, cudaStream_t s) {
   if (!ntasks) return;
-  k_part_count<<<ntasks, kPartThreads, 0, s>>>(bins, bin_stride, trees, nodes, tasks, flags, left);
-  after_launch("partition_count");
-}
-
-void launch_partition_scatter(const TreeArrays* src, const TreeArrays* dst, const PartNode* nodes,
-                              const PartTask* tasks, u32 ntasks, const u32* flags, const i64* left_off,
-                              const i64* right_off, cudaStream_t s) {
-  if (!ntasks) return;
-  k_part_scatter<<<ntasks, kPartThreads, 0, s>>>(src, dst, nodes, tasks, flags, left_off, right_off);
-  after_launch("partition_scatter");
+  k_partition<<<ntasks, kPartThreads, 0, s>>>(bins, bin_stride, src, dst, nodes, tasks, cursors);
+  after_launch("partition");
 }
 
 }  // namespace dp

@@ -71,13 +71,20 @@ void launch_scales(int K, const u32* gmax_bits, const u32* hmax_bits, Scales* sc
 
 // ---- histograms -------------------------------------------------------------
 // hist[slot][F][256][2] (int64) must be zeroed for every slot the tasks touch.
-// Every bin value must be < max_bins (<= 64 selects a smaller tile).
-void launch_histograms(const u8* bins, u64 bin_stride, u32 F, int max_bins, const TreeArrays* trees,
-                       const Scales* scales, const HistTask* tasks, u32 ntasks, i64* hist, cudaStream_t s);
+// Every bin value must be < max_bins (<= 64 selects a smaller tile).  With
+// quantized_gh the (g, h) arrays hold int32 pairs (see launch_quantize_gh);
+// otherwise fp32 pairs quantised with `scales`.  `counter` is one u32 of
+// device scratch (the task queue), reset by the launcher.  Positions must be
+// below 2^31.
+void launch_histograms(const u8* bins, u64 bin_stride, u32 F, int max_bins, bool quantized_gh,
+                       const TreeArrays* trees, const Scales* scales, const HistTask* tasks, u32 ntasks,
+                       u32* counter, i64* hist, cudaStream_t s);
 constexpr u32 kHistFeatureTile = 32;
-// Rows per histogram task for a launch over `total_rows` row-tiles: about two
-// tasks per SM, a multiple of the accumulation window.
+// Rows per histogram task for a launch over `total_rows` row-tiles (about
+// four tasks per SM; tasks tasks of one node and tile stay contiguous).
 u64 hist_chunk_rows(u64 total_rows);
+// gh[k][r] (fp32 pairs) -> int32 pairs rint(g * s_g), rint(h * s_h), in place.
+void launch_quantize_gh(float2* gh, u64 R, int K, const Scales* scales, cudaStream_t s);
 
 // hist[dst] = parent_hist[par] - hist[src] for each (par, src, dst) slot triple.
 void launch_subtract(i64* hist, const i64* parent_hist, u64 slot_elems, const u32* triples, u32 n, cudaStream_t s);
@@ -94,7 +101,7 @@ constexpr u32 kEvalFeatureChunk = 16;
 struct PartTask {
   u32 node;      // index into PartNode
   u32 pad;
-  i64 begin;     // positions [begin, end)
+  i64 begin;     // positions [begin, end), at most kPartChunk rows
   i64 end;
 };
 struct PartNode {
@@ -104,17 +111,15 @@ struct PartNode {
   i32 default_left;
   i32 missing_is_bin;  // has_missing[feature]
   i32 pad;
-  i64 begin;       // segment start
-  i64 nleft;       // filled by the host between count and scatter
+  i64 begin;           // segment [begin, end)
+  i64 end;
 };
-// Counts left-going rows per task (left[task]) and stores decision bits.
-void launch_partition_count(const u8* bins, u64 bin_stride, const TreeArrays* trees, const PartNode* nodes,
-                            const PartTask* tasks, u32 ntasks, u32* flags, u32* left, cudaStream_t s);
-// Scatters rows into the other buffer: left_off[task] / right_off[task] are
-// the exclusive offsets of the task's rows within its node's left / right part.
-void launch_partition_scatter(const TreeArrays* src, const TreeArrays* dst, const PartNode* nodes,
-                              const PartTask* tasks, u32 ntasks, const u32* flags, const i64* left_off,
-                              const i64* right_off, cudaStream_t s);
+// Splits every node's segment from `src` into `dst`: left rows fill
+// [begin, begin + nleft), right rows [begin + nleft, end).  cursors[2*node]
+// and cursors[2*node+1] (zeroed u32 scratch) end as the node's left and right
+// row counts.
+void launch_partition(const u8* bins, u64 bin_stride, const TreeArrays* src, const TreeArrays* dst,
+                      const PartNode* nodes, const PartTask* tasks, u32 ntasks, u32* cursors, cudaStream_t s);
 constexpr u32 kPartChunk = 4096;
 
 // ---- leaves -------------------------------------------------------------------

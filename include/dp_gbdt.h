@@ -143,12 +143,17 @@ DP_API int dp_gradients(int objective, int num_class, const float* margin, const
 DP_API int dp_hist_build(const uint8_t* bins, uint64_t bin_stride, uint32_t features, int32_t num_bins,
                          const float* gh, const uint32_t* ridx, const int64_t* seg_begin, const int64_t* seg_end,
                          int32_t nseg, float sg, float sh, int64_t* hist, void* stream);
+/* In place: gh[n][2] fp32 pairs -> int32 pairs rint(g*sg), rint(h*sh), the
+ * layout the training engine's histogram pass reads. */
+DP_API int dp_quantize_gh(float* gh, uint64_t n, float sg, float sh, void* stream);
 /* The same histogram build with its task list prepared once: dp_hist_prepare
  * uploads the tasks of the segments; dp_hist_run zeroes `hist` and enqueues
- * the kernel on `stream` without synchronising (for timing loops). */
+ * the kernel on `stream` without synchronising (for timing loops).  gh_kind 0:
+ * fp32 pairs quantised with sg/sh in the kernel; 1: int32 pairs from
+ * dp_quantize_gh. */
 DP_API int dp_hist_prepare(const uint8_t* bins, uint64_t bin_stride, uint32_t features, int32_t num_bins,
-                           const float* gh, const uint32_t* ridx, const int64_t* seg_begin, const int64_t* seg_end,
-                           int32_t nseg, float sg, float sh, int64_t* hist, void** out_plan);
+                           int32_t gh_kind, const void* gh, const uint32_t* ridx, const int64_t* seg_begin,
+                           const int64_t* seg_end, int32_t nseg, float sg, float sh, int64_t* hist, void** out_plan);
 DP_API int dp_hist_run(void* plan, void* stream);
 DP_API int dp_hist_free(void* plan);
 

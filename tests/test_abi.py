@@ -56,7 +56,7 @@ def test_parameters_follow_the_reference_tokens(dp):
     assert cfg["learner"]["gradient_booster"]["updater"][0]["name"] == "grow_gpu_hist"
     assert cfg["learner"]["objective"]["name"] == "multi:softmax"
     assert cfg["learner"]["learner_model_param"]["num_class"] == "3"
-    assert cfg["dp_b200_gbdt"]["quantiser"] == {"grad_bits": 17, "hess_bits": 18, "window_rows": 8192}
+    assert cfg["dp_b200_gbdt"]["quantiser"] == {"grad_bits": 17, "hess_bits": 18, "window_rows": 16383}
     assert b.boosted_rounds() == 0
 
 

@@ -178,3 +178,33 @@ def test_split_evaluation_matches_oracle(dp, orc, lam, alpha, gamma, mcw, nan_fr
     np.testing.assert_array_equal(gi[valid], oi[valid])
     np.testing.assert_array_equal(gg[valid].view(np.uint64), og[valid].view(np.uint64))
     np.testing.assert_array_equal(gl[valid], ol[valid])
+
+
+@pytest.mark.parametrize("F,nodes,nbins,R", [(32, 1, 256, 1_500_000), (128, 3, 256, 300_000), (48, 9, 64, 400_000)])
+def test_quantized_histogram_plan_matches_oracle(dp, orc, F, nodes, nbins, R):
+    """The engine's layout: int32 (g, h) pairs from dp_quantize_gh, tasks from a
+    prepared plan, many tasks per node and several accumulation windows."""
+    import ctypes
+    rng = np.random.default_rng(F + nodes)
+    stride = (F + 15) // 16 * 16
+    bins = rng.integers(0, nbins, (R, stride)).astype(np.uint8)
+    gh = np.stack([rng.standard_normal(R), rng.random(R)], 1).astype(np.float32)
+    ridx = rng.permutation(R).astype(np.uint32)
+    edges = np.concatenate([[0], np.sort(rng.choice(np.arange(1, R), nodes - 1, replace=False)), [R]]).astype(np.int64)
+    sb, se = np.ascontiguousarray(edges[:-1]), np.ascontiguousarray(edges[1:])
+    sg, sh = orc.quantizer(gh)
+    ghd = cuda(gh)
+    dp.check(dp.lib().dp_quantize_gh(ptr(ghd), R, sg, sh, None))
+    q = ghd.cpu().numpy().view(np.int32)
+    np.testing.assert_array_equal(q[:, 0], np.rint(gh[:, 0] * np.float32(sg)).astype(np.int32))
+    hist = torch.empty((nodes, F, 256, 2), dtype=torch.int64, device="cuda")
+    plan = ctypes.c_void_p()
+    binsd, ridxd = cuda(bins), cuda(ridx)
+    dp.check(dp.lib().dp_hist_prepare(ptr(binsd), stride, F, nbins, 1, ptr(ghd), ptr(ridxd), sb.ctypes.data,
+                                      se.ctypes.data, nodes, sg, sh, ptr(hist), ctypes.byref(plan)))
+    for _ in range(2):  # reruns must give the same result (the plan re-zeroes its output)
+        dp.check(dp.lib().dp_hist_run(plan, None))
+    torch.cuda.synchronize()
+    dp.check(dp.lib().dp_hist_free(plan))
+    ohist = orc.histograms(bins, F, gh, ridx, sb, se, sg, sh, threads=8)
+    np.testing.assert_array_equal(hist.cpu().numpy(), ohist)
