@@ -244,6 +244,37 @@ def hist_sweep(torch, dp, device, peak_gbs: float) -> list[dict]:
     return out
 
 
+def hist_case(rows: int, nodes: int, nbins: int, features: int = 32) -> None:
+    """One config-5 histogram case: random bins, seeded uniform row->node
+    assignment, node-grouped row lists, quantised (g, h); three launches."""
+    import ctypes
+    import torch
+    import dp_gbdt as dp
+    g = torch.Generator(device="cuda")
+    g.manual_seed(SEED + 5)
+    bins = torch.randint(0, nbins, (rows, features), dtype=torch.uint8, device="cuda", generator=g)
+    gh = torch.stack([torch.randn(rows, device="cuda", generator=g), torch.rand(rows, device="cuda", generator=g)],
+                     1).contiguous()
+    node = torch.randint(0, nodes, (rows,), device="cuda", generator=g)
+    ridx = torch.argsort(node, stable=True).to(torch.int32)
+    ghp = gh[ridx.long()].contiguous()
+    dp.check(dp.lib().dp_quantize_gh(ghp.data_ptr(), rows, 2.0 ** 15, 2.0 ** 16, None))
+    counts = torch.bincount(node, minlength=nodes).cpu().numpy()
+    edges = np.concatenate([[0], np.cumsum(counts)]).astype(np.int64)
+    sb, se = np.ascontiguousarray(edges[:-1]), np.ascontiguousarray(edges[1:])
+    hist = torch.empty((nodes, features, 256, 2), dtype=torch.int64, device="cuda")
+    plan = ctypes.c_void_p()
+    dp.check(dp.lib().dp_hist_prepare(bins.data_ptr(), features, features, nbins, 1, ghp.data_ptr(), ridx.data_ptr(),
+                                      sb.ctypes.data, se.ctypes.data, nodes, 2.0 ** 15, 2.0 ** 16, hist.data_ptr(),
+                                      ctypes.byref(plan)))
+    stream = torch.cuda.current_stream().cuda_stream
+    for _ in range(3):
+        dp.check(dp.lib().dp_hist_run(plan, stream))
+    torch.cuda.synchronize()
+    dp.check(dp.lib().dp_hist_free(plan))
+    print(json.dumps({"hist_case": [rows, nodes, nbins], "ok": True}))
+
+
 # --------------------------------------------------------------------------- main GPU arm
 def main() -> None:
     ap = argparse.ArgumentParser()
@@ -253,9 +284,15 @@ def main() -> None:
     ap.add_argument("--impl", default="b200")
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--hist-case", default=None,
+                    help="ROWS,NODES,BINS: only run the config-5 histogram on one small case (3 launches), "
+                         "for profilers")
     args = ap.parse_args()
     if args.impl == "reference":
         reference_arm(args)
+        return
+    if args.hist_case:
+        hist_case(*(int(v) for v in args.hist_case.split(",")))
         return
     assert args.warmup >= 3, "at least 3 warm-up rounds"
 
