@@ -97,6 +97,10 @@ bool ends_with(const std::string& s, const std::string& suf) {
 
 }  // namespace
 
+namespace dp {
+void set_last_error(const std::string& msg) { g_last_error = msg; }
+}  // namespace dp
+
 extern "C" {
 
 void XGBoostVersion(int* major, int* minor, int* patch) {

@@ -22,6 +22,8 @@ struct Error : std::runtime_error {
 };
 
 [[noreturn]] inline void fail(const std::string& msg) { throw Error(msg); }
+// Sets the thread-local message returned by XGBGetLastError (defined beside it).
+void set_last_error(const std::string& msg);
 inline void need(bool ok, const std::string& msg) {
   if (!ok) fail(msg);
 }

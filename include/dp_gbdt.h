@@ -157,6 +157,24 @@ DP_API int dp_hist_prepare(const uint8_t* bins, uint64_t bin_stride, uint32_t fe
 DP_API int dp_hist_run(void* plan, void* stream);
 DP_API int dp_hist_free(void* plan);
 
+/* dp_hist_build for callers that cannot allocate device memory (a process
+ * whose device memory is reserved up front by its own pool, or a latency path
+ * that must not call cudaMalloc/cudaFree).  No counterpart in the reference.
+ * Same arguments and result as dp_hist_build, but the scratch (task list, task
+ * counter, descriptors) lives in one fixed file-scope device array of about
+ * 1 MiB that every GPU loading the library keeps until exit; nothing is
+ * allocated per call.  Limit: at most 32768 histogram tasks, i.e. roughly
+ * (non-empty segments) x ceil(features / 32) <= 32768; larger calls fail with
+ * a message (XGBGetLastError) naming the need and the capacity.  The first
+ * call on a device looks up the array's device address, so make it before any
+ * stream capture.  Calls share the array: calls that overlap on the GPU (other
+ * streams or threads) race, so serialise them.  The task counter is zeroed on
+ * every call and only tasks written by the call are read. */
+DP_API int dp_hist_build_noalloc(const uint8_t* bins, uint64_t bin_stride, uint32_t features, int32_t num_bins,
+                                 const float* gh, const uint32_t* ridx, const int64_t* seg_begin,
+                                 const int64_t* seg_end, int32_t nseg, float sg, float sh, int64_t* hist,
+                                 void* stream);
+
 /* Best split per node from hist[N][F][256][2] (device) and quantised totals
  * totals[N][2] (host); outputs on the host: out_i[N][4] = feature, bin,
  * default_left, valid; out_gain[N]; out_left[N][2]. */
