@@ -56,6 +56,17 @@ enum Objective { kSquaredError = 0, kLogistic = 1, kSoftprob = 2, kSoftmax = 3 }
 
 thread_local std::string last_error;
 
+// Row-sharded runs: the only exchange steps are element-wise integer
+// all-reduces (op 0 = sum, 1 = max) over every rank's buffer.  A null
+// callback means a single rank.
+typedef void (*AllReduceFn)(int64_t* buf, int64_t n, int op, void* ctx);
+struct Comm {
+  AllReduceFn fn = nullptr;
+  void* ctx = nullptr;
+  void sum(int64_t* b, int64_t n) const { if (fn && n) fn(b, n, 0, ctx); }
+  void max(int64_t* b, int64_t n) const { if (fn && n) fn(b, n, 1, ctx); }
+};
+
 // ---------------------------------------------------------------------------
 // exp(x) in double: Cody & Waite (1980) argument reduction x = k*ln2 + r with
 // ln2 split into a 24-bit head (k*head is exact for |k| < 2^29) and a tail,
@@ -174,6 +185,126 @@ static inline uint8_t bin_of(float a, const float* cut, int nb, bool has_mv, flo
   return uint8_t(std::upper_bound(cut, cut + (nb - 1), a) - cut);
 }
 
+// ---------------------------------------------------------------------------
+// The same cut rule computed without sorting, by exact radix selection on the
+// monotone 32-bit key of each value (the GPU path's algorithm): counts per
+// 16-bit key prefix, then two 8-bit refinements restricted to at most 256
+// active prefixes per feature (prefixes holding a wanted rank, or every
+// non-empty prefix while the column may have <= B distinct values).  Counts
+// are summed over ranks, so every rank reaches the same cuts.
+static inline uint32_t fkey(float v) {
+  if (v == 0.0f) v = 0.0f;
+  uint32_t u;
+  std::memcpy(&u, &v, 4);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+static inline float keyf(uint32_t k) {
+  const uint32_t u = (k & 0x80000000u) ? (k & 0x7fffffffu) : ~k;
+  float v;
+  std::memcpy(&v, &u, 4);
+  return v;
+}
+static inline bool holds_target(int64_t base, int64_t cnt, int64_t n, int64_t B) {
+  if (cnt == 0) return false;
+  if (base == 0) return true;
+  const int64_t klo = (base * B + n - 1) / n;
+  int64_t khi = ((base + cnt) * B + n - 1) / n - 1;
+  if (khi > B - 1) khi = B - 1;
+  return klo <= khi;
+}
+
+Cuts radix_cuts(const float* x, uint64_t R, uint32_t F, uint64_t stride, int max_bin, bool has_mv, float mv,
+                const Comm& comm) {
+  struct Entry { uint32_t prefix; int64_t base, cnt; };
+  struct State { int64_t n = 0; int64_t B = 0; bool mode = false; std::vector<Entry> act; };
+  int64_t rtot = int64_t(R);
+  comm.sum(&rtot, 1);
+  std::vector<State> st(F);
+  std::vector<int64_t> cnt(size_t(F) * 65536, 0);
+  for (uint64_t r = 0; r < R; ++r)
+    for (uint32_t f = 0; f < F; ++f) {
+      const float v = x[r * stride + f];
+      if (!is_missing(v, has_mv, mv)) ++cnt[size_t(f) * 65536 + (fkey(v) >> 16)];
+    }
+  comm.sum(cnt.data(), int64_t(cnt.size()));
+  for (uint32_t f = 0; f < F; ++f) {
+    State& S = st[f];
+    const int64_t* c = &cnt[size_t(f) * 65536];
+    int64_t nz = 0;
+    for (int b = 0; b < 65536; ++b) { S.n += c[b]; nz += c[b] != 0; }
+    S.B = std::min(max_bin, 256);
+    if (S.n < rtot && S.B > 255) S.B = 255;
+    S.mode = nz <= S.B;
+    int64_t cum = 0;
+    for (int b = 0; b < 65536; ++b) {
+      if (c[b] && (S.mode || holds_target(cum, c[b], S.n, S.B))) S.act.push_back({uint32_t(b), cum, c[b]});
+      cum += c[b];
+    }
+  }
+  for (int shift : {16, 8}) {
+    std::vector<int64_t> c8(size_t(F) * 256 * 256, 0);
+    for (uint64_t r = 0; r < R; ++r)
+      for (uint32_t f = 0; f < F; ++f) {
+        const float v = x[r * stride + f];
+        if (is_missing(v, has_mv, mv)) continue;
+        const uint32_t k = fkey(v), pfx = k >> shift;
+        const auto& act = st[f].act;
+        auto it = std::lower_bound(act.begin(), act.end(), pfx,
+                                   [](const Entry& e, uint32_t p) { return e.prefix < p; });
+        if (it != act.end() && it->prefix == pfx)
+          ++c8[(size_t(f) * 256 + size_t(it - act.begin())) * 256 + ((k >> (shift - 8)) & 0xffu)];
+      }
+    comm.sum(c8.data(), int64_t(c8.size()));
+    for (uint32_t f = 0; f < F; ++f) {
+      State& S = st[f];
+      int64_t nz = 0;
+      for (size_t a = 0; a < S.act.size(); ++a)
+        for (int d = 0; d < 256; ++d) nz += c8[(size_t(f) * 256 + a) * 256 + d] != 0;
+      S.mode = S.mode && nz <= S.B;
+      std::vector<Entry> next;
+      for (size_t a = 0; a < S.act.size(); ++a) {
+        int64_t cum = S.act[a].base;
+        for (int d = 0; d < 256; ++d) {
+          const int64_t v = c8[(size_t(f) * 256 + a) * 256 + d];
+          if (v && (S.mode || holds_target(cum, v, S.n, S.B))) next.push_back({(S.act[a].prefix << 8) | uint32_t(d), cum, v});
+          cum += v;
+        }
+      }
+      S.act.swap(next);
+    }
+  }
+  Cuts out;
+  out.F = F;
+  out.cut.assign(size_t(F) * 256, 0.f);
+  out.nbins.assign(F, 1);
+  out.has_missing.assign(F, 0);
+  for (uint32_t f = 0; f < F; ++f) {
+    const State& S = st[f];
+    float* cf = &out.cut[size_t(f) * 256];
+    int nb = 0;
+    if (S.n > 0 && !S.act.empty()) {
+      if (S.mode) {
+        for (size_t i = 1; i < S.act.size(); ++i) cf[nb++] = keyf(S.act[i].prefix);
+      } else {
+        const uint32_t mn = S.act[0].prefix;
+        size_t e = 0;
+        uint32_t last = 0;
+        for (int64_t k = 1; k < S.B; ++k) {
+          const int64_t rank = (k * S.n) / S.B;
+          while (e + 1 < S.act.size() && S.act[e].base + S.act[e].cnt <= rank) ++e;
+          const uint32_t key = S.act[e].prefix;
+          if (key == mn || (nb > 0 && key <= last)) continue;
+          cf[nb++] = keyf(key);
+          last = key;
+        }
+      }
+    }
+    out.nbins[f] = uint16_t(nb + 1);
+    out.has_missing[f] = S.n < rtot;
+  }
+  return out;
+}
+
 void bin_matrix(const float* x, uint64_t R, uint32_t F, uint64_t stride, const Cuts& c, bool has_mv, float mv,
                 uint8_t* bins, uint64_t bstride, int threads) {
   parallel_for(int64_t(R), threads, [&](int64_t b, int64_t e, int) {
@@ -228,12 +359,22 @@ float quant_scale(float vmax, int bits) {
   return std::ldexp(1.0f, bits - e);
 }
 
-void quantizer(const float* gh, uint64_t R, float* sg, float* sh) {
+void quantizer(const float* gh, uint64_t R, float* sg, float* sh, const Comm& comm = Comm()) {
   float mg = 0.f, mh = 0.f;
   for (uint64_t r = 0; r < R; ++r) {
     mg = std::max(mg, std::fabs(gh[2 * r]));
     mh = std::max(mh, gh[2 * r + 1]);
   }
+  // non-negative floats order like their bit patterns
+  uint32_t bg, bh;
+  std::memcpy(&bg, &mg, 4);
+  std::memcpy(&bh, &mh, 4);
+  int64_t m[2] = {int64_t(bg), int64_t(bh)};
+  comm.max(m, 2);
+  bg = uint32_t(m[0]);
+  bh = uint32_t(m[1]);
+  std::memcpy(&mg, &bg, 4);
+  std::memcpy(&mh, &bh, 4);
   *sg = quant_scale(mg, kGradBits);
   *sh = quant_scale(mh, kHessBits);
 }
@@ -379,7 +520,7 @@ struct Tree {
 // Grows one tree.  ghp is the tree's (g,h) in row order; on return `leaf_of`
 // holds the leaf id of every row.
 Tree grow_tree(const uint8_t* bins, uint64_t bstride, uint32_t F, uint64_t R, const Cuts& c, const float* gh_rows,
-               float sg, float sh, const Params& p, std::vector<int32_t>& leaf_of) {
+               float sg, float sh, const Params& p, std::vector<int32_t>& leaf_of, const Comm& comm = Comm()) {
   Tree t;
   std::vector<uint32_t> ridx(R), ridx2(R);
   std::vector<float> ghp(gh_rows, gh_rows + 2 * R), ghp2(2 * R);
@@ -394,6 +535,7 @@ Tree grow_tree(const uint8_t* bins, uint64_t bstride, uint32_t F, uint64_t R, co
   {
     int64_t b = 0, e = int64_t(R);
     histograms(bins, bstride, F, ghp.data(), ridx.data(), &b, &e, 1, sg, sh, open[0].hist.data(), p.threads);
+    comm.sum(open[0].hist.data(), int64_t(hsz));
   }
   int64_t G0 = 0, H0 = 0;
   for (int b = 0; b < 256; ++b) { G0 += open[0].hist[2 * b]; H0 += open[0].hist[2 * b + 1]; }
@@ -439,6 +581,13 @@ Tree grow_tree(const uint8_t* bins, uint64_t bstride, uint32_t F, uint64_t R, co
       std::copy(ridx2.begin() + o.begin, ridx2.begin() + o.begin + o.count, ridx.begin() + o.begin);
       std::copy(ghp2.begin() + 2 * o.begin, ghp2.begin() + 2 * (o.begin + o.count), ghp.begin() + 2 * o.begin);
     }
+    // Row counts over all ranks decide which child is built directly.
+    std::vector<int64_t> gcnt(2 * split_idx.size());
+    for (size_t j = 0; j < split_idx.size(); ++j) {
+      gcnt[2 * j] = nleft[j];
+      gcnt[2 * j + 1] = open[split_idx[j]].count - nleft[j];
+    }
+    comm.sum(gcnt.data(), int64_t(gcnt.size()));
     // Children and their histograms.
     std::vector<int64_t> sb, se;
     std::vector<std::pair<size_t, int>> build;  // (index into next, which child)
@@ -468,7 +617,9 @@ Tree grow_tree(const uint8_t* bins, uint64_t bstride, uint32_t F, uint64_t R, co
       for (size_t j = 0; j < split_idx.size(); ++j) {
         Open& L = next[2 * j];
         Open& Rn = next[2 * j + 1];
-        size_t sm = (p.subtract && Rn.count < L.count) ? 2 * j + 1 : 2 * j;
+        (void)L;
+        (void)Rn;
+        size_t sm = (p.subtract && gcnt[2 * j + 1] < gcnt[2 * j]) ? 2 * j + 1 : 2 * j;
         small_idx.push_back(sm);
         if (!p.subtract) small_idx.push_back(2 * j + 1);
       }
@@ -479,6 +630,7 @@ Tree grow_tree(const uint8_t* bins, uint64_t bstride, uint32_t F, uint64_t R, co
       std::vector<int64_t> hs(hsz * small_idx.size());
       histograms(bins, bstride, F, ghp.data(), ridx.data(), sb.data(), se.data(), int64_t(small_idx.size()), sg, sh,
                  hs.data(), p.threads);
+      comm.sum(hs.data(), int64_t(hs.size()));
       for (size_t k = 0; k < small_idx.size(); ++k)
         next[small_idx[k]].hist.assign(hs.begin() + hsz * k, hs.begin() + hsz * (k + 1));
       if (p.subtract) {
@@ -519,6 +671,7 @@ struct Model {
   std::vector<float> label;
   std::vector<Tree> trees;
   std::vector<float> scales;  // per tree: sg, sh
+  Comm comm;
 };
 
 void train_rounds(Model& m, int rounds) {
@@ -531,10 +684,10 @@ void train_rounds(Model& m, int rounds) {
     for (int k = 0; k < K; ++k) {
       const float* ghk = gh.data() + size_t(k) * m.R * 2;
       float sg, sh;
-      quantizer(ghk, m.R, &sg, &sh);
+      quantizer(ghk, m.R, &sg, &sh, m.comm);
       m.scales.push_back(sg);
       m.scales.push_back(sh);
-      round_trees[k] = grow_tree(m.bins.data(), m.bstride, m.F, m.R, m.cuts, ghk, sg, sh, m.p, leaf_of[k]);
+      round_trees[k] = grow_tree(m.bins.data(), m.bstride, m.F, m.R, m.cuts, ghk, sg, sh, m.p, leaf_of[k], m.comm);
     }
     for (int k = 0; k < K; ++k) {
       const Tree& t = round_trees[k];
@@ -643,6 +796,50 @@ void* orc_train(const float* x, uint64_t R, uint32_t F, uint64_t stride, const f
     orc::last_error = e.what();
     return nullptr;
   }
+}
+
+// The same run over this rank's rows, with `fn` summing / maxing int64 buffers
+// over all ranks (null: one rank).  Cuts use the radix-selection search.
+void* orc_train_sharded(const float* x, uint64_t R, uint32_t F, uint64_t stride, const float* label, int objective,
+                        int K, int max_depth, int max_bin, double eta, double lambda, double alpha, double gamma,
+                        double mcw, float base_margin, int rounds, int threads, orc::AllReduceFn fn, void* ctx) {
+  try {
+    auto m = new orc::Model;
+    m->comm.fn = fn;
+    m->comm.ctx = ctx;
+    m->p.objective = objective;
+    m->p.K = K;
+    m->p.max_depth = max_depth;
+    m->p.max_bin = max_bin;
+    m->p.eta = eta; m->p.lambda = lambda; m->p.alpha = alpha; m->p.gamma = gamma; m->p.mcw = mcw;
+    m->p.base_margin = base_margin;
+    m->p.threads = std::max(1, threads);
+    m->R = R;
+    m->F = F;
+    m->cuts = orc::radix_cuts(x, R, F, stride, max_bin, false, 0.f, m->comm);
+    m->bstride = (F + 15) / 16 * 16;
+    m->bins.resize(std::max<uint64_t>(R, 1) * m->bstride);
+    orc::bin_matrix(x, R, F, stride, m->cuts, false, 0.f, m->bins.data(), m->bstride, m->p.threads);
+    m->label.assign(label, label + R);
+    m->margin.assign(R * K, base_margin);
+    orc::train_rounds(*m, rounds);
+    return m;
+  } catch (const std::exception& e) {
+    orc::last_error = e.what();
+    return nullptr;
+  }
+}
+
+int orc_radix_cuts(const float* x, uint64_t R, uint32_t F, uint64_t stride, int max_bin, int has_mv, float mv,
+                   float* cut, uint16_t* nbins, uint8_t* has_missing, orc::AllReduceFn fn, void* ctx) {
+  orc::Comm comm;
+  comm.fn = fn;
+  comm.ctx = ctx;
+  auto c = orc::radix_cuts(x, R, F, stride, max_bin, has_mv, mv, comm);
+  std::memcpy(cut, c.cut.data(), c.cut.size() * sizeof(float));
+  std::memcpy(nbins, c.nbins.data(), c.nbins.size() * sizeof(uint16_t));
+  std::memcpy(has_missing, c.has_missing.data(), c.has_missing.size());
+  return 0;
 }
 
 int orc_train_more(void* h, int rounds) {

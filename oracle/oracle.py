@@ -21,6 +21,9 @@ OBJECTIVES = {"reg:squarederror": 0, "binary:logistic": 1, "multi:softprob": 2, 
 
 _lib = None
 
+# all-reduce callback of the sharded runs: (int64* buf, n, op 0=sum 1=max, ctx)
+ALLREDUCE = C.CFUNCTYPE(None, C.POINTER(C.c_int64), C.c_int64, C.c_int, C.c_void_p)
+
 
 def lib() -> C.CDLL:
     global _lib
@@ -42,6 +45,10 @@ def lib() -> C.CDLL:
         L.orc_train.restype = P
         L.orc_train.argtypes = [P, u64, u32, u64, P, i32, i32, i32, i32, C.c_double, C.c_double, C.c_double,
                                 C.c_double, C.c_double, C.c_float, i32, i32, i32]
+        L.orc_train_sharded.restype = P
+        L.orc_train_sharded.argtypes = [P, u64, u32, u64, P, i32, i32, i32, i32, C.c_double, C.c_double, C.c_double,
+                                        C.c_double, C.c_double, C.c_float, i32, i32, ALLREDUCE, P]
+        L.orc_radix_cuts.argtypes = [P, u64, u32, u64, i32, i32, C.c_float, P, P, P, ALLREDUCE, P]
         L.orc_train_more.argtypes = [P, i32]
         L.orc_free.argtypes = [P]
         L.orc_num_trees.argtypes = [P]
@@ -76,6 +83,29 @@ def cuts(x: np.ndarray, max_bin: int = 256, threads: int = 1, missing: float | N
     lib().orc_cuts(_p(x), R, F, F, max_bin, int(missing is not None), float(missing or 0.0), _p(cut), _p(nb),
                    _p(hm), threads)
     return cut, nb, hm
+
+
+def radix_cuts(x: np.ndarray, max_bin: int = 256, allreduce=None, missing: float | None = None):
+    """Cuts by the radix-selection search (the GPU algorithm) over this rank's
+    rows; `allreduce(buf: np.ndarray[int64], op: int)` sums / maxes in place
+    over all ranks (None: one rank)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    R, F = x.shape
+    cut = np.zeros((F, 256), np.float32)
+    nb = np.zeros(F, np.uint16)
+    hm = np.zeros(F, np.uint8)
+    cb = _callback(allreduce)
+    lib().orc_radix_cuts(_p(x), R, F, F, max_bin, int(missing is not None), float(missing or 0.0), _p(cut), _p(nb),
+                         _p(hm), cb, None)
+    return cut, nb, hm
+
+
+def _callback(allreduce):
+    if allreduce is None:
+        return ALLREDUCE()
+    def fn(buf, n, op, ctx):
+        allreduce(np.ctypeslib.as_array(buf, shape=(n,)), op)
+    return ALLREDUCE(fn)
 
 
 def bin_matrix(x: np.ndarray, cut, nb, hm, threads: int = 1, missing: float | None = None) -> np.ndarray:
@@ -154,6 +184,28 @@ class Model:
                                  int(subtract))
         if not self.h:
             raise RuntimeError(lib().orc_last_error().decode())
+
+    @classmethod
+    def sharded(cls, x: np.ndarray, y: np.ndarray, allreduce, objective: str = "reg:squarederror",
+                num_class: int = 1, max_depth: int = 6, max_bin: int = 256, eta: float = 0.3, reg_lambda: float = 1.0,
+                alpha: float = 0.0, gamma: float = 0.0, min_child_weight: float = 1.0, base_margin: float = 0.0,
+                rounds: int = 1, threads: int = 1) -> "Model":
+        """Training over this rank's rows; `allreduce(buf, op)` combines int64
+        buffers over the ranks in place (op 0 = sum, 1 = max)."""
+        self = cls.__new__(cls)
+        self.x = np.ascontiguousarray(x, dtype=np.float32)
+        self.y = np.ascontiguousarray(y, dtype=np.float32)
+        R, F = self.x.shape
+        self.R, self.F = R, F
+        K = num_class if objective.startswith("multi:") else 1
+        self.K = K
+        self._cb = _callback(allreduce)
+        self.h = lib().orc_train_sharded(_p(self.x), R, F, F, _p(self.y), OBJECTIVES[objective], K, max_depth,
+                                         max_bin, eta, reg_lambda, alpha, gamma, min_child_weight, base_margin,
+                                         rounds, threads, self._cb, None)
+        if not self.h:
+            raise RuntimeError(lib().orc_last_error().decode())
+        return self
 
     def __del__(self):
         if getattr(self, "h", None):

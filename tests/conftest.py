@@ -4,7 +4,7 @@ import sys
 import pytest
 
 ROOT = pathlib.Path(__file__).resolve().parents[1]
-for sub in ("decision-programs_b200", "oracle"):
+for sub in ("decision-programs_b200", "oracle", "tests"):
     p = str(ROOT / sub)
     if p not in sys.path:
         sys.path.insert(0, p)
