@@ -80,8 +80,8 @@ def make_chunk(torch, c: int, device):
     return x, y
 
 
-def shard(torch, rank: int, world: int, device):
-    nchunks = ROWS // CHUNK
+def shard(torch, rank: int, world: int, device, rows: int = ROWS):
+    nchunks = rows // CHUNK
     mine = [c for c in range(nchunks) if c * world // nchunks == rank]
     xs, ys = zip(*(make_chunk(torch, c, device) for c in mine))
     return torch.cat(xs).contiguous(), torch.cat(ys).contiguous()
@@ -284,6 +284,9 @@ def main() -> None:
     ap.add_argument("--impl", default="b200")
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--rows", type=int, default=ROWS,
+                    help="total rows (default: config 4's 10M; smaller for profiler captures)")
     ap.add_argument("--hist-case", default=None,
                     help="ROWS,NODES,BINS: only run the config-5 histogram on one small case (3 launches), "
                          "for profilers")
@@ -317,7 +320,8 @@ def main() -> None:
     peaks = measured_peaks()
     peak_gbs = float(peaks["hbm_gbs"])
 
-    x, y = shard(torch, rank, world, device)
+    assert args.rows % CHUNK == 0 and args.rows // CHUNK >= world, f"--rows must be a multiple of {CHUNK}"
+    x, y = shard(torch, rank, world, device, args.rows)
     rows_local = x.shape[0]
     comm = None
     if world > 1:
@@ -363,7 +367,8 @@ def main() -> None:
     barrier()
     ms = max_over_ranks(ms_local)
     prof = b.profile()
-    value = ROWS * args.steps / (ms / 1e3)
+    prof.pop("log", None)
+    value = args.rows * args.steps / (ms / 1e3)
     hist = prof.get("histograms", {"launches": 0, "ms": 0.0, "alg_bytes": 0.0})
     hist_ms_per_launch = hist["ms"] / max(1, hist["launches"])
     achieved = hist["alg_bytes"] / max(1, hist["launches"]) / (hist_ms_per_launch / 1e3) / 1e9 if hist["ms"] else 0.0
@@ -376,33 +381,10 @@ def main() -> None:
     d.free()
 
     # ---- end to end through the C-ABI with host buffers
-    xh = torch.empty_like(x, device="cpu").pin_memory()
-    yh = torch.empty_like(y, device="cpu").pin_memory()
-    xh.copy_(x)
-    yh.copy_(y)
-    xd, yd = torch.empty_like(x), torch.empty_like(y)
+    e2e = None
+    if not args.no_e2e:
+        e2e = end_to_end(torch, dp, x, y, args, local, comm, barrier, max_over_ranks, world)
     del x, y
-    barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    xd.copy_(xh, non_blocking=True)
-    yd.copy_(yh, non_blocking=True)
-    torch.cuda.synchronize()
-    d2 = dp.DMatrix.from_torch(xd, yd)
-    b2 = dp.Booster(PARAMS | {"device": f"cuda:{local}"}, [d2])
-    if comm is not None:
-        b2.set_comm(comm)
-    rounds_e2e = args.warmup + args.steps
-    for i in range(rounds_e2e):
-        b2.update(d2, i)
-    raw = b2.save_raw()
-    e1.record()
-    torch.cuda.synchronize()
-    e2e_ms = max_over_ranks(e0.elapsed_time(e1))
-    e2e_value = ROWS * rounds_e2e / (e2e_ms / 1e3)
-    b2.free()
-    d2.free()
-    del xd, yd, xh, yh
     torch.cuda.empty_cache()
 
     sweep = None
@@ -428,12 +410,10 @@ def main() -> None:
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "u8 bins / int64 sums",
         "data": "synthetic (seeded), inputs larger than L2",
-        "config": {"workload": WORKLOAD, "rows": ROWS, "features": FEATURES, "max_depth": DEPTH, "max_bin": 256,
-                   "parallelism": f"rows sharded over {world} GPU(s)", "l2": "inputs (1.28 GB bins) exceed L2"},
-        "e2e": {"value": e2e_value, "unit": "rows*trees/s",
-                "h2d_bytes_per_step": int(ROWS * (FEATURES + 1) * 4 / rounds_e2e),
-                "d2h_bytes_per_step": int(len(raw) * world / rounds_e2e),
-                "note": f"host fp32 inputs -> DMatrix (cuts+bins) -> {rounds_e2e} rounds -> JSON model"},
+        "config": {"workload": WORKLOAD, "rows": args.rows, "features": FEATURES, "max_depth": DEPTH,
+                   "max_bin": 256, "parallelism": f"rows sharded over {world} GPU(s)",
+                   "l2": "inputs (1.28 GB bins) exceed L2"},
+        "e2e": e2e,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak_gbs, "unit": "GB/s",
                      "frac": achieved / peak_gbs, "traffic": traffic, "kernel": "k_hist",
                      "peak_source": "measured" if not peaks.get("fallback") else "fallback",
@@ -448,6 +428,39 @@ def main() -> None:
     if sweep is not None:
         line["hist_sweep"] = sweep
     print(json.dumps(line), flush=True)
+
+
+def end_to_end(torch, dp, x, y, args, local, comm, barrier, max_over_ranks, world) -> dict:
+    """The metric through the C-ABI from pinned host buffers: H2D copy, DMatrix
+    (cuts and bins), W+K rounds, the JSON model read back."""
+    xh = torch.empty_like(x, device="cpu").pin_memory()
+    yh = torch.empty_like(y, device="cpu").pin_memory()
+    xh.copy_(x)
+    yh.copy_(y)
+    xd, yd = torch.empty_like(x), torch.empty_like(y)
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    xd.copy_(xh, non_blocking=True)
+    yd.copy_(yh, non_blocking=True)
+    torch.cuda.synchronize()
+    d2 = dp.DMatrix.from_torch(xd, yd)
+    b2 = dp.Booster(PARAMS | {"device": f"cuda:{local}"}, [d2])
+    if comm is not None:
+        b2.set_comm(comm)
+    rounds_e2e = args.warmup + args.steps
+    for i in range(rounds_e2e):
+        b2.update(d2, i)
+    raw = b2.save_raw()
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1))
+    b2.free()
+    d2.free()
+    return {"value": args.rows * rounds_e2e / (e2e_ms / 1e3), "unit": "rows*trees/s",
+            "h2d_bytes_per_step": int(args.rows * (FEATURES + 1) * 4 / rounds_e2e),
+            "d2h_bytes_per_step": int(len(raw) * world / rounds_e2e),
+            "note": f"host fp32 inputs -> DMatrix (cuts+bins) -> {rounds_e2e} rounds -> JSON model"}
 
 
 if __name__ == "__main__":

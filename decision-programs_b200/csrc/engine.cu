@@ -1,6 +1,7 @@
 #include "engine.h"
 
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
 #include <sstream>
 
@@ -17,11 +18,15 @@ cudaEvent_t Profiler::take() {
   DP_CUDA(cudaEventCreate(&e));
   return e;
 }
-void Profiler::begin(cudaStream_t s, const char* name, double alg_bytes) {
-  if (!on_) return;
+int Profiler::begin(cudaStream_t s, const char* name, double alg_bytes) {
+  if (!on_) return -1;
   Pending p{take(), take(), name, alg_bytes};
   DP_CUDA(cudaEventRecord(p.a, s));
   pending_.push_back(p);
+  return int(pending_.size()) - 1;
+}
+void Profiler::set_bytes(int idx, double alg_bytes) {
+  if (idx >= 0 && size_t(idx) < pending_.size()) pending_[idx].bytes = alg_bytes;
 }
 void Profiler::end(cudaStream_t s) {
   if (!on_) return;
@@ -35,6 +40,8 @@ void Profiler::resolve() {
     st.launches += 1;
     st.ms += ms;
     st.bytes += p.bytes;
+    if (log_.size() >= 4096) log_.erase(log_.begin(), log_.begin() + 2048);
+    log_.push_back(Entry{p.name, ms, p.bytes});
     free_.push_back(p.a);
     free_.push_back(p.b);
   }
@@ -50,7 +57,11 @@ std::string Profiler::json() const {
     o << "\"" << kv.first << "\":{\"launches\":" << kv.second.launches << ",\"ms\":" << kv.second.ms
       << ",\"alg_bytes\":" << kv.second.bytes << "}";
   }
-  o << "}";
+  // the most recent launches in order: [name, ms, algorithmic bytes]
+  o << (first ? "" : ",") << "\"log\":[";
+  for (size_t i = 0; i < log_.size(); ++i)
+    o << (i ? "," : "") << "[\"" << log_[i].name << "\"," << log_[i].ms << "," << log_[i].bytes << "]";
+  o << "]}";
   return o.str();
 }
 Profiler::~Profiler() {
@@ -61,7 +72,14 @@ Profiler::~Profiler() {
 // ---------------------------------------------------------------- engine
 namespace {
 constexpr u32 kFT = kHistFeatureTile;
-constexpr i64 kLeafChunk = 16384;
+
+u64 env_u64(const char* name, u64 dflt) {
+  const char* v = std::getenv(name);
+  if (!v || !*v) return dflt;
+  char* end = nullptr;
+  const unsigned long long x = std::strtoull(v, &end, 10);
+  return (end && *end == 0) ? u64(x) : dflt;
+}
 }
 
 Engine::Engine(DMatrix& d, const TrainParams& p, Comm* comm) : d_(d), p_(p), comm_(comm), device_(d.device()) {
@@ -114,6 +132,11 @@ Engine::Engine(DMatrix& d, const TrainParams& p, Comm* comm) : d_(d), p_(p), com
   scales_.resize(K_);
   hist_counter_.resize(1);
   arena_.reserve(size_t(8) << 20);
+  ctr_h_.reserve(1);
+  DP_CUDA(cudaDeviceGetAttribute(&sms_, cudaDevAttrMultiProcessorCount, device_));
+  // testing knobs: force the exact-count path of deep levels
+  async_open_limit_ = env_u64("DP_ASYNC_OPEN_LIMIT", async_open_limit_);
+  async_hist_bytes_ = env_u64("DP_ASYNC_HIST_BYTES", async_hist_bytes_);
 }
 
 Engine::~Engine() {
@@ -137,7 +160,6 @@ T* Engine::stage(const std::vector<T>& v) {
   if (off + bytes > arena_.size()) {
     // all staged copies must land before the arena is replaced
     DP_CUDA(cudaStreamSynchronize(stream_));
-    prof_.resolve();
     size_t want = std::max(arena_.size() * 2, bytes + 4096);
     PinnedBuf<u8> fresh;
     fresh.reserve(want);
@@ -155,6 +177,56 @@ void Engine::upload(DevBuf<T>& dst, const std::vector<T>& v) {
   if (v.empty()) return;
   T* src = stage(v);
   DP_CUDA(cudaMemcpyAsync(dst.get(), src, v.size() * sizeof(T), cudaMemcpyHostToDevice, stream_));
+}
+
+template <class T>
+void Engine::grow(DevBuf<T>& b, size_t n) {
+  if (n <= b.size()) return;
+  DP_CUDA(cudaStreamSynchronize(stream_));
+  b.resize(n);
+}
+
+template <class T>
+void Engine::grow_keep(DevBuf<T>& b, size_t n) {
+  if (n <= b.size()) return;
+  DevBuf<T> fresh(n);
+  if (b.size()) DP_CUDA(cudaMemcpyAsync(fresh.get(), b.get(), b.size() * sizeof(T), cudaMemcpyDeviceToDevice, stream_));
+  DP_CUDA(cudaStreamSynchronize(stream_));
+  b = std::move(fresh);
+}
+
+RoundBuffers Engine::round_buffers(int depth, u64 cap_split, u64 cap_next) const {
+  const int c = depth & 1, n = 1 - c;
+  RoundBuffers b{};
+  b.nodes = nodes_.get();
+  b.next_id = next_id_.get();
+  b.tree_first = tree_first_.get();
+  b.open_cur = open_[c].get();
+  b.open_next = open_[n].get();
+  b.build = build_[c].get();
+  b.build_next = build_[n].get();
+  b.triples_next = triples_[n].get();
+  b.hist_tasks = hist_tasks_.get();
+  b.eval_nodes = eval_nodes_.get();
+  b.best = best_.get();
+  b.split_idx = split_idx_.get();
+  b.part_nodes = part_nodes_.get();
+  b.part_tasks = part_tasks_.get();
+  b.cursors = cursors_.get();
+  b.gleft = gleft_.get();
+  b.leaves = leaves_.get();
+  b.leaf_tasks = leaf_tasks_.get();
+  b.ctr = ctr_.get();
+  b.stats = stats_.get();
+  b.K = u32(K_);
+  b.maxn = u32(std::min<u64>(nodes_.size() / u64(K_), u64(1) << 31));
+  b.cap_split = cap_split;
+  b.cap_next = cap_next;
+  b.cap_hist_tasks = hist_tasks_.size();
+  b.cap_part_tasks = part_tasks_.size();
+  b.cap_leaves = leaves_.size();
+  b.cap_leaf_tasks = leaf_tasks_.size();
+  return b;
 }
 
 template <class T>
@@ -178,10 +250,13 @@ void Engine::boost_round(Model& m) {
   const int K = K_;
   const u64 R = R_;
   const u32 F = F_;
+  const int D = p_.max_depth;
   const u32 ftiles = (F + kFT - 1) / kFT;
+  const u32 nchunks = (F + kEvalFeatureChunk - 1) / kEvalFeatureChunk;
   const SplitParams sp = p_.split_params();
-  const std::vector<float>& cut = q_->cut_h;
-  const std::vector<u8>& hm = q_->has_missing_h;
+  const u64 Rt = std::max<u64>(q_->rows_total, 1);
+  const u64 RK = std::max<u64>(R, 1) * u64(K);
+  const u64 slot_bytes = slot_elems_ * sizeof(i64);
 
   // ---- gradients and quantiser scales
   DP_CUDA(cudaMemsetAsync(gmax_.get(), 0, K * sizeof(u32), stream_));
@@ -198,200 +273,154 @@ void Engine::boost_round(Model& m) {
   // (g, h) become exact int32 pairs once per round; every later pass reads them
   launch_quantize_gh(gh_[0].get(), R, K, scales_.get(), stream_);
   for (int k = 0; k < K; ++k) launch_iota(ridx_[0].get() + u64(k) * R, R, stream_);
-  const Scales* sc_h = download(scales_.get(), K);
 
-  std::vector<Tree> trees(K);
-  std::vector<std::vector<i64>> ngq(K), nhq(K);  // quantised node totals
-  std::vector<Open> open;
-  for (int k = 0; k < K; ++k) {
-    trees[k].klass = k;
-    trees[k].add_node(-1);
-    ngq[k].push_back(0);
-    nhq[k].push_back(0);
-    open.push_back(Open{k, 0, k, 0, i64(R), i64(q_->rows_total), 0, 0});
-  }
-  sync();
-  std::vector<Scales> scales(sc_h, sc_h + K);
+  // ---- round state: K roots, open at depth 0 and built directly
+  grow(ctr_, 1);
+  grow(stats_, size_t(D) + 1);
+  grow(next_id_, K);
+  grow(tree_first_, K);
+  grow(open_[0], K);
+  grow(build_[0], K);
+  grow_keep(nodes_, size_t(K));
+  RoundCounters* const ctr = ctr_.get();  // allocated once; never regrown
+  DP_CUDA(cudaMemsetAsync(stats_.get(), 0, (size_t(D) + 1) * sizeof(LevelStats), stream_));
+  launch_round_init(round_buffers(0, 0, 0), R, q_->rows_total, stream_);
 
-  std::vector<Leaf> leaves;
-  std::vector<std::pair<int, int>> build;   // (slot, index into open) of nodes built directly
-  std::vector<u32> triples;
-  for (int k = 0; k < K; ++k) build.push_back({k, k});
-  int set = 0, region = 0;
-  for (int depth = 0; depth < p_.max_depth && !open.empty(); ++depth) {
-    // ---- histograms of the build set (slots [0, nbuild) of this region)
-    const u64 nslots = std::max<u64>(open.size(), 1);
-    hist_[region].reserve(nslots * slot_elems_);
+  // Host-side upper bounds of the device counts, which size the buffers:
+  // open nodes of this level, node ids per tree, closed leaves.  Every open
+  // node holds at least one row over all ranks (a split with an empty side
+  // has gain -gamma <= 0), so open nodes never exceed K * rows.
+  u64 open_hi = u64(K), ids_hi = 1, leaves_hi = 0;
+  std::vector<int> pi_hist(D, -1), pi_sub(D, -1), pi_eval(D, -1);
+  int set = 0, region = 0, depth = 0;
+  for (; depth < D; ++depth) {
+    u64 nbuild_hi = depth == 0 ? u64(K) : (open_hi + 1) / 2;
+    if (open_hi > async_open_limit_ || open_hi * slot_bytes > async_hist_bytes_) {
+      DP_CUDA(cudaMemcpyAsync(ctr_h_.get(), ctr, sizeof(RoundCounters), cudaMemcpyDeviceToHost, stream_));
+      DP_CUDA(cudaStreamSynchronize(stream_));
+      open_hi = ctr_h_.get()->n_open;
+      nbuild_hi = ctr_h_.get()->n_build;
+      if (open_hi == 0) break;
+    }
+    const u64 next_hi = std::min<u64>(2 * open_hi, u64(K) * Rt);
+    const u64 ids_next = std::min<u64>({ids_hi + 2 * std::min<u64>(open_hi, u64(1) << depth),
+                                        (u64(1) << (depth + 2)) - 1, 2 * Rt + 1});
+    grow(hist_[region], std::max<u64>(open_hi, 1) * slot_elems_);
+    grow(hist_tasks_, (nbuild_hi + 4 * u64(sms_) + 1) * ftiles);
+    grow(eval_nodes_, open_hi);
+    grow(best_, open_hi);
+    grow(cand_, open_hi * nchunks);
+    grow(split_idx_, open_hi);
+    grow(part_nodes_, open_hi);
+    grow(cursors_, 2 * open_hi);
+    grow(gleft_, open_hi);
+    grow(part_tasks_, (RK + kPartChunk - 1) / kPartChunk + open_hi);
+    grow(open_[(depth + 1) & 1], next_hi);
+    grow(build_[(depth + 1) & 1], open_hi);
+    grow(triples_[(depth + 1) & 1], 3 * open_hi);
+    grow_keep(leaves_, leaves_hi + open_hi);
+    grow_keep(nodes_, ids_next * K);
+    const RoundBuffers rb = round_buffers(depth, open_hi, next_hi);
     i64* hist = hist_[region].get();
-    const u64 nbuild = build.size();
-    DP_CUDA(cudaMemsetAsync(hist, 0, nbuild * slot_elems_ * sizeof(i64), stream_));
-    std::vector<HistTask> tasks;
-    double rows_built = 0;
-    for (auto& b : build) rows_built += double(open[b.second].count);
-    const i64 chunk = i64(hist_chunk_rows(u64(rows_built) * ftiles));
-    for (auto& b : build) {
-      const Open& o = open[b.second];
-      if (o.count == 0) continue;
-      const i64 pieces = (o.count + chunk - 1) / chunk;
-      const i64 piece = (o.count + pieces - 1) / pieces;
-      for (u32 ft = 0; ft < ftiles; ++ft)
-        for (i64 s = o.begin; s < o.begin + o.count; s += piece)
-          tasks.push_back(HistTask{u32(b.first), ft * kFT, u32(o.tree), 0, s,
-                                   std::min<i64>(o.begin + o.count, s + piece)});
-    }
-    upload(hist_tasks_, tasks);
-    prof_.begin(stream_, "histograms", rows_built * (double(F) + 12.0) + double(nbuild) * slot_elems_ * 8.0);
+
+    // ---- histograms of the directly built nodes, then their siblings
+    launch_hist_tasks(rb, ftiles, depth, stream_);
+    launch_zero_slots(rb, hist, slot_elems_, comm_ ? nbuild_hi : 0, stream_);
+    pi_hist[depth] = prof_.begin(stream_, "histograms", 0.0);
     launch_histograms(q_->bins.get(), q_->bin_stride, F, max_bins_, true, tarr_[set].get(), scales_.get(),
-                      hist_tasks_.get(), u32(tasks.size()), hist_counter_.get(), hist, stream_);
+                      hist_tasks_.get(), 0, hist_counter_.get(), hist, stream_, &ctr->n_hist_tasks);
     prof_.end(stream_);
-    if (comm_) comm_->sum_i64(hist, nbuild * slot_elems_, stream_);
-    if (!triples.empty()) {
-      upload(triples_, triples);
-      prof_.begin(stream_, "subtract", double(triples.size() / 3) * slot_elems_ * 24.0);
-      launch_subtract(hist, hist_[1 - region].get(), slot_elems_, triples_.get(), u32(triples.size() / 3), stream_);
+    if (comm_) comm_->sum_i64(hist, nbuild_hi * slot_elems_, stream_);
+    if (depth > 0) {
+      pi_sub[depth] = prof_.begin(stream_, "subtract", 0.0);
+      launch_subtract_dev(hist, hist_[1 - region].get(), slot_elems_, triples_[depth & 1].get(), &ctr->n_triples,
+                          stream_);
       prof_.end(stream_);
+    } else {
+      launch_root_totals(rb, hist, slot_elems_, stream_);
     }
-    if (depth == 0) {
-      // root totals from feature 0 of each root histogram
-      std::vector<const i64*> h0(K);
-      for (int k = 0; k < K; ++k) h0[k] = download(hist + u64(k) * slot_elems_, 2 * kMaxBins);
-      sync();
-      for (int k = 0; k < K; ++k) {
-        i64 gq = 0, hq = 0;
-        for (int b = 0; b < kMaxBins; ++b) { gq += h0[k][2 * b]; hq += h0[k][2 * b + 1]; }
-        open[k].gq = gq;
-        open[k].hq = hq;
-        ngq[k][0] = gq;
-        nhq[k][0] = hq;
-      }
-    }
-    // ---- split evaluation
-    std::vector<EvalNode> en(open.size());
-    for (size_t i = 0; i < open.size(); ++i)
-      en[i] = EvalNode{u32(open[i].slot), u32(open[i].tree), open[i].gq, open[i].hq};
-    upload(eval_nodes_, en);
-    const u32 nchunks = (F + kEvalFeatureChunk - 1) / kEvalFeatureChunk;
-    cand_.reserve(open.size() * nchunks);
-    best_.reserve(open.size());
-    prof_.begin(stream_, "eval_splits", double(open.size()) * slot_elems_ * 8.0);
-    launch_eval_splits(hist, F, q_->nbins.get(), q_->has_missing.get(), eval_nodes_.get(), u32(open.size()),
-                       scales_.get(), sp, cand_.get(), best_.get(), stream_);
+
+    // ---- split evaluation and decisions
+    launch_make_eval(rb, stream_);
+    pi_eval[depth] = prof_.begin(stream_, "eval_splits", 0.0);
+    launch_eval_splits_dev(hist, F, q_->nbins.get(), q_->has_missing.get(), eval_nodes_.get(), &ctr->n_open,
+                           scales_.get(), sp, cand_.get(), best_.get(), stream_);
     prof_.end(stream_);
-    const SplitCand* best_h = download(best_.get(), open.size());
-    sync();
-    std::vector<SplitCand> best(best_h, best_h + open.size());
+    launch_decide(rb, q_->cut.get(), q_->has_missing.get(), depth, D, set, stream_);
 
-    std::vector<int> split;  // indices into open
-    for (size_t i = 0; i < open.size(); ++i) {
-      if (best[i].feature >= 0 && best[i].gain > 0.0) split.push_back(int(i));
-      else leaves.push_back(Leaf{open[i].tree, open[i].id, set, open[i].begin, open[i].count});
-    }
-    if (split.empty()) { open.clear(); break; }
-
-    // ---- partition
-    std::vector<PartNode> pn(split.size());
-    std::vector<PartTask> pt;
-    for (size_t j = 0; j < split.size(); ++j) {
-      const Open& o = open[split[j]];
-      const SplitCand& c = best[split[j]];
-      pn[j] = PartNode{u32(o.tree), c.feature, c.bin, c.default_left, i32(hm[c.feature]), 0, o.begin,
-                       o.begin + o.count};
-      for (i64 s = o.begin; s < o.begin + o.count; s += kPartChunk)
-        pt.push_back(PartTask{u32(j), 0, s, std::min<i64>(o.begin + o.count, s + kPartChunk)});
-    }
-    upload(part_nodes_, pn);
-    upload(part_tasks_, pt);
-    cursors_.reserve(2 * split.size());
-    DP_CUDA(cudaMemsetAsync(cursors_.get(), 0, 2 * split.size() * sizeof(u32), stream_));
+    // ---- partition and the children's segments
     prof_.begin(stream_, "partition", 0.0);
-    launch_partition(q_->bins.get(), q_->bin_stride, tarr_[set].get(), tarr_[1 - set].get(), part_nodes_.get(),
-                     part_tasks_.get(), u32(pt.size()), cursors_.get(), stream_);
+    launch_partition_dev(q_->bins.get(), q_->bin_stride, tarr_[set].get(), tarr_[1 - set].get(), part_nodes_.get(),
+                         part_tasks_.get(), &ctr->n_part_tasks, cursors_.get(), stream_);
     prof_.end(stream_);
-    const u32* cur_h = download(cursors_.get(), 2 * split.size());
-    sync();
-    std::vector<i64> nleft(split.size());
-    for (size_t j = 0; j < split.size(); ++j) {
-      nleft[j] = cur_h[2 * j];
-      need(i64(cur_h[2 * j]) + i64(cur_h[2 * j + 1]) == open[split[j]].count, "partition lost rows");
-    }
-    std::vector<i64> gleft(nleft);
-    if (comm_) {
-      counts_.reserve(std::max<size_t>(split.size(), 1));
-      upload(counts_, nleft);
-      comm_->sum_i64(counts_.get(), split.size(), stream_);
-      const i64* g_h = download(counts_.get(), split.size());
-      sync();
-      gleft.assign(g_h, g_h + split.size());
-    }
+    launch_copy_left(rb, stream_);
+    if (comm_) comm_->sum_i64(gleft_.get(), open_hi, stream_);
+    launch_children(rb, depth, D, stream_);
 
-    // ---- children
-    std::vector<Open> next;
-    const bool more = depth + 1 < p_.max_depth;
-    const u32 ns = u32(split.size());
-    build.clear();
-    triples.clear();
-    for (size_t j = 0; j < split.size(); ++j) {
-      const Open& o = open[split[j]];
-      const SplitCand& c = best[split[j]];
-      Tree& t = trees[o.tree];
-      const int lid = t.add_node(o.id);
-      const int rid = t.add_node(o.id);
-      t.left[o.id] = lid;
-      t.right[o.id] = rid;
-      ngq[o.tree].push_back(c.gl);
-      nhq[o.tree].push_back(c.hl);
-      ngq[o.tree].push_back(o.gq - c.gl);
-      nhq[o.tree].push_back(o.hq - c.hl);
-      t.feature[o.id] = c.feature;
-      t.cond[o.id] = cut[u64(c.feature) * kMaxBins + c.bin];
-      t.default_left[o.id] = u8(c.default_left);
-      t.loss_change[o.id] = float(c.gain);
-      const i64 gl_cnt = gleft[j], gr_cnt = o.gcount - gleft[j];
-      const bool right_small = gr_cnt < gl_cnt;
-      const int lslot = right_small ? int(ns + j) : int(j);
-      const int rslot = right_small ? int(j) : int(ns + j);
-      next.push_back(Open{o.tree, lid, lslot, o.begin, nleft[j], gl_cnt, c.gl, c.hl});
-      next.push_back(Open{o.tree, rid, rslot, o.begin + nleft[j], o.count - nleft[j], gr_cnt, o.gq - c.gl,
-                          o.hq - c.hl});
-      if (more) {
-        build.push_back({int(j), int(next.size()) - (right_small ? 1 : 2)});
-        triples.push_back(u32(o.slot));
-        triples.push_back(u32(j));
-        triples.push_back(u32(ns + j));
-      }
-    }
-    open.swap(next);
+    leaves_hi += open_hi;
+    open_hi = next_hi;
+    ids_hi = ids_next;
     set = 1 - set;
     region = 1 - region;
-    if (!more) break;
   }
-  for (const Open& o : open) leaves.push_back(Leaf{o.tree, o.id, set, o.begin, o.count});
 
-  // ---- node statistics, leaf values and margin update
-  std::vector<LeafTask> lt;
-  for (const Leaf& l : leaves) {
-    Tree& t = trees[l.tree];
-    const float v = leaf_weight(ngq[l.tree][l.id], nhq[l.tree][l.id], scales[l.tree].sg, scales[l.tree].sh, sp);
-    t.cond[l.id] = v;
-    t.feature[l.id] = 0;
-    const u32* ridx = ridx_[l.set].get() + u64(l.tree) * R;
-    for (i64 s = l.begin; s < l.begin + l.count; s += kLeafChunk)
-      lt.push_back(LeafTask{ridx, s, std::min<i64>(l.begin + l.count, s + kLeafChunk), v, u32(l.tree)});
-  }
-  for (int k = 0; k < K; ++k) {
-    Tree& t = trees[k];
-    const double ish = 1.0 / double(scales[k].sh);
-    for (size_t id = 0; id < t.size(); ++id) {
-      t.base_weight[id] = leaf_weight(ngq[k][id], nhq[k][id], scales[k].sg, scales[k].sh, sp);
-      t.sum_hess[id] = float(double(nhq[k][id]) * ish);
-    }
-  }
-  upload(leaf_tasks_, lt);
+  // ---- nodes still open close as leaves; leaf values and margin update
+  grow_keep(leaves_, leaves_hi + open_hi);
+  leaves_hi += open_hi;
+  grow(leaf_tasks_, (RK + kLeafChunkRows - 1) / kLeafChunkRows + leaves_hi);
+  const RoundBuffers rb = round_buffers(depth, open_hi, open_hi);
+  launch_decide(rb, q_->cut.get(), q_->has_missing.get(), D, D, set, stream_);
+  u32* const sets[2] = {ridx_[0].get(), ridx_[1].get()};
+  launch_leaf_values(rb, scales_.get(), sp, sets, R, stream_);
   prof_.begin(stream_, "leaf_update", double(R) * K * 12.0);
-  launch_leaf_update(leaf_tasks_.get(), u32(lt.size()), margin_.get(), u32(K), stream_);
+  launch_leaf_update_dev(leaf_tasks_.get(), &ctr->n_leaf_tasks, margin_.get(), u32(K), stream_);
   prof_.end(stream_);
-  sync();
-  for (auto& t : trees) m.trees.push_back(std::move(t));
+
+  // ---- one read-back of the round
+  const u64 ids_read = std::min<u64>(ids_hi, nodes_.size() / u64(K));
+  DP_CUDA(cudaStreamSynchronize(stream_));
+  arena_off_ = 0;
+  arena_.reserve(ids_read * K * sizeof(NodeRec) + sizeof(RoundCounters) + K * (sizeof(u32) + sizeof(Scales)) +
+                 (size_t(D) + 1) * sizeof(LevelStats) + 5 * 256);
+  const RoundCounters* c_h = download(ctr, 1);
+  const u32* nid_h = download(next_id_.get(), K);
+  const Scales* sc_h = download(scales_.get(), K);
+  const LevelStats* st_h = download(stats_.get(), size_t(D) + 1);
+  const NodeRec* nd_h = download(nodes_.get(), ids_read * K);
+  DP_CUDA(cudaStreamSynchronize(stream_));
+  const u32 ovf = c_h->overflow;
+  if (ovf & kOvfLostRows) fail("partition lost rows");
+  if (ovf) fail("internal error: a per-round work list overflowed (flags " + std::to_string(ovf) + ")");
+  for (int d = 0; d < D; ++d) {
+    const LevelStats& st = st_h[d];
+    prof_.set_bytes(pi_hist[d], double(st.rows_built) * (double(F) + 12.0) + double(st.n_build) * slot_bytes);
+    prof_.set_bytes(pi_sub[d], double(st.n_build) * slot_bytes * 3.0);
+    prof_.set_bytes(pi_eval[d], double(st.n_open) * slot_bytes);
+  }
+  prof_.resolve();
+
+  for (int k = 0; k < K; ++k) {
+    const u64 n = nid_h[k];
+    need(n >= 1 && n <= ids_read, "internal error: node count of a tree out of range");
+    Tree t;
+    t.klass = k;
+    const Scales sc = sc_h[k];
+    const double ish = 1.0 / double(sc.sh);
+    for (u64 id = 0; id < n; ++id) {
+      const NodeRec& r = nd_h[id * K + k];
+      t.add_node(r.parent);
+      t.left[id] = r.left;
+      t.right[id] = r.right;
+      t.feature[id] = r.left < 0 ? 0 : r.feature;
+      t.cond[id] = r.cond;
+      t.default_left[id] = u8(r.default_left);
+      t.loss_change[id] = r.gain;
+      t.base_weight[id] = leaf_weight(r.gq, r.hq, sc.sg, sc.sh, sp);
+      t.sum_hess[id] = float(double(r.hq) * ish);
+    }
+    m.trees.push_back(std::move(t));
+  }
+  arena_off_ = 0;
   m.iteration_indptr.push_back(int(m.trees.size()));
 }
 

@@ -2,6 +2,8 @@
 // boosting round level-synchronously on the GPU (one histogram, split and
 // partition launch per level for all K trees), with sibling subtraction and
 // row-sharded histogram sums over `comm` when several GPUs share the rows.
+// Every per-level decision is taken on the device (level.h), so a round is
+// enqueued without waiting and its trees are read back once at the end.
 #pragma once
 #include <cuda_runtime.h>
 
@@ -13,6 +15,7 @@
 #include "common.h"
 #include "dmatrix.h"
 #include "kernels.h"
+#include "level.h"
 #include "model.h"
 
 namespace dp {
@@ -22,11 +25,14 @@ class Profiler {
  public:
   void enable(bool on) { on_ = on; }
   bool enabled() const { return on_; }
-  void begin(cudaStream_t s, const char* name, double alg_bytes);
+  // Returns the launch's index for set_bytes (-1 when disabled).
+  int begin(cudaStream_t s, const char* name, double alg_bytes);
+  // Algorithmic bytes of a launch known only after it ran (before resolve()).
+  void set_bytes(int idx, double alg_bytes);
   void end(cudaStream_t s);
   void resolve();  // after the stream has been synchronised
   std::string json() const;
-  void reset() { stats_.clear(); }
+  void reset() { stats_.clear(); log_.clear(); }
   ~Profiler();
 
  private:
@@ -36,6 +42,8 @@ class Profiler {
   std::vector<Pending> pending_;
   std::vector<cudaEvent_t> free_;
   std::map<std::string, Stat> stats_;
+  struct Entry { std::string name; float ms; double bytes; };
+  std::vector<Entry> log_;  // the most recent launches, bounded
   cudaEvent_t take();
 };
 
@@ -56,14 +64,6 @@ class Engine {
   std::vector<float> margins() const;
 
  private:
-  struct Open {
-    int tree, id, slot;
-    i64 begin, count;      // local positions
-    i64 gcount;            // rows over all ranks
-    i64 gq, hq;
-  };
-  struct Leaf { int tree, id, set; i64 begin, count; };
-
   void sync();
   template <class T>
   T* stage(const std::vector<T>& v);  // copies into the pinned arena
@@ -71,6 +71,13 @@ class Engine {
   void upload(DevBuf<T>& dst, const std::vector<T>& v);
   template <class T>
   const T* download(const T* src, size_t n);  // into the arena; valid after sync()
+  // Capacity growth between launches: `grow` drops the contents, `grow_keep`
+  // keeps them; both wait for the stream first, since it may still use them.
+  template <class T>
+  void grow(DevBuf<T>& b, size_t n);
+  template <class T>
+  void grow_keep(DevBuf<T>& b, size_t n);
+  RoundBuffers round_buffers(int depth, u64 cap_split, u64 cap_next) const;
 
   DMatrix& d_;
   TrainParams p_;
@@ -93,14 +100,27 @@ class Engine {
   DevBuf<i64> hist_[2];
   DevBuf<HistTask> hist_tasks_;
   DevBuf<u32> hist_counter_;
-  DevBuf<u32> triples_;
   DevBuf<EvalNode> eval_nodes_;
   DevBuf<SplitCand> cand_, best_;
   DevBuf<PartNode> part_nodes_;
   DevBuf<PartTask> part_tasks_;
   DevBuf<u32> cursors_;
-  DevBuf<i64> counts_;
   DevBuf<LeafTask> leaf_tasks_;
+  // round state on the device (level.h)
+  DevBuf<NodeRec> nodes_;
+  DevBuf<u32> next_id_, tree_first_, split_idx_;
+  DevBuf<OpenRec> open_[2];
+  DevBuf<u32> build_[2], triples_[2];
+  DevBuf<i64> gleft_;
+  DevBuf<LeafRec> leaves_;
+  DevBuf<RoundCounters> ctr_;
+  DevBuf<LevelStats> stats_;
+  PinnedBuf<RoundCounters> ctr_h_;
+  int sms_ = 148;
+  // A level whose open-node bound exceeds either limit first reads the exact
+  // counts back (one small copy) and sizes its buffers by them.
+  u64 async_open_limit_ = u64(1) << 16;
+  u64 async_hist_bytes_ = u64(4) << 30;
 
   PinnedBuf<u8> arena_;
   size_t arena_off_ = 0;

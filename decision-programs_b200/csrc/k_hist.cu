@@ -43,6 +43,7 @@ struct HistArgs {
   u64 bstride;
   u32 F;
   u32 ntasks;
+  const u32* ntasks_dev;  // when set, the task count is read from device memory
   const TreeArrays* trees;
   const Scales* scales;
   const HistTask* tasks;
@@ -94,6 +95,7 @@ __global__ void __launch_bounds__(THREADS) k_hist(HistArgs a) {
   for (int j = 0; j < 16; ++j) colj[j] = h16 + ((s + u32(j)) & 15u);
   u32 key_slot = kNoRow, key_f0 = 0, key_tree = 0;  // current accumulation target (block-uniform)
   u32 in_window = 0;                                // rows in the u32 planes since the last fold
+  const u32 ntasks = a.ntasks_dev ? *a.ntasks_dev : a.ntasks;
 
   auto fold = [&]() {
     for (int i = threadIdx.x; i < kCells; i += THREADS) {
@@ -109,7 +111,7 @@ __global__ void __launch_bounds__(THREADS) k_hist(HistArgs a) {
     if (threadIdx.x == 0) s_task = atomicAdd(a.counter, 1u);
     __syncthreads();  // also: every warp has finished the previous task
     const u32 ti = s_task;
-    const bool done = ti >= a.ntasks;
+    const bool done = ti >= ntasks;
     HistTask t{};
     if (!done) t = a.tasks[ti];
     const bool same = !done && t.slot == key_slot && t.f0 == key_f0 && t.tree == key_tree;
@@ -213,7 +215,7 @@ void launch_hist_variant(const HistArgs& a, cudaStream_t s) {
     grid_cap = sms * (per_sm > 0 ? per_sm : 1);
     configured_device = dev;
   }
-  const u32 grid = a.ntasks < u32(grid_cap) ? a.ntasks : u32(grid_cap);
+  const u32 grid = (a.ntasks_dev || a.ntasks >= u32(grid_cap)) ? u32(grid_cap) : a.ntasks;
   DP_CUDA(cudaMemsetAsync(a.counter, 0, sizeof(u32), s));
   k_hist<MB, THREADS, QUANT><<<grid, THREADS, kSmem, s>>>(a);
 }
@@ -233,13 +235,43 @@ __global__ void __launch_bounds__(256) k_subtract(i64* hist, const i64* __restri
   }
 }
 
+// Same subtraction with the triple count in device memory: a fixed grid walks
+// (triple, 2048-element chunk) work items.
+__global__ void __launch_bounds__(256) k_subtract_dev(i64* hist, const i64* __restrict__ parent, u64 slot_elems,
+                                                      const u32* __restrict__ triples, const u32* __restrict__ n_dev) {
+  const u32 n = *n_dev;
+  const u64 n2 = slot_elems / 2;
+  const u64 chunks = (n2 + 2047) / 2048;
+  for (u64 w = blockIdx.x; w < u64(n) * chunks; w += gridDim.x) {
+    const u32 tr = u32(w / chunks);
+    const u64 c0 = (w % chunks) * 2048;
+    const u32 par = triples[3 * tr], src = triples[3 * tr + 1], dst = triples[3 * tr + 2];
+    const longlong2* a = reinterpret_cast<const longlong2*>(parent + u64(par) * slot_elems);
+    const longlong2* b = reinterpret_cast<const longlong2*>(hist + u64(src) * slot_elems);
+    longlong2* c = reinterpret_cast<longlong2*>(hist + u64(dst) * slot_elems);
+    for (u64 i = c0 + threadIdx.x; i < c0 + 2048 && i < n2; i += blockDim.x) {
+      const longlong2 x = a[i], y = b[i];
+      c[i] = make_longlong2(x.x - y.x, x.y - y.y);
+    }
+  }
+}
+
 }  // namespace
+
+void launch_subtract_dev(i64* hist, const i64* parent_hist, u64 slot_elems, const u32* triples, const u32* n_dev,
+                         cudaStream_t s) {
+  int dev = 0, sms = 148;
+  DP_CUDA(cudaGetDevice(&dev));
+  DP_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  k_subtract_dev<<<sms * 8, 256, 0, s>>>(hist, parent_hist, slot_elems, triples, n_dev);
+  after_launch("subtract");
+}
 
 void launch_histograms(const u8* bins, u64 bin_stride, u32 F, int max_bins, bool quantized_gh,
                        const TreeArrays* trees, const Scales* scales, const HistTask* tasks, u32 ntasks,
-                       u32* counter, i64* hist, cudaStream_t s) {
-  if (!ntasks) return;
-  const HistArgs a{bins, bin_stride, F, ntasks, trees, scales, tasks, counter, hist};
+                       u32* counter, i64* hist, cudaStream_t s, const u32* ntasks_dev) {
+  if (!ntasks && !ntasks_dev) return;
+  const HistArgs a{bins, bin_stride, F, ntasks, ntasks_dev, trees, scales, tasks, counter, hist};
   if (max_bins <= 64) {
     if (quantized_gh) launch_hist_variant<64, 512, true>(a, s);
     else launch_hist_variant<64, 512, false>(a, s);

@@ -1,0 +1,396 @@
+// Per-level bookkeeping kernels of a boosting round (see level.h).  They are
+// tiny next to the histogram and partition passes; what they buy is that no
+// count ever has to travel to the host inside a round.  The work lists they
+// write (histogram, partition and margin-update tasks) are the ones the host
+// used to build, in the same order.
+#include "level.h"
+
+namespace dp {
+
+namespace {
+
+constexpr int kBook = 1024;  // threads of the single-block bookkeeping kernels
+constexpr i64 kLeafChunk = kLeafChunkRows;
+
+// Exclusive block-wide scan (blockDim.x == kBook); *total gets the sum.
+__device__ u64 scan_block(u64 v, u64* total) {
+  __shared__ u64 ws[33];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  u64 incl = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const u64 t = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += t;
+  }
+  if (lane == 31) ws[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    const u64 w = ws[lane];
+    u64 wi = w;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const u64 t = __shfl_up_sync(0xffffffffu, wi, o);
+      if (lane >= o) wi += t;
+    }
+    ws[lane] = wi - w;
+    if (lane == 31) ws[32] = wi;
+  }
+  __syncthreads();
+  const u64 out = ws[warp] + incl - v;
+  const u64 tot = ws[32];
+  __syncthreads();
+  *total = tot;
+  return out;
+}
+
+// Expands a chunk of up to kBook items into tasks with the whole block: the
+// calling thread's item owns `cnt` tasks; emit(j, q, t) runs once per task
+// with j the owning thread, q the task's index within the item and t its
+// global index base + (position in chunk), for t < cap only.  Returns the
+// chunk's task count (all of them, including any past cap).
+template <class Emit>
+__device__ u64 expand(u64 cnt, u64 base, u64 cap, Emit emit) {
+  __shared__ u64 s_off[kBook];
+  u64 n = 0;
+  s_off[threadIdx.x] = scan_block(cnt, &n);
+  __syncthreads();
+  for (u64 t = threadIdx.x; t < n; t += kBook) {
+    int lo = 0, hi = kBook;  // s_off[lo] <= t < s_off[hi] (hi == kBook: past the end)
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (s_off[mid] <= t) lo = mid;
+      else hi = mid;
+    }
+    if (base + t < cap) emit(lo, t - s_off[lo], base + t);
+  }
+  __syncthreads();
+  return n;
+}
+
+__device__ __forceinline__ NodeRec& node_at(const RoundBuffers& b, u32 tree, u32 id) {
+  return b.nodes[u64(id) * b.K + tree];
+}
+
+__global__ void k_round_init(RoundBuffers b, u64 R, u64 R_total) {
+  for (u32 k = threadIdx.x; k < b.K; k += blockDim.x) {
+    b.open_cur[k] = OpenRec{k, 0u, k, 0u, 0, i64(R), i64(R_total)};
+    b.build[k] = k;
+    b.next_id[k] = 1u;
+    node_at(b, k, 0) = NodeRec{0, 0, -1, -1, -1, -1, 0, 0, 0.f, 0.f};
+  }
+  if (threadIdx.x == 0) {
+    RoundCounters c{};
+    c.n_open = b.K;
+    c.n_build = b.K;
+    *b.ctr = c;
+  }
+}
+
+// Histogram tasks of the build list: about four tasks per SM of equal row
+// counts, the feature tiles of one row range adjacent in the queue so that
+// blocks running at the same time read all sectors of the same rows.
+__global__ void __launch_bounds__(kBook) k_hist_tasks(RoundBuffers b, u32 ftiles, u32 nsm, int depth) {
+  __shared__ i64 s_begin[kBook], s_count[kBook];
+  __shared__ u32 s_slot[kBook], s_tree[kBook];
+  const u32 nb = b.ctr->n_build;
+  u64 rows = 0, total = 0;
+  for (u32 i = threadIdx.x; i < nb; i += kBook) rows += u64(b.open_cur[b.build[i]].count);
+  scan_block(rows, &total);
+  const u64 target = u64(nsm) * 4;
+  u64 chunk = (total * ftiles + target - 1) / target;
+  if (chunk < 2048) chunk = 2048;
+  u64 base = 0;
+  for (u32 c0 = 0; c0 < nb; c0 += kBook) {
+    const u32 i = c0 + threadIdx.x;
+    u64 pieces = 0;
+    if (i < nb) {
+      const OpenRec o = b.open_cur[b.build[i]];
+      s_begin[threadIdx.x] = o.begin;
+      s_count[threadIdx.x] = o.count;
+      s_slot[threadIdx.x] = o.slot;
+      s_tree[threadIdx.x] = o.tree;
+      pieces = o.count > 0 ? (u64(o.count) + chunk - 1) / chunk : 0;
+    }
+    base += expand(pieces * ftiles, base, b.cap_hist_tasks, [&](int j, u64 q, u64 t) {
+      const i64 cnt = s_count[j], beg0 = s_begin[j], end0 = beg0 + cnt;
+      const i64 np = (cnt + i64(chunk) - 1) / i64(chunk);
+      const i64 piece = (cnt + np - 1) / np;
+      const i64 p = i64(q / ftiles);
+      const u32 ft = u32(q % ftiles);
+      const i64 beg = beg0 + p * piece < end0 ? beg0 + p * piece : end0;
+      const i64 end = beg + piece < end0 ? beg + piece : end0;
+      b.hist_tasks[t] = HistTask{s_slot[j], ft * kHistFeatureTile, s_tree[j], 0u, beg, end};
+    });
+  }
+  if (threadIdx.x == 0) {
+    if (base > b.cap_hist_tasks) b.ctr->overflow |= kOvfHistTasks;
+    b.ctr->n_hist_tasks = u32(base < b.cap_hist_tasks ? base : b.cap_hist_tasks);
+    b.stats[depth].rows_built = i64(total);
+    b.stats[depth].n_build = nb;
+    b.stats[depth].n_open = b.ctr->n_open;
+  }
+}
+
+__global__ void k_zero_slots(const RoundCounters* __restrict__ ctr, i64* hist, u64 slot_elems, u64 min_slots) {
+  const u64 nb = ctr->n_build > min_slots ? ctr->n_build : min_slots;
+  const u64 n2 = nb * slot_elems / 2;
+  longlong2* h = reinterpret_cast<longlong2*>(hist);
+  for (u64 i = u64(blockIdx.x) * blockDim.x + threadIdx.x; i < n2; i += u64(gridDim.x) * blockDim.x)
+    h[i] = make_longlong2(0, 0);
+}
+
+// Root totals from feature 0 of each root histogram (one block per tree):
+// every row lands in exactly one bin of every feature.
+__global__ void k_root_totals(RoundBuffers b, const i64* __restrict__ hist, u64 slot_elems) {
+  __shared__ i64 sg[256], sh[256];
+  const u32 k = blockIdx.x;
+  const i64* h = hist + u64(k) * slot_elems;
+  sg[threadIdx.x] = h[2 * threadIdx.x];
+  sh[threadIdx.x] = h[2 * threadIdx.x + 1];
+  __syncthreads();
+  for (int o = 128; o > 0; o >>= 1) {
+    if (int(threadIdx.x) < o) {
+      sg[threadIdx.x] += sg[threadIdx.x + o];
+      sh[threadIdx.x] += sh[threadIdx.x + o];
+    }
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    NodeRec& n = node_at(b, k, 0);
+    n.gq = sg[0];
+    n.hq = sh[0];
+  }
+}
+
+__global__ void k_make_eval(RoundBuffers b) {
+  const u32 n = b.ctr->n_open;
+  for (u32 i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const OpenRec o = b.open_cur[i];
+    const NodeRec& r = node_at(b, o.tree, o.id);
+    b.eval_nodes[i] = EvalNode{o.slot, o.tree, r.gq, r.hq};
+  }
+}
+
+// Splits or closes every open node, in open-list order (trees contiguous,
+// node ids ascending).  Child ids follow creation order within each tree: the
+// split of rank r in its tree gets left = next_id + 2r, right = left + 1.
+__global__ void __launch_bounds__(kBook) k_decide(RoundBuffers b, const float* __restrict__ cut,
+                                                  const u8* __restrict__ has_missing, int depth, int max_depth,
+                                                  int set) {
+  __shared__ i64 s_begin[kBook], s_end[kBook];
+  __shared__ u32 s_rank[kBook];
+  const u32 n_open = b.ctr->n_open;
+  u64 split_base = 0, part_base = 0;
+  u64 leaf_base = b.ctr->n_leaves;
+  for (u32 c0 = 0; c0 < n_open; c0 += kBook) {
+    const u32 i = c0 + threadIdx.x;
+    const bool valid = i < n_open;
+    OpenRec o{};
+    SplitCand bs{};
+    bs.feature = -1;
+    if (valid) {
+      o = b.open_cur[i];
+      if (depth < max_depth) bs = b.best[i];
+    }
+    const bool split = valid && depth < max_depth && bs.feature >= 0 && bs.gain > 0.0;
+    const bool leaf = valid && !split;
+    u64 ns = 0, nl = 0;
+    const u64 rs = split_base + scan_block(split ? 1 : 0, &ns);
+    const u64 rl = leaf_base + scan_block(leaf ? 1 : 0, &nl);
+    const bool first_of_tree = valid && (i == 0 || b.open_cur[i - 1].tree != o.tree);
+    const bool last_of_tree = valid && (i + 1 == n_open || b.open_cur[i + 1].tree != o.tree);
+    if (first_of_tree) b.tree_first[o.tree] = u32(rs);
+    __syncthreads();
+    bool ok = false;
+    if (split) {
+      const u32 rank = u32(rs) - b.tree_first[o.tree];
+      const u32 lid = b.next_id[o.tree] + 2 * rank, rid = lid + 1;
+      ok = rid < b.maxn && rs < b.cap_split;
+      if (ok) {
+        NodeRec& p = node_at(b, o.tree, o.id);
+        p.left = i32(lid);
+        p.right = i32(rid);
+        p.feature = bs.feature;
+        p.bin = bs.bin;
+        p.default_left = bs.default_left;
+        p.cond = cut[u64(bs.feature) * kMaxBins + bs.bin];
+        p.gain = float(bs.gain);
+        node_at(b, o.tree, lid) = NodeRec{bs.gl, bs.hl, -1, -1, i32(o.id), -1, 0, 0, 0.f, 0.f};
+        node_at(b, o.tree, rid) = NodeRec{p.gq - bs.gl, p.hq - bs.hl, -1, -1, i32(o.id), -1, 0, 0, 0.f, 0.f};
+        b.part_nodes[rs] = PartNode{o.tree, bs.feature, bs.bin, bs.default_left, i32(has_missing[bs.feature]), 0,
+                                    o.begin, o.begin + o.count};
+        b.split_idx[rs] = i;
+        b.cursors[2 * rs] = 0u;
+        b.cursors[2 * rs + 1] = 0u;
+      } else {
+        atomicOr(&b.ctr->overflow, kOvfNodes);
+      }
+    }
+    if (leaf) {
+      if (rl < b.cap_leaves) b.leaves[rl] = LeafRec{o.tree, o.id, u32(set), 0u, o.begin, o.count};
+      else atomicOr(&b.ctr->overflow, kOvfLeaves);
+    }
+    s_begin[threadIdx.x] = o.begin;
+    s_end[threadIdx.x] = o.begin + o.count;
+    s_rank[threadIdx.x] = u32(rs);
+    __syncthreads();  // every node of this chunk has read next_id
+    if (last_of_tree) b.next_id[o.tree] += 2u * (u32(rs) + (split ? 1u : 0u) - b.tree_first[o.tree]);
+    const u64 ptasks = (ok && o.count > 0) ? (u64(o.count) + kPartChunk - 1) / kPartChunk : 0;
+    part_base += expand(ptasks, part_base, b.cap_part_tasks, [&](int j, u64 q, u64 t) {
+      const i64 beg = s_begin[j] + i64(q) * kPartChunk;
+      const i64 end = beg + kPartChunk < s_end[j] ? beg + kPartChunk : s_end[j];
+      b.part_tasks[t] = PartTask{s_rank[j], 0u, beg, end};
+    });
+    split_base += ns;
+    leaf_base += nl;
+  }
+  if (threadIdx.x == 0) {
+    b.ctr->n_split = u32(split_base < b.cap_split ? split_base : b.cap_split);
+    b.ctr->n_part_tasks = u32(part_base < b.cap_part_tasks ? part_base : b.cap_part_tasks);
+    if (part_base > b.cap_part_tasks) b.ctr->overflow |= kOvfPartTasks;
+    b.ctr->n_leaves = u32(leaf_base < b.cap_leaves ? leaf_base : b.cap_leaves);
+  }
+}
+
+__global__ void k_copy_left(RoundBuffers b) {
+  const u32 n = b.ctr->n_split;
+  for (u32 j = blockIdx.x * blockDim.x + threadIdx.x; j < n; j += gridDim.x * blockDim.x)
+    b.gleft[j] = i64(b.cursors[2 * j]);
+}
+
+// Children of every split node become the next level's open list; the one
+// with fewer rows over all ranks (ties: left) is built directly, its sibling
+// is the parent minus it.
+__global__ void k_children(RoundBuffers b, int depth, int max_depth) {
+  const u32 ns = b.ctr->n_split;
+  const bool more = depth + 1 < max_depth;
+  for (u32 j = blockIdx.x * blockDim.x + threadIdx.x; j < ns; j += gridDim.x * blockDim.x) {
+    const OpenRec o = b.open_cur[b.split_idx[j]];
+    const NodeRec& p = node_at(b, o.tree, o.id);
+    const i64 nleft = i64(b.cursors[2 * j]);
+    if (nleft + i64(b.cursors[2 * j + 1]) != o.count) atomicOr(&b.ctr->overflow, kOvfLostRows);
+    if (2 * u64(j) + 1 >= b.cap_next) {
+      atomicOr(&b.ctr->overflow, kOvfOpen);
+      continue;
+    }
+    const i64 gl = b.gleft[j], gr = o.gcount - gl;
+    const bool right_small = gr < gl;
+    const u32 lslot = right_small ? ns + j : j, rslot = right_small ? j : ns + j;
+    b.open_next[2 * j] = OpenRec{o.tree, u32(p.left), lslot, 0u, o.begin, nleft, gl};
+    b.open_next[2 * j + 1] = OpenRec{o.tree, u32(p.right), rslot, 0u, o.begin + nleft, o.count - nleft, gr};
+    if (more) {
+      b.build_next[j] = right_small ? 2 * j + 1 : 2 * j;
+      b.triples_next[3 * j] = o.slot;
+      b.triples_next[3 * j + 1] = j;
+      b.triples_next[3 * j + 2] = ns + j;
+    }
+  }
+}
+
+__global__ void k_children_counts(RoundBuffers b, int depth, int max_depth) {
+  const u32 ns = b.ctr->n_split;
+  const bool more = depth + 1 < max_depth;
+  const bool fits = 2 * u64(ns) <= b.cap_next;
+  b.ctr->n_open = fits ? 2 * ns : 0u;
+  b.ctr->n_build = (more && fits) ? ns : 0u;
+  b.ctr->n_triples = (more && fits) ? ns : 0u;
+}
+
+// Leaf values into the node records, then the margin-update tasks (chunks of
+// up to kLeafChunk rows of each leaf segment).
+__global__ void __launch_bounds__(kBook) k_leaf_values(RoundBuffers b, const Scales* __restrict__ scales,
+                                                       SplitParams p, const u32* ridx0, const u32* ridx1, u64 R) {
+  __shared__ i64 s_begin[kBook], s_end[kBook];
+  __shared__ const u32* s_ridx[kBook];
+  __shared__ float s_value[kBook];
+  __shared__ u32 s_tree[kBook];
+  const u32 nl = b.ctr->n_leaves;
+  u64 base = 0;
+  for (u32 c0 = 0; c0 < nl; c0 += kBook) {
+    const u32 i = c0 + threadIdx.x;
+    u64 chunks = 0;
+    if (i < nl) {
+      const LeafRec l = b.leaves[i];
+      NodeRec& n = node_at(b, l.tree, l.id);
+      const Scales sc = scales[l.tree];
+      const float v = leaf_weight(n.gq, n.hq, sc.sg, sc.sh, p);
+      n.cond = v;
+      n.feature = 0;
+      s_begin[threadIdx.x] = l.begin;
+      s_end[threadIdx.x] = l.begin + l.count;
+      s_ridx[threadIdx.x] = (l.set ? ridx1 : ridx0) + u64(l.tree) * R;
+      s_value[threadIdx.x] = v;
+      s_tree[threadIdx.x] = l.tree;
+      chunks = l.count > 0 ? (u64(l.count) + kLeafChunk - 1) / kLeafChunk : 0;
+    }
+    base += expand(chunks, base, b.cap_leaf_tasks, [&](int j, u64 q, u64 t) {
+      const i64 beg = s_begin[j] + i64(q) * kLeafChunk;
+      const i64 end = beg + kLeafChunk < s_end[j] ? beg + kLeafChunk : s_end[j];
+      b.leaf_tasks[t] = LeafTask{s_ridx[j], beg, end, s_value[j], s_tree[j]};
+    });
+  }
+  if (threadIdx.x == 0) {
+    if (base > b.cap_leaf_tasks) b.ctr->overflow |= kOvfLeafTasks;
+    b.ctr->n_leaf_tasks = u32(base < b.cap_leaf_tasks ? base : b.cap_leaf_tasks);
+  }
+}
+
+int sm_count() {
+  int dev = 0, sms = 148;
+  DP_CUDA(cudaGetDevice(&dev));
+  DP_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  return sms;
+}
+
+}  // namespace
+
+void launch_round_init(const RoundBuffers& b, u64 R, u64 R_total, cudaStream_t s) {
+  k_round_init<<<1, 256, 0, s>>>(b, R, R_total);
+  after_launch("round_init");
+}
+
+void launch_hist_tasks(const RoundBuffers& b, u32 ftiles, int depth, cudaStream_t s) {
+  k_hist_tasks<<<1, kBook, 0, s>>>(b, ftiles, u32(sm_count()), depth);
+  after_launch("hist_tasks");
+}
+
+void launch_zero_slots(const RoundBuffers& b, i64* hist, u64 slot_elems, u64 min_slots, cudaStream_t s) {
+  k_zero_slots<<<sm_count() * 4, 256, 0, s>>>(b.ctr, hist, slot_elems, min_slots);
+  after_launch("zero_slots");
+}
+
+void launch_root_totals(const RoundBuffers& b, const i64* hist, u64 slot_elems, cudaStream_t s) {
+  k_root_totals<<<b.K, 256, 0, s>>>(b, hist, slot_elems);
+  after_launch("root_totals");
+}
+
+void launch_make_eval(const RoundBuffers& b, cudaStream_t s) {
+  k_make_eval<<<sm_count(), 256, 0, s>>>(b);
+  after_launch("make_eval");
+}
+
+void launch_decide(const RoundBuffers& b, const float* cut, const u8* has_missing, int depth, int max_depth,
+                   int set, cudaStream_t s) {
+  k_decide<<<1, kBook, 0, s>>>(b, cut, has_missing, depth, max_depth, set);
+  after_launch("decide");
+}
+
+void launch_copy_left(const RoundBuffers& b, cudaStream_t s) {
+  k_copy_left<<<sm_count(), 256, 0, s>>>(b);
+  after_launch("copy_left");
+}
+
+void launch_children(const RoundBuffers& b, int depth, int max_depth, cudaStream_t s) {
+  k_children<<<sm_count(), 256, 0, s>>>(b, depth, max_depth);
+  after_launch("children");
+  k_children_counts<<<1, 1, 0, s>>>(b, depth, max_depth);
+  after_launch("children_counts");
+}
+
+void launch_leaf_values(const RoundBuffers& b, const Scales* scales, SplitParams p, u32* const ridx_sets[2], u64 R,
+                        cudaStream_t s) {
+  k_leaf_values<<<1, kBook, 0, s>>>(b, scales, p, ridx_sets[0], ridx_sets[1], R);
+  after_launch("leaf_values");
+}
+
+}  // namespace dp

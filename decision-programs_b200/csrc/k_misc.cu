@@ -110,12 +110,16 @@ __global__ void k_scales(int K, const u32* gmax, const u32* hmax, Scales* scales
 }
 
 // One block per leaf task; rows of a leaf are updated in place.
-__global__ void __launch_bounds__(256) k_leaf_update(const LeafTask* __restrict__ tasks, float* margin, u32 K) {
-  const LeafTask t = tasks[blockIdx.x];
-  for (i64 i = t.begin + threadIdx.x; i < t.end; i += blockDim.x) {
-    const u32 r = t.ridx[i];
-    float* m = margin + u64(r) * K + t.klass;
-    *m = *m + t.value;
+__global__ void __launch_bounds__(256) k_leaf_update(const LeafTask* __restrict__ tasks, u32 ntasks_host,
+                                                      const u32* __restrict__ ntasks_dev, float* margin, u32 K) {
+  const u32 n = ntasks_dev ? *ntasks_dev : ntasks_host;
+  for (u32 task = blockIdx.x; task < n; task += gridDim.x) {
+    const LeafTask t = tasks[task];
+    for (i64 i = t.begin + threadIdx.x; i < t.end; i += blockDim.x) {
+      const u32 r = t.ridx[i];
+      float* m = margin + u64(r) * K + t.klass;
+      *m = *m + t.value;
+    }
   }
 }
 
@@ -175,7 +179,15 @@ void launch_quantize_gh(float2* gh, u64 R, int K, const Scales* scales, cudaStre
 
 void launch_leaf_update(const LeafTask* tasks, u32 ntasks, float* margin, u32 K, cudaStream_t s) {
   if (!ntasks) return;
-  k_leaf_update<<<ntasks, 256, 0, s>>>(tasks, margin, K);
+  k_leaf_update<<<ntasks, 256, 0, s>>>(tasks, ntasks, nullptr, margin, K);
+  after_launch("leaf_update");
+}
+
+void launch_leaf_update_dev(const LeafTask* tasks, const u32* ntasks_dev, float* margin, u32 K, cudaStream_t s) {
+  int dev = 0, sms = 148;
+  DP_CUDA(cudaGetDevice(&dev));
+  DP_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  k_leaf_update<<<sms * 8, 256, 0, s>>>(tasks, 0, ntasks_dev, margin, K);
   after_launch("leaf_update");
 }
 

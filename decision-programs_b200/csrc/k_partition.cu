@@ -27,16 +27,15 @@ __device__ __forceinline__ bool goes_left(u8 b, const PartNode& nd) {
   return int(b) <= nd.bin;
 }
 
-__global__ void __launch_bounds__(kPartThreads) k_partition(const u8* __restrict__ bins, u64 bstride,
-                                                            const TreeArrays* __restrict__ src,
-                                                            const TreeArrays* __restrict__ dst,
-                                                            const PartNode* __restrict__ nodes,
-                                                            const PartTask* __restrict__ tasks,
-                                                            u32* __restrict__ cursors) {
+__device__ __forceinline__ void partition_task(u32 task, const u8* __restrict__ bins, u64 bstride,
+                                               const TreeArrays* __restrict__ src,
+                                               const TreeArrays* __restrict__ dst,
+                                               const PartNode* __restrict__ nodes,
+                                               const PartTask* __restrict__ tasks, u32* __restrict__ cursors) {
   __shared__ u32 ballots[kWordsPerTask];
   __shared__ u32 wsum[kPartThreads / 32];
   __shared__ u32 base_lr[2];
-  const PartTask t = tasks[blockIdx.x];
+  const PartTask t = tasks[task];
   const PartNode nd = nodes[t.node];
   const TreeArrays s = src[nd.tree];
   const TreeArrays d = dst[nd.tree];
@@ -100,6 +99,28 @@ __global__ void __launch_bounds__(kPartThreads) k_partition(const u8* __restrict
     }
     run_left += step_left;
   }
+  __syncthreads();  // shared state is reused by the block's next task
+}
+
+__global__ void __launch_bounds__(kPartThreads) k_partition(const u8* __restrict__ bins, u64 bstride,
+                                                            const TreeArrays* __restrict__ src,
+                                                            const TreeArrays* __restrict__ dst,
+                                                            const PartNode* __restrict__ nodes,
+                                                            const PartTask* __restrict__ tasks,
+                                                            u32* __restrict__ cursors) {
+  partition_task(blockIdx.x, bins, bstride, src, dst, nodes, tasks, cursors);
+}
+
+// Task count in device memory: a fixed grid walks the tasks.
+__global__ void __launch_bounds__(kPartThreads) k_partition_dev(const u8* __restrict__ bins, u64 bstride,
+                                                                const TreeArrays* __restrict__ src,
+                                                                const TreeArrays* __restrict__ dst,
+                                                                const PartNode* __restrict__ nodes,
+                                                                const PartTask* __restrict__ tasks,
+                                                                const u32* __restrict__ ntasks,
+                                                                u32* __restrict__ cursors) {
+  const u32 n = *ntasks;
+  for (u32 t = blockIdx.x; t < n; t += gridDim.x) partition_task(t, bins, bstride, src, dst, nodes, tasks, cursors);
 }
 
 }  // namespace
@@ -108,6 +129,16 @@ void launch_partition(const u8* bins, u64 bin_stride, const TreeArrays* src, con
                       const PartNode* nodes, const PartTask* tasks, u32 ntasks, u32* cursors, cudaStream_t s) {
   if (!ntasks) return;
   k_partition<<<ntasks, kPartThreads, 0, s>>>(bins, bin_stride, src, dst, nodes, tasks, cursors);
+  after_launch("partition");
+}
+
+void launch_partition_dev(const u8* bins, u64 bin_stride, const TreeArrays* src, const TreeArrays* dst,
+                          const PartNode* nodes, const PartTask* tasks, const u32* ntasks_dev, u32* cursors,
+                          cudaStream_t s) {
+  int dev = 0, sms = 148;
+  DP_CUDA(cudaGetDevice(&dev));
+  DP_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  k_partition_dev<<<sms * 8, kPartThreads, 0, s>>>(bins, bin_stride, src, dst, nodes, tasks, ntasks_dev, cursors);
   after_launch("partition");
 }
 

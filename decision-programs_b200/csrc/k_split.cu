@@ -38,14 +38,13 @@ __device__ __forceinline__ Best shfl_best(const Best& v, int src) {
   return o;
 }
 
-__global__ void __launch_bounds__(kEvalThreads) k_eval(const i64* __restrict__ hist, u32 F,
-                                                       const u16* __restrict__ nbins,
-                                                       const u8* __restrict__ has_missing,
-                                                       const EvalNode* __restrict__ nodes,
-                                                       const Scales* __restrict__ scales, SplitParams p, u32 nchunks,
-                                                       SplitCand* __restrict__ cand) {
+// Best candidate of one (node, feature chunk) work item, written to cand[w].
+__device__ __forceinline__ void eval_item(u32 w, const i64* __restrict__ hist, u32 F, const u16* __restrict__ nbins,
+                                          const u8* __restrict__ has_missing, const EvalNode* __restrict__ nodes,
+                                          const Scales* __restrict__ scales, const SplitParams& p, u32 nchunks,
+                                          SplitCand* __restrict__ cand) {
   __shared__ Best wbest[kEvalThreads / 32];
-  const u32 node = blockIdx.x / nchunks, chunk = blockIdx.x % nchunks;
+  const u32 node = w / nchunks, chunk = w % nchunks;
   const EvalNode nd = nodes[node];
   const Scales sc = scales[nd.tree];
   const double isg = 1.0 / double(sc.sg), ish = 1.0 / double(sc.sh);
@@ -109,8 +108,8 @@ __global__ void __launch_bounds__(kEvalThreads) k_eval(const i64* __restrict__ h
   __syncthreads();
   if (threadIdx.x == 0) {
     Best b = wbest[0];
-    for (int w = 1; w < kEvalThreads / 32; ++w)
-      if (better(wbest[w], b)) b = wbest[w];
+    for (int wi = 1; wi < kEvalThreads / 32; ++wi)
+      if (better(wbest[wi], b)) b = wbest[wi];
     SplitCand out;
     out.gain = b.gain;
     out.gl = b.gl;
@@ -119,14 +118,37 @@ __global__ void __launch_bounds__(kEvalThreads) k_eval(const i64* __restrict__ h
     out.bin = b.b;
     out.default_left = b.d;
     out.pad = 0;
-    cand[blockIdx.x] = out;
+    cand[w] = out;
   }
+  __syncthreads();  // wbest is reused by the next work item of this block
 }
 
-__global__ void k_reduce_cands(const SplitCand* __restrict__ cand, u32 nnodes, u32 nchunks,
-                               SplitCand* __restrict__ best) {
-  const u32 n = blockIdx.x * blockDim.x + threadIdx.x;
-  if (n >= nnodes) return;
+__global__ void __launch_bounds__(kEvalThreads) k_eval(const i64* __restrict__ hist, u32 F,
+                                                       const u16* __restrict__ nbins,
+                                                       const u8* __restrict__ has_missing,
+                                                       const EvalNode* __restrict__ nodes,
+                                                       const Scales* __restrict__ scales, SplitParams p, u32 nchunks,
+                                                       SplitCand* __restrict__ cand) {
+  eval_item(blockIdx.x, hist, F, nbins, has_missing, nodes, scales, p, nchunks, cand);
+}
+
+// Node count in device memory: a fixed grid walks the work items.
+__global__ void __launch_bounds__(kEvalThreads) k_eval_dev(const i64* __restrict__ hist, u32 F,
+                                                           const u16* __restrict__ nbins,
+                                                           const u8* __restrict__ has_missing,
+                                                           const EvalNode* __restrict__ nodes,
+                                                           const Scales* __restrict__ scales, SplitParams p,
+                                                           u32 nchunks, const u32* __restrict__ nnodes,
+                                                           SplitCand* __restrict__ cand) {
+  const u32 items = *nnodes * nchunks;
+  for (u32 w = blockIdx.x; w < items; w += gridDim.x)
+    eval_item(w, hist, F, nbins, has_missing, nodes, scales, p, nchunks, cand);
+}
+
+__global__ void k_reduce_cands(const SplitCand* __restrict__ cand, u32 nnodes_host, const u32* __restrict__ nnodes_dev,
+                               u32 nchunks, SplitCand* __restrict__ best) {
+  const u32 nnodes = nnodes_dev ? *nnodes_dev : nnodes_host;
+  for (u32 n = blockIdx.x * blockDim.x + threadIdx.x; n < nnodes; n += gridDim.x * blockDim.x) {
   SplitCand b = cand[u64(n) * nchunks];
   for (u32 c = 1; c < nchunks; ++c) {
     const SplitCand x = cand[u64(n) * nchunks + c];
@@ -134,6 +156,7 @@ __global__ void k_reduce_cands(const SplitCand* __restrict__ cand, u32 nnodes, u
     if (x.gain > b.gain) b = x;
   }
   best[n] = b;
+  }
 }
 
 }  // namespace
@@ -145,7 +168,21 @@ void launch_eval_splits(const i64* hist, u32 F, const u16* nbins, const u8* has_
   const u32 nchunks = (F + kEvalFeatureChunk - 1) / kEvalFeatureChunk;
   k_eval<<<nnodes * nchunks, kEvalThreads, 0, s>>>(hist, F, nbins, has_missing, nodes, scales, p, nchunks, cand);
   after_launch("eval_splits");
-  k_reduce_cands<<<(nnodes + 127) / 128, 128, 0, s>>>(cand, nnodes, nchunks, best);
+  k_reduce_cands<<<(nnodes + 127) / 128, 128, 0, s>>>(cand, nnodes, nullptr, nchunks, best);
+  after_launch("reduce_splits");
+}
+
+void launch_eval_splits_dev(const i64* hist, u32 F, const u16* nbins, const u8* has_missing, const EvalNode* nodes,
+                            const u32* nnodes_dev, const Scales* scales, SplitParams p, SplitCand* cand,
+                            SplitCand* best, cudaStream_t s) {
+  int dev = 0, sms = 148;
+  DP_CUDA(cudaGetDevice(&dev));
+  DP_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  const u32 nchunks = (F + kEvalFeatureChunk - 1) / kEvalFeatureChunk;
+  k_eval_dev<<<sms * 8, kEvalThreads, 0, s>>>(hist, F, nbins, has_missing, nodes, scales, p, nchunks, nnodes_dev,
+                                               cand);
+  after_launch("eval_splits");
+  k_reduce_cands<<<sms, 128, 0, s>>>(cand, 0, nnodes_dev, nchunks, best);
   after_launch("reduce_splits");
 }
 

@@ -76,9 +76,11 @@ void launch_scales(int K, const u32* gmax_bits, const u32* hmax_bits, Scales* sc
 // otherwise fp32 pairs quantised with `scales`.  `counter` is one u32 of
 // device scratch (the task queue), reset by the launcher.  Positions must be
 // below 2^31.
+// With ntasks_dev set, the task count is read from device memory (ntasks is
+// then ignored) and the grid covers every SM.
 void launch_histograms(const u8* bins, u64 bin_stride, u32 F, int max_bins, bool quantized_gh,
                        const TreeArrays* trees, const Scales* scales, const HistTask* tasks, u32 ntasks,
-                       u32* counter, i64* hist, cudaStream_t s);
+                       u32* counter, i64* hist, cudaStream_t s, const u32* ntasks_dev = nullptr);
 constexpr u32 kHistFeatureTile = 32;
 // Rows per histogram task for a launch over `total_rows` row-tiles (about
 // four tasks per SM; tasks tasks of one node and tile stay contiguous).
@@ -88,6 +90,9 @@ void launch_quantize_gh(float2* gh, u64 R, int K, const Scales* scales, cudaStre
 
 // hist[dst] = parent_hist[par] - hist[src] for each (par, src, dst) slot triple.
 void launch_subtract(i64* hist, const i64* parent_hist, u64 slot_elems, const u32* triples, u32 n, cudaStream_t s);
+// The same with the triple count in device memory.
+void launch_subtract_dev(i64* hist, const i64* parent_hist, u64 slot_elems, const u32* triples, const u32* n_dev,
+                         cudaStream_t s);
 
 // ---- split evaluation --------------------------------------------------------
 // Per (node, feature chunk) candidate into cand[node][chunk]; then the best per
@@ -96,6 +101,10 @@ void launch_eval_splits(const i64* hist, u32 F, const u16* nbins, const u8* has_
                         u32 nnodes, const Scales* scales, SplitParams p, SplitCand* cand, SplitCand* best,
                         cudaStream_t s);
 constexpr u32 kEvalFeatureChunk = 16;
+// The same with the node count in device memory.
+void launch_eval_splits_dev(const i64* hist, u32 F, const u16* nbins, const u8* has_missing, const EvalNode* nodes,
+                            const u32* nnodes_dev, const Scales* scales, SplitParams p, SplitCand* cand,
+                            SplitCand* best, cudaStream_t s);
 
 // ---- partition ----------------------------------------------------------------
 struct PartTask {
@@ -121,6 +130,10 @@ struct PartNode {
 void launch_partition(const u8* bins, u64 bin_stride, const TreeArrays* src, const TreeArrays* dst,
                       const PartNode* nodes, const PartTask* tasks, u32 ntasks, u32* cursors, cudaStream_t s);
 constexpr u32 kPartChunk = 4096;
+// The same with the task count in device memory.
+void launch_partition_dev(const u8* bins, u64 bin_stride, const TreeArrays* src, const TreeArrays* dst,
+                          const PartNode* nodes, const PartTask* tasks, const u32* ntasks_dev, u32* cursors,
+                          cudaStream_t s);
 
 // ---- leaves -------------------------------------------------------------------
 struct LeafTask {
@@ -130,6 +143,7 @@ struct LeafTask {
   u32 klass;
 };
 void launch_leaf_update(const LeafTask* tasks, u32 ntasks, float* margin, u32 K, cudaStream_t s);
+void launch_leaf_update_dev(const LeafTask* tasks, const u32* ntasks_dev, float* margin, u32 K, cudaStream_t s);
 
 // ---- misc ---------------------------------------------------------------------
 void launch_iota(u32* p, u64 n, cudaStream_t s);

@@ -1,0 +1,94 @@
+// Device-side bookkeeping of one boosting round: node records of the K trees,
+// the open nodes of the current level, and the work lists each level's
+// kernels consume.  Every count lives in device memory, so the host enqueues a
+// whole round without waiting and reads the trees back once.  Every buffer a
+// kernel writes carries its capacity; a write past it sets a bit of
+// RoundCounters::overflow instead of touching memory, and the host turns a set
+// bit into an error after the round.
+#pragma once
+#include "kernels.h"
+
+namespace dp {
+
+// One tree node; records are laid out [node id][tree] so that capacity grows
+// by appending.
+struct NodeRec {
+  i64 gq, hq;              // quantised totals over all ranks
+  i32 left, right, parent, feature;
+  i32 bin, default_left;
+  float cond, gain;        // split threshold (leaf value at a leaf), gain
+};
+static_assert(sizeof(NodeRec) == 48, "node record layout");
+
+struct OpenRec {
+  u32 tree, id, slot, pad;
+  i64 begin, count;        // this rank's positions
+  i64 gcount;              // rows over all ranks
+};
+
+struct LeafRec {
+  u32 tree, id, set, pad;
+  i64 begin, count;
+};
+
+struct RoundCounters {
+  u32 n_open, n_build, n_split, n_hist_tasks;
+  u32 n_part_tasks, n_leaves, n_leaf_tasks, n_triples;
+  u32 overflow, pad[7];
+};
+
+// Overflow bits.
+enum : u32 {
+  kOvfHistTasks = 1, kOvfNodes = 2, kOvfLeaves = 4, kOvfPartTasks = 8, kOvfLeafTasks = 16,
+  kOvfLostRows = 32, kOvfOpen = 64,
+};
+
+constexpr i64 kLeafChunkRows = 16384;  // rows per margin-update task
+
+struct LevelStats {
+  i64 rows_built;          // this rank's rows in directly built nodes
+  u32 n_build, n_open;
+};
+
+struct RoundBuffers {
+  NodeRec* nodes;          // [maxn][K]
+  u32* next_id;            // [K]
+  u32* tree_first;         // [K] scratch of the decision kernel
+  OpenRec* open_cur;       // this level's open nodes (trees contiguous, ids ascending)
+  OpenRec* open_next;      // [cap_next]
+  u32* build;              // open indices of this level's directly built nodes
+  u32* build_next;         // [cap_split]
+  u32* triples_next;       // [3 * cap_split] (parent slot, small slot, large slot)
+  HistTask* hist_tasks;    // [cap_hist_tasks]
+  EvalNode* eval_nodes;    // [cap_split]
+  SplitCand* best;         // [cap_split]
+  u32* split_idx;          // [cap_split]
+  PartNode* part_nodes;    // [cap_split]
+  PartTask* part_tasks;    // [cap_part_tasks]
+  u32* cursors;            // [2 * cap_split]
+  i64* gleft;              // [cap_split]
+  LeafRec* leaves;         // [cap_leaves]
+  LeafTask* leaf_tasks;    // [cap_leaf_tasks]
+  RoundCounters* ctr;
+  LevelStats* stats;       // [max_depth + 1]
+  u32 K, maxn;
+  u64 cap_split, cap_next, cap_hist_tasks, cap_part_tasks, cap_leaves, cap_leaf_tasks;
+};
+
+void launch_round_init(const RoundBuffers& b, u64 R, u64 R_total, cudaStream_t s);
+void launch_hist_tasks(const RoundBuffers& b, u32 ftiles, int depth, cudaStream_t s);
+// Zeroes max(device n_build, min_slots) histogram slots.
+void launch_zero_slots(const RoundBuffers& b, i64* hist, u64 slot_elems, u64 min_slots, cudaStream_t s);
+void launch_root_totals(const RoundBuffers& b, const i64* hist, u64 slot_elems, cudaStream_t s);
+void launch_make_eval(const RoundBuffers& b, cudaStream_t s);
+// Splits (depth < max_depth, gain > 0) or closes every open node.
+void launch_decide(const RoundBuffers& b, const float* cut, const u8* has_missing, int depth, int max_depth,
+                   int set, cudaStream_t s);
+void launch_copy_left(const RoundBuffers& b, cudaStream_t s);
+void launch_children(const RoundBuffers& b, int depth, int max_depth, cudaStream_t s);
+// ridx_sets[s] is the base of the K per-tree row-index arrays of set s
+// (tree k at + k * R).
+void launch_leaf_values(const RoundBuffers& b, const Scales* scales, SplitParams p, u32* const ridx_sets[2], u64 R,
+                        cudaStream_t s);
+
+}  // namespace dp

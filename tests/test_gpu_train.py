@@ -109,6 +109,23 @@ def test_regularisation_and_shapes(dp, orc, hp):
     run(dp, orc, x, y, "binary:logistic", 4, **hp)
 
 
+@pytest.mark.parametrize("objective,K", [("binary:logistic", 1), ("multi:softprob", 4)])
+def test_deep_trees_with_exact_level_counts(dp, orc, monkeypatch, objective, K):
+    """Levels whose open-node bound passes the limits read the exact counts
+    back before sizing their buffers; trees stop growing at different depths."""
+    monkeypatch.setenv("DP_ASYNC_OPEN_LIMIT", "3")
+    monkeypatch.setenv("DP_ASYNC_HIST_BYTES", str(6 * 16 * 256 * 16))
+    x, y = c1_data(3000, seed=11)
+    if K > 1:
+        y = np.digitize(x[:, 0] + x[:, 3], [-1.0, 0.0, 1.0]).astype(np.float32)
+    run(dp, orc, x, y, objective, 3, K=K, max_depth=13, min_child_weight=0.0)
+
+
+def test_deep_trees_device_resident_levels(dp, orc):
+    x, y = c1_data(6000, seed=12)
+    run(dp, orc, x, y, "binary:logistic", 2, max_depth=14, min_child_weight=0.0, reg_lambda=0.1)
+
+
 @pytest.mark.parametrize("R", [1, 2, 7, 33])
 def test_tiny_inputs(dp, orc, R):
     rng = np.random.default_rng(R)
