@@ -119,38 +119,71 @@ int XGBuildInfo(const char** out) {
 
 const char* XGBGetLastError(void) { return g_last_error.c_str(); }
 
-int XGDMatrixCreateFromCudaArrayInterface(const char* data, const char* config, DMatrixHandle* out) {
-  DP_API_BEGIN();
-  need(out != nullptr, "output handle pointer is null");
+namespace {
+// Shape, row stride (elements) and missing value of a dense fp32 matrix
+// described by an array interface and an XGBoost DMatrix config.
+struct DenseSpec {
+  dp::u64 rows = 0, cols = 0, stride = 0;
+  bool has_mv = false;
+  float mv = 0.f;
+  const float* ptr = nullptr;
+};
+
+DenseSpec dense_spec(const char* data, const char* config) {
   const ArrayInterface a = parse_array(data);
   need(a.typestr == "<f4", "only little-endian float32 (<f4) matrices are supported");
   need(a.shape.size() == 2, "matrix array interface must be two-dimensional");
-  const dp::u64 rows = a.shape[0], cols = a.shape[1];
-  need(cols > 0 && cols <= 0x7fffffffULL, "matrix column count out of range");
-  dp::u64 stride = cols;
+  DenseSpec d;
+  d.rows = a.shape[0];
+  d.cols = a.shape[1];
+  need(d.cols > 0 && d.cols <= 0x7fffffffULL, "matrix column count out of range");
+  d.stride = d.cols;
   if (!a.strides.empty()) {
     need(a.strides.size() == 2 && a.strides[1] == 4 && a.strides[0] > 0 && a.strides[0] % 4 == 0,
          "matrix strides must be row-major with 4-byte elements");
-    stride = dp::u64(a.strides[0]) / 4;
+    d.stride = dp::u64(a.strides[0]) / 4;
   }
-  bool has_mv = false;
-  float mv = 0.f;
   if (config && *config) {
     const dp::json::Value c = dp::json::parse(config);
     if (const auto* m = c.find("missing")) {
-      const double d = m->as_double();
-      if (!std::isnan(d)) { has_mv = true; mv = float(d); }
+      const double v = m->as_double();
+      if (!std::isnan(v)) { d.has_mv = true; d.mv = float(v); }
     }
   }
-  need(rows == 0 || a.ptr != 0, "matrix data pointer is null");
-  const int dev = rows ? pointer_device(reinterpret_cast<const void*>(a.ptr), false) : 0;
+  need(d.rows == 0 || a.ptr != 0, "matrix data pointer is null");
+  d.ptr = reinterpret_cast<const float*>(a.ptr);
+  return d;
+}
+}  // namespace
+
+int XGDMatrixCreateFromCudaArrayInterface(const char* data, const char* config, DMatrixHandle* out) {
+  DP_API_BEGIN();
+  need(out != nullptr, "output handle pointer is null");
+  const DenseSpec m = dense_spec(data, config);
+  const int dev = m.rows ? pointer_device(m.ptr, false) : 0;
   {
     dp::DeviceGuard g(dev);
     // the producer may still be writing on its own stream
     dp::cuda_check(cudaDeviceSynchronize(), "synchronise producer");
   }
-  auto d = std::make_unique<dp::DMatrix>(reinterpret_cast<const float*>(a.ptr), rows, dp::u32(cols), stride, dev,
-                                         has_mv, mv);
+  auto d = std::make_unique<dp::DMatrix>(m.ptr, m.rows, dp::u32(m.cols), m.stride, dev, m.has_mv, m.mv);
+  *out = d.release();
+  DP_API_END();
+}
+
+int XGDMatrixCreateFromDense(const char* data, const char* config, DMatrixHandle* out) {
+  DP_API_BEGIN();
+  need(out != nullptr, "output handle pointer is null");
+  const DenseSpec m = dense_spec(data, config);
+  int dev = 0;
+  dp::cuda_check(cudaGetDevice(&dev), "cudaGetDevice");
+  if (m.rows) {
+    cudaPointerAttributes attr{};
+    dp::cuda_check(cudaPointerGetAttributes(&attr, m.ptr), "cudaPointerGetAttributes");
+    need(attr.type == cudaMemoryTypeHost || attr.type == cudaMemoryTypeUnregistered,
+         "XGDMatrixCreateFromDense takes host memory; use XGDMatrixCreateFromCudaArrayInterface for device memory");
+  }
+  auto d = dp::DMatrix::from_host(m.ptr, m.rows, dp::u32(m.cols), m.stride, dev, m.has_mv, m.mv);
   *out = d.release();
   DP_API_END();
 }

@@ -1,8 +1,14 @@
 #include "dmatrix.h"
 
+#include <algorithm>
+
 #include "quantile.h"
 
 namespace dp {
+
+namespace {
+constexpr const char* kInfMessage = "Input data contains `inf` or a value too large, while `missing` is not set to `inf`";
+}
 
 DMatrix::DMatrix(const float* x, u64 rows, u32 cols, u64 stride, int device, bool has_mv, float mv)
     : x_(x), rows_(rows), stride_(stride), cols_(cols), device_(device), has_mv_(has_mv), mv_(mv) {
@@ -11,11 +17,75 @@ DMatrix::DMatrix(const float* x, u64 rows, u32 cols, u64 stride, int device, boo
   DeviceGuard g(device_);
   if (rows_ == 0) return;
   DevBuf<u32> bad(1);
+  prefix_counts_.resize(u64(cols_) * kPrefixBuckets);
   DP_CUDA(cudaMemset(bad.get(), 0, sizeof(u32)));
-  launch_check_finite(x_, rows_, cols_, stride_, bad.get(), nullptr);
+  DP_CUDA(cudaMemset(prefix_counts_.get(), 0, prefix_counts_.size() * sizeof(u32)));
+  launch_prefix_counts(x_, rows_, cols_, stride_, has_mv_, mv_, prefix_counts_.get(), bad.get(), nullptr);
+  check_bad(bad.get());
+}
+
+std::unique_ptr<DMatrix> DMatrix::from_host(const float* x, u64 rows, u32 cols, u64 stride, int device, bool has_mv,
+                                            float mv) {
+  need(cols > 0, "DMatrix needs at least one column");
+  need(stride >= cols, "DMatrix row stride is smaller than its column count");
+  std::unique_ptr<DMatrix> d(new DMatrix());
+  d->rows_ = rows;
+  d->cols_ = cols;
+  d->stride_ = cols;
+  d->device_ = device;
+  d->has_mv_ = has_mv;
+  d->mv_ = mv;
+  DeviceGuard g(device);
+  d->owned_.resize(std::max<u64>(rows, 1) * cols);
+  d->x_ = d->owned_.get();
+  if (rows == 0) return d;
+  DevBuf<u32> bad(1);
+  d->prefix_counts_.resize(u64(cols) * kPrefixBuckets);
+  cudaStream_t copy = nullptr, count = nullptr;
+  cudaEvent_t landed = nullptr;
+  DP_CUDA(cudaStreamCreateWithFlags(&copy, cudaStreamNonBlocking));
+  DP_CUDA(cudaStreamCreateWithFlags(&count, cudaStreamNonBlocking));
+  DP_CUDA(cudaEventCreateWithFlags(&landed, cudaEventDisableTiming));
+  try {
+    DP_CUDA(cudaMemsetAsync(bad.get(), 0, sizeof(u32), count));
+    DP_CUDA(cudaMemsetAsync(d->prefix_counts_.get(), 0, d->prefix_counts_.size() * sizeof(u32), count));
+    // about 32 MB per chunk: the counting pass of chunk i runs while chunk
+    // i + 1 crosses the host link
+    const u64 chunk = std::max<u64>(1, (u64(32) << 20) / (u64(cols) * sizeof(float)));
+    for (u64 r0 = 0; r0 < rows; r0 += chunk) {
+      const u64 n = std::min<u64>(chunk, rows - r0);
+      float* dst = d->owned_.get() + r0 * cols;
+      const float* src = x + r0 * stride;
+      if (stride == cols)
+        DP_CUDA(cudaMemcpyAsync(dst, src, n * cols * sizeof(float), cudaMemcpyHostToDevice, copy));
+      else
+        DP_CUDA(cudaMemcpy2DAsync(dst, cols * sizeof(float), src, stride * sizeof(float), cols * sizeof(float), n,
+                                  cudaMemcpyHostToDevice, copy));
+      DP_CUDA(cudaEventRecord(landed, copy));
+      DP_CUDA(cudaStreamWaitEvent(count, landed, 0));
+      launch_prefix_counts(dst, n, cols, cols, has_mv, mv, d->prefix_counts_.get(), bad.get(), count);
+    }
+    DP_CUDA(cudaStreamSynchronize(copy));
+    DP_CUDA(cudaStreamSynchronize(count));
+  } catch (...) {
+    cudaStreamSynchronize(copy);
+    cudaStreamSynchronize(count);
+    cudaEventDestroy(landed);
+    cudaStreamDestroy(copy);
+    cudaStreamDestroy(count);
+    throw;
+  }
+  cudaEventDestroy(landed);
+  cudaStreamDestroy(copy);
+  cudaStreamDestroy(count);
+  d->check_bad(bad.get());
+  return d;
+}
+
+void DMatrix::check_bad(const u32* bad_dev) {
   u32 h = 0;
-  DP_CUDA(cudaMemcpy(&h, bad.get(), sizeof h, cudaMemcpyDeviceToHost));
-  need(h == 0, "Input data contains `inf` or a value too large, while `missing` is not set to `inf`");
+  DP_CUDA(cudaMemcpy(&h, bad_dev, sizeof h, cudaMemcpyDeviceToHost));
+  need(h == 0, kInfMessage);
 }
 
 void DMatrix::set_labels_device(const float* y, u64 n) {
@@ -39,7 +109,8 @@ const Quantized& DMatrix::quantized(int max_bin, Comm* comm, cudaStream_t s) {
   q->has_missing.resize(cols_);
   q->rows_total = comm ? comm->sum_host_u64(rows_, s) : rows_;
   CutsDevice cd{q->cut.get(), q->nbins.get(), q->has_missing.get()};
-  compute_cuts(x_, rows_, cols_, stride_, max_bin, has_mv_, mv_, q->rows_total, comm, cd, s);
+  compute_cuts(x_, rows_, cols_, stride_, max_bin, has_mv_, mv_, q->rows_total, comm, cd, s,
+               prefix_counts_.size() ? prefix_counts_.get() : nullptr);
   q->bins.resize(std::max<u64>(rows_, 1) * q->bin_stride);
   launch_bin_matrix(x_, rows_, cols_, stride_, has_mv_, mv_, cd, q->bins.get(), q->bin_stride, s);
   q->cut_h.resize(q->cut.size());

@@ -1,9 +1,12 @@
-// Training matrix handed over by XGDMatrixCreateFromCudaArrayInterface: a
-// borrowed dense fp32 device matrix (NaN = missing) plus owned labels, and the
-// cached quantile cuts / uint8 bin matrix built at the first boosting round.
-// Mirrors the reference's use: a borrowed CUDA pointer that must stay valid
-// while the DMatrix lives (native/class_native_training.cuh:49-53,
-// native/class_study_oof.cu:532-534).
+// Training matrix: a dense fp32 device matrix (NaN = missing) plus owned
+// labels, the first-pass prefix counts of the cut search (taken while the
+// matrix is read for its validity check, or while it uploads), and the cached
+// quantile cuts / uint8 bin matrix built at the first boosting round.
+// XGDMatrixCreateFromCudaArrayInterface borrows a CUDA pointer that must stay
+// valid while the DMatrix lives, as the reference uses it
+// (native/class_native_training.cuh:49-53, native/class_study_oof.cu:532-534);
+// XGDMatrixCreateFromDense copies a host matrix into device memory the
+// DMatrix owns, in chunks that overlap the copy with the counting pass.
 #pragma once
 #include <memory>
 #include <string>
@@ -30,7 +33,11 @@ struct Quantized {
 
 class DMatrix {
  public:
+  // Borrowed device matrix.
   DMatrix(const float* x, u64 rows, u32 cols, u64 stride, int device, bool has_mv, float mv);
+  // Host matrix copied to `device`.
+  static std::unique_ptr<DMatrix> from_host(const float* x, u64 rows, u32 cols, u64 stride, int device, bool has_mv,
+                                            float mv);
 
   void set_labels_device(const float* y, u64 n);
   void set_labels_host(const float* y, u64 n);
@@ -45,7 +52,11 @@ class DMatrix {
   bool has_labels() const { return labels_n_ == rows_; }
 
  private:
+  DMatrix() = default;
+  void check_bad(const u32* bad_dev);
   const float* x_ = nullptr;
+  DevBuf<float> owned_;        // host-sourced matrix
+  DevBuf<u32> prefix_counts_;  // [cols][kPrefixBuckets], this rank's rows
   u64 rows_ = 0, stride_ = 0;
   u32 cols_ = 0;
   int device_ = 0;

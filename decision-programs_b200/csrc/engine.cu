@@ -1,6 +1,7 @@
 #include "engine.h"
 
 #include <algorithm>
+#include <chrono>
 #include <cstdlib>
 #include <cstring>
 #include <sstream>
@@ -57,8 +58,16 @@ std::string Profiler::json() const {
     o << "\"" << kv.first << "\":{\"launches\":" << kv.second.launches << ",\"ms\":" << kv.second.ms
       << ",\"alg_bytes\":" << kv.second.bytes << "}";
   }
+  // host phases: {name: [count, ms]}
+  o << (first ? "" : ",") << "\"host_ms\":{";
+  bool hfirst = true;
+  for (const auto& kv : host_) {
+    o << (hfirst ? "" : ",") << "\"" << kv.first << "\":[" << kv.second.first << "," << kv.second.second << "]";
+    hfirst = false;
+  }
+  o << "}";
   // the most recent launches in order: [name, ms, algorithmic bytes]
-  o << (first ? "" : ",") << "\"log\":[";
+  o << ",\"log\":[";
   for (size_t i = 0; i < log_.size(); ++i)
     o << (i ? "," : "") << "[\"" << log_[i].name << "\"," << log_[i].ms << "," << log_[i].bytes << "]";
   o << "]}";
@@ -72,6 +81,10 @@ Profiler::~Profiler() {
 // ---------------------------------------------------------------- engine
 namespace {
 constexpr u32 kFT = kHistFeatureTile;
+
+double ms_since(std::chrono::steady_clock::time_point t0) {
+  return std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+}
 
 u64 env_u64(const char* name, u64 dflt) {
   const char* v = std::getenv(name);
@@ -91,7 +104,10 @@ Engine::Engine(DMatrix& d, const TrainParams& p, Comm* comm) : d_(d), p_(p), com
   R_ = d_.rows();
   F_ = d_.cols();
   need(R_ < (u64(1) << 31), "row count per device exceeds 2^31");
+  auto t0 = std::chrono::steady_clock::now();
   q_ = &d_.quantized(p_.max_bin, comm_, stream_);
+  prof_.host("quantize", ms_since(t0));
+  t0 = std::chrono::steady_clock::now();
   slot_elems_ = u64(F_) * kMaxBins * 2;
   max_bins_ = 0;
   for (u32 f = 0; f < F_; ++f) {
@@ -115,10 +131,14 @@ Engine::Engine(DMatrix& d, const TrainParams& p, Comm* comm) : d_(d), p_(p), com
   }
   const u64 RK = std::max<u64>(R_, 1) * u64(K_);
   margin_.resize(RK);
-  std::vector<float> m0(RK);
-  for (u64 r = 0; r < std::max<u64>(R_, 1); ++r)
-    for (int k = 0; k < K_; ++k) m0[r * K_ + k] = p_.base_margin(k);
-  DP_CUDA(cudaMemcpy(margin_.get(), m0.data(), RK * sizeof(float), cudaMemcpyHostToDevice));
+  {
+    std::vector<float> base(K_);
+    for (int k = 0; k < K_; ++k) base[k] = p_.base_margin(k);
+    DevBuf<float> base_d(K_);
+    DP_CUDA(cudaMemcpyAsync(base_d.get(), base.data(), K_ * sizeof(float), cudaMemcpyHostToDevice, stream_));
+    launch_init_margins(margin_.get(), std::max<u64>(R_, 1), K_, base_d.get(), stream_);
+    DP_CUDA(cudaStreamSynchronize(stream_));
+  }
   for (int s = 0; s < 2; ++s) {
     gh_[s].resize(RK);
     ridx_[s].resize(RK);
@@ -131,12 +151,14 @@ Engine::Engine(DMatrix& d, const TrainParams& p, Comm* comm) : d_(d), p_(p), com
   hmax_.resize(K_);
   scales_.resize(K_);
   hist_counter_.resize(1);
-  arena_.reserve(size_t(8) << 20);
+  arena_.reserve(size_t(1) << 20);
   ctr_h_.reserve(1);
   DP_CUDA(cudaDeviceGetAttribute(&sms_, cudaDevAttrMultiProcessorCount, device_));
   // testing knobs: force the exact-count path of deep levels
   async_open_limit_ = env_u64("DP_ASYNC_OPEN_LIMIT", async_open_limit_);
   async_hist_bytes_ = env_u64("DP_ASYNC_HIST_BYTES", async_hist_bytes_);
+  presize();
+  prof_.host("engine_init", ms_since(t0));
 }
 
 Engine::~Engine() {
@@ -182,17 +204,74 @@ void Engine::upload(DevBuf<T>& dst, const std::vector<T>& v) {
 template <class T>
 void Engine::grow(DevBuf<T>& b, size_t n) {
   if (n <= b.size()) return;
+  const auto t0 = std::chrono::steady_clock::now();
   DP_CUDA(cudaStreamSynchronize(stream_));
   b.resize(n);
+  prof_.host("grow", ms_since(t0));
 }
 
 template <class T>
 void Engine::grow_keep(DevBuf<T>& b, size_t n) {
   if (n <= b.size()) return;
+  const auto t0 = std::chrono::steady_clock::now();
   DevBuf<T> fresh(n);
   if (b.size()) DP_CUDA(cudaMemcpyAsync(fresh.get(), b.get(), b.size() * sizeof(T), cudaMemcpyDeviceToDevice, stream_));
   DP_CUDA(cudaStreamSynchronize(stream_));
   b = std::move(fresh);
+  prof_.host("grow", ms_since(t0));
+}
+
+void Engine::presize() {
+  const u64 K = u64(K_), D = u64(p_.max_depth);
+  const u64 Rt = std::max<u64>(q_->rows_total, 1);
+  const u64 RK = std::max<u64>(R_, 1) * K;
+  const u64 slot_bytes = slot_elems_ * sizeof(i64);
+  const u32 ftiles = (F_ + kFT - 1) / kFT;
+  const u32 nchunks = (F_ + kEvalFeatureChunk - 1) / kEvalFeatureChunk;
+  // the same bounds the level loop of boost_round derives
+  u64 open_hi = K, ids_hi = 1, leaves_hi = 0;
+  u64 hist[2] = {0, 0}, tasks = 0, split = 0, opens[2] = {K, 0}, builds[2] = {K, 0};
+  bool complete = true;
+  for (u64 depth = 0; depth < D; ++depth) {
+    if (open_hi > async_open_limit_ || open_hi * slot_bytes > async_hist_bytes_) {
+      complete = false;
+      break;
+    }
+    const u64 nbuild_hi = depth == 0 ? K : (open_hi + 1) / 2;
+    const u64 next_hi = std::min<u64>(2 * open_hi, K * Rt);
+    hist[depth & 1] = std::max<u64>(hist[depth & 1], std::max<u64>(open_hi, 1) * slot_elems_);
+    tasks = std::max<u64>(tasks, (nbuild_hi + 4 * u64(sms_) + 1) * ftiles);
+    split = std::max<u64>(split, open_hi);
+    opens[(depth + 1) & 1] = std::max<u64>(opens[(depth + 1) & 1], next_hi);
+    builds[(depth + 1) & 1] = std::max<u64>(builds[(depth + 1) & 1], open_hi);
+    leaves_hi += open_hi;
+    ids_hi = std::min<u64>({ids_hi + 2 * std::min<u64>(open_hi, u64(1) << depth), (u64(1) << (depth + 2)) - 1,
+                            2 * Rt + 1});
+    open_hi = next_hi;
+  }
+  if (complete) leaves_hi += open_hi;
+  for (int r = 0; r < 2; ++r) {
+    grow(hist_[r], hist[r]);
+    grow(open_[r], opens[r]);
+    grow(build_[r], builds[r]);
+    grow(triples_[r], 3 * builds[r]);
+  }
+  grow(hist_tasks_, tasks);
+  grow(eval_nodes_, split);
+  grow(best_, split);
+  grow(cand_, split * nchunks);
+  grow(split_idx_, split);
+  grow(part_nodes_, split);
+  grow(cursors_, 2 * split);
+  grow(gleft_, split);
+  grow(part_tasks_, (RK + kPartChunk - 1) / kPartChunk + split);
+  grow(leaves_, leaves_hi);
+  grow(leaf_tasks_, (RK + kLeafChunkRows - 1) / kLeafChunkRows + leaves_hi);
+  grow(nodes_, ids_hi * K);
+  grow(ctr_, 1);
+  grow(stats_, size_t(D) + 1);
+  grow(next_id_, K);
+  grow(tree_first_, K);
 }
 
 RoundBuffers Engine::round_buffers(int depth, u64 cap_split, u64 cap_next) const {
@@ -247,6 +326,7 @@ std::vector<float> Engine::margins() const {
 
 void Engine::boost_round(Model& m) {
   DeviceGuard g(device_);
+  const auto t_round = std::chrono::steady_clock::now();
   const int K = K_;
   const u64 R = R_;
   const u32 F = F_;
@@ -378,7 +458,11 @@ void Engine::boost_round(Model& m) {
 
   // ---- one read-back of the round
   const u64 ids_read = std::min<u64>(ids_hi, nodes_.size() / u64(K));
+  prof_.host("round_enqueue", ms_since(t_round));
+  auto t_wait = std::chrono::steady_clock::now();
   DP_CUDA(cudaStreamSynchronize(stream_));
+  prof_.host("round_wait", ms_since(t_wait));
+  t_wait = std::chrono::steady_clock::now();
   arena_off_ = 0;
   arena_.reserve(ids_read * K * sizeof(NodeRec) + sizeof(RoundCounters) + K * (sizeof(u32) + sizeof(Scales)) +
                  (size_t(D) + 1) * sizeof(LevelStats) + 5 * 256);
@@ -422,6 +506,7 @@ void Engine::boost_round(Model& m) {
   }
   arena_off_ = 0;
   m.iteration_indptr.push_back(int(m.trees.size()));
+  prof_.host("round_readback", ms_since(t_wait));
 }
 
 }  // namespace dp

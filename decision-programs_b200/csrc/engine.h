@@ -32,7 +32,13 @@ class Profiler {
   void end(cudaStream_t s);
   void resolve();  // after the stream has been synchronised
   std::string json() const;
-  void reset() { stats_.clear(); log_.clear(); }
+  void reset() { stats_.clear(); log_.clear(); host_.clear(); }
+  // Host-side time of a phase (always recorded; cheap).
+  void host(const char* name, double ms) {
+    auto& h = host_[name];
+    h.first += 1;
+    h.second += ms;
+  }
   ~Profiler();
 
  private:
@@ -44,6 +50,7 @@ class Profiler {
   std::map<std::string, Stat> stats_;
   struct Entry { std::string name; float ms; double bytes; };
   std::vector<Entry> log_;  // the most recent launches, bounded
+  std::map<std::string, std::pair<u64, double>> host_;  // phase -> (count, ms)
   cudaEvent_t take();
 };
 
@@ -78,6 +85,9 @@ class Engine {
   template <class T>
   void grow_keep(DevBuf<T>& b, size_t n);
   RoundBuffers round_buffers(int depth, u64 cap_split, u64 cap_next) const;
+  // Sizes every round buffer for the levels whose bounds stay within the
+  // asynchronous limits, so steady rounds allocate nothing.
+  void presize();
 
   DMatrix& d_;
   TrainParams p_;

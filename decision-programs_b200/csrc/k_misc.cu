@@ -123,6 +123,11 @@ __global__ void __launch_bounds__(256) k_leaf_update(const LeafTask* __restrict_
   }
 }
 
+__global__ void k_init_margins(float* __restrict__ margin, u64 n, int K, const float* __restrict__ base) {
+  for (u64 i = u64(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += u64(gridDim.x) * blockDim.x)
+    margin[i] = base[i % u64(K)];
+}
+
 __global__ void k_iota(u32* p, u64 n) {
   for (u64 i = u64(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += u64(gridDim.x) * blockDim.x) p[i] = u32(i);
 }
@@ -189,6 +194,13 @@ void launch_leaf_update_dev(const LeafTask* tasks, const u32* ntasks_dev, float*
   DP_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
   k_leaf_update<<<sms * 8, 256, 0, s>>>(tasks, 0, ntasks_dev, margin, K);
   after_launch("leaf_update");
+}
+
+void launch_init_margins(float* margin, u64 R, int K, const float* base, cudaStream_t s) {
+  const u64 n = R * u64(K);
+  if (!n) return;
+  k_init_margins<<<grid_for(n, 256), 256, 0, s>>>(margin, n, K, base);
+  after_launch("init_margins");
 }
 
 void launch_iota(u32* p, u64 n, cudaStream_t s) {

@@ -63,19 +63,36 @@ __device__ __forceinline__ bool holds_target(u64 base, u64 cnt, u64 n, u32 B) {
   return klo <= khi;
 }
 
-// Pass 1: count per (feature, 16-bit key prefix).
+constexpr int kUnroll = 4;  // rows of loads in flight per thread
+
+// Pass 1: count per (feature, 16-bit key prefix).  Lane = feature of a
+// 32-feature tile, warp = row: each warp load is one contiguous 128-byte run.
+// Infinite values (not the missing value) are flagged in bad[0].
 __global__ void __launch_bounds__(256) k_count16(const float* __restrict__ x, u64 R, u32 F, u64 stride, int has_mv,
-                                                 float mv, u32* __restrict__ cnt) {
+                                                 float mv, u32* __restrict__ cnt, u32* __restrict__ bad) {
   const u32 ftiles = (F + kTile - 1) / kTile;
   const u32 ft = blockIdx.y % ftiles;
   const u32 f = ft * kTile + (threadIdx.x & 31);
-  const u32 rows_per_block = (blockDim.x / 32);
-  for (u64 r = u64(blockIdx.x) * rows_per_block + (threadIdx.x >> 5); r < R; r += u64(gridDim.x) * rows_per_block) {
-    if (f >= F) continue;
-    const float v = x[r * stride + f];
-    if (missing(v, has_mv, mv)) continue;
-    atomicAdd(cnt + u64(f) * 65536 + (fkey(v) >> 16), 1u);
+  const u64 step = u64(gridDim.x) * (blockDim.x / 32);
+  u32* c = cnt + u64(f) * 65536;
+  bool inf = false;
+  if (f < F) {
+    for (u64 r0 = u64(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5); r0 < R; r0 += kUnroll * step) {
+      float v[kUnroll];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const u64 r = r0 + u * step;
+        v[u] = r < R ? x[r * stride + f] : __int_as_float(0x7fc00000);
+      }
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        if (missing(v[u], has_mv, mv)) continue;
+        inf |= isinf(v[u]);
+        atomicAdd(c + (fkey(v[u]) >> 16), 1u);
+      }
+    }
   }
+  if (bad && __any_sync(0xffffffffu, inf) && (threadIdx.x & 31) == 0) atomicOr(bad, 1u);
 }
 
 // Block-wide exclusive scan of one value per thread (blockDim.x <= 1024);
@@ -168,11 +185,13 @@ __global__ void __launch_bounds__(1024) k_select16(const u32* __restrict__ cnt, 
 }
 
 // Passes 2 and 3: count the next 8-bit digit of values whose prefix is active.
-// shift = bits below the active prefix (16, then 8).
+// shift = bits below the active prefix (16, then 8).  The active lists sit in
+// shared memory with a row stride of kSlots + 1 words, so the 32 lanes of a
+// warp (32 features) searching at the same index hit 32 different banks.
 __global__ void __launch_bounds__(256) k_count8(const float* __restrict__ x, u64 R, u32 F, u64 stride, int has_mv,
                                                 float mv, const FeatState* __restrict__ st, int shift,
                                                 u32* __restrict__ cnt) {
-  __shared__ u32 pre[kTile][kSlots];
+  __shared__ u32 pre[kTile][kSlots + 1];
   __shared__ u32 nact[kTile];
   const u32 ftiles = (F + kTile - 1) / kTile;
   const u32 ft = blockIdx.y % ftiles;
@@ -187,22 +206,29 @@ __global__ void __launch_bounds__(256) k_count8(const float* __restrict__ x, u64
   __syncthreads();
   const u32 fl = threadIdx.x & 31;
   const u32 f = ft * kTile + fl;
-  const u32 na = nact[fl];
-  const u32 rows_per_block = blockDim.x / 32;
-  for (u64 r = u64(blockIdx.x) * rows_per_block + (threadIdx.x >> 5); r < R; r += u64(gridDim.x) * rows_per_block) {
-    if (f >= F || na == 0) continue;
-    const float v = x[r * stride + f];
-    if (missing(v, has_mv, mv)) continue;
-    const u32 k = fkey(v);
-    const u32 p = k >> shift;
-    // lower bound of p in the ascending active list
-    u32 lo = 0, hi = na;
-    while (lo < hi) {
-      const u32 mid = (lo + hi) >> 1;
-      if (pre[fl][mid] < p) lo = mid + 1; else hi = mid;
+  const u32 na = f < F ? nact[fl] : 0;
+  if (na == 0) return;
+  const u32* P = pre[fl];
+  const u64 step = u64(gridDim.x) * (blockDim.x / 32);
+  for (u64 r0 = u64(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5); r0 < R; r0 += kUnroll * step) {
+    float v[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const u64 r = r0 + u * step;
+      v[u] = r < R ? x[r * stride + f] : __int_as_float(0x7fc00000);
     }
-    if (lo < na && pre[fl][lo] == p)
-      atomicAdd(cnt + (u64(f) * kSlots + lo) * 256 + ((k >> (shift - 8)) & 0xffu), 1u);
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      if (missing(v[u], has_mv, mv)) continue;
+      const u32 k = fkey(v[u]);
+      const u32 p = k >> shift;
+      // first active prefix >= p (entries past nact hold 0xffffffff)
+      u32 pos = 0;
+#pragma unroll
+      for (u32 w = kSlots / 2; w > 0; w >>= 1)
+        if (P[pos + w - 1] < p) pos += w;
+      if (pos < na && P[pos] == p) atomicAdd(cnt + (u64(f) * kSlots + pos) * 256 + ((k >> (shift - 8)) & 0xffu), 1u);
+    }
   }
 }
 
@@ -295,42 +321,49 @@ __global__ void k_finalize(FeatState* __restrict__ st, u32 F, u64 R_total, float
 }
 
 // bins[r][f] = #boundaries <= x (255 for missing); padding columns are zero.
+// Boundaries past a feature's last one read +inf, so a fixed eight-step
+// search counts the boundaries <= x; rows of kSlots + 1 words keep the lanes'
+// lookups in distinct banks.
 __global__ void __launch_bounds__(256) k_bin(const float* __restrict__ x, u64 R, u32 F, u64 stride, int has_mv,
                                              float mv, const float* __restrict__ cut, const u16* __restrict__ nbins,
                                              u8* __restrict__ bins, u64 bstride) {
-  __shared__ float c[kTile][256];
-  __shared__ u32 ncut[kTile];
+  __shared__ float c[kTile][kSlots + 1];
   const u32 ftiles = (u32(bstride) + kTile - 1) / kTile;
   const u32 ft = blockIdx.y % ftiles;
-  for (int i = threadIdx.x; i < kTile * 256; i += blockDim.x) {
-    const u32 fl = i / 256, f = ft * kTile + fl;
-    c[fl][i % 256] = f < F ? cut[u64(f) * 256 + i % 256] : 0.0f;
-  }
-  if (threadIdx.x < kTile) {
-    const u32 f = ft * kTile + threadIdx.x;
-    ncut[threadIdx.x] = f < F ? u32(nbins[f]) - 1 : 0;
+  for (int i = threadIdx.x; i < kTile * kSlots; i += blockDim.x) {
+    const u32 fl = i / kSlots, j = i % kSlots, f = ft * kTile + fl;
+    c[fl][j] = (f < F && j + 1 < nbins[f]) ? cut[u64(f) * kSlots + j] : __int_as_float(0x7f800000);
   }
   __syncthreads();
   const u32 fl = threadIdx.x & 31, f = ft * kTile + fl;
   if (f >= bstride) return;
-  const u32 nc = ncut[fl];
-  const u32 rows_per_block = blockDim.x / 32;
-  for (u64 r = u64(blockIdx.x) * rows_per_block + (threadIdx.x >> 5); r < R; r += u64(gridDim.x) * rows_per_block) {
-    u8 b = 0;
-    if (f < F) {
-      const float v = x[r * stride + f];
-      if (missing(v, has_mv, mv)) {
-        b = kMissingBin;
-      } else {
-        u32 lo = 0, hi = nc;
-        while (lo < hi) {
-          const u32 mid = (lo + hi) >> 1;
-          if (c[fl][mid] <= v) lo = mid + 1; else hi = mid;
-        }
-        b = u8(lo);
-      }
+  const float* C = c[fl];
+  const u64 step = u64(gridDim.x) * (blockDim.x / 32);
+  for (u64 r0 = u64(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5); r0 < R; r0 += kUnroll * step) {
+    float v[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const u64 r = r0 + u * step;
+      v[u] = (r < R && f < F) ? x[r * stride + f] : 0.0f;
     }
-    bins[r * bstride + f] = b;
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const u64 r = r0 + u * step;
+      if (r >= R) break;
+      u8 b = 0;
+      if (f < F) {
+        if (missing(v[u], has_mv, mv)) {
+          b = kMissingBin;
+        } else {
+          u32 pos = 0;
+#pragma unroll
+          for (u32 w = kSlots / 2; w > 0; w >>= 1)
+            if (C[pos + w - 1] <= v[u]) pos += w;
+          b = u8(pos);
+        }
+      }
+      bins[r * bstride + f] = b;
+    }
   }
 }
 
@@ -346,19 +379,29 @@ unsigned row_blocks(u64 R, u32 rows_per_block, u32 ftiles) {
 
 }  // namespace
 
+void launch_prefix_counts(const float* x, u64 R, u32 F, u64 stride, bool has_mv, float mv, u32* cnt, u32* bad,
+                          cudaStream_t s) {
+  if (!R || !F) return;
+  const u32 ftiles = (F + kTile - 1) / kTile;
+  const dim3 grid(row_blocks(R, 8, ftiles), ftiles);
+  k_count16<<<grid, 256, 0, s>>>(x, R, F, stride, int(has_mv), mv, cnt, bad);
+  after_launch("cut_count16");
+}
+
 void compute_cuts(const float* x, u64 R, u32 F, u64 stride, int max_bin, bool has_mv, float mv, u64 R_total,
-                  Comm* comm, const CutsDevice& out, cudaStream_t s) {
+                  Comm* comm, const CutsDevice& out, cudaStream_t s, const u32* prefix_counts) {
   need(F > 0, "cuts need at least one feature");
   need(R_total < (u64(1) << 32), "row count exceeds the 32-bit count range of the cut search");
   need(max_bin >= 2, "max_bin must be at least 2");
   const u32 ftiles = (F + kTile - 1) / kTile;
-  DevBuf<u32> cnt(u64(F) * 65536);
+  DevBuf<u32> cnt(u64(F) * kPrefixBuckets);
   DevBuf<FeatState> st(F);
-  DP_CUDA(cudaMemsetAsync(cnt.get(), 0, cnt.size() * sizeof(u32), s));
   const dim3 grid(row_blocks(R, 8, ftiles), ftiles);
-  if (R) {
-    k_count16<<<grid, 256, 0, s>>>(x, R, F, stride, int(has_mv), mv, cnt.get());
-    after_launch("cut_count16");
+  if (prefix_counts) {
+    DP_CUDA(cudaMemcpyAsync(cnt.get(), prefix_counts, cnt.size() * sizeof(u32), cudaMemcpyDeviceToDevice, s));
+  } else {
+    DP_CUDA(cudaMemsetAsync(cnt.get(), 0, cnt.size() * sizeof(u32), s));
+    launch_prefix_counts(x, R, F, stride, has_mv, mv, cnt.get(), nullptr, s);
   }
   if (comm) comm->sum_u32(cnt.get(), cnt.size(), s);
   k_select16<<<F, 1024, 0, s>>>(cnt.get(), R_total, max_bin, st.get());

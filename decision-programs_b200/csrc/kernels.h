@@ -147,6 +147,8 @@ void launch_leaf_update_dev(const LeafTask* tasks, const u32* ntasks_dev, float*
 
 // ---- misc ---------------------------------------------------------------------
 void launch_iota(u32* p, u64 n, cudaStream_t s);
+// margin[r][k] = base[k] for r < R.
+void launch_init_margins(float* margin, u64 R, int K, const float* base, cudaStream_t s);
 // Flags (atomicOr into bad[0]) any +-inf in x[r*stride + f].
 void launch_check_finite(const float* x, u64 R, u32 F, u64 stride, u32* bad, cudaStream_t s);
 // Labels: flags values that are not valid for the objective.

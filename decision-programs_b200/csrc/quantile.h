@@ -5,10 +5,21 @@
 
 namespace dp {
 
+constexpr u64 kPrefixBuckets = 65536;  // 16-bit key prefixes per feature
+
+// First pass of the cut search over rows [0, R) of x: per (feature, 16-bit
+// key prefix) counts of the non-missing values are added into
+// cnt[F][kPrefixBuckets]; an infinite value that is not the missing value
+// sets bad[0] (bad may be null).  Rows may arrive in several calls.
+void launch_prefix_counts(const float* x, u64 R, u32 F, u64 stride, bool has_mv, float mv, u32* cnt, u32* bad,
+                          cudaStream_t s);
+
 // Cuts over the rows of every rank (comm == nullptr for one GPU); R_total is
-// the row count over all ranks.  Synchronises `s` before returning.
+// the row count over all ranks.  prefix_counts, when given, holds this rank's
+// first-pass counts (launch_prefix_counts) and the pass is not repeated.
+// Synchronises `s` before returning.
 void compute_cuts(const float* x, u64 R, u32 F, u64 stride, int max_bin, bool has_mv, float mv, u64 R_total,
-                  Comm* comm, const CutsDevice& out, cudaStream_t s);
+                  Comm* comm, const CutsDevice& out, cudaStream_t s, const u32* prefix_counts = nullptr);
 
 void launch_bin_matrix(const float* x, u64 R, u32 F, u64 stride, bool has_mv, float mv, const CutsDevice& cuts,
                        u8* bins, u64 bin_stride, cudaStream_t s);

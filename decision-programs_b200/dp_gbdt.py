@@ -21,6 +21,7 @@ LIB_PATH = HERE / "libdp_gbdt.so"
 
 EXPORTED = [
     "XGBoostVersion", "XGBuildInfo", "XGBGetLastError", "XGDMatrixCreateFromCudaArrayInterface",
+    "XGDMatrixCreateFromDense",
     "XGDMatrixSetInfoFromInterface", "XGDMatrixSetFloatInfo", "XGDMatrixNumRow", "XGDMatrixNumCol",
     "XGDMatrixFree", "XGBoosterCreate", "XGBoosterFree", "XGBoosterSetParam", "XGBoosterUpdateOneIter",
     "XGBoosterBoostedRounds", "XGBoosterSaveJsonConfig", "XGBoosterSaveModel", "XGBoosterSaveModelToBuffer",
@@ -53,6 +54,7 @@ def lib() -> C.CDLL:
         L.XGBuildInfo.argtypes = [C.POINTER(C.c_char_p)]
         L.XGBGetLastError.restype = C.c_char_p
         L.XGDMatrixCreateFromCudaArrayInterface.argtypes = [C.c_char_p, C.c_char_p, C.POINTER(P)]
+        L.XGDMatrixCreateFromDense.argtypes = [C.c_char_p, C.c_char_p, C.POINTER(P)]
         L.XGDMatrixSetInfoFromInterface.argtypes = [P, C.c_char_p, C.c_char_p]
         L.XGDMatrixSetFloatInfo.argtypes = [P, C.c_char_p, P, u64]
         L.XGDMatrixNumRow.argtypes = [P, C.POINTER(u64)]
@@ -123,7 +125,8 @@ def array_interface(ptr: int, shape: Iterable[int], typestr: str = "<f4", stride
 
 
 class DMatrix:
-    """Borrowed dense fp32 CUDA matrix [R][F] (NaN = missing)."""
+    """Dense fp32 matrix [R][F] (NaN = missing): a borrowed CUDA matrix, or a
+    host matrix copied to the current CUDA device (from_host)."""
 
     def __init__(self, data_ptr: int, rows: int, cols: int, label_ptr: int | None = None, row_stride: int | None = None,
                  missing: float = math.nan, keepalive=None):
@@ -147,6 +150,29 @@ class DMatrix:
             y = y.contiguous()
             d._keep = (x, y)
             d.set_label_ptr(y.data_ptr(), y.shape[0])
+        return d
+
+    @classmethod
+    def from_host(cls, x, y=None, missing: float = math.nan) -> "DMatrix":
+        """x: host float32 [R, F] (numpy array or CPU torch tensor, rows
+        contiguous; pinned memory copies fastest); y: host float32 [R].
+        Goes through XGDMatrixCreateFromDense."""
+        if hasattr(x, "data_ptr"):
+            assert not x.is_cuda and x.dim() == 2 and x.element_size() == 4 and x.stride(1) == 1
+            ptr, (rows, cols), row_stride = x.data_ptr(), x.shape, x.stride(0)
+        else:
+            import numpy as np
+            assert x.dtype == np.float32 and x.ndim == 2 and x.strides[1] == 4
+            ptr, (rows, cols), row_stride = x.ctypes.data, x.shape, x.strides[0] // 4
+        d = cls.__new__(cls)
+        d.handle = C.c_void_p()
+        strides = None if row_stride == cols else [int(row_stride) * 4, 4]
+        cfg = '{"missing":NaN,"nthread":2}' if math.isnan(missing) else json.dumps({"missing": missing, "nthread": 2})
+        check(lib().XGDMatrixCreateFromDense(array_interface(ptr, [rows, cols], strides=strides).encode(),
+                                             cfg.encode(), C.byref(d.handle)))
+        d._keep = None  # the library holds its own copy
+        if y is not None:
+            d.set_label_host(y.numpy() if hasattr(y, "numpy") else y)
         return d
 
     def set_label_ptr(self, ptr: int, n: int) -> None:

@@ -47,6 +47,14 @@ DP_API const char* XGBGetLastError(void);
  * native/class_model_native_adapter.cuh:26). */
 DP_API int XGDMatrixCreateFromCudaArrayInterface(const char* data, const char* config, DMatrixHandle* out);
 
+/* Dense fp32 HOST matrix (same array-interface and config JSON, host data
+ * pointer), copied to the calling thread's current CUDA device.  XGBoost C API
+ * function; the reference binds only the CUDA variant above.  The copy runs in
+ * chunks that overlap the first counting pass of the quantile cuts; pinned
+ * host memory lets the chunks stream at the host link's rate.  The host
+ * buffer may be released when the call returns. */
+DP_API int XGDMatrixCreateFromDense(const char* data, const char* config, DMatrixHandle* out);
+
 /* field "label": f32 [R] array interface (device or host memory); copied.
  * Replaces native/class_native_training.cuh:52. */
 DP_API int XGDMatrixSetInfoFromInterface(DMatrixHandle handle, const char* field, const char* data);

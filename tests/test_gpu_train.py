@@ -134,6 +134,43 @@ def test_tiny_inputs(dp, orc, R):
     run(dp, orc, x, y, "reg:squarederror", 3, max_depth=4, min_child_weight=0.0)
 
 
+@pytest.mark.parametrize("strided", [False, True])
+def test_host_matrix_trains_the_same_trees(dp, orc, strided):
+    """XGDMatrixCreateFromDense (host data, overlapped upload) grows the
+    oracle's trees; with a row stride wider than the column count too."""
+    rng = np.random.default_rng(31)
+    R, F = 70000, 12  # several upload chunks
+    x = rng.standard_normal((R, F)).astype(np.float32)
+    x[rng.random((R, F)) < 0.05] = np.nan
+    y = (np.nan_to_num(x[:, 0]) - 0.5 * np.nan_to_num(x[:, 3]) + 0.1 * rng.standard_normal(R)).astype(np.float32)
+    xs = x
+    if strided:
+        wide = np.zeros((R, F + 5), np.float32)
+        wide[:, :F] = x
+        xs = wide[:, :F]
+    params = {"objective": "reg:squarederror", "tree_method": "hist", "device": "cuda:0", "max_depth": 6,
+              "max_bin": 256, "eta": 0.3}
+    torch.cuda.set_device(0)
+    d = dp.DMatrix.from_host(xs, y)
+    assert d.num_row() == R and d.num_col() == F
+    b = dp.train(params, d, 3)
+    o = orc.Model(x, y, "reg:squarederror", max_depth=6, max_bin=256, eta=0.3, rounds=3, threads=8)
+    compare_models(b, o, 1)
+    np.testing.assert_array_equal(b.margins(R, 1).view(np.uint32), o.margins().view(np.uint32))
+
+
+def test_host_matrix_refuses_inf_and_device_memory(dp):
+    x = np.zeros((100, 3), np.float32)
+    x[7, 1] = np.inf
+    with pytest.raises(dp.DPError, match="inf"):
+        dp.DMatrix.from_host(x)
+    xd = torch.zeros((10, 3), device="cuda")
+    with pytest.raises(dp.DPError, match="host memory"):
+        h = dp.C.c_void_p()
+        dp.check(dp.lib().XGDMatrixCreateFromDense(dp.array_interface(xd.data_ptr(), [10, 3]).encode(), b"{}",
+                                                   dp.C.byref(h)))
+
+
 def test_config_reports_cuda_updater_and_model_reloads(dp, orc, tmp_path):
     x, y = c1_data(3000, seed=2)
     b, o, _ = run(dp, orc, x, y, "binary:logistic", 3, max_depth=3)
