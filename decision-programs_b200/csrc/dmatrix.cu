@@ -112,7 +112,8 @@ const Quantized& DMatrix::quantized(int max_bin, Comm* comm, cudaStream_t s) {
   compute_cuts(x_, rows_, cols_, stride_, max_bin, has_mv_, mv_, q->rows_total, comm, cd, s,
                prefix_counts_.size() ? prefix_counts_.get() : nullptr);
   q->bins.resize(std::max<u64>(rows_, 1) * q->bin_stride);
-  launch_bin_matrix(x_, rows_, cols_, stride_, has_mv_, mv_, cd, q->bins.get(), q->bin_stride, s);
+  q->bins_blk.resize(std::max<u64>((rows_ + 31) / 32, 1) * 32 * cols_);
+  launch_bin_matrix(x_, rows_, cols_, stride_, has_mv_, mv_, cd, q->bins.get(), q->bin_stride, s, q->bins_blk.get());
   q->cut_h.resize(q->cut.size());
   q->nbins_h.resize(cols_);
   q->has_missing_h.resize(cols_);

@@ -25,6 +25,7 @@ struct Quantized {
   DevBuf<u16> nbins;        // [F]
   DevBuf<u8> has_missing;   // [F]
   DevBuf<u8> bins;          // [R][bin_stride]
+  DevBuf<u8> bins_blk;      // [ceil(R/32)][F][32]: codes of one feature for 32 rows per sector
   std::vector<float> cut_h;
   std::vector<u16> nbins_h;
   std::vector<u8> has_missing_h;

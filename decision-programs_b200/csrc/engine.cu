@@ -430,7 +430,7 @@ void Engine::boost_round(Model& m) {
 
     // ---- partition and the children's segments
     prof_.begin(stream_, "partition", 0.0);
-    launch_partition_dev(q_->bins.get(), q_->bin_stride, tarr_[set].get(), tarr_[1 - set].get(), part_nodes_.get(),
+    launch_partition_dev(q_->bins_blk.get(), 32 * u64(F), tarr_[set].get(), tarr_[1 - set].get(), part_nodes_.get(),
                          part_tasks_.get(), &ctr->n_part_tasks, cursors_.get(), stream_);
     prof_.end(stream_);
     launch_copy_left(rb, stream_);

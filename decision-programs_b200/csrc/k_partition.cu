@@ -5,6 +5,10 @@
 // the missing code follows default_left (native/class_tree_runtime_compare.cu:47,
 // native/class_runtime.cu:128).
 //
+// The split feature's code of row r is read from the 32-row blocked bin
+// layout (bins_blk[r / 32][f][r % 32]), so one 32-byte sector serves up to 32
+// rows of a node instead of one row per 128-byte row-major line.
+//
 // One pass: a block decides its task's rows (decision bits kept in shared
 // memory), reserves space in its node's left and right parts with one atomic
 // add on each of the node's cursors, then scatters: left rows upward from the
@@ -27,7 +31,7 @@ __device__ __forceinline__ bool goes_left(u8 b, const PartNode& nd) {
   return int(b) <= nd.bin;
 }
 
-__device__ __forceinline__ void partition_task(u32 task, const u8* __restrict__ bins, u64 bstride,
+__device__ __forceinline__ void partition_task(u32 task, const u8* __restrict__ bins_blk, u64 blk_stride,
                                                const TreeArrays* __restrict__ src,
                                                const TreeArrays* __restrict__ dst,
                                                const PartNode* __restrict__ nodes,
@@ -39,7 +43,7 @@ __device__ __forceinline__ void partition_task(u32 task, const u8* __restrict__ 
   const PartNode nd = nodes[t.node];
   const TreeArrays s = src[nd.tree];
   const TreeArrays d = dst[nd.tree];
-  const u8* col = bins + nd.feature;
+  const u8* col = bins_blk + u64(nd.feature) * 32;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const u32 n = u32(t.end - t.begin);
 
@@ -54,7 +58,8 @@ __device__ __forceinline__ void partition_task(u32 task, const u8* __restrict__ 
     }
     u8 b[kIlp];
 #pragma unroll
-    for (int u = 0; u < kIlp; ++u) b[u] = r[u] != 0xffffffffu ? __ldg(col + u64(r[u]) * bstride) : u8(0);
+    for (int u = 0; u < kIlp; ++u)
+      b[u] = r[u] != 0xffffffffu ? __ldg(col + u64(r[u] >> 5) * blk_stride + (r[u] & 31u)) : u8(0);
 #pragma unroll
     for (int u = 0; u < kIlp; ++u) {
       const bool go = r[u] != 0xffffffffu && goes_left(b[u], nd);
@@ -102,17 +107,17 @@ __device__ __forceinline__ void partition_task(u32 task, const u8* __restrict__ 
   __syncthreads();  // shared state is reused by the block's next task
 }
 
-__global__ void __launch_bounds__(kPartThreads) k_partition(const u8* __restrict__ bins, u64 bstride,
+__global__ void __launch_bounds__(kPartThreads) k_partition(const u8* __restrict__ bins_blk, u64 blk_stride,
                                                             const TreeArrays* __restrict__ src,
                                                             const TreeArrays* __restrict__ dst,
                                                             const PartNode* __restrict__ nodes,
                                                             const PartTask* __restrict__ tasks,
                                                             u32* __restrict__ cursors) {
-  partition_task(blockIdx.x, bins, bstride, src, dst, nodes, tasks, cursors);
+  partition_task(blockIdx.x, bins_blk, blk_stride, src, dst, nodes, tasks, cursors);
 }
 
 // Task count in device memory: a fixed grid walks the tasks.
-__global__ void __launch_bounds__(kPartThreads) k_partition_dev(const u8* __restrict__ bins, u64 bstride,
+__global__ void __launch_bounds__(kPartThreads) k_partition_dev(const u8* __restrict__ bins_blk, u64 blk_stride,
                                                                 const TreeArrays* __restrict__ src,
                                                                 const TreeArrays* __restrict__ dst,
                                                                 const PartNode* __restrict__ nodes,
@@ -120,25 +125,27 @@ __global__ void __launch_bounds__(kPartThreads) k_partition_dev(const u8* __rest
                                                                 const u32* __restrict__ ntasks,
                                                                 u32* __restrict__ cursors) {
   const u32 n = *ntasks;
-  for (u32 t = blockIdx.x; t < n; t += gridDim.x) partition_task(t, bins, bstride, src, dst, nodes, tasks, cursors);
+  for (u32 t = blockIdx.x; t < n; t += gridDim.x)
+    partition_task(t, bins_blk, blk_stride, src, dst, nodes, tasks, cursors);
 }
 
 }  // namespace
 
-void launch_partition(const u8* bins, u64 bin_stride, const TreeArrays* src, const TreeArrays* dst,
+void launch_partition(const u8* bins_blk, u64 blk_stride, const TreeArrays* src, const TreeArrays* dst,
                       const PartNode* nodes, const PartTask* tasks, u32 ntasks, u32* cursors, cudaStream_t s) {
   if (!ntasks) return;
-  k_partition<<<ntasks, kPartThreads, 0, s>>>(bins, bin_stride, src, dst, nodes, tasks, cursors);
+  k_partition<<<ntasks, kPartThreads, 0, s>>>(bins_blk, blk_stride, src, dst, nodes, tasks, cursors);
   after_launch("partition");
 }
 
-void launch_partition_dev(const u8* bins, u64 bin_stride, const TreeArrays* src, const TreeArrays* dst,
+void launch_partition_dev(const u8* bins_blk, u64 blk_stride, const TreeArrays* src, const TreeArrays* dst,
                           const PartNode* nodes, const PartTask* tasks, const u32* ntasks_dev, u32* cursors,
                           cudaStream_t s) {
   int dev = 0, sms = 148;
   DP_CUDA(cudaGetDevice(&dev));
   DP_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-  k_partition_dev<<<sms * 8, kPartThreads, 0, s>>>(bins, bin_stride, src, dst, nodes, tasks, ntasks_dev, cursors);
+  k_partition_dev<<<sms * 8, kPartThreads, 0, s>>>(bins_blk, blk_stride, src, dst, nodes, tasks, ntasks_dev,
+                                                    cursors);
   after_launch("partition");
 }
 

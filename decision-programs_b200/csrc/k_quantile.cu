@@ -323,11 +323,16 @@ __global__ void k_finalize(FeatState* __restrict__ st, u32 F, u64 R_total, float
 // bins[r][f] = #boundaries <= x (255 for missing); padding columns are zero.
 // Boundaries past a feature's last one read +inf, so a fixed eight-step
 // search counts the boundaries <= x; rows of kSlots + 1 words keep the lanes'
-// lookups in distinct banks.
+// lookups in distinct banks.  A block bins 32-row tiles of a 32-feature
+// slice: lane = feature, warp = rows warp + 8u.  With bins_blk set, the tile
+// is also written in the 32-row blocked layout
+// bins_blk[r / 32][f][r % 32] (see launch_bin_matrix) through a shared-memory
+// transpose, as 4-byte stores.
 __global__ void __launch_bounds__(256) k_bin(const float* __restrict__ x, u64 R, u32 F, u64 stride, int has_mv,
                                              float mv, const float* __restrict__ cut, const u16* __restrict__ nbins,
-                                             u8* __restrict__ bins, u64 bstride) {
+                                             u8* __restrict__ bins, u64 bstride, u8* __restrict__ bins_blk) {
   __shared__ float c[kTile][kSlots + 1];
+  __shared__ __align__(4) u8 tile[kTile][36];  // [feature][row of the tile], padded
   const u32 ftiles = (u32(bstride) + kTile - 1) / kTile;
   const u32 ft = blockIdx.y % ftiles;
   for (int i = threadIdx.x; i < kTile * kSlots; i += blockDim.x) {
@@ -335,23 +340,22 @@ __global__ void __launch_bounds__(256) k_bin(const float* __restrict__ x, u64 R,
     c[fl][j] = (f < F && j + 1 < nbins[f]) ? cut[u64(f) * kSlots + j] : __int_as_float(0x7f800000);
   }
   __syncthreads();
-  const u32 fl = threadIdx.x & 31, f = ft * kTile + fl;
-  if (f >= bstride) return;
+  const u32 fl = threadIdx.x & 31, f = ft * kTile + fl, warp = threadIdx.x >> 5;
   const float* C = c[fl];
-  const u64 step = u64(gridDim.x) * (blockDim.x / 32);
-  for (u64 r0 = u64(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5); r0 < R; r0 += kUnroll * step) {
+  const u64 ntiles = (R + 31) / 32;
+  for (u64 tb = blockIdx.x; tb < ntiles; tb += gridDim.x) {
     float v[kUnroll];
 #pragma unroll
     for (int u = 0; u < kUnroll; ++u) {
-      const u64 r = r0 + u * step;
+      const u64 r = tb * 32 + warp + 8 * u;
       v[u] = (r < R && f < F) ? x[r * stride + f] : 0.0f;
     }
 #pragma unroll
     for (int u = 0; u < kUnroll; ++u) {
-      const u64 r = r0 + u * step;
-      if (r >= R) break;
+      const u32 rl = warp + 8 * u;
+      const u64 r = tb * 32 + rl;
       u8 b = 0;
-      if (f < F) {
+      if (r < R && f < F) {
         if (missing(v[u], has_mv, mv)) {
           b = kMissingBin;
         } else {
@@ -362,7 +366,16 @@ __global__ void __launch_bounds__(256) k_bin(const float* __restrict__ x, u64 R,
           b = u8(pos);
         }
       }
-      bins[r * bstride + f] = b;
+      if (r < R && f < bstride) bins[r * bstride + f] = b;
+      tile[fl][rl] = b;
+    }
+    if (bins_blk) {
+      __syncthreads();
+      const u32 tf = threadIdx.x >> 3, tr = (threadIdx.x & 7) * 4, gf = ft * kTile + tf;
+      if (gf < F)
+        *reinterpret_cast<u32*>(bins_blk + tb * (32 * u64(F)) + u64(gf) * 32 + tr) =
+            *reinterpret_cast<const u32*>(&tile[tf][tr]);
+      __syncthreads();
     }
   }
 }
@@ -423,11 +436,11 @@ void compute_cuts(const float* x, u64 R, u32 F, u64 stride, int max_bin, bool ha
 }
 
 void launch_bin_matrix(const float* x, u64 R, u32 F, u64 stride, bool has_mv, float mv, const CutsDevice& cuts,
-                       u8* bins, u64 bin_stride, cudaStream_t s) {
+                       u8* bins, u64 bin_stride, cudaStream_t s, u8* bins_blk) {
   if (!R) return;
   const u32 ftiles = u32((bin_stride + kTile - 1) / kTile);
-  const dim3 grid(row_blocks(R, 8, ftiles), ftiles);
-  k_bin<<<grid, 256, 0, s>>>(x, R, F, stride, int(has_mv), mv, cuts.cut, cuts.nbins, bins, bin_stride);
+  const dim3 grid(row_blocks(R, 32, ftiles), ftiles);
+  k_bin<<<grid, 256, 0, s>>>(x, R, F, stride, int(has_mv), mv, cuts.cut, cuts.nbins, bins, bin_stride, bins_blk);
   after_launch("bin_matrix");
 }
 

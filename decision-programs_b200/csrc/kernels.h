@@ -126,12 +126,13 @@ struct PartNode {
 // Splits every node's segment from `src` into `dst`: left rows fill
 // [begin, begin + nleft), right rows [begin + nleft, end).  cursors[2*node]
 // and cursors[2*node+1] (zeroed u32 scratch) end as the node's left and right
-// row counts.
-void launch_partition(const u8* bins, u64 bin_stride, const TreeArrays* src, const TreeArrays* dst,
+// row counts.  Bin codes come from the 32-row blocked layout:
+// bins_blk[(r / 32) * blk_stride + f * 32 + r % 32], blk_stride = 32 * F.
+void launch_partition(const u8* bins_blk, u64 blk_stride, const TreeArrays* src, const TreeArrays* dst,
                       const PartNode* nodes, const PartTask* tasks, u32 ntasks, u32* cursors, cudaStream_t s);
 constexpr u32 kPartChunk = 4096;
 // The same with the task count in device memory.
-void launch_partition_dev(const u8* bins, u64 bin_stride, const TreeArrays* src, const TreeArrays* dst,
+void launch_partition_dev(const u8* bins_blk, u64 blk_stride, const TreeArrays* src, const TreeArrays* dst,
                           const PartNode* nodes, const PartTask* tasks, const u32* ntasks_dev, u32* cursors,
                           cudaStream_t s);
 

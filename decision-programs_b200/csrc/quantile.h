@@ -21,7 +21,11 @@ void launch_prefix_counts(const float* x, u64 R, u32 F, u64 stride, bool has_mv,
 void compute_cuts(const float* x, u64 R, u32 F, u64 stride, int max_bin, bool has_mv, float mv, u64 R_total,
                   Comm* comm, const CutsDevice& out, cudaStream_t s, const u32* prefix_counts = nullptr);
 
+// bins[r * bin_stride + f] (row-major, bin_stride >= F, padding zeroed) and,
+// when bins_blk is set, the same codes in the 32-row blocked layout
+// bins_blk[(r / 32) * 32 * F + f * 32 + r % 32] (ceil(R / 32) * 32 * F bytes),
+// where the codes of one feature for 32 consecutive rows share a sector.
 void launch_bin_matrix(const float* x, u64 R, u32 F, u64 stride, bool has_mv, float mv, const CutsDevice& cuts,
-                       u8* bins, u64 bin_stride, cudaStream_t s);
+                       u8* bins, u64 bin_stride, cudaStream_t s, u8* bins_blk = nullptr);
 
 }  // namespace dp

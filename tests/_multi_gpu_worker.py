@@ -29,6 +29,8 @@ def data(case: str):
         y = np.argmax(x[:, :4] + 0.3 * rng.standard_normal((R, 4)), 1).astype(np.float32)
         return x, y, {"objective": "multi:softprob", "num_class": 4, "max_depth": 5}
     y = (x[:, 0] * x[:, 1] + np.sin(x[:, 2]) + 0.1 * rng.standard_normal(R)).astype(np.float32)
+    if case == "deep_exact_host":
+        return x, y, {"objective": "reg:squarederror", "max_depth": 11, "min_child_weight": 0.0}
     return x, y, {"objective": "reg:squarederror", "max_depth": 8}
 
 
@@ -45,7 +47,10 @@ def main() -> None:
         comm = dp.Comm(bytes(uid.numpy().tobytes()), world, rank, local)
         x, y, params = data(case)
         lo, hi = rank * len(y) // world, (rank + 1) * len(y) // world
-        d = dp.DMatrix.from_torch(torch.from_numpy(x[lo:hi]).cuda(), torch.from_numpy(y[lo:hi]).cuda())
+        if case.endswith("_host"):
+            d = dp.DMatrix.from_host(np.ascontiguousarray(x[lo:hi]), np.ascontiguousarray(y[lo:hi]))
+        else:
+            d = dp.DMatrix.from_torch(torch.from_numpy(x[lo:hi]).cuda(), torch.from_numpy(y[lo:hi]).cuda())
         b = dp.train(params | {"device": f"cuda:{local}"}, d, rounds, comm=comm)
         K = params.get("num_class", 1)
         (out_dir / f"rank{rank}.json").write_bytes(b.save_raw())

@@ -25,12 +25,15 @@ def free_port() -> int:
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs at least two GPUs")
-@pytest.mark.parametrize("case,K", [("squared", 1), ("logistic_nan", 1), ("softprob", 4)])
+@pytest.mark.parametrize("case,K", [("squared", 1), ("logistic_nan", 1), ("softprob", 4), ("deep_exact_host", 1)])
 def test_sharded_ranks_match_the_oracle(orc, tmp_path, case, K):
     import _multi_gpu_worker as w
     world = min(torch.cuda.device_count(), 4)
     rounds = 4
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    if case == "deep_exact_host":
+        # host matrices; levels past 3 open nodes read exact counts back first
+        env.update(DP_ASYNC_OPEN_LIMIT="3", DP_ASYNC_HIST_BYTES=str(8 * 24 * 256 * 16))
     cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            f"--nproc-per-node={world}", "--master-addr=127.0.0.1", f"--master-port={free_port()}",
            str(ROOT / "tests" / "_multi_gpu_worker.py"), case, str(tmp_path), str(rounds)]
@@ -39,7 +42,8 @@ def test_sharded_ranks_match_the_oracle(orc, tmp_path, case, K):
     models = [(tmp_path / f"rank{k}.json").read_bytes() for k in range(world)]
     assert all(m == models[0] for m in models)
     x, y, params = w.data(case)
-    o = orc.Model(x, y, params["objective"], num_class=K, max_depth=params["max_depth"], rounds=rounds, threads=8)
+    o = orc.Model(x, y, params["objective"], num_class=K, max_depth=params["max_depth"], rounds=rounds, threads=8,
+                  min_child_weight=params.get("min_child_weight", 1.0))
     trees = json.loads(models[0])["learner"]["gradient_booster"]["model"]["trees"]
     assert len(trees) == o.num_trees()
     for i, t in enumerate(trees):
