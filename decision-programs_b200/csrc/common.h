@@ -5,8 +5,10 @@
 
 #include <atomic>
 #include <cstdint>
+#include <functional>
 #include <stdexcept>
 #include <string>
+#include <vector>
 
 namespace dp {
 
@@ -61,8 +63,9 @@ class DeviceGuard {
   int prev_ = 0, dev_ = 0;
 };
 
-// Owned device allocation (stream-ordered free is not needed: every owner
-// synchronises its stream before it is destroyed).
+// Device buffer: an owned allocation, or a view into a slab (see SlabPlan)
+// that it never frees.  Stream-ordered frees are not needed: every owner
+// synchronises its stream before it is destroyed.
 template <class T>
 class DevBuf {
  public:
@@ -71,9 +74,16 @@ class DevBuf {
   ~DevBuf() { release(); }
   DevBuf(const DevBuf&) = delete;
   DevBuf& operator=(const DevBuf&) = delete;
-  DevBuf(DevBuf&& o) noexcept : p_(o.p_), n_(o.n_) { o.p_ = nullptr; o.n_ = 0; }
+  DevBuf(DevBuf&& o) noexcept : p_(o.p_), n_(o.n_), owned_(o.owned_) { o.p_ = nullptr; o.n_ = 0; }
   DevBuf& operator=(DevBuf&& o) noexcept {
-    if (this != &o) { release(); p_ = o.p_; n_ = o.n_; o.p_ = nullptr; o.n_ = 0; }
+    if (this != &o) {
+      release();
+      p_ = o.p_;
+      n_ = o.n_;
+      owned_ = o.owned_;
+      o.p_ = nullptr;
+      o.n_ = 0;
+    }
     return *this;
   }
   void resize(size_t n) {
@@ -81,15 +91,24 @@ class DevBuf {
     release();
     if (n) DP_CUDA(cudaMalloc(&p_, n * sizeof(T)));
     n_ = n;
+    owned_ = true;
   }
   // Grows (never shrinks) the capacity; contents are not preserved.
   void reserve(size_t n) {
     if (n > n_) resize(n);
   }
+  // Becomes a view of n elements at p (memory owned elsewhere).
+  void adopt(T* p, size_t n) {
+    release();
+    p_ = p;
+    n_ = n;
+    owned_ = false;
+  }
   void release() {
-    if (p_) cudaFree(p_);
+    if (p_ && owned_) cudaFree(p_);
     p_ = nullptr;
     n_ = 0;
+    owned_ = true;
   }
   T* get() const { return p_; }
   size_t size() const { return n_; }
@@ -97,6 +116,38 @@ class DevBuf {
  private:
   T* p_ = nullptr;
   size_t n_ = 0;
+  bool owned_ = true;
+};
+
+// Places several buffers in one device allocation: on this class of GPU a
+// cudaMalloc or cudaFree costs about half a millisecond whatever its size.
+// want() records a buffer that must hold n elements (ignored when it already
+// does); commit() allocates the slab, appends it to `slabs` (which must
+// outlive the views) and turns every recorded buffer into a view of it,
+// 256-byte aligned.
+class SlabPlan {
+ public:
+  template <class T>
+  void want(DevBuf<T>& b, size_t n) {
+    if (n <= b.size()) return;
+    const size_t off = (bytes_ + 255) & ~size_t(255);
+    bytes_ = off + n * sizeof(T);
+    DevBuf<T>* bp = &b;
+    binds_.push_back([bp, off, n](unsigned char* base) { bp->adopt(reinterpret_cast<T*>(base + off), n); });
+  }
+  void commit(std::vector<DevBuf<unsigned char>>& slabs) {
+    if (binds_.empty()) return;
+    slabs.emplace_back(bytes_);
+    unsigned char* base = slabs.back().get();
+    for (auto& f : binds_) f(base);
+    binds_.clear();
+    bytes_ = 0;
+  }
+  size_t bytes() const { return bytes_; }
+
+ private:
+  size_t bytes_ = 0;
+  std::vector<std::function<void(unsigned char*)>> binds_;
 };
 
 // Owned pinned host staging buffer.

@@ -1,6 +1,7 @@
 #include "dmatrix.h"
 
 #include <algorithm>
+#include <chrono>
 
 #include "quantile.h"
 
@@ -16,12 +17,13 @@ DMatrix::DMatrix(const float* x, u64 rows, u32 cols, u64 stride, int device, boo
   need(stride >= cols, "DMatrix row stride is smaller than its column count");
   DeviceGuard g(device_);
   if (rows_ == 0) return;
-  DevBuf<u32> bad(1);
-  prefix_counts_.resize(u64(cols_) * kPrefixBuckets);
-  DP_CUDA(cudaMemset(bad.get(), 0, sizeof(u32)));
+  // the counts, then one flag word for infinite values
+  prefix_counts_.resize(u64(cols_) * kPrefixBuckets + 1);
+  u32* bad = prefix_counts_.get() + u64(cols_) * kPrefixBuckets;
   DP_CUDA(cudaMemset(prefix_counts_.get(), 0, prefix_counts_.size() * sizeof(u32)));
-  launch_prefix_counts(x_, rows_, cols_, stride_, has_mv_, mv_, prefix_counts_.get(), bad.get(), nullptr);
-  check_bad(bad.get());
+  launch_prefix_counts(x_, rows_, cols_, stride_, has_mv_, mv_, prefix_counts_.get(), bad, nullptr);
+  check_bad(bad);
+  prefix_valid_ = true;
 }
 
 std::unique_ptr<DMatrix> DMatrix::from_host(const float* x, u64 rows, u32 cols, u64 stride, int device, bool has_mv,
@@ -39,15 +41,14 @@ std::unique_ptr<DMatrix> DMatrix::from_host(const float* x, u64 rows, u32 cols, 
   d->owned_.resize(std::max<u64>(rows, 1) * cols);
   d->x_ = d->owned_.get();
   if (rows == 0) return d;
-  DevBuf<u32> bad(1);
-  d->prefix_counts_.resize(u64(cols) * kPrefixBuckets);
+  d->prefix_counts_.resize(u64(cols) * kPrefixBuckets + 1);
+  u32* bad = d->prefix_counts_.get() + u64(cols) * kPrefixBuckets;
   cudaStream_t copy = nullptr, count = nullptr;
   cudaEvent_t landed = nullptr;
   DP_CUDA(cudaStreamCreateWithFlags(&copy, cudaStreamNonBlocking));
   DP_CUDA(cudaStreamCreateWithFlags(&count, cudaStreamNonBlocking));
   DP_CUDA(cudaEventCreateWithFlags(&landed, cudaEventDisableTiming));
   try {
-    DP_CUDA(cudaMemsetAsync(bad.get(), 0, sizeof(u32), count));
     DP_CUDA(cudaMemsetAsync(d->prefix_counts_.get(), 0, d->prefix_counts_.size() * sizeof(u32), count));
     // about 32 MB per chunk: the counting pass of chunk i runs while chunk
     // i + 1 crosses the host link
@@ -63,7 +64,7 @@ std::unique_ptr<DMatrix> DMatrix::from_host(const float* x, u64 rows, u32 cols, 
                                   cudaMemcpyHostToDevice, copy));
       DP_CUDA(cudaEventRecord(landed, copy));
       DP_CUDA(cudaStreamWaitEvent(count, landed, 0));
-      launch_prefix_counts(dst, n, cols, cols, has_mv, mv, d->prefix_counts_.get(), bad.get(), count);
+      launch_prefix_counts(dst, n, cols, cols, has_mv, mv, d->prefix_counts_.get(), bad, count);
     }
     DP_CUDA(cudaStreamSynchronize(copy));
     DP_CUDA(cudaStreamSynchronize(count));
@@ -78,7 +79,8 @@ std::unique_ptr<DMatrix> DMatrix::from_host(const float* x, u64 rows, u32 cols, 
   cudaEventDestroy(landed);
   cudaStreamDestroy(copy);
   cudaStreamDestroy(count);
-  d->check_bad(bad.get());
+  d->check_bad(bad);
+  d->prefix_valid_ = true;
   return d;
 }
 
@@ -104,15 +106,22 @@ const Quantized& DMatrix::quantized(int max_bin, Comm* comm, cudaStream_t s) {
   auto q = std::make_unique<Quantized>();
   q->max_bin = max_bin;
   q->bin_stride = (u64(cols_) + 15) / 16 * 16;
-  q->cut.resize(u64(cols_) * kMaxBins);
-  q->nbins.resize(cols_);
-  q->has_missing.resize(cols_);
+  SlabPlan plan;
+  plan.want(q->cut, u64(cols_) * kMaxBins);
+  plan.want(q->nbins, cols_);
+  plan.want(q->has_missing, cols_);
+  plan.want(q->bins, std::max<u64>(rows_, 1) * q->bin_stride);
+  plan.want(q->bins_blk, std::max<u64>((rows_ + 31) / 32, 1) * 32 * cols_);
+  auto t0 = std::chrono::steady_clock::now();
+  plan.commit(q->slabs);
+  const double ms_alloc = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
   q->rows_total = comm ? comm->sum_host_u64(rows_, s) : rows_;
   CutsDevice cd{q->cut.get(), q->nbins.get(), q->has_missing.get()};
+  // the first-pass counts taken at construction are consumed by the search
   compute_cuts(x_, rows_, cols_, stride_, max_bin, has_mv_, mv_, q->rows_total, comm, cd, s,
-               prefix_counts_.size() ? prefix_counts_.get() : nullptr);
-  q->bins.resize(std::max<u64>(rows_, 1) * q->bin_stride);
-  q->bins_blk.resize(std::max<u64>((rows_ + 31) / 32, 1) * 32 * cols_);
+               prefix_valid_ ? prefix_counts_.get() : nullptr);
+  prefix_valid_ = false;
+  const double ms_cuts = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
   launch_bin_matrix(x_, rows_, cols_, stride_, has_mv_, mv_, cd, q->bins.get(), q->bin_stride, s, q->bins_blk.get());
   q->cut_h.resize(q->cut.size());
   q->nbins_h.resize(cols_);
@@ -121,6 +130,9 @@ const Quantized& DMatrix::quantized(int max_bin, Comm* comm, cudaStream_t s) {
   DP_CUDA(cudaMemcpyAsync(q->nbins_h.data(), q->nbins.get(), cols_ * sizeof(u16), cudaMemcpyDeviceToHost, s));
   DP_CUDA(cudaMemcpyAsync(q->has_missing_h.data(), q->has_missing.get(), cols_, cudaMemcpyDeviceToHost, s));
   DP_CUDA(cudaStreamSynchronize(s));
+  q->host_ms_alloc = ms_alloc;
+  q->host_ms_cuts = ms_cuts - ms_alloc;
+  q->host_ms_bins = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count() - ms_cuts;
   q_ = std::move(q);
   return *q_;
 }

@@ -19,6 +19,7 @@
 namespace dp {
 
 struct Quantized {
+  std::vector<DevBuf<u8>> slabs;  // memory of the device buffers below
   int max_bin = 0;
   u64 bin_stride = 0;       // bytes per row of `bins` (multiple of 16)
   DevBuf<float> cut;        // [F][256]
@@ -30,6 +31,7 @@ struct Quantized {
   std::vector<u16> nbins_h;
   std::vector<u8> has_missing_h;
   u64 rows_total = 0;       // over all ranks
+  double host_ms_alloc = 0, host_ms_cuts = 0, host_ms_bins = 0;  // build phases (host clock)
 };
 
 class DMatrix {
@@ -57,7 +59,8 @@ class DMatrix {
   void check_bad(const u32* bad_dev);
   const float* x_ = nullptr;
   DevBuf<float> owned_;        // host-sourced matrix
-  DevBuf<u32> prefix_counts_;  // [cols][kPrefixBuckets], this rank's rows
+  DevBuf<u32> prefix_counts_;  // [cols][kPrefixBuckets] this rank's rows, then a flag word
+  bool prefix_valid_ = false;  // counts present and not yet consumed by a cut search
   u64 rows_ = 0, stride_ = 0;
   u32 cols_ = 0;
   int device_ = 0;

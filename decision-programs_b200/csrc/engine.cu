@@ -107,6 +107,11 @@ Engine::Engine(DMatrix& d, const TrainParams& p, Comm* comm) : d_(d), p_(p), com
   auto t0 = std::chrono::steady_clock::now();
   q_ = &d_.quantized(p_.max_bin, comm_, stream_);
   prof_.host("quantize", ms_since(t0));
+  if (q_->host_ms_alloc + q_->host_ms_cuts + q_->host_ms_bins > 0) {
+    prof_.host("quantize_alloc", q_->host_ms_alloc);
+    prof_.host("quantize_cuts", q_->host_ms_cuts);
+    prof_.host("quantize_bins", q_->host_ms_bins);
+  }
   t0 = std::chrono::steady_clock::now();
   slot_elems_ = u64(F_) * kMaxBins * 2;
   max_bins_ = 0;
@@ -114,50 +119,54 @@ Engine::Engine(DMatrix& d, const TrainParams& p, Comm* comm) : d_(d), p_(p), com
     max_bins_ = std::max<int>(max_bins_, q_->nbins_h[f]);
     if (q_->has_missing_h[f]) max_bins_ = kMaxBins;
   }
-  // label validation for the objective
-  {
-    DevBuf<u32> bad(1);
-    DP_CUDA(cudaMemsetAsync(bad.get(), 0, 4, stream_));
-    launch_check_labels(d_.labels(), R_, p_.objective_id(), K_, bad.get(), stream_);
-    u32 h = 0;
-    DP_CUDA(cudaMemcpyAsync(&h, bad.get(), 4, cudaMemcpyDeviceToHost, stream_));
-    DP_CUDA(cudaStreamSynchronize(stream_));
-    if (h) {
-      if (p_.objective_id() == kLogistic) fail("label must be in [0,1] for logistic regression");
-      if (p_.objective_id() == kSoftprob || p_.objective_id() == kSoftmax)
-        fail("label must be an integer in [0, num_class) for multi-class objectives");
-      fail("label contains NaN or infinity");
-    }
-  }
-  const u64 RK = std::max<u64>(R_, 1) * u64(K_);
-  margin_.resize(RK);
-  {
-    std::vector<float> base(K_);
-    for (int k = 0; k < K_; ++k) base[k] = p_.base_margin(k);
-    DevBuf<float> base_d(K_);
-    DP_CUDA(cudaMemcpyAsync(base_d.get(), base.data(), K_ * sizeof(float), cudaMemcpyHostToDevice, stream_));
-    launch_init_margins(margin_.get(), std::max<u64>(R_, 1), K_, base_d.get(), stream_);
-    DP_CUDA(cudaStreamSynchronize(stream_));
-  }
-  for (int s = 0; s < 2; ++s) {
-    gh_[s].resize(RK);
-    ridx_[s].resize(RK);
-    std::vector<TreeArrays> ta(K_);
-    for (int k = 0; k < K_; ++k) ta[k] = TreeArrays{ridx_[s].get() + u64(k) * R_, gh_[s].get() + u64(k) * R_};
-    tarr_[s].resize(K_);
-    DP_CUDA(cudaMemcpy(tarr_[s].get(), ta.data(), K_ * sizeof(TreeArrays), cudaMemcpyHostToDevice));
-  }
-  gmax_.resize(K_);
-  hmax_.resize(K_);
-  scales_.resize(K_);
-  hist_counter_.resize(1);
-  arena_.reserve(size_t(1) << 20);
-  ctr_h_.reserve(1);
   DP_CUDA(cudaDeviceGetAttribute(&sms_, cudaDevAttrMultiProcessorCount, device_));
   // testing knobs: force the exact-count path of deep levels
   async_open_limit_ = env_u64("DP_ASYNC_OPEN_LIMIT", async_open_limit_);
   async_hist_bytes_ = env_u64("DP_ASYNC_HIST_BYTES", async_hist_bytes_);
-  presize();
+
+  // every device buffer of the engine in one allocation
+  const u64 RK = std::max<u64>(R_, 1) * u64(K_);
+  SlabPlan plan;
+  plan.want(margin_, RK);
+  for (int s = 0; s < 2; ++s) {
+    plan.want(gh_[s], RK);
+    plan.want(ridx_[s], RK);
+    plan.want(tarr_[s], K_);
+  }
+  plan.want(gmax_, K_);
+  plan.want(hmax_, K_);
+  plan.want(scales_, K_);
+  plan.want(hist_counter_, 1);
+  plan.want(scratch_, 1 + size_t(K_));
+  presize(plan);
+  const auto t_alloc = std::chrono::steady_clock::now();
+  plan.commit(slabs_);
+  prof_.host("engine_alloc", ms_since(t_alloc));
+  arena_.reserve(size_t(1) << 20);
+
+  // label validation, initial margins, per-tree array tables; one wait
+  std::vector<float> base(K_);
+  for (int k = 0; k < K_; ++k) base[k] = p_.base_margin(k);
+  float* base_d = reinterpret_cast<float*>(scratch_.get() + 1);
+  DP_CUDA(cudaMemsetAsync(scratch_.get(), 0, sizeof(u32), stream_));
+  launch_check_labels(d_.labels(), R_, p_.objective_id(), K_, scratch_.get(), stream_);
+  std::memcpy(arena_.get() + kArenaHead, base.data(), K_ * sizeof(float));
+  DP_CUDA(cudaMemcpyAsync(base_d, arena_.get() + kArenaHead, K_ * sizeof(float), cudaMemcpyHostToDevice, stream_));
+  launch_init_margins(margin_.get(), std::max<u64>(R_, 1), K_, base_d, stream_);
+  std::vector<TreeArrays> ta(2 * size_t(K_));
+  for (int s = 0; s < 2; ++s)
+    for (int k = 0; k < K_; ++k) ta[s * K_ + k] = TreeArrays{ridx_[s].get() + u64(k) * R_, gh_[s].get() + u64(k) * R_};
+  DP_CUDA(cudaMemcpy(tarr_[0].get(), ta.data(), K_ * sizeof(TreeArrays), cudaMemcpyHostToDevice));
+  DP_CUDA(cudaMemcpy(tarr_[1].get(), ta.data() + K_, K_ * sizeof(TreeArrays), cudaMemcpyHostToDevice));
+  u32 bad = 0;
+  DP_CUDA(cudaMemcpyAsync(&bad, scratch_.get(), sizeof(u32), cudaMemcpyDeviceToHost, stream_));
+  DP_CUDA(cudaStreamSynchronize(stream_));
+  if (bad) {
+    if (p_.objective_id() == kLogistic) fail("label must be in [0,1] for logistic regression");
+    if (p_.objective_id() == kSoftprob || p_.objective_id() == kSoftmax)
+      fail("label must be an integer in [0, num_class) for multi-class objectives");
+    fail("label contains NaN or infinity");
+  }
   prof_.host("engine_init", ms_since(t0));
 }
 
@@ -172,13 +181,13 @@ Engine::~Engine() {
 void Engine::sync() {
   DP_CUDA(cudaStreamSynchronize(stream_));
   prof_.resolve();
-  arena_off_ = 0;
+  arena_off_ = kArenaHead;
 }
 
 template <class T>
 T* Engine::stage(const std::vector<T>& v) {
   const size_t bytes = v.size() * sizeof(T);
-  size_t off = (arena_off_ + 255) & ~size_t(255);
+  size_t off = (std::max(arena_off_, kArenaHead) + 255) & ~size_t(255);
   if (off + bytes > arena_.size()) {
     // all staged copies must land before the arena is replaced
     DP_CUDA(cudaStreamSynchronize(stream_));
@@ -186,7 +195,7 @@ T* Engine::stage(const std::vector<T>& v) {
     PinnedBuf<u8> fresh;
     fresh.reserve(want);
     arena_.swap(fresh);
-    off = 0;
+    off = kArenaHead;
   }
   std::memcpy(arena_.get() + off, v.data(), bytes);
   arena_off_ = off + bytes;
@@ -221,7 +230,7 @@ void Engine::grow_keep(DevBuf<T>& b, size_t n) {
   prof_.host("grow", ms_since(t0));
 }
 
-void Engine::presize() {
+void Engine::presize(SlabPlan& plan) {
   const u64 K = u64(K_), D = u64(p_.max_depth);
   const u64 Rt = std::max<u64>(q_->rows_total, 1);
   const u64 RK = std::max<u64>(R_, 1) * K;
@@ -251,27 +260,27 @@ void Engine::presize() {
   }
   if (complete) leaves_hi += open_hi;
   for (int r = 0; r < 2; ++r) {
-    grow(hist_[r], hist[r]);
-    grow(open_[r], opens[r]);
-    grow(build_[r], builds[r]);
-    grow(triples_[r], 3 * builds[r]);
+    plan.want(hist_[r], hist[r]);
+    plan.want(open_[r], opens[r]);
+    plan.want(build_[r], builds[r]);
+    plan.want(triples_[r], 3 * builds[r]);
   }
-  grow(hist_tasks_, tasks);
-  grow(eval_nodes_, split);
-  grow(best_, split);
-  grow(cand_, split * nchunks);
-  grow(split_idx_, split);
-  grow(part_nodes_, split);
-  grow(cursors_, 2 * split);
-  grow(gleft_, split);
-  grow(part_tasks_, (RK + kPartChunk - 1) / kPartChunk + split);
-  grow(leaves_, leaves_hi);
-  grow(leaf_tasks_, (RK + kLeafChunkRows - 1) / kLeafChunkRows + leaves_hi);
-  grow(nodes_, ids_hi * K);
-  grow(ctr_, 1);
-  grow(stats_, size_t(D) + 1);
-  grow(next_id_, K);
-  grow(tree_first_, K);
+  plan.want(hist_tasks_, tasks);
+  plan.want(eval_nodes_, split);
+  plan.want(best_, split);
+  plan.want(cand_, split * nchunks);
+  plan.want(split_idx_, split);
+  plan.want(part_nodes_, split);
+  plan.want(cursors_, 2 * split);
+  plan.want(gleft_, split);
+  plan.want(part_tasks_, (RK + kPartChunk - 1) / kPartChunk + split);
+  plan.want(leaves_, leaves_hi);
+  plan.want(leaf_tasks_, (RK + kLeafChunkRows - 1) / kLeafChunkRows + leaves_hi);
+  plan.want(nodes_, ids_hi * K);
+  plan.want(ctr_, 1);
+  plan.want(stats_, size_t(D) + 1);
+  plan.want(next_id_, K);
+  plan.want(tree_first_, K);
 }
 
 RoundBuffers Engine::round_buffers(int depth, u64 cap_split, u64 cap_next) const {
@@ -376,10 +385,11 @@ void Engine::boost_round(Model& m) {
   for (; depth < D; ++depth) {
     u64 nbuild_hi = depth == 0 ? u64(K) : (open_hi + 1) / 2;
     if (open_hi > async_open_limit_ || open_hi * slot_bytes > async_hist_bytes_) {
-      DP_CUDA(cudaMemcpyAsync(ctr_h_.get(), ctr, sizeof(RoundCounters), cudaMemcpyDeviceToHost, stream_));
+      RoundCounters* c_h = reinterpret_cast<RoundCounters*>(arena_.get());  // the arena's head
+      DP_CUDA(cudaMemcpyAsync(c_h, ctr, sizeof(RoundCounters), cudaMemcpyDeviceToHost, stream_));
       DP_CUDA(cudaStreamSynchronize(stream_));
-      open_hi = ctr_h_.get()->n_open;
-      nbuild_hi = ctr_h_.get()->n_build;
+      open_hi = c_h->n_open;
+      nbuild_hi = c_h->n_build;
       if (open_hi == 0) break;
     }
     const u64 next_hi = std::min<u64>(2 * open_hi, u64(K) * Rt);
@@ -463,8 +473,8 @@ void Engine::boost_round(Model& m) {
   DP_CUDA(cudaStreamSynchronize(stream_));
   prof_.host("round_wait", ms_since(t_wait));
   t_wait = std::chrono::steady_clock::now();
-  arena_off_ = 0;
-  arena_.reserve(ids_read * K * sizeof(NodeRec) + sizeof(RoundCounters) + K * (sizeof(u32) + sizeof(Scales)) +
+  arena_off_ = kArenaHead;
+  arena_.reserve(kArenaHead + ids_read * K * sizeof(NodeRec) + sizeof(RoundCounters) + K * (sizeof(u32) + sizeof(Scales)) +
                  (size_t(D) + 1) * sizeof(LevelStats) + 5 * 256);
   const RoundCounters* c_h = download(ctr, 1);
   const u32* nid_h = download(next_id_.get(), K);
@@ -504,7 +514,7 @@ void Engine::boost_round(Model& m) {
     }
     m.trees.push_back(std::move(t));
   }
-  arena_off_ = 0;
+  arena_off_ = kArenaHead;
   m.iteration_indptr.push_back(int(m.trees.size()));
   prof_.host("round_readback", ms_since(t_wait));
 }

@@ -87,7 +87,7 @@ class Engine {
   RoundBuffers round_buffers(int depth, u64 cap_split, u64 cap_next) const;
   // Sizes every round buffer for the levels whose bounds stay within the
   // asynchronous limits, so steady rounds allocate nothing.
-  void presize();
+  void presize(SlabPlan& plan);
 
   DMatrix& d_;
   TrainParams p_;
@@ -101,6 +101,7 @@ class Engine {
   int max_bins_ = kMaxBins;  // bin codes are < max_bins_ (missing code 255 included)
   u64 slot_elems_ = 0;
 
+  std::vector<DevBuf<u8>> slabs_;  // memory of the DevBuf views below
   DevBuf<float> margin_;
   DevBuf<float2> gh_[2];
   DevBuf<u32> ridx_[2];
@@ -125,15 +126,18 @@ class Engine {
   DevBuf<LeafRec> leaves_;
   DevBuf<RoundCounters> ctr_;
   DevBuf<LevelStats> stats_;
-  PinnedBuf<RoundCounters> ctr_h_;
+  DevBuf<u32> scratch_;  // [0]: label check flag; [1, 1 + K): initial margins (f32 bits)
   int sms_ = 148;
   // A level whose open-node bound exceeds either limit first reads the exact
   // counts back (one small copy) and sizes its buffers by them.
   u64 async_open_limit_ = u64(1) << 16;
   u64 async_hist_bytes_ = u64(4) << 30;
 
+  // Pinned staging: the first kArenaHead bytes hold round counters read back
+  // mid-round; staged copies start after them.
+  static constexpr size_t kArenaHead = 256;
   PinnedBuf<u8> arena_;
-  size_t arena_off_ = 0;
+  size_t arena_off_ = kArenaHead;
   Profiler prof_;
 };
 

@@ -402,34 +402,37 @@ void launch_prefix_counts(const float* x, u64 R, u32 F, u64 stride, bool has_mv,
 }
 
 void compute_cuts(const float* x, u64 R, u32 F, u64 stride, int max_bin, bool has_mv, float mv, u64 R_total,
-                  Comm* comm, const CutsDevice& out, cudaStream_t s, const u32* prefix_counts) {
+                  Comm* comm, const CutsDevice& out, cudaStream_t s, u32* prefix_counts) {
   need(F > 0, "cuts need at least one feature");
   need(R_total < (u64(1) << 32), "row count exceeds the 32-bit count range of the cut search");
   need(max_bin >= 2, "max_bin must be at least 2");
   const u32 ftiles = (F + kTile - 1) / kTile;
-  DevBuf<u32> cnt(u64(F) * kPrefixBuckets);
-  DevBuf<FeatState> st(F);
   const dim3 grid(row_blocks(R, 8, ftiles), ftiles);
-  if (prefix_counts) {
-    DP_CUDA(cudaMemcpyAsync(cnt.get(), prefix_counts, cnt.size() * sizeof(u32), cudaMemcpyDeviceToDevice, s));
-  } else {
-    DP_CUDA(cudaMemsetAsync(cnt.get(), 0, cnt.size() * sizeof(u32), s));
-    launch_prefix_counts(x, R, F, stride, has_mv, mv, cnt.get(), nullptr, s);
+  // scratch: the count words (the caller's prefix counts when given), then
+  // the per-feature search state
+  const u64 cnt_words = u64(F) * kPrefixBuckets;
+  const u64 st_off = prefix_counts ? 0 : (cnt_words * sizeof(u32) + 255) / 256 * 256;
+  DevBuf<u8> scratch(st_off + u64(F) * sizeof(FeatState));
+  u32* cnt = prefix_counts ? prefix_counts : reinterpret_cast<u32*>(scratch.get());
+  FeatState* st = reinterpret_cast<FeatState*>(scratch.get() + st_off);
+  if (!prefix_counts) {
+    DP_CUDA(cudaMemsetAsync(cnt, 0, cnt_words * sizeof(u32), s));
+    launch_prefix_counts(x, R, F, stride, has_mv, mv, cnt, nullptr, s);
   }
-  if (comm) comm->sum_u32(cnt.get(), cnt.size(), s);
-  k_select16<<<F, 1024, 0, s>>>(cnt.get(), R_total, max_bin, st.get());
+  if (comm) comm->sum_u32(cnt, cnt_words, s);
+  k_select16<<<F, 1024, 0, s>>>(cnt, R_total, max_bin, st);
   after_launch("cut_select16");
   for (int shift : {16, 8}) {
-    DP_CUDA(cudaMemsetAsync(cnt.get(), 0, u64(F) * kSlots * 256 * sizeof(u32), s));
+    DP_CUDA(cudaMemsetAsync(cnt, 0, u64(F) * kSlots * 256 * sizeof(u32), s));
     if (R) {
-      k_count8<<<grid, 256, 0, s>>>(x, R, F, stride, int(has_mv), mv, st.get(), shift, cnt.get());
+      k_count8<<<grid, 256, 0, s>>>(x, R, F, stride, int(has_mv), mv, st, shift, cnt);
       after_launch("cut_count8");
     }
-    if (comm) comm->sum_u32(cnt.get(), u64(F) * kSlots * 256, s);
-    k_select8<<<F, 256, 0, s>>>(cnt.get(), st.get());
+    if (comm) comm->sum_u32(cnt, u64(F) * kSlots * 256, s);
+    k_select8<<<F, 256, 0, s>>>(cnt, st);
     after_launch("cut_select8");
   }
-  k_finalize<<<(F + 127) / 128, 128, 0, s>>>(st.get(), F, R_total, out.cut, out.nbins, out.has_missing);
+  k_finalize<<<(F + 127) / 128, 128, 0, s>>>(st, F, R_total, out.cut, out.nbins, out.has_missing);
   after_launch("cut_finalize");
   // temporaries are freed after the stream drains
   DP_CUDA(cudaStreamSynchronize(s));

@@ -16,10 +16,11 @@ void launch_prefix_counts(const float* x, u64 R, u32 F, u64 stride, bool has_mv,
 
 // Cuts over the rows of every rank (comm == nullptr for one GPU); R_total is
 // the row count over all ranks.  prefix_counts, when given, holds this rank's
-// first-pass counts (launch_prefix_counts) and the pass is not repeated.
-// Synchronises `s` before returning.
+// first-pass counts (launch_prefix_counts, F * kPrefixBuckets words): the pass
+// is not repeated and the buffer is used as the search's scratch, so its
+// contents are lost.  Synchronises `s` before returning.
 void compute_cuts(const float* x, u64 R, u32 F, u64 stride, int max_bin, bool has_mv, float mv, u64 R_total,
-                  Comm* comm, const CutsDevice& out, cudaStream_t s, const u32* prefix_counts = nullptr);
+                  Comm* comm, const CutsDevice& out, cudaStream_t s, u32* prefix_counts = nullptr);
 
 // bins[r * bin_stride + f] (row-major, bin_stride >= F, padding zeroed) and,
 // when bins_blk is set, the same codes in the 32-row blocked layout
