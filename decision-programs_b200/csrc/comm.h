@@ -1,7 +1,8 @@
 // Collective interface used by the training path when rows are sharded over
 // several GPUs (one process per GPU).  The reference is single-GPU
-// (native/class_model_train.cu:42); the only exchange steps the sharded path
-// needs are sums of integer count / histogram arrays and maxima of floats.
+// (native/class_model_train.cu:42); the exchange steps the sharded path needs
+// are sums of integer counts, maxima of floats, a reduce-scatter of integer
+// histograms over feature groups and an all-gather of split candidates.
 #pragma once
 #include <cuda_runtime.h>
 
@@ -20,6 +21,11 @@ class Comm {
   virtual void sum_u32(std::uint32_t* d, size_t n, cudaStream_t s) = 0;
   virtual void sum_i64(std::int64_t* d, size_t n, cudaStream_t s) = 0;
   virtual void max_u32(std::uint32_t* d, size_t n, cudaStream_t s) = 0;
+  // recv[0, recv_n) = the element-wise sum over ranks of this rank's block
+  // send[rank * recv_n, (rank + 1) * recv_n); send holds size() blocks.
+  virtual void reduce_scatter_i64(const std::int64_t* send, std::int64_t* recv, size_t recv_n, cudaStream_t s) = 0;
+  // recv[r * bytes, (r + 1) * bytes) = rank r's send[0, bytes).
+  virtual void all_gather_bytes(const void* send, void* recv, size_t bytes, cudaStream_t s) = 0;
   // Host scalar helpers (synchronous).
   virtual std::uint64_t sum_host_u64(std::uint64_t v, cudaStream_t s) = 0;
 };

@@ -21,6 +21,9 @@ struct NcclApi {
   ncclResult_t (*comm_init_rank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
   ncclResult_t (*all_reduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
                              cudaStream_t) = nullptr;
+  ncclResult_t (*reduce_scatter)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                                 cudaStream_t) = nullptr;
+  ncclResult_t (*all_gather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
   ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
   const char* (*error_string)(ncclResult_t) = nullptr;
 };
@@ -36,9 +39,12 @@ const NcclApi& nccl() {
     api.get_unique_id = reinterpret_cast<decltype(api.get_unique_id)>(dlsym(h, "ncclGetUniqueId"));
     api.comm_init_rank = reinterpret_cast<decltype(api.comm_init_rank)>(dlsym(h, "ncclCommInitRank"));
     api.all_reduce = reinterpret_cast<decltype(api.all_reduce)>(dlsym(h, "ncclAllReduce"));
+    api.reduce_scatter = reinterpret_cast<decltype(api.reduce_scatter)>(dlsym(h, "ncclReduceScatter"));
+    api.all_gather = reinterpret_cast<decltype(api.all_gather)>(dlsym(h, "ncclAllGather"));
     api.comm_destroy = reinterpret_cast<decltype(api.comm_destroy)>(dlsym(h, "ncclCommDestroy"));
     api.error_string = reinterpret_cast<decltype(api.error_string)>(dlsym(h, "ncclGetErrorString"));
-    if (!api.get_unique_id || !api.comm_init_rank || !api.all_reduce || !api.comm_destroy || !api.error_string) {
+    if (!api.get_unique_id || !api.comm_init_rank || !api.all_reduce || !api.reduce_scatter || !api.all_gather ||
+        !api.comm_destroy || !api.error_string) {
       error = "NCCL library lacks a required symbol";
       api = NcclApi{};
     }
@@ -71,6 +77,13 @@ class NcclComm final : public Comm {
   int size() const override { return size_; }
   void sum_u32(u32* d, size_t n, cudaStream_t s) override {
     if (n) check(nccl().all_reduce(d, d, n, ncclUint32, ncclSum, comm_, s), "ncclAllReduce(u32 sum)");
+  }
+  void reduce_scatter_i64(const i64* send, i64* recv, size_t recv_n, cudaStream_t s) override {
+    if (recv_n)
+      check(nccl().reduce_scatter(send, recv, recv_n, ncclInt64, ncclSum, comm_, s), "ncclReduceScatter(i64 sum)");
+  }
+  void all_gather_bytes(const void* send, void* recv, size_t bytes, cudaStream_t s) override {
+    if (bytes) check(nccl().all_gather(send, recv, bytes, ncclUint8, comm_, s), "ncclAllGather(bytes)");
   }
   void sum_i64(i64* d, size_t n, cudaStream_t s) override {
     if (n) check(nccl().all_reduce(d, d, n, ncclInt64, ncclSum, comm_, s), "ncclAllReduce(i64 sum)");

@@ -113,7 +113,13 @@ Engine::Engine(DMatrix& d, const TrainParams& p, Comm* comm) : d_(d), p_(p), com
     prof_.host("quantize_bins", q_->host_ms_bins);
   }
   t0 = std::chrono::steady_clock::now();
-  slot_elems_ = u64(F_) * kMaxBins * 2;
+  G_ = comm_ ? comm_->size() : 1;
+  rank_ = comm_ ? comm_->rank() : 0;
+  fg_ = (F_ + u32(G_) - 1) / u32(G_);
+  f_own0_ = u32(rank_) * fg_;
+  f_own_n_ = f_own0_ < F_ ? std::min(fg_, F_ - f_own0_) : 0;
+  slot_elems_ = u64(fg_) * kMaxBins * 2;
+  full_slot_elems_ = u64(G_) * slot_elems_;
   max_bins_ = 0;
   for (u32 f = 0; f < F_; ++f) {
     max_bins_ = std::max<int>(max_bins_, q_->nbins_h[f]);
@@ -133,11 +139,11 @@ Engine::Engine(DMatrix& d, const TrainParams& p, Comm* comm) : d_(d), p_(p), com
     plan.want(ridx_[s], RK);
     plan.want(tarr_[s], K_);
   }
-  plan.want(gmax_, K_);
-  plan.want(hmax_, K_);
+  plan.want(ghmax_, 2 * size_t(K_));
   plan.want(scales_, K_);
   plan.want(hist_counter_, 1);
   plan.want(scratch_, 1 + size_t(K_));
+  plan.want(gh_totals_, 2 * size_t(K_));
   presize(plan);
   const auto t_alloc = std::chrono::steady_clock::now();
   plan.commit(slabs_);
@@ -239,7 +245,7 @@ void Engine::presize(SlabPlan& plan) {
   const u32 nchunks = (F_ + kEvalFeatureChunk - 1) / kEvalFeatureChunk;
   // the same bounds the level loop of boost_round derives
   u64 open_hi = K, ids_hi = 1, leaves_hi = 0;
-  u64 hist[2] = {0, 0}, tasks = 0, split = 0, opens[2] = {K, 0}, builds[2] = {K, 0};
+  u64 hist[2] = {0, 0}, tasks = 0, split = 0, opens[2] = {K, 0}, builds[2] = {K, 0}, send = 0;
   bool complete = true;
   for (u64 depth = 0; depth < D; ++depth) {
     if (open_hi > async_open_limit_ || open_hi * slot_bytes > async_hist_bytes_) {
@@ -250,6 +256,7 @@ void Engine::presize(SlabPlan& plan) {
     const u64 next_hi = std::min<u64>(2 * open_hi, K * Rt);
     hist[depth & 1] = std::max<u64>(hist[depth & 1], std::max<u64>(open_hi, 1) * slot_elems_);
     tasks = std::max<u64>(tasks, (nbuild_hi + 4 * u64(sms_) + 1) * ftiles);
+    if (G_ > 1) send = std::max<u64>(send, nbuild_hi * full_slot_elems_);
     split = std::max<u64>(split, open_hi);
     opens[(depth + 1) & 1] = std::max<u64>(opens[(depth + 1) & 1], next_hi);
     builds[(depth + 1) & 1] = std::max<u64>(builds[(depth + 1) & 1], open_hi);
@@ -268,11 +275,15 @@ void Engine::presize(SlabPlan& plan) {
   plan.want(hist_tasks_, tasks);
   plan.want(eval_nodes_, split);
   plan.want(best_, split);
-  plan.want(cand_, split * nchunks);
+  plan.want(cand_, split * std::max<u32>(nchunks, 1));
+  if (G_ > 1) {
+    plan.want(send_, send);
+    plan.want(best_local_, split);
+    plan.want(gathered_, split * u64(G_));
+  }
   plan.want(split_idx_, split);
   plan.want(part_nodes_, split);
   plan.want(cursors_, 2 * split);
-  plan.want(gleft_, split);
   plan.want(part_tasks_, (RK + kPartChunk - 1) / kPartChunk + split);
   plan.want(leaves_, leaves_hi);
   plan.want(leaf_tasks_, (RK + kLeafChunkRows - 1) / kLeafChunkRows + leaves_hi);
@@ -301,12 +312,12 @@ RoundBuffers Engine::round_buffers(int depth, u64 cap_split, u64 cap_next) const
   b.part_nodes = part_nodes_.get();
   b.part_tasks = part_tasks_.get();
   b.cursors = cursors_.get();
-  b.gleft = gleft_.get();
   b.leaves = leaves_.get();
   b.leaf_tasks = leaf_tasks_.get();
   b.ctr = ctr_.get();
   b.stats = stats_.get();
   b.K = u32(K_);
+  b.by_hess = G_ > 1 ? 1u : 0u;
   b.maxn = u32(std::min<u64>(nodes_.size() / u64(K_), u64(1) << 31));
   b.cap_split = cap_split;
   b.cap_next = cap_next;
@@ -348,20 +359,24 @@ void Engine::boost_round(Model& m) {
   const u64 slot_bytes = slot_elems_ * sizeof(i64);
 
   // ---- gradients and quantiser scales
-  DP_CUDA(cudaMemsetAsync(gmax_.get(), 0, K * sizeof(u32), stream_));
-  DP_CUDA(cudaMemsetAsync(hmax_.get(), 0, K * sizeof(u32), stream_));
+  u32* const gmax = ghmax_.get();  // [K] |g| maxima, then [K] h maxima (f32 bits)
+  u32* const hmax = ghmax_.get() + K;
+  DP_CUDA(cudaMemsetAsync(gmax, 0, 2 * size_t(K) * sizeof(u32), stream_));
   prof_.begin(stream_, "gradients", double(R) * K * (4 + 8) + double(R) * 4);
-  launch_gradients(p_.objective_id(), K, margin_.get(), d_.labels(), R, gh_[0].get(), gmax_.get(), hmax_.get(),
+  launch_gradients(p_.objective_id(), K, margin_.get(), d_.labels(), R, gh_[0].get(), gmax, hmax,
                    stream_);
   prof_.end(stream_);
   if (comm_) {
-    comm_->max_u32(gmax_.get(), K, stream_);
-    comm_->max_u32(hmax_.get(), K, stream_);
+    comm_->max_u32(gmax, 2 * size_t(K), stream_);
   }
-  launch_scales(K, gmax_.get(), hmax_.get(), scales_.get(), stream_);
+  launch_scales(K, gmax, hmax, scales_.get(), stream_);
   // (g, h) become exact int32 pairs once per round; every later pass reads them
   launch_quantize_gh(gh_[0].get(), R, K, scales_.get(), stream_);
   for (int k = 0; k < K; ++k) launch_iota(ridx_[0].get() + u64(k) * R, R, stream_);
+  // root totals: the quantised sums over every rank's rows
+  DP_CUDA(cudaMemsetAsync(gh_totals_.get(), 0, 2 * size_t(K) * sizeof(i64), stream_));
+  launch_gh_totals(gh_[0].get(), R, K, gh_totals_.get(), stream_);
+  if (comm_) comm_->sum_i64(gh_totals_.get(), 2 * size_t(K), stream_);
 
   // ---- round state: K roots, open at depth 0 and built directly
   grow(ctr_, 1);
@@ -373,7 +388,7 @@ void Engine::boost_round(Model& m) {
   grow_keep(nodes_, size_t(K));
   RoundCounters* const ctr = ctr_.get();  // allocated once; never regrown
   DP_CUDA(cudaMemsetAsync(stats_.get(), 0, (size_t(D) + 1) * sizeof(LevelStats), stream_));
-  launch_round_init(round_buffers(0, 0, 0), R, q_->rows_total, stream_);
+  launch_round_init(round_buffers(0, 0, 0), R, gh_totals_.get(), stream_);
 
   // Host-side upper bounds of the device counts, which size the buffers:
   // open nodes of this level, node ids per tree, closed leaves.  Every open
@@ -399,11 +414,15 @@ void Engine::boost_round(Model& m) {
     grow(hist_tasks_, (nbuild_hi + 4 * u64(sms_) + 1) * ftiles);
     grow(eval_nodes_, open_hi);
     grow(best_, open_hi);
-    grow(cand_, open_hi * nchunks);
+    grow(cand_, open_hi * std::max<u32>(nchunks, 1));
+    if (G_ > 1) {
+      grow(send_, nbuild_hi * full_slot_elems_);
+      grow(best_local_, open_hi);
+      grow(gathered_, open_hi * u64(G_));
+    }
     grow(split_idx_, open_hi);
     grow(part_nodes_, open_hi);
     grow(cursors_, 2 * open_hi);
-    grow(gleft_, open_hi);
     grow(part_tasks_, (RK + kPartChunk - 1) / kPartChunk + open_hi);
     grow(open_[(depth + 1) & 1], next_hi);
     grow(build_[(depth + 1) & 1], open_hi);
@@ -413,29 +432,45 @@ void Engine::boost_round(Model& m) {
     const RoundBuffers rb = round_buffers(depth, open_hi, next_hi);
     i64* hist = hist_[region].get();
 
-    // ---- histograms of the directly built nodes, then their siblings
+    // ---- histograms of the directly built nodes, then their siblings.  With
+    // several ranks, each builds partial histograms of all features for its
+    // rows (group-major), and a reduce-scatter leaves every rank the sums of
+    // its own feature group.
     launch_hist_tasks(rb, ftiles, depth, stream_);
-    launch_zero_slots(rb, hist, slot_elems_, comm_ ? nbuild_hi : 0, stream_);
+    i64* hout = G_ > 1 ? send_.get() : hist;
+    const u64 out_slot = G_ > 1 ? full_slot_elems_ : slot_elems_;
+    launch_zero_slots(rb, hout, out_slot, G_ > 1 ? nbuild_hi : 0, stream_);
+    const HistLayout lay{fg_, slot_elems_, nbuild_hi * slot_elems_};
     pi_hist[depth] = prof_.begin(stream_, "histograms", 0.0);
     launch_histograms(q_->bins.get(), q_->bin_stride, F, max_bins_, true, tarr_[set].get(), scales_.get(),
-                      hist_tasks_.get(), 0, hist_counter_.get(), hist, stream_, &ctr->n_hist_tasks);
+                      hist_tasks_.get(), 0, hist_counter_.get(), hout, stream_, &ctr->n_hist_tasks,
+                      G_ > 1 ? &lay : nullptr);
     prof_.end(stream_);
-    if (comm_) comm_->sum_i64(hist, nbuild_hi * slot_elems_, stream_);
+    if (G_ > 1) {
+      prof_.begin(stream_, "exchange_hist", double(nbuild_hi * full_slot_elems_) * sizeof(i64));
+      comm_->reduce_scatter_i64(send_.get(), hist, nbuild_hi * slot_elems_, stream_);
+      prof_.end(stream_);
+    }
     if (depth > 0) {
       pi_sub[depth] = prof_.begin(stream_, "subtract", 0.0);
       launch_subtract_dev(hist, hist_[1 - region].get(), slot_elems_, triples_[depth & 1].get(), &ctr->n_triples,
                           stream_);
       prof_.end(stream_);
-    } else {
-      launch_root_totals(rb, hist, slot_elems_, stream_);
     }
 
-    // ---- split evaluation and decisions
-    launch_make_eval(rb, stream_);
+    // ---- split evaluation over this rank's feature group, then (G > 1) the
+    // per-node best over all groups
     pi_eval[depth] = prof_.begin(stream_, "eval_splits", 0.0);
-    launch_eval_splits_dev(hist, F, q_->nbins.get(), q_->has_missing.get(), eval_nodes_.get(), &ctr->n_open,
-                           scales_.get(), sp, cand_.get(), best_.get(), stream_);
+    launch_eval_splits_dev(hist, f_own_n_, q_->nbins.get() + f_own0_, q_->has_missing.get() + f_own0_,
+                           eval_nodes_.get(), &ctr->n_open, scales_.get(), sp, cand_.get(),
+                           G_ > 1 ? best_local_.get() : best_.get(), stream_, fg_, f_own0_);
     prof_.end(stream_);
+    if (G_ > 1) {
+      prof_.begin(stream_, "exchange_cands", double(open_hi * u64(G_)) * sizeof(SplitCand));
+      comm_->all_gather_bytes(best_local_.get(), gathered_.get(), open_hi * sizeof(SplitCand), stream_);
+      prof_.end(stream_);
+      launch_pick_best(gathered_.get(), open_hi, G_, &ctr->n_open, best_.get(), stream_);
+    }
     launch_decide(rb, q_->cut.get(), q_->has_missing.get(), depth, D, set, stream_);
 
     // ---- partition and the children's segments
@@ -443,8 +478,6 @@ void Engine::boost_round(Model& m) {
     launch_partition_dev(q_->bins_blk.get(), 32 * u64(F), tarr_[set].get(), tarr_[1 - set].get(), part_nodes_.get(),
                          part_tasks_.get(), &ctr->n_part_tasks, cursors_.get(), stream_);
     prof_.end(stream_);
-    launch_copy_left(rb, stream_);
-    if (comm_) comm_->sum_i64(gleft_.get(), open_hi, stream_);
     launch_children(rb, depth, D, stream_);
 
     leaves_hi += open_hi;
@@ -487,7 +520,8 @@ void Engine::boost_round(Model& m) {
   if (ovf) fail("internal error: a per-round work list overflowed (flags " + std::to_string(ovf) + ")");
   for (int d = 0; d < D; ++d) {
     const LevelStats& st = st_h[d];
-    prof_.set_bytes(pi_hist[d], double(st.rows_built) * (double(F) + 12.0) + double(st.n_build) * slot_bytes);
+    prof_.set_bytes(pi_hist[d], double(st.rows_built) * (double(F) + 12.0) +
+                                    double(st.n_build) * double(F) * kMaxBins * 16.0);
     prof_.set_bytes(pi_sub[d], double(st.n_build) * slot_bytes * 3.0);
     prof_.set_bytes(pi_eval[d], double(st.n_open) * slot_bytes);
   }

@@ -99,20 +99,29 @@ class Engine {
   u32 F_ = 0;
   int K_ = 1;
   int max_bins_ = kMaxBins;  // bin codes are < max_bins_ (missing code 255 included)
-  u64 slot_elems_ = 0;
+  // Feature groups: with G ranks each owns fg_ = ceil(F / G) consecutive
+  // features (the last group may be short or empty).  A rank keeps the
+  // summed histograms of its own group only: slot_elems_ = fg_ * 2 * 256.
+  int G_ = 1, rank_ = 0;
+  u32 fg_ = 0, f_own0_ = 0, f_own_n_ = 0;
+  u64 slot_elems_ = 0;       // elements of one own-group histogram slot
+  u64 full_slot_elems_ = 0;  // elements of one slot over all groups (G * fg_ * 2 * 256)
 
   std::vector<DevBuf<u8>> slabs_;  // memory of the DevBuf views below
   DevBuf<float> margin_;
   DevBuf<float2> gh_[2];
   DevBuf<u32> ridx_[2];
   DevBuf<TreeArrays> tarr_[2];
-  DevBuf<u32> gmax_, hmax_;
+  DevBuf<u32> ghmax_;  // gradient and hessian maxima of the round, [2][K]
   DevBuf<Scales> scales_;
   DevBuf<i64> hist_[2];
   DevBuf<HistTask> hist_tasks_;
   DevBuf<u32> hist_counter_;
   DevBuf<EvalNode> eval_nodes_;
   DevBuf<SplitCand> cand_, best_;
+  DevBuf<i64> send_;                       // this rank's partial histograms, group-major (G > 1)
+  DevBuf<SplitCand> best_local_, gathered_;  // own-group candidates; all ranks' (G > 1)
+  DevBuf<i64> gh_totals_;                  // [K][2] root sums
   DevBuf<PartNode> part_nodes_;
   DevBuf<PartTask> part_tasks_;
   DevBuf<u32> cursors_;
@@ -122,7 +131,6 @@ class Engine {
   DevBuf<u32> next_id_, tree_first_, split_idx_;
   DevBuf<OpenRec> open_[2];
   DevBuf<u32> build_[2], triples_[2];
-  DevBuf<i64> gleft_;
   DevBuf<LeafRec> leaves_;
   DevBuf<RoundCounters> ctr_;
   DevBuf<LevelStats> stats_;

@@ -49,6 +49,7 @@ struct HistArgs {
   const HistTask* tasks;
   u32* counter;
   i64* hist;
+  HistLayout layout;
 };
 
 template <bool QUANT>
@@ -120,14 +121,17 @@ __global__ void __launch_bounds__(THREADS) k_hist(HistArgs a) {
       __syncthreads();
       // consecutive threads take consecutive bins of one feature: the global
       // atomics of a warp cover one contiguous 512-byte run
-      i64* out = a.hist + u64(key_slot) * a.F * (2 * kMaxBins);
+      i64* out = a.hist + u64(key_slot) * a.layout.slot_stride;
       for (int idx = threadIdx.x; idx < kCells; idx += THREADS) {
         const int f = idx / MB, b = idx % MB;
         const long long gs = Wg[f * kWRow + b], hs = Wh[f * kWRow + b];
         Wg[f * kWRow + b] = 0;
         Wh[f * kWRow + b] = 0;
-        if (!(gs | hs) || key_f0 + u32(f) >= a.F) continue;
-        unsigned long long* cell = reinterpret_cast<unsigned long long*>(out + (u64(key_f0 + f) * kMaxBins + b) * 2);
+        const u32 gf = key_f0 + u32(f);
+        if (!(gs | hs) || gf >= a.F) continue;
+        const u32 grp = gf / a.layout.fg, fl = gf - grp * a.layout.fg;
+        unsigned long long* cell = reinterpret_cast<unsigned long long*>(
+            out + grp * a.layout.group_stride + (u64(fl) * kMaxBins + b) * 2);
         atomicAdd(cell, static_cast<unsigned long long>(gs));
         atomicAdd(cell + 1, static_cast<unsigned long long>(hs));
       }
@@ -269,9 +273,11 @@ void launch_subtract_dev(i64* hist, const i64* parent_hist, u64 slot_elems, cons
 
 void launch_histograms(const u8* bins, u64 bin_stride, u32 F, int max_bins, bool quantized_gh,
                        const TreeArrays* trees, const Scales* scales, const HistTask* tasks, u32 ntasks,
-                       u32* counter, i64* hist, cudaStream_t s, const u32* ntasks_dev) {
+                       u32* counter, i64* hist, cudaStream_t s, const u32* ntasks_dev, const HistLayout* layout) {
   if (!ntasks && !ntasks_dev) return;
-  const HistArgs a{bins, bin_stride, F, ntasks, ntasks_dev, trees, scales, tasks, counter, hist};
+  const HistLayout lay = layout ? *layout : HistLayout{F, u64(F) * 2 * kMaxBins, 0};
+  need(lay.fg > 0, "histogram layout needs a positive feature group size");
+  const HistArgs a{bins, bin_stride, F, ntasks, ntasks_dev, trees, scales, tasks, counter, hist, lay};
   if (max_bins <= 64) {
     if (quantized_gh) launch_hist_variant<64, 512, true>(a, s);
     else launch_hist_variant<64, 512, false>(a, s);

@@ -71,12 +71,12 @@ __device__ __forceinline__ NodeRec& node_at(const RoundBuffers& b, u32 tree, u32
   return b.nodes[u64(id) * b.K + tree];
 }
 
-__global__ void k_round_init(RoundBuffers b, u64 R, u64 R_total) {
+__global__ void k_round_init(RoundBuffers b, u64 R, const i64* __restrict__ totals) {
   for (u32 k = threadIdx.x; k < b.K; k += blockDim.x) {
-    b.open_cur[k] = OpenRec{k, 0u, k, 0u, 0, i64(R), i64(R_total)};
+    b.open_cur[k] = OpenRec{k, 0u, k, 0u, 0, i64(R)};
     b.build[k] = k;
     b.next_id[k] = 1u;
-    node_at(b, k, 0) = NodeRec{0, 0, -1, -1, -1, -1, 0, 0, 0.f, 0.f};
+    node_at(b, k, 0) = NodeRec{totals[2 * k], totals[2 * k + 1], -1, -1, -1, -1, 0, 0, 0.f, 0.f};
   }
   if (threadIdx.x == 0) {
     RoundCounters c{};
@@ -122,12 +122,19 @@ __global__ void __launch_bounds__(kBook) k_hist_tasks(RoundBuffers b, u32 ftiles
       b.hist_tasks[t] = HistTask{s_slot[j], ft * kHistFeatureTile, s_tree[j], 0u, beg, end};
     });
   }
+  // split-evaluation inputs of the open nodes
+  const u32 n_open = b.ctr->n_open;
+  for (u32 i = threadIdx.x; i < n_open; i += kBook) {
+    const OpenRec o = b.open_cur[i];
+    const NodeRec& r = node_at(b, o.tree, o.id);
+    b.eval_nodes[i] = EvalNode{o.slot, o.tree, r.gq, r.hq};
+  }
   if (threadIdx.x == 0) {
     if (base > b.cap_hist_tasks) b.ctr->overflow |= kOvfHistTasks;
     b.ctr->n_hist_tasks = u32(base < b.cap_hist_tasks ? base : b.cap_hist_tasks);
     b.stats[depth].rows_built = i64(total);
     b.stats[depth].n_build = nb;
-    b.stats[depth].n_open = b.ctr->n_open;
+    b.stats[depth].n_open = n_open;
   }
 }
 
@@ -137,38 +144,6 @@ __global__ void k_zero_slots(const RoundCounters* __restrict__ ctr, i64* hist, u
   longlong2* h = reinterpret_cast<longlong2*>(hist);
   for (u64 i = u64(blockIdx.x) * blockDim.x + threadIdx.x; i < n2; i += u64(gridDim.x) * blockDim.x)
     h[i] = make_longlong2(0, 0);
-}
-
-// Root totals from feature 0 of each root histogram (one block per tree):
-// every row lands in exactly one bin of every feature.
-__global__ void k_root_totals(RoundBuffers b, const i64* __restrict__ hist, u64 slot_elems) {
-  __shared__ i64 sg[256], sh[256];
-  const u32 k = blockIdx.x;
-  const i64* h = hist + u64(k) * slot_elems;
-  sg[threadIdx.x] = h[2 * threadIdx.x];
-  sh[threadIdx.x] = h[2 * threadIdx.x + 1];
-  __syncthreads();
-  for (int o = 128; o > 0; o >>= 1) {
-    if (int(threadIdx.x) < o) {
-      sg[threadIdx.x] += sg[threadIdx.x + o];
-      sh[threadIdx.x] += sh[threadIdx.x + o];
-    }
-    __syncthreads();
-  }
-  if (threadIdx.x == 0) {
-    NodeRec& n = node_at(b, k, 0);
-    n.gq = sg[0];
-    n.hq = sh[0];
-  }
-}
-
-__global__ void k_make_eval(RoundBuffers b) {
-  const u32 n = b.ctr->n_open;
-  for (u32 i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
-    const OpenRec o = b.open_cur[i];
-    const NodeRec& r = node_at(b, o.tree, o.id);
-    b.eval_nodes[i] = EvalNode{o.slot, o.tree, r.gq, r.hq};
-  }
 }
 
 // Splits or closes every open node, in open-list order (trees contiguous,
@@ -252,32 +227,30 @@ __global__ void __launch_bounds__(kBook) k_decide(RoundBuffers b, const float* _
   }
 }
 
-__global__ void k_copy_left(RoundBuffers b) {
-  const u32 n = b.ctr->n_split;
-  for (u32 j = blockIdx.x * blockDim.x + threadIdx.x; j < n; j += gridDim.x * blockDim.x)
-    b.gleft[j] = i64(b.cursors[2 * j]);
-}
-
-// Children of every split node become the next level's open list; the one
-// with fewer rows over all ranks (ties: left) is built directly, its sibling
-// is the parent minus it.
+// Children of every split node become the next level's open list (see
+// RoundBuffers::by_hess for which child is built directly).  Block 0 also
+// sets the next level's counts.
 __global__ void k_children(RoundBuffers b, int depth, int max_depth) {
   const u32 ns = b.ctr->n_split;
   const bool more = depth + 1 < max_depth;
+  const bool fits = 2 * u64(ns) <= b.cap_next;
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    b.ctr->n_open = fits ? 2 * ns : 0u;
+    b.ctr->n_build = (more && fits) ? ns : 0u;
+    b.ctr->n_triples = (more && fits) ? ns : 0u;
+    if (!fits) atomicOr(&b.ctr->overflow, kOvfOpen);
+  }
+  if (!fits) return;
   for (u32 j = blockIdx.x * blockDim.x + threadIdx.x; j < ns; j += gridDim.x * blockDim.x) {
     const OpenRec o = b.open_cur[b.split_idx[j]];
     const NodeRec& p = node_at(b, o.tree, o.id);
-    const i64 nleft = i64(b.cursors[2 * j]);
-    if (nleft + i64(b.cursors[2 * j + 1]) != o.count) atomicOr(&b.ctr->overflow, kOvfLostRows);
-    if (2 * u64(j) + 1 >= b.cap_next) {
-      atomicOr(&b.ctr->overflow, kOvfOpen);
-      continue;
-    }
-    const i64 gl = b.gleft[j], gr = o.gcount - gl;
-    const bool right_small = gr < gl;
+    const i64 nleft = i64(b.cursors[2 * j]), nright = i64(b.cursors[2 * j + 1]);
+    if (nleft + nright != o.count) atomicOr(&b.ctr->overflow, kOvfLostRows);
+    const bool right_small = b.by_hess ? node_at(b, o.tree, u32(p.right)).hq < node_at(b, o.tree, u32(p.left)).hq
+                                       : nright < nleft;
     const u32 lslot = right_small ? ns + j : j, rslot = right_small ? j : ns + j;
-    b.open_next[2 * j] = OpenRec{o.tree, u32(p.left), lslot, 0u, o.begin, nleft, gl};
-    b.open_next[2 * j + 1] = OpenRec{o.tree, u32(p.right), rslot, 0u, o.begin + nleft, o.count - nleft, gr};
+    b.open_next[2 * j] = OpenRec{o.tree, u32(p.left), lslot, 0u, o.begin, nleft};
+    b.open_next[2 * j + 1] = OpenRec{o.tree, u32(p.right), rslot, 0u, o.begin + nleft, o.count - nleft};
     if (more) {
       b.build_next[j] = right_small ? 2 * j + 1 : 2 * j;
       b.triples_next[3 * j] = o.slot;
@@ -285,15 +258,6 @@ __global__ void k_children(RoundBuffers b, int depth, int max_depth) {
       b.triples_next[3 * j + 2] = ns + j;
     }
   }
-}
-
-__global__ void k_children_counts(RoundBuffers b, int depth, int max_depth) {
-  const u32 ns = b.ctr->n_split;
-  const bool more = depth + 1 < max_depth;
-  const bool fits = 2 * u64(ns) <= b.cap_next;
-  b.ctr->n_open = fits ? 2 * ns : 0u;
-  b.ctr->n_build = (more && fits) ? ns : 0u;
-  b.ctr->n_triples = (more && fits) ? ns : 0u;
 }
 
 // Leaf values into the node records, then the margin-update tasks (chunks of
@@ -344,8 +308,8 @@ int sm_count() {
 
 }  // namespace
 
-void launch_round_init(const RoundBuffers& b, u64 R, u64 R_total, cudaStream_t s) {
-  k_round_init<<<1, 256, 0, s>>>(b, R, R_total);
+void launch_round_init(const RoundBuffers& b, u64 R, const i64* gh_totals, cudaStream_t s) {
+  k_round_init<<<1, 256, 0, s>>>(b, R, gh_totals);
   after_launch("round_init");
 }
 
@@ -359,32 +323,15 @@ void launch_zero_slots(const RoundBuffers& b, i64* hist, u64 slot_elems, u64 min
   after_launch("zero_slots");
 }
 
-void launch_root_totals(const RoundBuffers& b, const i64* hist, u64 slot_elems, cudaStream_t s) {
-  k_root_totals<<<b.K, 256, 0, s>>>(b, hist, slot_elems);
-  after_launch("root_totals");
-}
-
-void launch_make_eval(const RoundBuffers& b, cudaStream_t s) {
-  k_make_eval<<<sm_count(), 256, 0, s>>>(b);
-  after_launch("make_eval");
-}
-
 void launch_decide(const RoundBuffers& b, const float* cut, const u8* has_missing, int depth, int max_depth,
                    int set, cudaStream_t s) {
   k_decide<<<1, kBook, 0, s>>>(b, cut, has_missing, depth, max_depth, set);
   after_launch("decide");
 }
 
-void launch_copy_left(const RoundBuffers& b, cudaStream_t s) {
-  k_copy_left<<<sm_count(), 256, 0, s>>>(b);
-  after_launch("copy_left");
-}
-
 void launch_children(const RoundBuffers& b, int depth, int max_depth, cudaStream_t s) {
   k_children<<<sm_count(), 256, 0, s>>>(b, depth, max_depth);
   after_launch("children");
-  k_children_counts<<<1, 1, 0, s>>>(b, depth, max_depth);
-  after_launch("children_counts");
 }
 
 void launch_leaf_values(const RoundBuffers& b, const Scales* scales, SplitParams p, u32* const ridx_sets[2], u64 R,

@@ -101,6 +101,38 @@ __global__ void __launch_bounds__(256) k_quantize_gh(float2* gh, u64 R, int K, c
   }
 }
 
+// grid (blocks, K): block sums of tree k's int32 pairs, one atomic per block.
+__global__ void __launch_bounds__(256) k_gh_totals(const int2* __restrict__ gh, u64 R, i64* __restrict__ totals) {
+  const u32 k = blockIdx.y;
+  const int2* g = gh + u64(k) * R;
+  long long sg = 0, sh = 0;
+  for (u64 i = u64(blockIdx.x) * blockDim.x + threadIdx.x; i < R; i += u64(gridDim.x) * blockDim.x) {
+    const int2 v = g[i];
+    sg += v.x;
+    sh += v.y;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    sg += __shfl_xor_sync(0xffffffffu, sg, o);
+    sh += __shfl_xor_sync(0xffffffffu, sh, o);
+  }
+  __shared__ long long wg[8], wh[8];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (lane == 0) {
+    wg[warp] = sg;
+    wh[warp] = sh;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < 8; ++w) {
+      sg += wg[w];
+      sh += wh[w];
+    }
+    atomicAdd(reinterpret_cast<unsigned long long*>(totals + 2 * k), static_cast<unsigned long long>(sg));
+    atomicAdd(reinterpret_cast<unsigned long long*>(totals + 2 * k + 1), static_cast<unsigned long long>(sh));
+  }
+}
+
 __global__ void k_scales(int K, const u32* gmax, const u32* hmax, Scales* scales) {
   const int k = blockIdx.x * blockDim.x + threadIdx.x;
   if (k < K) {
@@ -180,6 +212,13 @@ void launch_quantize_gh(float2* gh, u64 R, int K, const Scales* scales, cudaStre
   if (!R) return;
   k_quantize_gh<<<grid_for(R * u64(K), 256), 256, 0, s>>>(gh, R, K, scales);
   after_launch("quantize_gh");
+}
+
+void launch_gh_totals(const float2* gh_quantized, u64 R, int K, i64* totals, cudaStream_t s) {
+  if (!R) return;
+  const dim3 grid(grid_for(R, 256), unsigned(K));
+  k_gh_totals<<<grid, 256, 0, s>>>(reinterpret_cast<const int2*>(gh_quantized), R, totals);
+  after_launch("gh_totals");
 }
 
 void launch_leaf_update(const LeafTask* tasks, u32 ntasks, float* margin, u32 K, cudaStream_t s) {

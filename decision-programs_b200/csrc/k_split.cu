@@ -42,7 +42,7 @@ __device__ __forceinline__ Best shfl_best(const Best& v, int src) {
 __device__ __forceinline__ void eval_item(u32 w, const i64* __restrict__ hist, u32 F, const u16* __restrict__ nbins,
                                           const u8* __restrict__ has_missing, const EvalNode* __restrict__ nodes,
                                           const Scales* __restrict__ scales, const SplitParams& p, u32 nchunks,
-                                          SplitCand* __restrict__ cand) {
+                                          SplitCand* __restrict__ cand, u32 fstride, u32 f_base) {
   __shared__ Best wbest[kEvalThreads / 32];
   const u32 node = w / nchunks, chunk = w % nchunks;
   const EvalNode nd = nodes[node];
@@ -57,7 +57,7 @@ __device__ __forceinline__ void eval_item(u32 w, const i64* __restrict__ hist, u
     const int nb = nbins[f];
     if (nb < 2) continue;
     const bool hm = has_missing[f] != 0;
-    const i64* hf = hist + (u64(nd.slot) * F + f) * (2 * kMaxBins);
+    const i64* hf = hist + (u64(nd.slot) * fstride + f) * (2 * kMaxBins);
     const i64 gm = hm ? hf[2 * kMissingBin] : 0, hmq = hm ? hf[2 * kMissingBin + 1] : 0;
     i64 g[8], h[8];
     const longlong2* v = reinterpret_cast<const longlong2*>(hf) + 8 * lane;
@@ -93,7 +93,7 @@ __device__ __forceinline__ void eval_item(u32 w, const i64* __restrict__ hist, u
         const i64 grq = nd.gq - glq, hrq = nd.hq - hlq;
         const double gain = split_gain(double(glq) * isg, double(hlq) * ish, double(grq) * isg,
                                        double(hrq) * ish, sp, p);
-        const Best c{gain, glq, hlq, i32(f), b, d};
+        const Best c{gain, glq, hlq, i32(f_base + f), b, d};
         if (better(c, best)) best = c;
       }
     }
@@ -129,7 +129,7 @@ __global__ void __launch_bounds__(kEvalThreads) k_eval(const i64* __restrict__ h
                                                        const EvalNode* __restrict__ nodes,
                                                        const Scales* __restrict__ scales, SplitParams p, u32 nchunks,
                                                        SplitCand* __restrict__ cand) {
-  eval_item(blockIdx.x, hist, F, nbins, has_missing, nodes, scales, p, nchunks, cand);
+  eval_item(blockIdx.x, hist, F, nbins, has_missing, nodes, scales, p, nchunks, cand, F, 0);
 }
 
 // Node count in device memory: a fixed grid walks the work items.
@@ -139,10 +139,23 @@ __global__ void __launch_bounds__(kEvalThreads) k_eval_dev(const i64* __restrict
                                                            const EvalNode* __restrict__ nodes,
                                                            const Scales* __restrict__ scales, SplitParams p,
                                                            u32 nchunks, const u32* __restrict__ nnodes,
-                                                           SplitCand* __restrict__ cand) {
+                                                           SplitCand* __restrict__ cand, u32 fstride, u32 f_base) {
   const u32 items = *nnodes * nchunks;
   for (u32 w = blockIdx.x; w < items; w += gridDim.x)
-    eval_item(w, hist, F, nbins, has_missing, nodes, scales, p, nchunks, cand);
+    eval_item(w, hist, F, nbins, has_missing, nodes, scales, p, nchunks, cand, fstride, f_base);
+}
+
+__global__ void k_pick_best(const SplitCand* __restrict__ gathered, u64 stride, int nranks,
+                            const u32* __restrict__ nnodes, SplitCand* __restrict__ best) {
+  const u32 n = *nnodes;
+  for (u32 i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    SplitCand b = gathered[i];
+    for (int r = 1; r < nranks; ++r) {
+      const SplitCand x = gathered[u64(r) * stride + i];
+      if (x.gain > b.gain) b = x;
+    }
+    best[i] = b;
+  }
 }
 
 __global__ void k_reduce_cands(const SplitCand* __restrict__ cand, u32 nnodes_host, const u32* __restrict__ nnodes_dev,
@@ -174,16 +187,27 @@ void launch_eval_splits(const i64* hist, u32 F, const u16* nbins, const u8* has_
 
 void launch_eval_splits_dev(const i64* hist, u32 F, const u16* nbins, const u8* has_missing, const EvalNode* nodes,
                             const u32* nnodes_dev, const Scales* scales, SplitParams p, SplitCand* cand,
-                            SplitCand* best, cudaStream_t s) {
+                            SplitCand* best, cudaStream_t s, u32 fstride, u32 f_base) {
   int dev = 0, sms = 148;
   DP_CUDA(cudaGetDevice(&dev));
   DP_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-  const u32 nchunks = (F + kEvalFeatureChunk - 1) / kEvalFeatureChunk;
+  // at least one chunk, so that a node over zero features still gets its
+  // "no candidate" entry
+  const u32 nchunks = F ? (F + kEvalFeatureChunk - 1) / kEvalFeatureChunk : 1;
   k_eval_dev<<<sms * 8, kEvalThreads, 0, s>>>(hist, F, nbins, has_missing, nodes, scales, p, nchunks, nnodes_dev,
-                                               cand);
+                                               cand, fstride ? fstride : F, f_base);
   after_launch("eval_splits");
   k_reduce_cands<<<sms, 128, 0, s>>>(cand, 0, nnodes_dev, nchunks, best);
   after_launch("reduce_splits");
+}
+
+void launch_pick_best(const SplitCand* gathered, u64 stride, int nranks, const u32* nnodes_dev, SplitCand* best,
+                      cudaStream_t s) {
+  int dev = 0, sms = 148;
+  DP_CUDA(cudaGetDevice(&dev));
+  DP_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  k_pick_best<<<sms, 128, 0, s>>>(gathered, stride, nranks, nnodes_dev, best);
+  after_launch("pick_best");
 }
 
 }  // namespace dp

@@ -78,15 +78,31 @@ void launch_scales(int K, const u32* gmax_bits, const u32* hmax_bits, Scales* sc
 // below 2^31.
 // With ntasks_dev set, the task count is read from device memory (ntasks is
 // then ignored) and the grid covers every SM.
+// Output layout (element offsets; a cell is the (g, h) pair of one bin):
+// feature f of slot s lands at (f / fg) * group_stride + s * slot_stride +
+// (f % fg) * 2 * kMaxBins.  The default (layout == nullptr) is fg = F,
+// slot_stride = F * 2 * kMaxBins: hist[slot][F][256][2].  Feature groups of
+// fg features let the sums of each group be contiguous over the built slots
+// (what a reduce-scatter over feature groups needs).
+struct HistLayout {
+  u32 fg;
+  u64 slot_stride;
+  u64 group_stride;
+};
 void launch_histograms(const u8* bins, u64 bin_stride, u32 F, int max_bins, bool quantized_gh,
                        const TreeArrays* trees, const Scales* scales, const HistTask* tasks, u32 ntasks,
-                       u32* counter, i64* hist, cudaStream_t s, const u32* ntasks_dev = nullptr);
+                       u32* counter, i64* hist, cudaStream_t s, const u32* ntasks_dev = nullptr,
+                       const HistLayout* layout = nullptr);
 constexpr u32 kHistFeatureTile = 32;
 // Rows per histogram task for a launch over `total_rows` row-tiles (about
 // four tasks per SM; tasks tasks of one node and tile stay contiguous).
 u64 hist_chunk_rows(u64 total_rows);
 // gh[k][r] (fp32 pairs) -> int32 pairs rint(g * s_g), rint(h * s_h), in place.
 void launch_quantize_gh(float2* gh, u64 R, int K, const Scales* scales, cudaStream_t s);
+// totals[2k], totals[2k+1] += sums of the quantised g and h of tree k (int32
+// pairs from launch_quantize_gh); totals must be zeroed.  Every row falls in
+// exactly one bin of every feature, so these are each root histogram's sums.
+void launch_gh_totals(const float2* gh_quantized, u64 R, int K, i64* totals, cudaStream_t s);
 
 // hist[dst] = parent_hist[par] - hist[src] for each (par, src, dst) slot triple.
 void launch_subtract(i64* hist, const i64* parent_hist, u64 slot_elems, const u32* triples, u32 n, cudaStream_t s);
@@ -101,10 +117,17 @@ void launch_eval_splits(const i64* hist, u32 F, const u16* nbins, const u8* has_
                         u32 nnodes, const Scales* scales, SplitParams p, SplitCand* cand, SplitCand* best,
                         cudaStream_t s);
 constexpr u32 kEvalFeatureChunk = 16;
-// The same with the node count in device memory.
+// The same with the node count in device memory, over F features that sit
+// at a stride of fstride features per slot (0: F) and whose global ids start
+// at f_base (nbins / has_missing point at the first of them).  F may be 0:
+// every node then gets "no candidate" (gain -inf, feature -1).
 void launch_eval_splits_dev(const i64* hist, u32 F, const u16* nbins, const u8* has_missing, const EvalNode* nodes,
                             const u32* nnodes_dev, const Scales* scales, SplitParams p, SplitCand* cand,
-                            SplitCand* best, cudaStream_t s);
+                            SplitCand* best, cudaStream_t s, u32 fstride = 0, u32 f_base = 0);
+// best[i] = the best of gathered[r * stride + i] over r < nranks (rank order
+// is feature order, so on equal gain the lower rank's candidate stays).
+void launch_pick_best(const SplitCand* gathered, u64 stride, int nranks, const u32* nnodes_dev, SplitCand* best,
+                      cudaStream_t s);
 
 // ---- partition ----------------------------------------------------------------
 struct PartTask {

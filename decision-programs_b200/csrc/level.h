@@ -23,7 +23,6 @@ static_assert(sizeof(NodeRec) == 48, "node record layout");
 struct OpenRec {
   u32 tree, id, slot, pad;
   i64 begin, count;        // this rank's positions
-  i64 gcount;              // rows over all ranks
 };
 
 struct LeafRec {
@@ -66,25 +65,30 @@ struct RoundBuffers {
   PartNode* part_nodes;    // [cap_split]
   PartTask* part_tasks;    // [cap_part_tasks]
   u32* cursors;            // [2 * cap_split]
-  i64* gleft;              // [cap_split]
   LeafRec* leaves;         // [cap_leaves]
   LeafTask* leaf_tasks;    // [cap_leaf_tasks]
   RoundCounters* ctr;
   LevelStats* stats;       // [max_depth + 1]
   u32 K, maxn;
+  // Which child of a split is built directly (the other is parent minus it):
+  // the one with fewer rows, or, when rows are sharded (by_hess), the one
+  // with the smaller hessian sum, which every rank knows without an exchange.
+  // Ties go left.  The choice changes no result, only the work.
+  u32 by_hess;
   u64 cap_split, cap_next, cap_hist_tasks, cap_part_tasks, cap_leaves, cap_leaf_tasks;
 };
 
-void launch_round_init(const RoundBuffers& b, u64 R, u64 R_total, cudaStream_t s);
+// Roots of the K trees; their totals come from gh_totals ([K][2], summed over
+// all ranks).
+void launch_round_init(const RoundBuffers& b, u64 R, const i64* gh_totals, cudaStream_t s);
+// Histogram tasks of the build list, and the split-evaluation inputs of every
+// open node.
 void launch_hist_tasks(const RoundBuffers& b, u32 ftiles, int depth, cudaStream_t s);
 // Zeroes max(device n_build, min_slots) histogram slots.
 void launch_zero_slots(const RoundBuffers& b, i64* hist, u64 slot_elems, u64 min_slots, cudaStream_t s);
-void launch_root_totals(const RoundBuffers& b, const i64* hist, u64 slot_elems, cudaStream_t s);
-void launch_make_eval(const RoundBuffers& b, cudaStream_t s);
 // Splits (depth < max_depth, gain > 0) or closes every open node.
 void launch_decide(const RoundBuffers& b, const float* cut, const u8* has_missing, int depth, int max_depth,
                    int set, cudaStream_t s);
-void launch_copy_left(const RoundBuffers& b, cudaStream_t s);
 void launch_children(const RoundBuffers& b, int depth, int max_depth, cudaStream_t s);
 // ridx_sets[s] is the base of the K per-tree row-index arrays of set s
 // (tree k at + k * R).
