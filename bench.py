@@ -348,6 +348,9 @@ def main() -> None:
     b = dp.Booster(PARAMS | {"device": f"cuda:{local}"}, [d])
     if comm is not None:
         b.set_comm(comm)
+    # profiling on from the start, so the warm-up rounds already capture the
+    # round graph with its timing events; enabling again resets the counters
+    b.set_profiling(True)
     for i in range(args.warmup):
         b.update(d, i)
     b.set_profiling(True)

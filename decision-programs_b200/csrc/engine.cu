@@ -19,34 +19,69 @@ cudaEvent_t Profiler::take() {
   DP_CUDA(cudaEventCreate(&e));
   return e;
 }
+void Profiler::record(cudaEvent_t e, cudaStream_t s) {
+  // inside a stream capture an external record becomes an event node of the graph
+  if (capturing_) DP_CUDA(cudaEventRecordWithFlags(e, s, cudaEventRecordExternal));
+  else DP_CUDA(cudaEventRecord(e, s));
+}
 int Profiler::begin(cudaStream_t s, const char* name, double alg_bytes) {
   if (!on_) return -1;
   Pending p{take(), take(), name, alg_bytes};
-  DP_CUDA(cudaEventRecord(p.a, s));
+  record(p.a, s);
   pending_.push_back(p);
   return int(pending_.size()) - 1;
 }
 void Profiler::set_bytes(int idx, double alg_bytes) {
-  if (idx >= 0 && size_t(idx) < pending_.size()) pending_[idx].bytes = alg_bytes;
+  std::vector<Pending>& v = graph_round_ ? graph_pending_ : pending_;
+  if (idx >= 0 && size_t(idx) < v.size()) v[idx].bytes = alg_bytes;
 }
 void Profiler::end(cudaStream_t s) {
   if (!on_) return;
-  DP_CUDA(cudaEventRecord(pending_.back().b, s));
+  record(pending_.back().b, s);
+}
+bool Profiler::accumulate(const Pending& p) {
+  float ms = 0.f;
+  const cudaError_t e = cudaEventElapsedTime(&ms, p.a, p.b);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  auto& st = stats_[p.name];
+  st.launches += 1;
+  st.ms += ms;
+  st.bytes += p.bytes;
+  if (log_.size() >= 4096) log_.erase(log_.begin(), log_.begin() + 2048);
+  log_.push_back(Entry{p.name, ms, p.bytes});
+  return true;
 }
 void Profiler::resolve() {
+  if (graph_round_) {
+    for (const auto& p : graph_pending_)
+      if (!accumulate(p)) graph_timing_failed_ = true;
+    graph_round_ = false;
+  }
   for (auto& p : pending_) {
-    float ms = 0.f;
-    DP_CUDA(cudaEventElapsedTime(&ms, p.a, p.b));
-    auto& st = stats_[p.name];
-    st.launches += 1;
-    st.ms += ms;
-    st.bytes += p.bytes;
-    if (log_.size() >= 4096) log_.erase(log_.begin(), log_.begin() + 2048);
-    log_.push_back(Entry{p.name, ms, p.bytes});
+    if (!accumulate(p)) fail("cudaEventElapsedTime failed on a profiled launch");
     free_.push_back(p.a);
     free_.push_back(p.b);
   }
   pending_.clear();
+}
+void Profiler::abort_capture() {
+  capturing_ = false;
+  for (auto& p : pending_) {
+    free_.push_back(p.a);
+    free_.push_back(p.b);
+  }
+  pending_.clear();
+}
+void Profiler::drop_graph() {
+  for (auto& p : graph_pending_) {
+    free_.push_back(p.a);
+    free_.push_back(p.b);
+  }
+  graph_pending_.clear();
+  graph_round_ = false;
 }
 std::string Profiler::json() const {
   std::ostringstream o;
@@ -75,6 +110,7 @@ std::string Profiler::json() const {
 }
 Profiler::~Profiler() {
   for (auto& p : pending_) { cudaEventDestroy(p.a); cudaEventDestroy(p.b); }
+  for (auto& p : graph_pending_) { cudaEventDestroy(p.a); cudaEventDestroy(p.b); }
   for (auto e : free_) cudaEventDestroy(e);
 }
 
@@ -129,6 +165,7 @@ Engine::Engine(DMatrix& d, const TrainParams& p, Comm* comm) : d_(d), p_(p), com
   // testing knobs: force the exact-count path of deep levels
   async_open_limit_ = env_u64("DP_ASYNC_OPEN_LIMIT", async_open_limit_);
   async_hist_bytes_ = env_u64("DP_ASYNC_HIST_BYTES", async_hist_bytes_);
+  graphs_ = env_u64("DP_CUDA_GRAPHS", 1) != 0;
 
   // every device buffer of the engine in one allocation
   const u64 RK = std::max<u64>(R_, 1) * u64(K_);
@@ -180,6 +217,7 @@ Engine::~Engine() {
   if (stream_) {
     DeviceGuard g(device_);
     cudaStreamSynchronize(stream_);
+    drop_graph();
     cudaStreamDestroy(stream_);
   }
 }
@@ -219,6 +257,8 @@ void Engine::upload(DevBuf<T>& dst, const std::vector<T>& v) {
 template <class T>
 void Engine::grow(DevBuf<T>& b, size_t n) {
   if (n <= b.size()) return;
+  need(!capturing_, "internal error: buffer growth while capturing a round");
+  drop_graph();  // the graph holds the old address
   const auto t0 = std::chrono::steady_clock::now();
   DP_CUDA(cudaStreamSynchronize(stream_));
   b.resize(n);
@@ -228,6 +268,8 @@ void Engine::grow(DevBuf<T>& b, size_t n) {
 template <class T>
 void Engine::grow_keep(DevBuf<T>& b, size_t n) {
   if (n <= b.size()) return;
+  need(!capturing_, "internal error: buffer growth while capturing a round");
+  drop_graph();
   const auto t0 = std::chrono::steady_clock::now();
   DevBuf<T> fresh(n);
   if (b.size()) DP_CUDA(cudaMemcpyAsync(fresh.get(), b.get(), b.size() * sizeof(T), cudaMemcpyDeviceToDevice, stream_));
@@ -344,9 +386,81 @@ std::vector<float> Engine::margins() const {
   return out;
 }
 
+bool Engine::all_levels_async() const {
+  const u64 K = u64(K_), Rt = std::max<u64>(q_->rows_total, 1);
+  const u64 slot_bytes = slot_elems_ * sizeof(i64);
+  u64 open_hi = K;
+  for (int depth = 0; depth < p_.max_depth; ++depth) {
+    if (open_hi > async_open_limit_ || open_hi * slot_bytes > async_hist_bytes_) return false;
+    open_hi = std::min<u64>(2 * open_hi, K * Rt);
+  }
+  return true;
+}
+
+void Engine::drop_graph() {
+  if (graph_exec_) cudaGraphExecDestroy(graph_exec_);
+  if (graph_) cudaGraphDestroy(graph_);
+  graph_exec_ = nullptr;
+  graph_ = nullptr;
+  prof_.drop_graph();
+}
+
 void Engine::boost_round(Model& m) {
   DeviceGuard g(device_);
   const auto t_round = std::chrono::steady_clock::now();
+  // Rounds after the first replay one CUDA graph of the whole round when every
+  // level stays within the asynchronous bounds (nothing then waits on the
+  // host inside a round, and buffers no longer move).
+  const bool graphable = graphs_ && rounds_ >= 1 && all_levels_async();
+  RoundOut out;
+  if (graphable && graph_exec_ && graph_prof_ == prof_.enabled()) {
+    DP_CUDA(cudaGraphLaunch(graph_exec_, stream_));
+    count_launch(graph_launches_);
+    prof_.graph_round();
+    out = graph_out_;
+  } else if (graphable) {
+    drop_graph();
+    const u64 l0 = launch_counter().load();
+    prof_.start_capture();
+    capturing_ = true;
+    bool captured = false;
+    DP_CUDA(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
+    try {
+      out = enqueue_round();
+      captured = cudaStreamEndCapture(stream_, &graph_) == cudaSuccess && graph_ != nullptr;
+    } catch (...) {
+      cudaGraph_t partial = nullptr;
+      cudaStreamEndCapture(stream_, &partial);
+      if (partial) cudaGraphDestroy(partial);
+    }
+    capturing_ = false;
+    const u64 n = launch_counter().load() - l0;
+    launch_counter().fetch_sub(n);  // captured, not run
+    if (captured && cudaGraphInstantiate(&graph_exec_, graph_, 0) == cudaSuccess) {
+      prof_.finish_capture();
+      graph_launches_ = n;
+      graph_prof_ = prof_.enabled();
+      graph_out_ = out;
+      DP_CUDA(cudaGraphLaunch(graph_exec_, stream_));
+      count_launch(graph_launches_);
+      prof_.graph_round();
+    } else {
+      // capture is unavailable here: run this and later rounds directly
+      cudaGetLastError();
+      prof_.abort_capture();
+      drop_graph();
+      graphs_ = false;
+      out = enqueue_round();
+    }
+  } else {
+    out = enqueue_round();
+  }
+  prof_.host("round_enqueue", ms_since(t_round));
+  finish_round(m, out);
+  ++rounds_;
+}
+
+Engine::RoundOut Engine::enqueue_round() {
   const int K = K_;
   const u64 R = R_;
   const u32 F = F_;
@@ -499,9 +613,22 @@ void Engine::boost_round(Model& m) {
   launch_leaf_update_dev(leaf_tasks_.get(), &ctr->n_leaf_tasks, margin_.get(), u32(K), stream_);
   prof_.end(stream_);
 
-  // ---- one read-back of the round
-  const u64 ids_read = std::min<u64>(ids_hi, nodes_.size() / u64(K));
-  prof_.host("round_enqueue", ms_since(t_round));
+  RoundOut out;
+  out.ids_hi = ids_hi;
+  out.pi_hist = std::move(pi_hist);
+  out.pi_sub = std::move(pi_sub);
+  out.pi_eval = std::move(pi_eval);
+  return out;
+}
+
+void Engine::finish_round(Model& m, const RoundOut& out) {
+  const int K = K_;
+  const u32 F = F_;
+  const int D = p_.max_depth;
+  const SplitParams sp = p_.split_params();
+  const u64 slot_bytes = slot_elems_ * sizeof(i64);
+  RoundCounters* const ctr = ctr_.get();
+  const u64 ids_read = std::min<u64>(out.ids_hi, nodes_.size() / u64(K));
   auto t_wait = std::chrono::steady_clock::now();
   DP_CUDA(cudaStreamSynchronize(stream_));
   prof_.host("round_wait", ms_since(t_wait));
@@ -520,12 +647,17 @@ void Engine::boost_round(Model& m) {
   if (ovf) fail("internal error: a per-round work list overflowed (flags " + std::to_string(ovf) + ")");
   for (int d = 0; d < D; ++d) {
     const LevelStats& st = st_h[d];
-    prof_.set_bytes(pi_hist[d], double(st.rows_built) * (double(F) + 12.0) +
-                                    double(st.n_build) * double(F) * kMaxBins * 16.0);
-    prof_.set_bytes(pi_sub[d], double(st.n_build) * slot_bytes * 3.0);
-    prof_.set_bytes(pi_eval[d], double(st.n_open) * slot_bytes);
+    prof_.set_bytes(out.pi_hist[d], double(st.rows_built) * (double(F) + 12.0) +
+                                        double(st.n_build) * double(F) * kMaxBins * 16.0);
+    prof_.set_bytes(out.pi_sub[d], double(st.n_build) * slot_bytes * 3.0);
+    prof_.set_bytes(out.pi_eval[d], double(st.n_open) * slot_bytes);
   }
   prof_.resolve();
+  if (prof_.graph_timing_failed()) {
+    // this driver does not time graph event nodes: profiled rounds run directly
+    graphs_ = false;
+    drop_graph();
+  }
 
   for (int k = 0; k < K; ++k) {
     const u64 n = nid_h[k];

@@ -27,6 +27,19 @@ class Profiler {
   bool enabled() const { return on_; }
   // Returns the launch's index for set_bytes (-1 when disabled).
   int begin(cudaStream_t s, const char* name, double alg_bytes);
+  // Graph capture: launches timed between start_capture and finish_capture
+  // are recorded as event nodes of the graph and kept; graph_round() marks
+  // the current round as a replay whose times resolve() reads from them.
+  void start_capture() { capturing_ = true; }
+  void finish_capture() {
+    capturing_ = false;
+    graph_pending_ = std::move(pending_);
+    pending_.clear();
+  }
+  void abort_capture();
+  void drop_graph();
+  void graph_round() { graph_round_ = true; }
+  bool graph_timing_failed() const { return graph_timing_failed_; }
   // Algorithmic bytes of a launch known only after it ran (before resolve()).
   void set_bytes(int idx, double alg_bytes);
   void end(cudaStream_t s);
@@ -45,7 +58,11 @@ class Profiler {
   struct Pending { cudaEvent_t a, b; std::string name; double bytes; };
   struct Stat { u64 launches = 0; double ms = 0.0; double bytes = 0.0; };
   bool on_ = false;
+  bool capturing_ = false, graph_round_ = false, graph_timing_failed_ = false;
+  void record(cudaEvent_t e, cudaStream_t s);
+  bool accumulate(const Pending& p);
   std::vector<Pending> pending_;
+  std::vector<Pending> graph_pending_;
   std::vector<cudaEvent_t> free_;
   std::map<std::string, Stat> stats_;
   struct Entry { std::string name; float ms; double bytes; };
@@ -63,7 +80,10 @@ class Engine {
 
   void boost_round(Model& m);
   // Regularisation / depth / learning-rate changes between rounds.
-  void update_params(const TrainParams& p) { p_ = p; }
+  void update_params(const TrainParams& p) {
+    p_ = p;
+    drop_graph();  // parameters are baked into the captured launches
+  }
   DMatrix* matrix() const { return &d_; }
   Profiler& profiler() { return prof_; }
   cudaStream_t stream() const { return stream_; }
@@ -85,6 +105,15 @@ class Engine {
   template <class T>
   void grow_keep(DevBuf<T>& b, size_t n);
   RoundBuffers round_buffers(int depth, u64 cap_split, u64 cap_next) const;
+  // What the host needs after a round's work is enqueued.
+  struct RoundOut {
+    u64 ids_hi = 1;                             // bound on node ids per tree
+    std::vector<int> pi_hist, pi_sub, pi_eval;  // profiler entries per level
+  };
+  RoundOut enqueue_round();                       // every launch of one round
+  void finish_round(Model& m, const RoundOut& out);  // one read-back, the trees
+  bool all_levels_async() const;
+  void drop_graph();
   // Sizes every round buffer for the levels whose bounds stay within the
   // asynchronous limits, so steady rounds allocate nothing.
   void presize(SlabPlan& plan);
@@ -136,6 +165,15 @@ class Engine {
   DevBuf<LevelStats> stats_;
   DevBuf<u32> scratch_;  // [0]: label check flag; [1, 1 + K): initial margins (f32 bits)
   int sms_ = 148;
+  // CUDA graph of a whole round (replayed while the bounds and buffers hold)
+  bool graphs_ = true;  // DP_CUDA_GRAPHS=0 turns capture off
+  bool capturing_ = false;
+  cudaGraph_t graph_ = nullptr;
+  cudaGraphExec_t graph_exec_ = nullptr;
+  bool graph_prof_ = false;
+  u64 graph_launches_ = 0;
+  RoundOut graph_out_;
+  u64 rounds_ = 0;
   // A level whose open-node bound exceeds either limit first reads the exact
   // counts back (one small copy) and sizes its buffers by them.
   u64 async_open_limit_ = u64(1) << 16;

@@ -126,6 +126,28 @@ def test_deep_trees_device_resident_levels(dp, orc):
     run(dp, orc, x, y, "binary:logistic", 2, max_depth=14, min_child_weight=0.0, reg_lambda=0.1)
 
 
+@pytest.mark.parametrize("graphs", ["0", "1"])
+def test_direct_and_graph_rounds_agree(dp, orc, monkeypatch, graphs):
+    """Rounds after the first replay a captured CUDA graph; with capture off
+    (DP_CUDA_GRAPHS=0) every round is launched directly.  Both grow the
+    oracle's trees, with the profiler on for part of the rounds."""
+    monkeypatch.setenv("DP_CUDA_GRAPHS", graphs)
+    x, y = c1_data(12000, seed=13)
+    params = {"objective": "binary:logistic", "tree_method": "hist", "device": "cuda:0", "max_depth": 6,
+              "max_bin": 256, "eta": 0.3}
+    d = dp.DMatrix.from_torch(cuda(x), cuda(y))
+    b = dp.Booster(params, [d])
+    for i in range(6):
+        if i == 3:
+            b.set_profiling(True)
+        b.update(d, i)
+    prof = b.profile()
+    assert prof["histograms"]["launches"] == 3 * 6 and prof["histograms"]["ms"] > 0
+    o = orc.Model(x, y, "binary:logistic", max_depth=6, max_bin=256, eta=0.3, rounds=6, threads=8)
+    compare_models(b, o, 1)
+    np.testing.assert_array_equal(b.margins(len(y), 1).view(np.uint32), o.margins().view(np.uint32))
+
+
 @pytest.mark.parametrize("R", [1, 2, 7, 33])
 def test_tiny_inputs(dp, orc, R):
     rng = np.random.default_rng(R)
