@@ -350,6 +350,8 @@ RoundBuffers Engine::round_buffers(int depth, u64 cap_split, u64 cap_next) const
   b.hist_tasks = hist_tasks_.get();
   b.eval_nodes = eval_nodes_.get();
   b.best = best_.get();
+  b.gathered = gathered_.get();
+  b.nranks = u32(G_);
   b.split_idx = split_idx_.get();
   b.part_nodes = part_nodes_.get();
   b.part_tasks = part_tasks_.get();
@@ -583,7 +585,6 @@ Engine::RoundOut Engine::enqueue_round() {
       prof_.begin(stream_, "exchange_cands", double(open_hi * u64(G_)) * sizeof(SplitCand));
       comm_->all_gather_bytes(best_local_.get(), gathered_.get(), open_hi * sizeof(SplitCand), stream_);
       prof_.end(stream_);
-      launch_pick_best(gathered_.get(), open_hi, G_, &ctr->n_open, best_.get(), stream_);
     }
     launch_decide(rb, q_->cut.get(), q_->has_missing.get(), depth, D, set, stream_);
 

@@ -95,17 +95,33 @@ __global__ void __launch_bounds__(THREADS) k_hist(HistArgs a) {
 #pragma unroll
   for (int j = 0; j < 16; ++j) colj[j] = h16 + ((s + u32(j)) & 15u);
   u32 key_slot = kNoRow, key_f0 = 0, key_tree = 0;  // current accumulation target (block-uniform)
+  bool key_excl = false;  // the key's task is the only one writing its (slot, tile)
   u32 in_window = 0;                                // rows in the u32 planes since the last fold
   const u32 ntasks = a.ntasks_dev ? *a.ntasks_dev : a.ntasks;
 
+  // Moves the window sums into the int64 planes (transposed to [feature][bin])
+  // and clears the window.  The first fold of a key copies (the planes hold
+  // the previous key's drained values), later folds add.
+  bool w_clean = true;  // block-uniform
   auto fold = [&]() {
-    for (int i = threadIdx.x; i < kCells; i += THREADS) {
-      const int b = i / kFT, f = i % kFT;
-      Wg[f * kWRow + b] += static_cast<long long>(static_cast<int>(Lg[i]));
-      Wh[f * kWRow + b] += static_cast<long long>(Lh[i]);
-      Lg[i] = 0u;
-      Lh[i] = 0u;
+    if (w_clean) {
+      for (int i = threadIdx.x; i < kCells; i += THREADS) {
+        const int b = i / kFT, f = i % kFT;
+        Wg[f * kWRow + b] = static_cast<long long>(static_cast<int>(Lg[i]));
+        Wh[f * kWRow + b] = static_cast<long long>(Lh[i]);
+        Lg[i] = 0u;
+        Lh[i] = 0u;
+      }
+    } else {
+      for (int i = threadIdx.x; i < kCells; i += THREADS) {
+        const int b = i / kFT, f = i % kFT;
+        Wg[f * kWRow + b] += static_cast<long long>(static_cast<int>(Lg[i]));
+        Wh[f * kWRow + b] += static_cast<long long>(Lh[i]);
+        Lg[i] = 0u;
+        Lh[i] = 0u;
+      }
     }
+    w_clean = false;
   };
 
   for (;;) {
@@ -119,22 +135,26 @@ __global__ void __launch_bounds__(THREADS) k_hist(HistArgs a) {
     if (!same && key_slot != kNoRow) {
       fold();
       __syncthreads();
-      // consecutive threads take consecutive bins of one feature: the global
-      // atomics of a warp cover one contiguous 512-byte run
+      // consecutive threads take consecutive bins of one feature: a warp
+      // covers one contiguous 512-byte run.  A task that alone covers its
+      // (slot, tile) stores every cell (16-byte stores, no read of the line);
+      // otherwise non-zero cells are added with 64-bit reductions.
       i64* out = a.hist + u64(key_slot) * a.layout.slot_stride;
       for (int idx = threadIdx.x; idx < kCells; idx += THREADS) {
         const int f = idx / MB, b = idx % MB;
         const long long gs = Wg[f * kWRow + b], hs = Wh[f * kWRow + b];
-        Wg[f * kWRow + b] = 0;
-        Wh[f * kWRow + b] = 0;
         const u32 gf = key_f0 + u32(f);
-        if (!(gs | hs) || gf >= a.F) continue;
+        if (gf >= a.F) continue;
         const u32 grp = gf / a.layout.fg, fl = gf - grp * a.layout.fg;
-        unsigned long long* cell = reinterpret_cast<unsigned long long*>(
-            out + grp * a.layout.group_stride + (u64(fl) * kMaxBins + b) * 2);
-        atomicAdd(cell, static_cast<unsigned long long>(gs));
-        atomicAdd(cell + 1, static_cast<unsigned long long>(hs));
+        i64* cell = out + grp * a.layout.group_stride + (u64(fl) * kMaxBins + b) * 2;
+        if (key_excl) {
+          *reinterpret_cast<longlong2*>(cell) = make_longlong2(gs, hs);
+        } else if (gs | hs) {
+          atomicAdd(reinterpret_cast<unsigned long long*>(cell), static_cast<unsigned long long>(gs));
+          atomicAdd(reinterpret_cast<unsigned long long*>(cell) + 1, static_cast<unsigned long long>(hs));
+        }
       }
+      w_clean = true;
       key_slot = kNoRow;
       in_window = 0;
     }
@@ -143,6 +163,7 @@ __global__ void __launch_bounds__(THREADS) k_hist(HistArgs a) {
     key_slot = t.slot;
     key_f0 = t.f0;
     key_tree = t.tree;
+    key_excl = t.excl != 0;
     const TreeArrays ta = a.trees[t.tree];
     Scales sc{1.f, 1.f};
     if (!QUANT) sc = a.scales[t.tree];

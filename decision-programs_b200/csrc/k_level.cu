@@ -119,7 +119,8 @@ __global__ void __launch_bounds__(kBook) k_hist_tasks(RoundBuffers b, u32 ftiles
       const u32 ft = u32(q % ftiles);
       const i64 beg = beg0 + p * piece < end0 ? beg0 + p * piece : end0;
       const i64 end = beg + piece < end0 ? beg + piece : end0;
-      b.hist_tasks[t] = HistTask{s_slot[j], ft * kHistFeatureTile, s_tree[j], 0u, beg, end};
+      // a node covered by one row range is the only writer of its tiles
+      b.hist_tasks[t] = HistTask{s_slot[j], ft * kHistFeatureTile, s_tree[j], np == 1 ? 1u : 0u, beg, end};
     });
   }
   // split-evaluation inputs of the open nodes
@@ -165,7 +166,17 @@ __global__ void __launch_bounds__(kBook) k_decide(RoundBuffers b, const float* _
     bs.feature = -1;
     if (valid) {
       o = b.open_cur[i];
-      if (depth < max_depth) bs = b.best[i];
+      if (depth < max_depth) {
+        if (b.nranks > 1) {
+          bs = b.gathered[i];
+          for (u32 r = 1; r < b.nranks; ++r) {
+            const SplitCand x = b.gathered[u64(r) * b.cap_split + i];
+            if (x.gain > bs.gain) bs = x;
+          }
+        } else {
+          bs = b.best[i];
+        }
+      }
     }
     const bool split = valid && depth < max_depth && bs.feature >= 0 && bs.gain > 0.0;
     const bool leaf = valid && !split;

@@ -145,19 +145,6 @@ __global__ void __launch_bounds__(kEvalThreads) k_eval_dev(const i64* __restrict
     eval_item(w, hist, F, nbins, has_missing, nodes, scales, p, nchunks, cand, fstride, f_base);
 }
 
-__global__ void k_pick_best(const SplitCand* __restrict__ gathered, u64 stride, int nranks,
-                            const u32* __restrict__ nnodes, SplitCand* __restrict__ best) {
-  const u32 n = *nnodes;
-  for (u32 i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
-    SplitCand b = gathered[i];
-    for (int r = 1; r < nranks; ++r) {
-      const SplitCand x = gathered[u64(r) * stride + i];
-      if (x.gain > b.gain) b = x;
-    }
-    best[i] = b;
-  }
-}
-
 __global__ void k_reduce_cands(const SplitCand* __restrict__ cand, u32 nnodes_host, const u32* __restrict__ nnodes_dev,
                                u32 nchunks, SplitCand* __restrict__ best) {
   const u32 nnodes = nnodes_dev ? *nnodes_dev : nnodes_host;
@@ -194,20 +181,14 @@ void launch_eval_splits_dev(const i64* hist, u32 F, const u16* nbins, const u8* 
   // at least one chunk, so that a node over zero features still gets its
   // "no candidate" entry
   const u32 nchunks = F ? (F + kEvalFeatureChunk - 1) / kEvalFeatureChunk : 1;
+  // with one feature chunk the chunk candidate is the node's best
   k_eval_dev<<<sms * 8, kEvalThreads, 0, s>>>(hist, F, nbins, has_missing, nodes, scales, p, nchunks, nnodes_dev,
-                                               cand, fstride ? fstride : F, f_base);
+                                               nchunks == 1 ? best : cand, fstride ? fstride : F, f_base);
   after_launch("eval_splits");
-  k_reduce_cands<<<sms, 128, 0, s>>>(cand, 0, nnodes_dev, nchunks, best);
-  after_launch("reduce_splits");
-}
-
-void launch_pick_best(const SplitCand* gathered, u64 stride, int nranks, const u32* nnodes_dev, SplitCand* best,
-                      cudaStream_t s) {
-  int dev = 0, sms = 148;
-  DP_CUDA(cudaGetDevice(&dev));
-  DP_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-  k_pick_best<<<sms, 128, 0, s>>>(gathered, stride, nranks, nnodes_dev, best);
-  after_launch("pick_best");
+  if (nchunks > 1) {
+    k_reduce_cands<<<sms, 128, 0, s>>>(cand, 0, nnodes_dev, nchunks, best);
+    after_launch("reduce_splits");
+  }
 }
 
 }  // namespace dp

@@ -18,7 +18,7 @@ struct HistTask {
   u32 slot;
   u32 f0;
   u32 tree;   // selects the (g,h) / row-index arrays of this tree
-  u32 pad;
+  u32 excl;   // 1: no other task covers this (slot, tile); its sums are stored, not added
   i64 begin;
   i64 end;
 };
@@ -124,10 +124,6 @@ constexpr u32 kEvalFeatureChunk = 16;
 void launch_eval_splits_dev(const i64* hist, u32 F, const u16* nbins, const u8* has_missing, const EvalNode* nodes,
                             const u32* nnodes_dev, const Scales* scales, SplitParams p, SplitCand* cand,
                             SplitCand* best, cudaStream_t s, u32 fstride = 0, u32 f_base = 0);
-// best[i] = the best of gathered[r * stride + i] over r < nranks (rank order
-// is feature order, so on equal gain the lower rank's candidate stays).
-void launch_pick_best(const SplitCand* gathered, u64 stride, int nranks, const u32* nnodes_dev, SplitCand* best,
-                      cudaStream_t s);
 
 // ---- partition ----------------------------------------------------------------
 struct PartTask {

@@ -61,6 +61,11 @@ struct RoundBuffers {
   HistTask* hist_tasks;    // [cap_hist_tasks]
   EvalNode* eval_nodes;    // [cap_split]
   SplitCand* best;         // [cap_split]
+  // With several ranks: every rank's best per open node, [nranks][cap_split];
+  // the decision takes the best over ranks in rank order (rank order is
+  // feature order, so on equal gain the lower feature stays).
+  const SplitCand* gathered;
+  u32 nranks;
   u32* split_idx;          // [cap_split]
   PartNode* part_nodes;    // [cap_split]
   PartTask* part_tasks;    // [cap_part_tasks]
