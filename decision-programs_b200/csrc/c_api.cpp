@@ -321,6 +321,40 @@ int XGBoosterSlice(BoosterHandle handle, int begin_layer, int end_layer, int ste
   DP_API_END();
 }
 
+int XGBoosterPredictFromCudaArray(BoosterHandle handle, const char* values, const char* config, DMatrixHandle m,
+                                  const bst_ulong** out_shape, bst_ulong* out_dim, const float** out_result) {
+  DP_API_BEGIN();
+  (void)m;  // the proxy DMatrix of XGBoost's inplace prediction carries nothing needed here
+  dp::Booster* b = as_booster(handle);
+  need(out_shape && out_dim && out_result, "output pointers are null");
+  need(config != nullptr, "prediction config is null");
+  const DenseSpec spec = dense_spec(values, config);
+  const dp::json::Value c = dp::json::parse(config);
+  dp::Booster::PredictRequest q;
+  q.x = spec.ptr;
+  q.rows = spec.rows;
+  q.cols = spec.cols;
+  q.stride = spec.stride;
+  q.has_mv = spec.has_mv;
+  q.mv = spec.mv;
+  if (const auto* v = c.find("type")) q.type = int(v->as_int());
+  if (const auto* v = c.find("iteration_begin")) q.it_begin = int(v->as_int());
+  if (const auto* v = c.find("iteration_end")) q.it_end = int(v->as_int());
+  if (const auto* v = c.find("strict_shape")) q.strict_shape = v->as_bool();
+  q.device = q.rows ? pointer_device(spec.ptr, false) : 0;
+  {
+    dp::DeviceGuard g(q.device);
+    // the producer may still be writing on its own stream
+    dp::cuda_check(cudaDeviceSynchronize(), "synchronise producer");
+  }
+  const dp::u64* shape = nullptr;
+  dp::u64 dims = 0;
+  *out_result = b->predict(q, &shape, &dims);
+  *out_shape = reinterpret_cast<const bst_ulong*>(shape);
+  *out_dim = bst_ulong(dims);
+  DP_API_END();
+}
+
 int XGBoosterGetNumFeature(BoosterHandle handle, bst_ulong* out) {
   DP_API_BEGIN();
   *out = bst_ulong(as_booster(handle)->model.num_feature);

@@ -26,6 +26,7 @@ EXPORTED = [
     "XGDMatrixFree", "XGBoosterCreate", "XGBoosterFree", "XGBoosterSetParam", "XGBoosterUpdateOneIter",
     "XGBoosterBoostedRounds", "XGBoosterSaveJsonConfig", "XGBoosterSaveModel", "XGBoosterSaveModelToBuffer",
     "XGBoosterLoadModelFromBuffer", "XGBoosterLoadModel", "XGBoosterSlice", "XGBoosterGetNumFeature",
+    "XGBoosterPredictFromCudaArray",
     "dp_comm_unique_id", "dp_comm_create", "dp_comm_free", "dp_booster_set_comm", "dp_booster_set_profiling",
     "dp_booster_profile", "dp_booster_margins", "dp_launch_count", "dp_quantile_cuts", "dp_bin_matrix",
     "dp_gradients", "dp_hist_build", "dp_hist_build_noalloc", "dp_quantize_gh", "dp_hist_prepare", "dp_hist_run", "dp_hist_free", "dp_eval_splits",
@@ -72,6 +73,8 @@ def lib() -> C.CDLL:
         L.XGBoosterLoadModel.argtypes = [P, C.c_char_p]
         L.XGBoosterSlice.argtypes = [P, i32, i32, i32, C.POINTER(P)]
         L.XGBoosterGetNumFeature.argtypes = [P, C.POINTER(u64)]
+        L.XGBoosterPredictFromCudaArray.argtypes = [P, C.c_char_p, C.c_char_p, P, C.POINTER(C.POINTER(u64)),
+                                                    C.POINTER(u64), C.POINTER(C.POINTER(f32))]
         L.dp_comm_unique_id.argtypes = [P]
         L.dp_comm_create.argtypes = [P, i32, i32, i32, C.POINTER(P)]
         L.dp_comm_free.argtypes = [P]
@@ -273,6 +276,38 @@ class Booster:
         p = C.c_char_p()
         check(lib().dp_booster_profile(self.handle, C.byref(p)))
         return json.loads(p.value.decode())
+
+    def predict(self, x, margin: bool = False, iteration_begin: int = 0, iteration_end: int = 0,
+                strict_shape: bool = True, missing: float = math.nan):
+        """XGBoosterPredictFromCudaArray over a CUDA float32 tensor [R, F]
+        (row stride allowed).  Returns a new CUDA tensor holding a copy of the
+        booster-owned output, shaped as the call reports it."""
+        import torch
+        assert x.is_cuda and x.dtype == torch.float32 and x.dim() == 2 and x.stride(1) == 1
+        strides = None if x.stride(0) == x.shape[1] else [int(x.stride(0)) * 4, 4]
+        cfg = {"type": 1 if margin else 0, "training": False, "iteration_begin": iteration_begin,
+               "iteration_end": iteration_end, "strict_shape": strict_shape, "cache_id": 0}
+        text = json.dumps(cfg, separators=(",", ":"))[:-1] + (',"missing":NaN}' if math.isnan(missing)
+                                                               else f',"missing":{missing!r}}}')
+        shape = C.POINTER(C.c_uint64)()
+        dims = C.c_uint64()
+        out = C.POINTER(C.c_float)()
+        check(lib().XGBoosterPredictFromCudaArray(self.handle, array_interface(x.data_ptr(), list(x.shape),
+                                                                               strides=strides).encode(),
+                                                  text.encode(), None, C.byref(shape), C.byref(dims),
+                                                  C.byref(out)))
+        dims_t = tuple(shape[i] for i in range(dims.value))
+        n = 1
+        for d in dims_t:
+            n *= d
+        res = torch.empty(dims_t, dtype=torch.float32, device=x.device)
+        if n:
+            from cuda.bindings import runtime as rt
+            err, = rt.cudaMemcpy(res.data_ptr(), C.cast(out, C.c_void_p).value, n * 4,
+                                 rt.cudaMemcpyKind.cudaMemcpyDeviceToDevice)
+            if err != rt.cudaError_t.cudaSuccess:
+                raise DPError(f"copy of the prediction failed: {err}")
+        return res
 
     def margins(self, rows: int, outputs: int):
         import numpy as np

@@ -113,6 +113,22 @@ DP_API int XGBoosterSlice(BoosterHandle handle, int begin_layer, int end_layer, 
 /* native/class_model_convert.cpp:112. */
 DP_API int XGBoosterGetNumFeature(BoosterHandle handle, bst_ulong* out);
 
+/* Prediction over a dense fp32 CUDA matrix (array interface as for
+ * XGDMatrixCreateFromCudaArrayInterface).  config: {"type":0|1,
+ * "training":false,"iteration_begin":b,"iteration_end":e (0 = all rounds),
+ * "strict_shape":true|false,"cache_id":0,"missing":NaN|value}.  type 0 is the
+ * objective's output (squared error: the margin; logistic: probability;
+ * multi:softprob: K probabilities; multi:softmax: the class index as float),
+ * type 1 the raw margins [R][K].  *out_result is a device pointer on the
+ * input's device, owned by the booster until the next call on it; out_shape
+ * is [R, width] with strict_shape (width K for margins and probabilities,
+ * else 1), else [R] when width is 1.  The proxy handle m may be null.
+ * Replaces native/class_study_train.cu:158 and
+ * native/class_model_native_adapter.cuh:30. */
+DP_API int XGBoosterPredictFromCudaArray(BoosterHandle handle, const char* values, const char* config,
+                                         DMatrixHandle m, const bst_ulong** out_shape, bst_ulong* out_dim,
+                                         const float** out_result);
+
 /* ---- extensions (no counterpart in the reference, which is single-GPU) --- */
 
 /* Multi-GPU: rank 0 creates a 128-byte NCCL unique id, every rank creates a

@@ -700,6 +700,56 @@ void train_rounds(Model& m, int rounds) {
   }
 }
 
+// Prediction with the trained ensemble.  Routing restates the reference's
+// runtime: x < split_condition goes left and a missing value follows
+// default_left (native/class_tree_runtime_compare.cu:47,
+// native/class_runtime.cu:128); a leaf carries its value in split_conditions
+// (native/class_io.hpp:187-201).  Margins add the leaves of rounds
+// [it_begin, it_end) to the base margin in tree order, in float, as training
+// does; the transforms use the gradients' arithmetic (double, dp_exp, rounded
+// to float).  type 1: margins [R][K]; type 0: squared error -> margin,
+// logistic -> probability, softprob -> K probabilities, softmax -> class index.
+void predict(const Model& m, const float* x, uint64_t R, uint64_t stride, int type, int it_begin, int it_end,
+             int has_mv, float mv, float* out) {
+  const int K = m.p.K;
+  const size_t t0 = size_t(it_begin) * K, t1 = size_t(it_end) * K;
+  std::vector<float> mg(static_cast<size_t>(K));
+  std::vector<double> p(static_cast<size_t>(K));
+  for (uint64_t r = 0; r < R; ++r) {
+    const float* xr = x + r * stride;
+    for (int k = 0; k < K; ++k) mg[k] = m.p.base_margin;
+    for (size_t t = t0; t < t1 && t < m.trees.size(); ++t) {
+      const Tree& tr = m.trees[t];
+      const int k = int(t % size_t(K));
+      int id = 0;
+      while (tr.left[id] >= 0) {
+        const float v = xr[tr.feature[id]];
+        const bool miss = std::isnan(v) || (has_mv && v == mv);
+        id = miss ? (tr.default_left[id] ? tr.left[id] : tr.right[id]) : (v < tr.cond[id] ? tr.left[id] : tr.right[id]);
+      }
+      mg[k] = mg[k] + tr.cond[id];
+    }
+    if (type == 1) {
+      for (int k = 0; k < K; ++k) out[r * K + k] = mg[k];
+    } else if (m.p.objective == kSquaredError) {
+      out[r] = mg[0];
+    } else if (m.p.objective == kLogistic) {
+      out[r] = float(1.0 / (1.0 + dp_exp(-double(mg[0]))));
+    } else if (m.p.objective == kSoftprob) {
+      double mx = mg[0];
+      for (int k = 1; k < K; ++k) mx = std::max(mx, double(mg[k]));
+      double sum = 0.0;
+      for (int k = 0; k < K; ++k) { p[k] = dp_exp(double(mg[k]) - mx); sum = sum + p[k]; }
+      for (int k = 0; k < K; ++k) out[r * K + k] = float(p[k] / sum);
+    } else {
+      int best = 0;
+      for (int k = 1; k < K; ++k)
+        if (mg[k] > mg[best]) best = k;
+      out[r] = float(best);
+    }
+  }
+}
+
 }  // namespace orc
 
 // ---------------------------------------------------------------------------
@@ -865,6 +915,21 @@ int orc_tree(void* h, int t, int32_t* left, int32_t* right, int32_t* feature, fl
   std::memcpy(sum_hess, tr.sum_hess.data(), n * 4);
   std::memcpy(bin, tr.bin.data(), n * 4);
   return 0;
+}
+
+int orc_predict(void* h, const float* x, uint64_t R, uint64_t stride, int type, int it_begin, int it_end,
+                int has_mv, float mv, float* out) {
+  try {
+    const orc::Model& m = *static_cast<orc::Model*>(h);
+    const int rounds = int(m.trees.size()) / m.p.K;
+    if (it_end == 0) it_end = rounds;
+    if (it_begin < 0 || it_begin > it_end || it_end > rounds) throw std::runtime_error("iteration range");
+    orc::predict(m, x, R, stride, type, it_begin, it_end, has_mv, mv, out);
+    return 0;
+  } catch (const std::exception& e) {
+    orc::last_error = e.what();
+    return -1;
+  }
 }
 
 void orc_margins(void* h, float* out) {

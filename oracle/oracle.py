@@ -55,6 +55,7 @@ def lib() -> C.CDLL:
         L.orc_tree_size.argtypes = [P, i32]
         L.orc_tree.argtypes = [P, i32] + [P] * 9
         L.orc_margins.argtypes = [P, P]
+        L.orc_predict.argtypes = [P, P, u64, u64, i32, i32, i32, i32, C.c_float, P]
         L.orc_scales.argtypes = [P, P]
         L.orc_model_cuts.argtypes = [P, P, P, P]
         L.orc_last_error.restype = C.c_char_p
@@ -230,6 +231,22 @@ class Model:
         keys = ["left_children", "right_children", "split_indices", "split_conditions", "default_left",
                 "base_weights", "loss_changes", "sum_hessian", "split_bins"]
         lib().orc_tree(self.h, t, *[_p(out[k]) for k in keys])
+        return out
+
+    def predict(self, x: np.ndarray, margin: bool = False, iteration_begin: int = 0, iteration_end: int = 0,
+                missing: float = float("nan"), objective: str = None) -> np.ndarray:
+        """Predictions of the trained ensemble: margins [R, K] (margin=True) or
+        the objective's output ([R, K] probabilities for softprob, else [R])."""
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        R = x.shape[0]
+        softprob = objective == "multi:softprob"
+        width = self.K if (margin or softprob) else 1
+        out = np.zeros((R, width), np.float32)
+        has_mv = not np.isnan(missing)
+        rc = lib().orc_predict(self.h, _p(x), R, x.shape[1], 1 if margin else 0, iteration_begin, iteration_end,
+                               int(has_mv), C.c_float(0.0 if not has_mv else missing), _p(out))
+        if rc != 0:
+            raise RuntimeError(lib().orc_last_error().decode())
         return out
 
     def margins(self) -> np.ndarray:
