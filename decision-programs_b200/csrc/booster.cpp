@@ -15,9 +15,6 @@ void Booster::update_one_iter(int iter, DMatrix* d) {
   const int K = params.K();
   need(K >= 1, "num_class must be at least 1 for multi-class objectives");
   if (params.objective.rfind("multi:", 0) == 0) need(params.num_class >= 2, "num_class must be at least 2");
-  need(params.subsample == 1.0 && params.colsample_bytree == 1.0 && params.colsample_bylevel == 1.0 &&
-           params.colsample_bynode == 1.0,
-       "row and column sampling (subsample / colsample_* below 1) are not implemented by this library");
   if (params.device >= 0) need(params.device == d->device(), "booster device differs from the matrix device");
   if (params.device < 0) params.device = d->device();
   const bool shape_changed = engine_ && (engine_->matrix() != d || engine_objective_ != params.objective ||

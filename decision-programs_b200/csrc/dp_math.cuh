@@ -100,4 +100,34 @@ DP_HD float leaf_weight(std::int64_t gq, std::int64_t hq, float sg, float sh, co
   return float(w * p.eta);
 }
 
+// ---- sampling (subsample, colsample_*) -------------------------------------
+// Counter-based random numbers, identical on the host and the device: the
+// output function of SplitMix64 (Steele, Lea and Flood, "Fast splittable
+// pseudorandom number generators", OOPSLA 2014) applied to a chain of key
+// words (seed, round, kind and class, then two indices).
+DP_HD std::uint64_t mix64(std::uint64_t z) {
+  z ^= z >> 30;
+  z *= 0xbf58476d1ce4e5b9ULL;
+  z ^= z >> 27;
+  z *= 0x94d049bb133111ebULL;
+  z ^= z >> 31;
+  return z;
+}
+enum SampleKind : std::uint32_t { kSampleRow = 1, kSampleTree = 2, kSampleLevel = 3, kSampleNode = 4 };
+DP_HD std::uint64_t sample_hash(std::int64_t seed, std::uint32_t round, std::uint32_t klass, std::uint32_t kind,
+                                std::uint64_t a, std::uint64_t b) {
+  std::uint64_t h = mix64(std::uint64_t(seed) + 0x9e3779b97f4a7c15ULL);
+  h = mix64(h ^ std::uint64_t(round));
+  h = mix64(h ^ ((std::uint64_t(kind) << 32) | std::uint64_t(klass)));
+  h = mix64(h ^ a);
+  return mix64(h ^ b);
+}
+// Uniform in [0, 1) from the top 53 bits.
+DP_HD double sample_uniform(std::uint64_t h) { return double(h >> 11) * (1.0 / 9007199254740992.0); }
+// Features kept from n candidates at fraction c: max(1, floor(c n)), at most n.
+DP_HD std::uint32_t sample_count(double c, std::uint32_t n) {
+  const std::uint32_t k = std::uint32_t(c * double(n));
+  return n == 0 ? 0u : (k < 1u ? 1u : (k > n ? n : k));
+}
+
 }  // namespace dp

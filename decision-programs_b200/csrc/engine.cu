@@ -181,10 +181,23 @@ Engine::Engine(DMatrix& d, const TrainParams& p, Comm* comm) : d_(d), p_(p), com
   plan.want(hist_counter_, 1);
   plan.want(scratch_, 1 + size_t(K_));
   plan.want(gh_totals_, 2 * size_t(K_));
+  plan.want(round_dev_, 1);
+  mask_words_ = (F_ + 31) / 32;
   presize(plan);
   const auto t_alloc = std::chrono::steady_clock::now();
   plan.commit(slabs_);
   prof_.host("engine_alloc", ms_since(t_alloc));
+  if (G_ > 1) {
+    // this rank's first global row: the rows of the lower ranks
+    DevBuf<u64> rows(1 + size_t(G_));
+    const u64 mine = R_;
+    DP_CUDA(cudaMemcpy(rows.get(), &mine, sizeof(u64), cudaMemcpyHostToDevice));
+    comm_->all_gather_bytes(rows.get(), rows.get() + 1, sizeof(u64), stream_);
+    std::vector<u64> all(G_);
+    DP_CUDA(cudaMemcpyAsync(all.data(), rows.get() + 1, G_ * sizeof(u64), cudaMemcpyDeviceToHost, stream_));
+    DP_CUDA(cudaStreamSynchronize(stream_));
+    for (int r = 0; r < rank_; ++r) row0_ += all[r];
+  }
   arena_.reserve(size_t(1) << 20);
 
   // label validation, initial margins, per-tree array tables; one wait
@@ -330,6 +343,7 @@ void Engine::presize(SlabPlan& plan) {
   plan.want(leaves_, leaves_hi);
   plan.want(leaf_tasks_, (RK + kLeafChunkRows - 1) / kLeafChunkRows + leaves_hi);
   plan.want(nodes_, ids_hi * K);
+  if (col_sampling()) plan.want(fmask_, split * mask_words_);
   plan.want(ctr_, 1);
   plan.want(stats_, size_t(D) + 1);
   plan.want(next_id_, K);
@@ -414,6 +428,14 @@ void Engine::boost_round(Model& m) {
   // level stays within the asynchronous bounds (nothing then waits on the
   // host inside a round, and buffers no longer move).
   const bool graphable = graphs_ && rounds_ >= 1 && all_levels_async();
+  const bool sampling = row_sampling() || col_sampling();
+  if (sampling && dev_round_ != u64(m.rounds())) {
+    // the sampling hashes read the round from device memory, so a captured
+    // round stays valid from one round to the next
+    u32* r_h = reinterpret_cast<u32*>(arena_.get() + 128);  // in the arena's head
+    *r_h = u32(m.rounds());
+    DP_CUDA(cudaMemcpyAsync(round_dev_.get(), r_h, sizeof(u32), cudaMemcpyHostToDevice, stream_));
+  }
   RoundOut out;
   if (graphable && graph_exec_ && graph_prof_ == prof_.enabled()) {
     DP_CUDA(cudaGraphLaunch(graph_exec_, stream_));
@@ -459,6 +481,7 @@ void Engine::boost_round(Model& m) {
   }
   prof_.host("round_enqueue", ms_since(t_round));
   finish_round(m, out);
+  dev_round_ = sampling ? u64(m.rounds()) : ~u64(0);  // the round's last kernel advanced it
   ++rounds_;
 }
 
@@ -479,8 +502,9 @@ Engine::RoundOut Engine::enqueue_round() {
   u32* const hmax = ghmax_.get() + K;
   DP_CUDA(cudaMemsetAsync(gmax, 0, 2 * size_t(K) * sizeof(u32), stream_));
   prof_.begin(stream_, "gradients", double(R) * K * (4 + 8) + double(R) * 4);
-  launch_gradients(p_.objective_id(), K, margin_.get(), d_.labels(), R, gh_[0].get(), gmax, hmax,
-                   stream_);
+  RowSample rs;
+  if (row_sampling()) rs = RowSample{p_.subsample, p_.seed, round_dev_.get(), row0_};
+  launch_gradients(p_.objective_id(), K, margin_.get(), d_.labels(), R, gh_[0].get(), gmax, hmax, stream_, rs);
   prof_.end(stream_);
   if (comm_) {
     comm_->max_u32(gmax, 2 * size_t(K), stream_);
@@ -537,6 +561,7 @@ Engine::RoundOut Engine::enqueue_round() {
       grow(gathered_, open_hi * u64(G_));
     }
     grow(split_idx_, open_hi);
+    if (col_sampling()) grow(fmask_, open_hi * mask_words_);
     grow(part_nodes_, open_hi);
     grow(cursors_, 2 * open_hi);
     grow(part_tasks_, (RK + kPartChunk - 1) / kPartChunk + open_hi);
@@ -576,10 +601,14 @@ Engine::RoundOut Engine::enqueue_round() {
 
     // ---- split evaluation over this rank's feature group, then (G > 1) the
     // per-node best over all groups
+    if (col_sampling())
+      launch_feature_masks(rb, F, p_.seed, round_dev_.get(), p_.colsample_bytree, p_.colsample_bylevel,
+                           p_.colsample_bynode, depth, fmask_.get(), mask_words_, stream_);
     pi_eval[depth] = prof_.begin(stream_, "eval_splits", 0.0);
     launch_eval_splits_dev(hist, f_own_n_, q_->nbins.get() + f_own0_, q_->has_missing.get() + f_own0_,
                            eval_nodes_.get(), &ctr->n_open, scales_.get(), sp, cand_.get(),
-                           G_ > 1 ? best_local_.get() : best_.get(), stream_, fg_, f_own0_);
+                           G_ > 1 ? best_local_.get() : best_.get(), stream_, fg_, f_own0_,
+                           col_sampling() ? fmask_.get() : nullptr, mask_words_);
     prof_.end(stream_);
     if (G_ > 1) {
       prof_.begin(stream_, "exchange_cands", double(open_hi * u64(G_)) * sizeof(SplitCand));
@@ -613,6 +642,7 @@ Engine::RoundOut Engine::enqueue_round() {
   prof_.begin(stream_, "leaf_update", double(R) * K * 12.0);
   launch_leaf_update_dev(leaf_tasks_.get(), &ctr->n_leaf_tasks, margin_.get(), u32(K), stream_);
   prof_.end(stream_);
+  if (row_sampling() || col_sampling()) launch_bump_round(round_dev_.get(), stream_);
 
   RoundOut out;
   out.ids_hi = ids_hi;

@@ -113,6 +113,10 @@ class Engine {
   RoundOut enqueue_round();                       // every launch of one round
   void finish_round(Model& m, const RoundOut& out);  // one read-back, the trees
   bool all_levels_async() const;
+  bool row_sampling() const { return p_.subsample < 1.0; }
+  bool col_sampling() const {
+    return p_.colsample_bytree < 1.0 || p_.colsample_bylevel < 1.0 || p_.colsample_bynode < 1.0;
+  }
   void drop_graph();
   // Sizes every round buffer for the levels whose bounds stay within the
   // asynchronous limits, so steady rounds allocate nothing.
@@ -164,6 +168,13 @@ class Engine {
   DevBuf<RoundCounters> ctr_;
   DevBuf<LevelStats> stats_;
   DevBuf<u32> scratch_;  // [0]: label check flag; [1, 1 + K): initial margins (f32 bits)
+  // sampling: the round counter the sampling hashes read (device), this
+  // rank's first global row, per-node feature masks of a level
+  DevBuf<u32> round_dev_;
+  DevBuf<u32> fmask_;
+  u32 mask_words_ = 0;
+  u64 row0_ = 0;
+  u64 dev_round_ = ~u64(0);  // value of round_dev_ when known
   int sms_ = 148;
   // CUDA graph of a whole round (replayed while the bounds and buffers hold)
   bool graphs_ = true;  // DP_CUDA_GRAPHS=0 turns capture off

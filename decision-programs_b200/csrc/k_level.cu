@@ -310,6 +310,68 @@ __global__ void __launch_bounds__(kBook) k_leaf_values(RoundBuffers b, const Sca
   }
 }
 
+constexpr u32 kMaskThreads = 256;
+
+// One block per open node (grid-stride); shared: the hash of every feature
+// and two membership flags per feature.
+__global__ void __launch_bounds__(kMaskThreads) k_feature_masks(RoundBuffers b, u32 F, long long seed,
+                                                                const u32* __restrict__ round_dev, double c_tree,
+                                                                double c_level, double c_node, int depth,
+                                                                u32* __restrict__ fmask, u32 W) {
+  extern __shared__ __align__(8) unsigned char msm[];
+  u64* key = reinterpret_cast<u64*>(msm);
+  u8* in = msm + 8 * u64(F);
+  u8* keep = in + F;
+  __shared__ u32 s_count;
+  const u32 n_open = b.ctr->n_open;
+  const u32 round = *round_dev;
+  for (u32 i = blockIdx.x; i < n_open; i += gridDim.x) {
+    const OpenRec o = b.open_cur[i];
+    for (u32 f = threadIdx.x; f < F; f += kMaskThreads) in[f] = 1;
+    // one nested selection: the `c` fraction of the current set with the
+    // smallest (hash, feature)
+    auto select = [&](double c, u32 kind, u64 index) {
+      if (c >= 1.0) return;
+      if (threadIdx.x == 0) s_count = 0;
+      __syncthreads();
+      u32 mine = 0;
+      for (u32 f = threadIdx.x; f < F; f += kMaskThreads) {
+        key[f] = sample_hash(seed, round, o.tree, kind, f, index);
+        mine += in[f];
+      }
+      atomicAdd(&s_count, mine);
+      __syncthreads();
+      const u32 want = sample_count(c, s_count);
+      for (u32 f = threadIdx.x; f < F; f += kMaskThreads) {
+        u32 rank = 0;
+        if (in[f]) {
+          const u64 kf = key[f];
+          for (u32 g = 0; g < F; ++g) rank += (in[g] && (key[g] < kf || (key[g] == kf && g < f))) ? 1u : 0u;
+        }
+        keep[f] = in[f] && rank < want;
+      }
+      __syncthreads();
+      for (u32 f = threadIdx.x; f < F; f += kMaskThreads) in[f] = keep[f];
+      __syncthreads();
+    };
+    __syncthreads();
+    select(c_tree, kSampleTree, 0);
+    select(c_level, kSampleLevel, u64(depth));
+    select(c_node, kSampleNode, u64(o.id));
+    for (u32 w = threadIdx.x; w < W; w += kMaskThreads) {
+      u32 bits = 0;
+      for (u32 j = 0; j < 32; ++j) {
+        const u32 f = w * 32 + j;
+        if (f < F && in[f]) bits |= 1u << j;
+      }
+      fmask[u64(i) * W + w] = bits;
+    }
+    __syncthreads();
+  }
+}
+
+__global__ void k_bump_round(u32* round_dev) { *round_dev += 1u; }
+
 int sm_count() {
   int dev = 0, sms = 148;
   DP_CUDA(cudaGetDevice(&dev));
@@ -349,6 +411,28 @@ void launch_leaf_values(const RoundBuffers& b, const Scales* scales, SplitParams
                         cudaStream_t s) {
   k_leaf_values<<<1, kBook, 0, s>>>(b, scales, p, ridx_sets[0], ridx_sets[1], R);
   after_launch("leaf_values");
+}
+
+void launch_feature_masks(const RoundBuffers& b, u32 F, long long seed, const u32* round_dev, double c_tree,
+                          double c_level, double c_node, int depth, u32* fmask, u32 W, cudaStream_t s) {
+  need(F <= 16384, "column sampling supports at most 16384 features");
+  const size_t smem = 10 * size_t(F);
+  static thread_local int configured_device = -1;
+  int dev = 0;
+  DP_CUDA(cudaGetDevice(&dev));
+  if (configured_device != dev) {
+    DP_CUDA(cudaFuncSetAttribute(k_feature_masks, cudaFuncAttributeMaxDynamicSharedMemorySize, 10 * 16384));
+    configured_device = dev;
+  }
+  const u32 blocks = u32(b.cap_split < 4096 ? (b.cap_split ? b.cap_split : 1) : 4096);
+  k_feature_masks<<<blocks, kMaskThreads, smem, s>>>(b, F, seed, round_dev, c_tree, c_level, c_node, depth, fmask,
+                                                     W);
+  after_launch("feature_masks");
+}
+
+void launch_bump_round(u32* round_dev, cudaStream_t s) {
+  k_bump_round<<<1, 1, 0, s>>>(round_dev);
+  after_launch("bump_round");
 }
 
 }  // namespace dp

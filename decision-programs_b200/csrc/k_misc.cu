@@ -28,8 +28,13 @@ __device__ __forceinline__ u32 warp_max(u32 b) {
 // block and class.
 __global__ void __launch_bounds__(256) k_gradients(int objective, int K, const float* __restrict__ margin,
                                                     const float* __restrict__ label, u64 R, float2* __restrict__ gh,
-                                                    u32* gmax, u32* hmax) {
+                                                    u32* gmax, u32* hmax, RowSample rs) {
   __shared__ u32 smg[kSharedClasses], smh[kSharedClasses];
+  const bool sampling = rs.rate < 1.0;
+  const u32 round = sampling ? *rs.round : 0u;
+  auto kept = [&](u64 r, int k) {
+    return !sampling || sample_uniform(sample_hash(rs.seed, round, u32(k), kSampleRow, rs.row0 + r, 0)) < rs.rate;
+  };
   const bool shared_max = K <= kSharedClasses;
   for (int k = threadIdx.x; k < kSharedClasses; k += blockDim.x) { smg[k] = 0u; smh[k] = 0u; }
   __syncthreads();
@@ -51,6 +56,7 @@ __global__ void __launch_bounds__(256) k_gradients(int objective, int K, const f
           g = float(p - y);
           h = float(fmax(p * (1.0 - p), 1e-16));
         }
+        if (!kept(r, 0)) g = h = 0.f;
         gh[r] = make_float2(g, h);
         lg = max(lg, __float_as_uint(fabsf(g)));
         lh = max(lh, __float_as_uint(h));
@@ -69,6 +75,7 @@ __global__ void __launch_bounds__(256) k_gradients(int objective, int K, const f
           const double pk = dp_exp(double(m[k]) - mx) / s;
           g = float(pk - (double(k) == y ? 1.0 : 0.0));
           h = float(fmax(2.0 * pk * (1.0 - pk), 1e-16));
+          if (!kept(r, k)) g = h = 0.f;
           gh[u64(k) * R + r] = make_float2(g, h);
         }
         const u32 wg = warp_max(__float_as_uint(fabsf(g))), wh = warp_max(__float_as_uint(h));
@@ -197,9 +204,10 @@ int grid_for(u64 n, int block) {
 }  // namespace
 
 void launch_gradients(int objective, int K, const float* margin, const float* label, u64 R, float2* gh,
-                      u32* gmax_bits, u32* hmax_bits, cudaStream_t s) {
+                      u32* gmax_bits, u32* hmax_bits, cudaStream_t s, const RowSample& rs) {
   if (R == 0) return;
-  k_gradients<<<grid_for(R, 256), 256, 0, s>>>(objective, K, margin, label, R, gh, gmax_bits, hmax_bits);
+  need(rs.rate >= 1.0 || rs.round != nullptr, "row sampling needs the round counter");
+  k_gradients<<<grid_for(R, 256), 256, 0, s>>>(objective, K, margin, label, R, gh, gmax_bits, hmax_bits, rs);
   after_launch("gradients");
 }
 

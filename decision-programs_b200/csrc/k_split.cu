@@ -42,7 +42,8 @@ __device__ __forceinline__ Best shfl_best(const Best& v, int src) {
 __device__ __forceinline__ void eval_item(u32 w, const i64* __restrict__ hist, u32 F, const u16* __restrict__ nbins,
                                           const u8* __restrict__ has_missing, const EvalNode* __restrict__ nodes,
                                           const Scales* __restrict__ scales, const SplitParams& p, u32 nchunks,
-                                          SplitCand* __restrict__ cand, u32 fstride, u32 f_base) {
+                                          SplitCand* __restrict__ cand, u32 fstride, u32 f_base,
+                                          const u32* __restrict__ fmask, u32 mask_words) {
   __shared__ Best wbest[kEvalThreads / 32];
   const u32 node = w / nchunks, chunk = w % nchunks;
   const EvalNode nd = nodes[node];
@@ -56,6 +57,10 @@ __device__ __forceinline__ void eval_item(u32 w, const i64* __restrict__ hist, u
   for (u32 f = chunk * kEvalFeatureChunk + warp; f < f_end; f += kEvalThreads / 32) {
     const int nb = nbins[f];
     if (nb < 2) continue;
+    if (fmask) {
+      const u32 gf = f_base + f;
+      if (!((fmask[u64(node) * mask_words + (gf >> 5)] >> (gf & 31u)) & 1u)) continue;
+    }
     const bool hm = has_missing[f] != 0;
     const i64* hf = hist + (u64(nd.slot) * fstride + f) * (2 * kMaxBins);
     const i64 gm = hm ? hf[2 * kMissingBin] : 0, hmq = hm ? hf[2 * kMissingBin + 1] : 0;
@@ -129,7 +134,7 @@ __global__ void __launch_bounds__(kEvalThreads) k_eval(const i64* __restrict__ h
                                                        const EvalNode* __restrict__ nodes,
                                                        const Scales* __restrict__ scales, SplitParams p, u32 nchunks,
                                                        SplitCand* __restrict__ cand) {
-  eval_item(blockIdx.x, hist, F, nbins, has_missing, nodes, scales, p, nchunks, cand, F, 0);
+  eval_item(blockIdx.x, hist, F, nbins, has_missing, nodes, scales, p, nchunks, cand, F, 0, nullptr, 0);
 }
 
 // Node count in device memory: a fixed grid walks the work items.
@@ -139,10 +144,11 @@ __global__ void __launch_bounds__(kEvalThreads) k_eval_dev(const i64* __restrict
                                                            const EvalNode* __restrict__ nodes,
                                                            const Scales* __restrict__ scales, SplitParams p,
                                                            u32 nchunks, const u32* __restrict__ nnodes,
-                                                           SplitCand* __restrict__ cand, u32 fstride, u32 f_base) {
+                                                           SplitCand* __restrict__ cand, u32 fstride, u32 f_base,
+                                                           const u32* __restrict__ fmask, u32 mask_words) {
   const u32 items = *nnodes * nchunks;
   for (u32 w = blockIdx.x; w < items; w += gridDim.x)
-    eval_item(w, hist, F, nbins, has_missing, nodes, scales, p, nchunks, cand, fstride, f_base);
+    eval_item(w, hist, F, nbins, has_missing, nodes, scales, p, nchunks, cand, fstride, f_base, fmask, mask_words);
 }
 
 __global__ void k_reduce_cands(const SplitCand* __restrict__ cand, u32 nnodes_host, const u32* __restrict__ nnodes_dev,
@@ -174,7 +180,8 @@ void launch_eval_splits(const i64* hist, u32 F, const u16* nbins, const u8* has_
 
 void launch_eval_splits_dev(const i64* hist, u32 F, const u16* nbins, const u8* has_missing, const EvalNode* nodes,
                             const u32* nnodes_dev, const Scales* scales, SplitParams p, SplitCand* cand,
-                            SplitCand* best, cudaStream_t s, u32 fstride, u32 f_base) {
+                            SplitCand* best, cudaStream_t s, u32 fstride, u32 f_base, const u32* fmask,
+                            u32 mask_words) {
   int dev = 0, sms = 148;
   DP_CUDA(cudaGetDevice(&dev));
   DP_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
@@ -183,7 +190,8 @@ void launch_eval_splits_dev(const i64* hist, u32 F, const u16* nbins, const u8* 
   const u32 nchunks = F ? (F + kEvalFeatureChunk - 1) / kEvalFeatureChunk : 1;
   // with one feature chunk the chunk candidate is the node's best
   k_eval_dev<<<sms * 8, kEvalThreads, 0, s>>>(hist, F, nbins, has_missing, nodes, scales, p, nchunks, nnodes_dev,
-                                               nchunks == 1 ? best : cand, fstride ? fstride : F, f_base);
+                                               nchunks == 1 ? best : cand, fstride ? fstride : F, f_base, fmask,
+                                               mask_words);
   after_launch("eval_splits");
   if (nchunks > 1) {
     k_reduce_cands<<<sms, 128, 0, s>>>(cand, 0, nnodes_dev, nchunks, best);

@@ -62,10 +62,20 @@ struct CutsDevice {
 // ---- gradients --------------------------------------------------------------
 enum Objective : int { kSquaredError = 0, kLogistic = 1, kSoftprob = 2, kSoftmax = 3 };
 
+// Row sampling of one round: with rate < 1, row r of tree k is kept iff
+// sample_uniform(sample_hash(seed, *round, k, kSampleRow, row0 + r, 0)) <
+// rate; a dropped row's (g, h) become (0, 0) before the maxima, so it adds
+// nothing to any histogram.  row0 is this rank's first global row.
+struct RowSample {
+  double rate = 1.0;
+  long long seed = 0;
+  const u32* round = nullptr;  // device counter of the current round
+  u64 row0 = 0;
+};
 // gh[k][r] from margins [R][K] and labels; maxima of |g| and h per class are
 // atomically maxed into gmax[k], hmax[k] (float bits as u32; must be zeroed).
 void launch_gradients(int objective, int K, const float* margin, const float* label, u64 R, float2* gh,
-                      u32* gmax_bits, u32* hmax_bits, cudaStream_t s);
+                      u32* gmax_bits, u32* hmax_bits, cudaStream_t s, const RowSample& rs = RowSample());
 // scales[k] from the maxima.
 void launch_scales(int K, const u32* gmax_bits, const u32* hmax_bits, Scales* scales, cudaStream_t s);
 
@@ -121,9 +131,12 @@ constexpr u32 kEvalFeatureChunk = 16;
 // at a stride of fstride features per slot (0: F) and whose global ids start
 // at f_base (nbins / has_missing point at the first of them).  F may be 0:
 // every node then gets "no candidate" (gain -inf, feature -1).
+// With fmask set, feature f (global id) of the open node at index i is a
+// candidate only if bit f of fmask[i * mask_words ...] is set.
 void launch_eval_splits_dev(const i64* hist, u32 F, const u16* nbins, const u8* has_missing, const EvalNode* nodes,
                             const u32* nnodes_dev, const Scales* scales, SplitParams p, SplitCand* cand,
-                            SplitCand* best, cudaStream_t s, u32 fstride = 0, u32 f_base = 0);
+                            SplitCand* best, cudaStream_t s, u32 fstride = 0, u32 f_base = 0,
+                            const u32* fmask = nullptr, u32 mask_words = 0);
 
 // ---- partition ----------------------------------------------------------------
 struct PartTask {

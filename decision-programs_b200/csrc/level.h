@@ -95,6 +95,17 @@ void launch_zero_slots(const RoundBuffers& b, i64* hist, u64 slot_elems, u64 min
 void launch_decide(const RoundBuffers& b, const float* cut, const u8* has_missing, int depth, int max_depth,
                    int set, cudaStream_t s);
 void launch_children(const RoundBuffers& b, int depth, int max_depth, cudaStream_t s);
+// Column sampling of this level: for every open node, the features that may
+// split it, as bits fmask[i * W + f / 32].  Nested exact-count selections
+// (the candidates with the smallest sample_hash, ties to the lower feature):
+// the tree keeps max(1, floor(c_tree F)) features (kind kSampleTree, index
+// 0), the level that fraction c_level of the tree's (kSampleLevel, index
+// depth), the node c_node of the level's (kSampleNode, index node id).  The
+// round comes from *round_dev.  F must be at most 16384.
+void launch_feature_masks(const RoundBuffers& b, u32 F, long long seed, const u32* round_dev, double c_tree,
+                          double c_level, double c_node, int depth, u32* fmask, u32 W, cudaStream_t s);
+// *round_dev += 1 (the end of a round).
+void launch_bump_round(u32* round_dev, cudaStream_t s);
 // ridx_sets[s] is the base of the K per-tree row-index arrays of set s
 // (tree k at + k * R).
 void launch_leaf_values(const RoundBuffers& b, const Scales* scales, SplitParams p, u32* const ridx_sets[2], u64 R,

@@ -439,7 +439,58 @@ struct Params {
   float base_margin = 0.0f;
   int threads = 1;
   int subtract = 1;
+  // sampling
+  double subsample = 1.0, cs_tree = 1.0, cs_level = 1.0, cs_node = 1.0;
+  int64_t seed = 0;
+  uint64_t row0 = 0;  // first global row of this rank
 };
+
+// ---- sampling: a counter-based hash (the output function of SplitMix64,
+// Steele, Lea and Flood, OOPSLA 2014) over a chain of key words.  Row r of
+// tree (round, k) is kept iff uniform(hash(seed, round, k, ROW, r, 0)) <
+// subsample; feature sets are nested exact-count selections of the smallest
+// (hash, feature): the tree keeps max(1, floor(c_tree F)) (kind TREE, index
+// 0), each level that fraction of the tree's (LEVEL, depth), each node that
+// fraction of the level's (NODE, node id).
+uint64_t mix64(uint64_t z) {
+  z ^= z >> 30;
+  z *= 0xbf58476d1ce4e5b9ULL;
+  z ^= z >> 27;
+  z *= 0x94d049bb133111ebULL;
+  z ^= z >> 31;
+  return z;
+}
+enum { kRow = 1, kTreeSet = 2, kLevelSet = 3, kNodeSet = 4 };
+uint64_t sample_hash(int64_t seed, uint32_t round, uint32_t k, uint32_t kind, uint64_t a, uint64_t b) {
+  uint64_t h = mix64(uint64_t(seed) + 0x9e3779b97f4a7c15ULL);
+  h = mix64(h ^ uint64_t(round));
+  h = mix64(h ^ ((uint64_t(kind) << 32) | uint64_t(k)));
+  h = mix64(h ^ a);
+  return mix64(h ^ b);
+}
+double sample_uniform(uint64_t h) { return double(h >> 11) * (1.0 / 9007199254740992.0); }
+uint32_t sample_count(double c, uint32_t n) {
+  const uint32_t k = uint32_t(c * double(n));
+  return n == 0 ? 0u : std::min(n, std::max(1u, k));
+}
+// Features that may split node `node` at `depth` of tree (round, k).
+std::vector<uint8_t> feature_set(const Params& p, uint32_t round, uint32_t k, int depth, int node, uint32_t F) {
+  std::vector<uint8_t> in(F, 1);
+  auto select = [&](double c, uint32_t kind, uint64_t index) {
+    if (c >= 1.0) return;
+    std::vector<std::pair<uint64_t, uint32_t>> v;
+    for (uint32_t f = 0; f < F; ++f)
+      if (in[f]) v.push_back({sample_hash(p.seed, round, k, kind, f, index), f});
+    const uint32_t n = sample_count(c, uint32_t(v.size()));
+    std::sort(v.begin(), v.end());
+    std::fill(in.begin(), in.end(), uint8_t(0));
+    for (uint32_t i = 0; i < n; ++i) in[v[i].second] = 1;
+  };
+  select(p.cs_tree, kTreeSet, 0);
+  select(p.cs_level, kLevelSet, uint64_t(depth));
+  select(p.cs_node, kNodeSet, uint64_t(node));
+  return in;
+}
 
 struct Split {
   double gain = -std::numeric_limits<double>::infinity();
@@ -460,7 +511,7 @@ static inline double score(double g, double h, const Params& p) {
 }
 
 Split best_split(const int64_t* hist, uint32_t F, const Cuts& c, int64_t gq, int64_t hq, float sg, float sh,
-                 const Params& p) {
+                 const Params& p, const uint8_t* allowed = nullptr) {
   const double isg = 1.0 / double(sg), ish = 1.0 / double(sh);
   const double G = double(gq) * isg, H = double(hq) * ish;
   const double sp = score(G, H, p);
@@ -468,6 +519,7 @@ Split best_split(const int64_t* hist, uint32_t F, const Cuts& c, int64_t gq, int
   for (uint32_t f = 0; f < F; ++f) {
     const int nb = c.nbins[f];
     if (nb < 2) continue;
+    if (allowed && !allowed[f]) continue;
     const int64_t* hf = hist + size_t(f) * 256 * 2;
     const bool hm = c.has_missing[f];
     const int64_t gm = hm ? hf[2 * kMissingBin] : 0, hmq = hm ? hf[2 * kMissingBin + 1] : 0;
@@ -520,7 +572,9 @@ struct Tree {
 // Grows one tree.  ghp is the tree's (g,h) in row order; on return `leaf_of`
 // holds the leaf id of every row.
 Tree grow_tree(const uint8_t* bins, uint64_t bstride, uint32_t F, uint64_t R, const Cuts& c, const float* gh_rows,
-               float sg, float sh, const Params& p, std::vector<int32_t>& leaf_of, const Comm& comm = Comm()) {
+               float sg, float sh, const Params& p, std::vector<int32_t>& leaf_of, const Comm& comm = Comm(),
+               uint32_t round = 0, uint32_t klass = 0) {
+  const bool col_sampling = p.cs_tree < 1.0 || p.cs_level < 1.0 || p.cs_node < 1.0;
   Tree t;
   std::vector<uint32_t> ridx(R), ridx2(R);
   std::vector<float> ghp(gh_rows, gh_rows + 2 * R), ghp2(2 * R);
@@ -545,7 +599,10 @@ Tree grow_tree(const uint8_t* bins, uint64_t bstride, uint32_t F, uint64_t R, co
     std::vector<Split> splits(open.size());
     parallel_tasks(int64_t(open.size()), p.threads, [&](int64_t i, int) {
       const int id = open[i].id;
-      splits[i] = best_split(open[i].hist.data(), F, c, t.gq[id], t.hq[id], sg, sh, p);
+      std::vector<uint8_t> allowed;
+      if (col_sampling) allowed = feature_set(p, round, klass, depth, id, F);
+      splits[i] = best_split(open[i].hist.data(), F, c, t.gq[id], t.hq[id], sg, sh, p,
+                             col_sampling ? allowed.data() : nullptr);
     });
     std::vector<Open> next;
     std::vector<int> split_idx;
@@ -678,7 +735,15 @@ void train_rounds(Model& m, int rounds) {
   const int K = m.p.K;
   std::vector<float> gh(size_t(K) * m.R * 2);
   for (int it = 0; it < rounds; ++it) {
+    const uint32_t round = uint32_t(m.trees.size() / size_t(K));
     gradients(m.p.objective, K, m.margin.data(), m.label.data(), m.R, gh.data(), m.p.threads);
+    if (m.p.subsample < 1.0)
+      for (int k = 0; k < K; ++k)
+        for (uint64_t r = 0; r < m.R; ++r)
+          if (!(sample_uniform(sample_hash(m.p.seed, round, uint32_t(k), kRow, m.p.row0 + r, 0)) < m.p.subsample)) {
+            gh[(size_t(k) * m.R + r) * 2] = 0.0f;
+            gh[(size_t(k) * m.R + r) * 2 + 1] = 0.0f;
+          }
     std::vector<std::vector<int32_t>> leaf_of(K);
     std::vector<Tree> round_trees(K);
     for (int k = 0; k < K; ++k) {
@@ -687,7 +752,8 @@ void train_rounds(Model& m, int rounds) {
       quantizer(ghk, m.R, &sg, &sh, m.comm);
       m.scales.push_back(sg);
       m.scales.push_back(sh);
-      round_trees[k] = grow_tree(m.bins.data(), m.bstride, m.F, m.R, m.cuts, ghk, sg, sh, m.p, leaf_of[k], m.comm);
+      round_trees[k] = grow_tree(m.bins.data(), m.bstride, m.F, m.R, m.cuts, ghk, sg, sh, m.p, leaf_of[k], m.comm,
+                                 round, uint32_t(k));
     }
     for (int k = 0; k < K; ++k) {
       const Tree& t = round_trees[k];
@@ -890,6 +956,17 @@ int orc_radix_cuts(const float* x, uint64_t R, uint32_t F, uint64_t stride, int 
   std::memcpy(nbins, c.nbins.data(), c.nbins.size() * sizeof(uint16_t));
   std::memcpy(has_missing, c.has_missing.data(), c.has_missing.size());
   return 0;
+}
+
+void orc_set_sampling(void* h, double subsample, double cs_tree, double cs_level, double cs_node, int64_t seed,
+                      uint64_t row0) {
+  orc::Params& p = static_cast<orc::Model*>(h)->p;
+  p.subsample = subsample;
+  p.cs_tree = cs_tree;
+  p.cs_level = cs_level;
+  p.cs_node = cs_node;
+  p.seed = seed;
+  p.row0 = row0;
 }
 
 int orc_train_more(void* h, int rounds) {

@@ -50,6 +50,7 @@ def lib() -> C.CDLL:
                                         C.c_double, C.c_double, C.c_float, i32, i32, ALLREDUCE, P]
         L.orc_radix_cuts.argtypes = [P, u64, u32, u64, i32, i32, C.c_float, P, P, P, ALLREDUCE, P]
         L.orc_train_more.argtypes = [P, i32]
+        L.orc_set_sampling.argtypes = [P, C.c_double, C.c_double, C.c_double, C.c_double, i64, u64]
         L.orc_free.argtypes = [P]
         L.orc_num_trees.argtypes = [P]
         L.orc_tree_size.argtypes = [P, i32]
@@ -173,18 +174,24 @@ class Model:
     def __init__(self, x: np.ndarray, y: np.ndarray, objective: str = "reg:squarederror", num_class: int = 1,
                  max_depth: int = 6, max_bin: int = 256, eta: float = 0.3, reg_lambda: float = 1.0,
                  alpha: float = 0.0, gamma: float = 0.0, min_child_weight: float = 1.0, base_margin: float = 0.0,
-                 rounds: int = 1, threads: int = 1, subtract: bool = True):
+                 rounds: int = 1, threads: int = 1, subtract: bool = True, subsample: float = 1.0,
+                 colsample_bytree: float = 1.0, colsample_bylevel: float = 1.0, colsample_bynode: float = 1.0,
+                 seed: int = 0):
         self.x = np.ascontiguousarray(x, dtype=np.float32)
         self.y = np.ascontiguousarray(y, dtype=np.float32)
         R, F = self.x.shape
         self.R, self.F = R, F
         K = num_class if objective.startswith("multi:") else 1
         self.K = K
+        sampling = (subsample, colsample_bytree, colsample_bylevel, colsample_bynode) != (1.0, 1.0, 1.0, 1.0)
         self.h = lib().orc_train(_p(self.x), R, F, F, _p(self.y), OBJECTIVES[objective], K, max_depth, max_bin,
-                                 eta, reg_lambda, alpha, gamma, min_child_weight, base_margin, rounds, threads,
-                                 int(subtract))
+                                 eta, reg_lambda, alpha, gamma, min_child_weight, base_margin,
+                                 0 if sampling else rounds, threads, int(subtract))
         if not self.h:
             raise RuntimeError(lib().orc_last_error().decode())
+        if sampling:
+            lib().orc_set_sampling(self.h, subsample, colsample_bytree, colsample_bylevel, colsample_bynode, seed, 0)
+            lib().orc_train_more(self.h, rounds)
 
     @classmethod
     def sharded(cls, x: np.ndarray, y: np.ndarray, allreduce, objective: str = "reg:squarederror",

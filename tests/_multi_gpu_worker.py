@@ -31,6 +31,9 @@ def data(case: str):
     y = (x[:, 0] * x[:, 1] + np.sin(x[:, 2]) + 0.1 * rng.standard_normal(R)).astype(np.float32)
     if case == "deep_exact_host":
         return x, y, {"objective": "reg:squarederror", "max_depth": 11, "min_child_weight": 0.0}
+    if case == "sampled":
+        return x, y, {"objective": "reg:squarederror", "max_depth": 6, "subsample": 0.7, "colsample_bytree": 0.8,
+                      "colsample_bynode": 0.5, "seed": 77}
     return x, y, {"objective": "reg:squarederror", "max_depth": 8}
 
 

@@ -25,7 +25,8 @@ def free_port() -> int:
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs at least two GPUs")
-@pytest.mark.parametrize("case,K", [("squared", 1), ("logistic_nan", 1), ("softprob", 4), ("deep_exact_host", 1)])
+@pytest.mark.parametrize("case,K", [("squared", 1), ("logistic_nan", 1), ("softprob", 4), ("deep_exact_host", 1),
+                                    ("sampled", 1)])
 def test_sharded_ranks_match_the_oracle(orc, tmp_path, case, K):
     import _multi_gpu_worker as w
     world = min(torch.cuda.device_count(), 4)
@@ -42,8 +43,10 @@ def test_sharded_ranks_match_the_oracle(orc, tmp_path, case, K):
     models = [(tmp_path / f"rank{k}.json").read_bytes() for k in range(world)]
     assert all(m == models[0] for m in models)
     x, y, params = w.data(case)
+    sampling = {k: params[k] for k in ("subsample", "colsample_bytree", "colsample_bylevel", "colsample_bynode",
+                                        "seed") if k in params}
     o = orc.Model(x, y, params["objective"], num_class=K, max_depth=params["max_depth"], rounds=rounds, threads=8,
-                  min_child_weight=params.get("min_child_weight", 1.0))
+                  min_child_weight=params.get("min_child_weight", 1.0), **sampling)
     trees = json.loads(models[0])["learner"]["gradient_booster"]["model"]["trees"]
     assert len(trees) == o.num_trees()
     for i, t in enumerate(trees):

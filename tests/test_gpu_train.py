@@ -148,6 +148,39 @@ def test_direct_and_graph_rounds_agree(dp, orc, monkeypatch, graphs):
     np.testing.assert_array_equal(b.margins(len(y), 1).view(np.uint32), o.margins().view(np.uint32))
 
 
+SAMPLING_CASES = [
+    dict(subsample=0.6),
+    dict(colsample_bytree=0.5),
+    dict(colsample_bylevel=0.7),
+    dict(colsample_bynode=0.4),
+    dict(subsample=0.8, colsample_bytree=0.8, colsample_bylevel=0.75, colsample_bynode=0.6, seed=12345),
+]
+
+
+@pytest.mark.parametrize("sampling", SAMPLING_CASES)
+@pytest.mark.parametrize("objective,K", [("binary:logistic", 1), ("multi:softprob", 3)])
+def test_sampling_matches_oracle(dp, orc, sampling, objective, K):
+    """Row and column sampling with the counter-based hash: the GPU path
+    (rounds after the first replayed as a graph) grows the oracle's trees."""
+    rng = np.random.default_rng(21)
+    R, F = 7000, 23
+    x = rng.standard_normal((R, F)).astype(np.float32)
+    x[rng.random((R, F)) < 0.03] = np.nan
+    s = np.nan_to_num(x[:, 0]) + 0.7 * np.nan_to_num(x[:, 3]) - 0.5 * np.nan_to_num(x[:, 11])
+    y = (s > 0).astype(np.float32) if K == 1 else np.digitize(s, [-0.6, 0.6]).astype(np.float32)
+    params = {"objective": objective, "tree_method": "hist", "device": "cuda:0", "max_depth": 5, "max_bin": 256,
+              "eta": 0.3}
+    if K > 1:
+        params["num_class"] = K
+    params.update({k: v for k, v in sampling.items()})
+    d = dp.DMatrix.from_torch(cuda(x), cuda(y))
+    b = dp.train(params, d, 4)
+    o = orc.Model(x, y, objective, num_class=K, max_depth=5, max_bin=256, eta=0.3, rounds=4, threads=8,
+                  **sampling)
+    compare_models(b, o, K)
+    np.testing.assert_array_equal(b.margins(R, K).view(np.uint32), o.margins().view(np.uint32))
+
+
 @pytest.mark.parametrize("R", [1, 2, 7, 33])
 def test_tiny_inputs(dp, orc, R):
     rng = np.random.default_rng(R)
