@@ -69,3 +69,36 @@ def test_reference_trainer_runs_on_libdp_gbdt(orc, tmp_path):
         np.testing.assert_array_equal(np.array(t["default_left"], np.uint8), ot["default_left"])
         np.testing.assert_array_equal(np.array(t["split_conditions"], np.float32).view(np.uint32),
                                       ot["split_conditions"].view(np.uint32))
+
+
+READER = ROOT / "oracle" / "_ref" / "ref_read_model"
+
+
+@pytest.mark.skipif(not READER.exists(), reason="reference reader not built (needs the reference sources)")
+def test_reference_converter_reads_gpu_trained_models(dp, orc, tmp_path):
+    """A multi:softprob model trained on the GPU and saved through
+    XGBoosterSaveModel is read by the reference converter's reader
+    (native/class_io.hpp:99-242) with the oracle's trees bit for bit."""
+    import torch
+    from test_ref_reader import check_against_trees, read_with_reference
+
+    rng = np.random.default_rng(33)
+    R, F, K = 6000, 9, 5
+    x = rng.standard_normal((R, F)).astype(np.float32)
+    x[rng.random((R, F)) < 0.05] = np.nan
+    y = np.argmax(np.nan_to_num(x[:, :K]) + 0.4 * rng.standard_normal((R, K)), 1).astype(np.float32)
+    params = {"objective": "multi:softprob", "num_class": K, "tree_method": "hist", "device": "cuda:0",
+              "max_depth": 4, "max_bin": 256, "eta": 0.3}
+    d = dp.DMatrix.from_torch(torch.from_numpy(x).cuda(), torch.from_numpy(y).cuda())
+    b = dp.train(params, d, 3)
+    path = tmp_path / "model.json"
+    b.save_model(str(path))
+    doc = read_with_reference(path)
+    o = orc.Model(x, y, "multi:softprob", num_class=K, max_depth=4, max_bin=256, eta=0.3, rounds=3, threads=8)
+    trees = []
+    for i in range(o.num_trees()):
+        t = o.tree(i)
+        t["klass"] = i % K
+        trees.append(t)
+    check_against_trees(doc, trees, K)
+    assert doc["features"] == F
