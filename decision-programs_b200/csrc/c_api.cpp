@@ -500,15 +500,27 @@ HistPlan* make_hist_plan(const uint8_t* bins, uint64_t bin_stride, uint32_t feat
     total += dp::u64(seg_end[i] - seg_begin[i]);
   }
   const int64_t chunk = int64_t(dp::hist_chunk_rows(total * ftiles));
+  // Queue order: piece index first, then segment, then feature tile.  With
+  // row lists grouped by node and ascending inside a node, the p-th pieces of
+  // all nodes cover about the same range of rows, so the blocks running at
+  // one time read neighbouring rows of the bin matrix instead of every
+  // N-th row of one node.
+  std::vector<int64_t> pieces(size_t(std::max(nseg, 0))), piece(size_t(std::max(nseg, 0)));
+  int64_t max_pieces = 0;
   for (int32_t i = 0; i < nseg; ++i) {
     const int64_t n = seg_end[i] - seg_begin[i];
-    if (n == 0) continue;
-    const int64_t pieces = (n + chunk - 1) / chunk, piece = (n + pieces - 1) / pieces;
-    for (dp::u32 ft = 0; ft < ftiles; ++ft)
-      for (int64_t b = seg_begin[i]; b < seg_end[i]; b += piece)
-        tasks.push_back(dp::HistTask{dp::u32(i), ft * dp::kHistFeatureTile, 0, 0, b,
-                                     std::min<int64_t>(seg_end[i], b + piece)});
+    pieces[i] = n ? (n + chunk - 1) / chunk : 0;
+    piece[i] = n ? (n + pieces[i] - 1) / pieces[i] : 0;
+    max_pieces = std::max(max_pieces, pieces[i]);
   }
+  for (int64_t q = 0; q < max_pieces; ++q)
+    for (int32_t i = 0; i < nseg; ++i) {
+      const int64_t b = seg_begin[i] + q * piece[i];
+      if (q >= pieces[i] || b >= seg_end[i]) continue;
+      for (dp::u32 ft = 0; ft < ftiles; ++ft)
+        tasks.push_back(dp::HistTask{dp::u32(i), ft * dp::kHistFeatureTile, 0, 0, b,
+                                     std::min<int64_t>(seg_end[i], b + piece[i])});
+    }
   p->ntasks = dp::u32(tasks.size());
   p->tasks.resize(std::max<size_t>(tasks.size(), 1));
   p->trees.resize(1);
@@ -592,7 +604,8 @@ int dp_eval_splits(const int64_t* hist, int32_t nnodes, uint32_t features, const
   need(nnodes >= 0, "invalid node count");
   if (nnodes == 0) return 0;
   std::vector<dp::EvalNode> en(nnodes);
-  for (int32_t n = 0; n < nnodes; ++n) en[n] = dp::EvalNode{dp::u32(n), 0, totals[2 * n], totals[2 * n + 1]};
+  for (int32_t n = 0; n < nnodes; ++n)
+    en[n] = dp::EvalNode{dp::u32(n), 0, totals[2 * n], totals[2 * n + 1], dp::kNoSlot, 0};
   const dp::u32 nchunks = (features + dp::kEvalFeatureChunk - 1) / dp::kEvalFeatureChunk;
   dp::DevBuf<dp::EvalNode> de(nnodes);
   dp::DevBuf<dp::SplitCand> cand(size_t(nnodes) * nchunks), best(nnodes);

@@ -359,6 +359,7 @@ RoundBuffers Engine::round_buffers(int depth, u64 cap_split, u64 cap_next) const
   b.open_cur = open_[c].get();
   b.open_next = open_[n].get();
   b.build = build_[c].get();
+  b.triples = triples_[c].get();
   b.build_next = build_[n].get();
   b.triples_next = triples_[n].get();
   b.hist_tasks = hist_tasks_.get();
@@ -535,7 +536,7 @@ Engine::RoundOut Engine::enqueue_round() {
   // node holds at least one row over all ranks (a split with an empty side
   // has gain -gamma <= 0), so open nodes never exceed K * rows.
   u64 open_hi = u64(K), ids_hi = 1, leaves_hi = 0;
-  std::vector<int> pi_hist(D, -1), pi_sub(D, -1), pi_eval(D, -1);
+  std::vector<int> pi_hist(D, -1), pi_eval(D, -1);
   int set = 0, region = 0, depth = 0;
   for (; depth < D; ++depth) {
     u64 nbuild_hi = depth == 0 ? u64(K) : (open_hi + 1) / 2;
@@ -592,13 +593,6 @@ Engine::RoundOut Engine::enqueue_round() {
       comm_->reduce_scatter_i64(send_.get(), hist, nbuild_hi * slot_elems_, stream_);
       prof_.end(stream_);
     }
-    if (depth > 0) {
-      pi_sub[depth] = prof_.begin(stream_, "subtract", 0.0);
-      launch_subtract_dev(hist, hist_[1 - region].get(), slot_elems_, triples_[depth & 1].get(), &ctr->n_triples,
-                          stream_);
-      prof_.end(stream_);
-    }
-
     // ---- split evaluation over this rank's feature group, then (G > 1) the
     // per-node best over all groups
     if (col_sampling())
@@ -608,7 +602,8 @@ Engine::RoundOut Engine::enqueue_round() {
     launch_eval_splits_dev(hist, f_own_n_, q_->nbins.get() + f_own0_, q_->has_missing.get() + f_own0_,
                            eval_nodes_.get(), &ctr->n_open, scales_.get(), sp, cand_.get(),
                            G_ > 1 ? best_local_.get() : best_.get(), stream_, fg_, f_own0_,
-                           col_sampling() ? fmask_.get() : nullptr, mask_words_);
+                           col_sampling() ? fmask_.get() : nullptr, mask_words_, hist_[1 - region].get(),
+                           depth + 1 < D ? 1 : 0);
     prof_.end(stream_);
     if (G_ > 1) {
       prof_.begin(stream_, "exchange_cands", double(open_hi * u64(G_)) * sizeof(SplitCand));
@@ -647,7 +642,6 @@ Engine::RoundOut Engine::enqueue_round() {
   RoundOut out;
   out.ids_hi = ids_hi;
   out.pi_hist = std::move(pi_hist);
-  out.pi_sub = std::move(pi_sub);
   out.pi_eval = std::move(pi_eval);
   return out;
 }
@@ -680,8 +674,10 @@ void Engine::finish_round(Model& m, const RoundOut& out) {
     const LevelStats& st = st_h[d];
     prof_.set_bytes(out.pi_hist[d], double(st.rows_built) * (double(F) + 12.0) +
                                         double(st.n_build) * double(F) * kMaxBins * 16.0);
-    prof_.set_bytes(out.pi_sub[d], double(st.n_build) * slot_bytes * 3.0);
-    prof_.set_bytes(out.pi_eval[d], double(st.n_open) * slot_bytes);
+    // built nodes read once; a derived sibling reads parent and sibling and
+    // (before the last level) writes itself
+    const double derived = d > 0 ? double(st.n_open - st.n_build) : 0.0;
+    prof_.set_bytes(out.pi_eval[d], (double(st.n_open) + derived * (d + 1 < D ? 2.0 : 1.0)) * slot_bytes);
   }
   prof_.resolve();
   if (prof_.graph_timing_failed()) {

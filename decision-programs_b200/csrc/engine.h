@@ -108,7 +108,7 @@ class Engine {
   // What the host needs after a round's work is enqueued.
   struct RoundOut {
     u64 ids_hi = 1;                             // bound on node ids per tree
-    std::vector<int> pi_hist, pi_sub, pi_eval;  // profiler entries per level
+    std::vector<int> pi_hist, pi_eval;          // profiler entries per level
   };
   RoundOut enqueue_round();                       // every launch of one round
   void finish_round(Model& m, const RoundOut& out);  // one read-back, the trees

@@ -123,12 +123,19 @@ __global__ void __launch_bounds__(kBook) k_hist_tasks(RoundBuffers b, u32 ftiles
       b.hist_tasks[t] = HistTask{s_slot[j], ft * kHistFeatureTile, s_tree[j], np == 1 ? 1u : 0u, beg, end};
     });
   }
-  // split-evaluation inputs of the open nodes
-  const u32 n_open = b.ctr->n_open;
+  // split-evaluation inputs of the open nodes; a node in slot ns + j (the
+  // larger sibling of triple j) is derived from its parent and slot j
+  const u32 n_open = b.ctr->n_open, nt = b.ctr->n_triples;
   for (u32 i = threadIdx.x; i < n_open; i += kBook) {
     const OpenRec o = b.open_cur[i];
     const NodeRec& r = node_at(b, o.tree, o.id);
-    b.eval_nodes[i] = EvalNode{o.slot, o.tree, r.gq, r.hq};
+    u32 par = kNoSlot, small = 0;
+    if (depth > 0 && o.slot >= nt && o.slot - nt < nt) {
+      const u32 j = o.slot - nt;
+      par = b.triples[3 * j];
+      small = b.triples[3 * j + 1];
+    }
+    b.eval_nodes[i] = EvalNode{o.slot, o.tree, r.gq, r.hq, par, small};
   }
   if (threadIdx.x == 0) {
     if (base > b.cap_hist_tasks) b.ctr->overflow |= kOvfHistTasks;

@@ -39,11 +39,12 @@ __device__ __forceinline__ Best shfl_best(const Best& v, int src) {
 }
 
 // Best candidate of one (node, feature chunk) work item, written to cand[w].
-__device__ __forceinline__ void eval_item(u32 w, const i64* __restrict__ hist, u32 F, const u16* __restrict__ nbins,
+__device__ __forceinline__ void eval_item(u32 w, i64* hist, u32 F, const u16* __restrict__ nbins,
                                           const u8* __restrict__ has_missing, const EvalNode* __restrict__ nodes,
                                           const Scales* __restrict__ scales, const SplitParams& p, u32 nchunks,
                                           SplitCand* __restrict__ cand, u32 fstride, u32 f_base,
-                                          const u32* __restrict__ fmask, u32 mask_words) {
+                                          const u32* __restrict__ fmask, u32 mask_words,
+                                          const i64* __restrict__ parent, int store_derived) {
   __shared__ Best wbest[kEvalThreads / 32];
   const u32 node = w / nchunks, chunk = w % nchunks;
   const EvalNode nd = nodes[node];
@@ -57,21 +58,44 @@ __device__ __forceinline__ void eval_item(u32 w, const i64* __restrict__ hist, u
   for (u32 f = chunk * kEvalFeatureChunk + warp; f < f_end; f += kEvalThreads / 32) {
     const int nb = nbins[f];
     if (nb < 2) continue;
+    // lane l holds bins [8l, 8l + 8); a derived sibling is parent - built
+    // sibling, stored for the next level whatever this node's feature mask
+    i64* hf = hist + (u64(nd.slot) * fstride + f) * (2 * kMaxBins);
+    longlong2 x[8];
+    if (nd.par != kNoSlot) {
+      const longlong2* pv =
+          reinterpret_cast<const longlong2*>(parent + (u64(nd.par) * fstride + f) * (2 * kMaxBins)) + 8 * lane;
+      const longlong2* sv =
+          reinterpret_cast<const longlong2*>(hist + (u64(nd.small) * fstride + f) * (2 * kMaxBins)) + 8 * lane;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const longlong2 a = pv[j], b = sv[j];
+        x[j] = make_longlong2(a.x - b.x, a.y - b.y);
+      }
+      if (store_derived) {
+        longlong2* dv = reinterpret_cast<longlong2*>(hf) + 8 * lane;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) dv[j] = x[j];
+      }
+    } else {
+      const longlong2* v = reinterpret_cast<const longlong2*>(hf) + 8 * lane;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) x[j] = v[j];
+    }
     if (fmask) {
       const u32 gf = f_base + f;
       if (!((fmask[u64(node) * mask_words + (gf >> 5)] >> (gf & 31u)) & 1u)) continue;
     }
     const bool hm = has_missing[f] != 0;
-    const i64* hf = hist + (u64(nd.slot) * fstride + f) * (2 * kMaxBins);
-    const i64 gm = hm ? hf[2 * kMissingBin] : 0, hmq = hm ? hf[2 * kMissingBin + 1] : 0;
+    // the missing code is bin 255: lane 31's last pair
+    const i64 gm31 = __shfl_sync(0xffffffffu, x[7].x, 31), hm31 = __shfl_sync(0xffffffffu, x[7].y, 31);
+    const i64 gm = hm ? gm31 : 0, hmq = hm ? hm31 : 0;
     i64 g[8], h[8];
-    const longlong2* v = reinterpret_cast<const longlong2*>(hf) + 8 * lane;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      const longlong2 x = v[j];
       const bool value_bin = 8 * lane + j < nb;  // missing bin and empty tail excluded
-      g[j] = value_bin ? x.x : 0;
-      h[j] = value_bin ? x.y : 0;
+      g[j] = value_bin ? x[j].x : 0;
+      h[j] = value_bin ? x[j].y : 0;
     }
     i64 sg_l = 0, sh_l = 0;
 #pragma unroll
@@ -128,27 +152,29 @@ __device__ __forceinline__ void eval_item(u32 w, const i64* __restrict__ hist, u
   __syncthreads();  // wbest is reused by the next work item of this block
 }
 
-__global__ void __launch_bounds__(kEvalThreads) k_eval(const i64* __restrict__ hist, u32 F,
+__global__ void __launch_bounds__(kEvalThreads) k_eval(i64* hist, u32 F,
                                                        const u16* __restrict__ nbins,
                                                        const u8* __restrict__ has_missing,
                                                        const EvalNode* __restrict__ nodes,
                                                        const Scales* __restrict__ scales, SplitParams p, u32 nchunks,
                                                        SplitCand* __restrict__ cand) {
-  eval_item(blockIdx.x, hist, F, nbins, has_missing, nodes, scales, p, nchunks, cand, F, 0, nullptr, 0);
+  eval_item(blockIdx.x, hist, F, nbins, has_missing, nodes, scales, p, nchunks, cand, F, 0, nullptr, 0, nullptr, 0);
 }
 
 // Node count in device memory: a fixed grid walks the work items.
-__global__ void __launch_bounds__(kEvalThreads) k_eval_dev(const i64* __restrict__ hist, u32 F,
+__global__ void __launch_bounds__(kEvalThreads) k_eval_dev(i64* hist, u32 F,
                                                            const u16* __restrict__ nbins,
                                                            const u8* __restrict__ has_missing,
                                                            const EvalNode* __restrict__ nodes,
                                                            const Scales* __restrict__ scales, SplitParams p,
                                                            u32 nchunks, const u32* __restrict__ nnodes,
                                                            SplitCand* __restrict__ cand, u32 fstride, u32 f_base,
-                                                           const u32* __restrict__ fmask, u32 mask_words) {
+                                                           const u32* __restrict__ fmask, u32 mask_words,
+                                                           const i64* __restrict__ parent, int store_derived) {
   const u32 items = *nnodes * nchunks;
   for (u32 w = blockIdx.x; w < items; w += gridDim.x)
-    eval_item(w, hist, F, nbins, has_missing, nodes, scales, p, nchunks, cand, fstride, f_base, fmask, mask_words);
+    eval_item(w, hist, F, nbins, has_missing, nodes, scales, p, nchunks, cand, fstride, f_base, fmask, mask_words,
+              parent, store_derived);
 }
 
 __global__ void k_reduce_cands(const SplitCand* __restrict__ cand, u32 nnodes_host, const u32* __restrict__ nnodes_dev,
@@ -172,7 +198,8 @@ void launch_eval_splits(const i64* hist, u32 F, const u16* nbins, const u8* has_
                         cudaStream_t s) {
   if (!nnodes) return;
   const u32 nchunks = (F + kEvalFeatureChunk - 1) / kEvalFeatureChunk;
-  k_eval<<<nnodes * nchunks, kEvalThreads, 0, s>>>(hist, F, nbins, has_missing, nodes, scales, p, nchunks, cand);
+  k_eval<<<nnodes * nchunks, kEvalThreads, 0, s>>>(const_cast<i64*>(hist), F, nbins, has_missing, nodes, scales, p,
+                                                   nchunks, cand);
   after_launch("eval_splits");
   k_reduce_cands<<<(nnodes + 127) / 128, 128, 0, s>>>(cand, nnodes, nullptr, nchunks, best);
   after_launch("reduce_splits");
@@ -181,7 +208,7 @@ void launch_eval_splits(const i64* hist, u32 F, const u16* nbins, const u8* has_
 void launch_eval_splits_dev(const i64* hist, u32 F, const u16* nbins, const u8* has_missing, const EvalNode* nodes,
                             const u32* nnodes_dev, const Scales* scales, SplitParams p, SplitCand* cand,
                             SplitCand* best, cudaStream_t s, u32 fstride, u32 f_base, const u32* fmask,
-                            u32 mask_words) {
+                            u32 mask_words, const i64* parent_hist, int store_derived) {
   int dev = 0, sms = 148;
   DP_CUDA(cudaGetDevice(&dev));
   DP_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
@@ -189,9 +216,9 @@ void launch_eval_splits_dev(const i64* hist, u32 F, const u16* nbins, const u8* 
   // "no candidate" entry
   const u32 nchunks = F ? (F + kEvalFeatureChunk - 1) / kEvalFeatureChunk : 1;
   // with one feature chunk the chunk candidate is the node's best
-  k_eval_dev<<<sms * 8, kEvalThreads, 0, s>>>(hist, F, nbins, has_missing, nodes, scales, p, nchunks, nnodes_dev,
-                                               nchunks == 1 ? best : cand, fstride ? fstride : F, f_base, fmask,
-                                               mask_words);
+  k_eval_dev<<<sms * 8, kEvalThreads, 0, s>>>(const_cast<i64*>(hist), F, nbins, has_missing, nodes, scales, p,
+                                               nchunks, nnodes_dev, nchunks == 1 ? best : cand, fstride ? fstride : F,
+                                               f_base, fmask, mask_words, parent_hist, store_derived);
   after_launch("eval_splits");
   if (nchunks > 1) {
     k_reduce_cands<<<sms, 128, 0, s>>>(cand, 0, nnodes_dev, nchunks, best);

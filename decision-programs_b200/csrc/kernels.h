@@ -44,11 +44,17 @@ struct SplitCand {
   i32 pad;
 };
 
-// Open node handed to split evaluation.
+constexpr u32 kNoSlot = 0xffffffffu;
+
+// Open node handed to split evaluation.  A node whose histogram was not built
+// (the larger sibling) has par != kNoSlot: its histogram is parent[par] -
+// hist[small], derived while it is evaluated and stored into its slot.
 struct EvalNode {
   u32 slot;   // histogram slot
   u32 tree;
   i64 gq, hq; // quantised totals
+  u32 par;    // parent slot in the previous level's histograms, or kNoSlot
+  u32 small;  // slot of the built sibling
 };
 
 // ---- binning (quantile cuts by exact radix selection) ---------------------
@@ -133,10 +139,13 @@ constexpr u32 kEvalFeatureChunk = 16;
 // every node then gets "no candidate" (gain -inf, feature -1).
 // With fmask set, feature f (global id) of the open node at index i is a
 // candidate only if bit f of fmask[i * mask_words ...] is set.
+// Derived siblings read parent_hist; with store_derived their histograms are
+// written into their slots (needed when the next level subtracts from them).
 void launch_eval_splits_dev(const i64* hist, u32 F, const u16* nbins, const u8* has_missing, const EvalNode* nodes,
                             const u32* nnodes_dev, const Scales* scales, SplitParams p, SplitCand* cand,
                             SplitCand* best, cudaStream_t s, u32 fstride = 0, u32 f_base = 0,
-                            const u32* fmask = nullptr, u32 mask_words = 0);
+                            const u32* fmask = nullptr, u32 mask_words = 0, const i64* parent_hist = nullptr,
+                            int store_derived = 0);
 
 // ---- partition ----------------------------------------------------------------
 struct PartTask {

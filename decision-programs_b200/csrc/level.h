@@ -56,6 +56,7 @@ struct RoundBuffers {
   OpenRec* open_cur;       // this level's open nodes (trees contiguous, ids ascending)
   OpenRec* open_next;      // [cap_next]
   u32* build;              // open indices of this level's directly built nodes
+  const u32* triples;      // this level's (parent slot, small slot, large slot), [n_triples]
   u32* build_next;         // [cap_split]
   u32* triples_next;       // [3 * cap_split] (parent slot, small slot, large slot)
   HistTask* hist_tasks;    // [cap_hist_tasks]
