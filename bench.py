@@ -23,6 +23,7 @@ from __future__ import annotations
 
 import argparse
 import json
+import re
 import os
 import pathlib
 import statistics
@@ -376,10 +377,13 @@ def main() -> None:
     hist = prof.get("histograms", {"launches": 0, "ms": 0.0, "alg_bytes": 0.0})
     hist_ms_per_launch = hist["ms"] / max(1, hist["launches"])
     achieved = hist["alg_bytes"] / max(1, hist["launches"]) / (hist_ms_per_launch / 1e3) / 1e9 if hist["ms"] else 0.0
+    # DRAM bytes per histogram launch of this workload, from the committed ncu
+    # summary (one-pass capture of one full round at full size)
     traffic = None
-    tfile = ROOT / "profiles" / "hist_traffic.json"
-    if tfile.exists():
-        traffic = json.loads(tfile.read_text()).get("bytes_per_launch_config4")
+    tfile = ROOT / "profiles" / "k_hist_config4_traffic.md"
+    if tfile.exists() and args.rows == ROWS and world == 1:
+        m = re.search(r"^bytes_per_launch_config4:\s*(\d+)", tfile.read_text(), re.M)
+        traffic = int(m.group(1)) if m else None
     model_bytes = len(b.save_raw())
     b.free()
     d.free()

@@ -90,16 +90,13 @@ __device__ __forceinline__ void eval_item(u32 w, i64* hist, u32 F, const u16* __
     // the missing code is bin 255: lane 31's last pair
     const i64 gm31 = __shfl_sync(0xffffffffu, x[7].x, 31), hm31 = __shfl_sync(0xffffffffu, x[7].y, 31);
     const i64 gm = hm ? gm31 : 0, hmq = hm ? hm31 : 0;
-    i64 g[8], h[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const bool value_bin = 8 * lane + j < nb;  // missing bin and empty tail excluded
-      g[j] = value_bin ? x[j].x : 0;
-      h[j] = value_bin ? x[j].y : 0;
-    }
     i64 sg_l = 0, sh_l = 0;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) { sg_l += g[j]; sh_l += h[j]; }
+    for (int j = 0; j < 8; ++j) {
+      if (8 * lane + j >= nb) x[j] = make_longlong2(0, 0);  // missing bin and empty tail excluded
+      sg_l += x[j].x;
+      sh_l += x[j].y;
+    }
     // exclusive warp scan of the lane sums
     i64 eg = sg_l, eh = sh_l;
 #pragma unroll
@@ -111,8 +108,8 @@ __device__ __forceinline__ void eval_item(u32 w, i64* hist, u32 F, const u16* __
     eh -= sh_l;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      eg += g[j];
-      eh += h[j];
+      eg += x[j].x;
+      eh += x[j].y;
       const int b = 8 * lane + j;
       if (b > nb - 2) continue;
 #pragma unroll
@@ -162,7 +159,7 @@ __global__ void __launch_bounds__(kEvalThreads) k_eval(i64* hist, u32 F,
 }
 
 // Node count in device memory: a fixed grid walks the work items.
-__global__ void __launch_bounds__(kEvalThreads) k_eval_dev(i64* hist, u32 F,
+__global__ void __launch_bounds__(kEvalThreads, 3) k_eval_dev(i64* hist, u32 F,
                                                            const u16* __restrict__ nbins,
                                                            const u8* __restrict__ has_missing,
                                                            const EvalNode* __restrict__ nodes,
