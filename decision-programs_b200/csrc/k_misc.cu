@@ -152,12 +152,23 @@ __global__ void k_scales(int K, const u32* gmax, const u32* hmax, Scales* scales
 __global__ void __launch_bounds__(256) k_leaf_update(const LeafTask* __restrict__ tasks, u32 ntasks_host,
                                                       const u32* __restrict__ ntasks_dev, float* margin, u32 K) {
   const u32 n = ntasks_dev ? *ntasks_dev : ntasks_host;
+  constexpr int kU = 4;  // rows in flight per thread
   for (u32 task = blockIdx.x; task < n; task += gridDim.x) {
     const LeafTask t = tasks[task];
-    for (i64 i = t.begin + threadIdx.x; i < t.end; i += blockDim.x) {
-      const u32 r = t.ridx[i];
-      float* m = margin + u64(r) * K + t.klass;
-      *m = *m + t.value;
+    for (i64 i0 = t.begin + threadIdx.x; i0 < t.end; i0 += i64(blockDim.x) * kU) {
+      u32 r[kU];
+      float m[kU];
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const i64 i = i0 + i64(u) * blockDim.x;
+        r[u] = i < t.end ? t.ridx[i] : 0xffffffffu;
+      }
+#pragma unroll
+      for (int u = 0; u < kU; ++u)
+        if (r[u] != 0xffffffffu) m[u] = margin[u64(r[u]) * K + t.klass];
+#pragma unroll
+      for (int u = 0; u < kU; ++u)
+        if (r[u] != 0xffffffffu) margin[u64(r[u]) * K + t.klass] = m[u] + t.value;
     }
   }
 }

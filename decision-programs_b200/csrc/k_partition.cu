@@ -22,9 +22,11 @@ namespace dp {
 namespace {
 
 constexpr int kPartThreads = 256;
-constexpr int kIlp = 4;  // independent row gathers in flight per thread
+constexpr int kIlp = 8;  // independent row gathers in flight per thread
+constexpr int kScatterSteps = 4;  // 256-position steps whose (g, h) loads are in flight together
 constexpr int kWordsPerTask = kPartChunk / 32;
 static_assert(kPartChunk % (kPartThreads * kIlp) == 0, "task rows are whole gather rounds");
+static_assert(kPartChunk % (kPartThreads * kScatterSteps) == 0, "task rows are whole scatter rounds");
 
 __device__ __forceinline__ bool goes_left(u8 b, const PartNode& nd) {
   if (nd.missing_is_bin && b == kMissingBin) return nd.default_left != 0;
@@ -37,6 +39,7 @@ __device__ __forceinline__ void partition_task(u32 task, const u8* __restrict__ 
                                                const PartNode* __restrict__ nodes,
                                                const PartTask* __restrict__ tasks, u32* __restrict__ cursors) {
   __shared__ u32 ballots[kWordsPerTask];
+  __shared__ u32 s_ridx[kPartChunk];  // the task's row indices, read once
   __shared__ u32 wsum[kPartThreads / 32];
   __shared__ u32 base_lr[2];
   const PartTask t = tasks[task];
@@ -55,6 +58,7 @@ __device__ __forceinline__ void partition_task(u32 task, const u8* __restrict__ 
     for (int u = 0; u < kIlp; ++u) {
       const u32 i = base + u * kPartThreads + threadIdx.x;
       r[u] = i < n ? __ldg(s.ridx + t.begin + i) : 0xffffffffu;
+      if (i < n) s_ridx[i] = r[u];
     }
     u8 b[kIlp];
 #pragma unroll
@@ -80,29 +84,40 @@ __device__ __forceinline__ void partition_task(u32 task, const u8* __restrict__ 
   }
   __syncthreads();
 
-  // scatter, 256 positions per step; ranks from the stored ballots
+  // scatter, 256 positions per step, kScatterSteps steps' (g, h) loads in
+  // flight together; ranks from the stored ballots
   u32 run_left = 0;
   const i64 lbase = nd.begin + base_lr[0];
   const i64 rtop = nd.end - 1 - i64(base_lr[1]);
-  for (u32 base = 0; base < n; base += kPartThreads) {
-    const u32 wi = base / 32 + warp;
-    const u32 ballot = base + warp * 32 < n ? ballots[wi] : 0u;
-    u32 before = 0, step_left = 0;
+  for (u32 base0 = 0; base0 < n; base0 += kPartThreads * kScatterSteps) {
+    float2 g[kScatterSteps];
 #pragma unroll
-    for (int w = 0; w < kPartThreads / 32; ++w) {
-      const u32 c = (base + w * 32 < n) ? __popc(ballots[base / 32 + w]) : 0u;
-      if (w < warp) before += c;
-      step_left += c;
+    for (int u = 0; u < kScatterSteps; ++u) {
+      const u32 i = base0 + u * kPartThreads + threadIdx.x;
+      if (i < n) g[u] = __ldg(s.gh + t.begin + i);
     }
-    const u32 i = base + threadIdx.x;
-    if (i < n) {
-      const bool go = (ballot >> lane) & 1u;
-      const u32 lrank = run_left + before + __popc(ballot & ((1u << lane) - 1u));
-      const i64 to = go ? lbase + lrank : rtop - i64(i - lrank);
-      d.ridx[to] = s.ridx[t.begin + i];
-      d.gh[to] = s.gh[t.begin + i];
+#pragma unroll
+    for (int u = 0; u < kScatterSteps; ++u) {
+      const u32 base = base0 + u * kPartThreads;
+      const u32 wi = base / 32 + warp;
+      const u32 ballot = base + warp * 32 < n ? ballots[wi] : 0u;
+      u32 before = 0, step_left = 0;
+#pragma unroll
+      for (int w = 0; w < kPartThreads / 32; ++w) {
+        const u32 c = (base + w * 32 < n) ? __popc(ballots[base / 32 + w]) : 0u;
+        if (w < warp) before += c;
+        step_left += c;
+      }
+      const u32 i = base + threadIdx.x;
+      if (i < n) {
+        const bool go = (ballot >> lane) & 1u;
+        const u32 lrank = run_left + before + __popc(ballot & ((1u << lane) - 1u));
+        const i64 to = go ? lbase + lrank : rtop - i64(i - lrank);
+        d.ridx[to] = s_ridx[i];
+        d.gh[to] = g[u];
+      }
+      run_left += step_left;
     }
-    run_left += step_left;
   }
   __syncthreads();  // shared state is reused by the block's next task
 }
