@@ -30,12 +30,15 @@ namespace {
 constexpr int kFT = kHistFeatureTile;  // 32 features per tile
 constexpr int kRPW = 16;               // rows per warp step (two lanes per row)
 #ifndef DP_HIST_UNROLL
-#define DP_HIST_UNROLL 4
+#define DP_HIST_UNROLL 6  // the 256-bin kernel's row steps in flight (the 64-bin one keeps 4)
 #endif
 #ifndef DP_HIST_THREADS
 #define DP_HIST_THREADS 1024
 #endif
-constexpr int kUnroll = DP_HIST_UNROLL;  // row steps in flight per warp
+// row steps in flight per warp: measured best at 6 for the 1024-thread
+// 256-bin kernel and at 4 for the 512-thread 64-bin kernel
+template <int MB>
+__host__ __device__ constexpr int unroll_for() { return MB >= 256 ? DP_HIST_UNROLL : 4; }
 constexpr u32 kNoRow = 0xffffffffu;
 
 struct HistArgs {
@@ -74,6 +77,7 @@ __global__ void __launch_bounds__(THREADS) k_hist(HistArgs a) {
   constexpr int kWCells = kFT * kWRow;
   constexpr int kWarps = THREADS / 32;
   constexpr u32 kStep = u32(kWarps) * kRPW;
+  constexpr int kUnroll = unroll_for<MB>();
   u32* Lg = reinterpret_cast<u32*>(smem);
   u32* Lh = Lg + kCells;
   long long* Wg = reinterpret_cast<long long*>(Lh + kCells);
@@ -91,9 +95,14 @@ __global__ void __launch_bounds__(THREADS) k_hist(HistArgs a) {
   const bool rot8 = (s & 8u) != 0, rot4 = (s & 4u) != 0;   // word rotation by s >> 2
   const u32 rsh = 8u * (s & 3u);                           // byte rotation by s & 3
   // column of atomic step j: feature 16h + ((s + j) & 15) of the tile
+#ifdef DP_HIST_COLJ_TABLE
   u32 colj[16];
 #pragma unroll
   for (int j = 0; j < 16; ++j) colj[j] = h16 + ((s + u32(j)) & 15u);
+#define DP_COLJ(j) colj[j]
+#else
+#define DP_COLJ(j) (h16 + ((s + u32(j)) & 15u))
+#endif
   u32 key_slot = kNoRow, key_f0 = 0, key_tree = 0;  // current accumulation target (block-uniform)
   bool key_excl = false;  // the key's task is the only one writing its (slot, tile)
   u32 in_window = 0;                                // rows in the u32 planes since the last fold
@@ -207,7 +216,7 @@ __global__ void __launch_bounds__(THREADS) k_hist(HistArgs a) {
           for (int j = 0; j < 16; ++j) {
             const u32 b = (w[j >> 2] >> (8 * (j & 3))) & 0xffu;
             if (MB < 256 && b >= u32(MB)) continue;
-            const u32 cell = b * kFT + colj[j];
+            const u32 cell = b * kFT + DP_COLJ(j);
             atomicAdd(Lg + cell, gq[u]);
             atomicAdd(Lh + cell, hq[u]);
           }
@@ -245,52 +254,7 @@ void launch_hist_variant(const HistArgs& a, cudaStream_t s) {
   k_hist<MB, THREADS, QUANT><<<grid, THREADS, kSmem, s>>>(a);
 }
 
-// hist[dst] = parent[par] - hist[src]; one block handles 2048 int64 of one triple.
-__global__ void __launch_bounds__(256) k_subtract(i64* hist, const i64* __restrict__ parent, u64 slot_elems,
-                                                  const u32* __restrict__ triples) {
-  const u32 tr = blockIdx.y;
-  const u32 par = triples[3 * tr], src = triples[3 * tr + 1], dst = triples[3 * tr + 2];
-  const longlong2* a = reinterpret_cast<const longlong2*>(parent + u64(par) * slot_elems);
-  const longlong2* b = reinterpret_cast<const longlong2*>(hist + u64(src) * slot_elems);
-  longlong2* c = reinterpret_cast<longlong2*>(hist + u64(dst) * slot_elems);
-  const u64 n2 = slot_elems / 2;
-  for (u64 i = u64(blockIdx.x) * blockDim.x + threadIdx.x; i < n2; i += u64(gridDim.x) * blockDim.x) {
-    const longlong2 x = a[i], y = b[i];
-    c[i] = make_longlong2(x.x - y.x, x.y - y.y);
-  }
-}
-
-// Same subtraction with the triple count in device memory: a fixed grid walks
-// (triple, 2048-element chunk) work items.
-__global__ void __launch_bounds__(256) k_subtract_dev(i64* hist, const i64* __restrict__ parent, u64 slot_elems,
-                                                      const u32* __restrict__ triples, const u32* __restrict__ n_dev) {
-  const u32 n = *n_dev;
-  const u64 n2 = slot_elems / 2;
-  const u64 chunks = (n2 + 2047) / 2048;
-  for (u64 w = blockIdx.x; w < u64(n) * chunks; w += gridDim.x) {
-    const u32 tr = u32(w / chunks);
-    const u64 c0 = (w % chunks) * 2048;
-    const u32 par = triples[3 * tr], src = triples[3 * tr + 1], dst = triples[3 * tr + 2];
-    const longlong2* a = reinterpret_cast<const longlong2*>(parent + u64(par) * slot_elems);
-    const longlong2* b = reinterpret_cast<const longlong2*>(hist + u64(src) * slot_elems);
-    longlong2* c = reinterpret_cast<longlong2*>(hist + u64(dst) * slot_elems);
-    for (u64 i = c0 + threadIdx.x; i < c0 + 2048 && i < n2; i += blockDim.x) {
-      const longlong2 x = a[i], y = b[i];
-      c[i] = make_longlong2(x.x - y.x, x.y - y.y);
-    }
-  }
-}
-
 }  // namespace
-
-void launch_subtract_dev(i64* hist, const i64* parent_hist, u64 slot_elems, const u32* triples, const u32* n_dev,
-                         cudaStream_t s) {
-  int dev = 0, sms = 148;
-  DP_CUDA(cudaGetDevice(&dev));
-  DP_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-  k_subtract_dev<<<sms * 8, 256, 0, s>>>(hist, parent_hist, slot_elems, triples, n_dev);
-  after_launch("subtract");
-}
 
 void launch_histograms(const u8* bins, u64 bin_stride, u32 F, int max_bins, bool quantized_gh,
                        const TreeArrays* trees, const Scales* scales, const HistTask* tasks, u32 ntasks,
@@ -316,14 +280,6 @@ u64 hist_chunk_rows(u64 total_rows) {
   const u64 target = u64(sms) * 4;  // about four tasks per SM, balanced by the task queue
   const u64 chunk = (total_rows + target - 1) / target;
   return chunk < 2048 ? 2048 : chunk;
-}
-
-void launch_subtract(i64* hist, const i64* parent_hist, u64 slot_elems, const u32* triples, u32 n, cudaStream_t s) {
-  if (!n) return;
-  const u64 blocks = (slot_elems / 2 + 2047) / 2048;
-  dim3 grid(unsigned(blocks ? blocks : 1), n);
-  k_subtract<<<grid, 256, 0, s>>>(hist, parent_hist, slot_elems, triples);
-  after_launch("subtract");
 }
 
 }  // namespace dp

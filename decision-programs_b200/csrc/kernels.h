@@ -120,12 +120,6 @@ void launch_quantize_gh(float2* gh, u64 R, int K, const Scales* scales, cudaStre
 // exactly one bin of every feature, so these are each root histogram's sums.
 void launch_gh_totals(const float2* gh_quantized, u64 R, int K, i64* totals, cudaStream_t s);
 
-// hist[dst] = parent_hist[par] - hist[src] for each (par, src, dst) slot triple.
-void launch_subtract(i64* hist, const i64* parent_hist, u64 slot_elems, const u32* triples, u32 n, cudaStream_t s);
-// The same with the triple count in device memory.
-void launch_subtract_dev(i64* hist, const i64* parent_hist, u64 slot_elems, const u32* triples, const u32* n_dev,
-                         cudaStream_t s);
-
 // ---- split evaluation --------------------------------------------------------
 // Per (node, feature chunk) candidate into cand[node][chunk]; then the best per
 // node into best[node].
