@@ -156,6 +156,7 @@ Engine::Engine(DMatrix& d, const TrainParams& p, Comm* comm) : d_(d), p_(p), com
   f_own_n_ = f_own0_ < F_ ? std::min(fg_, F_ - f_own0_) : 0;
   slot_elems_ = u64(fg_) * kMaxBins * 2;
   full_slot_elems_ = u64(G_) * slot_elems_;
+  nchunks_ = std::max<u32>(1, (fg_ + kEvalFeatureChunk - 1) / kEvalFeatureChunk);
   max_bins_ = 0;
   for (u32 f = 0; f < F_; ++f) {
     max_bins_ = std::max<int>(max_bins_, q_->nbins_h[f]);
@@ -297,7 +298,6 @@ void Engine::presize(SlabPlan& plan) {
   const u64 RK = std::max<u64>(R_, 1) * K;
   const u64 slot_bytes = slot_elems_ * sizeof(i64);
   const u32 ftiles = (F_ + kFT - 1) / kFT;
-  const u32 nchunks = (F_ + kEvalFeatureChunk - 1) / kEvalFeatureChunk;
   // the same bounds the level loop of boost_round derives
   u64 open_hi = K, ids_hi = 1, leaves_hi = 0;
   u64 hist[2] = {0, 0}, tasks = 0, split = 0, opens[2] = {K, 0}, builds[2] = {K, 0}, send = 0;
@@ -329,12 +329,10 @@ void Engine::presize(SlabPlan& plan) {
   }
   plan.want(hist_tasks_, tasks);
   plan.want(eval_nodes_, split);
-  plan.want(best_, split);
-  plan.want(cand_, split * std::max<u32>(nchunks, 1));
+  plan.want(cand_, split * nchunks_);
   if (G_ > 1) {
     plan.want(send_, send);
-    plan.want(best_local_, split);
-    plan.want(gathered_, split * u64(G_));
+    plan.want(gathered_, split * nchunks_ * u64(G_));
   }
   plan.want(split_idx_, split);
   plan.want(part_nodes_, split);
@@ -364,9 +362,9 @@ RoundBuffers Engine::round_buffers(int depth, u64 cap_split, u64 cap_next) const
   b.triples_next = triples_[n].get();
   b.hist_tasks = hist_tasks_.get();
   b.eval_nodes = eval_nodes_.get();
-  b.best = best_.get();
-  b.gathered = gathered_.get();
+  b.cands = G_ > 1 ? gathered_.get() : cand_.get();
   b.nranks = u32(G_);
+  b.nchunks = nchunks_;
   b.split_idx = split_idx_.get();
   b.part_nodes = part_nodes_.get();
   b.part_tasks = part_tasks_.get();
@@ -492,7 +490,6 @@ Engine::RoundOut Engine::enqueue_round() {
   const u32 F = F_;
   const int D = p_.max_depth;
   const u32 ftiles = (F + kFT - 1) / kFT;
-  const u32 nchunks = (F + kEvalFeatureChunk - 1) / kEvalFeatureChunk;
   const SplitParams sp = p_.split_params();
   const u64 Rt = std::max<u64>(q_->rows_total, 1);
   const u64 RK = std::max<u64>(R, 1) * u64(K);
@@ -538,6 +535,7 @@ Engine::RoundOut Engine::enqueue_round() {
   u64 open_hi = u64(K), ids_hi = 1, leaves_hi = 0;
   std::vector<int> pi_hist(D, -1), pi_eval(D, -1);
   int set = 0, region = 0, depth = 0;
+  bool zeroed_by_children = false;  // this level's output slots were zeroed by the previous level
   for (; depth < D; ++depth) {
     u64 nbuild_hi = depth == 0 ? u64(K) : (open_hi + 1) / 2;
     if (open_hi > async_open_limit_ || open_hi * slot_bytes > async_hist_bytes_) {
@@ -554,12 +552,10 @@ Engine::RoundOut Engine::enqueue_round() {
     grow(hist_[region], std::max<u64>(open_hi, 1) * slot_elems_);
     grow(hist_tasks_, (nbuild_hi + 4 * u64(sms_) + 1) * ftiles);
     grow(eval_nodes_, open_hi);
-    grow(best_, open_hi);
-    grow(cand_, open_hi * std::max<u32>(nchunks, 1));
+    grow(cand_, open_hi * nchunks_);
     if (G_ > 1) {
       grow(send_, nbuild_hi * full_slot_elems_);
-      grow(best_local_, open_hi);
-      grow(gathered_, open_hi * u64(G_));
+      grow(gathered_, open_hi * nchunks_ * u64(G_));
     }
     grow(split_idx_, open_hi);
     if (col_sampling()) grow(fmask_, open_hi * mask_words_);
@@ -581,7 +577,7 @@ Engine::RoundOut Engine::enqueue_round() {
     launch_hist_tasks(rb, ftiles, depth, stream_);
     i64* hout = G_ > 1 ? send_.get() : hist;
     const u64 out_slot = G_ > 1 ? full_slot_elems_ : slot_elems_;
-    launch_zero_slots(rb, hout, out_slot, G_ > 1 ? nbuild_hi : 0, stream_);
+    if (!zeroed_by_children) launch_zero_slots(rb, hout, out_slot, G_ > 1 ? nbuild_hi : 0, stream_);
     const HistLayout lay{fg_, slot_elems_, nbuild_hi * slot_elems_};
     pi_hist[depth] = prof_.begin(stream_, "histograms", 0.0);
     launch_histograms(q_->bins.get(), q_->bin_stride, F, max_bins_, true, tarr_[set].get(), scales_.get(),
@@ -599,15 +595,15 @@ Engine::RoundOut Engine::enqueue_round() {
       launch_feature_masks(rb, F, p_.seed, round_dev_.get(), p_.colsample_bytree, p_.colsample_bylevel,
                            p_.colsample_bynode, depth, fmask_.get(), mask_words_, stream_);
     pi_eval[depth] = prof_.begin(stream_, "eval_splits", 0.0);
-    launch_eval_splits_dev(hist, f_own_n_, q_->nbins.get() + f_own0_, q_->has_missing.get() + f_own0_,
-                           eval_nodes_.get(), &ctr->n_open, scales_.get(), sp, cand_.get(),
-                           G_ > 1 ? best_local_.get() : best_.get(), stream_, fg_, f_own0_,
-                           col_sampling() ? fmask_.get() : nullptr, mask_words_, hist_[1 - region].get(),
-                           depth + 1 < D ? 1 : 0);
+    launch_eval_candidates_dev(hist, f_own_n_, q_->nbins.get() + f_own0_, q_->has_missing.get() + f_own0_,
+                               eval_nodes_.get(), &ctr->n_open, scales_.get(), sp, cand_.get(), nchunks_, stream_,
+                               fg_, f_own0_, col_sampling() ? fmask_.get() : nullptr, mask_words_,
+                               hist_[1 - region].get(), depth + 1 < D ? 1 : 0);
     prof_.end(stream_);
     if (G_ > 1) {
-      prof_.begin(stream_, "exchange_cands", double(open_hi * u64(G_)) * sizeof(SplitCand));
-      comm_->all_gather_bytes(best_local_.get(), gathered_.get(), open_hi * sizeof(SplitCand), stream_);
+      const u64 bytes = open_hi * nchunks_ * sizeof(SplitCand);
+      prof_.begin(stream_, "exchange_cands", double(bytes * u64(G_)));
+      comm_->all_gather_bytes(cand_.get(), gathered_.get(), bytes, stream_);
       prof_.end(stream_);
     }
     launch_decide(rb, q_->cut.get(), q_->has_missing.get(), depth, D, set, stream_);
@@ -617,7 +613,18 @@ Engine::RoundOut Engine::enqueue_round() {
     launch_partition_dev(q_->bins_blk.get(), 32 * u64(F), tarr_[set].get(), tarr_[1 - set].get(), part_nodes_.get(),
                          part_tasks_.get(), &ctr->n_part_tasks, cursors_.get(), stream_);
     prof_.end(stream_);
-    launch_children(rb, depth, D, stream_);
+    // the children kernel zeroes the next level's output slots when their
+    // buffer is already large enough (so the next level does not regrow it)
+    {
+      const u64 nb_next = (next_hi + 1) / 2;
+      const bool next_async = next_hi <= async_open_limit_ && next_hi * slot_bytes <= async_hist_bytes_;
+      i64* z = G_ > 1 ? send_.get() : hist_[1 - region].get();
+      const u64 zsize = G_ > 1 ? send_.size() : hist_[1 - region].size();
+      const u64 zslot = G_ > 1 ? full_slot_elems_ : slot_elems_;
+      const bool zfit = (G_ > 1 ? nb_next : next_hi) * zslot <= zsize;
+      zeroed_by_children = depth + 1 < D && next_async && zfit;
+      launch_children(rb, depth, D, stream_, zeroed_by_children ? z : nullptr, zslot, G_ > 1 ? nb_next : 0);
+    }
 
     leaves_hi += open_hi;
     open_hi = next_hi;

@@ -137,6 +137,7 @@ class Engine {
   // summed histograms of its own group only: slot_elems_ = fg_ * 2 * 256.
   int G_ = 1, rank_ = 0;
   u32 fg_ = 0, f_own0_ = 0, f_own_n_ = 0;
+  u32 nchunks_ = 1;          // feature chunks of split evaluation per group (>= 1, equal on every rank)
   u64 slot_elems_ = 0;       // elements of one own-group histogram slot
   u64 full_slot_elems_ = 0;  // elements of one slot over all groups (G * fg_ * 2 * 256)
 
@@ -151,9 +152,9 @@ class Engine {
   DevBuf<HistTask> hist_tasks_;
   DevBuf<u32> hist_counter_;
   DevBuf<EvalNode> eval_nodes_;
-  DevBuf<SplitCand> cand_, best_;
+  DevBuf<SplitCand> cand_;                 // [open][nchunks_] this rank's candidates
   DevBuf<i64> send_;                       // this rank's partial histograms, group-major (G > 1)
-  DevBuf<SplitCand> best_local_, gathered_;  // own-group candidates; all ranks' (G > 1)
+  DevBuf<SplitCand> gathered_;             // [G][open][nchunks_] all ranks' candidates (G > 1)
   DevBuf<i64> gh_totals_;                  // [K][2] root sums
   DevBuf<PartNode> part_nodes_;
   DevBuf<PartTask> part_tasks_;

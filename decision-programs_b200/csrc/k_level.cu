@@ -174,15 +174,13 @@ __global__ void __launch_bounds__(kBook) k_decide(RoundBuffers b, const float* _
     if (valid) {
       o = b.open_cur[i];
       if (depth < max_depth) {
-        if (b.nranks > 1) {
-          bs = b.gathered[i];
-          for (u32 r = 1; r < b.nranks; ++r) {
-            const SplitCand x = b.gathered[u64(r) * b.cap_split + i];
-            if (x.gain > bs.gain) bs = x;
+        bool first = true;
+        for (u32 r = 0; r < b.nranks; ++r)
+          for (u32 c = 0; c < b.nchunks; ++c) {
+            const SplitCand x = b.cands[(u64(r) * b.cap_split + i) * b.nchunks + c];
+            if (first || x.gain > bs.gain) bs = x;
+            first = false;
           }
-        } else {
-          bs = b.best[i];
-        }
       }
     }
     const bool split = valid && depth < max_depth && bs.feature >= 0 && bs.gain > 0.0;
@@ -248,10 +246,17 @@ __global__ void __launch_bounds__(kBook) k_decide(RoundBuffers b, const float* _
 // Children of every split node become the next level's open list (see
 // RoundBuffers::by_hess for which child is built directly).  Block 0 also
 // sets the next level's counts.
-__global__ void k_children(RoundBuffers b, int depth, int max_depth) {
+__global__ void k_children(RoundBuffers b, int depth, int max_depth, i64* zero, u64 slot_elems, u64 min_slots) {
   const u32 ns = b.ctr->n_split;
   const bool more = depth + 1 < max_depth;
   const bool fits = 2 * u64(ns) <= b.cap_next;
+  if (zero && more) {
+    // the next level's output slots (the parents this level read are done)
+    const u64 n2 = (ns > min_slots ? u64(ns) : min_slots) * slot_elems / 2;
+    longlong2* z = reinterpret_cast<longlong2*>(zero);
+    for (u64 k = u64(blockIdx.x) * blockDim.x + threadIdx.x; k < n2; k += u64(gridDim.x) * blockDim.x)
+      z[k] = make_longlong2(0, 0);
+  }
   if (blockIdx.x == 0 && threadIdx.x == 0) {
     b.ctr->n_open = fits ? 2 * ns : 0u;
     b.ctr->n_build = (more && fits) ? ns : 0u;
@@ -409,8 +414,9 @@ void launch_decide(const RoundBuffers& b, const float* cut, const u8* has_missin
   after_launch("decide");
 }
 
-void launch_children(const RoundBuffers& b, int depth, int max_depth, cudaStream_t s) {
-  k_children<<<sm_count(), 256, 0, s>>>(b, depth, max_depth);
+void launch_children(const RoundBuffers& b, int depth, int max_depth, cudaStream_t s, i64* zero, u64 slot_elems,
+                     u64 min_slots) {
+  k_children<<<sm_count() * (zero ? 4 : 1), 256, 0, s>>>(b, depth, max_depth, zero, slot_elems, min_slots);
   after_launch("children");
 }
 

@@ -223,4 +223,18 @@ void launch_eval_splits_dev(const i64* hist, u32 F, const u16* nbins, const u8* 
   }
 }
 
+void launch_eval_candidates_dev(const i64* hist, u32 F, const u16* nbins, const u8* has_missing,
+                                const EvalNode* nodes, const u32* nnodes_dev, const Scales* scales, SplitParams p,
+                                SplitCand* cand, u32 nchunks, cudaStream_t s, u32 fstride, u32 f_base,
+                                const u32* fmask, u32 mask_words, const i64* parent_hist, int store_derived) {
+  need(nchunks >= 1 && nchunks * kEvalFeatureChunk >= F, "candidate chunks do not cover the features");
+  int dev = 0, sms = 148;
+  DP_CUDA(cudaGetDevice(&dev));
+  DP_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  k_eval_dev<<<sms * 8, kEvalThreads, 0, s>>>(const_cast<i64*>(hist), F, nbins, has_missing, nodes, scales, p,
+                                               nchunks, nnodes_dev, cand, fstride ? fstride : F, f_base, fmask,
+                                               mask_words, parent_hist, store_derived);
+  after_launch("eval_splits");
+}
+
 }  // namespace dp

@@ -61,12 +61,12 @@ struct RoundBuffers {
   u32* triples_next;       // [3 * cap_split] (parent slot, small slot, large slot)
   HistTask* hist_tasks;    // [cap_hist_tasks]
   EvalNode* eval_nodes;    // [cap_split]
-  SplitCand* best;         // [cap_split]
-  // With several ranks: every rank's best per open node, [nranks][cap_split];
-  // the decision takes the best over ranks in rank order (rank order is
-  // feature order, so on equal gain the lower feature stays).
-  const SplitCand* gathered;
-  u32 nranks;
+  // Split candidates per (rank, open node, feature chunk),
+  // [nranks][cap_split][nchunks]; the decision takes the best in that order
+  // (rank order and chunk order are feature order, so on equal gain the
+  // lower feature stays).
+  const SplitCand* cands;
+  u32 nranks, nchunks;
   u32* split_idx;          // [cap_split]
   PartNode* part_nodes;    // [cap_split]
   PartTask* part_tasks;    // [cap_part_tasks]
@@ -95,7 +95,10 @@ void launch_zero_slots(const RoundBuffers& b, i64* hist, u64 slot_elems, u64 min
 // Splits (depth < max_depth, gain > 0) or closes every open node.
 void launch_decide(const RoundBuffers& b, const float* cut, const u8* has_missing, int depth, int max_depth,
                    int set, cudaStream_t s);
-void launch_children(const RoundBuffers& b, int depth, int max_depth, cudaStream_t s);
+// With zero set (and depth + 1 < max_depth), also zeroes max(n_split,
+// min_slots) slots of slot_elems int64 at zero: the next level's output.
+void launch_children(const RoundBuffers& b, int depth, int max_depth, cudaStream_t s, i64* zero = nullptr,
+                     u64 slot_elems = 0, u64 min_slots = 0);
 // Column sampling of this level: for every open node, the features that may
 // split it, as bits fmask[i * W + f / 32].  Nested exact-count selections
 // (the candidates with the smallest sample_hash, ties to the lower feature):
