@@ -187,8 +187,11 @@ def reference_arm(args) -> None:
     line = {
         "impl": "reference", "metric": "boosting rows*trees/s (config 4 step, 1 tree)", "value": value,
         "unit": "rows*trees/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * rows / value,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "u8 bins / int64 sums",
-        "data": "synthetic (seeded)", "config": {"workload": WORKLOAD, "rows": ROWS, "features": FEATURES},
+        "data": "synthetic (seeded)",
+        "config": {"workload": WORKLOAD, "rows": ROWS, "features": FEATURES, "max_depth": DEPTH, "max_bin": 256,
+                   "parallelism": f"CPU oracle on {threads} host threads; each step a {rows}-row sample"},
         "cpu_baseline": {"value": value, "unit": "rows*trees/s", "cores": threads, "kind": "port",
                          "sample": f"first {rows} rows of the config-4 data, one depth-10 tree per step "
                                    f"(C++ oracle, {threads} threads)"},
