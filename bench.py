@@ -352,12 +352,14 @@ def main() -> None:
     b = dp.Booster(PARAMS | {"device": f"cuda:{local}"}, [d])
     if comm is not None:
         b.set_comm(comm)
-    # profiling on from the start, so the warm-up rounds already capture the
-    # round graph with its timing events; enabling again resets the counters
-    b.set_profiling(True)
+    # timing events around the histogram launches only (the least
+    # instrumentation of the timed rounds), on from the start so that the
+    # warm-up rounds capture the round graph with them; enabling again resets
+    # the counters
+    b.set_profiling(True, histograms_only=True)
     for i in range(args.warmup):
         b.update(d, i)
-    b.set_profiling(True)
+    b.set_profiling(True, histograms_only=True)
     clocks = ClockSampler(torch, local)
     clocks.start()
     barrier()
@@ -373,11 +375,18 @@ def main() -> None:
     ms_local = ev0.elapsed_time(ev1)
     barrier()
     ms = max_over_ranks(ms_local)
-    prof = b.profile()
-    prof.pop("log", None)
-    host_ms = prof.pop("host_ms", None)
+    hist = b.profile().get("histograms", {"launches": 0, "ms": 0.0, "alg_bytes": 0.0})
+    # the per-kernel breakdown comes from a few more rounds with every launch
+    # timed, after the timed region
+    b.set_profiling(True)
+    breakdown_rounds = 3
+    for i in range(breakdown_rounds):
+        b.update(d, args.warmup + args.steps + i)
+    torch.cuda.synchronize()
+    prof = {k: {**v, "launches_per_round": v["launches"] / breakdown_rounds, "ms_per_round": v["ms"] / breakdown_rounds}
+            for k, v in b.profile().items() if isinstance(v, dict) and "ms" in v}
+    host_ms = b.profile().get("host_ms")
     value = args.rows * args.steps / (ms / 1e3)
-    hist = prof.get("histograms", {"launches": 0, "ms": 0.0, "alg_bytes": 0.0})
     hist_ms_per_launch = hist["ms"] / max(1, hist["launches"])
     achieved = hist["alg_bytes"] / max(1, hist["launches"]) / (hist_ms_per_launch / 1e3) / 1e9 if hist["ms"] else 0.0
     # DRAM bytes per histogram launch of this workload, from the committed ncu

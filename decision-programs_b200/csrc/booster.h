@@ -20,7 +20,7 @@ class Booster {
   TrainParams params;
   Model model;
   Comm* comm = nullptr;  // borrowed (dp_booster_set_comm)
-  bool profiling = false;
+  int profiling = 0;  // profiler mode (see Profiler::enable)
 
   void set_param(const std::string& key, const std::string& value);
   void update_one_iter(int iter, DMatrix* d);

@@ -393,7 +393,8 @@ int dp_booster_set_comm(BoosterHandle handle, void* comm) {
 int dp_booster_set_profiling(BoosterHandle handle, int on) {
   DP_API_BEGIN();
   dp::Booster* b = as_booster(handle);
-  b->profiling = on != 0;
+  need(on >= 0 && on <= 2, "profiling mode must be 0, 1 or 2");
+  b->profiling = on;
   if (b->engine()) {
     b->engine()->profiler().enable(b->profiling);
     if (b->profiling) b->engine()->profiler().reset();

@@ -25,7 +25,8 @@ void Profiler::record(cudaEvent_t e, cudaStream_t s) {
   else DP_CUDA(cudaEventRecord(e, s));
 }
 int Profiler::begin(cudaStream_t s, const char* name, double alg_bytes) {
-  if (!on_) return -1;
+  open_ = mode_ == 1 || (mode_ == 2 && std::strcmp(name, "histograms") == 0);
+  if (!open_) return -1;
   Pending p{take(), take(), name, alg_bytes};
   record(p.a, s);
   pending_.push_back(p);
@@ -36,7 +37,8 @@ void Profiler::set_bytes(int idx, double alg_bytes) {
   if (idx >= 0 && size_t(idx) < v.size()) v[idx].bytes = alg_bytes;
 }
 void Profiler::end(cudaStream_t s) {
-  if (!on_) return;
+  if (!open_) return;
+  open_ = false;
   record(pending_.back().b, s);
 }
 bool Profiler::accumulate(const Pending& p) {
@@ -436,7 +438,7 @@ void Engine::boost_round(Model& m) {
     DP_CUDA(cudaMemcpyAsync(round_dev_.get(), r_h, sizeof(u32), cudaMemcpyHostToDevice, stream_));
   }
   RoundOut out;
-  if (graphable && graph_exec_ && graph_prof_ == prof_.enabled()) {
+  if (graphable && graph_exec_ && graph_prof_ == prof_.mode()) {
     DP_CUDA(cudaGraphLaunch(graph_exec_, stream_));
     count_launch(graph_launches_);
     prof_.graph_round();
@@ -462,7 +464,7 @@ void Engine::boost_round(Model& m) {
     if (captured && cudaGraphInstantiate(&graph_exec_, graph_, 0) == cudaSuccess) {
       prof_.finish_capture();
       graph_launches_ = n;
-      graph_prof_ = prof_.enabled();
+      graph_prof_ = prof_.mode();
       graph_out_ = out;
       DP_CUDA(cudaGraphLaunch(graph_exec_, stream_));
       count_launch(graph_launches_);

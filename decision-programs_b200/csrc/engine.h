@@ -23,8 +23,11 @@ namespace dp {
 // Per-kernel timing with CUDA events on the engine's stream.
 class Profiler {
  public:
-  void enable(bool on) { on_ = on; }
-  bool enabled() const { return on_; }
+  // Mode 0: off; 1: every timed launch; 2: histogram launches only (the
+  // cheapest instrumentation of a timed round).
+  void enable(int mode) { mode_ = mode; }
+  bool enabled() const { return mode_ != 0; }
+  int mode() const { return mode_; }
   // Returns the launch's index for set_bytes (-1 when disabled).
   int begin(cudaStream_t s, const char* name, double alg_bytes);
   // Graph capture: launches timed between start_capture and finish_capture
@@ -57,7 +60,8 @@ class Profiler {
  private:
   struct Pending { cudaEvent_t a, b; std::string name; double bytes; };
   struct Stat { u64 launches = 0; double ms = 0.0; double bytes = 0.0; };
-  bool on_ = false;
+  int mode_ = 0;
+  bool open_ = false;  // the last begin() recorded an event
   bool capturing_ = false, graph_round_ = false, graph_timing_failed_ = false;
   void record(cudaEvent_t e, cudaStream_t s);
   bool accumulate(const Pending& p);
@@ -182,7 +186,7 @@ class Engine {
   bool capturing_ = false;
   cudaGraph_t graph_ = nullptr;
   cudaGraphExec_t graph_exec_ = nullptr;
-  bool graph_prof_ = false;
+  int graph_prof_ = 0;  // profiler mode the graph was captured with
   u64 graph_launches_ = 0;
   RoundOut graph_out_;
   u64 rounds_ = 0;

@@ -269,8 +269,11 @@ class Booster:
     def set_comm(self, comm: "Comm") -> None:
         check(lib().dp_booster_set_comm(self.handle, comm.handle))
 
-    def set_profiling(self, on: bool) -> None:
-        check(lib().dp_booster_set_profiling(self.handle, int(on)))
+    def set_profiling(self, on, histograms_only: bool = False) -> None:
+        """Mode 1 (on=True): every instrumented launch; histograms_only: mode 2;
+        on=False: off.  Enabling resets the counters."""
+        mode = 0 if not on else (2 if histograms_only else 1)
+        check(lib().dp_booster_set_profiling(self.handle, mode))
 
     def profile(self) -> dict:
         p = C.c_char_p()

@@ -140,7 +140,10 @@ DP_API int dp_comm_free(void* comm);
 DP_API int dp_booster_set_comm(BoosterHandle handle, void* comm);
 
 /* Per-kernel CUDA-event timings of the training rounds ({"name":{"launches",
- * "ms","alg_bytes"}}), collected on the launching stream while enabled. */
+ * "ms","alg_bytes"}}), collected on the launching stream while enabled:
+ * mode 1 times every instrumented launch, mode 2 only the histogram launches
+ * (the least instrumentation), 0 turns timing off.  Enabling resets the
+ * counters. */
 DP_API int dp_booster_set_profiling(BoosterHandle handle, int on);
 DP_API int dp_booster_profile(BoosterHandle handle, const char** out_json);
 
