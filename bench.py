@@ -387,6 +387,19 @@ def main() -> None:
             for k, v in b.profile().items() if isinstance(v, dict) and "ms" in v}
     host_ms = b.profile().get("host_ms")
     value = args.rows * args.steps / (ms / 1e3)
+    # NVLink: bytes this rank sends in the histogram reduce-scatter ((G-1)/G of
+    # its partial histograms) over the exchange's event time, against the
+    # measured peer-copy rate per direction (770 GB/s on this pool)
+    nvlink = None
+    if world > 1 and "exchange_hist" in prof:
+        ex = prof["exchange_hist"]
+        sent = ex["alg_bytes"] * (world - 1) / world
+        nvlink = {"collective": "reduce-scatter of int64 histograms + all-gather of split candidates",
+                  "bytes_per_round_per_rank": sent / breakdown_rounds,
+                  "achieved_GBps": sent / (ex["ms"] / 1e3) / 1e9 if ex["ms"] else 0.0,
+                  "peak_GBps": 770.0, "peak_source": "measured peer copy per direction (profiling recipe)",
+                  "frac": (sent / (ex["ms"] / 1e3) / 1e9 / 770.0) if ex["ms"] else 0.0,
+                  "note": "exchange time includes waiting for the slowest rank's histogram"}
     hist_ms_per_launch = hist["ms"] / max(1, hist["launches"])
     achieved = hist["alg_bytes"] / max(1, hist["launches"]) / (hist_ms_per_launch / 1e3) / 1e9 if hist["ms"] else 0.0
     # DRAM bytes per histogram launch of this workload, from the committed ncu
@@ -441,6 +454,7 @@ def main() -> None:
         "gpu_launches": launches,
         "clocks": clk,
         "kernel_profile": prof,
+        "nvlink": nvlink,
         "host_ms": host_ms,
         "model_bytes": model_bytes,
     }
