@@ -200,6 +200,146 @@ def reference_arm(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+# --------------------------------------------------------------------------- configs 1-3
+def c1_data(torch, device):
+    """Config 1: 20,000 x 16 N(0,1); y = 1[x0 + 0.5 x1 x2 + N(0, 0.3) > 0]."""
+    g = torch.Generator(device=device)
+    g.manual_seed(SEED + 1)
+    x = torch.randn((20_000, 16), device=device, generator=g)
+    noise = 0.3 * torch.randn(20_000, device=device, generator=g)
+    y = ((x[:, 0] + 0.5 * x[:, 1] * x[:, 2] + noise) > 0).float()
+    return x.contiguous(), y
+
+
+def c2_data(torch, device):
+    """Config 2: 1,000,000 x 64 (32 columns N(0,1), 32 Uniform(0,1)); label =
+    sign of a seeded sparse linear-plus-pairwise teacher (centred at its
+    median), 10% of labels flipped."""
+    R = 1_000_000
+    g = torch.Generator(device=device)
+    g.manual_seed(SEED + 2)
+    x = torch.cat([torch.randn((R, 32), device=device, generator=g),
+                   torch.rand((R, 32), device=device, generator=g)], 1).contiguous()
+    rs = np.random.RandomState(SEED + 2)
+    lin = rs.choice(64, 12, replace=False)
+    w = rs.normal(0.0, 1.0, 12)
+    pairs = rs.choice(64, (6, 2))
+    c = rs.normal(0.0, 1.0, 6)
+    score = torch.zeros(R, device=device)
+    for f, wf in zip(lin, w):
+        score += float(wf) * x[:, int(f)]
+    for (i, j), cf in zip(pairs, c):
+        score += float(cf) * x[:, int(i)] * x[:, int(j)]
+    y = (score > score.median()).float()
+    flip = torch.rand(R, device=device, generator=g) < 0.1
+    y = torch.where(flip, 1.0 - y, y)
+    return x, y.contiguous()
+
+
+def c3_data(torch, device):
+    """Config 3 (MNIST-shaped, synthetic): 60,000 x 784 uint8 values, 80%
+    zeros, non-zeros Uniform{1..255}; 10 classes = argmax of a seeded linear
+    teacher on the features.  Values go in as fp32 (integers 0..255)."""
+    R, F = 60_000, 784
+    g = torch.Generator(device=device)
+    g.manual_seed(SEED + 3)
+    nz = torch.rand((R, F), device=device, generator=g) < 0.2
+    v = torch.randint(1, 256, (R, F), device=device, generator=g).float()
+    x = torch.where(nz, v, torch.zeros((), device=device)).contiguous()
+    w = torch.randn((F, 10), device=device, generator=g)
+    y = torch.argmax(x @ w, 1).float().contiguous()
+    return x, y
+
+
+CONFIGS = [
+    ("config1", c1_data, {"objective": "binary:logistic", "max_depth": 4}, 20, 1),
+    ("config2", c2_data, {"objective": "binary:logistic", "max_depth": 8}, 100, 1),
+    ("config3", c3_data, {"objective": "multi:softprob", "num_class": 10, "max_depth": 6}, 50, 10),
+]
+# rounds of each config that the CPU oracle times (config 1 in full)
+CPU_ROUNDS = {"config1": 20, "config2": 10, "config3": 2}
+
+
+def same_trees(gpu_trees: list[dict], o) -> bool:
+    """Field-by-field equality of the library's trees and the oracle's
+    (structure, features, default directions exact; fp32 fields bit-exact)."""
+    if len(gpu_trees) != o.num_trees():
+        return False
+    for i, t in enumerate(gpu_trees):
+        ot = o.tree(i)
+        for f in ("left_children", "right_children", "split_indices", "default_left"):
+            if not np.array_equal(np.array(t[f], np.int64), ot[f].astype(np.int64)):
+                return False
+        for f in ("split_conditions", "base_weights", "loss_changes", "sum_hessian"):
+            if not np.array_equal(np.array(t[f], np.float32).view(np.uint32), ot[f].view(np.uint32)):
+                return False
+    return True
+
+
+def config_runs(torch, dp, device, peak_gbs: float, threads: int, cpu: bool) -> list[dict]:
+    """Configs 1-3 at full size on one GPU: one whole training run (every
+    round, from a new booster; the DMatrix built before) timed with CUDA events
+    after an identical untimed run; inputs resident in HBM.  Beside each, the
+    CPU oracle on the same data (config 1 in full, configs 2-3 for their first
+    rounds), and for config 1 whether the trees are identical."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    out = []
+    for name, make, hp, rounds, K in CONFIGS:
+        x, y = make(torch, device)
+        R, F = x.shape
+        params = {"tree_method": "hist", "max_bin": 256, "eta": 0.3, "lambda": 1.0, "min_child_weight": 1.0,
+                  "device": f"cuda:{device.index or 0}"} | hp
+        t0 = time.perf_counter()
+        d = dp.DMatrix.from_torch(x, y)
+        torch.cuda.synchronize()
+        dmatrix_ms = 1e3 * (time.perf_counter() - t0)
+        for timed in (False, True):
+            b = dp.Booster(params, [d])
+            b.set_profiling(True, histograms_only=True)
+            ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize()
+            ev0.record()
+            for i in range(rounds):
+                b.update(d, i)
+            ev1.record()
+            torch.cuda.synchronize()
+            if not timed:
+                b.free()
+        ms = ev0.elapsed_time(ev1)
+        hist = b.profile().get("histograms", {"launches": 0, "ms": 0.0, "alg_bytes": 0.0})
+        trees = b.trees() if name == "config1" else None
+        b.free()
+        d.free()
+        line = {"config": name, "rows": R, "features": F, "max_depth": hp["max_depth"], "rounds": rounds,
+                "trees_per_round": K, "objective": hp["objective"], "ms_total": ms,
+                "ms_per_tree": ms / (rounds * K), "rows_trees_per_s": R * rounds * K / (ms / 1e3),
+                "dmatrix_ms": dmatrix_ms,
+                "histograms": {"launches": hist["launches"], "ms": hist["ms"],
+                               "GBps": hist["alg_bytes"] / (hist["ms"] / 1e3) / 1e9 if hist["ms"] else 0.0,
+                               "frac_hbm": (hist["alg_bytes"] / (hist["ms"] / 1e3) / 1e9 / peak_gbs)
+                               if hist["ms"] else 0.0}}
+        if name == "config3":
+            line["l2_note"] = "47 MB of bins fit in the 126 MB L2: GB/s is HBM-equivalent"
+        if cpu:
+            import oracle
+            xc, yc = x.cpu().numpy(), y.cpu().numpy()
+            cr = CPU_ROUNDS[name]
+            m = oracle.Model(xc, yc, hp["objective"], num_class=K, max_depth=hp["max_depth"], max_bin=256, eta=0.3,
+                             rounds=0, threads=threads)
+            t1 = time.perf_counter()
+            m.train_more(cr)
+            dt = time.perf_counter() - t1
+            line["cpu_oracle"] = {"rounds": cr, "seconds": dt, "rows_trees_per_s": R * cr * K / dt,
+                                  "cores": threads}
+            if trees is not None:
+                line["trees_identical_to_oracle"] = same_trees(trees, m)
+            del m
+        del x, y
+        out.append(line)
+        torch.cuda.empty_cache()
+    return out
+
+
 # --------------------------------------------------------------------------- histogram sweep (config 5)
 def hist_sweep(torch, dp, device, peak_gbs: float) -> list[dict]:
     R, F = 100_000_000, 32
@@ -289,6 +429,7 @@ def main() -> None:
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-configs", action="store_true", help="skip the config 1-3 runs")
     ap.add_argument("--rows", type=int, default=ROWS,
                     help="total rows (default: config 4's 10M; smaller for profiler captures)")
     ap.add_argument("--hist-case", default=None,
@@ -386,6 +527,7 @@ def main() -> None:
     prof = {k: {**v, "launches_per_round": v["launches"] / breakdown_rounds, "ms_per_round": v["ms"] / breakdown_rounds}
             for k, v in b.profile().items() if isinstance(v, dict) and "ms" in v}
     host_ms = b.profile().get("host_ms")
+    levels = per_level(b.profile().get("log", []))
     value = args.rows * args.steps / (ms / 1e3)
     # NVLink: bytes this rank sends in the histogram reduce-scatter ((G-1)/G of
     # its partial histograms) over the exchange's event time, against the
@@ -422,14 +564,17 @@ def main() -> None:
 
     sweep = None
     cpu = None
+    configs = None
     if rank == 0 and world == 1:
+        if not args.no_configs:
+            configs = config_runs(torch, dp, device, peak_gbs, len(os.sched_getaffinity(0)), not args.no_cpu)
         if not args.no_sweep:
             sweep = hist_sweep(torch, dp, device, peak_gbs)
         if not args.no_cpu:
             threads = len(os.sched_getaffinity(0))
-            r = cpu_oracle_run(500_000, 1, threads)
+            r = cpu_oracle_run(4_000_000, 8, threads)
             cpu = {"value": r["value"], "unit": "rows*trees/s", "cores": threads, "kind": "port",
-                   "sample": f"first 500000 rows of the config-4 data, one depth-10 tree "
+                   "sample": f"first 4000000 rows of the config-4 data, eight depth-10 trees "
                              f"(C++ oracle, {threads} threads, {r['seconds']:.1f} s)"}
     if comm is not None:
         comm.free()
@@ -451,10 +596,12 @@ def main() -> None:
                      "frac": achieved / peak_gbs, "traffic": traffic, "kernel": "k_hist",
                      "peak_source": "measured" if not peaks.get("fallback") else "fallback",
                      "launches": hist["launches"], "ms_per_launch": hist_ms_per_launch},
+        "rows_features_per_s": value * FEATURES,
         "gpu_launches": launches,
         "clocks": clk,
         "kernel_profile": prof,
         "nvlink": nvlink,
+        "levels_last_round": levels,
         "host_ms": host_ms,
         "model_bytes": model_bytes,
     }
@@ -462,7 +609,25 @@ def main() -> None:
         line["cpu_baseline"] = cpu
     if sweep is not None:
         line["hist_sweep"] = sweep
+    if configs is not None:
+        line["configs"] = configs
     print(json.dumps(line), flush=True)
+
+
+def per_level(log: list) -> list[dict]:
+    """Per-depth device times (ms) of the last profiled round, from the
+    profiler's launch log [name, ms, bytes] in launch order: a round starts at
+    'gradients' and every 'histograms' entry starts a level."""
+    starts = [i for i, e in enumerate(log) if e[0] == "gradients"]
+    if not starts:
+        return []
+    levels: list[dict] = []
+    for name, ms, _ in log[starts[-1]:]:
+        if name == "histograms":
+            levels.append({})
+        if levels:
+            levels[-1][name] = round(levels[-1].get(name, 0.0) + ms, 4)
+    return levels
 
 
 def end_to_end(torch, dp, x, y, args, local, comm, barrier, max_over_ranks, world) -> dict:

@@ -216,7 +216,8 @@ class Model:
         return self
 
     def __del__(self):
-        if getattr(self, "h", None):
+        # at interpreter exit the module globals may already be gone
+        if getattr(self, "h", None) and lib is not None:
             lib().orc_free(self.h)
             self.h = None
 
