@@ -46,6 +46,7 @@ __device__ __forceinline__ void eval_item(u32 w, i64* hist, u32 F, const u16* __
                                           const u32* __restrict__ fmask, u32 mask_words,
                                           const i64* __restrict__ parent, int store_derived) {
   __shared__ Best wbest[kEvalThreads / 32];
+  __shared__ longlong2 stage[kEvalThreads / 32][kMaxBins];  // one 4 KB transpose stage per warp
   const u32 node = w / nchunks, chunk = w % nchunks;
   const EvalNode nd = nodes[node];
   const Scales sc = scales[nd.tree];
@@ -58,33 +59,53 @@ __device__ __forceinline__ void eval_item(u32 w, i64* hist, u32 F, const u16* __
   for (u32 f = chunk * kEvalFeatureChunk + warp; f < f_end; f += kEvalThreads / 32) {
     const int nb = nbins[f];
     if (nb < 2) continue;
-    // lane l holds bins [8l, 8l + 8); a derived sibling is parent - built
-    // sibling, stored for the next level whatever this node's feature mask
+    // Coalesced loads (lane l takes bins 32j + l), a derived sibling formed
+    // and stored in that order (parent - built sibling, stored for the next
+    // level whatever this node's feature mask), then a transpose through the
+    // warp's shared-memory stage so that lane l holds bins [8l, 8l + 8) for
+    // the scan.  The stage is swizzled (16-byte chunk c at c ^ ((c >> 3) & 7))
+    // so that both the row-wise writes and the column-wise reads of eight
+    // consecutive lanes hit eight distinct bank groups.
     i64* hf = hist + (u64(nd.slot) * fstride + f) * (2 * kMaxBins);
     longlong2 x[8];
     if (nd.par != kNoSlot) {
       const longlong2* pv =
-          reinterpret_cast<const longlong2*>(parent + (u64(nd.par) * fstride + f) * (2 * kMaxBins)) + 8 * lane;
+          reinterpret_cast<const longlong2*>(parent + (u64(nd.par) * fstride + f) * (2 * kMaxBins)) + lane;
       const longlong2* sv =
-          reinterpret_cast<const longlong2*>(hist + (u64(nd.small) * fstride + f) * (2 * kMaxBins)) + 8 * lane;
+          reinterpret_cast<const longlong2*>(hist + (u64(nd.small) * fstride + f) * (2 * kMaxBins)) + lane;
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        const longlong2 a = pv[j], b = sv[j];
+        const longlong2 a = pv[32 * j], b = sv[32 * j];
         x[j] = make_longlong2(a.x - b.x, a.y - b.y);
       }
       if (store_derived) {
-        longlong2* dv = reinterpret_cast<longlong2*>(hf) + 8 * lane;
+        longlong2* dv = reinterpret_cast<longlong2*>(hf) + lane;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) dv[j] = x[j];
+        for (int j = 0; j < 8; ++j) dv[32 * j] = x[j];
       }
     } else {
-      const longlong2* v = reinterpret_cast<const longlong2*>(hf) + 8 * lane;
+      const longlong2* v = reinterpret_cast<const longlong2*>(hf) + lane;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) x[j] = v[j];
+      for (int j = 0; j < 8; ++j) x[j] = v[32 * j];
     }
     if (fmask) {
       const u32 gf = f_base + f;
       if (!((fmask[u64(node) * mask_words + (gf >> 5)] >> (gf & 31u)) & 1u)) continue;
+    }
+    {
+      longlong2* st = stage[warp];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const u32 c = 32u * j + u32(lane);
+        st[c ^ ((c >> 3) & 7u)] = x[j];
+      }
+      __syncwarp();
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const u32 c = 8u * u32(lane) + j;
+        x[j] = st[c ^ ((c >> 3) & 7u)];
+      }
+      __syncwarp();  // the stage is rewritten by the warp's next feature
     }
     const bool hm = has_missing[f] != 0;
     // the missing code is bin 255: lane 31's last pair

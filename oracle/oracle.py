@@ -183,6 +183,7 @@ class Model:
         self.R, self.F = R, F
         K = num_class if objective.startswith("multi:") else 1
         self.K = K
+        self.objective = objective
         sampling = (subsample, colsample_bytree, colsample_bylevel, colsample_bynode) != (1.0, 1.0, 1.0, 1.0)
         self.h = lib().orc_train(_p(self.x), R, F, F, _p(self.y), OBJECTIVES[objective], K, max_depth, max_bin,
                                  eta, reg_lambda, alpha, gamma, min_child_weight, base_margin,
@@ -207,6 +208,7 @@ class Model:
         self.R, self.F = R, F
         K = num_class if objective.startswith("multi:") else 1
         self.K = K
+        self.objective = objective
         self._cb = _callback(allreduce)
         self.h = lib().orc_train_sharded(_p(self.x), R, F, F, _p(self.y), OBJECTIVES[objective], K, max_depth,
                                          max_bin, eta, reg_lambda, alpha, gamma, min_child_weight, base_margin,
@@ -244,10 +246,14 @@ class Model:
     def predict(self, x: np.ndarray, margin: bool = False, iteration_begin: int = 0, iteration_end: int = 0,
                 missing: float = float("nan"), objective: str = None) -> np.ndarray:
         """Predictions of the trained ensemble: margins [R, K] (margin=True) or
-        the objective's output ([R, K] probabilities for softprob, else [R])."""
+        the objective's output ([R, K] probabilities for softprob, else [R]).
+        The transform is the trained model's objective; `objective` only
+        states it and must agree."""
         x = np.ascontiguousarray(x, dtype=np.float32)
         R = x.shape[0]
-        softprob = objective == "multi:softprob"
+        if objective is not None and objective != self.objective:
+            raise ValueError(f"model objective is {self.objective}, not {objective}")
+        softprob = self.objective == "multi:softprob"
         width = self.K if (margin or softprob) else 1
         out = np.zeros((R, width), np.float32)
         has_mv = not np.isnan(missing)

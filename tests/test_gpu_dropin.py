@@ -102,3 +102,62 @@ def test_reference_converter_reads_gpu_trained_models(dp, orc, tmp_path):
         trees.append(t)
     check_against_trees(doc, trees, K)
     assert doc["features"] == F
+
+
+RESIDENT = ROOT / "oracle" / "_ref" / "ref_resident"
+
+
+@pytest.mark.skipif(not RESIDENT.exists(), reason="reference resident trainer not built (needs the reference sources)")
+def test_reference_resident_trainer_lifecycle(orc, tmp_path):
+    """The reference's resident trainer (native/class_study_train.cu, built
+    unmodified with the harness oracle/ref_resident.cpp) trains through
+    libdp_gbdt.so, predicts classes, margins and probabilities from device
+    memory, slices a round prefix (XGBoosterSlice) and restores the full model
+    from its buffer (XGBoosterLoadModelFromBuffer); its own checks on shapes,
+    device output, configuration and round counts run on every call.  Models
+    and predictions must equal the oracle's bit for bit."""
+    rng = np.random.default_rng(57)
+    R, F, K, rounds, cut = 4000, 7, 4, 5, 2
+    x = rng.standard_normal((R, F)).astype(np.float32)
+    x[rng.random((R, F)) < 0.04] = np.nan
+    y = np.argmax(np.nan_to_num(x[:, :K]) + 0.3 * rng.standard_normal((R, K)), 1).astype(np.uint32)
+    (tmp_path / "values.f32").write_bytes(x.astype("<f4").tobytes())
+    (tmp_path / "labels.u32").write_bytes(y.astype("<u4").tobytes())
+    (tmp_path / "meta.json").write_text(json.dumps({"rows": R, "features": F, "classes": K, "rounds": rounds,
+                                                    "max_depth": 4, "slice_rounds": cut}))
+    r = subprocess.run([str(RESIDENT), str(LIB), sha(LIB), str(tmp_path)], capture_output=True, text=True,
+                       timeout=300)
+    assert r.returncode == 0, r.stderr + r.stdout
+
+    def f32(name, shape):
+        return np.fromfile(tmp_path / name, dtype="<f4").reshape(shape)
+
+    o = orc.Model(x, y.astype(np.float32), "multi:softmax", num_class=K, max_depth=4, max_bin=256, eta=0.3,
+                  rounds=rounds, threads=4)
+    bits = lambda a: np.ascontiguousarray(a, np.float32).view(np.uint32)  # noqa: E731
+    model = json.loads((tmp_path / "model.json").read_text())
+    trees = model["learner"]["gradient_booster"]["model"]["trees"]
+    assert len(trees) == o.num_trees() == rounds * K
+    for i, t in enumerate(trees):
+        ot = o.tree(i)
+        for f in ["left_children", "right_children", "split_indices"]:
+            np.testing.assert_array_equal(np.array(t[f]), ot[f])
+        np.testing.assert_array_equal(bits(t["split_conditions"]), bits(ot["split_conditions"]))
+    margins = o.predict(x, margin=True)
+    np.testing.assert_array_equal(bits(f32("margins.f32", (R, K))), bits(margins))
+    np.testing.assert_array_equal(bits(f32("restored_margins.f32", (R, K))), bits(margins))
+    np.testing.assert_array_equal(f32("classes.f32", (R,)), o.predict(x, objective="multi:softmax").reshape(R))
+    # the probability view is the same trees under multi:softprob
+    op = orc.Model(x, y.astype(np.float32), "multi:softprob", num_class=K, max_depth=4, max_bin=256, eta=0.3,
+                   rounds=rounds, threads=4)
+    np.testing.assert_array_equal(bits(f32("probs.f32", (R, K))), bits(op.predict(x)))
+    # the slice keeps the first `cut` rounds: its trees and margins
+    sliced = json.loads((tmp_path / "slice.json").read_text())["learner"]["gradient_booster"]["model"]
+    assert len(sliced["trees"]) == cut * K and sliced["gbtree_model_param"]["num_trees"] == str(cut * K)
+    for a, b in zip(sliced["trees"], trees[:cut * K]):
+        assert a["split_conditions"] == b["split_conditions"] and a["split_indices"] == b["split_indices"]
+    np.testing.assert_array_equal(bits(f32("slice_margins.f32", (R, K))),
+                                  bits(o.predict(x, margin=True, iteration_end=cut)))
+    session = json.loads((tmp_path / "session.json").read_text())
+    assert session["train_metrics"]["CUDA_training"] is True
+    assert session["slice_metrics"]["FIT_performed"] is False
