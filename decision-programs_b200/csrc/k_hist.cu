@@ -55,6 +55,24 @@ struct HistArgs {
   HistLayout layout;
 };
 
+// 16 bytes of a row's bin codes.  With `line` the load also asks L2 to fetch
+// the whole 128-byte line: when rows are whole lines (row stride a multiple
+// of 128 bytes) the line holds this row's other feature tiles, which the
+// tasks of the same piece (queued next to this one) read at about the same
+// time, so DRAM serves one line instead of four separate 32-byte sectors.
+__device__ __forceinline__ uint4 load_codes(const u8* p, bool line) {
+#ifndef DP_HIST_NO_LINE_FETCH
+  if (line) {
+    uint4 v;
+    asm volatile("ld.global.nc.L2::128B.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+  }
+#endif
+  return __ldg(reinterpret_cast<const uint4*>(p));
+}
+
 template <bool QUANT>
 __device__ __forceinline__ void load_q(const TreeArrays& ta, const Scales& sc, u32 i, u32& gq, u32& hq) {
   if (QUANT) {
@@ -178,6 +196,7 @@ __global__ void __launch_bounds__(THREADS) k_hist(HistArgs a) {
     if (!QUANT) sc = a.scales[t.tree];
     // halves past the row's bin_stride (last tile of a row) are never read
     const bool qvalid = u64(t.f0) + h16 < a.bstride;
+    const bool line_rows = (a.bstride & 127u) == 0;
     const u8* base = a.bins + t.f0 + h16;
     u32 pos = u32(t.begin);
     const u32 tend = u32(t.end);
@@ -199,7 +218,7 @@ __global__ void __launch_bounds__(THREADS) k_hist(HistArgs a) {
           gq[u] = 0u;
           hq[u] = 0u;
           if (row[u] != kNoRow) {
-            v[u] = __ldg(reinterpret_cast<const uint4*>(base + u64(row[u]) * a.bstride));
+            v[u] = load_codes(base + u64(row[u]) * a.bstride, line_rows);
             load_q<QUANT>(ta, sc, i0 + u * kStep, gq[u], hq[u]);
           }
         }
