@@ -341,7 +341,7 @@ def config_runs(torch, dp, device, peak_gbs: float, threads: int, cpu: bool) -> 
 
 
 # --------------------------------------------------------------------------- histogram sweep (config 5)
-def hist_sweep(torch, dp, device, peak_gbs: float) -> list[dict]:
+def hist_sweep(torch, dp, device, peak_gbs: float, atomic_ceiling: float) -> list[dict]:
     R, F = 100_000_000, 32
     out = []
     g = torch.Generator(device=device)
@@ -380,7 +380,8 @@ def hist_sweep(torch, dp, device, peak_gbs: float) -> list[dict]:
             alg = R * (F + 12) + N * F * 256 * 16
             out.append({"bins": B, "nodes": N, "ms": round(ms, 4), "GB/s": round(alg / ms / 1e6, 1),
                         "frac_hbm": round(alg / ms / 1e6 / peak_gbs, 3),
-                        "rows_features_per_s": R * F / (ms / 1e3)})
+                        "rows_features_per_s": R * F / (ms / 1e3),
+                        "frac_atomic_ceiling": round(R * F / (ms / 1e3) / atomic_ceiling, 3) if atomic_ceiling else None})
             del ridx, ghp, hist
         del bins
     del gh
@@ -488,6 +489,11 @@ def main() -> None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
+    # ---- the histogram kernel's shared-atomic ceiling on this GPU (its bound)
+    ceiling = dp.C.c_double(0.0)
+    dp.check(dp.lib().dp_probe_hist_atomics(20000, dp.C.byref(ceiling), None))
+    torch.cuda.synchronize()
+
     # ---- device-resident timing
     d = dp.DMatrix.from_torch(x, y)
     b = dp.Booster(PARAMS | {"device": f"cuda:{local}"}, [d])
@@ -542,6 +548,12 @@ def main() -> None:
                   "peak_GBps": 770.0, "peak_source": "measured peer copy per direction (profiling recipe)",
                   "frac": (sent / (ex["ms"] / 1e3) / 1e9 / 770.0) if ex["ms"] else 0.0,
                   "note": "exchange time includes waiting for the slowest rank's histogram"}
+    hist_pairs_per_s = hist.get("units", 0.0) / (hist["ms"] / 1e3) if hist["ms"] else 0.0
+    atomic_roofline = {"kernel": "k_hist", "unit": "(row, feature) pairs/s", "achieved": hist_pairs_per_s,
+                       "ceiling": ceiling.value, "frac": hist_pairs_per_s / ceiling.value if ceiling.value else 0.0,
+                       "ceiling_source": "dp_probe_hist_atomics: the kernel's shared-memory update loop alone "
+                                         "(two 32-bit atomics per pair, one 1024-thread block per SM), "
+                                         "measured in this run"}
     hist_ms_per_launch = hist["ms"] / max(1, hist["launches"])
     achieved = hist["alg_bytes"] / max(1, hist["launches"]) / (hist_ms_per_launch / 1e3) / 1e9 if hist["ms"] else 0.0
     # DRAM bytes per histogram launch of this workload, from the committed ncu
@@ -569,7 +581,7 @@ def main() -> None:
         if not args.no_configs:
             configs = config_runs(torch, dp, device, peak_gbs, len(os.sched_getaffinity(0)), not args.no_cpu)
         if not args.no_sweep:
-            sweep = hist_sweep(torch, dp, device, peak_gbs)
+            sweep = hist_sweep(torch, dp, device, peak_gbs, ceiling.value)
         if not args.no_cpu:
             threads = len(os.sched_getaffinity(0))
             r = cpu_oracle_run(4_000_000, 8, threads)
@@ -597,6 +609,7 @@ def main() -> None:
                      "peak_source": "measured" if not peaks.get("fallback") else "fallback",
                      "launches": hist["launches"], "ms_per_launch": hist_ms_per_launch},
         "rows_features_per_s": value * FEATURES,
+        "atomic_roofline": atomic_roofline,
         "gpu_launches": launches,
         "clocks": clk,
         "kernel_profile": prof,

@@ -36,6 +36,10 @@ void Profiler::set_bytes(int idx, double alg_bytes) {
   std::vector<Pending>& v = graph_round_ ? graph_pending_ : pending_;
   if (idx >= 0 && size_t(idx) < v.size()) v[idx].bytes = alg_bytes;
 }
+void Profiler::set_units(int idx, double units) {
+  std::vector<Pending>& v = graph_round_ ? graph_pending_ : pending_;
+  if (idx >= 0 && size_t(idx) < v.size()) v[idx].units = units;
+}
 void Profiler::end(cudaStream_t s) {
   if (!open_) return;
   open_ = false;
@@ -52,6 +56,7 @@ bool Profiler::accumulate(const Pending& p) {
   st.launches += 1;
   st.ms += ms;
   st.bytes += p.bytes;
+  st.units += p.units;
   if (log_.size() >= 4096) log_.erase(log_.begin(), log_.begin() + 2048);
   log_.push_back(Entry{p.name, ms, p.bytes});
   return true;
@@ -93,7 +98,7 @@ std::string Profiler::json() const {
     if (!first) o << ",";
     first = false;
     o << "\"" << kv.first << "\":{\"launches\":" << kv.second.launches << ",\"ms\":" << kv.second.ms
-      << ",\"alg_bytes\":" << kv.second.bytes << "}";
+      << ",\"alg_bytes\":" << kv.second.bytes << ",\"units\":" << kv.second.units << "}";
   }
   // host phases: {name: [count, ms]}
   o << (first ? "" : ",") << "\"host_ms\":{";
@@ -683,6 +688,7 @@ void Engine::finish_round(Model& m, const RoundOut& out) {
     const LevelStats& st = st_h[d];
     prof_.set_bytes(out.pi_hist[d], double(st.rows_built) * (double(F) + 12.0) +
                                         double(st.n_build) * double(F) * kMaxBins * 16.0);
+    prof_.set_units(out.pi_hist[d], double(st.rows_built) * double(F));
     // built nodes read once; a derived sibling reads parent and sibling and
     // (before the last level) writes itself
     const double derived = d > 0 ? double(st.n_open - st.n_build) : 0.0;

@@ -45,6 +45,8 @@ class Profiler {
   bool graph_timing_failed() const { return graph_timing_failed_; }
   // Algorithmic bytes of a launch known only after it ran (before resolve()).
   void set_bytes(int idx, double alg_bytes);
+  // Work units of a launch (histograms: (row, feature) pairs), known after it ran.
+  void set_units(int idx, double units);
   void end(cudaStream_t s);
   void resolve();  // after the stream has been synchronised
   std::string json() const;
@@ -58,8 +60,8 @@ class Profiler {
   ~Profiler();
 
  private:
-  struct Pending { cudaEvent_t a, b; std::string name; double bytes; };
-  struct Stat { u64 launches = 0; double ms = 0.0; double bytes = 0.0; };
+  struct Pending { cudaEvent_t a, b; std::string name; double bytes; double units = 0.0; };
+  struct Stat { u64 launches = 0; double ms = 0.0; double bytes = 0.0; double units = 0.0; };
   int mode_ = 0;
   bool open_ = false;  // the last begin() recorded an event
   bool capturing_ = false, graph_round_ = false, graph_timing_failed_ = false;

@@ -73,6 +73,10 @@ __device__ __forceinline__ uint4 load_codes(const u8* p, bool line) {
   return __ldg(reinterpret_cast<const uint4*>(p));
 }
 
+__device__ __forceinline__ u32 smem_addr(const void* p) {
+  return static_cast<u32>(__cvta_generic_to_shared(p));
+}
+
 template <bool QUANT>
 __device__ __forceinline__ void load_q(const TreeArrays& ta, const Scales& sc, u32 i, u32& gq, u32& hq) {
   if (QUANT) {
@@ -90,6 +94,13 @@ template <int MB, int THREADS, bool QUANT>
 __global__ void __launch_bounds__(THREADS) k_hist(HistArgs a) {
   extern __shared__ __align__(16) unsigned char smem[];
   __shared__ u32 s_task;
+  static_assert(unroll_for<MB>() % 2 == 0, "the two lanes of a row slot split the prefetch");
+  // Row-index prefetch through shared memory (the 64-bin kernel, measured
+  // 10-15% faster with it); the 256-bin kernel keeps direct loads: its planes
+  // already fill most of shared memory, and with the stage it ran slower.
+  constexpr bool kPrefetch = MB < 256;
+  // per warp, two stages of the row indices of one iteration
+  __shared__ u32 s_rows[kPrefetch ? (THREADS / 32) * 2 * unroll_for<MB>() * kRPW : 1];
   constexpr int kCells = MB * kFT;          // u32 planes: [bin][feature]
   constexpr int kWRow = MB + 1;              // int64 planes: [feature][bin], rows padded
   constexpr int kWCells = kFT * kWRow;
@@ -203,12 +214,52 @@ __global__ void __launch_bounds__(THREADS) k_hist(HistArgs a) {
     while (pos < tend) {
       const u32 room = u32(kWindowRows) - in_window;
       const u32 end = (tend - pos) < room ? tend : pos + room;
-      for (u32 i0 = pos + u32(warp) * kRPW + s; i0 < end; i0 += kStep * kUnroll) {
-        u32 row[kUnroll];
+      // Warp-uniform iterations over this warp's positions w0 + s + u * kStep.
+      // The row indices of the next iteration are copied into the warp's
+      // shared stage with cp.async while this one runs, so an iteration waits
+      // for one global round trip (the codes and (g, h)), not two.
+      u32* const stage0 = s_rows + warp * (2 * kUnroll * kRPW);
+      auto prefetch = [&](u32 w0, u32* st) {
+        // the two lanes of a row slot split its kUnroll indices
 #pragma unroll
-        for (int u = 0; u < kUnroll; ++u) {
-          const u32 i = i0 + u * kStep;
-          row[u] = (i < end && qvalid) ? __ldg(ta.ridx + i) : kNoRow;
+        for (int q = 0; q < kUnroll / 2; ++q) {
+          const int u = q + int(lane & 1) * (kUnroll / 2);
+          const u32 i = w0 + s + u32(u) * kStep;
+          u32* dst = st + u * kRPW + s;
+          if (i < end) {
+            asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_addr(dst)), "l"(ta.ridx + i)
+                         : "memory");
+          } else {
+            *dst = kNoRow;
+          }
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+      };
+      int cur = 0;
+      if constexpr (kPrefetch) prefetch(pos + u32(warp) * kRPW, stage0);
+      for (u32 w0 = pos + u32(warp) * kRPW; w0 < end; w0 += kStep * kUnroll) {
+        const u32 i0 = w0 + s;
+        u32 row[kUnroll];
+        if constexpr (kPrefetch) {
+          const u32 w1 = w0 + kStep * kUnroll;
+          u32* const st = stage0 + cur * (kUnroll * kRPW);
+          if (w1 < end) {
+            prefetch(w1, stage0 + (cur ^ 1) * (kUnroll * kRPW));
+          } else {
+            asm volatile("cp.async.commit_group;" ::: "memory");  // an empty group keeps the wait uniform
+          }
+          asm volatile("cp.async.wait_group 1;" ::: "memory");
+          __syncwarp();
+#pragma unroll
+          for (int u = 0; u < kUnroll; ++u) row[u] = qvalid ? st[u * kRPW + s] : kNoRow;
+          __syncwarp();  // the stage is refilled by the iteration after next
+          cur ^= 1;
+        } else {
+#pragma unroll
+          for (int u = 0; u < kUnroll; ++u) {
+            const u32 i = i0 + u * kStep;
+            row[u] = (i < end && qvalid) ? __ldg(ta.ridx + i) : kNoRow;
+          }
         }
         uint4 v[kUnroll];
         u32 gq[kUnroll], hq[kUnroll];
@@ -240,6 +291,10 @@ __global__ void __launch_bounds__(THREADS) k_hist(HistArgs a) {
             atomicAdd(Lh + cell, hq[u]);
           }
         }
+      }
+      if constexpr (kPrefetch) {
+        asm volatile("cp.async.wait_all;" ::: "memory");
+        __syncwarp();
       }
       in_window += end - pos;
       pos = end;

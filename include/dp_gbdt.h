@@ -184,6 +184,14 @@ DP_API int dp_hist_prepare(const uint8_t* bins, uint64_t bin_stride, uint32_t fe
 DP_API int dp_hist_run(void* plan, void* stream);
 DP_API int dp_hist_free(void* plan);
 
+/* Shared-memory update ceiling of the histogram kernel on the current device:
+ * the kernel's inner loop (two 32-bit shared atomics per (row, feature) pair,
+ * 32 distinct banks per warp step, one 1024-thread block per SM) run alone for
+ * `steps` warp steps over register-generated bin codes, with no global-memory
+ * traffic.  Writes the measured (row, feature) pairs per second.  No
+ * counterpart in the reference; a measurement aid for the histogram roofline. */
+DP_API int dp_probe_hist_atomics(uint32_t steps, double* pairs_per_second, void* stream);
+
 /* dp_hist_build for callers that cannot allocate device memory (a process
  * whose device memory is reserved up front by its own pool, or a latency path
  * that must not call cudaMalloc/cudaFree).  No counterpart in the reference.
