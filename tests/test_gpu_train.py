@@ -280,3 +280,27 @@ def test_golden_fixtures(dp, name):
     K = d["num_class"]
     np.testing.assert_array_equal(b.margins(len(y), K).view(np.uint32),
                                   np.array(d["expected"]["margin"], np.float32).view(np.uint32))
+
+
+FROZEN = json.loads((GOLDEN / "configs" / "frozen.json").read_text())
+
+
+@pytest.mark.parametrize("name", sorted(FROZEN))
+def test_config_fixtures(dp, name):
+    """Configs 1-4 (config 1 full size, the others scaled down) through the C
+    API: the trees and training margins equal the frozen oracle outputs of
+    tests/golden/make_config_fixtures.py bit for bit."""
+    import sys
+    sys.path.insert(0, str(GOLDEN))
+    import config_data
+    fx = FROZEN[name]
+    x, y = config_data.data(name)
+    params = {"objective": fx["objective"], "tree_method": "hist", "device": "cuda:0",
+              "max_depth": fx["max_depth"], "max_bin": fx["max_bin"], "eta": fx["eta"]}
+    if fx["objective"].startswith("multi:"):
+        params["num_class"] = fx["num_class"]
+    b = dp.train(params, dp.DMatrix.from_torch(cuda(x), cuda(y)), fx["rounds"])
+    trees = b.trees()
+    assert [len(t["left_children"]) for t in trees] == fx["nodes_per_tree"]
+    assert config_data.tree_digest(trees) == fx["trees_sha256"]
+    assert config_data.array_digest(b.margins(len(y), fx["num_class"])) == fx["margins_sha256"]

@@ -146,3 +146,33 @@ def test_oracle_prediction_routing_by_hand(orc):
     xt = np.array([[cond - 1e-3], [cond], [np.nan]], np.float32)
     got = m.predict(xt, margin=True)[:, 0]
     np.testing.assert_array_equal(got, np.array([left, right, left if dl else right], np.float32))
+
+
+FROZEN = json.loads((GOLDEN / "configs" / "frozen.json").read_text())
+
+
+@pytest.mark.parametrize("name", sorted(FROZEN))
+def test_oracle_reproduces_config_fixtures(orc, name):
+    """The oracle on configs 1-4 (config 1 full size, the others scaled down;
+    tests/golden/config_data.py) still gives the frozen cuts, trees and margins
+    of tests/golden/make_config_fixtures.py."""
+    import hashlib
+    import sys
+    sys.path.insert(0, str(GOLDEN))
+    import config_data
+    fx = FROZEN[name]
+    x, y = config_data.data(name)
+    assert x.shape == (fx["rows"], fx["features"])
+    m = orc.Model(x, y, fx["objective"], num_class=fx["num_class"], max_depth=fx["max_depth"],
+                  max_bin=fx["max_bin"], eta=fx["eta"], rounds=fx["rounds"], threads=4)
+    cut, nb, hm = m.cuts()
+    hc = hashlib.sha256()
+    for f in range(x.shape[1]):
+        hc.update(np.asarray(cut[f][: max(int(nb[f]) - 1, 0)], dtype="<f4").tobytes())
+    hc.update(np.asarray(nb, dtype="<u2").tobytes())
+    hc.update(np.asarray(hm, dtype=np.uint8).tobytes())
+    assert hc.hexdigest() == fx["cuts_sha256"]
+    trees = [m.tree(i) for i in range(m.num_trees())]
+    assert [len(t["left_children"]) for t in trees] == fx["nodes_per_tree"]
+    assert config_data.tree_digest(trees) == fx["trees_sha256"]
+    assert config_data.array_digest(m.margins()) == fx["margins_sha256"]
