@@ -11,6 +11,7 @@
 #include <vector>
 
 #include "booster.h"
+#include "csv.h"
 #include "comm.h"
 #include "dmatrix.h"
 #include "json.h"
@@ -632,6 +633,80 @@ int dp_eval_splits(const int64_t* hist, int32_t nnodes, uint32_t features, const
     out_gain[n] = b[n].gain;
     out_left[2 * n] = b[n].gl;
     out_left[2 * n + 1] = b[n].hl;
+  }
+  DP_API_END();
+}
+
+// ---- CSV input transport (native/decision_programs_csv.hpp:36-67)
+namespace {
+struct CsvHandle {
+  std::unique_ptr<dp::CsvDense> d;
+  int device = 0;
+};
+CsvHandle* csv_handle(void* h) {
+  dp::need(h != nullptr, "invalid CSV handle");
+  return static_cast<CsvHandle*>(h);
+}
+}  // namespace
+
+int dp_csv_decode(const char* bytes, uint64_t size, const char* target, const char* header_mode, void* stream,
+                  void** out) {
+  DP_API_BEGIN();
+  dp::need(out != nullptr && (bytes != nullptr || size == 0), "dp_csv_decode: invalid arguments");
+  auto h = std::make_unique<CsvHandle>();
+  dp::cuda_check(cudaGetDevice(&h->device), "cudaGetDevice");
+  h->d = dp::csv_decode(bytes, size, target ? target : "", header_mode ? header_mode : "auto",
+                        static_cast<cudaStream_t>(stream));
+  *out = h.release();
+  DP_API_END();
+}
+
+int dp_csv_shape(void* csv, uint64_t* rows, uint32_t* features, uint32_t* classes, int32_t* header) {
+  DP_API_BEGIN();
+  const auto& d = *csv_handle(csv)->d;
+  if (rows) *rows = d.rows;
+  if (features) *features = d.features;
+  if (classes) *classes = d.classes;
+  if (header) *header = d.header ? 1 : 0;
+  DP_API_END();
+}
+
+int dp_csv_data(void* csv, const float** values, const uint32_t** labels) {
+  DP_API_BEGIN();
+  const auto& d = *csv_handle(csv)->d;
+  if (values) *values = d.values.get();
+  if (labels) *labels = d.has_target ? d.labels.get() : nullptr;
+  DP_API_END();
+}
+
+int dp_csv_metadata(void* csv, const char** json, double* device_ms) {
+  DP_API_BEGIN();
+  const auto& d = *csv_handle(csv)->d;
+  if (json) *json = d.meta.c_str();
+  if (device_ms) *device_ms = d.ms_device;
+  DP_API_END();
+}
+
+int dp_csv_copy(void* csv, float* values, uint32_t* labels) {
+  DP_API_BEGIN();
+  CsvHandle* h = csv_handle(csv);
+  dp::DeviceGuard g(h->device);
+  const auto& d = *h->d;
+  if (values && d.rows)
+    dp::cuda_check(cudaMemcpy(values, d.values.get(), d.rows * d.features * sizeof(float), cudaMemcpyDeviceToHost),
+                   "copy CSV values");
+  if (labels && d.has_target && d.rows)
+    dp::cuda_check(cudaMemcpy(labels, d.labels.get(), d.rows * sizeof(uint32_t), cudaMemcpyDeviceToHost),
+                   "copy CSV labels");
+  DP_API_END();
+}
+
+int dp_csv_free(void* csv) {
+  DP_API_BEGIN();
+  if (csv) {
+    CsvHandle* h = static_cast<CsvHandle*>(csv);
+    dp::DeviceGuard g(h->device);
+    delete h;
   }
   DP_API_END();
 }

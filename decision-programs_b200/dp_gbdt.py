@@ -29,7 +29,7 @@ EXPORTED = [
     "XGBoosterPredictFromCudaArray",
     "dp_comm_unique_id", "dp_comm_create", "dp_comm_free", "dp_booster_set_comm", "dp_booster_set_profiling",
     "dp_booster_profile", "dp_booster_margins", "dp_launch_count", "dp_quantile_cuts", "dp_bin_matrix",
-    "dp_gradients", "dp_hist_build", "dp_hist_build_noalloc", "dp_probe_hist_atomics", "dp_quantize_gh", "dp_hist_prepare", "dp_hist_run", "dp_hist_free", "dp_eval_splits",
+    "dp_gradients", "dp_hist_build", "dp_hist_build_noalloc", "dp_probe_hist_atomics", "dp_csv_decode", "dp_csv_shape", "dp_csv_data", "dp_csv_metadata", "dp_csv_copy", "dp_csv_free", "dp_quantize_gh", "dp_hist_prepare", "dp_hist_run", "dp_hist_free", "dp_eval_splits",
 ]
 
 OBJECTIVE_IDS = {"reg:squarederror": 0, "binary:logistic": 1, "multi:softprob": 2, "multi:softmax": 3}
@@ -91,6 +91,13 @@ def lib() -> C.CDLL:
         L.dp_hist_build_noalloc.argtypes = [P, u64, C.c_uint32, C.c_int32, P, P, P, P, C.c_int32, f32, f32, P, P]
         L.dp_quantize_gh.argtypes = [P, u64, f32, f32, P]
         L.dp_probe_hist_atomics.argtypes = [C.c_uint32, C.POINTER(C.c_double), P]
+        L.dp_csv_decode.argtypes = [C.c_char_p, u64, C.c_char_p, C.c_char_p, P, C.POINTER(P)]
+        L.dp_csv_shape.argtypes = [P, C.POINTER(u64), C.POINTER(C.c_uint32), C.POINTER(C.c_uint32),
+                                   C.POINTER(C.c_int32)]
+        L.dp_csv_data.argtypes = [P, C.POINTER(P), C.POINTER(P)]
+        L.dp_csv_metadata.argtypes = [P, C.POINTER(C.c_char_p), C.POINTER(C.c_double)]
+        L.dp_csv_copy.argtypes = [P, P, P]
+        L.dp_csv_free.argtypes = [P]
         L.dp_hist_prepare.argtypes = [P, u64, C.c_uint32, C.c_int32, C.c_int32, P, P, P, P, C.c_int32, f32, f32,
                                       P, C.POINTER(P)]
         L.dp_hist_run.argtypes = [P, P]
@@ -352,6 +359,46 @@ class Comm:
         if self.handle:
             check(lib().dp_comm_free(self.handle))
             self.handle = C.c_void_p()
+
+
+class CsvTable:
+    """The GPU CSV decoder (dp_csv_decode): the reference's
+    decision_programs_csv::decode (native/decision_programs_csv.hpp:36-67).
+    `values_ptr` / `labels_ptr` are device pointers owned by this object."""
+
+    def __init__(self, data: bytes, target: str | None = None, header: str = "auto"):
+        h = C.c_void_p()
+        check(lib().dp_csv_decode(data, len(data), (target or "").encode(), header.encode(), None, C.byref(h)))
+        self.handle = h
+        rows, feats, classes, hdr = C.c_uint64(), C.c_uint32(), C.c_uint32(), C.c_int32()
+        check(lib().dp_csv_shape(h, C.byref(rows), C.byref(feats), C.byref(classes), C.byref(hdr)))
+        self.rows, self.features, self.classes, self.header = rows.value, feats.value, classes.value, bool(hdr.value)
+        meta, ms = C.c_char_p(), C.c_double()
+        check(lib().dp_csv_metadata(h, C.byref(meta), C.byref(ms)))
+        m = json.loads(meta.value.decode())
+        self.names, self.label_mapping, self.device_ms = m["names"], m["label_mapping"], ms.value
+        v, lb = C.c_void_p(), C.c_void_p()
+        check(lib().dp_csv_data(h, C.byref(v), C.byref(lb)))
+        self.values_ptr, self.labels_ptr = v.value, lb.value
+
+    def to_numpy(self):
+        import numpy as np
+        values = np.empty((self.rows, self.features), np.float32)
+        labels = np.empty(self.rows, np.uint32) if self.labels_ptr else None
+        check(lib().dp_csv_copy(self.handle, values.ctypes.data,
+                                labels.ctypes.data if labels is not None else None))
+        return values, labels
+
+    def free(self) -> None:
+        if self.handle:
+            check(lib().dp_csv_free(self.handle))
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
 
 
 def train(params: dict, dtrain: DMatrix, rounds: int, comm: Comm | None = None) -> Booster:

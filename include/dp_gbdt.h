@@ -184,6 +184,30 @@ DP_API int dp_hist_prepare(const uint8_t* bins, uint64_t bin_stride, uint32_t fe
 DP_API int dp_hist_run(void* plan, void* stream);
 DP_API int dp_hist_free(void* plan);
 
+/* CSV input transport on the GPU.  Replaces the reference's host-side
+ * decision_programs_csv::decode(bytes, target, header) at
+ * native/decision_programs_csv.hpp:36-67 (called at
+ * native/decision_programs_cli.cpp:140): the same accepted inputs (RFC 4180
+ * quoting, "\r\n" / "\r" / "\n" record ends, dropped empty lines, equal
+ * column counts), the same header detection and target resolution (a header
+ * name, "last" or a zero-based index; NULL or "" for none), the same feature
+ * parsing (trimmed; empty, nan, na, null -> NaN; correctly rounded finite
+ * binary32, bit for bit) and class labels (unsigned integers, or any text
+ * numbered in order of first appearance), and the same error messages
+ * (XGBGetLastError).  `bytes` is host memory; the decoded matrix stays on the
+ * current device as row-major fp32 [rows][features] (a borrowed input for
+ * XGDMatrixCreateFromCudaArrayInterface while the handle lives) with u32
+ * labels.  dp_csv_metadata gives {"header": bool, "names": [...],
+ * "label_mapping": null | [{"class": id, "label": text}, ...]} (what the
+ * reference's Dense holds) and the device time of the decode. */
+DP_API int dp_csv_decode(const char* bytes, uint64_t size, const char* target, const char* header_mode,
+                         void* stream, void** out);
+DP_API int dp_csv_shape(void* csv, uint64_t* rows, uint32_t* features, uint32_t* classes, int32_t* header);
+DP_API int dp_csv_data(void* csv, const float** values, const uint32_t** labels);
+DP_API int dp_csv_metadata(void* csv, const char** json, double* device_ms);
+DP_API int dp_csv_copy(void* csv, float* values, uint32_t* labels);
+DP_API int dp_csv_free(void* csv);
+
 /* Shared-memory update ceiling of the histogram kernel on the current device:
  * the kernel's inner loop (two 32-bit shared atomics per (row, feature) pair,
  * 32 distinct banks per warp step, one 1024-thread block per SM) run alone for
