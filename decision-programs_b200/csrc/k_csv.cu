@@ -142,36 +142,49 @@ __global__ void k_quote_counts(const u8* __restrict__ text, u64 n, u64* __restri
   if (threadIdx.x == 0) counts[blockIdx.x] = total;
 }
 
-// Structural delimiters of this thread's bytes: with `pos` set, written at
-// out_base + their rank; returns their count.
+// Structural delimiters of this thread's bytes.  The count pass stores the
+// block's delimiter and record-end counts; the write pass stores every
+// delimiter's position in order and, for each record end, that delimiter's
+// index (so record r starts at field rec_end[r - 1] + 1).
 template <bool WRITE>
 __device__ __forceinline__ void delimiters(const u8* __restrict__ text, u64 n, const u64* __restrict__ qbase,
-                                           const u64* __restrict__ dbase, u64* __restrict__ pos, u8* __restrict__ kind,
-                                           u64* __restrict__ counts) {
+                                           const u64* __restrict__ dbase, const u64* __restrict__ rbase,
+                                           u64* __restrict__ pos, u64* __restrict__ rec_end, u64* __restrict__ counts,
+                                           u64* __restrict__ rcounts) {
   const u64 base = u64(blockIdx.x) * kBlockBytes + u64(threadIdx.x) * kBytesPerThread;
   u64 q = 0;
   for (int k = 0; k < kBytesPerThread; ++k) q += (base + k < n && text[base + k] == '"');
   const u64 qbefore = qbase[blockIdx.x] + block_scan_u64(q, nullptr);
   u32 parity = u32(qbefore & 1u);
-  u64 d = 0;
-  u8 prev = base > 0 && base - 1 < n ? text[base - 1] : u8(0);
+  u64 d = 0, r = 0;
+  const u8 prev0 = base > 0 && base - 1 < n ? text[base - 1] : u8(0);
+  u8 prev = prev0;
   for (int k = 0; k < kBytesPerThread; ++k) {
     const u64 i = base + k;
     if (i >= n) break;
     const u8 c = text[i];
-    if (c == '"') parity ^= 1u;
-    else if (!parity && (c == ',' || c == '\r' || (c == '\n' && prev != '\r'))) ++d;
+    if (c == '"') {
+      parity ^= 1u;
+    } else if (!parity && (c == ',' || c == '\r' || (c == '\n' && prev != '\r'))) {
+      ++d;
+      r += c != ',';
+    }
     prev = c;
   }
   if (!WRITE) {
-    u64 total = 0;
-    block_scan_u64(d, &total);
-    if (threadIdx.x == 0) counts[blockIdx.x] = total;
+    u64 dt = 0, rt = 0;
+    block_scan_u64(d, &dt);
+    block_scan_u64(r, &rt);
+    if (threadIdx.x == 0) {
+      counts[blockIdx.x] = dt;
+      rcounts[blockIdx.x] = rt;
+    }
     return;
   }
   u64 at = dbase[blockIdx.x] + block_scan_u64(d, nullptr);
+  u64 rat = rbase[blockIdx.x] + block_scan_u64(r, nullptr);
   parity = u32(qbefore & 1u);
-  prev = base > 0 && base - 1 < n ? text[base - 1] : u8(0);
+  prev = prev0;
   for (int k = 0; k < kBytesPerThread; ++k) {
     const u64 i = base + k;
     if (i >= n) break;
@@ -180,19 +193,20 @@ __device__ __forceinline__ void delimiters(const u8* __restrict__ text, u64 n, c
       parity ^= 1u;
     } else if (!parity && (c == ',' || c == '\r' || (c == '\n' && prev != '\r'))) {
       pos[at] = i;
-      kind[at] = c == ',' ? 0 : 1;
+      if (c != ',') rec_end[rat++] = at;
       ++at;
     }
     prev = c;
   }
 }
 __global__ void k_delim_counts(const u8* __restrict__ text, u64 n, const u64* __restrict__ qbase,
-                               u64* __restrict__ counts) {
-  delimiters<false>(text, n, qbase, nullptr, nullptr, nullptr, counts);
+                               u64* __restrict__ counts, u64* __restrict__ rcounts) {
+  delimiters<false>(text, n, qbase, nullptr, nullptr, nullptr, nullptr, counts, rcounts);
 }
 __global__ void k_delim_write(const u8* __restrict__ text, u64 n, const u64* __restrict__ qbase,
-                              const u64* __restrict__ dbase, u64* __restrict__ pos, u8* __restrict__ kind) {
-  delimiters<true>(text, n, qbase, dbase, pos, kind, nullptr);
+                              const u64* __restrict__ dbase, const u64* __restrict__ rbase, u64* __restrict__ pos,
+                              u64* __restrict__ rec_end) {
+  delimiters<true>(text, n, qbase, dbase, rbase, pos, rec_end, nullptr, nullptr);
 }
 
 // byte range of field j: after the previous delimiter (and the '\n' of a
@@ -209,7 +223,7 @@ __device__ __forceinline__ void field_range(const u8* text, u64 n, const u64* dp
 }
 
 __global__ void k_fields(const u8* __restrict__ text, u64 n, const u64* __restrict__ dpos, u64 ndelim, u64 nf,
-                         u64* __restrict__ cstart, u32* __restrict__ clen, u8* __restrict__ flags,
+                         u32* __restrict__ clen, u8* __restrict__ flags,
                          unsigned long long* __restrict__ err) {
   const u64 j = u64(blockIdx.x) * blockDim.x + threadIdx.x;
   if (j >= nf) return;
@@ -249,31 +263,36 @@ __global__ void k_fields(const u8* __restrict__ text, u64 n, const u64* __restri
       }
   }
   if (ce == cs) fl |= kContentEmpty;
-  cstart[j] = cs;
   clen[j] = u32(ce - cs < 0xffffffffull ? ce - cs : 0xffffffffull);
   flags[j] = u8(fl);
 }
 
-__global__ void k_rec_flags(const u8* __restrict__ kind, u64 ndelim, u64 nf, u64* __restrict__ is_end) {
-  const u64 j = u64(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (j < nf) is_end[j] = j < ndelim ? u64(kind[j]) : 0;
-}
-__global__ void k_rec_first(const u8* __restrict__ kind, u64 nf, const u64* __restrict__ rec_of,
-                            u64* __restrict__ rec_first) {
-  const u64 j = u64(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (j < nf && (j == 0 || kind[j - 1] == 1)) rec_first[rec_of[j]] = j;
+// record r's first field: 0, or the field after record end r - 1
+__global__ void k_rec_first(const u64* __restrict__ rec_end, u64 nrec, u64 nf, u64* __restrict__ rec_first) {
+  const u64 r = u64(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (r > nrec) return;
+  rec_first[r] = r == 0 ? 0 : (r == nrec ? nf : rec_end[r - 1] + 1);
 }
 __global__ void k_records(const u64* __restrict__ rec_first, u64 nrec, const u8* __restrict__ flags,
                           u64* __restrict__ kept, unsigned long long* __restrict__ cmin,
                           unsigned long long* __restrict__ cmax) {
   const u64 r = u64(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (r >= nrec) return;
-  const u64 cnt = rec_first[r + 1] - rec_first[r];
-  const bool drop = cnt == 1 && (flags[rec_first[r]] & kContentEmpty);
-  kept[r] = drop ? 0 : 1;
-  if (!drop) {
-    atomicMin(cmin, static_cast<unsigned long long>(cnt));
-    atomicMax(cmax, static_cast<unsigned long long>(cnt));
+  unsigned long long lo = ~0ull, hi = 0;
+  if (r < nrec) {
+    const u64 cnt = rec_first[r + 1] - rec_first[r];
+    const bool drop = cnt == 1 && (flags[rec_first[r]] & kContentEmpty);
+    kept[r] = drop ? 0 : 1;
+    if (!drop) lo = hi = cnt;
+  }
+  // one pair of atomics per warp
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    lo = min(lo, __shfl_xor_sync(0xffffffffu, lo, o));
+    hi = max(hi, __shfl_xor_sync(0xffffffffu, hi, o));
+  }
+  if ((threadIdx.x & 31) == 0 && hi) {
+    atomicMin(cmin, lo);
+    atomicMax(cmax, hi);
   }
 }
 __global__ void k_compact(const u64* __restrict__ kept, const u64* __restrict__ kidx, u64 nrec, u64* __restrict__ list) {
@@ -284,7 +303,10 @@ __global__ void k_compact(const u64* __restrict__ kept, const u64* __restrict__ 
 // ---- decoding
 struct Cells {
   const u8* text;
-  const u64* cstart;
+  u64 n;
+  const u64* dpos;
+  u64 ndelim;
+  const u8* flags;
   const u32* clen;
   const u64* rec_first;
   const u64* kept_list;
@@ -298,13 +320,19 @@ struct Cells {
 __device__ __forceinline__ u64 cell_field(const Cells& c, u64 row, u32 col) {
   return c.rec_first[c.kept_list[c.first + row]] + col;
 }
+// first content byte of field j (after the opening quote of a quoted field)
+__device__ __forceinline__ const u8* content(const Cells& c, u64 j) {
+  u64 s, e;
+  field_range(c.text, c.n, c.dpos, c.ndelim, j, &s, &e);
+  return c.text + s + ((c.flags[j] & kQuoted) ? 1 : 0);
+}
 
 __global__ void k_labels_numeric(Cells c, u32* __restrict__ numeric) {
   const u64 row = u64(blockIdx.x) * blockDim.x + threadIdx.x;
   if (row >= c.rows) return;
   const u64 j = cell_field(c, row, c.target);
   u32 v;
-  if (!dec::parse_label_token(c.text + c.cstart[j], c.clen[j], &v)) atomicAnd(numeric, 0u);
+  if (!dec::parse_label_token(content(c, j), c.clen[j], &v)) atomicAnd(numeric, 0u);
 }
 
 __global__ void k_cells(Cells c, bool numeric, float* __restrict__ values, u32* __restrict__ labels,
@@ -314,7 +342,7 @@ __global__ void k_cells(Cells c, bool numeric, float* __restrict__ values, u32* 
   const u64 row = t / c.columns;
   const u32 col = u32(t % c.columns);
   const u64 j = cell_field(c, row, col);
-  const u8* p = c.text + c.cstart[j];
+  const u8* p = content(c, j);
   const u32 len = c.clen[j];
   const unsigned long long rec = c.first + row;
   if (col == c.target) {
@@ -371,7 +399,7 @@ __global__ void k_label_insert(Cells c, const u8* __restrict__ flags, LabelTable
   const u64 row = u64(blockIdx.x) * blockDim.x + threadIdx.x;
   if (row >= c.rows) return;
   const u64 j = cell_field(c, row, c.target);
-  const u8* p = c.text + c.cstart[j];
+  const u8* p = content(c, j);
   const bool esc = flags[j] & kEscape;
   u32 b, e;
   label_span(p, c.clen[j], &b, &e);
@@ -404,8 +432,8 @@ __global__ void k_label_verify(Cells c, const u8* __restrict__ flags, LabelTable
   const u64 rep = tab.first_row[slot_of[row]];
   if (rep == row) return;
   const u64 j = cell_field(c, row, c.target), k = cell_field(c, rep, c.target);
-  const u8* p = c.text + c.cstart[j];
-  const u8* q = c.text + c.cstart[k];
+  const u8* p = content(c, j);
+  const u8* q = content(c, k);
   const bool pe = flags[j] & kEscape, qe = flags[k] & kEscape;
   u32 pb, pend, qb, qend;
   label_span(p, c.clen[j], &pb, &pend);
@@ -433,7 +461,7 @@ __global__ void k_label_lengths(Cells c, const u8* __restrict__ flags, const u32
   const u32 d = blockIdx.x * blockDim.x + threadIdx.x;
   if (d >= nd) return;
   const u64 j = cell_field(c, dist_first[d], c.target);
-  const u8* p = c.text + c.cstart[j];
+  const u8* p = content(c, j);
   const bool esc = flags[j] & kEscape;
   u32 b, e;
   label_span(p, c.clen[j], &b, &e);
@@ -446,7 +474,7 @@ __global__ void k_label_gather(Cells c, const u8* __restrict__ flags, const u32*
   const u32 d = blockIdx.x * blockDim.x + threadIdx.x;
   if (d >= nd) return;
   const u64 j = cell_field(c, dist_first[d], c.target);
-  const u8* p = c.text + c.cstart[j];
+  const u8* p = content(c, j);
   const bool esc = flags[j] & kEscape;
   u32 b, e;
   label_span(p, c.clen[j], &b, &e);
@@ -495,39 +523,76 @@ std::unique_ptr<CsvDense> csv_decode(const char* bytes, u64 n, const std::string
       cudaEventDestroy(b);
     }
   } events{ev0, ev1};
-  DevBuf<u8> text(std::max<u64>(n, 1));
+  // device memory in two slabs (a cudaMalloc / cudaFree costs about half a
+  // millisecond each on this GPU): what the structure pass needs, then the
+  // per-delimiter, per-field and per-record arrays once their count is known
+  std::vector<DevBuf<u8>> slabs;
+  const u64 nb = std::max<u64>(1, (n + kBlockBytes - 1) / kBlockBytes);
+  need(nb < (u64(1) << 31), "CSV input too large");
+  DevBuf<u8> text;
+  DevBuf<unsigned long long> sc;
+  DevBuf<u64> qcnt, qbase, dcnt, dbase, rcnt, rbase, tmp;
+  {
+    SlabPlan plan;
+    plan.want(text, nb * kBlockBytes);  // zero-padded to whole blocks
+    plan.want(sc, 8);
+    plan.want(qcnt, nb);
+    plan.want(qbase, nb);
+    plan.want(dcnt, nb);
+    plan.want(dbase, nb);
+    plan.want(rcnt, nb);
+    plan.want(rbase, nb);
+    plan.want(tmp, nb / (kCsvThreads * 4) + 2);
+    plan.commit(slabs);
+  }
   if (n) DP_CUDA(cudaMemcpyAsync(text.get(), bytes, n, cudaMemcpyHostToDevice, s));
+  DP_CUDA(cudaMemsetAsync(text.get() + n, 0, nb * kBlockBytes - n, s));
   DP_CUDA(cudaEventRecord(ev0, s));
 
   // small device scalars: [0] quote total, [1] delimiter total, [2] error key,
   // [3] min count, [4] max count, [5] kept total, [6] record-end total
-  DevBuf<unsigned long long> sc(8);
   const unsigned long long init[8] = {0, 0, ~0ull, ~0ull, 0, 0, 0, 0};
   DP_CUDA(cudaMemcpyAsync(sc.get(), init, sizeof init, cudaMemcpyHostToDevice, s));
   u64* sq = reinterpret_cast<u64*>(sc.get());
-  DevBuf<u64> tmp;
 
   // quote parity and structural delimiters
-  const u64 nb = std::max<u64>(1, (n + kBlockBytes - 1) / kBlockBytes);
-  need(nb < (u64(1) << 31), "CSV input too large");
-  DevBuf<u64> qcnt(nb), qbase(nb), dcnt(nb), dbase(nb);
   k_quote_counts<<<u32(nb), kCsvThreads, 0, s>>>(text.get(), n, qcnt.get());
   exclusive_scan(qcnt.get(), qbase.get(), nb, sq + 0, tmp, s);
-  k_delim_counts<<<u32(nb), kCsvThreads, 0, s>>>(text.get(), n, qbase.get(), dcnt.get());
+  k_delim_counts<<<u32(nb), kCsvThreads, 0, s>>>(text.get(), n, qbase.get(), dcnt.get(), rcnt.get());
   exclusive_scan(dcnt.get(), dbase.get(), nb, sq + 1, tmp, s);
+  exclusive_scan(rcnt.get(), rbase.get(), nb, sq + 6, tmp, s);
   after_launch("csv delimiters");
-  const u64 ndelim = read1(sq + 1, s);
-  DevBuf<u64> dpos(std::max<u64>(ndelim, 1));
-  DevBuf<u8> dkind(std::max<u64>(ndelim, 1));
-  k_delim_write<<<u32(nb), kCsvThreads, 0, s>>>(text.get(), n, qbase.get(), dbase.get(), dpos.get(), dkind.get());
+  u64 totals[7];
+  DP_CUDA(cudaMemcpyAsync(totals, sq, sizeof totals, cudaMemcpyDeviceToHost, s));
+  DP_CUDA(cudaStreamSynchronize(s));
+  const u64 ndelim = totals[1], nends = totals[6];
+  // fields: one per delimiter plus possibly a trailing one; records likewise
+  const u64 nfmax = ndelim + 1, nrecmax = nends + 1;
+  DevBuf<u64> dpos, rec_end, rec_first, kept, kidx, kept_list, tmp2;
+  DevBuf<u8> flags;
+  DevBuf<u32> clen, aux;
+  {
+    SlabPlan plan;
+    plan.want(dpos, nfmax);
+    plan.want(rec_end, nrecmax);
+    plan.want(clen, nfmax);
+    plan.want(flags, nfmax);
+    plan.want(rec_first, nrecmax + 1);
+    plan.want(kept, nrecmax);
+    plan.want(kidx, nrecmax);
+    plan.want(kept_list, nrecmax);
+    plan.want(tmp2, nrecmax / (kCsvThreads * 4) + 2);
+    plan.want(aux, 4);
+    plan.commit(slabs);
+  }
+  k_delim_write<<<u32(nb), kCsvThreads, 0, s>>>(text.get(), n, qbase.get(), dbase.get(), rbase.get(), dpos.get(),
+                                                rec_end.get());
   after_launch("csv delimiters");
 
   // the trailing field counts when it has bytes or follows a ','
   u64 last_pos = 0;
-  u8 last_kind = 1;
   if (ndelim) {
     DP_CUDA(cudaMemcpyAsync(&last_pos, dpos.get() + ndelim - 1, sizeof(u64), cudaMemcpyDeviceToHost, s));
-    DP_CUDA(cudaMemcpyAsync(&last_kind, dkind.get() + ndelim - 1, 1, cudaMemcpyDeviceToHost, s));
     DP_CUDA(cudaStreamSynchronize(s));
   }
   u64 tail_start = 0;
@@ -535,34 +600,25 @@ std::unique_ptr<CsvDense> csv_decode(const char* bytes, u64 n, const std::string
     tail_start = last_pos + 1;
     if (bytes[last_pos] == '\r' && tail_start < n && bytes[tail_start] == '\n') ++tail_start;
   }
-  const bool tail = tail_start < n || (ndelim && last_kind == 0);
+  const bool tail = tail_start < n || (ndelim && bytes[last_pos] == ',');
   const u64 nf = ndelim + (tail ? 1 : 0);
 
-  DevBuf<u64> cstart(std::max<u64>(nf, 1));
-  DevBuf<u32> clen(std::max<u64>(nf, 1));
-  DevBuf<u8> flags(std::max<u64>(nf, 1));
   if (nf)
-    k_fields<<<grid_for(nf), 256, 0, s>>>(text.get(), n, dpos.get(), ndelim, nf, cstart.get(), clen.get(),
+    k_fields<<<grid_for(nf), 256, 0, s>>>(text.get(), n, dpos.get(), ndelim, nf, clen.get(),
                                           flags.get(), sc.get() + 2);
   after_launch("csv fields");
   const unsigned long long qerr = read1(sc.get() + 2, s);
-  const u64 quotes = read1(sq + 0, s);
+  const u64 quotes = totals[0];
   if (qerr != ~0ull) bad((qerr & 0xff) == kErrAfterClose ? "CSV characters after closing quote"
                                                           : "CSV quote inside unquoted field");
   if (quotes & 1u) bad("CSV unterminated quoted field");
 
   // records
-  DevBuf<u64> is_end(std::max<u64>(nf, 1)), rec_of(std::max<u64>(nf, 1));
-  if (nf) k_rec_flags<<<grid_for(nf), 256, 0, s>>>(dkind.get(), ndelim, nf, is_end.get());
-  exclusive_scan(is_end.get(), rec_of.get(), nf, sq + 6, tmp, s);
-  const u64 nends = read1(sq + 6, s);
   const u64 nrec = nends + (tail ? 1 : 0);
   if (nrec == 0) bad("CSV contains no records");
-  DevBuf<u64> rec_first(nrec + 1), kept(nrec), kidx(nrec), kept_list(nrec);
-  k_rec_first<<<grid_for(nf), 256, 0, s>>>(dkind.get(), nf, rec_of.get(), rec_first.get());
-  DP_CUDA(cudaMemcpyAsync(rec_first.get() + nrec, &nf, sizeof(u64), cudaMemcpyHostToDevice, s));
+  k_rec_first<<<grid_for(nrec + 1), 256, 0, s>>>(rec_end.get(), nrec, nf, rec_first.get());
   k_records<<<grid_for(nrec), 256, 0, s>>>(rec_first.get(), nrec, flags.get(), kept.get(), sc.get() + 3, sc.get() + 4);
-  exclusive_scan(kept.get(), kidx.get(), nrec, sq + 5, tmp, s);
+  exclusive_scan(kept.get(), kidx.get(), nrec, sq + 5, tmp2, s);
   k_compact<<<grid_for(nrec), 256, 0, s>>>(kept.get(), kidx.get(), nrec, kept_list.get());
   after_launch("csv records");
   unsigned long long h[8];
@@ -582,10 +638,27 @@ std::unique_ptr<CsvDense> csv_decode(const char* bytes, u64 n, const std::string
   std::vector<u64> h_cs(columns);
   std::vector<u32> h_cl(columns);
   std::vector<u8> h_fl(columns);
-  DP_CUDA(cudaMemcpyAsync(h_cs.data(), cstart.get() + f0, columns * sizeof(u64), cudaMemcpyDeviceToHost, s));
+  // content starts from the delimiter positions: field j starts after
+  // delimiter j - 1 (and the '\n' of a "\r\n"), plus an opening quote
+  std::vector<u64> h_dp(columns + 1, 0);
+  if (f0 > 0)
+    DP_CUDA(cudaMemcpyAsync(h_dp.data(), dpos.get() + f0 - 1, std::min<u64>(columns, ndelim - (f0 - 1)) * sizeof(u64),
+                            cudaMemcpyDeviceToHost, s));
+  else if (ndelim)
+    DP_CUDA(cudaMemcpyAsync(h_dp.data() + 1, dpos.get(), std::min<u64>(columns - 1, ndelim) * sizeof(u64),
+                            cudaMemcpyDeviceToHost, s));
   DP_CUDA(cudaMemcpyAsync(h_cl.data(), clen.get() + f0, columns * sizeof(u32), cudaMemcpyDeviceToHost, s));
   DP_CUDA(cudaMemcpyAsync(h_fl.data(), flags.get() + f0, columns, cudaMemcpyDeviceToHost, s));
   DP_CUDA(cudaStreamSynchronize(s));
+  for (u64 c = 0; c < columns; ++c) {
+    const u64 j = f0 + c;
+    u64 st = 0;
+    if (j > 0) {
+      st = h_dp[c] + 1;  // h_dp[c] = dpos[j - 1]
+      if (bytes[h_dp[c]] == '\r' && st < n && bytes[st] == '\n') ++st;
+    }
+    h_cs[c] = st + ((h_fl[c] & kQuoted) ? 1 : 0);
+  }
   std::vector<std::string> rec0(columns);
   for (u64 c = 0; c < columns; ++c) {
     std::string v;
@@ -651,9 +724,10 @@ std::unique_ptr<CsvDense> csv_decode(const char* bytes, u64 n, const std::string
   out->header = header;
   out->has_target = has_target;
   out->values.resize(std::max<u64>(rows * features, 1));
-  Cells cells{text.get(), cstart.get(), clen.get(), rec_first.get(), kept_list.get(), first, rows, u32(columns),
+  Cells cells{text.get(), n, dpos.get(), ndelim, flags.get(), clen.get(), rec_first.get(), kept_list.get(), first, rows,
+              u32(columns),
               u32(target_index), u32(features)};
-  DevBuf<u32> aux(4);  // [0] numeric labels, [1] max label, [2] table overflow, [3] collision
+  // aux: [0] numeric labels, [1] max label, [2] table overflow, [3] collision
   const u32 init_aux[4] = {1u, 0u, 0u, 0u};
   DP_CUDA(cudaMemcpyAsync(aux.get(), init_aux, sizeof init_aux, cudaMemcpyHostToDevice, s));
   bool numeric = has_target;
