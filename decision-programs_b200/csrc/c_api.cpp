@@ -701,6 +701,21 @@ int dp_csv_copy(void* csv, float* values, uint32_t* labels) {
   DP_API_END();
 }
 
+int dp_csv_parse_feature(const char* token, uint64_t size, float* value) {
+  DP_API_BEGIN();
+  dp::need(token != nullptr || size == 0, "dp_csv_parse_feature: token missing");
+  dp::need(size < (uint64_t(1) << 32), "dp_csv_parse_feature: token too long");
+  float v = 0.0f;
+  const bool ok =
+      dp::csv_parse_feature_host(reinterpret_cast<const unsigned char*>(token), static_cast<dp::u32>(size), &v);
+  if (value) *value = v;
+  if (!ok) {
+    g_last_error = "token refused";
+    return 1;
+  }
+  DP_API_END();
+}
+
 int dp_csv_free(void* csv) {
   DP_API_BEGIN();
   if (csv) {

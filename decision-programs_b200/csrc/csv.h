@@ -29,4 +29,9 @@ struct CsvDense {
 std::unique_ptr<CsvDense> csv_decode(const char* bytes, u64 n, const std::string& target,
                                      const std::string& header_mode, cudaStream_t s);
 
+// The host build of the decoder's per-field rule (the reference's feature(),
+// native/decision_programs_csv.hpp:28-34): true with *value set when the
+// token is accepted.  The same code runs on the device for every cell.
+bool csv_parse_feature_host(const unsigned char* p, u32 n, float* value);
+
 }  // namespace dp

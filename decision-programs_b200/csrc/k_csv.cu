@@ -510,6 +510,10 @@ bool host_feature(const std::string& t) {
 
 }  // namespace
 
+bool csv_parse_feature_host(const unsigned char* p, u32 n, float* value) {
+  return dec::parse_feature_token(p, n, value);
+}
+
 std::unique_ptr<CsvDense> csv_decode(const char* bytes, u64 n, const std::string& target,
                                      const std::string& header_mode, cudaStream_t s) {
   auto out = std::make_unique<CsvDense>();

@@ -29,7 +29,7 @@ EXPORTED = [
     "XGBoosterPredictFromCudaArray",
     "dp_comm_unique_id", "dp_comm_create", "dp_comm_free", "dp_booster_set_comm", "dp_booster_set_profiling",
     "dp_booster_profile", "dp_booster_margins", "dp_launch_count", "dp_quantile_cuts", "dp_bin_matrix",
-    "dp_gradients", "dp_hist_build", "dp_hist_build_noalloc", "dp_probe_hist_atomics", "dp_csv_decode", "dp_csv_shape", "dp_csv_data", "dp_csv_metadata", "dp_csv_copy", "dp_csv_free", "dp_quantize_gh", "dp_hist_prepare", "dp_hist_run", "dp_hist_free", "dp_eval_splits",
+    "dp_gradients", "dp_hist_build", "dp_hist_build_noalloc", "dp_probe_hist_atomics", "dp_csv_decode", "dp_csv_shape", "dp_csv_data", "dp_csv_metadata", "dp_csv_copy", "dp_csv_free", "dp_csv_parse_feature", "dp_quantize_gh", "dp_hist_prepare", "dp_hist_run", "dp_hist_free", "dp_eval_splits",
 ]
 
 OBJECTIVE_IDS = {"reg:squarederror": 0, "binary:logistic": 1, "multi:softprob": 2, "multi:softmax": 3}
@@ -98,6 +98,7 @@ def lib() -> C.CDLL:
         L.dp_csv_metadata.argtypes = [P, C.POINTER(C.c_char_p), C.POINTER(C.c_double)]
         L.dp_csv_copy.argtypes = [P, P, P]
         L.dp_csv_free.argtypes = [P]
+        L.dp_csv_parse_feature.argtypes = [C.c_char_p, u64, C.POINTER(C.c_float)]
         L.dp_hist_prepare.argtypes = [P, u64, C.c_uint32, C.c_int32, C.c_int32, P, P, P, P, C.c_int32, f32, f32,
                                       P, C.POINTER(P)]
         L.dp_hist_run.argtypes = [P, P]

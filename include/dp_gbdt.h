@@ -207,6 +207,10 @@ DP_API int dp_csv_data(void* csv, const float** values, const uint32_t** labels)
 DP_API int dp_csv_metadata(void* csv, const char** json, double* device_ms);
 DP_API int dp_csv_copy(void* csv, float* values, uint32_t* labels);
 DP_API int dp_csv_free(void* csv);
+/* The decoder's rule for one feature token, on the host (the reference's
+ * feature(), native/decision_programs_csv.hpp:28-34): returns 0 with *value
+ * set when the token is accepted, 1 when it is refused, -1 on bad arguments. */
+DP_API int dp_csv_parse_feature(const char* token, uint64_t size, float* value);
 
 /* Shared-memory update ceiling of the histogram kernel on the current device:
  * the kernel's inner loop (two 32-bit shared atomics per (row, feature) pair,

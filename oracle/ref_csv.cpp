@@ -4,12 +4,19 @@
 // GPU CSV decoder and as the CPU baseline of its benchmark.
 //
 //   ref_csv <input.csv> <target or -> <header mode> <out dir> [repeats]
+//   ref_csv --tokens <tokens file> <out file>
+//
+// The second form runs the reference's feature() on each line of the tokens
+// file (lines end in '\n'; the token is the line's bytes) and writes one
+// line per token: "1 <hex bits of the float>" when accepted, "0" otherwise.
 //
 // Writes <out>/values.f32, <out>/labels.u32 and <out>/meta.json (rows,
 // features, classes, header, names, label_mapping, seconds per decode), or
 // <out>/error.txt with the exception's message.  A target of "-" decodes
 // without one.
 #include <chrono>
+#include <cstdio>
+#include <cstring>
 #include <fstream>
 #include <iostream>
 #include <iterator>
@@ -17,6 +24,24 @@
 #include "decision_programs_csv.hpp"
 
 int main(int argc, char** argv) {
+  if (argc == 4 && std::string(argv[1]) == "--tokens") {
+    std::ifstream in(argv[2], std::ios::binary);
+    std::ofstream out(argv[3]);
+    std::string line;
+    char buf[16];
+    while (std::getline(in, line)) {
+      float v = 0.0f;
+      if (decision_programs_csv::feature(line, v)) {
+        unsigned bits;
+        std::memcpy(&bits, &v, 4);
+        std::snprintf(buf, sizeof buf, "%08x", bits);
+        out << "1 " << buf << "\n";
+      } else {
+        out << "0\n";
+      }
+    }
+    return 0;
+  }
   if (argc < 5) {
     std::cerr << "usage: ref_csv <input.csv> <target|-> <header> <out dir> [repeats]\n";
     return 2;
