@@ -112,6 +112,14 @@ EDGE = [
     (b"x,y\n" + b"1," + b"9" * 200 + b"\n", "x", "auto"),
     (b"x,y\n0." + b"0" * 60 + b"1,2\n", "y", "auto"),
     (b"x,y\n \t 1.25 \t ,1\n", "y", "auto"),
+    (b"\xef\xbb\xbfx,y\n1,2\n", "y", "auto"),
+    (b"\xef\xbb\xbfx,y\n1,2\n", "x", "auto"),
+    (b"x,y\n\"1\r\n\",1\n2,\"a\r\nb\"\n", "y", "auto"),
+    (b"x,y\n\" 2.5\t\",\"lab,el\"\n3,\"lab,el\"\n", "y", "auto"),
+    (b"x,y\n1,\"\"\"q\"\"\"\n2,\"\"\"q\"\"\"\n", "y", "auto"),
+    (b"a,b,c\n1,2,3\n\"\"\n4,5,6\n", "", "auto"),
+    (b"a,b\r\n\r\n1,2\r\n", "", "auto"),
+    (b",\n,\n", "", "no"),
 ]
 
 
