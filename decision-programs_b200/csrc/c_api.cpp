@@ -3,6 +3,7 @@
 
 #include <cuda_runtime.h>
 
+#include <cstdlib>
 #include <cstring>
 #include <fstream>
 #include <memory>
@@ -475,6 +476,8 @@ struct HistPlan {
   dp::DevBuf<dp::TreeArrays> trees;
   dp::DevBuf<dp::Scales> scales;
   dp::DevBuf<dp::u32> counter;
+  bool wide = false;
+  dp::DevBuf<int64_t> scratch;  // window sums of the 64-feature kernel
   int device = 0;
 };
 
@@ -494,14 +497,21 @@ HistPlan* make_hist_plan(const uint8_t* bins, uint64_t bin_stride, uint32_t feat
   p->hist = hist;
   p->nseg = nseg;
   std::vector<dp::HistTask> tasks;
-  const dp::u32 ftiles = (features + dp::kHistFeatureTile - 1) / dp::kHistFeatureTile;
+  // the training path's choice: 256-bin matrices wider than one tile use the
+  // 64-feature kernel (DP_HIST_WIDE=0 keeps the 32-feature one)
+  const char* wide_env = std::getenv("DP_HIST_WIDE");
+  p->wide = num_bins > 64 && features > dp::kHistFeatureTile && !(wide_env && std::string(wide_env) == "0");
+  const dp::u32 tile = p->wide ? dp::kHistWideTile : dp::kHistFeatureTile;
+  const dp::u32 ftiles = (features + tile - 1) / tile;
   dp::u64 total = 0;
   for (int32_t i = 0; i < nseg; ++i) {
     need(seg_begin[i] >= 0 && seg_end[i] >= seg_begin[i] && seg_end[i] < (int64_t(1) << 31),
          "invalid segment bounds (positions must be below 2^31)");
     total += dp::u64(seg_end[i] - seg_begin[i]);
   }
-  const int64_t chunk = int64_t(dp::hist_chunk_rows(total * ftiles));
+  int64_t chunk = int64_t(dp::hist_chunk_rows(total * ftiles));
+  // testing knob: longer tasks, so that tests reach the multi-window folds
+  if (const char* c = std::getenv("DP_HIST_MIN_CHUNK")) chunk = std::max<int64_t>(chunk, std::atoll(c));
   // Queue order: piece index first, then segment, then feature tile.  With
   // row lists grouped by node and ascending inside a node, the p-th pieces of
   // all nodes cover about the same range of rows, so the blocks running at
@@ -520,14 +530,14 @@ HistPlan* make_hist_plan(const uint8_t* bins, uint64_t bin_stride, uint32_t feat
       const int64_t b = seg_begin[i] + q * piece[i];
       if (q >= pieces[i] || b >= seg_end[i]) continue;
       for (dp::u32 ft = 0; ft < ftiles; ++ft)
-        tasks.push_back(dp::HistTask{dp::u32(i), ft * dp::kHistFeatureTile, 0, 0, b,
-                                     std::min<int64_t>(seg_end[i], b + piece[i])});
+        tasks.push_back(dp::HistTask{dp::u32(i), ft * tile, 0, 0, b, std::min<int64_t>(seg_end[i], b + piece[i])});
     }
   p->ntasks = dp::u32(tasks.size());
   p->tasks.resize(std::max<size_t>(tasks.size(), 1));
   p->trees.resize(1);
   p->scales.resize(1);
   p->counter.resize(1);
+  if (p->wide) p->scratch.resize(dp::hist_wide_scratch_elems());
   const dp::TreeArrays th{const_cast<uint32_t*>(ridx), reinterpret_cast<float2*>(const_cast<void*>(gh))};
   const dp::Scales sc{sg, sh};
   dp::cuda_check(cudaMemcpy(p->trees.get(), &th, sizeof th, cudaMemcpyHostToDevice), "upload");
@@ -542,8 +552,13 @@ HistPlan* make_hist_plan(const uint8_t* bins, uint64_t bin_stride, uint32_t feat
 void run_hist_plan(const HistPlan& p, cudaStream_t s) {
   const dp::u64 slot = dp::u64(p.features) * dp::kMaxBins * 2;
   if (p.nseg) dp::cuda_check(cudaMemsetAsync(p.hist, 0, dp::u64(p.nseg) * slot * sizeof(int64_t), s), "memset");
-  dp::launch_histograms(p.bins, p.bin_stride, p.features, p.num_bins, p.quantized, p.trees.get(), p.scales.get(),
-                        p.tasks.get(), p.ntasks, p.counter.get(), p.hist, s);
+  if (p.wide)
+    dp::launch_histograms_wide(p.bins, p.bin_stride, p.features, p.quantized, p.trees.get(), p.scales.get(),
+                               p.tasks.get(), p.ntasks, p.counter.get(), p.hist, s, nullptr, nullptr,
+                               const_cast<int64_t*>(p.scratch.get()), p.scratch.size());
+  else
+    dp::launch_histograms(p.bins, p.bin_stride, p.features, p.num_bins, p.quantized, p.trees.get(), p.scales.get(),
+                          p.tasks.get(), p.ntasks, p.counter.get(), p.hist, s);
 }
 
 }  // namespace

@@ -170,6 +170,12 @@ Engine::Engine(DMatrix& d, const TrainParams& p, Comm* comm) : d_(d), p_(p), com
     if (q_->has_missing_h[f]) max_bins_ = kMaxBins;
   }
   DP_CUDA(cudaDeviceGetAttribute(&sms_, cudaDevAttrMultiProcessorCount, device_));
+  // On one GPU, 256-bin matrices wider than one tile take the 64-feature
+  // kernel (config 4: histograms 3.19 against 3.25 ms per round); with rows
+  // sharded the 32-feature kernel, whose drains are coalesced, is faster
+  // (2 GPUs: 1.88 against 2.16 ms).  DP_HIST_WIDE=0 / 1 overrides.
+  wide_ = max_bins_ > 64 && F_ > kFT && env_u64("DP_HIST_WIDE", G_ == 1 ? 1 : 0) != 0;
+  hist_tile_ = wide_ ? kHistWideTile : kFT;
   // testing knobs: force the exact-count path of deep levels
   async_open_limit_ = env_u64("DP_ASYNC_OPEN_LIMIT", async_open_limit_);
   async_hist_bytes_ = env_u64("DP_ASYNC_HIST_BYTES", async_hist_bytes_);
@@ -187,6 +193,7 @@ Engine::Engine(DMatrix& d, const TrainParams& p, Comm* comm) : d_(d), p_(p), com
   plan.want(ghmax_, 2 * size_t(K_));
   plan.want(scales_, K_);
   plan.want(hist_counter_, 1);
+  if (wide_) plan.want(hist_scratch_, hist_wide_scratch_elems());
   plan.want(scratch_, 1 + size_t(K_));
   plan.want(gh_totals_, 2 * size_t(K_));
   plan.want(round_dev_, 1);
@@ -304,7 +311,7 @@ void Engine::presize(SlabPlan& plan) {
   const u64 Rt = std::max<u64>(q_->rows_total, 1);
   const u64 RK = std::max<u64>(R_, 1) * K;
   const u64 slot_bytes = slot_elems_ * sizeof(i64);
-  const u32 ftiles = (F_ + kFT - 1) / kFT;
+  const u32 ftiles = (F_ + hist_tile_ - 1) / hist_tile_;
   // the same bounds the level loop of boost_round derives
   u64 open_hi = K, ids_hi = 1, leaves_hi = 0;
   u64 hist[2] = {0, 0}, tasks = 0, split = 0, opens[2] = {K, 0}, builds[2] = {K, 0}, send = 0;
@@ -496,7 +503,7 @@ Engine::RoundOut Engine::enqueue_round() {
   const u64 R = R_;
   const u32 F = F_;
   const int D = p_.max_depth;
-  const u32 ftiles = (F + kFT - 1) / kFT;
+  const u32 ftiles = (F + hist_tile_ - 1) / hist_tile_;
   const SplitParams sp = p_.split_params();
   const u64 Rt = std::max<u64>(q_->rows_total, 1);
   const u64 RK = std::max<u64>(R, 1) * u64(K);
@@ -581,15 +588,20 @@ Engine::RoundOut Engine::enqueue_round() {
     // several ranks, each builds partial histograms of all features for its
     // rows (group-major), and a reduce-scatter leaves every rank the sums of
     // its own feature group.
-    launch_hist_tasks(rb, ftiles, depth, stream_);
+    launch_hist_tasks(rb, ftiles, hist_tile_, depth, stream_);
     i64* hout = G_ > 1 ? send_.get() : hist;
     const u64 out_slot = G_ > 1 ? full_slot_elems_ : slot_elems_;
     if (!zeroed_by_children) launch_zero_slots(rb, hout, out_slot, G_ > 1 ? nbuild_hi : 0, stream_);
     const HistLayout lay{fg_, slot_elems_, nbuild_hi * slot_elems_};
     pi_hist[depth] = prof_.begin(stream_, "histograms", 0.0);
-    launch_histograms(q_->bins.get(), q_->bin_stride, F, max_bins_, true, tarr_[set].get(), scales_.get(),
-                      hist_tasks_.get(), 0, hist_counter_.get(), hout, stream_, &ctr->n_hist_tasks,
-                      G_ > 1 ? &lay : nullptr);
+    if (wide_)
+      launch_histograms_wide(q_->bins.get(), q_->bin_stride, F, true, tarr_[set].get(), scales_.get(),
+                             hist_tasks_.get(), 0, hist_counter_.get(), hout, stream_, &ctr->n_hist_tasks,
+                             G_ > 1 ? &lay : nullptr, hist_scratch_.get(), hist_scratch_.size());
+    else
+      launch_histograms(q_->bins.get(), q_->bin_stride, F, max_bins_, true, tarr_[set].get(), scales_.get(),
+                        hist_tasks_.get(), 0, hist_counter_.get(), hout, stream_, &ctr->n_hist_tasks,
+                        G_ > 1 ? &lay : nullptr);
     prof_.end(stream_);
     if (G_ > 1) {
       prof_.begin(stream_, "exchange_hist", double(nbuild_hi * full_slot_elems_) * sizeof(i64));

@@ -157,6 +157,10 @@ class Engine {
   DevBuf<i64> hist_[2];
   DevBuf<HistTask> hist_tasks_;
   DevBuf<u32> hist_counter_;
+  // 64-feature histogram tasks (k_hist_wide) and their window-sum scratch
+  bool wide_ = false;
+  u32 hist_tile_ = kHistFeatureTile;
+  DevBuf<i64> hist_scratch_;
   DevBuf<EvalNode> eval_nodes_;
   DevBuf<SplitCand> cand_;                 // [open][nchunks_] this rank's candidates
   DevBuf<i64> send_;                       // this rank's partial histograms, group-major (G > 1)

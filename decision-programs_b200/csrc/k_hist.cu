@@ -308,6 +308,185 @@ __global__ void __launch_bounds__(THREADS) k_hist(HistArgs a) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// 256-bin kernel over 64-feature tiles (the training path's kernel when the
+// matrix has more than 32 features).
+//
+// Same task queue and output as k_hist, but a task covers 64 features: a
+// warp step takes 8 rows x 64 bytes (four lanes per row, 16 bytes each), so a
+// scattered row costs one cache-line lookup per 64 features instead of one per
+// 32 -- the lookups share the L1/shared data path with the shared atomics,
+// which is what bounds k_hist.  Two u32 planes [bin][64 features] fill 128 KB
+// of shared memory, so the int64 window sums move to a block-private scratch
+// in global memory (L2-resident, the planes' layout, coalesced folds).  Lane
+// (s, q) rotates its 16 bytes by s + 8 (q >> 1): in every atomic step the 16
+// lanes of q = 0, 2 (and of q = 1, 3) hit 16 distinct banks.
+constexpr int kWide = 64;
+
+template <bool QUANT>
+__global__ void __launch_bounds__(1024) k_hist_wide(HistArgs a, long long* __restrict__ wscr) {
+  constexpr int MB = 256, THREADS = 1024;
+  constexpr int kCells = MB * kWide;
+  constexpr int kRows = 8;                       // rows per warp step
+  constexpr u32 kStep = u32(THREADS / 32) * kRows;
+  constexpr int kUnroll = 6;
+  extern __shared__ __align__(16) unsigned char smem[];
+  __shared__ u32 s_task;
+  u32* Lg = reinterpret_cast<u32*>(smem);
+  u32* Lh = Lg + kCells;
+  long long* Sg = wscr + u64(blockIdx.x) * 2 * kCells;
+  long long* Sh = Sg + kCells;
+  for (int i = threadIdx.x; i < kCells; i += THREADS) {
+    Lg[i] = 0u;
+    Lh[i] = 0u;
+  }
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const u32 s8 = u32(lane) >> 2, q = u32(lane & 3);
+  const u32 rot = (s8 + 8u * (q >> 1)) & 15u;
+  const bool rot8 = (rot & 8u) != 0, rot4 = (rot & 4u) != 0;
+  const u32 rsh = 8u * (rot & 3u);
+  const u32 q16 = 16u * q;
+  u32 key_slot = kNoRow, key_f0 = 0, key_tree = 0;
+  bool key_excl = false;
+  u32 in_window = 0;
+  bool s_clean = true;  // the scratch holds nothing of the current key (block-uniform)
+  const u32 ntasks = a.ntasks_dev ? *a.ntasks_dev : a.ntasks;
+
+  auto fold = [&]() {
+    for (int i = threadIdx.x; i < kCells; i += THREADS) {
+      const long long g = static_cast<long long>(static_cast<int>(Lg[i]));
+      const long long h = static_cast<long long>(Lh[i]);
+      Sg[i] = s_clean ? g : Sg[i] + g;
+      Sh[i] = s_clean ? h : Sh[i] + h;
+      Lg[i] = 0u;
+      Lh[i] = 0u;
+    }
+    s_clean = false;
+  };
+
+  for (;;) {
+    if (threadIdx.x == 0) s_task = atomicAdd(a.counter, 1u);
+    __syncthreads();
+    const u32 ti = s_task;
+    const bool done = ti >= ntasks;
+    HistTask t{};
+    if (!done) t = a.tasks[ti];
+    const bool same = !done && t.slot == key_slot && t.f0 == key_f0 && t.tree == key_tree;
+    if (!same && key_slot != kNoRow) {
+      // scratch + last window straight to the output; each thread keeps the
+      // cells it folded, so no barrier is needed between the two
+      i64* out = a.hist + u64(key_slot) * a.layout.slot_stride;
+      for (int i = threadIdx.x; i < kCells; i += THREADS) {
+        const int b = i / kWide, f = i % kWide;
+        long long gs = static_cast<long long>(static_cast<int>(Lg[i]));
+        long long hs = static_cast<long long>(Lh[i]);
+        if (!s_clean) {
+          gs += Sg[i];
+          hs += Sh[i];
+        }
+        Lg[i] = 0u;
+        Lh[i] = 0u;
+        const u32 gf = key_f0 + u32(f);
+        if (gf >= a.F) continue;
+        const u32 grp = gf / a.layout.fg, fl = gf - grp * a.layout.fg;
+        i64* cell = out + grp * a.layout.group_stride + (u64(fl) * kMaxBins + b) * 2;
+        if (key_excl) {
+          *reinterpret_cast<longlong2*>(cell) = make_longlong2(gs, hs);
+        } else if (gs | hs) {
+          atomicAdd(reinterpret_cast<unsigned long long*>(cell), static_cast<unsigned long long>(gs));
+          atomicAdd(reinterpret_cast<unsigned long long*>(cell) + 1, static_cast<unsigned long long>(hs));
+        }
+      }
+      s_clean = true;
+      key_slot = kNoRow;
+      in_window = 0;
+    }
+    if (done) break;
+    __syncthreads();  // s_task read by all; the planes cleared by the drain
+    key_slot = t.slot;
+    key_f0 = t.f0;
+    key_tree = t.tree;
+    key_excl = t.excl != 0;
+    const TreeArrays ta = a.trees[t.tree];
+    Scales sc{1.f, 1.f};
+    if (!QUANT) sc = a.scales[t.tree];
+    const bool qvalid = u64(t.f0) + q16 < a.bstride;
+    const bool line_rows = (a.bstride & 127u) == 0;
+    const u8* base = a.bins + t.f0 + q16;
+    u32 pos = u32(t.begin);
+    const u32 tend = u32(t.end);
+    while (pos < tend) {
+      const u32 room = u32(kWindowRows) - in_window;
+      const u32 end = (tend - pos) < room ? tend : pos + room;
+      for (u32 i0 = pos + u32(warp) * kRows + s8; i0 < end; i0 += kStep * kUnroll) {
+        u32 row[kUnroll];
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+          const u32 i = i0 + u * kStep;
+          row[u] = (i < end && qvalid) ? __ldg(ta.ridx + i) : kNoRow;
+        }
+        uint4 v[kUnroll];
+        u32 gq[kUnroll], hq[kUnroll];
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+          v[u] = make_uint4(0u, 0u, 0u, 0u);
+          gq[u] = 0u;
+          hq[u] = 0u;
+          if (row[u] != kNoRow) {
+            v[u] = load_codes(base + u64(row[u]) * a.bstride, line_rows);
+            load_q<QUANT>(ta, sc, i0 + u * kStep, gq[u], hq[u]);
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+          if (row[u] == kNoRow) continue;
+          u32 t0 = rot8 ? v[u].z : v[u].x, t1 = rot8 ? v[u].w : v[u].y;
+          u32 t2 = rot8 ? v[u].x : v[u].z, t3 = rot8 ? v[u].y : v[u].w;
+          const u32 x0 = rot4 ? t1 : t0, x1 = rot4 ? t2 : t1, x2 = rot4 ? t3 : t2, x3 = rot4 ? t0 : t3;
+          const u32 w[4] = {__funnelshift_r(x0, x1, rsh), __funnelshift_r(x1, x2, rsh), __funnelshift_r(x2, x3, rsh),
+                            __funnelshift_r(x3, x0, rsh)};
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const u32 b = (w[j >> 2] >> (8 * (j & 3))) & 0xffu;
+            const u32 cell = b * kWide + q16 + ((rot + u32(j)) & 15u);
+            atomicAdd(Lg + cell, gq[u]);
+            atomicAdd(Lh + cell, hq[u]);
+          }
+        }
+      }
+      in_window += end - pos;
+      pos = end;
+      if (in_window == u32(kWindowRows)) {
+        __syncthreads();
+        fold();
+        __syncthreads();
+        in_window = 0;
+      }
+    }
+  }
+}
+
+template <bool QUANT>
+void launch_hist_wide_variant(const HistArgs& a, i64* scratch, u64 scratch_elems, cudaStream_t s) {
+  constexpr int kSmem = 256 * kWide * 8;
+  static thread_local int configured_device = -1;
+  static thread_local int grid_cap = 0;
+  int dev = 0;
+  DP_CUDA(cudaGetDevice(&dev));
+  if (configured_device != dev) {
+    DP_CUDA(cudaFuncSetAttribute(k_hist_wide<QUANT>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem));
+    int sms = 0, per_sm = 0;
+    DP_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    DP_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_hist_wide<QUANT>, 1024, kSmem));
+    grid_cap = sms * (per_sm > 0 ? per_sm : 1);
+    configured_device = dev;
+  }
+  const u32 grid = (a.ntasks_dev || a.ntasks >= u32(grid_cap)) ? u32(grid_cap) : a.ntasks;
+  need(scratch_elems >= u64(grid) * 2 * 256 * kWide, "internal error: histogram window scratch too small for the grid");
+  DP_CUDA(cudaMemsetAsync(a.counter, 0, sizeof(u32), s));
+  k_hist_wide<QUANT><<<grid, 1024, kSmem, s>>>(a, reinterpret_cast<long long*>(scratch));
+}
+
 template <int MB, int THREADS, bool QUANT>
 void launch_hist_variant(const HistArgs& a, cudaStream_t s) {
   constexpr int kSmem = MB * kFT * (4 + 4) + kFT * (MB + 1) * (8 + 8);
@@ -344,6 +523,28 @@ void launch_histograms(const u8* bins, u64 bin_stride, u32 F, int max_bins, bool
     if (quantized_gh) launch_hist_variant<256, DP_HIST_THREADS, true>(a, s);
     else launch_hist_variant<256, DP_HIST_THREADS, false>(a, s);
   }
+  after_launch("histograms");
+}
+
+u64 hist_wide_scratch_elems() {
+  int dev = 0, sms = 148, per_sm = 1;
+  DP_CUDA(cudaGetDevice(&dev));
+  DP_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  DP_CUDA(cudaFuncSetAttribute(k_hist_wide<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 256 * kWide * 8));
+  DP_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_hist_wide<true>, 1024, 256 * kWide * 8));
+  return u64(sms) * u64(per_sm > 0 ? per_sm : 1) * 2 * 256 * kWide;
+}
+
+void launch_histograms_wide(const u8* bins, u64 bin_stride, u32 F, bool quantized_gh, const TreeArrays* trees,
+                            const Scales* scales, const HistTask* tasks, u32 ntasks, u32* counter, i64* hist,
+                            cudaStream_t s, const u32* ntasks_dev, const HistLayout* layout, i64* scratch,
+                            u64 scratch_elems) {
+  if (!ntasks && !ntasks_dev) return;
+  const HistLayout lay = layout ? *layout : HistLayout{F, u64(F) * 2 * kMaxBins, 0};
+  need(lay.fg > 0, "histogram layout needs a positive feature group size");
+  const HistArgs a{bins, bin_stride, F, ntasks, ntasks_dev, trees, scales, tasks, counter, hist, lay};
+  if (quantized_gh) launch_hist_wide_variant<true>(a, scratch, scratch_elems, s);
+  else launch_hist_wide_variant<false>(a, scratch, scratch_elems, s);
   after_launch("histograms");
 }
 

@@ -89,7 +89,7 @@ __global__ void k_round_init(RoundBuffers b, u64 R, const i64* __restrict__ tota
 // Histogram tasks of the build list: about four tasks per SM of equal row
 // counts, the feature tiles of one row range adjacent in the queue so that
 // blocks running at the same time read all sectors of the same rows.
-__global__ void __launch_bounds__(kBook) k_hist_tasks(RoundBuffers b, u32 ftiles, u32 nsm, int depth) {
+__global__ void __launch_bounds__(kBook) k_hist_tasks(RoundBuffers b, u32 ftiles, u32 tile, u32 nsm, int depth) {
   __shared__ i64 s_begin[kBook], s_count[kBook];
   __shared__ u32 s_slot[kBook], s_tree[kBook];
   const u32 nb = b.ctr->n_build;
@@ -120,7 +120,7 @@ __global__ void __launch_bounds__(kBook) k_hist_tasks(RoundBuffers b, u32 ftiles
       const i64 beg = beg0 + p * piece < end0 ? beg0 + p * piece : end0;
       const i64 end = beg + piece < end0 ? beg + piece : end0;
       // a node covered by one row range is the only writer of its tiles
-      b.hist_tasks[t] = HistTask{s_slot[j], ft * kHistFeatureTile, s_tree[j], np == 1 ? 1u : 0u, beg, end};
+      b.hist_tasks[t] = HistTask{s_slot[j], ft * tile, s_tree[j], np == 1 ? 1u : 0u, beg, end};
     });
   }
   // split-evaluation inputs of the open nodes; a node in slot ns + j (the
@@ -398,8 +398,8 @@ void launch_round_init(const RoundBuffers& b, u64 R, const i64* gh_totals, cudaS
   after_launch("round_init");
 }
 
-void launch_hist_tasks(const RoundBuffers& b, u32 ftiles, int depth, cudaStream_t s) {
-  k_hist_tasks<<<1, kBook, 0, s>>>(b, ftiles, u32(sm_count()), depth);
+void launch_hist_tasks(const RoundBuffers& b, u32 ftiles, u32 tile, int depth, cudaStream_t s) {
+  k_hist_tasks<<<1, kBook, 0, s>>>(b, ftiles, tile, u32(sm_count()), depth);
   after_launch("hist_tasks");
 }
 

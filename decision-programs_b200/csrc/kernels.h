@@ -110,6 +110,15 @@ void launch_histograms(const u8* bins, u64 bin_stride, u32 F, int max_bins, bool
                        u32* counter, i64* hist, cudaStream_t s, const u32* ntasks_dev = nullptr,
                        const HistLayout* layout = nullptr);
 constexpr u32 kHistFeatureTile = 32;
+// The 256-bin build over 64-feature tasks (HistTask.f0 a multiple of 64):
+// same inputs and output as launch_histograms, plus a scratch of at least
+// hist_wide_scratch_elems() int64 for the window sums (one launch at a time).
+constexpr u32 kHistWideTile = 64;
+void launch_histograms_wide(const u8* bins, u64 bin_stride, u32 F, bool quantized_gh, const TreeArrays* trees,
+                            const Scales* scales, const HistTask* tasks, u32 ntasks, u32* counter, i64* hist,
+                            cudaStream_t s, const u32* ntasks_dev, const HistLayout* layout, i64* scratch,
+                            u64 scratch_elems);
+u64 hist_wide_scratch_elems();
 // Rows per histogram task for a launch over `total_rows` row-tiles (about
 // four tasks per SM; tasks tasks of one node and tile stay contiguous).
 u64 hist_chunk_rows(u64 total_rows);

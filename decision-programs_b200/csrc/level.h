@@ -89,7 +89,9 @@ struct RoundBuffers {
 void launch_round_init(const RoundBuffers& b, u64 R, const i64* gh_totals, cudaStream_t s);
 // Histogram tasks of the build list, and the split-evaluation inputs of every
 // open node.
-void launch_hist_tasks(const RoundBuffers& b, u32 ftiles, int depth, cudaStream_t s);
+// `tile` features per task (32, or 64 for the wide histogram kernel); ftiles
+// tasks per row range.
+void launch_hist_tasks(const RoundBuffers& b, u32 ftiles, u32 tile, int depth, cudaStream_t s);
 // Zeroes max(device n_build, min_slots) histogram slots.
 void launch_zero_slots(const RoundBuffers& b, i64* hist, u64 slot_elems, u64 min_slots, cudaStream_t s);
 // Splits (depth < max_depth, gain > 0) or closes every open node.

@@ -149,6 +149,32 @@ def test_histograms_match_oracle(dp, orc, F, nodes, seed, nbins, R):
     assert (ohist[-1] == 0).all()
 
 
+@pytest.mark.parametrize("wide", ["0", "1"])
+@pytest.mark.parametrize("F,nodes,chunk", [(64, 1, 0), (100, 3, 40000), (160, 2, 70000)])
+def test_both_256_bin_kernels_with_long_tasks(dp, orc, monkeypatch, wide, F, nodes, chunk):
+    """The 32- and 64-feature 256-bin kernels (DP_HIST_WIDE) on tasks long
+    enough to fold several 16383-row windows (DP_HIST_MIN_CHUNK), with
+    partial last tiles and a feature count above one tile."""
+    monkeypatch.setenv("DP_HIST_WIDE", wide)
+    if chunk:
+        monkeypatch.setenv("DP_HIST_MIN_CHUNK", str(chunk))
+    R = 150000
+    rng = np.random.default_rng(40 + F)
+    stride = (F + 15) // 16 * 16
+    bins = rng.integers(0, 256, (R, stride)).astype(np.uint8)
+    bins[:, F:] = 0
+    gh = np.stack([rng.standard_normal(R), rng.random(R)], 1).astype(np.float32)
+    ridx = rng.permutation(R).astype(np.uint32)
+    cuts = np.sort(rng.choice(np.arange(1, R), nodes - 1, replace=False)) if nodes > 1 else np.array([], np.int64)
+    edges = np.concatenate([[0], cuts, [R]]).astype(np.int64)
+    sb, se = np.ascontiguousarray(edges[:-1]), np.ascontiguousarray(edges[1:])
+    sg, sh = orc.quantizer(gh)
+    hist = torch.zeros((len(sb), F, 256, 2), dtype=torch.int64, device="cuda")
+    dp.check(dp.lib().dp_hist_build(ptr(cuda(bins)), stride, F, 256, ptr(cuda(gh)), ptr(cuda(ridx)), sb.ctypes.data,
+                                    se.ctypes.data, len(sb), sg, sh, ptr(hist), None))
+    np.testing.assert_array_equal(hist.cpu().numpy(), orc.histograms(bins, F, gh, ridx, sb, se, sg, sh, threads=4))
+
+
 @pytest.mark.parametrize("lam,alpha,gamma,mcw,nan_frac", [(1.0, 0.0, 0.0, 1.0, 0.0), (2.0, 0.5, 0.3, 5.0, 0.1),
                                                           (0.0, 0.0, 0.0, 0.0, 0.3), (1.0, 2.0, 0.0, 0.1, 0.0)])
 def test_split_evaluation_matches_oracle(dp, orc, lam, alpha, gamma, mcw, nan_frac):

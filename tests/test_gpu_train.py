@@ -121,6 +121,18 @@ def test_deep_trees_with_exact_level_counts(dp, orc, monkeypatch, objective, K):
     run(dp, orc, x, y, objective, 3, K=K, max_depth=13, min_child_weight=0.0)
 
 
+@pytest.mark.parametrize("wide", ["0", "1"])
+def test_both_histogram_kernels_train_the_same_trees(dp, orc, monkeypatch, wide):
+    """Training with the 32- or the 64-feature histogram kernel (DP_HIST_WIDE),
+    a feature count that leaves the last tile partial, and missing values."""
+    monkeypatch.setenv("DP_HIST_WIDE", wide)
+    rng = np.random.default_rng(31)
+    x = rng.standard_normal((9000, 100)).astype(np.float32)
+    x[rng.random(x.shape) < 0.03] = np.nan
+    y = (np.nan_to_num(x[:, 0]) + 0.5 * np.nan_to_num(x[:, 77]) + 0.2 * rng.standard_normal(9000)).astype(np.float32)
+    run(dp, orc, x, y, "reg:squarederror", 3, max_depth=6)
+
+
 def test_deep_trees_device_resident_levels(dp, orc):
     x, y = c1_data(6000, seed=12)
     run(dp, orc, x, y, "binary:logistic", 2, max_depth=14, min_child_weight=0.0, reg_lambda=0.1)
