@@ -223,27 +223,6 @@ void launch_eval_splits(const i64* hist, u32 F, const u16* nbins, const u8* has_
   after_launch("reduce_splits");
 }
 
-void launch_eval_splits_dev(const i64* hist, u32 F, const u16* nbins, const u8* has_missing, const EvalNode* nodes,
-                            const u32* nnodes_dev, const Scales* scales, SplitParams p, SplitCand* cand,
-                            SplitCand* best, cudaStream_t s, u32 fstride, u32 f_base, const u32* fmask,
-                            u32 mask_words, const i64* parent_hist, int store_derived) {
-  int dev = 0, sms = 148;
-  DP_CUDA(cudaGetDevice(&dev));
-  DP_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-  // at least one chunk, so that a node over zero features still gets its
-  // "no candidate" entry
-  const u32 nchunks = F ? (F + kEvalFeatureChunk - 1) / kEvalFeatureChunk : 1;
-  // with one feature chunk the chunk candidate is the node's best
-  k_eval_dev<<<sms * 8, kEvalThreads, 0, s>>>(const_cast<i64*>(hist), F, nbins, has_missing, nodes, scales, p,
-                                               nchunks, nnodes_dev, nchunks == 1 ? best : cand, fstride ? fstride : F,
-                                               f_base, fmask, mask_words, parent_hist, store_derived);
-  after_launch("eval_splits");
-  if (nchunks > 1) {
-    k_reduce_cands<<<sms, 128, 0, s>>>(cand, 0, nnodes_dev, nchunks, best);
-    after_launch("reduce_splits");
-  }
-}
-
 void launch_eval_candidates_dev(const i64* hist, u32 F, const u16* nbins, const u8* has_missing,
                                 const EvalNode* nodes, const u32* nnodes_dev, const Scales* scales, SplitParams p,
                                 SplitCand* cand, u32 nchunks, cudaStream_t s, u32 fstride, u32 f_base,

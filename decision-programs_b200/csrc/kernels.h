@@ -145,17 +145,12 @@ constexpr u32 kEvalFeatureChunk = 16;
 // Per (node, feature chunk) candidates only, cand[node * nchunks + chunk],
 // with nchunks >= ceil(F / kEvalFeatureChunk) and >= 1 (chunks past the
 // features hold "no candidate"); the caller takes the best over chunks.
+// Derived siblings read parent_hist; with store_derived their histograms are
+// written into their slots (needed when the next level subtracts from them).
 void launch_eval_candidates_dev(const i64* hist, u32 F, const u16* nbins, const u8* has_missing,
                                 const EvalNode* nodes, const u32* nnodes_dev, const Scales* scales, SplitParams p,
                                 SplitCand* cand, u32 nchunks, cudaStream_t s, u32 fstride, u32 f_base,
                                 const u32* fmask, u32 mask_words, const i64* parent_hist, int store_derived);
-// Derived siblings read parent_hist; with store_derived their histograms are
-// written into their slots (needed when the next level subtracts from them).
-void launch_eval_splits_dev(const i64* hist, u32 F, const u16* nbins, const u8* has_missing, const EvalNode* nodes,
-                            const u32* nnodes_dev, const Scales* scales, SplitParams p, SplitCand* cand,
-                            SplitCand* best, cudaStream_t s, u32 fstride = 0, u32 f_base = 0,
-                            const u32* fmask = nullptr, u32 mask_words = 0, const i64* parent_hist = nullptr,
-                            int store_derived = 0);
 
 // ---- partition ----------------------------------------------------------------
 struct PartTask {
