@@ -174,13 +174,29 @@ __global__ void __launch_bounds__(kBook) k_decide(RoundBuffers b, const float* _
     if (valid) {
       o = b.open_cur[i];
       if (depth < max_depth) {
-        bool first = true;
-        for (u32 r = 0; r < b.nranks; ++r)
-          for (u32 c = 0; c < b.nchunks; ++c) {
-            const SplitCand x = b.cands[(u64(r) * b.cap_split + i) * b.nchunks + c];
-            if (first || x.gain > bs.gain) bs = x;
-            first = false;
+        // the first maximum over (rank, chunk) in that order: gains are read
+        // eight at a time with independent loads, then the winner whole
+        const u32 nk = b.nranks * b.nchunks;
+        u32 best_k = 0;
+        double best_g = 0.0;
+        for (u32 k0 = 0; k0 < nk; k0 += 8) {
+          double g[8];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const u32 k = k0 + u, r = k / b.nchunks, c = k - r * b.nchunks;
+            g[u] = k < nk ? b.cands[(u64(r) * b.cap_split + i) * b.nchunks + c].gain : 0.0;
           }
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const u32 k = k0 + u;
+            if (k < nk && (k == 0 || g[u] > best_g)) {
+              best_g = g[u];
+              best_k = k;
+            }
+          }
+        }
+        const u32 r = best_k / b.nchunks, c = best_k - r * b.nchunks;
+        bs = b.cands[(u64(r) * b.cap_split + i) * b.nchunks + c];
       }
     }
     const bool split = valid && depth < max_depth && bs.feature >= 0 && bs.gain > 0.0;
