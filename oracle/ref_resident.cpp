@@ -13,7 +13,9 @@
 // "slice_rounds"}; <dir>/values.f32 [rows][features]; <dir>/labels.u32 [rows].
 // Writes model.json, slice.json (the first slice_rounds rounds), classes.f32
 // [rows], margins.f32 / probs.f32 [rows][classes], slice_margins.f32 and
-// restored_margins.f32 (after restoring model.json), session.json.
+// restored_margins.f32 (after restoring model.json), model2.json (a second
+// trial on the same matrix: depth second_max_depth, eta 0.5, lambda 2),
+// session.json.
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -112,8 +114,17 @@ int main(int argc, char** argv) {
     auto restored = take(trainer.predict(values, R, true), R * K);
     spill(dir + "/restored_margins.f32", restored.data(), restored.size() * 4);
 
+    // a second trial on the same resident matrix, as hyper-parameter search
+    // and out-of-fold teachers do (class_study_train.cu:324-332)
+    nlohmann::json hp2 = hp;
+    hp2["max_depth"] = meta.value("second_max_depth", 3);
+    hp2["eta"] = 0.5;
+    hp2["lambda"] = 2.0;
+    const auto second = trainer.train(hp2);
+    spill(dir + "/model2.json", second.model_json.data(), second.model_json.size());
+
     nlohmann::json out = {{"session", trainer.metadata()}, {"train_metrics", trained.metrics},
-                          {"slice_metrics", sliced.metrics}};
+                          {"slice_metrics", sliced.metrics}, {"second_metrics", second.metrics}};
     const auto s = out.dump();
     spill(dir + "/session.json", s.data(), s.size());
     cudaFree(values);

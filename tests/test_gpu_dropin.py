@@ -161,3 +161,13 @@ def test_reference_resident_trainer_lifecycle(orc, tmp_path):
     session = json.loads((tmp_path / "session.json").read_text())
     assert session["train_metrics"]["CUDA_training"] is True
     assert session["slice_metrics"]["FIT_performed"] is False
+    # a second trial on the same resident matrix (the search / out-of-fold reuse)
+    assert session["second_metrics"]["trial"] == 2 and session["second_metrics"]["matrix_creations"] == 1
+    o2 = orc.Model(x, y.astype(np.float32), "multi:softmax", num_class=K, max_depth=3, max_bin=256, eta=0.5,
+                   reg_lambda=2.0, rounds=rounds, threads=4)
+    trees2 = json.loads((tmp_path / "model2.json").read_text())["learner"]["gradient_booster"]["model"]["trees"]
+    assert len(trees2) == o2.num_trees()
+    for i, t in enumerate(trees2):
+        ot = o2.tree(i)
+        np.testing.assert_array_equal(np.array(t["split_indices"]), ot["split_indices"])
+        np.testing.assert_array_equal(bits(t["split_conditions"]), bits(ot["split_conditions"]))
