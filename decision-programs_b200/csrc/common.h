@@ -2,6 +2,7 @@
 // launch accounting.
 #pragma once
 #include <cuda_runtime.h>
+#include <nvtx3/nvToolsExt.h>
 
 #include <atomic>
 #include <cstdint>
@@ -39,6 +40,15 @@ inline void cuda_check(cudaError_t e, const char* what) {
 // benchmark reports; kernel launches never read it).
 std::atomic<u64>& launch_counter();
 inline void count_launch(u64 n = 1) { launch_counter().fetch_add(n, std::memory_order_relaxed); }
+
+// NVTX range for the duration of a scope (what a system profiler shows for
+// the host side of rounds, levels and decodes; no cost without a profiler).
+struct NvtxRange {
+  explicit NvtxRange(const char* name) { nvtxRangePushA(name); }
+  ~NvtxRange() { nvtxRangePop(); }
+  NvtxRange(const NvtxRange&) = delete;
+  NvtxRange& operator=(const NvtxRange&) = delete;
+};
 // Checks the launch that was just issued and counts it.
 inline void after_launch(const char* what) {
   cuda_check(cudaGetLastError(), what);

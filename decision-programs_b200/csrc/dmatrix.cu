@@ -101,6 +101,7 @@ void DMatrix::set_labels_device(const float* y, u64 n) {
 void DMatrix::set_labels_host(const float* y, u64 n) { set_labels_device(y, n); }
 
 const Quantized& DMatrix::quantized(int max_bin, Comm* comm, cudaStream_t s) {
+  NvtxRange nv("dp_gbdt: cuts and bins");
   if (q_ && q_->max_bin == max_bin) return *q_;
   DeviceGuard g(device_);
   auto q = std::make_unique<Quantized>();

@@ -436,6 +436,7 @@ void Engine::drop_graph() {
 
 void Engine::boost_round(Model& m) {
   DeviceGuard g(device_);
+  NvtxRange nv("dp_gbdt: boosting round");
   const auto t_round = std::chrono::steady_clock::now();
   // Rounds after the first replay one CUDA graph of the whole round when every
   // level stays within the asynchronous bounds (nothing then waits on the
@@ -550,7 +551,10 @@ Engine::RoundOut Engine::enqueue_round() {
   std::vector<int> pi_hist(D, -1), pi_eval(D, -1);
   int set = 0, region = 0, depth = 0;
   bool zeroed_by_children = false;  // this level's output slots were zeroed by the previous level
+  static const char* const kLevelNames[] = {"level 0", "level 1", "level 2", "level 3", "level 4", "level 5",
+                                             "level 6", "level 7", "level 8", "level 9", "level 10+"};
   for (; depth < D; ++depth) {
+    NvtxRange nv_level(kLevelNames[depth < 10 ? depth : 10]);
     u64 nbuild_hi = depth == 0 ? u64(K) : (open_hi + 1) / 2;
     if (open_hi > async_open_limit_ || open_hi * slot_bytes > async_hist_bytes_) {
       RoundCounters* c_h = reinterpret_cast<RoundCounters*>(arena_.get());  // the arena's head
@@ -673,6 +677,7 @@ Engine::RoundOut Engine::enqueue_round() {
 }
 
 void Engine::finish_round(Model& m, const RoundOut& out) {
+  NvtxRange nv("dp_gbdt: round read-back");
   const int K = K_;
   const u32 F = F_;
   const int D = p_.max_depth;

@@ -516,6 +516,7 @@ bool csv_parse_feature_host(const unsigned char* p, u32 n, float* value) {
 
 std::unique_ptr<CsvDense> csv_decode(const char* bytes, u64 n, const std::string& target,
                                      const std::string& header_mode, cudaStream_t s) {
+  NvtxRange nv("dp_gbdt: CSV decode");
   auto out = std::make_unique<CsvDense>();
   cudaEvent_t ev0, ev1;
   DP_CUDA(cudaEventCreate(&ev0));
