@@ -180,7 +180,7 @@ __global__ void __launch_bounds__(kEvalThreads) k_eval(i64* hist, u32 F,
 }
 
 // Node count in device memory: a fixed grid walks the work items.
-__global__ void __launch_bounds__(kEvalThreads, 3) k_eval_dev(i64* hist, u32 F,
+__global__ void __launch_bounds__(kEvalThreads, 4) k_eval_dev(i64* hist, u32 F,
                                                            const u16* __restrict__ nbins,
                                                            const u8* __restrict__ has_missing,
                                                            const EvalNode* __restrict__ nodes,
