@@ -386,8 +386,9 @@ def csv_bench(dp, peak_gbs: float, cpu: bool) -> dict:
     out = {"rows": rows, "features": cols, "bytes": len(data), "device_ms": dev, "e2e_ms": e2e,
            "device_GBps": len(data) / (dev / 1e3) / 1e9, "e2e_GBps": len(data) / (e2e / 1e3) / 1e9,
            "device_frac_hbm_one_pass": len(data) / (dev / 1e3) / 1e9 / peak_gbs,
-           "note": "device time excludes the host->device copy of the text; the text is read about four times "
-                   "(quote count, delimiter count and write, field scan)"}
+           "note": "device time excludes the host->device copy of the text and the allocation made once the "
+                   "delimiters are counted; the text is read about four times (quote count, delimiter count and "
+                   "write, field scan)"}
     ref = ROOT / "oracle" / "_ref" / "ref_csv"
     if cpu and ref.exists():
         import subprocess
