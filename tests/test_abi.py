@@ -18,8 +18,8 @@ def declared_symbols():
 
 def test_header_declares_the_reference_subset():
     names = set(declared_symbols())
-    # every symbol the reference dlsym's on the training path (SURVEY-free list:
-    # native/class_native_training.cuh:51-69, native/class_model_native_adapter.cuh:21-30)
+    # every symbol the reference dlsym's on the training path
+    # (native/class_native_training.cuh:51-69, native/class_model_native_adapter.cuh:21-30)
     for s in ["XGBoostVersion", "XGBuildInfo", "XGBGetLastError", "XGDMatrixCreateFromCudaArrayInterface",
               "XGDMatrixSetInfoFromInterface", "XGBoosterCreate", "XGBoosterSetParam", "XGBoosterUpdateOneIter",
               "XGBoosterSaveJsonConfig", "XGBoosterBoostedRounds", "XGBoosterSaveModel",
