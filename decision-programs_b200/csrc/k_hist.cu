@@ -21,6 +21,13 @@
 //  * rows are gathered through the node's row-index segment; (g, h) is read
 //    in position order, already quantised to int32 pairs by the training
 //    engine (the kernel-level entry point may pass fp32 pairs instead).
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cstdlib>
+#include <cstring>
+
 #include "kernels.h"
 
 namespace dp {
@@ -487,6 +494,406 @@ void launch_hist_wide_variant(const HistArgs& a, i64* scratch, u64 scratch_elems
   k_hist_wide<QUANT><<<grid, 1024, kSmem, s>>>(a, reinterpret_cast<long long*>(scratch));
 }
 
+// ---------------------------------------------------------------------------
+// The 64-feature kernel with the row codes brought into shared memory by the
+// tensor memory accelerator instead of per-lane global loads: one untiled
+// bulk copy per row (cp.async.bulk), or with GATHER one tiled gather of four
+// rows per instruction (cp.async.bulk.tensor tile::gather4 over a tensor map
+// of the bin matrix: box `pitch` bytes x 1 row).
+//
+// Each warp owns two stages of 24 rows x 64 bytes and one mbarrier per stage,
+// and takes chunks of 24 consecutive row positions of the window (chunk c
+// goes to warp c mod 32).  Lanes 0..23 read the chunk's row indices; lanes
+// issue the chunk's copies (24 row copies, or 6 gathers of four rows whose
+// indices come by shuffles) and lane 0 arms the stage's barrier with the
+// chunk's byte count.  While the atomics of one chunk run, the copies of
+// the warp's next two chunks are in flight, and the scattered row reads use
+// the copy engine rather than the L1 load path that the shared atomics also
+// occupy.  The atomics, planes, window folds and drain are k_hist_wide's.
+//
+// Every barrier wait is bounded (about a second of global timer): a wait that
+// runs out ORs the status bit, the warp stops issuing, and the blocks leave
+// at their next task fetch after a bounded wait for their copies in flight.
+constexpr int kBulkRows = 24;
+constexpr int kBulkStages = 2;
+constexpr int kBulkStageBytes = kBulkRows * kWide;
+// planes, 128 bytes of alignment room, stages (128-byte aligned), barriers
+constexpr int kBulkSmem = 256 * kWide * 8 + 128 + 32 * kBulkStages * kBulkStageBytes + 32 * kBulkStages * 8;
+constexpr u64 kBulkWaitNs = 1000000000ull;
+
+__device__ __forceinline__ void mbar_init(u32 bar, u32 count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect(u32 bar, u32 bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(u32 bar, u32 parity) {
+  u32 ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ u64 global_ns() {
+  u64 t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// true when the barrier's phase of this parity completed, false after about
+// kBulkWaitNs without completion
+__device__ __forceinline__ bool mbar_wait_bounded(u32 bar, u32 parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const u64 t0 = global_ns();
+  for (u32 it = 1; it < (1u << 28); ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 255u) == 0 && global_ns() - t0 > kBulkWaitNs) return false;
+  }
+  return false;
+}
+
+// global -> this CTA's shared memory, completion counted on `bar` in bytes;
+// dst, src and bytes multiples of 16
+__device__ __forceinline__ void bulk_copy_g2s(u32 dst, const void* src, u32 bytes, u32 bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(bar)
+               : "memory");
+}
+
+// four rows (r0..r3) x the box width from column x of the tensor map's bin
+// matrix, one after the other into shared memory at dst (128-byte aligned)
+__device__ __forceinline__ void gather4_g2s(u32 dst, const CUtensorMap* map, int x, u32 r0, u32 r1, u32 r2, u32 r3,
+                                            u32 bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];" ::"r"(dst),
+      "l"(reinterpret_cast<u64>(map)), "r"(x), "r"(r0), "r"(r1), "r"(r2), "r"(r3), "r"(bar)
+      : "memory");
+}
+
+// The 64 shared-atomic pairs of one row's 16 codes held by lane (s, q) of
+// the 64-feature kernels: codes rotated by `rot` bytes (rot8, rot4, rsh its
+// word and byte parts) so that atomic step j updates feature
+// q16 + ((rot + j) & 15) of the tile.
+__device__ __forceinline__ void add_codes(u32* Lg, u32* Lh, uint4 v, u32 gq, u32 hq, bool rot8, bool rot4, u32 rsh,
+                                          u32 rot, u32 q16) {
+  const u32 t0 = rot8 ? v.z : v.x, t1 = rot8 ? v.w : v.y;
+  const u32 t2 = rot8 ? v.x : v.z, t3 = rot8 ? v.y : v.w;
+  const u32 x0 = rot4 ? t1 : t0, x1 = rot4 ? t2 : t1, x2 = rot4 ? t3 : t2, x3 = rot4 ? t0 : t3;
+  const u32 w[4] = {__funnelshift_r(x0, x1, rsh), __funnelshift_r(x1, x2, rsh), __funnelshift_r(x2, x3, rsh),
+                    __funnelshift_r(x3, x0, rsh)};
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const u32 b = (w[j >> 2] >> (8 * (j & 3))) & 0xffu;
+    const u32 cell = b * kWide + q16 + ((rot + u32(j)) & 15u);
+    atomicAdd(Lg + cell, gq);
+    atomicAdd(Lh + cell, hq);
+  }
+}
+
+template <bool QUANT, bool GATHER>
+__global__ void __launch_bounds__(1024) k_hist_bulk(HistArgs a, long long* __restrict__ wscr, u32* __restrict__ status,
+                                                    u32 status_bit, u32 pitch, u32 copy_warps,
+                                                    const __grid_constant__ CUtensorMap map) {
+  constexpr int MB = 256, THREADS = 1024, kWarps = THREADS / 32;
+  constexpr int kCells = MB * kWide;
+  constexpr int kSteps = kBulkRows / 8;  // 8-row steps per chunk
+  extern __shared__ __align__(16) unsigned char smem[];
+  __shared__ u32 s_task;
+  __shared__ u32 s_abort;
+  u32* Lg = reinterpret_cast<u32*>(smem);
+  u32* Lh = Lg + kCells;
+  const u32 planes_end = smem_addr(smem) + 2u * kCells * 4u;
+  unsigned char* stages = smem + 2 * kCells * 4 + (((planes_end + 127u) & ~127u) - planes_end);
+  unsigned long long* bars =
+      reinterpret_cast<unsigned long long*>(stages + kWarps * kBulkStages * kBulkStageBytes);
+  long long* Sg = wscr + u64(blockIdx.x) * 2 * kCells;
+  long long* Sh = Sg + kCells;
+  for (int i = threadIdx.x; i < kCells; i += THREADS) {
+    Lg[i] = 0u;
+    Lh[i] = 0u;
+  }
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  unsigned char* my_stages = stages + warp * kBulkStages * kBulkStageBytes;
+  const u32 stage_s = smem_addr(my_stages);
+  const u32 bar = smem_addr(bars + warp * kBulkStages);  // stage k's barrier at bar + 8 k
+  if (lane < kBulkStages) mbar_init(bar + 8u * u32(lane), 1u);
+  if (threadIdx.x == 0) s_abort = 0;
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  const u32 s8 = u32(lane) >> 2, q = u32(lane & 3);
+  const u32 rot = (s8 + 8u * (q >> 1)) & 15u;
+  const bool rot8 = (rot & 8u) != 0, rot4 = (rot & 4u) != 0;
+  const u32 rsh = 8u * (rot & 3u);
+  const u32 q16 = 16u * q;
+  u32 key_slot = kNoRow, key_f0 = 0, key_tree = 0;
+  bool key_excl = false;
+  u32 in_window = 0;
+  bool s_clean = true;
+  u32 parity = 0;     // bit k: the phase parity that stage k's next wait expects
+  u32 pending = 0;    // bit k: stage k has copies issued and not yet waited for
+  bool stop = false;  // this warp's wait ran out
+  const u32 ntasks = a.ntasks_dev ? *a.ntasks_dev : a.ntasks;
+  __syncthreads();
+
+  auto fold = [&]() {
+    for (int i = threadIdx.x; i < kCells; i += THREADS) {
+      const long long g = static_cast<long long>(static_cast<int>(Lg[i]));
+      const long long h = static_cast<long long>(Lh[i]);
+      Sg[i] = s_clean ? g : Sg[i] + g;
+      Sh[i] = s_clean ? h : Sh[i] + h;
+      Lg[i] = 0u;
+      Lh[i] = 0u;
+    }
+    s_clean = false;
+  };
+
+  for (;;) {
+    if (threadIdx.x == 0) s_task = *reinterpret_cast<volatile u32*>(&s_abort) ? 0xffffffffu : atomicAdd(a.counter, 1u);
+    __syncthreads();
+    const u32 ti = s_task;
+    const bool done = ti >= ntasks;
+    HistTask t{};
+    if (!done) t = a.tasks[ti];
+    const bool same = !done && t.slot == key_slot && t.f0 == key_f0 && t.tree == key_tree;
+    if (!same && key_slot != kNoRow) {
+      i64* out = a.hist + u64(key_slot) * a.layout.slot_stride;
+      for (int i = threadIdx.x; i < kCells; i += THREADS) {
+        const int b = i / kWide, f = i % kWide;
+        long long gs = static_cast<long long>(static_cast<int>(Lg[i]));
+        long long hs = static_cast<long long>(Lh[i]);
+        if (!s_clean) {
+          gs += Sg[i];
+          hs += Sh[i];
+        }
+        Lg[i] = 0u;
+        Lh[i] = 0u;
+        const u32 gf = key_f0 + u32(f);
+        if (gf >= a.F) continue;
+        const u32 grp = gf / a.layout.fg, fl = gf - grp * a.layout.fg;
+        i64* cell = out + grp * a.layout.group_stride + (u64(fl) * kMaxBins + b) * 2;
+        if (key_excl) {
+          *reinterpret_cast<longlong2*>(cell) = make_longlong2(gs, hs);
+        } else if (gs | hs) {
+          atomicAdd(reinterpret_cast<unsigned long long*>(cell), static_cast<unsigned long long>(gs));
+          atomicAdd(reinterpret_cast<unsigned long long*>(cell) + 1, static_cast<unsigned long long>(hs));
+        }
+      }
+      s_clean = true;
+      key_slot = kNoRow;
+      in_window = 0;
+    }
+    if (done) break;
+    __syncthreads();
+    key_slot = t.slot;
+    key_f0 = t.f0;
+    key_tree = t.tree;
+    key_excl = t.excl != 0;
+    const TreeArrays ta = a.trees[t.tree];
+    Scales sc{1.f, 1.f};
+    if (!QUANT) sc = a.scales[t.tree];
+    // bytes of each row's copy: the tile's codes inside the row stride (a
+    // multiple of 16); lanes past them hold no feature of the matrix
+    const u32 cbytes = u32(min(u64(kWide), a.bstride - t.f0));
+    const bool qvalid = q16 < cbytes;
+    const u8* src = a.bins + t.f0;
+    u32 pos = u32(t.begin);
+    const u32 tend = u32(t.end);
+    while (pos < tend) {
+      const u32 room = u32(kWindowRows) - in_window;
+      const u32 end = (tend - pos) < room ? tend : pos + room;
+      const u32 nchunks = (end - pos + kBulkRows - 1) / kBulkRows;
+      auto chunk_rows = [&](u32 cc) { return cc < nchunks ? min(u32(kBulkRows), end - pos - cc * kBulkRows) : 0u; };
+      // lane l < n: the row index of the chunk's l-th position
+      auto load_row = [&](u32 cc) {
+        return u32(lane) < chunk_rows(cc) ? __ldg(ta.ridx + pos + cc * kBulkRows + lane) : 0u;
+      };
+      // the raw (g, h) words of the lane's three rows of the chunk
+      auto load_gh = [&](u32 cc, u32* g, u32* h) {
+        const u32 n = chunk_rows(cc);
+#pragma unroll
+        for (int u = 0; u < kSteps; ++u) {
+          const u32 r = u32(u) * 8u + s8;
+          g[u] = h[u] = 0u;
+          if (r < n && qvalid) {
+            const uint2 w = __ldg(reinterpret_cast<const uint2*>(ta.gh) + pos + cc * kBulkRows + r);
+            g[u] = w.x;
+            h[u] = w.y;
+          }
+        }
+      };
+      auto issue = [&](u32 cc, u32 st, u32 row) {
+        const u32 n = chunk_rows(cc);
+        if constexpr (GATHER) {
+          // gather l takes the rows of lanes 4l..4l+3; the chunk's last
+          // gather repeats its first row where the chunk ends
+          const u32 ng = (n + 3u) / 4u;
+          u32 rr[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) rr[j] = __shfl_sync(0xffffffffu, row, (4 * lane + j) & 31);
+#pragma unroll
+          for (int j = 1; j < 4; ++j)
+            if (4u * u32(lane) + u32(j) >= n) rr[j] = rr[0];
+          if (lane == 0) mbar_arrive_expect(bar + 8u * st, ng * 4u * pitch);
+          if (u32(lane) < ng)
+            gather4_g2s(stage_s + st * kBulkStageBytes + u32(lane) * 256u, &map, int(t.f0), rr[0], rr[1], rr[2], rr[3],
+                        bar + 8u * st);
+        } else {
+          if (lane == 0) mbar_arrive_expect(bar + 8u * st, n * cbytes);
+          if (u32(lane) < n)
+            bulk_copy_g2s(stage_s + st * kBulkStageBytes + u32(lane) * kWide, src + u64(row) * a.bstride, cbytes,
+                          bar + 8u * st);
+        }
+        pending |= 1u << st;
+      };
+      // Register pipeline: while chunk k is counted, the copies of chunks
+      // k+1 and k+2 are in flight, and so are the (g, h) of chunk k+1 and the
+      // row indices of chunk k+3, so no global load latency stands between
+      // two chunks.
+      if (u32(warp) >= copy_warps) {
+        // the other warps count their chunks from direct loads, two chunks
+        // (six row steps) in flight at a time
+        const u8* base = a.bins + t.f0 + q16;
+        const bool line_rows = (a.bstride & 127u) == 0;
+        for (u32 c = u32(warp); c < nchunks; c += 2u * kWarps) {
+          u32 row[2 * kSteps], at[2 * kSteps];
+#pragma unroll
+          for (int u = 0; u < 2 * kSteps; ++u) {
+            const u32 cc = c + u32(u / kSteps) * kWarps, r = u32(u % kSteps) * 8u + s8;
+            at[u] = pos + cc * kBulkRows + r;
+            row[u] = (r < chunk_rows(cc) && qvalid) ? __ldg(ta.ridx + at[u]) : kNoRow;
+          }
+          uint4 v[2 * kSteps];
+          u32 gq[2 * kSteps], hq[2 * kSteps];
+#pragma unroll
+          for (int u = 0; u < 2 * kSteps; ++u) {
+            v[u] = make_uint4(0u, 0u, 0u, 0u);
+            gq[u] = hq[u] = 0u;
+            if (row[u] != kNoRow) {
+              v[u] = load_codes(base + u64(row[u]) * a.bstride, line_rows);
+              load_q<QUANT>(ta, sc, at[u], gq[u], hq[u]);
+            }
+          }
+#pragma unroll
+          for (int u = 0; u < 2 * kSteps; ++u)
+            if (row[u] != kNoRow) add_codes(Lg, Lh, v[u], gq[u], hq[u], rot8, rot4, rsh, rot, q16);
+        }
+      }
+      u32 c = u32(warp);
+      if (u32(warp) < copy_warps && !stop) {
+        const u32 r0 = load_row(c), r1 = load_row(c + kWarps);
+        if (c < nchunks) issue(c, 0, r0);
+        if (c + kWarps < nchunks) issue(c + kWarps, 1, r1);
+      }
+      const bool copies = u32(warp) < copy_warps;
+      u32 row_ahead = copies ? load_row(c + 2u * kWarps) : 0u;
+      u32 gn[kSteps], hn[kSteps];
+      load_gh(copies ? c : nchunks, gn, hn);
+      for (u32 k = 0; copies && !stop && c < nchunks; ++k, c += kWarps) {
+        const u32 st = k & 1u;
+        // one decision for the warp, so that it stays converged
+        if (!__all_sync(0xffffffffu, mbar_wait_bounded(bar + 8u * st, (parity >> st) & 1u))) {
+          stop = true;
+          if (lane == 0) {
+            atomicOr(status, status_bit);
+            *reinterpret_cast<volatile u32*>(&s_abort) = 1u;
+          }
+          break;
+        }
+        parity ^= 1u << st;
+        pending &= ~(1u << st);
+        const u32 n = chunk_rows(c);
+        const unsigned char* sb = my_stages + st * kBulkStageBytes;
+        uint4 v[kSteps];
+        u32 gq[kSteps], hq[kSteps];
+        bool ok[kSteps];
+#pragma unroll
+        for (int u = 0; u < kSteps; ++u) {
+          const u32 r = u32(u) * 8u + s8;
+          ok[u] = r < n && qvalid;
+          // a gather's four rows sit at `pitch` bytes from a 256-byte slot
+          const u32 at = GATHER ? (r >> 2) * 256u + (r & 3u) * pitch : r * u32(kWide);
+          v[u] = ok[u] ? *reinterpret_cast<const uint4*>(sb + at + q16) : make_uint4(0u, 0u, 0u, 0u);
+          if (QUANT) {
+            gq[u] = gn[u];
+            hq[u] = hn[u];
+          } else {
+            gq[u] = u32(quantize(__uint_as_float(gn[u]), sc.sg));
+            hq[u] = u32(quantize(__uint_as_float(hn[u]), sc.sh));
+          }
+        }
+        load_gh(c + kWarps, gn, hn);
+        __syncwarp();
+        if (c + 2u * kWarps < nchunks) {
+          // the stage's reads above come before the copies that refill it
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          issue(c + 2u * kWarps, st, row_ahead);
+        }
+        row_ahead = load_row(c + 3u * kWarps);
+#pragma unroll
+        for (int u = 0; u < kSteps; ++u)
+          if (ok[u]) add_codes(Lg, Lh, v[u], gq[u], hq[u], rot8, rot4, rsh, rot, q16);
+      }
+      in_window += end - pos;
+      pos = end;
+      if (in_window == u32(kWindowRows)) {
+        __syncthreads();
+        fold();
+        __syncthreads();
+        in_window = 0;
+      }
+    }
+  }
+  // only a warp whose wait ran out leaves copies in flight: give them the
+  // same bounded time before the block's shared memory is released
+  for (u32 st = 0; st < u32(kBulkStages); ++st)
+    if ((pending >> st) & 1u) mbar_wait_bounded(bar + 8u * st, (parity >> st) & 1u);
+}
+
+template <bool QUANT, bool GATHER>
+void launch_hist_bulk_variant(const HistArgs& a, i64* scratch, u64 scratch_elems, u32* status, u32 status_bit,
+                              const HistBinsMap* map, cudaStream_t s) {
+  static thread_local int configured_device = -1;
+  static thread_local int grid_cap = 0;
+  int dev = 0;
+  DP_CUDA(cudaGetDevice(&dev));
+  if (configured_device != dev) {
+    DP_CUDA(cudaFuncSetAttribute(k_hist_bulk<QUANT, GATHER>, cudaFuncAttributeMaxDynamicSharedMemorySize, kBulkSmem));
+    int sms = 0, per_sm = 0;
+    DP_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    DP_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_hist_bulk<QUANT, GATHER>, 1024, kBulkSmem));
+    need(per_sm > 0, "the bulk-copy histogram kernel does not fit on this device");
+    grid_cap = sms * per_sm;
+    configured_device = dev;
+  }
+  need(status != nullptr && status_bit != 0, "internal error: the bulk-copy histogram kernel needs a status word");
+  need((reinterpret_cast<uintptr_t>(a.bins) & 15u) == 0 && (a.bstride & 15u) == 0,
+       "internal error: bulk copies need 16-byte aligned bin rows");
+  CUtensorMap m{};
+  u32 pitch = kWide;
+  if (GATHER) {
+    need(map != nullptr && map->bins == a.bins && map->stride == a.bstride,
+         "internal error: the gather kernel needs the bin matrix's tensor map");
+    static_assert(sizeof(m) == sizeof(map->desc), "tensor map size");
+    std::memcpy(&m, map->desc, sizeof m);
+    pitch = map->box;
+  }
+  const u32 grid = (a.ntasks_dev || a.ntasks >= u32(grid_cap)) ? u32(grid_cap) : a.ntasks;
+  need(scratch_elems >= u64(grid) * 2 * 256 * kWide, "internal error: histogram window scratch too small for the grid");
+  // warps that take their codes by copies; the rest load them directly
+  const char* cw = std::getenv("DP_HIST_COPY_WARPS");
+  const u32 copy_warps = cw && *cw ? u32(std::min(32l, std::max(0l, std::strtol(cw, nullptr, 10)))) : 32u;
+  DP_CUDA(cudaMemsetAsync(a.counter, 0, sizeof(u32), s));
+  k_hist_bulk<QUANT, GATHER><<<grid, 1024, kBulkSmem, s>>>(a, reinterpret_cast<long long*>(scratch), status, status_bit,
+                                                           pitch, copy_warps, m);
+}
+
 template <int MB, int THREADS, bool QUANT>
 void launch_hist_variant(const HistArgs& a, cudaStream_t s) {
   constexpr int kSmem = MB * kFT * (4 + 4) + kFT * (MB + 1) * (8 + 8);
@@ -538,14 +945,52 @@ u64 hist_wide_scratch_elems() {
 void launch_histograms_wide(const u8* bins, u64 bin_stride, u32 F, bool quantized_gh, const TreeArrays* trees,
                             const Scales* scales, const HistTask* tasks, u32 ntasks, u32* counter, i64* hist,
                             cudaStream_t s, const u32* ntasks_dev, const HistLayout* layout, i64* scratch,
-                            u64 scratch_elems) {
+                            u64 scratch_elems, int bulk, u32* status, u32 bulk_status_bit, const HistBinsMap* map) {
   if (!ntasks && !ntasks_dev) return;
   const HistLayout lay = layout ? *layout : HistLayout{F, u64(F) * 2 * kMaxBins, 0};
   need(lay.fg > 0, "histogram layout needs a positive feature group size");
   const HistArgs a{bins, bin_stride, F, ntasks, ntasks_dev, trees, scales, tasks, counter, hist, lay};
-  if (quantized_gh) launch_hist_wide_variant<true>(a, scratch, scratch_elems, s);
-  else launch_hist_wide_variant<false>(a, scratch, scratch_elems, s);
+  if (bulk == 2) {
+    if (quantized_gh) launch_hist_bulk_variant<true, true>(a, scratch, scratch_elems, status, bulk_status_bit, map, s);
+    else launch_hist_bulk_variant<false, true>(a, scratch, scratch_elems, status, bulk_status_bit, map, s);
+  } else if (bulk == 1) {
+    if (quantized_gh) launch_hist_bulk_variant<true, false>(a, scratch, scratch_elems, status, bulk_status_bit, map, s);
+    else launch_hist_bulk_variant<false, false>(a, scratch, scratch_elems, status, bulk_status_bit, map, s);
+  } else if (quantized_gh) {
+    launch_hist_wide_variant<true>(a, scratch, scratch_elems, s);
+  } else {
+    launch_hist_wide_variant<false>(a, scratch, scratch_elems, s);
+  }
   after_launch("histograms");
+}
+
+void encode_hist_bins_map(const u8* bins, u64 stride, u64 rows, HistBinsMap* out) {
+  need((reinterpret_cast<uintptr_t>(bins) & 15u) == 0 && stride % 16 == 0 && stride > 0,
+       "internal error: a tensor map needs 16-byte aligned bin rows");
+  need(rows > 0 && rows <= 0x7fffffffull, "internal error: tensor map rows out of range");
+  static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+  if (!encode) {
+    cudaDriverEntryPointQueryResult q{};
+    void* fn = nullptr;
+    DP_CUDA(cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault, &q));
+    need(q == cudaDriverEntryPointSuccess && fn, "cuTensorMapEncodeTiled is not available from the driver");
+    encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  }
+  const u32 box = u32(stride < u64(kWide) ? stride : u64(kWide));
+  const cuuint64_t dims[2] = {stride, rows};
+  const cuuint64_t strides[1] = {stride};
+  const cuuint32_t boxdim[2] = {box, 1};
+  const cuuint32_t estride[2] = {1, 1};
+  CUtensorMap m{};
+  const CUresult r = encode(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<u8*>(bins), dims, strides, boxdim,
+                            estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  need(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed for the bin matrix (" + std::to_string(int(r)) + ")");
+  static_assert(sizeof(m) == sizeof(out->desc), "tensor map size");
+  std::memcpy(out->desc, &m, sizeof m);
+  out->bins = bins;
+  out->stride = stride;
+  out->box = box;
 }
 
 u64 hist_chunk_rows(u64 total_rows) {
