@@ -482,6 +482,9 @@ void launch_hist_wide_variant(const HistArgs& a, i64* scratch, u64 scratch_elems
   DP_CUDA(cudaGetDevice(&dev));
   if (configured_device != dev) {
     DP_CUDA(cudaFuncSetAttribute(k_hist_wide<QUANT>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem));
+    // shared-memory carve-out in percent (testing knob: how L1 size matters)
+    if (const char* c = std::getenv("DP_HIST_CARVEOUT"))
+      DP_CUDA(cudaFuncSetAttribute(k_hist_wide<QUANT>, cudaFuncAttributePreferredSharedMemoryCarveout, std::atoi(c)));
     int sms = 0, per_sm = 0;
     DP_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     DP_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_hist_wide<QUANT>, 1024, kSmem));
@@ -514,11 +517,11 @@ void launch_hist_wide_variant(const HistArgs& a, i64* scratch, u64 scratch_elems
 // Every barrier wait is bounded (about a second of global timer): a wait that
 // runs out ORs the status bit, the warp stops issuing, and the blocks leave
 // at their next task fetch after a bounded wait for their copies in flight.
-constexpr int kBulkRows = 24;
 constexpr int kBulkStages = 2;
-constexpr int kBulkStageBytes = kBulkRows * kWide;
-// planes, 128 bytes of alignment room, stages (128-byte aligned), barriers
-constexpr int kBulkSmem = 256 * kWide * 8 + 128 + 32 * kBulkStages * kBulkStageBytes + 32 * kBulkStages * 8;
+// planes, 128 bytes of alignment room, stages of ROWS rows (128-byte
+// aligned), barriers
+template <int ROWS>
+constexpr int bulk_smem() { return 256 * kWide * 8 + 128 + 32 * kBulkStages * ROWS * kWide + 32 * kBulkStages * 8; }
 constexpr u64 kBulkWaitNs = 1000000000ull;
 
 __device__ __forceinline__ void mbar_init(u32 bar, u32 count) {
@@ -598,13 +601,16 @@ __device__ __forceinline__ void add_codes(u32* Lg, u32* Lh, uint4 v, u32 gq, u32
   }
 }
 
-template <bool QUANT, bool GATHER>
+template <bool QUANT, bool GATHER, int kBulkRows>
 __global__ void __launch_bounds__(1024) k_hist_bulk(HistArgs a, long long* __restrict__ wscr, u32* __restrict__ status,
                                                     u32 status_bit, u32 pitch, u32 copy_warps,
                                                     const __grid_constant__ CUtensorMap map) {
   constexpr int MB = 256, THREADS = 1024, kWarps = THREADS / 32;
   constexpr int kCells = MB * kWide;
   constexpr int kSteps = kBulkRows / 8;  // 8-row steps per chunk
+  constexpr int kBulkStageBytes = kBulkRows * kWide;
+  constexpr int kDirect = 6 / kSteps;    // chunks per iteration of the direct-load warps
+  static_assert(kBulkRows % 8 == 0 && 6 % kSteps == 0, "chunks of 8, 16 or 24 rows");
   extern __shared__ __align__(16) unsigned char smem[];
   __shared__ u32 s_task;
   __shared__ u32 s_abort;
@@ -757,22 +763,22 @@ __global__ void __launch_bounds__(1024) k_hist_bulk(HistArgs a, long long* __res
       // row indices of chunk k+3, so no global load latency stands between
       // two chunks.
       if (u32(warp) >= copy_warps) {
-        // the other warps count their chunks from direct loads, two chunks
-        // (six row steps) in flight at a time
+        // the other warps count their chunks from direct loads, six row
+        // steps in flight at a time
         const u8* base = a.bins + t.f0 + q16;
         const bool line_rows = (a.bstride & 127u) == 0;
-        for (u32 c = u32(warp); c < nchunks; c += 2u * kWarps) {
-          u32 row[2 * kSteps], at[2 * kSteps];
+        for (u32 c = u32(warp); c < nchunks; c += u32(kDirect) * kWarps) {
+          u32 row[kDirect * kSteps], at[kDirect * kSteps];
 #pragma unroll
-          for (int u = 0; u < 2 * kSteps; ++u) {
+          for (int u = 0; u < kDirect * kSteps; ++u) {
             const u32 cc = c + u32(u / kSteps) * kWarps, r = u32(u % kSteps) * 8u + s8;
             at[u] = pos + cc * kBulkRows + r;
             row[u] = (r < chunk_rows(cc) && qvalid) ? __ldg(ta.ridx + at[u]) : kNoRow;
           }
-          uint4 v[2 * kSteps];
-          u32 gq[2 * kSteps], hq[2 * kSteps];
+          uint4 v[kDirect * kSteps];
+          u32 gq[kDirect * kSteps], hq[kDirect * kSteps];
 #pragma unroll
-          for (int u = 0; u < 2 * kSteps; ++u) {
+          for (int u = 0; u < kDirect * kSteps; ++u) {
             v[u] = make_uint4(0u, 0u, 0u, 0u);
             gq[u] = hq[u] = 0u;
             if (row[u] != kNoRow) {
@@ -781,7 +787,7 @@ __global__ void __launch_bounds__(1024) k_hist_bulk(HistArgs a, long long* __res
             }
           }
 #pragma unroll
-          for (int u = 0; u < 2 * kSteps; ++u)
+          for (int u = 0; u < kDirect * kSteps; ++u)
             if (row[u] != kNoRow) add_codes(Lg, Lh, v[u], gq[u], hq[u], rot8, rot4, rsh, rot, q16);
         }
       }
@@ -856,18 +862,18 @@ __global__ void __launch_bounds__(1024) k_hist_bulk(HistArgs a, long long* __res
     if ((pending >> st) & 1u) mbar_wait_bounded(bar + 8u * st, (parity >> st) & 1u);
 }
 
-template <bool QUANT, bool GATHER>
-void launch_hist_bulk_variant(const HistArgs& a, i64* scratch, u64 scratch_elems, u32* status, u32 status_bit,
+template <bool QUANT, bool GATHER, int ROWS>
+void launch_hist_bulk_rows(const HistArgs& a, i64* scratch, u64 scratch_elems, u32* status, u32 status_bit,
                               const HistBinsMap* map, cudaStream_t s) {
   static thread_local int configured_device = -1;
   static thread_local int grid_cap = 0;
   int dev = 0;
   DP_CUDA(cudaGetDevice(&dev));
   if (configured_device != dev) {
-    DP_CUDA(cudaFuncSetAttribute(k_hist_bulk<QUANT, GATHER>, cudaFuncAttributeMaxDynamicSharedMemorySize, kBulkSmem));
+    DP_CUDA(cudaFuncSetAttribute(k_hist_bulk<QUANT, GATHER, ROWS>, cudaFuncAttributeMaxDynamicSharedMemorySize, bulk_smem<ROWS>()));
     int sms = 0, per_sm = 0;
     DP_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-    DP_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_hist_bulk<QUANT, GATHER>, 1024, kBulkSmem));
+    DP_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_hist_bulk<QUANT, GATHER, ROWS>, 1024, bulk_smem<ROWS>()));
     need(per_sm > 0, "the bulk-copy histogram kernel does not fit on this device");
     grid_cap = sms * per_sm;
     configured_device = dev;
@@ -890,8 +896,19 @@ void launch_hist_bulk_variant(const HistArgs& a, i64* scratch, u64 scratch_elems
   const char* cw = std::getenv("DP_HIST_COPY_WARPS");
   const u32 copy_warps = cw && *cw ? u32(std::min(32l, std::max(0l, std::strtol(cw, nullptr, 10)))) : 32u;
   DP_CUDA(cudaMemsetAsync(a.counter, 0, sizeof(u32), s));
-  k_hist_bulk<QUANT, GATHER><<<grid, 1024, kBulkSmem, s>>>(a, reinterpret_cast<long long*>(scratch), status, status_bit,
+  k_hist_bulk<QUANT, GATHER, ROWS><<<grid, 1024, bulk_smem<ROWS>(), s>>>(a, reinterpret_cast<long long*>(scratch), status, status_bit,
                                                            pitch, copy_warps, m);
+}
+
+// chunk rows per stage: DP_HIST_BULK_ROWS 8, 16 or 24 (default 24)
+template <bool QUANT, bool GATHER>
+void launch_hist_bulk_variant(const HistArgs& a, i64* scratch, u64 scratch_elems, u32* status, u32 status_bit,
+                              const HistBinsMap* map, cudaStream_t s) {
+  const char* r = std::getenv("DP_HIST_BULK_ROWS");
+  const long rows = r && *r ? std::strtol(r, nullptr, 10) : 24;
+  if (rows == 8) launch_hist_bulk_rows<QUANT, GATHER, 8>(a, scratch, scratch_elems, status, status_bit, map, s);
+  else if (rows == 16) launch_hist_bulk_rows<QUANT, GATHER, 16>(a, scratch, scratch_elems, status, status_bit, map, s);
+  else launch_hist_bulk_rows<QUANT, GATHER, 24>(a, scratch, scratch_elems, status, status_bit, map, s);
 }
 
 template <int MB, int THREADS, bool QUANT>
