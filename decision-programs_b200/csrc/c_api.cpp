@@ -384,6 +384,13 @@ int dp_comm_free(void* comm) {
   DP_API_END();
 }
 
+int dp_comm_set_timeout(void* comm, int64_t timeout_ms) {
+  DP_API_BEGIN();
+  need(comm != nullptr, "communicator is null");
+  static_cast<dp::Comm*>(comm)->set_timeout_ms(timeout_ms);
+  DP_API_END();
+}
+
 int dp_booster_set_comm(BoosterHandle handle, void* comm) {
   DP_API_BEGIN();
   dp::Booster* b = as_booster(handle);

@@ -28,6 +28,13 @@ class Comm {
   virtual void all_gather_bytes(const void* send, void* recv, size_t bytes, cudaStream_t s) = 0;
   // Host scalar helpers (synchronous).
   virtual std::uint64_t sum_host_u64(std::uint64_t v, cudaStream_t s) = 0;
+  // Waits until stream s has drained.  A communicator error, or no completion
+  // within the timeout, aborts the communicator (its kernels in flight end on
+  // every stream; later calls fail) and throws std::runtime_error.
+  virtual void wait(cudaStream_t s) = 0;
+  // Deadline of wait() in milliseconds; <= 0 waits without one.  The default
+  // is DP_COMM_TIMEOUT_MS from the environment, else 600000 (ten minutes).
+  virtual void set_timeout_ms(std::int64_t ms) = 0;
 };
 
 // NCCL communicator over NVLink (libnccl.so.2 loaded with dlopen so that a

@@ -216,7 +216,7 @@ Engine::Engine(DMatrix& d, const TrainParams& p, Comm* comm) : d_(d), p_(p), com
     comm_->all_gather_bytes(rows.get(), rows.get() + 1, sizeof(u64), stream_);
     std::vector<u64> all(G_);
     DP_CUDA(cudaMemcpyAsync(all.data(), rows.get() + 1, G_ * sizeof(u64), cudaMemcpyDeviceToHost, stream_));
-    DP_CUDA(cudaStreamSynchronize(stream_));
+    sync_stream();
     for (int r = 0; r < rank_; ++r) row0_ += all[r];
   }
   arena_.reserve(size_t(1) << 20);
@@ -237,7 +237,7 @@ Engine::Engine(DMatrix& d, const TrainParams& p, Comm* comm) : d_(d), p_(p), com
   DP_CUDA(cudaMemcpy(tarr_[1].get(), ta.data() + K_, K_ * sizeof(TreeArrays), cudaMemcpyHostToDevice));
   u32 bad = 0;
   DP_CUDA(cudaMemcpyAsync(&bad, scratch_.get(), sizeof(u32), cudaMemcpyDeviceToHost, stream_));
-  DP_CUDA(cudaStreamSynchronize(stream_));
+  sync_stream();
   if (bad) {
     if (p_.objective_id() == kLogistic) fail("label must be in [0,1] for logistic regression");
     if (p_.objective_id() == kSoftprob || p_.objective_id() == kSoftmax)
@@ -257,7 +257,7 @@ Engine::~Engine() {
 }
 
 void Engine::sync() {
-  DP_CUDA(cudaStreamSynchronize(stream_));
+  sync_stream();
   prof_.resolve();
   arena_off_ = kArenaHead;
 }
@@ -268,7 +268,7 @@ T* Engine::stage(const std::vector<T>& v) {
   size_t off = (std::max(arena_off_, kArenaHead) + 255) & ~size_t(255);
   if (off + bytes > arena_.size()) {
     // all staged copies must land before the arena is replaced
-    DP_CUDA(cudaStreamSynchronize(stream_));
+    sync_stream();
     size_t want = std::max(arena_.size() * 2, bytes + 4096);
     PinnedBuf<u8> fresh;
     fresh.reserve(want);
@@ -294,7 +294,7 @@ void Engine::grow(DevBuf<T>& b, size_t n) {
   need(!capturing_, "internal error: buffer growth while capturing a round");
   drop_graph();  // the graph holds the old address
   const auto t0 = std::chrono::steady_clock::now();
-  DP_CUDA(cudaStreamSynchronize(stream_));
+  sync_stream();
   b.resize(n);
   prof_.host("grow", ms_since(t0));
 }
@@ -307,7 +307,7 @@ void Engine::grow_keep(DevBuf<T>& b, size_t n) {
   const auto t0 = std::chrono::steady_clock::now();
   DevBuf<T> fresh(n);
   if (b.size()) DP_CUDA(cudaMemcpyAsync(fresh.get(), b.get(), b.size() * sizeof(T), cudaMemcpyDeviceToDevice, stream_));
-  DP_CUDA(cudaStreamSynchronize(stream_));
+  sync_stream();
   b = std::move(fresh);
   prof_.host("grow", ms_since(t0));
 }
@@ -416,7 +416,7 @@ const T* Engine::download(const T* src, size_t n) {
 std::vector<float> Engine::margins() const {
   DeviceGuard g(device_);
   std::vector<float> out(R_ * K_);
-  DP_CUDA(cudaStreamSynchronize(stream_));
+  sync_stream();
   DP_CUDA(cudaMemcpy(out.data(), margin_.get(), out.size() * sizeof(float), cudaMemcpyDeviceToHost));
   return out;
 }
@@ -565,7 +565,7 @@ Engine::RoundOut Engine::enqueue_round() {
     if (open_hi > async_open_limit_ || open_hi * slot_bytes > async_hist_bytes_) {
       RoundCounters* c_h = reinterpret_cast<RoundCounters*>(arena_.get());  // the arena's head
       DP_CUDA(cudaMemcpyAsync(c_h, ctr, sizeof(RoundCounters), cudaMemcpyDeviceToHost, stream_));
-      DP_CUDA(cudaStreamSynchronize(stream_));
+      sync_stream();
       open_hi = c_h->n_open;
       nbuild_hi = c_h->n_build;
       if (open_hi == 0) break;
@@ -636,7 +636,7 @@ Engine::RoundOut Engine::enqueue_round() {
       comm_->all_gather_bytes(cand_.get(), gathered_.get(), bytes, stream_);
       prof_.end(stream_);
     }
-    launch_decide(rb, q_->cut.get(), q_->has_missing.get(), depth, D, set, stream_);
+    launch_decide(rb, q_->cut.get(), q_->has_missing.get(), F, depth, D, set, stream_);
 
     // ---- partition and the children's segments
     prof_.begin(stream_, "partition", 0.0);
@@ -668,7 +668,7 @@ Engine::RoundOut Engine::enqueue_round() {
   leaves_hi += open_hi;
   grow(leaf_tasks_, (RK + kLeafChunkRows - 1) / kLeafChunkRows + leaves_hi);
   const RoundBuffers rb = round_buffers(depth, open_hi, open_hi);
-  launch_decide(rb, q_->cut.get(), q_->has_missing.get(), D, D, set, stream_);
+  launch_decide(rb, q_->cut.get(), q_->has_missing.get(), F, D, D, set, stream_);
   u32* const sets[2] = {ridx_[0].get(), ridx_[1].get()};
   launch_leaf_values(rb, scales_.get(), sp, sets, R, stream_);
   prof_.begin(stream_, "leaf_update", double(R) * K * 12.0);
@@ -693,7 +693,7 @@ void Engine::finish_round(Model& m, const RoundOut& out) {
   RoundCounters* const ctr = ctr_.get();
   const u64 ids_read = std::min<u64>(out.ids_hi, nodes_.size() / u64(K));
   auto t_wait = std::chrono::steady_clock::now();
-  DP_CUDA(cudaStreamSynchronize(stream_));
+  sync_stream();
   prof_.host("round_wait", ms_since(t_wait));
   t_wait = std::chrono::steady_clock::now();
   arena_off_ = kArenaHead;
@@ -704,10 +704,11 @@ void Engine::finish_round(Model& m, const RoundOut& out) {
   const Scales* sc_h = download(scales_.get(), K);
   const LevelStats* st_h = download(stats_.get(), size_t(D) + 1);
   const NodeRec* nd_h = download(nodes_.get(), ids_read * K);
-  DP_CUDA(cudaStreamSynchronize(stream_));
+  sync_stream();
   const u32 ovf = c_h->overflow;
   if (ovf & kOvfLostRows) fail("partition lost rows");
   if (ovf & kOvfHistWait) fail("histogram bulk copies did not complete within the wait limit");
+  if (ovf & kOvfBadCand) fail("a split candidate from the rank exchange names no feature of the matrix");
   if (ovf) fail("internal error: a per-round work list overflowed (flags " + std::to_string(ovf) + ")");
   for (int d = 0; d < D; ++d) {
     const LevelStats& st = st_h[d];

@@ -98,6 +98,13 @@ class Engine {
 
  private:
   void sync();
+  // Waits for the stream; with a communicator, through its watchdog (a peer
+  // that stops or fails aborts the communicator and throws instead of waiting
+  // for good).
+  void sync_stream() const {
+    if (comm_ && G_ > 1) comm_->wait(stream_);
+    else DP_CUDA(cudaStreamSynchronize(stream_));
+  }
   template <class T>
   T* stage(const std::vector<T>& v);  // copies into the pinned arena
   template <class T>

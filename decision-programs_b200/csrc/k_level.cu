@@ -158,8 +158,8 @@ __global__ void k_zero_slots(const RoundCounters* __restrict__ ctr, i64* hist, u
 // node ids ascending).  Child ids follow creation order within each tree: the
 // split of rank r in its tree gets left = next_id + 2r, right = left + 1.
 __global__ void __launch_bounds__(kBook) k_decide(RoundBuffers b, const float* __restrict__ cut,
-                                                  const u8* __restrict__ has_missing, int depth, int max_depth,
-                                                  int set) {
+                                                  const u8* __restrict__ has_missing, u32 F, int depth,
+                                                  int max_depth, int set) {
   __shared__ i64 s_begin[kBook], s_end[kBook];
   __shared__ u32 s_rank[kBook];
   const u32 n_open = b.ctr->n_open;
@@ -199,7 +199,13 @@ __global__ void __launch_bounds__(kBook) k_decide(RoundBuffers b, const float* _
         bs = b.cands[(u64(r) * b.cap_split + i) * b.nchunks + c];
       }
     }
-    const bool split = valid && depth < max_depth && bs.feature >= 0 && bs.gain > 0.0;
+    // a candidate that came through the exchange names a feature and bin
+    // inside the matrix; anything else (an exchange that was aborted part way)
+    // is reported instead of indexing the cut table with it
+    const bool in_range = bs.feature >= 0 && u32(bs.feature) < F && bs.bin >= 0 && bs.bin < i32(kMaxBins);
+    if (valid && depth < max_depth && bs.gain > 0.0 && bs.feature >= 0 && !in_range)
+      atomicOr(&b.ctr->overflow, kOvfBadCand);
+    const bool split = valid && depth < max_depth && in_range && bs.gain > 0.0;
     const bool leaf = valid && !split;
     u64 ns = 0, nl = 0;
     const u64 rs = split_base + scan_block(split ? 1 : 0, &ns);
@@ -424,9 +430,9 @@ void launch_zero_slots(const RoundBuffers& b, i64* hist, u64 slot_elems, u64 min
   after_launch("zero_slots");
 }
 
-void launch_decide(const RoundBuffers& b, const float* cut, const u8* has_missing, int depth, int max_depth,
+void launch_decide(const RoundBuffers& b, const float* cut, const u8* has_missing, u32 F, int depth, int max_depth,
                    int set, cudaStream_t s) {
-  k_decide<<<1, kBook, 0, s>>>(b, cut, has_missing, depth, max_depth, set);
+  k_decide<<<1, kBook, 0, s>>>(b, cut, has_missing, F, depth, max_depth, set);
   after_launch("decide");
 }
 

@@ -39,7 +39,7 @@ struct RoundCounters {
 // Overflow bits.
 enum : u32 {
   kOvfHistTasks = 1, kOvfNodes = 2, kOvfLeaves = 4, kOvfPartTasks = 8, kOvfLeafTasks = 16,
-  kOvfLostRows = 32, kOvfOpen = 64, kOvfHistWait = 128,
+  kOvfLostRows = 32, kOvfOpen = 64, kOvfHistWait = 128, kOvfBadCand = 256,
 };
 
 constexpr i64 kLeafChunkRows = 16384;  // rows per margin-update task
@@ -95,7 +95,7 @@ void launch_hist_tasks(const RoundBuffers& b, u32 ftiles, u32 tile, int depth, c
 // Zeroes max(device n_build, min_slots) histogram slots.
 void launch_zero_slots(const RoundBuffers& b, i64* hist, u64 slot_elems, u64 min_slots, cudaStream_t s);
 // Splits (depth < max_depth, gain > 0) or closes every open node.
-void launch_decide(const RoundBuffers& b, const float* cut, const u8* has_missing, int depth, int max_depth,
+void launch_decide(const RoundBuffers& b, const float* cut, const u8* has_missing, u32 F, int depth, int max_depth,
                    int set, cudaStream_t s);
 // With zero set (and depth + 1 < max_depth), also zeroes max(n_split,
 // min_slots) slots of slot_elems int64 at zero: the next level's output.

@@ -138,6 +138,13 @@ DP_API int dp_comm_unique_id(void* out128);
 DP_API int dp_comm_create(const void* unique_id128, int nranks, int rank, int device, void** out);
 DP_API int dp_comm_free(void* comm);
 DP_API int dp_booster_set_comm(BoosterHandle handle, void* comm);
+/* Failure detection: every host wait of a round that has collectives in
+ * flight polls the communicator for an asynchronous error and gives up after
+ * timeout_ms (<= 0: no deadline; default DP_COMM_TIMEOUT_MS, else 600000).
+ * Either aborts the communicator, which ends its kernels in flight, and the
+ * training call returns -1 with the reason in XGBGetLastError(); the
+ * communicator and the booster are unusable afterwards. */
+DP_API int dp_comm_set_timeout(void* comm, int64_t timeout_ms);
 
 /* Per-kernel CUDA-event timings of the training rounds ({"name":{"launches",
  * "ms","alg_bytes"}}), collected on the launching stream while enabled:

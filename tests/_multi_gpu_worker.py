@@ -1,11 +1,17 @@
 """Worker of tests/test_gpu_multi.py, launched by torch.distributed.run: one
 process per GPU trains its shard of the rows through libdp_gbdt with an NCCL
-communicator and writes its model and margins to OUT_DIR/rank{r}.*"""
+communicator and writes its model and margins to OUT_DIR/rank{r}.*
+
+Case "peer_stops": after the first round every rank but 0 leaves the job
+(between rounds, with nothing of its own in flight); rank 0 runs the second
+round with a 3-second communicator deadline and writes what happened to
+OUT_DIR/rank0_failure.json."""
 import datetime
 import json
 import os
 import pathlib
 import sys
+import time
 
 ROOT = pathlib.Path(__file__).resolve().parents[1]
 sys.path.insert(0, str(ROOT / "decision-programs_b200"))
@@ -37,6 +43,26 @@ def data(case: str):
     return x, y, {"objective": "reg:squarederror", "max_depth": 8}
 
 
+def peer_stops(params: dict, d, comm, rank: int, out_dir: pathlib.Path) -> None:
+    b = dp.Booster(params, [d])
+    b.set_comm(comm)
+    b.update(d, 0)
+    torch.cuda.synchronize()
+    comm.set_timeout(3000)  # the first round keeps the default, which covers start-up skew
+    dist.barrier()  # every rank has finished the first round
+    if rank != 0:
+        os._exit(0)  # leaves without a word to the others; none of its work is in flight
+    t0 = time.monotonic()
+    try:
+        b.update(d, 1)
+        error = ""
+    except dp.DPError as e:
+        error = str(e)
+    (out_dir / "rank0_failure.json").write_text(json.dumps({"error": error, "seconds": time.monotonic() - t0}))
+    sys.stdout.flush()
+    os._exit(0)  # the process group and the communicator cannot be closed with a peer gone
+
+
 def main() -> None:
     case, out_dir, rounds = sys.argv[1], pathlib.Path(sys.argv[2]), int(sys.argv[3])
     rank, world, local = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"]), int(os.environ["LOCAL_RANK"])
@@ -54,6 +80,8 @@ def main() -> None:
             d = dp.DMatrix.from_host(np.ascontiguousarray(x[lo:hi]), np.ascontiguousarray(y[lo:hi]))
         else:
             d = dp.DMatrix.from_torch(torch.from_numpy(x[lo:hi]).cuda(), torch.from_numpy(y[lo:hi]).cuda())
+        if case == "peer_stops":
+            peer_stops(params | {"device": f"cuda:{local}"}, d, comm, rank, out_dir)
         b = dp.train(params | {"device": f"cuda:{local}"}, d, rounds, comm=comm)
         K = params.get("num_class", 1)
         (out_dir / f"rank{rank}.json").write_bytes(b.save_raw())
