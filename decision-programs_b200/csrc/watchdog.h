@@ -19,11 +19,13 @@ namespace dp {
 // error() -> std::string: an asynchronous failure ("" while there is none).
 // abort(): called at most once, before a non-empty return.
 // timeout_ms <= 0 waits without a deadline.  The first spin_us of the wait
-// poll back to back (short waits return at once), later polls sleep poll_us.
+// poll back to back, as a spinning stream synchronisation would, so that a
+// healthy round (a few milliseconds) returns as soon as it ends; later polls
+// sleep poll_us.
 // Returns "" on completion, otherwise the reason the wait was given up.
 template <class Done, class Error, class Abort>
 std::string wait_or_abort(Done&& done, Error&& error, Abort&& abort, std::int64_t timeout_ms,
-                          std::int64_t spin_us = 2000, std::int64_t poll_us = 100) {
+                          std::int64_t spin_us = 50000, std::int64_t poll_us = 100) {
   using clock = std::chrono::steady_clock;
   const auto t0 = clock::now();
   for (;;) {
