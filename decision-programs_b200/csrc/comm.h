@@ -8,6 +8,7 @@
 
 #include <cstddef>
 #include <cstdint>
+#include <functional>
 #include <string>
 
 namespace dp {
@@ -31,7 +32,10 @@ class Comm {
   // Waits until stream s has drained.  A communicator error, or no completion
   // within the timeout, aborts the communicator (its kernels in flight end on
   // every stream; later calls fail) and throws std::runtime_error.
-  virtual void wait(cudaStream_t s) = 0;
+  // before_abort runs just before the abort: it must release every CUDA graph
+  // that holds this communicator's calls, because NCCL's abort waits until
+  // those graphs are gone (a graph still in flight is freed when it ends).
+  virtual void wait(cudaStream_t s, const std::function<void()>& before_abort) = 0;
   // Deadline of wait() in milliseconds; <= 0 waits without one.  The default
   // is DP_COMM_TIMEOUT_MS from the environment, else 600000 (ten minutes).
   virtual void set_timeout_ms(std::int64_t ms) = 0;

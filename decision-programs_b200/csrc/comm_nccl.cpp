@@ -80,7 +80,7 @@ class NcclComm final : public Comm {
     if (scratch_) cudaFree(scratch_);
     if (comm_) nccl().comm_destroy(comm_);
   }
-  void wait(cudaStream_t s) override {
+  void wait(cudaStream_t s, const std::function<void()>& before_abort) override {
     live();
     const std::string why = wait_or_abort(
         [&] {
@@ -96,6 +96,7 @@ class NcclComm final : public Comm {
           return (r == ncclSuccess || r == ncclInProgress) ? std::string() : std::string(nccl().error_string(r));
         },
         [&] {
+          if (before_abort) before_abort();
           // ends this communicator's kernels in flight; the comm is unusable after
           nccl().comm_abort(comm_);
           comm_ = nullptr;
@@ -133,7 +134,7 @@ class NcclComm final : public Comm {
     check(nccl().all_reduce(scratch_, scratch_, 1, ncclUint64, ncclSum, comm_, s), "ncclAllReduce(u64 sum)");
     u64 out = 0;
     DP_CUDA(cudaMemcpyAsync(&out, scratch_, sizeof out, cudaMemcpyDeviceToHost, s));
-    wait(s);
+    wait(s, {});  // no graph holds this call
     return out;
   }
 

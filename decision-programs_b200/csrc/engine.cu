@@ -416,7 +416,8 @@ const T* Engine::download(const T* src, size_t n) {
 std::vector<float> Engine::margins() const {
   DeviceGuard g(device_);
   std::vector<float> out(R_ * K_);
-  sync_stream();
+  // margins are read after a round has ended: no collective is in flight
+  DP_CUDA(cudaStreamSynchronize(stream_));
   DP_CUDA(cudaMemcpy(out.data(), margin_.get(), out.size() * sizeof(float), cudaMemcpyDeviceToHost));
   return out;
 }

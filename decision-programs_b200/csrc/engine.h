@@ -100,10 +100,18 @@ class Engine {
   void sync();
   // Waits for the stream; with a communicator, through its watchdog (a peer
   // that stops or fails aborts the communicator and throws instead of waiting
-  // for good).
-  void sync_stream() const {
-    if (comm_ && G_ > 1) comm_->wait(stream_);
-    else DP_CUDA(cudaStreamSynchronize(stream_));
+  // for good).  Before an abort the round's CUDA graph, which holds the
+  // communicator's calls, is released (NCCL's abort waits for that), and
+  // rounds are no longer captured.
+  void sync_stream() {
+    if (comm_ && G_ > 1) {
+      comm_->wait(stream_, [this] {
+        drop_graph();
+        graphs_ = false;
+      });
+    } else {
+      DP_CUDA(cudaStreamSynchronize(stream_));
+    }
   }
   template <class T>
   T* stage(const std::vector<T>& v);  // copies into the pinned arena

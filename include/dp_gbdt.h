@@ -136,6 +136,9 @@ DP_API int XGBoosterPredictFromCudaArray(BoosterHandle handle, const char* value
  * round.  Rows are sharded across ranks; trees are identical on every rank. */
 DP_API int dp_comm_unique_id(void* out128);
 DP_API int dp_comm_create(const void* unique_id128, int nranks, int rank, int device, void** out);
+/* Free every booster attached to a communicator before the communicator:
+ * a booster's rounds are CUDA graphs that hold the communicator's calls, and
+ * NCCL's destroy waits until those graphs are released. */
 DP_API int dp_comm_free(void* comm);
 DP_API int dp_booster_set_comm(BoosterHandle handle, void* comm);
 /* Failure detection: every host wait of a round that has collectives in
