@@ -330,7 +330,11 @@ __global__ void __launch_bounds__(THREADS) k_hist(HistArgs a) {
 // lanes of q = 0, 2 (and of q = 1, 3) hit 16 distinct banks.
 constexpr int kWide = 64;
 
-template <bool QUANT>
+// TDRAIN: the drain goes through the scratch and is transposed in shared
+// memory, 32 features at a time, so that consecutive threads write
+// consecutive bins of one feature (512 contiguous bytes per warp) instead of
+// 64 features 4 KB apart.
+template <bool QUANT, bool TDRAIN = false>
 __global__ void __launch_bounds__(1024) k_hist_wide(HistArgs a, long long* __restrict__ wscr) {
   constexpr int MB = 256, THREADS = 1024;
   constexpr int kCells = MB * kWide;
@@ -383,25 +387,68 @@ __global__ void __launch_bounds__(1024) k_hist_wide(HistArgs a, long long* __res
       // scratch + last window straight to the output; each thread keeps the
       // cells it folded, so no barrier is needed between the two
       i64* out = a.hist + u64(key_slot) * a.layout.slot_stride;
-      for (int i = threadIdx.x; i < kCells; i += THREADS) {
-        const int b = i / kWide, f = i % kWide;
-        long long gs = static_cast<long long>(static_cast<int>(Lg[i]));
-        long long hs = static_cast<long long>(Lh[i]);
-        if (!s_clean) {
-          gs += Sg[i];
-          hs += Sh[i];
+      if constexpr (TDRAIN) {
+        auto put = [&](u32 f, u32 b, long long gs, long long hs) {
+          const u32 gf = key_f0 + f;
+          if (gf >= a.F) return;
+          const u32 grp = gf / a.layout.fg, fl = gf - grp * a.layout.fg;
+          i64* cell = out + grp * a.layout.group_stride + (u64(fl) * kMaxBins + b) * 2;
+          if (key_excl) {
+            *reinterpret_cast<longlong2*>(cell) = make_longlong2(gs, hs);
+          } else if (gs | hs) {
+            atomicAdd(reinterpret_cast<unsigned long long*>(cell), static_cast<unsigned long long>(gs));
+            atomicAdd(reinterpret_cast<unsigned long long*>(cell) + 1, static_cast<unsigned long long>(hs));
+          }
+        };
+        // the key's full sums into the scratch (each thread its own cells)
+        for (int i = threadIdx.x; i < kCells; i += THREADS) {
+          const long long g = static_cast<long long>(static_cast<int>(Lg[i]));
+          const long long h = static_cast<long long>(Lh[i]);
+          Sg[i] = s_clean ? g : Sg[i] + g;
+          Sh[i] = s_clean ? h : Sh[i] + h;
         }
-        Lg[i] = 0u;
-        Lh[i] = 0u;
-        const u32 gf = key_f0 + u32(f);
-        if (gf >= a.F) continue;
-        const u32 grp = gf / a.layout.fg, fl = gf - grp * a.layout.fg;
-        i64* cell = out + grp * a.layout.group_stride + (u64(fl) * kMaxBins + b) * 2;
-        if (key_excl) {
-          *reinterpret_cast<longlong2*>(cell) = make_longlong2(gs, hs);
-        } else if (gs | hs) {
-          atomicAdd(reinterpret_cast<unsigned long long*>(cell), static_cast<unsigned long long>(gs));
-          atomicAdd(reinterpret_cast<unsigned long long*>(cell) + 1, static_cast<unsigned long long>(hs));
+        __syncthreads();  // the planes are read; they become the staging area
+        // pairs T[f][b ^ f] for 32 features (128 KB): the XOR keeps both the
+        // staging writes and the bin-order reads at four wavefronts per warp
+        longlong2* T = reinterpret_cast<longlong2*>(smem);
+        for (u32 half = 0; half < 2; ++half) {
+          for (int i = threadIdx.x; i < kCells / 2; i += THREADS) {
+            const u32 b = u32(i) / 32u, fl = u32(i) % 32u, src = b * kWide + half * 32u + fl;
+            T[fl * MB + (b ^ fl)] = make_longlong2(Sg[src], Sh[src]);
+          }
+          __syncthreads();
+          for (int idx = threadIdx.x; idx < kCells / 2; idx += THREADS) {
+            const u32 fl = u32(idx) / MB, b = u32(idx) % MB;
+            const longlong2 v = T[fl * MB + (b ^ fl)];
+            put(half * 32u + fl, b, v.x, v.y);
+          }
+          __syncthreads();
+        }
+        for (int i = threadIdx.x; i < kCells; i += THREADS) {
+          Lg[i] = 0u;
+          Lh[i] = 0u;
+        }
+      } else {
+        for (int i = threadIdx.x; i < kCells; i += THREADS) {
+          const int b = i / kWide, f = i % kWide;
+          long long gs = static_cast<long long>(static_cast<int>(Lg[i]));
+          long long hs = static_cast<long long>(Lh[i]);
+          if (!s_clean) {
+            gs += Sg[i];
+            hs += Sh[i];
+          }
+          Lg[i] = 0u;
+          Lh[i] = 0u;
+          const u32 gf = key_f0 + u32(f);
+          if (gf >= a.F) continue;
+          const u32 grp = gf / a.layout.fg, fl = gf - grp * a.layout.fg;
+          i64* cell = out + grp * a.layout.group_stride + (u64(fl) * kMaxBins + b) * 2;
+          if (key_excl) {
+            *reinterpret_cast<longlong2*>(cell) = make_longlong2(gs, hs);
+          } else if (gs | hs) {
+            atomicAdd(reinterpret_cast<unsigned long long*>(cell), static_cast<unsigned long long>(gs));
+            atomicAdd(reinterpret_cast<unsigned long long*>(cell) + 1, static_cast<unsigned long long>(hs));
+          }
         }
       }
       s_clean = true;
@@ -473,28 +520,36 @@ __global__ void __launch_bounds__(1024) k_hist_wide(HistArgs a, long long* __res
   }
 }
 
-template <bool QUANT>
-void launch_hist_wide_variant(const HistArgs& a, i64* scratch, u64 scratch_elems, cudaStream_t s) {
+template <bool QUANT, bool TDRAIN>
+void launch_hist_wide_drain(const HistArgs& a, i64* scratch, u64 scratch_elems, cudaStream_t s) {
   constexpr int kSmem = 256 * kWide * 8;
   static thread_local int configured_device = -1;
   static thread_local int grid_cap = 0;
   int dev = 0;
   DP_CUDA(cudaGetDevice(&dev));
   if (configured_device != dev) {
-    DP_CUDA(cudaFuncSetAttribute(k_hist_wide<QUANT>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem));
+    DP_CUDA(cudaFuncSetAttribute(k_hist_wide<QUANT, TDRAIN>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem));
     // shared-memory carve-out in percent (testing knob: how L1 size matters)
     if (const char* c = std::getenv("DP_HIST_CARVEOUT"))
-      DP_CUDA(cudaFuncSetAttribute(k_hist_wide<QUANT>, cudaFuncAttributePreferredSharedMemoryCarveout, std::atoi(c)));
+      DP_CUDA(cudaFuncSetAttribute(k_hist_wide<QUANT, TDRAIN>, cudaFuncAttributePreferredSharedMemoryCarveout, std::atoi(c)));
     int sms = 0, per_sm = 0;
     DP_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-    DP_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_hist_wide<QUANT>, 1024, kSmem));
+    DP_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_hist_wide<QUANT, TDRAIN>, 1024, kSmem));
     grid_cap = sms * (per_sm > 0 ? per_sm : 1);
     configured_device = dev;
   }
   const u32 grid = (a.ntasks_dev || a.ntasks >= u32(grid_cap)) ? u32(grid_cap) : a.ntasks;
   need(scratch_elems >= u64(grid) * 2 * 256 * kWide, "internal error: histogram window scratch too small for the grid");
   DP_CUDA(cudaMemsetAsync(a.counter, 0, sizeof(u32), s));
-  k_hist_wide<QUANT><<<grid, 1024, kSmem, s>>>(a, reinterpret_cast<long long*>(scratch));
+  k_hist_wide<QUANT, TDRAIN><<<grid, 1024, kSmem, s>>>(a, reinterpret_cast<long long*>(scratch));
+}
+
+// DP_HIST_TDRAIN=1: the transposed drain
+template <bool QUANT>
+void launch_hist_wide_variant(const HistArgs& a, i64* scratch, u64 scratch_elems, cudaStream_t s) {
+  const char* t = std::getenv("DP_HIST_TDRAIN");
+  if (t && t[0] == '1' && t[1] == 0) launch_hist_wide_drain<QUANT, true>(a, scratch, scratch_elems, s);
+  else launch_hist_wide_drain<QUANT, false>(a, scratch, scratch_elems, s);
 }
 
 // ---------------------------------------------------------------------------
@@ -954,8 +1009,8 @@ u64 hist_wide_scratch_elems() {
   int dev = 0, sms = 148, per_sm = 1;
   DP_CUDA(cudaGetDevice(&dev));
   DP_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-  DP_CUDA(cudaFuncSetAttribute(k_hist_wide<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 256 * kWide * 8));
-  DP_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_hist_wide<true>, 1024, 256 * kWide * 8));
+  DP_CUDA(cudaFuncSetAttribute(k_hist_wide<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 256 * kWide * 8));
+  DP_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_hist_wide<true, false>, 1024, 256 * kWide * 8));
   return u64(sms) * u64(per_sm > 0 ? per_sm : 1) * 2 * 256 * kWide;
 }
 
