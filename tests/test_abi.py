@@ -78,6 +78,8 @@ def test_null_handles_are_refused(dp):
     assert dp.lib().XGBoosterBoostedRounds(None, C.byref(n)) == -1
     assert b"null" in dp.lib().XGBGetLastError()
     assert dp.lib().XGBoosterUpdateOneIter(None, 0, None) == -1
+    assert dp.lib().dp_comm_set_timeout(None, 1000) == -1
+    assert b"null" in dp.lib().XGBGetLastError()
 
 
 def _model(objective="multi:softprob", K=2):
