@@ -43,6 +43,39 @@ def test_hand_computed_stump(orc):
     np.testing.assert_array_equal(m.margins()[:, 0], [1, 1, 3, 3])
 
 
+@pytest.mark.parametrize("y,params,split,gain,leaves", [
+    # alpha 1: T(G) = sign(G) max(|G| - 1, 0).  Parent G = -8, H = 4: s = 49/4.
+    # x < 3: s_L = 1/2, s_R = 25/2 -> gain 0.375 (x < 2: -0.125, x < 4: -1.458);
+    # leaves -T(G)/H = 0.5 and 2.5
+    ([1, 1, 3, 3], {"alpha": 1.0}, 3.0, 0.375, (0.5, 2.5)),
+    # gamma 1.5 comes off the best gain 2 (x < 3): 0.5 > 0, so the split stays
+    ([1, 1, 3, 3], {"gamma": 1.5}, 3.0, 0.5, (1.0, 3.0)),
+    # gamma 2.5 leaves no positive gain: the root is a leaf, -G/H = 8/4
+    ([1, 1, 3, 3], {"gamma": 2.5}, None, None, (2.0,)),
+    # min_child_weight 2.5: every candidate has a side with H < 2.5
+    ([1, 1, 3, 3], {"min_child_weight": 2.5}, None, None, (2.0,)),
+    # y = 0, 4, 4, 4: the best split x < 2 (gain 6) has H_L = 1; with
+    # min_child_weight 1.5 only x < 3 is valid (gain 0.5 (8 + 32 - 36) = 2)
+    ([0, 4, 4, 4], {"min_child_weight": 1.5}, 3.0, 2.0, (2.0, 4.0)),
+])
+def test_regularisation_by_hand(orc, y, params, split, gain, leaves):
+    # x = 1..4, squared error from margin 0 (g = -y, h = 1), lambda 0, eta 1;
+    # the quantiser scales are powers of two, so every sum here is exact
+    x = np.array([[1.0], [2.0], [3.0], [4.0]], np.float32)
+    kw = {"reg_lambda": 0.0, "min_child_weight": 0.0} | params
+    m = orc.Model(x, np.array(y, np.float32), "reg:squarederror", max_depth=1, eta=1.0, rounds=1, **kw)
+    t = m.tree(0)
+    if split is None:
+        assert t["left_children"].tolist() == [-1]
+        assert t["split_conditions"].tolist() == list(leaves)
+        np.testing.assert_array_equal(m.margins()[:, 0], [leaves[0]] * 4)
+    else:
+        assert t["left_children"].tolist() == [1, -1, -1] and t["right_children"].tolist() == [2, -1, -1]
+        assert t["split_conditions"].tolist() == [split, *leaves]
+        assert t["loss_changes"][0] == np.float32(gain)
+        np.testing.assert_array_equal(m.margins()[:, 0], [leaves[0], leaves[0], leaves[1], leaves[1]])
+
+
 def test_quantile_boundaries_by_hand(orc):
     # 10 distinct values, max_bin 4: ranks floor(k*10/4) = 2, 5, 7 -> values 20, 50, 70
     x = (np.arange(10, dtype=np.float32) * 10)[::-1].reshape(-1, 1).copy()
