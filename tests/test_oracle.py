@@ -76,6 +76,20 @@ def test_regularisation_by_hand(orc, y, params, split, gain, leaves):
         np.testing.assert_array_equal(m.margins()[:, 0], [leaves[0], leaves[0], leaves[1], leaves[1]])
 
 
+def test_logistic_stump_by_hand(orc):
+    # margin 0: p = 1/2, g = 1/2 - y, h = 1/4.  y = 0, 0, 1, 1, lambda 0: parent
+    # G = 0 (s = 0); x < 3 has G = +-1, H = 1/2 on each side: gain 0.5 (2 + 2) = 2
+    # (x < 2 and x < 4: 2/3); leaves -G/H = -2 and 2
+    x = np.array([[1.0], [2.0], [3.0], [4.0]], np.float32)
+    m = orc.Model(x, np.array([0, 0, 1, 1], np.float32), "binary:logistic", max_depth=1, eta=1.0, reg_lambda=0.0,
+                  min_child_weight=0.0, rounds=1)
+    t = m.tree(0)
+    assert t["split_conditions"].tolist() == [3.0, -2.0, 2.0]
+    assert t["loss_changes"][0] == np.float32(2.0)
+    assert t["sum_hessian"].tolist() == [1.0, 0.5, 0.5]
+    np.testing.assert_array_equal(m.margins()[:, 0], [-2, -2, 2, 2])
+
+
 def test_quantile_boundaries_by_hand(orc):
     # 10 distinct values, max_bin 4: ranks floor(k*10/4) = 2, 5, 7 -> values 20, 50, 70
     x = (np.arange(10, dtype=np.float32) * 10)[::-1].reshape(-1, 1).copy()
