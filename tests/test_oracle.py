@@ -90,6 +90,21 @@ def test_logistic_stump_by_hand(orc):
     np.testing.assert_array_equal(m.margins()[:, 0], [-2, -2, 2, 2])
 
 
+def test_softprob_stumps_by_hand(orc):
+    # two classes from margin 0: p_k = 1/2, g_k = 1/2 - [y = k], h_k = 2 p (1 - p)
+    # = 1/2.  y = 0, 0, 1, 1, lambda 0: in each class's tree x < 3 has G = +-1,
+    # H = 1 on each side and parent G = 0: gain 0.5 (1 + 1) = 1; leaves -G/H
+    x = np.array([[1.0], [2.0], [3.0], [4.0]], np.float32)
+    m = orc.Model(x, np.array([0, 0, 1, 1], np.float32), "multi:softprob", num_class=2, max_depth=1, eta=1.0,
+                  reg_lambda=0.0, min_child_weight=0.0, rounds=1)
+    assert m.num_trees() == 2
+    assert m.tree(0)["split_conditions"].tolist() == [3.0, 1.0, -1.0]
+    assert m.tree(1)["split_conditions"].tolist() == [3.0, -1.0, 1.0]
+    for k in range(2):
+        assert m.tree(k)["loss_changes"][0] == np.float32(1.0)
+    np.testing.assert_array_equal(m.margins(), [[1, -1], [1, -1], [-1, 1], [-1, 1]])
+
+
 def test_quantile_boundaries_by_hand(orc):
     # 10 distinct values, max_bin 4: ranks floor(k*10/4) = 2, 5, 7 -> values 20, 50, 70
     x = (np.arange(10, dtype=np.float32) * 10)[::-1].reshape(-1, 1).copy()
