@@ -105,6 +105,28 @@ def test_softprob_stumps_by_hand(orc):
     np.testing.assert_array_equal(m.margins(), [[1, -1], [1, -1], [-1, 1], [-1, 1]])
 
 
+@pytest.mark.parametrize("y,gain,default_left,leaves,margins", [
+    # x = 1, 2, 3, NaN (bins 0, 1, 2 and the missing code), lambda 0.
+    # y = 1, 1, 3, 3: parent G = -8, H = 4 (s = 16).  x < 3 with the missing row
+    # right: s_L = 4/2, s_R = 36/2 -> gain 2; left: 25/3 + 9 -> 0.667; x < 2:
+    # 0.667 (right) and 0 (left).  Missing goes right; leaves 1 and 3
+    ([1, 1, 3, 3], 2.0, 0, (1.0, 3.0), [1, 1, 3, 3]),
+    # y = 1, 1, 3, 1: parent G = -6 (s = 9).  x < 3 with the missing row left:
+    # s_L = 9/3, s_R = 9/1 -> gain 1.5; right: 0.5; x < 2: 0.5 (left), 0.167
+    # (right).  Missing goes left; leaves 1 and 3, and the NaN row gets 1
+    ([1, 1, 3, 1], 1.5, 1, (1.0, 3.0), [1, 1, 3, 1]),
+])
+def test_missing_value_direction_by_hand(orc, y, gain, default_left, leaves, margins):
+    x = np.array([[1.0], [2.0], [3.0], [np.nan]], np.float32)
+    m = orc.Model(x, np.array(y, np.float32), "reg:squarederror", max_depth=1, eta=1.0, reg_lambda=0.0,
+                  min_child_weight=0.0, rounds=1)
+    t = m.tree(0)
+    assert t["split_conditions"].tolist() == [3.0, *leaves]
+    assert t["default_left"][0] == default_left
+    assert t["loss_changes"][0] == np.float32(gain)
+    np.testing.assert_array_equal(m.margins()[:, 0], margins)
+
+
 def test_quantile_boundaries_by_hand(orc):
     # 10 distinct values, max_bin 4: ranks floor(k*10/4) = 2, 5, 7 -> values 20, 50, 70
     x = (np.arange(10, dtype=np.float32) * 10)[::-1].reshape(-1, 1).copy()
