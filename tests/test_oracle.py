@@ -127,6 +127,36 @@ def test_missing_value_direction_by_hand(orc, y, gain, default_left, leaves, mar
     np.testing.assert_array_equal(m.margins()[:, 0], margins)
 
 
+def test_depth_two_tree_by_hand(orc):
+    # y = 1..4, lambda 0: root x < 3 (gain 0.5 (4.5 + 24.5 - 25) = 2; x < 2 and
+    # x < 4 give 1.5); then x < 2 under node 1 and x < 4 under node 2, each
+    # 0.25 (the other bins leave a side with H = 0, which is not valid).  Nodes
+    # are numbered in creation order: 1, 2 the root's children, 3..6 theirs
+    x = np.array([[1.0], [2.0], [3.0], [4.0]], np.float32)
+    m = orc.Model(x, np.array([1, 2, 3, 4], np.float32), "reg:squarederror", max_depth=2, eta=1.0, reg_lambda=0.0,
+                  min_child_weight=0.0, rounds=1)
+    t = m.tree(0)
+    assert t["left_children"].tolist() == [1, 3, 5, -1, -1, -1, -1]
+    assert t["right_children"].tolist() == [2, 4, 6, -1, -1, -1, -1]
+    assert t["split_conditions"].tolist() == [3.0, 2.0, 4.0, 1.0, 2.0, 3.0, 4.0]
+    assert t["loss_changes"][:3].tolist() == [2.0, 0.25, 0.25]
+    np.testing.assert_array_equal(m.margins()[:, 0], [1, 2, 3, 4])
+
+
+def test_second_round_by_hand(orc):
+    # eta 0.5, lambda 0, y = 1, 1, 3, 3.  Round 1: x < 3, leaves 0.5 and 1.5.
+    # Round 2 from those margins: g = -0.5, -0.5, -1.5, -1.5, parent G = -4
+    # (s = 4); x < 3: 0.5 (1/2 + 9/2 - 4) = 0.5, the others 1/6; leaves
+    # 0.5 * (1/2) = 0.25 and 0.5 * (3/2) = 0.75
+    x = np.array([[1.0], [2.0], [3.0], [4.0]], np.float32)
+    m = orc.Model(x, np.array([1, 1, 3, 3], np.float32), "reg:squarederror", max_depth=1, eta=0.5, reg_lambda=0.0,
+                  min_child_weight=0.0, rounds=2)
+    assert m.tree(0)["split_conditions"].tolist() == [3.0, 0.5, 1.5]
+    assert m.tree(1)["split_conditions"].tolist() == [3.0, 0.25, 0.75]
+    assert m.tree(1)["loss_changes"][0] == np.float32(0.5)
+    np.testing.assert_array_equal(m.margins()[:, 0], [0.75, 0.75, 2.25, 2.25])
+
+
 def test_quantile_boundaries_by_hand(orc):
     # 10 distinct values, max_bin 4: ranks floor(k*10/4) = 2, 5, 7 -> values 20, 50, 70
     x = (np.arange(10, dtype=np.float32) * 10)[::-1].reshape(-1, 1).copy()
