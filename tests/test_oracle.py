@@ -167,6 +167,24 @@ def test_quantile_boundaries_by_hand(orc):
     assert bins[::-1].tolist() == [0, 0, 1, 1, 1, 2, 2, 3, 3, 3]
 
 
+@pytest.mark.parametrize("values,max_bin,bounds,bins", [
+    # 4 distinct values, max_bin 4: every distinct value but the minimum
+    ([1, 1, 1, 1, 2, 2, 3, 4], 4, [2, 3, 4], [0, 0, 0, 0, 1, 1, 2, 3]),
+    # 7 distinct > 3: ranks floor(k 10 / 3) = 3, 6 -> values 3, 4
+    ([1, 2, 3, 3, 3, 3, 4, 5, 6, 7], 3, [3, 4], [0, 0, 1, 1, 1, 1, 2, 2, 2, 2]),
+    # ranks 3 and 6 both hold 5: one boundary after deduplication
+    ([1, 5, 5, 5, 5, 5, 5, 5, 7, 9], 3, [5], [0, 1, 1, 1, 1, 1, 1, 1, 1, 1]),
+    # ranks 3 and 6 hold the minimum, which is never a boundary: one bin
+    ([1, 1, 1, 1, 1, 1, 1, 2, 3, 4], 3, [], [0] * 10),
+])
+def test_cut_ranks_and_duplicates_by_hand(orc, values, max_bin, bounds, bins):
+    x = np.array(values, np.float32)[::-1].reshape(-1, 1).copy()  # order of the rows is irrelevant
+    cut, nb, hm = orc.cuts(x, max_bin)
+    assert hm[0] == 0 and nb[0] == len(bounds) + 1
+    assert cut[0, :len(bounds)].tolist() == [float(v) for v in bounds]
+    assert orc.bin_matrix(x, cut, nb, hm)[::-1, 0].tolist() == bins
+
+
 def test_missing_values_take_the_reserved_code(orc):
     x = np.array([[np.nan], [1.0], [2.0], [-0.0], [0.0]], np.float32)
     cut, nb, hm = orc.cuts(x, 256)
