@@ -156,48 +156,86 @@ class ClockSampler:
 
 
 # --------------------------------------------------------------------------- reference / CPU arm
-def cpu_oracle_run(rows: int, trees: int, threads: int) -> dict:
-    """Oracle (CPU restatement) on the first `rows` rows of the workload."""
-    import torch
+def config4_host(torch, rows: int = ROWS):
+    """The config-4 matrix and targets in host memory.  Generated with the
+    same per-chunk seeds as the GPU arm; on a machine with a GPU the chunks
+    are drawn on it (torch's CUDA generator), so both arms train on the same
+    values, and copied back.  Returns (x, y, where)."""
+    if torch.cuda.is_available():
+        x, y = shard(torch, 0, 1, torch.device("cuda", 0), rows)
+        xh, yh = x.cpu().numpy(), y.cpu().numpy()
+        del x, y
+        torch.cuda.empty_cache()
+        return xh, yh, "drawn on the GPU, as the GPU arm's"
+    x, y = shard(torch, 0, 1, "cpu", rows)
+    return x.numpy(), y.numpy(), "drawn on the CPU (no GPU: same distribution, other draws)"
+
+
+def oracle_model(x, y, threads: int):
+    """The CPU oracle on the config-4 data, cuts and bins built, no tree yet."""
     sys.path.insert(0, str(ROOT / "oracle"))
     import oracle
-    nchunks = (rows + CHUNK - 1) // CHUNK
-    xs, ys = zip(*(make_chunk(torch, c, "cpu") for c in range(nchunks)))
-    x = torch.cat(xs)[:rows].numpy()
-    y = torch.cat(ys)[:rows].numpy()
-    m = oracle.Model(x, y, "reg:squarederror", max_depth=DEPTH, max_bin=256, eta=0.3, rounds=0, threads=threads)
-    t0 = time.perf_counter()
-    m.train_more(trees)
-    dt = time.perf_counter() - t0
-    return {"value": rows * trees / dt, "seconds": dt, "rows": rows, "trees": trees}
+    return oracle.Model(x, y, "reg:squarederror", max_depth=DEPTH, max_bin=256, eta=0.3, reg_lambda=1.0,
+                        min_child_weight=1.0, rounds=0, threads=threads)
 
 
 def reference_arm(args) -> None:
+    """The CPU implementation of the path on the GPU arm's workload: the
+    oracle trains depth-10 trees over all 10M x 128 rows of config 4, one tree
+    per step, with every host thread; cuts and bins are built before the
+    timed steps, as the GPU arm's are."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
+    import torch
     threads = len(os.sched_getaffinity(0))
-    rows = 1_000_000
-    steps = []
+    x, y, where = config4_host(torch, ROWS)
+    m = oracle_model(x, y, threads)
     for _ in range(args.warmup):
-        cpu_oracle_run(rows, 1, threads)
+        m.train_more(1)
+    t0 = time.perf_counter()
     for _ in range(args.steps):
-        steps.append(cpu_oracle_run(rows, 1, threads)["value"])
-    value = statistics.median(steps)
+        m.train_more(1)
+    dt = time.perf_counter() - t0
+    value = ROWS * args.steps / dt
     line = {
         "impl": "reference", "metric": "boosting rows*trees/s (config 4 step, 1 tree)", "value": value,
         "unit": "rows*trees/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": 1e3 * rows / value,
+        "ms_per_step": 1e3 * dt / args.steps,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "u8 bins / int64 sums",
         "data": "synthetic (seeded)",
         "config": {"workload": WORKLOAD, "rows": ROWS, "features": FEATURES, "max_depth": DEPTH, "max_bin": 256,
-                   "parallelism": f"CPU oracle on {threads} host threads; each step a {rows}-row sample"},
+                   "parallelism": f"CPU oracle on {threads} host threads; every step one tree over all {ROWS} rows"},
         "cpu_baseline": {"value": value, "unit": "rows*trees/s", "cores": threads, "kind": "port",
-                         "sample": f"first {rows} rows of the config-4 data, one depth-10 tree per step "
-                                   f"(C++ oracle, {threads} threads)"},
+                         "sample": f"the whole config-4 workload ({ROWS} rows x {FEATURES} features, data {where}), "
+                                   f"one depth-10 tree per step, {args.steps} timed steps after {args.warmup} "
+                                   f"warm-up trees (C++ oracle, {threads} threads)"},
         "e2e": {"value": value, "unit": "rows*trees/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+# trees of the benchmarked run that are compared with the CPU oracle's
+C4_PARITY_TREES = 3
+
+
+def config4_cpu_leg(torch, first_trees: list[dict]) -> dict:
+    """CPU baseline and full-size parity of the benchmarked workload: the
+    oracle trains the first C4_PARITY_TREES trees over all 10M x 128 rows of
+    the same data (drawn on the GPU with the same seeds), timed on every host
+    thread, and its trees are compared field by field with the GPU run's."""
+    threads = len(os.sched_getaffinity(0))
+    x, y, where = config4_host(torch, ROWS)
+    m = oracle_model(x, y, threads)
+    t0 = time.perf_counter()
+    m.train_more(C4_PARITY_TREES)
+    dt = time.perf_counter() - t0
+    same = same_trees(first_trees, m)
+    del m, x, y
+    return {"value": ROWS * C4_PARITY_TREES / dt, "unit": "rows*trees/s", "cores": threads, "kind": "port",
+            "sample": f"the whole config-4 workload ({ROWS} rows, data {where}), the first {C4_PARITY_TREES} "
+                      f"depth-10 trees (C++ oracle, {threads} threads, {dt:.1f} s; cuts and bins built before)",
+            "trees_identical_to_oracle": same, "trees_compared": C4_PARITY_TREES}
 
 
 # --------------------------------------------------------------------------- configs 1-3
@@ -256,15 +294,18 @@ CONFIGS = [
     ("config2", c2_data, {"objective": "binary:logistic", "max_depth": 8}, 100, 1),
     ("config3", c3_data, {"objective": "multi:softprob", "num_class": 10, "max_depth": 6}, 50, 10),
 ]
-# rounds of each config that the CPU oracle times (config 1 in full)
-CPU_ROUNDS = {"config1": 20, "config2": 10, "config3": 2}
+# rounds of each config that the CPU oracle trains, timed and compared tree by
+# tree with the GPU run's first rounds (configs 1 and 2 in full)
+CPU_ROUNDS = {"config1": 20, "config2": 100, "config3": 5}
 
 
 def same_trees(gpu_trees: list[dict], o) -> bool:
-    """Field-by-field equality of the library's trees and the oracle's
-    (structure, features, default directions exact; fp32 fields bit-exact)."""
-    if len(gpu_trees) != o.num_trees():
+    """Field-by-field equality of the library's first trees and all of the
+    oracle's (structure, features, default directions exact; fp32 fields
+    bit-exact)."""
+    if len(gpu_trees) < o.num_trees() or o.num_trees() == 0:
         return False
+    gpu_trees = gpu_trees[:o.num_trees()]
     for i, t in enumerate(gpu_trees):
         ot = o.tree(i)
         for f in ("left_children", "right_children", "split_indices", "default_left"):
@@ -280,8 +321,8 @@ def config_runs(torch, dp, device, peak_gbs: float, threads: int, cpu: bool) -> 
     """Configs 1-3 at full size on one GPU: one whole training run (every
     round, from a new booster; the DMatrix built before) timed with CUDA events
     after an identical untimed run; inputs resident in HBM.  Beside each, the
-    CPU oracle on the same data (config 1 in full, configs 2-3 for their first
-    rounds), and for config 1 whether the trees are identical."""
+    CPU oracle on the same data (configs 1-2 in full, config 3 for its first
+    five rounds) and whether its trees equal the GPU run's first trees."""
     sys.path.insert(0, str(ROOT / "oracle"))
     out = []
     for name, make, hp, rounds, K in CONFIGS:
@@ -307,7 +348,7 @@ def config_runs(torch, dp, device, peak_gbs: float, threads: int, cpu: bool) -> 
                 b.free()
         ms = ev0.elapsed_time(ev1)
         hist = b.profile().get("histograms", {"launches": 0, "ms": 0.0, "alg_bytes": 0.0})
-        trees = b.trees() if name == "config1" else None
+        trees = b.trees()
         b.free()
         d.free()
         line = {"config": name, "rows": R, "features": F, "max_depth": hp["max_depth"], "rounds": rounds,
@@ -331,8 +372,8 @@ def config_runs(torch, dp, device, peak_gbs: float, threads: int, cpu: bool) -> 
             dt = time.perf_counter() - t1
             line["cpu_oracle"] = {"rounds": cr, "seconds": dt, "rows_trees_per_s": R * cr * K / dt,
                                   "cores": threads}
-            if trees is not None:
-                line["trees_identical_to_oracle"] = same_trees(trees, m)
+            line["trees_identical_to_oracle"] = same_trees(trees, m)
+            line["trees_compared"] = m.num_trees()
             del m
         del x, y
         out.append(line)
@@ -556,6 +597,9 @@ def main() -> None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
+    # ---- the NVLink denominator: NCCL's reduce-scatter rate between these GPUs
+    nccl_peak = measure_reduce_scatter(torch, dist, device, world, max_over_ranks) if world > 1 else None
+
     # ---- the histogram kernel's shared-atomic ceiling on this GPU (its bound)
     ceiling = dp.C.c_double(0.0)
     dp.check(dp.lib().dp_probe_hist_atomics(20000, dp.C.byref(ceiling), None))
@@ -604,16 +648,18 @@ def main() -> None:
     value = args.rows * args.steps / (ms / 1e3)
     # NVLink: bytes this rank sends in the histogram reduce-scatter ((G-1)/G of
     # its partial histograms) over the exchange's event time, against the
-    # measured peer-copy rate per direction (770 GB/s on this pool)
+    # reduce-scatter rate NCCL reaches between these GPUs at 1 GiB (measured
+    # above, in this run)
     nvlink = None
     if world > 1 and "exchange_hist" in prof:
         ex = prof["exchange_hist"]
         sent = ex["alg_bytes"] * (world - 1) / world
-        nvlink = {"collective": "reduce-scatter of int64 histograms + all-gather of split candidates",
+        peak = nccl_peak["GBps"]
+        nvlink = {"collective": "reduce-scatter of histogram partials + all-gather of split candidates",
                   "bytes_per_round_per_rank": sent / breakdown_rounds,
                   "achieved_GBps": sent / (ex["ms"] / 1e3) / 1e9 if ex["ms"] else 0.0,
-                  "peak_GBps": 770.0, "peak_source": "measured peer copy per direction (profiling recipe)",
-                  "frac": (sent / (ex["ms"] / 1e3) / 1e9 / 770.0) if ex["ms"] else 0.0,
+                  "peak_GBps": peak, "peak_source": nccl_peak["how"],
+                  "frac": (sent / (ex["ms"] / 1e3) / 1e9 / peak) if ex["ms"] and peak else 0.0,
                   "note": "exchange time includes waiting for the slowest rank's histogram"}
     hist_pairs_per_s = hist.get("units", 0.0) / (hist["ms"] / 1e3) if hist["ms"] else 0.0
     atomic_roofline = {"kernel": "k_hist", "unit": "(row, feature) pairs/s", "achieved": hist_pairs_per_s,
@@ -631,6 +677,8 @@ def main() -> None:
         m = re.search(r"^bytes_per_launch_config4:\s*(\d+)", tfile.read_text(), re.M)
         traffic = int(m.group(1)) if m else None
     model_bytes = len(b.save_raw())
+    # the first trees of this run, compared with the CPU oracle's below
+    first_trees = b.trees()[:C4_PARITY_TREES] if (world == 1 and args.rows == ROWS and not args.no_cpu) else None
     b.free()
     d.free()
 
@@ -652,12 +700,8 @@ def main() -> None:
             configs = config_runs(torch, dp, device, peak_gbs, len(os.sched_getaffinity(0)), not args.no_cpu)
         if not args.no_sweep:
             sweep = hist_sweep(torch, dp, device, peak_gbs, ceiling.value)
-        if not args.no_cpu:
-            threads = len(os.sched_getaffinity(0))
-            r = cpu_oracle_run(4_000_000, 8, threads)
-            cpu = {"value": r["value"], "unit": "rows*trees/s", "cores": threads, "kind": "port",
-                   "sample": f"first 4000000 rows of the config-4 data, eight depth-10 trees "
-                             f"(C++ oracle, {threads} threads, {r['seconds']:.1f} s)"}
+        if not args.no_cpu and first_trees is not None:
+            cpu = config4_cpu_leg(torch, first_trees)
     if comm is not None:
         comm.free()
     if world > 1:
@@ -689,6 +733,8 @@ def main() -> None:
         "model_bytes": model_bytes,
     }
     if cpu is not None:
+        line["trees_identical_to_oracle"] = cpu.pop("trees_identical_to_oracle")
+        line["trees_compared"] = cpu.pop("trees_compared")
         line["cpu_baseline"] = cpu
     if sweep is not None:
         line["hist_sweep"] = sweep
@@ -697,6 +743,33 @@ def main() -> None:
     if csv is not None:
         line["csv_ingest"] = csv
     print(json.dumps(line), flush=True)
+
+
+def measure_reduce_scatter(torch, dist, device, world: int, max_over_ranks) -> dict:
+    """Bytes each rank sends per second in an NCCL reduce-scatter of 1 GiB of
+    int64 per rank ((G-1)/G of the input crosses NVLink), the slowest rank's
+    time over ten back-to-back calls after three warm-up calls."""
+    n = (1 << 27) // world * world
+    inp = torch.ones(n, dtype=torch.int64, device=device)
+    out = torch.empty(n // world, dtype=torch.int64, device=device)
+    for _ in range(3):
+        dist.reduce_scatter_tensor(out, inp)
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 10
+    e0.record()
+    for _ in range(reps):
+        dist.reduce_scatter_tensor(out, inp)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1) / reps)
+    sent = n * 8 * (world - 1) / world
+    del inp, out
+    torch.cuda.empty_cache()
+    return {"GBps": sent / (ms / 1e3) / 1e9, "ms": ms,
+            "how": "NCCL reduce-scatter of 1 GiB int64 per rank between these GPUs, measured in this run "
+                   "(bytes sent per rank / time, slowest rank)"}
 
 
 def per_level(log: list) -> list[dict]:

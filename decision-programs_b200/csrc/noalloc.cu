@@ -10,7 +10,7 @@
 // __device__ array instead; every GPU that loads the library holds that array
 // (about 1 MiB) until the process exits.  Nothing is allocated per call: the
 // task list is staged through a small stack buffer and copied into the array.
-#include <mutex>
+#include <vector>
 
 #include "../../include/dp_gbdt.h"
 #include "kernels.h"
@@ -21,7 +21,6 @@ namespace {
 // segment and one 32-feature tile; a call needs at least
 // (segments with rows) x ceil(features / 32) tasks.
 constexpr uint32_t kNoAllocMaxTasks = 32768;
-constexpr int kMaxDevices = 64;
 
 struct NoAllocScratch {
   dp::HistTask tasks[kNoAllocMaxTasks];
@@ -32,21 +31,17 @@ struct NoAllocScratch {
 
 static __device__ __align__(256) NoAllocScratch g_noalloc_scratch;
 
-// Device address of the scratch array on `device` (the current device).  The
-// host symbol is only a stand-in, so the address is looked up once per device
-// with that device current.
-NoAllocScratch* scratch_on(int device) {
-  static std::mutex mu;
-  static NoAllocScratch* addr[kMaxDevices] = {};
-  dp::need(device >= 0 && device < kMaxDevices, "device ordinal out of range for the no-allocation scratch");
-  std::lock_guard<std::mutex> lock(mu);
-  if (!addr[device]) {
-    void* p = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (e != cudaSuccess) dp::fail(std::string("cudaGetSymbolAddress(no-allocation scratch): ") + cudaGetErrorString(e));
-    addr[device] = static_cast<NoAllocScratch*>(p);
-  }
-  return addr[device];
+// Device address of the scratch array on the current device.  The host
+// symbol is only a stand-in for it, so the address is looked up on every call
+// with the call's device current.  The lookup costs microseconds, nothing next
+// to the call's own stream synchronisation, and a cached address could go
+// stale: after cudaDeviceReset the library's device code is loaded anew and
+// the array may sit elsewhere.  On a device's first call the lookup also loads
+// that device code.
+NoAllocScratch* scratch_here() {
+  void* p = nullptr;
+  dp::cuda_check(cudaGetSymbolAddress(&p, g_noalloc_scratch), "cudaGetSymbolAddress(no-allocation scratch)");
+  return static_cast<NoAllocScratch*>(p);
 }
 
 }  // namespace
@@ -79,9 +74,7 @@ extern "C" int dp_hist_build_noalloc(const uint8_t* bins, uint64_t bin_stride, u
                " histogram tasks (at least " + std::to_string(min_tasks) +
                " = non-empty segments x feature tiles of 32), above its fixed capacity of " +
                std::to_string(kNoAllocMaxTasks) + "; use dp_hist_build for this size");
-    int dev = 0;
-    dp::cuda_check(cudaGetDevice(&dev), "cudaGetDevice");
-    NoAllocScratch* scratch = scratch_on(dev);
+    NoAllocScratch* scratch = scratch_here();
     cudaStream_t s = static_cast<cudaStream_t>(stream);
 
     const dp::TreeArrays th{const_cast<uint32_t*>(ridx), reinterpret_cast<float2*>(const_cast<float*>(gh))};
@@ -102,17 +95,30 @@ extern "C" int dp_hist_build_noalloc(const uint8_t* bins, uint64_t bin_stride, u
       written += dp::u64(fill);
       fill = 0;
     };
+    // Queue order: piece index, then segment, then feature tile, as the
+    // allocating entry point queues them: the p-th pieces of all segments of a
+    // node-grouped row list cover about the same rows, so blocks running at
+    // one time read neighbouring rows of the bin matrix.
+    std::vector<int64_t> piece(size_t(nseg), 0);
+    int64_t max_pieces = 0;
     for (int32_t i = 0; i < nseg; ++i) {
       const int64_t n = seg_end[i] - seg_begin[i];
       if (n <= 0) continue;
-      const int64_t pieces = (n + chunk - 1) / chunk, piece = (n + pieces - 1) / pieces;
-      for (dp::u32 ft = 0; ft < ftiles; ++ft)
-        for (int64_t b = seg_begin[i]; b < seg_end[i]; b += piece) {
+      const int64_t pieces = (n + chunk - 1) / chunk;
+      piece[i] = (n + pieces - 1) / pieces;
+      max_pieces = std::max(max_pieces, pieces);
+    }
+    for (int64_t q = 0; q < max_pieces; ++q)
+      for (int32_t i = 0; i < nseg; ++i) {
+        if (!piece[i]) continue;
+        const int64_t b = seg_begin[i] + q * piece[i];
+        if (b >= seg_end[i]) continue;
+        for (dp::u32 ft = 0; ft < ftiles; ++ft) {
           batch[fill++] = dp::HistTask{dp::u32(i), ft * dp::kHistFeatureTile, 0, 0, b,
-                                       std::min<int64_t>(seg_end[i], b + piece)};
+                                       std::min<int64_t>(seg_end[i], b + piece[i])};
           if (fill == kBatch) flush();
         }
-    }
+      }
     flush();
     const dp::u64 slot = dp::u64(features) * dp::kMaxBins * 2;
     if (nseg) dp::cuda_check(cudaMemsetAsync(hist, 0, dp::u64(nseg) * slot * sizeof(int64_t), s), "zero histograms");

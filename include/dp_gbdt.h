@@ -238,11 +238,14 @@ DP_API int dp_probe_hist_atomics(uint32_t steps, double* pairs_per_second, void*
  * 1 MiB that every GPU loading the library keeps until exit; nothing is
  * allocated per call.  Limit: at most 32768 histogram tasks, i.e. roughly
  * (non-empty segments) x ceil(features / 32) <= 32768; larger calls fail with
- * a message (XGBGetLastError) naming the need and the capacity.  The first
- * call on a device looks up the array's device address, so make it before any
- * stream capture.  Calls share the array: calls that overlap on the GPU (other
- * streams or threads) race, so serialise them.  The task counter is zeroed on
- * every call and only tasks written by the call are read. */
+ * a message (XGBGetLastError) naming the need and the capacity.  Every call
+ * looks up the array's device address on its device (cudaGetSymbolAddress);
+ * the first call on a device also loads the library's device code there, so
+ * make it before any stream capture.  The call waits for `stream`
+ * (cudaStreamSynchronize) before it returns.  Calls share the array: calls
+ * that overlap on the GPU (other streams or threads) race, so serialise them.
+ * The task counter is zeroed on every call and only tasks written by the call
+ * are read. */
 DP_API int dp_hist_build_noalloc(const uint8_t* bins, uint64_t bin_stride, uint32_t features, int32_t num_bins,
                                  const float* gh, const uint32_t* ridx, const int64_t* seg_begin,
                                  const int64_t* seg_end, int32_t nseg, float sg, float sh, int64_t* hist,

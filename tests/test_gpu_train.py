@@ -46,7 +46,7 @@ def run(dp, orc, x, y, objective, rounds, K=1, **hp):
     assert b.boosted_rounds() == rounds
     o = orc.Model(x, y, objective, num_class=K, max_depth=params["max_depth"], max_bin=params["max_bin"],
                   eta=params["eta"], reg_lambda=params["lambda"], alpha=params["alpha"], gamma=params["gamma"],
-                  min_child_weight=params["min_child_weight"], rounds=rounds, threads=8)
+                  min_child_weight=params["min_child_weight"], rounds=rounds, threads=orc.default_threads())
     trees = compare_models(b, o, K)
     R = x.shape[0]
     np.testing.assert_array_equal(b.margins(R, K).view(np.uint32), o.margins().view(np.uint32))

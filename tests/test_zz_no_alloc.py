@@ -55,18 +55,17 @@ def test_noalloc_histogram_equals_the_allocating_entry_point(dp):
 
 def test_noalloc_refuses_work_above_its_capacity(dp):
     lib = dp.lib()
-    R, F = 33, 32 * 1024  # 33 one-row segments x 1024 feature tiles = 33792 tasks > 32768
-    bins = torch.zeros((R, F), dtype=torch.uint8, device="cuda")
+    R, F = 32769, 1  # 32769 one-row segments x 1 feature tile = 32769 tasks > 32768
+    bins = torch.zeros((R, 16), dtype=torch.uint8, device="cuda")
     gh = torch.zeros((R, 2), dtype=torch.float32, device="cuda")
     ridx = torch.arange(R, dtype=torch.int32, device="cuda")
     sb = np.arange(R, dtype=np.int64)
     se = sb + 1
-    # sized for the full request, so the output stays in bounds whatever happens
+    # sized for the full request (134 MB), so the output stays in bounds
+    # whatever happens; the call must refuse on the host, before device work
     hist = torch.empty((R, F, 256, 2), dtype=torch.int64, device="cuda")
-    rc = lib.dp_hist_build_noalloc(bins.data_ptr(), F, F, 256, gh.data_ptr(), ridx.data_ptr(), sb.ctypes.data,
+    rc = lib.dp_hist_build_noalloc(bins.data_ptr(), 16, F, 256, gh.data_ptr(), ridx.data_ptr(), sb.ctypes.data,
                                    se.ctypes.data, R, 1.0, 1.0, hist.data_ptr(), None)
     assert rc == -1
     msg = lib.XGBGetLastError().decode()
-    assert "capacity of 32768" in msg and "33792" in msg
-    del hist
-    torch.cuda.empty_cache()
+    assert "capacity of 32768" in msg and "32769" in msg
