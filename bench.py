@@ -496,6 +496,82 @@ def hist_sweep(torch, dp, device, peak_gbs: float, atomic_ceiling: float) -> lis
     return out
 
 
+def hist_sweep_sharded(torch, dp, device, comm, world: int, rank: int, peak_gbs: float, nccl_peak: dict,
+                       max_over_ranks) -> list[dict]:
+    """Config 5 with its 100M rows sharded over the ranks: every rank builds
+    the partial histograms of its 100M/G rows, then the library's histogram
+    exchange (a reduce-scatter of the int64 partials) leaves each rank the
+    summed histograms of 1/G of the (node, feature) cells -- the feature
+    groups (or node groups) it evaluates.  Time per case = the slowest rank's
+    build + exchange (CUDA events on one stream, five launches after three
+    warm-ups).  HBM fraction per GPU (its rows' algorithmic bytes plus its
+    partial histograms); NVLink fraction against the NCCL reduce-scatter rate
+    measured in this run."""
+    R_total, F = 100_000_000, 32
+    R = R_total // world
+    out = []
+    g = torch.Generator(device=device)
+    g.manual_seed(SEED + 5 + 1000 * rank)
+    gh = torch.stack([torch.randn(R, device=device, generator=g), torch.rand(R, device=device, generator=g)],
+                     1).contiguous()
+    stream = torch.cuda.current_stream()
+    for B in (16, 64, 256):
+        bins = torch.randint(0, B, (R, F), dtype=torch.uint8, device=device, generator=g)
+        for N in (1, 8, 64, 1024):
+            node = torch.randint(0, N, (R,), device=device, generator=g)
+            ridx = torch.argsort(node, stable=True).to(torch.int32)
+            ghp = gh[ridx.long()].contiguous()
+            dp.check(dp.lib().dp_quantize_gh(ghp.data_ptr(), R, 2.0 ** 15, 2.0 ** 16, None))
+            counts = torch.bincount(node, minlength=N).cpu().numpy()
+            del node
+            edges = np.concatenate([[0], np.cumsum(counts)]).astype(np.int64)
+            sb, se = np.ascontiguousarray(edges[:-1]), np.ascontiguousarray(edges[1:])
+            hist = torch.empty((N, F, 256, 2), dtype=torch.int64, device=device)
+            n_cells = hist.numel()
+            assert n_cells % world == 0
+            recv = torch.empty(n_cells // world, dtype=torch.int64, device=device)
+            plan = dp.ctypes_void_p()
+            dp.check(dp.lib().dp_hist_prepare(bins.data_ptr(), F, F, B, 1, ghp.data_ptr(), ridx.data_ptr(),
+                                              sb.ctypes.data, se.ctypes.data, N, 2.0 ** 15, 2.0 ** 16,
+                                              hist.data_ptr(), dp.C.byref(plan)))
+
+            def step():
+                dp.check(dp.lib().dp_hist_run(plan, stream.cuda_stream))
+                comm.reduce_scatter_hist(hist.data_ptr(), recv.data_ptr(), n_cells // world, stream.cuda_stream)
+
+            for _ in range(3):
+                step()
+            torch.cuda.synchronize()
+            reps = 5
+            e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+            hist_ms = ex_ms = 0.0
+            for _ in range(reps):
+                e0.record()
+                dp.check(dp.lib().dp_hist_run(plan, stream.cuda_stream))
+                e1.record()
+                comm.reduce_scatter_hist(hist.data_ptr(), recv.data_ptr(), n_cells // world, stream.cuda_stream)
+                e2.record()
+                torch.cuda.synchronize()
+                hist_ms += e0.elapsed_time(e1) / reps
+                ex_ms += e1.elapsed_time(e2) / reps
+            dp.check(dp.lib().dp_hist_free(plan))
+            ms = max_over_ranks(hist_ms + ex_ms)
+            hist_ms, ex_ms = max_over_ranks(hist_ms), max_over_ranks(ex_ms)
+            alg = R * (F + 12) + N * F * 256 * 16
+            sent = n_cells * 8 * (world - 1) / world
+            out.append({"bins": B, "nodes": N, "gpus": world, "ms": round(ms, 4), "hist_ms": round(hist_ms, 4),
+                        "exchange_ms": round(ex_ms, 4),
+                        "rows_features_per_s": R_total * F / (ms / 1e3),
+                        "frac_hbm_per_gpu": round(alg / (hist_ms / 1e3) / 1e9 / peak_gbs, 3),
+                        "nvlink_GBps": round(sent / (ex_ms / 1e3) / 1e9, 1),
+                        "frac_nvlink": round(sent / (ex_ms / 1e3) / 1e9 / nccl_peak["GBps"], 3)})
+            del ridx, ghp, hist, recv
+        del bins
+    del gh
+    torch.cuda.empty_cache()
+    return out
+
+
 def hist_case(rows: int, nodes: int, nbins: int, features: int = 32) -> None:
     """One config-5 histogram case: random bins, seeded uniform row->node
     assignment, node-grouped row lists, quantised (g, h); three launches."""
@@ -702,6 +778,8 @@ def main() -> None:
             sweep = hist_sweep(torch, dp, device, peak_gbs, ceiling.value)
         if not args.no_cpu and first_trees is not None:
             cpu = config4_cpu_leg(torch, first_trees)
+    if world > 1 and not args.no_sweep:
+        sweep = hist_sweep_sharded(torch, dp, device, comm, world, rank, peak_gbs, nccl_peak, max_over_ranks)
     if comm is not None:
         comm.free()
     if world > 1:

@@ -391,6 +391,14 @@ int dp_comm_set_timeout(void* comm, int64_t timeout_ms) {
   DP_API_END();
 }
 
+int dp_comm_reduce_scatter_hist(void* comm, const int64_t* send, int64_t* recv, uint64_t recv_n, void* stream) {
+  DP_API_BEGIN();
+  need(comm != nullptr, "communicator is null");
+  need(recv_n == 0 || (send != nullptr && recv != nullptr), "null buffer");
+  static_cast<dp::Comm*>(comm)->reduce_scatter_i64(send, recv, recv_n, static_cast<cudaStream_t>(stream));
+  DP_API_END();
+}
+
 int dp_booster_set_comm(BoosterHandle handle, void* comm) {
   DP_API_BEGIN();
   dp::Booster* b = as_booster(handle);

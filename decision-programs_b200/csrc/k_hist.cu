@@ -28,6 +28,7 @@
 #include <cstdlib>
 #include <cstring>
 
+#include "hist_update.cuh"
 #include "kernels.h"
 
 namespace dp {
@@ -36,14 +37,21 @@ namespace {
 
 constexpr int kFT = kHistFeatureTile;  // 32 features per tile
 constexpr int kRPW = 16;               // rows per warp step (two lanes per row)
+// Row steps in flight per warp.  Measured on B200 with the packed update
+// (config 5, 100M x 32): 4 is best for the 32-feature 256-bin kernel (1, 8
+// and 1024 nodes: 1.19 / 1.89 / 2.15 ms against 1.20 / 1.98 / 2.28 with 6
+// and 1.22 / 2.01 / 2.31 with 8); the 64-feature kernel keeps 6 (config 4:
+// 3.06 ms of histograms per round against 3.07 with 4 and 3.31 with 8); the
+// 512-thread 64-bin kernel 4.
 #ifndef DP_HIST_UNROLL
-#define DP_HIST_UNROLL 6  // the 256-bin kernel's row steps in flight (the 64-bin one keeps 4)
+#define DP_HIST_UNROLL 4
+#endif
+#ifndef DP_HIST_WIDE_UNROLL
+#define DP_HIST_WIDE_UNROLL 6
 #endif
 #ifndef DP_HIST_THREADS
 #define DP_HIST_THREADS 1024
 #endif
-// row steps in flight per warp: measured best at 6 for the 1024-thread
-// 256-bin kernel and at 4 for the 512-thread 64-bin kernel
 template <int MB>
 __host__ __device__ constexpr int unroll_for() { return MB >= 256 ? DP_HIST_UNROLL : 4; }
 constexpr u32 kNoRow = 0xffffffffu;
@@ -80,10 +88,6 @@ __device__ __forceinline__ uint4 load_codes(const u8* p, bool line) {
   return __ldg(reinterpret_cast<const uint4*>(p));
 }
 
-__device__ __forceinline__ u32 smem_addr(const void* p) {
-  return static_cast<u32>(__cvta_generic_to_shared(p));
-}
-
 template <bool QUANT>
 __device__ __forceinline__ void load_q(const TreeArrays& ta, const Scales& sc, u32 i, u32& gq, u32& hq) {
   if (QUANT) {
@@ -108,17 +112,26 @@ __global__ void __launch_bounds__(THREADS) k_hist(HistArgs a) {
   constexpr bool kPrefetch = MB < 256;
   // per warp, two stages of the row indices of one iteration
   __shared__ u32 s_rows[kPrefetch ? (THREADS / 32) * 2 * unroll_for<MB>() * kRPW : 1];
-  constexpr int kCells = MB * kFT;          // u32 planes: [bin][feature]
+  // u32 planes [bin][feature]: all 256 bin rows for MB = 256; for MB < 256
+  // one more row, which takes the updates of codes >= MB (clamped to MB) and
+  // is never folded
+  constexpr int kRows = MB < 256 ? MB + 1 : 256;
+  constexpr u32 kHOff = u32(kRows) * kFT * 4;  // h plane offset in bytes
+  constexpr int kPlaneCells = kRows * kFT;
+  constexpr int kCells = MB * kFT;
   constexpr int kWRow = MB + 1;              // int64 planes: [feature][bin], rows padded
   constexpr int kWCells = kFT * kWRow;
   constexpr int kWarps = THREADS / 32;
   constexpr u32 kStep = u32(kWarps) * kRPW;
   constexpr int kUnroll = unroll_for<MB>();
-  u32* Lg = reinterpret_cast<u32*>(smem);
-  u32* Lh = Lg + kCells;
-  long long* Wg = reinterpret_cast<long long*>(Lh + kCells);
+  // bits of a code word that are set only by codes >= MB (MB = 64)
+  constexpr u32 kHighBits = MB == 64 ? 0xc0c0c0c0u : 0u;
+  static_assert(MB == 64 || MB == 256, "64- or 256-bin planes");
+  u32* Lg = reinterpret_cast<u32*>(smem + plane_pad(smem));
+  u32* Lh = Lg + kPlaneCells;
+  long long* Wg = reinterpret_cast<long long*>(Lh + kPlaneCells);
   long long* Wh = Wg + kWCells;
-  for (int i = threadIdx.x; i < kCells; i += THREADS) {
+  for (int i = threadIdx.x; i < kPlaneCells; i += THREADS) {
     Lg[i] = 0u;
     Lh[i] = 0u;
   }
@@ -128,17 +141,10 @@ __global__ void __launch_bounds__(THREADS) k_hist(HistArgs a) {
   }
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const u32 s = u32(lane) >> 1, h16 = u32(lane & 1) * 16u;  // row slot, feature half
-  const bool rot8 = (s & 8u) != 0, rot4 = (s & 4u) != 0;   // word rotation by s >> 2
-  const u32 rsh = 8u * (s & 3u);                           // byte rotation by s & 3
-  // column of atomic step j: feature 16h + ((s + j) & 15) of the tile
-#ifdef DP_HIST_COLJ_TABLE
-  u32 colj[16];
-#pragma unroll
-  for (int j = 0; j < 16; ++j) colj[j] = h16 + ((s + u32(j)) & 15u);
-#define DP_COLJ(j) colj[j]
-#else
-#define DP_COLJ(j) (h16 + ((s + u32(j)) & 15u))
-#endif
+  // atomic step j updates feature 16h + (j ^ s) of the tile; the planes start
+  // below 2^16 in the shared window (the system's reserved bytes and this
+  // kernel's static variables come first)
+  const LaneCols cols = lane_cols(smem_addr(Lg), h16, s);
   u32 key_slot = kNoRow, key_f0 = 0, key_tree = 0;  // current accumulation target (block-uniform)
   bool key_excl = false;  // the key's task is the only one writing its (slot, tile)
   u32 in_window = 0;                                // rows in the u32 planes since the last fold
@@ -281,23 +287,13 @@ __global__ void __launch_bounds__(THREADS) k_hist(HistArgs a) {
           }
         }
 #pragma unroll
-        for (int u = 0; u < kUnroll; ++u) {
-          if (row[u] == kNoRow) continue;
-          // rotate the 16 bytes right by s: byte j of w becomes byte (j + s) & 15 of the row half
-          u32 t0 = rot8 ? v[u].z : v[u].x, t1 = rot8 ? v[u].w : v[u].y;
-          u32 t2 = rot8 ? v[u].x : v[u].z, t3 = rot8 ? v[u].y : v[u].w;
-          const u32 x0 = rot4 ? t1 : t0, x1 = rot4 ? t2 : t1, x2 = rot4 ? t3 : t2, x3 = rot4 ? t0 : t3;
-          const u32 w[4] = {__funnelshift_r(x0, x1, rsh), __funnelshift_r(x1, x2, rsh),
-                            __funnelshift_r(x2, x3, rsh), __funnelshift_r(x3, x0, rsh)};
-#pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const u32 b = (w[j >> 2] >> (8 * (j & 3))) & 0xffu;
-            if (MB < 256 && b >= u32(MB)) continue;
-            const u32 cell = b * kFT + DP_COLJ(j);
-            atomicAdd(Lg + cell, gq[u]);
-            atomicAdd(Lh + cell, hq[u]);
+        for (int u = 0; u < kUnroll; ++u)
+          if (row[u] != kNoRow) {
+            if (MB < 256 && ((v[u].x | v[u].y | v[u].z | v[u].w) & kHighBits) != 0u)
+              add_row<kHOff, u32(MB)>(v[u], gq[u], hq[u], cols);  // a code >= MB: clamped to the spare row
+            else
+              add_row<kHOff>(v[u], gq[u], hq[u], cols);
           }
-        }
       }
       if constexpr (kPrefetch) {
         asm volatile("cp.async.wait_all;" ::: "memory");
@@ -322,55 +318,70 @@ __global__ void __launch_bounds__(THREADS) k_hist(HistArgs a) {
 // Same task queue and output as k_hist, but a task covers 64 features: a
 // warp step takes 8 rows x 64 bytes (four lanes per row, 16 bytes each), so a
 // scattered row costs one cache-line lookup per 64 features instead of one per
-// 32 -- the lookups share the L1/shared data path with the shared atomics,
-// which is what bounds k_hist.  Two u32 planes [bin][64 features] fill 128 KB
-// of shared memory, so the int64 window sums move to a block-private scratch
-// in global memory (L2-resident, the planes' layout, coalesced folds).  Lane
-// (s, q) rotates its 16 bytes by s + 8 (q >> 1): in every atomic step the 16
-// lanes of q = 0, 2 (and of q = 1, 3) hit 16 distinct banks.
+// 32 -- the lookups share the L1/shared data path with the shared atomics.
+// The u32 planes fill 128 KB of shared memory as two 64 KB regions, one per
+// 32-feature half of the tile, each a g plane [bin][32] and 32 KB above it an
+// h plane (the layout of k_hist, so the packed address arithmetic of add_row
+// applies, with the half in the address's high 16 bits).  The int64 window
+// sums live in a block-private scratch in global memory (L2-resident, layout
+// [bin][64], coalesced folds).  Lane (s, q) rotates its 16 bytes by
+// s + 8 (q >> 1): in every atomic step the 16 lanes of q = 0, 2 (and of
+// q = 1, 3) hit 16 distinct banks.
 constexpr int kWide = 64;
+constexpr u32 kWideRegion = 65536;  // bytes of one half's g and h planes
 
-// TDRAIN: the drain goes through the scratch and is transposed in shared
-// memory, 32 features at a time, so that consecutive threads write
-// consecutive bins of one feature (512 contiguous bytes per warp) instead of
-// 64 features 4 KB apart.
-template <bool QUANT, bool TDRAIN = false>
+// u32 index (from the planes' start) of the g cell of (bin b, tile feature f)
+// of the 64-feature kernels; its h cell is kWideH / 4 further
+__device__ __forceinline__ u32 wide_cell(u32 b, u32 f) {
+  return (f >> 5) * (kWideRegion / 4) + b * 32u + (f & 31u);
+}
+
+constexpr u32 kWideH = 32768;  // h plane offset of a 64-feature kernel's region, bytes
+
+// Lane constants of the 64-feature kernels: lane (s, q) reads 16 bytes at
+// feature 16 q of the tile from row slot s; its region is the half q >> 1, its
+// first column 16 (q & 1) there, and its key s + 8 (q >> 1) differs from
+// every other lane's of the same first column.
+__device__ __forceinline__ LaneCols wide_lane(u32 lane, const u32* planes) {
+  const u32 s8 = lane >> 2, q = lane & 3u;
+  return lane_cols(smem_addr(planes) + (q >> 1) * kWideRegion, 16u * (q & 1u), s8 + 8u * (q >> 1));
+}
+
+template <bool QUANT>
 __global__ void __launch_bounds__(1024) k_hist_wide(HistArgs a, long long* __restrict__ wscr) {
   constexpr int MB = 256, THREADS = 1024;
   constexpr int kCells = MB * kWide;
   constexpr int kRows = 8;                       // rows per warp step
   constexpr u32 kStep = u32(THREADS / 32) * kRows;
-  constexpr int kUnroll = 6;
+  constexpr int kUnroll = DP_HIST_WIDE_UNROLL;
+  constexpr u32 kH = kWideH / 4;
   extern __shared__ __align__(16) unsigned char smem[];
   __shared__ u32 s_task;
-  u32* Lg = reinterpret_cast<u32*>(smem);
-  u32* Lh = Lg + kCells;
+  u32* L = reinterpret_cast<u32*>(smem + plane_pad(smem));
   long long* Sg = wscr + u64(blockIdx.x) * 2 * kCells;
   long long* Sh = Sg + kCells;
-  for (int i = threadIdx.x; i < kCells; i += THREADS) {
-    Lg[i] = 0u;
-    Lh[i] = 0u;
-  }
+  for (int i = threadIdx.x; i < 2 * kCells; i += THREADS) L[i] = 0u;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const u32 s8 = u32(lane) >> 2, q = u32(lane & 3);
-  const u32 rot = (s8 + 8u * (q >> 1)) & 15u;
-  const bool rot8 = (rot & 8u) != 0, rot4 = (rot & 4u) != 0;
-  const u32 rsh = 8u * (rot & 3u);
-  const u32 q16 = 16u * q;
+  const u32 s8 = u32(lane) >> 2;
+  const LaneCols wl = wide_lane(u32(lane), L);
+  const u32 q16 = 16u * u32(lane & 3);
   u32 key_slot = kNoRow, key_f0 = 0, key_tree = 0;
   bool key_excl = false;
   u32 in_window = 0;
   bool s_clean = true;  // the scratch holds nothing of the current key (block-uniform)
   const u32 ntasks = a.ntasks_dev ? *a.ntasks_dev : a.ntasks;
 
+  // the window's sums into the scratch ([bin][64], cell i = b * 64 + f), the
+  // planes cleared; consecutive threads read consecutive columns of a half
   auto fold = [&]() {
     for (int i = threadIdx.x; i < kCells; i += THREADS) {
-      const long long g = static_cast<long long>(static_cast<int>(Lg[i]));
-      const long long h = static_cast<long long>(Lh[i]);
+      const u32 c = wide_cell(u32(i) / kWide, u32(i) % kWide);
+      const long long g = static_cast<long long>(static_cast<int>(L[c]));
+      const long long h = static_cast<long long>(L[c + kH]);
       Sg[i] = s_clean ? g : Sg[i] + g;
       Sh[i] = s_clean ? h : Sh[i] + h;
-      Lg[i] = 0u;
-      Lh[i] = 0u;
+      L[c] = 0u;
+      L[c + kH] = 0u;
     }
     s_clean = false;
   };
@@ -387,68 +398,26 @@ __global__ void __launch_bounds__(1024) k_hist_wide(HistArgs a, long long* __res
       // scratch + last window straight to the output; each thread keeps the
       // cells it folded, so no barrier is needed between the two
       i64* out = a.hist + u64(key_slot) * a.layout.slot_stride;
-      if constexpr (TDRAIN) {
-        auto put = [&](u32 f, u32 b, long long gs, long long hs) {
-          const u32 gf = key_f0 + f;
-          if (gf >= a.F) return;
-          const u32 grp = gf / a.layout.fg, fl = gf - grp * a.layout.fg;
-          i64* cell = out + grp * a.layout.group_stride + (u64(fl) * kMaxBins + b) * 2;
-          if (key_excl) {
-            *reinterpret_cast<longlong2*>(cell) = make_longlong2(gs, hs);
-          } else if (gs | hs) {
-            atomicAdd(reinterpret_cast<unsigned long long*>(cell), static_cast<unsigned long long>(gs));
-            atomicAdd(reinterpret_cast<unsigned long long*>(cell) + 1, static_cast<unsigned long long>(hs));
-          }
-        };
-        // the key's full sums into the scratch (each thread its own cells)
-        for (int i = threadIdx.x; i < kCells; i += THREADS) {
-          const long long g = static_cast<long long>(static_cast<int>(Lg[i]));
-          const long long h = static_cast<long long>(Lh[i]);
-          Sg[i] = s_clean ? g : Sg[i] + g;
-          Sh[i] = s_clean ? h : Sh[i] + h;
+      for (int i = threadIdx.x; i < kCells; i += THREADS) {
+        const u32 b = u32(i) / kWide, f = u32(i) % kWide;
+        const u32 c = wide_cell(b, f);
+        long long gs = static_cast<long long>(static_cast<int>(L[c]));
+        long long hs = static_cast<long long>(L[c + kH]);
+        if (!s_clean) {
+          gs += Sg[i];
+          hs += Sh[i];
         }
-        __syncthreads();  // the planes are read; they become the staging area
-        // pairs T[f][b ^ f] for 32 features (128 KB): the XOR keeps both the
-        // staging writes and the bin-order reads at four wavefronts per warp
-        longlong2* T = reinterpret_cast<longlong2*>(smem);
-        for (u32 half = 0; half < 2; ++half) {
-          for (int i = threadIdx.x; i < kCells / 2; i += THREADS) {
-            const u32 b = u32(i) / 32u, fl = u32(i) % 32u, src = b * kWide + half * 32u + fl;
-            T[fl * MB + (b ^ fl)] = make_longlong2(Sg[src], Sh[src]);
-          }
-          __syncthreads();
-          for (int idx = threadIdx.x; idx < kCells / 2; idx += THREADS) {
-            const u32 fl = u32(idx) / MB, b = u32(idx) % MB;
-            const longlong2 v = T[fl * MB + (b ^ fl)];
-            put(half * 32u + fl, b, v.x, v.y);
-          }
-          __syncthreads();
-        }
-        for (int i = threadIdx.x; i < kCells; i += THREADS) {
-          Lg[i] = 0u;
-          Lh[i] = 0u;
-        }
-      } else {
-        for (int i = threadIdx.x; i < kCells; i += THREADS) {
-          const int b = i / kWide, f = i % kWide;
-          long long gs = static_cast<long long>(static_cast<int>(Lg[i]));
-          long long hs = static_cast<long long>(Lh[i]);
-          if (!s_clean) {
-            gs += Sg[i];
-            hs += Sh[i];
-          }
-          Lg[i] = 0u;
-          Lh[i] = 0u;
-          const u32 gf = key_f0 + u32(f);
-          if (gf >= a.F) continue;
-          const u32 grp = gf / a.layout.fg, fl = gf - grp * a.layout.fg;
-          i64* cell = out + grp * a.layout.group_stride + (u64(fl) * kMaxBins + b) * 2;
-          if (key_excl) {
-            *reinterpret_cast<longlong2*>(cell) = make_longlong2(gs, hs);
-          } else if (gs | hs) {
-            atomicAdd(reinterpret_cast<unsigned long long*>(cell), static_cast<unsigned long long>(gs));
-            atomicAdd(reinterpret_cast<unsigned long long*>(cell) + 1, static_cast<unsigned long long>(hs));
-          }
+        L[c] = 0u;
+        L[c + kH] = 0u;
+        const u32 gf = key_f0 + f;
+        if (gf >= a.F) continue;
+        const u32 grp = gf / a.layout.fg, fl = gf - grp * a.layout.fg;
+        i64* cell = out + grp * a.layout.group_stride + (u64(fl) * kMaxBins + b) * 2;
+        if (key_excl) {
+          *reinterpret_cast<longlong2*>(cell) = make_longlong2(gs, hs);
+        } else if (gs | hs) {
+          atomicAdd(reinterpret_cast<unsigned long long*>(cell), static_cast<unsigned long long>(gs));
+          atomicAdd(reinterpret_cast<unsigned long long*>(cell) + 1, static_cast<unsigned long long>(hs));
         }
       }
       s_clean = true;
@@ -492,21 +461,8 @@ __global__ void __launch_bounds__(1024) k_hist_wide(HistArgs a, long long* __res
           }
         }
 #pragma unroll
-        for (int u = 0; u < kUnroll; ++u) {
-          if (row[u] == kNoRow) continue;
-          u32 t0 = rot8 ? v[u].z : v[u].x, t1 = rot8 ? v[u].w : v[u].y;
-          u32 t2 = rot8 ? v[u].x : v[u].z, t3 = rot8 ? v[u].y : v[u].w;
-          const u32 x0 = rot4 ? t1 : t0, x1 = rot4 ? t2 : t1, x2 = rot4 ? t3 : t2, x3 = rot4 ? t0 : t3;
-          const u32 w[4] = {__funnelshift_r(x0, x1, rsh), __funnelshift_r(x1, x2, rsh), __funnelshift_r(x2, x3, rsh),
-                            __funnelshift_r(x3, x0, rsh)};
-#pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const u32 b = (w[j >> 2] >> (8 * (j & 3))) & 0xffu;
-            const u32 cell = b * kWide + q16 + ((rot + u32(j)) & 15u);
-            atomicAdd(Lg + cell, gq[u]);
-            atomicAdd(Lh + cell, hq[u]);
-          }
-        }
+        for (int u = 0; u < kUnroll; ++u)
+          if (row[u] != kNoRow) add_row<kWideH>(v[u], gq[u], hq[u], wl);
       }
       in_window += end - pos;
       pos = end;
@@ -520,36 +476,28 @@ __global__ void __launch_bounds__(1024) k_hist_wide(HistArgs a, long long* __res
   }
 }
 
-template <bool QUANT, bool TDRAIN>
-void launch_hist_wide_drain(const HistArgs& a, i64* scratch, u64 scratch_elems, cudaStream_t s) {
-  constexpr int kSmem = 256 * kWide * 8;
+template <bool QUANT>
+void launch_hist_wide_variant(const HistArgs& a, i64* scratch, u64 scratch_elems, cudaStream_t s) {
+  constexpr int kSmem = int(kPlaneAlignPad) + 256 * kWide * 8;
   static thread_local int configured_device = -1;
   static thread_local int grid_cap = 0;
   int dev = 0;
   DP_CUDA(cudaGetDevice(&dev));
   if (configured_device != dev) {
-    DP_CUDA(cudaFuncSetAttribute(k_hist_wide<QUANT, TDRAIN>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem));
+    DP_CUDA(cudaFuncSetAttribute(k_hist_wide<QUANT>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem));
     // shared-memory carve-out in percent (testing knob: how L1 size matters)
     if (const char* c = std::getenv("DP_HIST_CARVEOUT"))
-      DP_CUDA(cudaFuncSetAttribute(k_hist_wide<QUANT, TDRAIN>, cudaFuncAttributePreferredSharedMemoryCarveout, std::atoi(c)));
+      DP_CUDA(cudaFuncSetAttribute(k_hist_wide<QUANT>, cudaFuncAttributePreferredSharedMemoryCarveout, std::atoi(c)));
     int sms = 0, per_sm = 0;
     DP_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-    DP_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_hist_wide<QUANT, TDRAIN>, 1024, kSmem));
+    DP_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_hist_wide<QUANT>, 1024, kSmem));
     grid_cap = sms * (per_sm > 0 ? per_sm : 1);
     configured_device = dev;
   }
   const u32 grid = (a.ntasks_dev || a.ntasks >= u32(grid_cap)) ? u32(grid_cap) : a.ntasks;
   need(scratch_elems >= u64(grid) * 2 * 256 * kWide, "internal error: histogram window scratch too small for the grid");
   DP_CUDA(cudaMemsetAsync(a.counter, 0, sizeof(u32), s));
-  k_hist_wide<QUANT, TDRAIN><<<grid, 1024, kSmem, s>>>(a, reinterpret_cast<long long*>(scratch));
-}
-
-// DP_HIST_TDRAIN=1: the transposed drain
-template <bool QUANT>
-void launch_hist_wide_variant(const HistArgs& a, i64* scratch, u64 scratch_elems, cudaStream_t s) {
-  const char* t = std::getenv("DP_HIST_TDRAIN");
-  if (t && t[0] == '1' && t[1] == 0) launch_hist_wide_drain<QUANT, true>(a, scratch, scratch_elems, s);
-  else launch_hist_wide_drain<QUANT, false>(a, scratch, scratch_elems, s);
+  k_hist_wide<QUANT><<<grid, 1024, kSmem, s>>>(a, reinterpret_cast<long long*>(scratch));
 }
 
 // ---------------------------------------------------------------------------
@@ -576,7 +524,7 @@ constexpr int kBulkStages = 2;
 // planes, 128 bytes of alignment room, stages of ROWS rows (128-byte
 // aligned), barriers
 template <int ROWS>
-constexpr int bulk_smem() { return 256 * kWide * 8 + 128 + 32 * kBulkStages * ROWS * kWide + 32 * kBulkStages * 8; }
+constexpr int bulk_smem() { return int(kPlaneAlignPad) + 256 * kWide * 8 + 32 * kBulkStages * ROWS * kWide + 32 * kBulkStages * 8; }
 constexpr u64 kBulkWaitNs = 1000000000ull;
 
 __device__ __forceinline__ void mbar_init(u32 bar, u32 count) {
@@ -636,26 +584,6 @@ __device__ __forceinline__ void gather4_g2s(u32 dst, const CUtensorMap* map, int
       : "memory");
 }
 
-// The 64 shared-atomic pairs of one row's 16 codes held by lane (s, q) of
-// the 64-feature kernels: codes rotated by `rot` bytes (rot8, rot4, rsh its
-// word and byte parts) so that atomic step j updates feature
-// q16 + ((rot + j) & 15) of the tile.
-__device__ __forceinline__ void add_codes(u32* Lg, u32* Lh, uint4 v, u32 gq, u32 hq, bool rot8, bool rot4, u32 rsh,
-                                          u32 rot, u32 q16) {
-  const u32 t0 = rot8 ? v.z : v.x, t1 = rot8 ? v.w : v.y;
-  const u32 t2 = rot8 ? v.x : v.z, t3 = rot8 ? v.y : v.w;
-  const u32 x0 = rot4 ? t1 : t0, x1 = rot4 ? t2 : t1, x2 = rot4 ? t3 : t2, x3 = rot4 ? t0 : t3;
-  const u32 w[4] = {__funnelshift_r(x0, x1, rsh), __funnelshift_r(x1, x2, rsh), __funnelshift_r(x2, x3, rsh),
-                    __funnelshift_r(x3, x0, rsh)};
-#pragma unroll
-  for (int j = 0; j < 16; ++j) {
-    const u32 b = (w[j >> 2] >> (8 * (j & 3))) & 0xffu;
-    const u32 cell = b * kWide + q16 + ((rot + u32(j)) & 15u);
-    atomicAdd(Lg + cell, gq);
-    atomicAdd(Lh + cell, hq);
-  }
-}
-
 template <bool QUANT, bool GATHER, int kBulkRows>
 __global__ void __launch_bounds__(1024) k_hist_bulk(HistArgs a, long long* __restrict__ wscr, u32* __restrict__ status,
                                                     u32 status_bit, u32 pitch, u32 copy_warps,
@@ -669,18 +597,15 @@ __global__ void __launch_bounds__(1024) k_hist_bulk(HistArgs a, long long* __res
   extern __shared__ __align__(16) unsigned char smem[];
   __shared__ u32 s_task;
   __shared__ u32 s_abort;
-  u32* Lg = reinterpret_cast<u32*>(smem);
-  u32* Lh = Lg + kCells;
-  const u32 planes_end = smem_addr(smem) + 2u * kCells * 4u;
-  unsigned char* stages = smem + 2 * kCells * 4 + (((planes_end + 127u) & ~127u) - planes_end);
+  constexpr u32 kH = kWideH / 4;
+  u32* L = reinterpret_cast<u32*>(smem + plane_pad(smem));  // the planes of k_hist_wide
+  // planes end 128-byte aligned (they start so and hold 128 KB)
+  unsigned char* stages = reinterpret_cast<unsigned char*>(L) + 2 * kCells * 4;
   unsigned long long* bars =
       reinterpret_cast<unsigned long long*>(stages + kWarps * kBulkStages * kBulkStageBytes);
   long long* Sg = wscr + u64(blockIdx.x) * 2 * kCells;
   long long* Sh = Sg + kCells;
-  for (int i = threadIdx.x; i < kCells; i += THREADS) {
-    Lg[i] = 0u;
-    Lh[i] = 0u;
-  }
+  for (int i = threadIdx.x; i < 2 * kCells; i += THREADS) L[i] = 0u;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   unsigned char* my_stages = stages + warp * kBulkStages * kBulkStageBytes;
   const u32 stage_s = smem_addr(my_stages);
@@ -688,11 +613,9 @@ __global__ void __launch_bounds__(1024) k_hist_bulk(HistArgs a, long long* __res
   if (lane < kBulkStages) mbar_init(bar + 8u * u32(lane), 1u);
   if (threadIdx.x == 0) s_abort = 0;
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-  const u32 s8 = u32(lane) >> 2, q = u32(lane & 3);
-  const u32 rot = (s8 + 8u * (q >> 1)) & 15u;
-  const bool rot8 = (rot & 8u) != 0, rot4 = (rot & 4u) != 0;
-  const u32 rsh = 8u * (rot & 3u);
-  const u32 q16 = 16u * q;
+  const u32 s8 = u32(lane) >> 2;
+  const LaneCols wl = wide_lane(u32(lane), L);
+  const u32 q16 = 16u * u32(lane & 3);
   u32 key_slot = kNoRow, key_f0 = 0, key_tree = 0;
   bool key_excl = false;
   u32 in_window = 0;
@@ -705,12 +628,13 @@ __global__ void __launch_bounds__(1024) k_hist_bulk(HistArgs a, long long* __res
 
   auto fold = [&]() {
     for (int i = threadIdx.x; i < kCells; i += THREADS) {
-      const long long g = static_cast<long long>(static_cast<int>(Lg[i]));
-      const long long h = static_cast<long long>(Lh[i]);
+      const u32 c = wide_cell(u32(i) / kWide, u32(i) % kWide);
+      const long long g = static_cast<long long>(static_cast<int>(L[c]));
+      const long long h = static_cast<long long>(L[c + kH]);
       Sg[i] = s_clean ? g : Sg[i] + g;
       Sh[i] = s_clean ? h : Sh[i] + h;
-      Lg[i] = 0u;
-      Lh[i] = 0u;
+      L[c] = 0u;
+      L[c + kH] = 0u;
     }
     s_clean = false;
   };
@@ -727,14 +651,15 @@ __global__ void __launch_bounds__(1024) k_hist_bulk(HistArgs a, long long* __res
       i64* out = a.hist + u64(key_slot) * a.layout.slot_stride;
       for (int i = threadIdx.x; i < kCells; i += THREADS) {
         const int b = i / kWide, f = i % kWide;
-        long long gs = static_cast<long long>(static_cast<int>(Lg[i]));
-        long long hs = static_cast<long long>(Lh[i]);
+        const u32 c = wide_cell(u32(b), u32(f));
+        long long gs = static_cast<long long>(static_cast<int>(L[c]));
+        long long hs = static_cast<long long>(L[c + kH]);
         if (!s_clean) {
           gs += Sg[i];
           hs += Sh[i];
         }
-        Lg[i] = 0u;
-        Lh[i] = 0u;
+        L[c] = 0u;
+        L[c + kH] = 0u;
         const u32 gf = key_f0 + u32(f);
         if (gf >= a.F) continue;
         const u32 grp = gf / a.layout.fg, fl = gf - grp * a.layout.fg;
@@ -843,7 +768,7 @@ __global__ void __launch_bounds__(1024) k_hist_bulk(HistArgs a, long long* __res
           }
 #pragma unroll
           for (int u = 0; u < kDirect * kSteps; ++u)
-            if (row[u] != kNoRow) add_codes(Lg, Lh, v[u], gq[u], hq[u], rot8, rot4, rsh, rot, q16);
+            if (row[u] != kNoRow) add_row<kWideH>(v[u], gq[u], hq[u], wl);
         }
       }
       u32 c = u32(warp);
@@ -899,7 +824,7 @@ __global__ void __launch_bounds__(1024) k_hist_bulk(HistArgs a, long long* __res
         row_ahead = load_row(c + 3u * kWarps);
 #pragma unroll
         for (int u = 0; u < kSteps; ++u)
-          if (ok[u]) add_codes(Lg, Lh, v[u], gq[u], hq[u], rot8, rot4, rsh, rot, q16);
+          if (ok[u]) add_row<kWideH>(v[u], gq[u], hq[u], wl);
       }
       in_window += end - pos;
       pos = end;
@@ -968,7 +893,8 @@ void launch_hist_bulk_variant(const HistArgs& a, i64* scratch, u64 scratch_elems
 
 template <int MB, int THREADS, bool QUANT>
 void launch_hist_variant(const HistArgs& a, cudaStream_t s) {
-  constexpr int kSmem = MB * kFT * (4 + 4) + kFT * (MB + 1) * (8 + 8);
+  constexpr int kRows = MB < 256 ? MB + 1 : 256;  // u32 plane rows (k_hist)
+  constexpr int kSmem = int(kPlaneAlignPad) + kRows * kFT * (4 + 4) + kFT * (MB + 1) * (8 + 8);
   static thread_local int configured_device = -1;
   static thread_local int grid_cap = 0;
   int dev = 0;
@@ -1009,8 +935,9 @@ u64 hist_wide_scratch_elems() {
   int dev = 0, sms = 148, per_sm = 1;
   DP_CUDA(cudaGetDevice(&dev));
   DP_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-  DP_CUDA(cudaFuncSetAttribute(k_hist_wide<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 256 * kWide * 8));
-  DP_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_hist_wide<true, false>, 1024, 256 * kWide * 8));
+  constexpr int kSmem = int(kPlaneAlignPad) + 256 * kWide * 8;
+  DP_CUDA(cudaFuncSetAttribute(k_hist_wide<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem));
+  DP_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_hist_wide<true>, 1024, kSmem));
   return u64(sms) * u64(per_sm > 0 ? per_sm : 1) * 2 * 256 * kWide;
 }
 

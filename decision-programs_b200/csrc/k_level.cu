@@ -96,6 +96,11 @@ __global__ void __launch_bounds__(kBook) k_hist_tasks(RoundBuffers b, u32 ftiles
   u64 rows = 0, total = 0;
   for (u32 i = threadIdx.x; i < nb; i += kBook) rows += u64(b.open_cur[b.build[i]].count);
   scan_block(rows, &total);
+  // About four tasks per SM: finer pieces keep the blocks running at one
+  // time on neighbouring rows (L2 reuse of lines shared by several nodes'
+  // rows); measured on B200 against one task per SM, which halves the
+  // pieces' drains but was 8% slower over a config-4 round and 50% slower
+  // for config 5 with 8 nodes.
   const u64 target = u64(nsm) * 4;
   u64 chunk = (total * ftiles + target - 1) / target;
   if (chunk < 2048) chunk = 2048;

@@ -9,7 +9,9 @@
 // 32 distinct banks, per warp step) -- over pseudo-random bin codes generated
 // in registers, with no global-memory traffic.  Its pairs per second are the
 // ceiling against which the histogram kernel's pairs per second are read.
+// The update itself is the kernels' add_row (hist_update.cuh).
 #include "../../include/dp_gbdt.h"
+#include "hist_update.cuh"
 #include "kernels.h"
 
 namespace dp {
@@ -26,30 +28,27 @@ __device__ __forceinline__ u32 xorshift32(u32 x) {
 }
 
 __global__ void __launch_bounds__(kProbeThreads) k_probe_atomics(u32 steps, u32* sink) {
-  extern __shared__ __align__(16) u32 planes[];
-  u32* Lg = planes;
-  u32* Lh = planes + kProbeCells;
+  extern __shared__ __align__(16) unsigned char smem[];
+  u32* planes = reinterpret_cast<u32*>(smem + plane_pad(smem));
   for (int i = threadIdx.x; i < 2 * kProbeCells; i += kProbeThreads) planes[i] = 0u;
   __syncthreads();
   const int lane = threadIdx.x & 31;
   const u32 s = u32(lane) >> 1, h16 = u32(lane & 1) * 16u;
+  const LaneCols cols = lane_cols(smem_addr(planes), h16, s);
   u32 x = 0x9e3779b9u ^ (threadIdx.x * 0x85ebca6bu) ^ (blockIdx.x * 0xc2b2ae35u);
   x = x ? x : 1u;
   const u32 gq = 3u + threadIdx.x, hq = 5u;
   for (u32 step = 0; step < steps; ++step) {
-    u32 w[4];
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      x = xorshift32(x);
-      w[k] = x;
-    }
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const u32 b = (w[j >> 2] >> (8 * (j & 3))) & 0xffu;
-      const u32 cell = b * kHistFeatureTile + h16 + ((s + u32(j)) & 15u);
-      atomicAdd(Lg + cell, gq);
-      atomicAdd(Lh + cell, hq);
-    }
+    uint4 v;
+    x = xorshift32(x);
+    v.x = x;
+    x = xorshift32(x);
+    v.y = x;
+    x = xorshift32(x);
+    v.z = x;
+    x = xorshift32(x);
+    v.w = x;
+    add_row<u32(kProbeCells) * 4u>(v, gq, hq, cols);
   }
   __syncthreads();
   u32 acc = 0;

@@ -148,6 +148,11 @@ DP_API int dp_booster_set_comm(BoosterHandle handle, void* comm);
  * training call returns -1 with the reason in XGBGetLastError(); the
  * communicator and the booster are unusable afterwards. */
 DP_API int dp_comm_set_timeout(void* comm, int64_t timeout_ms);
+/* The sharded path's histogram exchange on its own, for kernel-level builds
+ * over rows sharded across ranks: recv[0, recv_n) = the sum over ranks of
+ * each rank's block send[rank * recv_n, (rank + 1) * recv_n) of int64
+ * partial histograms (send holds nranks blocks), ordered on `stream`. */
+DP_API int dp_comm_reduce_scatter_hist(void* comm, const int64_t* send, int64_t* recv, uint64_t recv_n, void* stream);
 
 /* Per-kernel CUDA-event timings of the training rounds ({"name":{"launches",
  * "ms","alg_bytes"}}), collected on the launching stream while enabled:

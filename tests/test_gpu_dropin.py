@@ -104,6 +104,48 @@ def test_reference_converter_reads_gpu_trained_models(dp, orc, tmp_path):
     assert doc["features"] == F
 
 
+CONVERT = ROOT / "oracle" / "_ref" / "ref_convert_check"
+LIBRARY = ROOT / "decision-programs_b200" / "libdp_gbdt.so"
+
+
+@pytest.mark.skipif(not CONVERT.exists(), reason="reference converter harness not built (needs the reference sources)")
+@pytest.mark.parametrize("objective", ["multi:softprob", "multi:softmax"])
+def test_reference_converter_native_session(dp, orc, tmp_path, objective):
+    """The reference converter's acceptance of a GPU-trained model, run by the
+    converter's own code (native/class_model_convert.cpp, compiled unmodified):
+    source_shape() gates the model JSON, then its ResidentModel dlopens
+    libdp_gbdt as the native library, checks version and CUDA build, loads the
+    model from its buffer, checks feature count, objective, classes and device
+    in the JSON configuration, and predicts rows from device memory.  Its
+    margins and outputs equal the oracle's predictions bit for bit."""
+    import torch
+
+    rng = np.random.default_rng(44)
+    R, F, K = 5000, 7, 4
+    x = rng.standard_normal((R, F)).astype(np.float32)
+    x[rng.random((R, F)) < 0.05] = np.nan
+    y = np.argmax(np.nan_to_num(x[:, :K]) + 0.5 * rng.standard_normal((R, K)), 1).astype(np.float32)
+    params = {"objective": objective, "num_class": K, "tree_method": "hist", "device": "cuda:0",
+              "max_depth": 4, "max_bin": 256, "eta": 0.3}
+    d = dp.DMatrix.from_torch(torch.from_numpy(x).cuda(), torch.from_numpy(y).cuda())
+    b = dp.train(params, d, 3)
+    model = tmp_path / "model.json"
+    b.save_model(str(model))
+    rows = 700
+    xr = np.ascontiguousarray(x[:rows])
+    (tmp_path / "rows.f32").write_bytes(xr.tobytes())
+    r = subprocess.run([str(CONVERT), "native", str(model), str(LIBRARY), str(tmp_path / "rows.f32"), str(rows)],
+                       capture_output=True, text=True, timeout=300)
+    doc = json.loads(r.stdout)
+    assert r.returncode == 0 and doc["ok"], doc
+    assert (doc["features"], doc["classes"], doc["objective"]) == (F, K, objective)
+    o = orc.Model(x, y, objective, num_class=K, max_depth=4, max_bin=256, eta=0.3, rounds=3, threads=8)
+    margins = np.asarray(doc["margin_bits"], np.uint32).view(np.float32).reshape(rows, K)
+    np.testing.assert_array_equal(margins.view(np.uint32), o.predict(xr, margin=True).reshape(rows, K).view(np.uint32))
+    out = np.asarray(doc["output_bits"], np.uint32).view(np.float32)
+    np.testing.assert_array_equal(out.view(np.uint32), o.predict(xr).reshape(out.shape).view(np.uint32))
+
+
 RESIDENT = ROOT / "oracle" / "_ref" / "ref_resident"
 
 

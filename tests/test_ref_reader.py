@@ -84,3 +84,54 @@ def test_hand_written_model_survives_load_and_save(dp, tmp_path):
                "default_left": t["default_left"], "klass": i % 2} for i, t in enumerate(trees)]
     check_against_trees(doc, expect, 2)
     assert doc["features"] == 3
+
+
+SHAPE = ROOT / "oracle" / "_ref" / "ref_convert_shape"
+
+
+def convert_shape(path: pathlib.Path) -> dict:
+    r = subprocess.run([str(SHAPE), "shape", str(path)], capture_output=True, text=True, timeout=120)
+    return json.loads(r.stdout)
+
+
+@pytest.mark.skipif(not SHAPE.exists(), reason="reference converter harness not built (needs the reference sources)")
+@pytest.mark.parametrize("objective", ["multi:softprob", "multi:softmax", "binary:logistic"])
+def test_reference_converter_source_gate(dp, tmp_path, objective):
+    """The reference converter's own source gate, source_shape()
+    (native/class_model_convert.cpp:49-60, compiled unmodified), on models
+    saved by libdp_gbdt: gbtree, decimal num_feature / num_class /
+    num_target, version 3.4.1 pass; the converter accepts only multiclass
+    sources, so a binary:logistic model is refused with its own message."""
+    K = 3 if objective.startswith("multi:") else 1
+    trees = [{"base_weights": [0.0, 0.5, -0.5], "categories": [], "categories_nodes": [], "categories_segments": [],
+              "categories_sizes": [], "default_left": [0, 0, 0], "id": i, "left_children": [1, -1, -1],
+              "loss_changes": [1.0, 0.0, 0.0], "parents": [2147483647, 0, 0], "right_children": [2, -1, -1],
+              "split_conditions": [0.25, 0.5, -0.5], "split_indices": [i % 4, 0, 0], "split_type": [0, 0, 0],
+              "sum_hessian": [2.0, 1.0, 1.0],
+              "tree_param": {"num_deleted": "0", "num_feature": "4", "num_nodes": "3", "size_leaf_vector": "1"}}
+             for i in range(K)]
+    obj = {"name": objective}
+    if K > 1:
+        obj["softmax_multiclass_param"] = {"num_class": str(K)}
+    else:
+        obj["reg_loss_param"] = {"scale_pos_weight": "1"}
+    model = {"learner": {
+        "attributes": {}, "feature_names": [], "feature_types": [],
+        "gradient_booster": {"model": {"gbtree_model_param": {"num_parallel_tree": "1", "num_trees": str(K)},
+                                       "iteration_indptr": [0, K], "tree_info": list(range(K)), "trees": trees},
+                             "name": "gbtree"},
+        "learner_model_param": {"base_score": "[" + ",".join(["0"] * K) + "]" if K > 1 else "5E-1",
+                                "boost_from_average": "0", "num_class": str(K if K > 1 else 0),
+                                "num_feature": "4", "num_target": "1"},
+        "objective": obj},
+        "version": [3, 4, 1]}
+    b = dp.Booster({}, [])
+    b.load_raw(json.dumps(model).encode())
+    saved = tmp_path / "model.json"
+    saved.write_bytes(b.save_raw())
+    doc = convert_shape(saved)
+    if K > 1:
+        assert doc["ok"], doc
+        assert (doc["features"], doc["classes"], doc["objective"]) == (4, K, objective)
+    else:
+        assert not doc["ok"] and doc["error"] == "source must use multiclass softprob or softmax"
