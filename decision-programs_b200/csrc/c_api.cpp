@@ -491,11 +491,7 @@ struct HistPlan {
   dp::DevBuf<dp::TreeArrays> trees;
   dp::DevBuf<dp::Scales> scales;
   dp::DevBuf<dp::u32> counter;
-  bool wide = false;
-  dp::DevBuf<int64_t> scratch;  // window sums of the 64-feature kernel
-  int bulk = 0;                  // its codes by bulk copies (DP_HIST_BULK=1) or gathers (2)
-  dp::HistBinsMap map;           // the bin matrix's tensor map for the gathers
-  dp::DevBuf<dp::u32> status;    // set when a bulk copy did not complete in time
+  bool wide = false;             // the 64-feature kernel
   int device = 0;
 };
 
@@ -555,16 +551,6 @@ HistPlan* make_hist_plan(const uint8_t* bins, uint64_t bin_stride, uint32_t feat
   p->trees.resize(1);
   p->scales.resize(1);
   p->counter.resize(1);
-  if (p->wide) p->scratch.resize(dp::hist_wide_scratch_elems());
-  const char* bulk_env = std::getenv("DP_HIST_BULK");
-  if (p->wide && bulk_env && reinterpret_cast<uintptr_t>(bins) % 16 == 0) {
-    p->bulk = std::string(bulk_env) == "1" ? 1 : std::string(bulk_env) == "2" ? 2 : 0;
-    // the row count is not an argument: the map spans every row a position
-    // can name (row indices below 2^31); only rows the tasks name are read
-    if (p->bulk == 2) dp::encode_hist_bins_map(bins, bin_stride, 0x7fffffffull, &p->map);
-  }
-  p->status.resize(1);
-  dp::cuda_check(cudaMemset(p->status.get(), 0, sizeof(dp::u32)), "memset");
   const dp::TreeArrays th{const_cast<uint32_t*>(ridx), reinterpret_cast<float2*>(const_cast<void*>(gh))};
   const dp::Scales sc{sg, sh};
   dp::cuda_check(cudaMemcpy(p->trees.get(), &th, sizeof th, cudaMemcpyHostToDevice), "upload");
@@ -581,9 +567,7 @@ void run_hist_plan(const HistPlan& p, cudaStream_t s) {
   if (p.nseg) dp::cuda_check(cudaMemsetAsync(p.hist, 0, dp::u64(p.nseg) * slot * sizeof(int64_t), s), "memset");
   if (p.wide)
     dp::launch_histograms_wide(p.bins, p.bin_stride, p.features, p.quantized, p.trees.get(), p.scales.get(),
-                               p.tasks.get(), p.ntasks, p.counter.get(), p.hist, s, nullptr, nullptr,
-                               const_cast<int64_t*>(p.scratch.get()), p.scratch.size(), p.bulk,
-                               p.status.get(), 1u, &p.map);
+                               p.tasks.get(), p.ntasks, p.counter.get(), p.hist, s, nullptr, nullptr);
   else
     dp::launch_histograms(p.bins, p.bin_stride, p.features, p.num_bins, p.quantized, p.trees.get(), p.scales.get(),
                           p.tasks.get(), p.ntasks, p.counter.get(), p.hist, s);
@@ -602,9 +586,6 @@ int dp_hist_build(const uint8_t* bins, uint64_t bin_stride, uint32_t features, i
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   run_hist_plan(*p, s);
   dp::cuda_check(cudaStreamSynchronize(s), "histograms");
-  dp::u32 status = 0;
-  dp::cuda_check(cudaMemcpy(&status, p->status.get(), sizeof status, cudaMemcpyDeviceToHost), "download");
-  need(status == 0, "histogram bulk copies did not complete within the wait limit");
   DP_API_END();
 }
 

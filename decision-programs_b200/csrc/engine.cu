@@ -176,12 +176,6 @@ Engine::Engine(DMatrix& d, const TrainParams& p, Comm* comm) : d_(d), p_(p), com
   // (2 GPUs: 1.88 against 2.16 ms).  DP_HIST_WIDE=0 / 1 overrides.
   wide_ = max_bins_ > 64 && F_ > kFT && env_u64("DP_HIST_WIDE", G_ == 1 ? 1 : 0) != 0;
   hist_tile_ = wide_ ? kHistWideTile : kFT;
-  const u64 bulk_mode = env_u64("DP_HIST_BULK", 0);
-  bulk_ = wide_ && bulk_mode <= 2 && R_ > 0 && q_->bin_stride % 16 == 0 &&
-                  reinterpret_cast<uintptr_t>(q_->bins.get()) % 16 == 0
-              ? int(bulk_mode)
-              : 0;
-  if (bulk_ == 2) encode_hist_bins_map(q_->bins.get(), q_->bin_stride, R_, &bins_map_);
   // testing knobs: force the exact-count path of deep levels
   async_open_limit_ = env_u64("DP_ASYNC_OPEN_LIMIT", async_open_limit_);
   async_hist_bytes_ = env_u64("DP_ASYNC_HIST_BYTES", async_hist_bytes_);
@@ -199,7 +193,6 @@ Engine::Engine(DMatrix& d, const TrainParams& p, Comm* comm) : d_(d), p_(p), com
   plan.want(ghmax_, 2 * size_t(K_));
   plan.want(scales_, K_);
   plan.want(hist_counter_, 1);
-  if (wide_) plan.want(hist_scratch_, hist_wide_scratch_elems());
   plan.want(scratch_, 1 + size_t(K_));
   plan.want(gh_totals_, 2 * size_t(K_));
   plan.want(round_dev_, 1);
@@ -608,8 +601,7 @@ Engine::RoundOut Engine::enqueue_round() {
     if (wide_)
       launch_histograms_wide(q_->bins.get(), q_->bin_stride, F, true, tarr_[set].get(), scales_.get(),
                              hist_tasks_.get(), 0, hist_counter_.get(), hout, stream_, &ctr->n_hist_tasks,
-                             G_ > 1 ? &lay : nullptr, hist_scratch_.get(), hist_scratch_.size(), bulk_,
-                             &ctr->overflow, kOvfHistWait, &bins_map_);
+                             G_ > 1 ? &lay : nullptr);
     else
       launch_histograms(q_->bins.get(), q_->bin_stride, F, max_bins_, true, tarr_[set].get(), scales_.get(),
                         hist_tasks_.get(), 0, hist_counter_.get(), hout, stream_, &ctr->n_hist_tasks,
@@ -708,7 +700,6 @@ void Engine::finish_round(Model& m, const RoundOut& out) {
   sync_stream();
   const u32 ovf = c_h->overflow;
   if (ovf & kOvfLostRows) fail("partition lost rows");
-  if (ovf & kOvfHistWait) fail("histogram bulk copies did not complete within the wait limit");
   if (ovf & kOvfBadCand) fail("a split candidate from the rank exchange names no feature of the matrix");
   if (ovf) fail("internal error: a per-round work list overflowed (flags " + std::to_string(ovf) + ")");
   for (int d = 0; d < D; ++d) {

@@ -172,12 +172,9 @@ class Engine {
   DevBuf<i64> hist_[2];
   DevBuf<HistTask> hist_tasks_;
   DevBuf<u32> hist_counter_;
-  // 64-feature histogram tasks (k_hist_wide) and their window-sum scratch
+  // 64-feature histogram tasks (k_hist_wide)
   bool wide_ = false;
-  int bulk_ = 0;  // the 64-feature kernel's codes by bulk copies (1) or tensor gathers (2): DP_HIST_BULK
-  HistBinsMap bins_map_;  // the bin matrix's tensor map (bulk_ == 2)
   u32 hist_tile_ = kHistFeatureTile;
-  DevBuf<i64> hist_scratch_;
   DevBuf<EvalNode> eval_nodes_;
   DevBuf<SplitCand> cand_;                 // [open][nchunks_] this rank's candidates
   DevBuf<i64> send_;                       // this rank's partial histograms, group-major (G > 1)

@@ -111,28 +111,12 @@ void launch_histograms(const u8* bins, u64 bin_stride, u32 F, int max_bins, bool
                        const HistLayout* layout = nullptr);
 constexpr u32 kHistFeatureTile = 32;
 // The 256-bin build over 64-feature tasks (HistTask.f0 a multiple of 64):
-// same inputs and output as launch_histograms, plus a scratch of at least
-// hist_wide_scratch_elems() int64 for the window sums (one launch at a time).
-// With `bulk` 1 the row codes come into shared memory by one bulk copy per
-// row, with 2 by four-row tensor gathers through `map` (bins and bin_stride
-// 16-byte aligned); a copy that does not complete within about a second makes
-// the kernel OR `bulk_status_bit` into *status and stop early.
+// same inputs and output as launch_histograms; one block per SM, each using
+// all of its SM's tensor memory for the window sums.
 constexpr u32 kHistWideTile = 64;
-// A tensor map of the bin matrix for the gathers: [rows][stride] bytes, box
-// min(stride, 64) bytes x 1 row.
-struct HistBinsMap {
-  alignas(64) unsigned char desc[128];
-  const u8* bins = nullptr;
-  u64 stride = 0;
-  u32 box = 0;
-};
-void encode_hist_bins_map(const u8* bins, u64 stride, u64 rows, HistBinsMap* out);
 void launch_histograms_wide(const u8* bins, u64 bin_stride, u32 F, bool quantized_gh, const TreeArrays* trees,
                             const Scales* scales, const HistTask* tasks, u32 ntasks, u32* counter, i64* hist,
-                            cudaStream_t s, const u32* ntasks_dev, const HistLayout* layout, i64* scratch,
-                            u64 scratch_elems, int bulk = 0, u32* status = nullptr, u32 bulk_status_bit = 0,
-                            const HistBinsMap* map = nullptr);
-u64 hist_wide_scratch_elems();
+                            cudaStream_t s, const u32* ntasks_dev, const HistLayout* layout);
 // Rows per histogram task for a launch over `total_rows` row-tiles (about
 // four tasks per SM; tasks tasks of one node and tile stay contiguous).
 u64 hist_chunk_rows(u64 total_rows);

@@ -39,7 +39,7 @@ struct RoundCounters {
 // Overflow bits.
 enum : u32 {
   kOvfHistTasks = 1, kOvfNodes = 2, kOvfLeaves = 4, kOvfPartTasks = 8, kOvfLeafTasks = 16,
-  kOvfLostRows = 32, kOvfOpen = 64, kOvfHistWait = 128, kOvfBadCand = 256,
+  kOvfLostRows = 32, kOvfOpen = 64, kOvfBadCand = 256,
 };
 
 constexpr i64 kLeafChunkRows = 16384;  // rows per margin-update task

@@ -149,16 +149,15 @@ def test_histograms_match_oracle(dp, orc, F, nodes, seed, nbins, R):
     assert (ohist[-1] == 0).all()
 
 
-@pytest.mark.parametrize("wide", ["0", "1", "bulk", "gather"])
+@pytest.mark.parametrize("wide", ["0", "1"])
 @pytest.mark.parametrize("F,nodes,chunk", [(64, 1, 0), (100, 3, 40000), (160, 2, 70000), (40, 5, 0)])
 def test_both_256_bin_kernels_with_long_tasks(dp, orc, monkeypatch, wide, F, nodes, chunk):
-    """The 32- and 64-feature 256-bin kernels (DP_HIST_WIDE), the latter also
-    with its codes staged by bulk copies or by four-row tensor gathers
-    (DP_HIST_BULK 1 / 2), on tasks long enough to fold several 16383-row
-    windows (DP_HIST_MIN_CHUNK), with partial last tiles and a feature count
-    above one tile."""
-    monkeypatch.setenv("DP_HIST_WIDE", "0" if wide == "0" else "1")
-    monkeypatch.setenv("DP_HIST_BULK", {"bulk": "1", "gather": "2"}.get(wide, "0"))
+    """The 32- and 64-feature 256-bin kernels (DP_HIST_WIDE; the latter keeps
+    its window sums in tensor memory) on tasks long enough to fold several
+    16383-row windows (DP_HIST_MIN_CHUNK), with partial last tiles, a feature
+    count above one tile, nodes split into pieces (drained with atomics) and
+    nodes built whole (drained with stores)."""
+    monkeypatch.setenv("DP_HIST_WIDE", wide)
     if chunk:
         monkeypatch.setenv("DP_HIST_MIN_CHUNK", str(chunk))
     R = 150000

@@ -121,13 +121,11 @@ def test_deep_trees_with_exact_level_counts(dp, orc, monkeypatch, objective, K):
     run(dp, orc, x, y, objective, 3, K=K, max_depth=13, min_child_weight=0.0)
 
 
-@pytest.mark.parametrize("wide", ["0", "1", "bulk", "gather"])
+@pytest.mark.parametrize("wide", ["0", "1"])
 def test_both_histogram_kernels_train_the_same_trees(dp, orc, monkeypatch, wide):
     """Training with the 32- or the 64-feature histogram kernel (DP_HIST_WIDE),
-    the latter also with bulk-copied or gathered codes (DP_HIST_BULK 1 / 2), a
-    feature count that leaves the last tile partial, and missing values."""
-    monkeypatch.setenv("DP_HIST_WIDE", "0" if wide == "0" else "1")
-    monkeypatch.setenv("DP_HIST_BULK", {"bulk": "1", "gather": "2"}.get(wide, "0"))
+    a feature count that leaves the last tile partial, and missing values."""
+    monkeypatch.setenv("DP_HIST_WIDE", wide)
     rng = np.random.default_rng(31)
     x = rng.standard_normal((9000, 100)).astype(np.float32)
     x[rng.random(x.shape) < 0.03] = np.nan
