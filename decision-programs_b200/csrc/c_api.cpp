@@ -511,10 +511,13 @@ HistPlan* make_hist_plan(const uint8_t* bins, uint64_t bin_stride, uint32_t feat
   p->hist = hist;
   p->nseg = nseg;
   std::vector<dp::HistTask> tasks;
-  // the training path's choice: 256-bin matrices wider than one tile use the
-  // 64-feature kernel (DP_HIST_WIDE=0 keeps the 32-feature one)
+  // the training path's choice on one GPU: 256-bin matrices of more than 64
+  // features use the 64-feature kernel (DP_HIST_WIDE=0 / 1 overrides above
+  // 32 features)
   const char* wide_env = std::getenv("DP_HIST_WIDE");
-  p->wide = num_bins > 64 && features > dp::kHistFeatureTile && !(wide_env && std::string(wide_env) == "0");
+  const bool wide_default = features > 2 * dp::kHistFeatureTile;
+  p->wide = num_bins > 64 && features > dp::kHistFeatureTile &&
+            (wide_env && *wide_env ? std::string(wide_env) != "0" : wide_default);
   const dp::u32 tile = p->wide ? dp::kHistWideTile : dp::kHistFeatureTile;
   const dp::u32 ftiles = (features + tile - 1) / tile;
   dp::u64 total = 0;

@@ -170,11 +170,13 @@ Engine::Engine(DMatrix& d, const TrainParams& p, Comm* comm) : d_(d), p_(p), com
     if (q_->has_missing_h[f]) max_bins_ = kMaxBins;
   }
   DP_CUDA(cudaDeviceGetAttribute(&sms_, cudaDevAttrMultiProcessorCount, device_));
-  // On one GPU, 256-bin matrices wider than one tile take the 64-feature
-  // kernel (config 4: histograms 3.19 against 3.25 ms per round); with rows
-  // sharded the 32-feature kernel, whose drains are coalesced, is faster
-  // (2 GPUs: 1.88 against 2.16 ms).  DP_HIST_WIDE=0 / 1 overrides.
-  wide_ = max_bins_ > 64 && F_ > kFT && env_u64("DP_HIST_WIDE", G_ == 1 ? 1 : 0) != 0;
+  // On one GPU, 256-bin matrices of more than two 32-feature tiles take the
+  // 64-feature kernel (config 4, 128 features: histograms 2.79 against 3.13 ms
+  // per round); up to 64 features the 32-feature kernel is faster (config 2:
+  // 0.84 against 0.91 ms per round), and so it is with rows sharded (2 GPUs,
+  // before the 64-feature kernel drained through tensor memory: 1.88 against
+  // 2.16 ms).  DP_HIST_WIDE=0 / 1 overrides.
+  wide_ = max_bins_ > 64 && F_ > kFT && env_u64("DP_HIST_WIDE", (G_ == 1 && F_ > 2 * kFT) ? 1 : 0) != 0;
   hist_tile_ = wide_ ? kHistWideTile : kFT;
   // testing knobs: force the exact-count path of deep levels
   async_open_limit_ = env_u64("DP_ASYNC_OPEN_LIMIT", async_open_limit_);
