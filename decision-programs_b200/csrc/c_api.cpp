@@ -391,6 +391,12 @@ int dp_comm_set_timeout(void* comm, int64_t timeout_ms) {
   DP_API_END();
 }
 
+int dp_release_cached_memory(void) {
+  DP_API_BEGIN();
+  dp::SlabCache::release_all();
+  DP_API_END();
+}
+
 int dp_comm_reduce_scatter_hist(void* comm, const int64_t* send, int64_t* recv, uint64_t recv_n, void* stream) {
   DP_API_BEGIN();
   need(comm != nullptr, "communicator is null");

@@ -7,6 +7,8 @@
 #include <atomic>
 #include <cstdint>
 #include <functional>
+#include <mutex>
+#include <utility>
 #include <stdexcept>
 #include <string>
 #include <vector>
@@ -145,14 +147,8 @@ class SlabPlan {
     DevBuf<T>* bp = &b;
     binds_.push_back([bp, off, n](unsigned char* base) { bp->adopt(reinterpret_cast<T*>(base + off), n); });
   }
-  void commit(std::vector<DevBuf<unsigned char>>& slabs) {
-    if (binds_.empty()) return;
-    slabs.emplace_back(bytes_);
-    unsigned char* base = slabs.back().get();
-    for (auto& f : binds_) f(base);
-    binds_.clear();
-    bytes_ = 0;
-  }
+  // With device >= 0 (the current device) the slab may come from SlabCache.
+  void commit(std::vector<DevBuf<unsigned char>>& slabs, int device = -1);
   size_t bytes() const { return bytes_; }
 
  private:
@@ -160,20 +156,136 @@ class SlabPlan {
   std::vector<std::function<void(unsigned char*)>> binds_;
 };
 
-// Owned pinned host staging buffer.
+// Process-wide cache of one device slab per device, for the engines of
+// boosters that come and go on one training matrix (a hyper-parameter search
+// or out-of-fold fits create one per fit): cudaMalloc of a slab costs
+// milliseconds and cudaFree waits for the whole device.  A freed engine's slab
+// stays allocated until a later engine reuses it (it holds at least what is
+// asked for and at most twice that), another slab replaces it, or
+// release_all() (dp_release_cached_memory) frees it.
+class SlabCache {
+ public:
+  static DevBuf<unsigned char> take(int device, size_t bytes) {
+    DevBuf<unsigned char> out;
+    {
+      std::lock_guard<std::mutex> lock(mu());
+      auto& c = slots();
+      for (auto it = c.begin(); it != c.end(); ++it) {
+        if (it->first != device) continue;
+        if (it->second.size() >= bytes && it->second.size() <= 2 * bytes) out = std::move(it->second);
+        c.erase(it);  // a slab that does not fit is freed before the new allocation
+        break;
+      }
+    }
+    if (!out.get()) out.resize(bytes);
+    return out;
+  }
+  static void give(int device, DevBuf<unsigned char>&& slab) {
+    if (!slab.get()) return;
+    std::lock_guard<std::mutex> lock(mu());
+    auto& c = slots();
+    for (auto it = c.begin(); it != c.end(); ++it)
+      if (it->first == device) {
+        c.erase(it);
+        break;
+      }
+    c.emplace_back(device, std::move(slab));
+  }
+  static void release_all() {
+    std::lock_guard<std::mutex> lock(mu());
+    slots().clear();
+  }
+
+ private:
+  static std::mutex& mu() {
+    static std::mutex m;
+    return m;
+  }
+  static std::vector<std::pair<int, DevBuf<unsigned char>>>& slots() {
+    static auto* c = new std::vector<std::pair<int, DevBuf<unsigned char>>>();  // outlives static destruction
+    return *c;
+  }
+};
+
+inline void SlabPlan::commit(std::vector<DevBuf<unsigned char>>& slabs, int device) {
+  if (binds_.empty()) return;
+  if (device >= 0) slabs.push_back(SlabCache::take(device, bytes_));
+  else slabs.emplace_back(bytes_);
+  unsigned char* base = slabs.back().get();
+  for (auto& f : binds_) f(base);
+  binds_.clear();
+  bytes_ = 0;
+}
+
+// Process-wide cache of pinned host blocks.  cudaMallocHost costs about a
+// millisecond and cudaFreeHost waits for the whole device, so the staging
+// buffers of engines that come and go (a booster per fit in a
+// hyper-parameter search) reuse the blocks of engines already freed.  A
+// bounded number of blocks up to kMaxBytes each is kept; anything else is
+// freed.  Cached blocks are never handed to two owners at once.
+class PinnedCache {
+ public:
+  static constexpr size_t kMaxBlocks = 8, kMaxBytes = size_t(64) << 20;
+  // A block of at least `bytes`, and its actual size.
+  static void* take(size_t bytes, size_t* got) {
+    {
+      std::lock_guard<std::mutex> lock(mu());
+      auto& f = free_list();
+      size_t best = f.size();
+      for (size_t i = 0; i < f.size(); ++i)
+        if (f[i].second >= bytes && (best == f.size() || f[i].second < f[best].second)) best = i;
+      if (best < f.size()) {
+        void* p = f[best].first;
+        *got = f[best].second;
+        f.erase(f.begin() + long(best));
+        return p;
+      }
+    }
+    void* p = nullptr;
+    DP_CUDA(cudaMallocHost(&p, bytes));
+    *got = bytes;
+    return p;
+  }
+  static void give(void* p, size_t bytes) {
+    if (!p) return;
+    if (bytes <= kMaxBytes) {
+      std::lock_guard<std::mutex> lock(mu());
+      auto& f = free_list();
+      if (f.size() < kMaxBlocks) {
+        f.emplace_back(p, bytes);
+        return;
+      }
+    }
+    cudaFreeHost(p);
+  }
+
+ private:
+  static std::mutex& mu() {
+    static std::mutex m;
+    return m;
+  }
+  static std::vector<std::pair<void*, size_t>>& free_list() {
+    static auto* f = new std::vector<std::pair<void*, size_t>>();  // outlives static destruction
+    return *f;
+  }
+};
+
+// Owned pinned host staging buffer (blocks from PinnedCache).
 template <class T>
 class PinnedBuf {
  public:
   PinnedBuf() = default;
-  ~PinnedBuf() { if (p_) cudaFreeHost(p_); }
+  ~PinnedBuf() { PinnedCache::give(p_, n_ * sizeof(T)); }
   PinnedBuf(const PinnedBuf&) = delete;
   PinnedBuf& operator=(const PinnedBuf&) = delete;
   void reserve(size_t n) {
     if (n <= n_) return;
-    if (p_) cudaFreeHost(p_);
+    PinnedCache::give(p_, n_ * sizeof(T));
     p_ = nullptr;
-    DP_CUDA(cudaMallocHost(&p_, n * sizeof(T)));
-    n_ = n;
+    n_ = 0;
+    size_t got = 0;
+    p_ = static_cast<T*>(PinnedCache::take(n * sizeof(T), &got));
+    n_ = got / sizeof(T);
   }
   void swap(PinnedBuf& o) noexcept {
     T* p = p_; p_ = o.p_; o.p_ = p;

@@ -201,7 +201,7 @@ Engine::Engine(DMatrix& d, const TrainParams& p, Comm* comm) : d_(d), p_(p), com
   mask_words_ = (F_ + 31) / 32;
   presize(plan);
   const auto t_alloc = std::chrono::steady_clock::now();
-  plan.commit(slabs_);
+  plan.commit(slabs_, device_);  // a freed engine's slab is reused when it fits
   prof_.host("engine_alloc", ms_since(t_alloc));
   if (G_ > 1) {
     // this rank's first global row: the rows of the lower ranks
@@ -248,6 +248,8 @@ Engine::~Engine() {
     cudaStreamSynchronize(stream_);
     drop_graph();
     cudaStreamDestroy(stream_);
+    // nothing is in flight: the slab goes to the cache for the next engine
+    for (auto& slab : slabs_) SlabCache::give(device_, std::move(slab));
   }
 }
 

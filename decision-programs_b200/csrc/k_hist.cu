@@ -99,8 +99,72 @@ __device__ __forceinline__ void load_q(const TreeArrays& ta, const Scales& sc, u
   }
 }
 
+// Window sums of the 32-feature kernel in tensor memory: TMEM lane 32 q + t
+// holds feature t of the tile for the MB / 4 bins MB / 4 q .. (lane quarter
+// q), bin b' of those in columns 4 b' .. 4 b' + 3 (g low and high word, h low
+// and high word).  Warp w serves lane quarter w % 4 and NBW = MB / warps of
+// its bins.
+template <u32 MB, u32 NBW>
+struct TilePart {
+  u32 bin0, col;
+  __device__ __forceinline__ explicit TilePart(u32 tmem_base) {
+    const u32 w = threadIdx.x >> 5, tq = w & 3u;
+    bin0 = tq * (MB / 4u) + (w >> 2) * NBW;
+    col = tmem_at(tmem_base, 32u * tq, 4u * (w >> 2) * NBW);
+  }
+};
+
+// The window's u32 sums of this warp's cells (planes [bin][32], the h plane
+// hoff words after the g plane) into the int64 sums in TMEM; `clean`: the
+// key's first fold, which copies; `clear`: zero the planes.  Out of line, as
+// the 64-feature kernel's fold.
+template <u32 MB, u32 NBW>
+__device__ __noinline__ void tile_fold(u32* Lg, u32 hoff, u32 tmem_base, bool clean, bool clear) {
+  const TilePart<MB, NBW> tp(tmem_base);
+  const u32 t = threadIdx.x & 31u;
+#pragma unroll 1
+  for (u32 i = 0; i < NBW; ++i) {
+    u32 r[4];
+    if (!clean) tmem_ld4(tp.col + 4u * i, r);
+    const u32 cell = (tp.bin0 + i) * 32u + t;
+    const u32 g = Lg[cell], h = Lg[cell + hoff];
+    if (clear) {
+      Lg[cell] = 0u;
+      Lg[cell + hoff] = 0u;
+    }
+    if (!clean) {
+      tmem_wait_ld();
+    } else {
+      r[0] = r[1] = r[2] = r[3] = 0u;
+    }
+    const u64 G = ((u64(r[1]) << 32) | r[0]) + u64(i64(int(g)));
+    const u64 H = ((u64(r[3]) << 32) | r[2]) + u64(h);
+    r[0] = u32(G);
+    r[1] = u32(G >> 32);
+    r[2] = u32(H);
+    r[3] = u32(H >> 32);
+    tmem_st4(tp.col + 4u * i, r);
+  }
+  tmem_wait_st();
+}
+
+// shared memory of the 32-feature kernel: the u32 planes, or in the drain
+// the [feature][bin] int64 pairs staged over them
+// (256 bins: the window sums in tensor memory); with 64 bins the u32 planes
+// and after them int64 planes [feature][bin + 1] of the window sums, which
+// for this small kernel cost less than the tensor-memory fold (config 5, 64
+// bins, 8 nodes: 1.63 against 1.87 ms)
+template <int MB>
+constexpr int hist_smem() {
+  constexpr int rows = MB < 256 ? MB + 1 : 256;
+  constexpr int planes = rows * kHistFeatureTile * 8;
+  constexpr int stage = kHistFeatureTile * MB * 16;
+  constexpr int wplanes = kHistFeatureTile * (MB + 1) * 16;
+  return int(kPlaneAlignPad) + (MB == 256 ? (planes > stage ? planes : stage) : planes + wplanes);
+}
+
 template <int MB, int THREADS, bool QUANT>
-__global__ void __launch_bounds__(THREADS) k_hist(HistArgs a) {
+__global__ void __launch_bounds__(THREADS, THREADS <= 512 ? 2 : 1) k_hist(HistArgs a) {
   extern __shared__ __align__(16) unsigned char smem[];
   __shared__ u32 s_task;
   static_assert(unroll_for<MB>() % 2 == 0, "the two lanes of a row slot split the prefetch");
@@ -117,25 +181,32 @@ __global__ void __launch_bounds__(THREADS) k_hist(HistArgs a) {
   constexpr u32 kHOff = u32(kRows) * kFT * 4;  // h plane offset in bytes
   constexpr int kPlaneCells = kRows * kFT;
   constexpr int kCells = MB * kFT;
-  constexpr int kWRow = MB + 1;              // int64 planes: [feature][bin], rows padded
-  constexpr int kWCells = kFT * kWRow;
   constexpr int kWarps = THREADS / 32;
   constexpr u32 kStep = u32(kWarps) * kRPW;
   constexpr int kUnroll = unroll_for<MB>();
+  constexpr u32 kNBW = u32(MB) / u32(kWarps);               // bins of the window sums per warp
+  constexpr u32 kTmemCols = u32(MB);                         // 4 columns x MB / 4 bins per lane
+  static_assert(kNBW * u32(kWarps) == u32(MB) && kWarps % 4 == 0, "bins split evenly over the warps");
   // bits of a code word that are set only by codes >= MB (MB = 64)
   constexpr u32 kHighBits = MB == 64 ? 0xc0c0c0c0u : 0u;
   static_assert(MB == 64 || MB == 256, "64- or 256-bin planes");
+  constexpr bool kTmem = MB == 256;  // window sums in tensor memory, else in shared int64 planes
+  constexpr int kWRow = MB + 1;      // int64 planes [feature][bin], rows padded
+  constexpr int kWCells = kFT * kWRow;
+  __shared__ u32 s_tmem;
   u32* Lg = reinterpret_cast<u32*>(smem + plane_pad(smem));
   u32* Lh = Lg + kPlaneCells;
-  long long* Wg = reinterpret_cast<long long*>(Lh + kPlaneCells);
+  long long* Wg = reinterpret_cast<long long*>(Lh + kPlaneCells);  // (64 bins only)
   long long* Wh = Wg + kWCells;
   for (int i = threadIdx.x; i < kPlaneCells; i += THREADS) {
     Lg[i] = 0u;
     Lh[i] = 0u;
   }
-  for (int i = threadIdx.x; i < kWCells; i += THREADS) {
-    Wg[i] = 0;
-    Wh[i] = 0;
+  if constexpr (kTmem) {
+    if (threadIdx.x < 32) tmem_alloc(&s_tmem, kTmemCols);
+    tmem_fence_before_sync();
+    __syncthreads();
+    tmem_fence_after_sync();
   }
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const u32 s = u32(lane) >> 1, h16 = u32(lane & 1) * 16u;  // row slot, feature half
@@ -148,29 +219,19 @@ __global__ void __launch_bounds__(THREADS) k_hist(HistArgs a) {
   u32 in_window = 0;                                // rows in the u32 planes since the last fold
   const u32 ntasks = a.ntasks_dev ? *a.ntasks_dev : a.ntasks;
 
-  // Moves the window sums into the int64 planes (transposed to [feature][bin])
-  // and clears the window.  The first fold of a key copies (the planes hold
-  // the previous key's drained values), later folds add.
-  bool w_clean = true;  // block-uniform
-  auto fold = [&]() {
-    if (w_clean) {
-      for (int i = threadIdx.x; i < kCells; i += THREADS) {
-        const int b = i / kFT, f = i % kFT;
-        Wg[f * kWRow + b] = static_cast<long long>(static_cast<int>(Lg[i]));
-        Wh[f * kWRow + b] = static_cast<long long>(Lh[i]);
-        Lg[i] = 0u;
-        Lh[i] = 0u;
-      }
-    } else {
-      for (int i = threadIdx.x; i < kCells; i += THREADS) {
-        const int b = i / kFT, f = i % kFT;
-        Wg[f * kWRow + b] += static_cast<long long>(static_cast<int>(Lg[i]));
-        Wh[f * kWRow + b] += static_cast<long long>(Lh[i]);
-        Lg[i] = 0u;
-        Lh[i] = 0u;
-      }
+  bool t_clean = true;  // the window sums hold nothing of the current key (block-uniform)
+  // 64 bins: the window into the int64 planes (transposed to [feature][bin]),
+  // the window cleared; the key's first fold copies
+  auto wfold = [&]() {
+    for (int i = threadIdx.x; i < kCells; i += THREADS) {
+      const int b = i / kFT, f = i % kFT;
+      const long long g = static_cast<long long>(static_cast<int>(Lg[i])), h = static_cast<long long>(Lh[i]);
+      Wg[f * kWRow + b] = t_clean ? g : Wg[f * kWRow + b] + g;
+      Wh[f * kWRow + b] = t_clean ? h : Wh[f * kWRow + b] + h;
+      Lg[i] = 0u;
+      Lh[i] = 0u;
     }
-    w_clean = false;
+    t_clean = false;
   };
 
   for (;;) {
@@ -181,13 +242,10 @@ __global__ void __launch_bounds__(THREADS) k_hist(HistArgs a) {
     HistTask t{};
     if (!done) t = a.tasks[ti];
     const bool same = !done && t.slot == key_slot && t.f0 == key_f0 && t.tree == key_tree;
-    if (!same && key_slot != kNoRow) {
-      fold();
+    if (!same && key_slot != kNoRow && !kTmem) {
+      wfold();
       __syncthreads();
-      // consecutive threads take consecutive bins of one feature: a warp
-      // covers one contiguous 512-byte run.  A task that alone covers its
-      // (slot, tile) stores every cell (16-byte stores, no read of the line);
-      // otherwise non-zero cells are added with 64-bit reductions.
+      // consecutive threads take consecutive bins of one feature
       i64* out = a.hist + u64(key_slot) * a.layout.slot_stride;
       for (int idx = threadIdx.x; idx < kCells; idx += THREADS) {
         const int f = idx / MB, b = idx % MB;
@@ -203,7 +261,57 @@ __global__ void __launch_bounds__(THREADS) k_hist(HistArgs a) {
           atomicAdd(reinterpret_cast<unsigned long long*>(cell) + 1, static_cast<unsigned long long>(hs));
         }
       }
-      w_clean = true;
+      t_clean = true;
+      key_slot = kNoRow;
+      in_window = 0;
+    }
+    if (!same && key_slot != kNoRow && kTmem) {
+      tile_fold<u32(MB), kNBW>(Lg, u32(kPlaneCells), s_tmem, t_clean, false);  // the last window joins the sums
+      t_clean = false;
+      __syncthreads();  // the planes are read: they become the staging area
+      // [feature][bin] int64 pairs, bin index XOR feature (four wavefronts
+      // per warp both when a warp writes a bin of 32 features and when it
+      // reads 32 bins of one feature)
+      longlong2* T = reinterpret_cast<longlong2*>(Lg);
+      {
+        const TilePart<u32(MB), kNBW> tp(s_tmem);
+        const u32 t = u32(lane);
+#pragma unroll 1
+        for (u32 i = 0; i < kNBW; ++i) {
+          u32 r[4];
+          tmem_ld4(tp.col + 4u * i, r);
+          tmem_wait_ld();
+          const u32 b = tp.bin0 + i;
+          T[t * u32(MB) + (b ^ t)] = make_longlong2(static_cast<long long>((u64(r[1]) << 32) | r[0]),
+                                                     static_cast<long long>((u64(r[3]) << 32) | r[2]));
+        }
+      }
+      __syncthreads();
+      // consecutive threads take consecutive bins of one feature: a warp
+      // covers one contiguous 512-byte run.  A task that alone covers its
+      // (slot, tile) stores every cell (16-byte stores, no read of the line);
+      // otherwise non-zero cells are added with 64-bit reductions.
+      i64* out = a.hist + u64(key_slot) * a.layout.slot_stride;
+      for (int idx = threadIdx.x; idx < kCells; idx += THREADS) {
+        const u32 f = u32(idx) / u32(MB), b = u32(idx) % u32(MB);
+        const u32 gf = key_f0 + f;
+        if (gf >= a.F) continue;
+        const longlong2 v = T[f * u32(MB) + (b ^ f)];
+        const u32 grp = gf / a.layout.fg, fl = gf - grp * a.layout.fg;
+        i64* cell = out + grp * a.layout.group_stride + (u64(fl) * kMaxBins + b) * 2;
+        if (key_excl) {
+          *reinterpret_cast<longlong2*>(cell) = v;
+        } else if (v.x | v.y) {
+          atomicAdd(reinterpret_cast<unsigned long long*>(cell), static_cast<unsigned long long>(v.x));
+          atomicAdd(reinterpret_cast<unsigned long long*>(cell) + 1, static_cast<unsigned long long>(v.y));
+        }
+      }
+      __syncthreads();  // the staging area is read before it is cleared
+      for (int i = threadIdx.x; i < kPlaneCells; i += THREADS) {
+        Lg[i] = 0u;
+        Lh[i] = 0u;
+      }
+      t_clean = true;
       key_slot = kNoRow;
       in_window = 0;
     }
@@ -301,11 +409,21 @@ __global__ void __launch_bounds__(THREADS) k_hist(HistArgs a) {
       pos = end;
       if (in_window == u32(kWindowRows)) {
         __syncthreads();
-        fold();
+        if constexpr (kTmem) {
+          tile_fold<u32(MB), kNBW>(Lg, u32(kPlaneCells), s_tmem, t_clean, true);
+          t_clean = false;
+        } else {
+          wfold();
+        }
         __syncthreads();
         in_window = 0;
       }
     }
+  }
+  if constexpr (kTmem) {
+    tmem_fence_before_sync();
+    __syncthreads();
+    if (threadIdx.x < 32) tmem_dealloc(s_tmem, kTmemCols);
   }
 }
 
@@ -563,8 +681,7 @@ void launch_hist_wide_variant(const HistArgs& a, cudaStream_t s) {
 
 template <int MB, int THREADS, bool QUANT>
 void launch_hist_variant(const HistArgs& a, cudaStream_t s) {
-  constexpr int kRows = MB < 256 ? MB + 1 : 256;  // u32 plane rows (k_hist)
-  constexpr int kSmem = int(kPlaneAlignPad) + kRows * kFT * (4 + 4) + kFT * (MB + 1) * (8 + 8);
+  constexpr int kSmem = hist_smem<MB>();
   static thread_local int configured_device = -1;
   static thread_local int grid_cap = 0;
   int dev = 0;
@@ -574,7 +691,11 @@ void launch_hist_variant(const HistArgs& a, cudaStream_t s) {
     int sms = 0, per_sm = 0;
     DP_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     DP_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_hist<MB, THREADS, QUANT>, THREADS, kSmem));
-    grid_cap = sms * (per_sm > 0 ? per_sm : 1);
+    // every block allocates MB tensor-memory columns; the blocks one SM holds
+    // must fit its 512 (an allocation beyond them would wait for a release)
+    need(per_sm >= 1 && (MB < 256 || per_sm * MB <= 512),
+         "internal error: histogram blocks per SM exceed the tensor memory");
+    grid_cap = sms * per_sm;
     configured_device = dev;
   }
   const u32 grid = (a.ntasks_dev || a.ntasks >= u32(grid_cap)) ? u32(grid_cap) : a.ntasks;

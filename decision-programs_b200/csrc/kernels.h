@@ -133,7 +133,13 @@ void launch_gh_totals(const float2* gh_quantized, u64 R, int K, i64* totals, cud
 void launch_eval_splits(const i64* hist, u32 F, const u16* nbins, const u8* has_missing, const EvalNode* nodes,
                         u32 nnodes, const Scales* scales, SplitParams p, SplitCand* cand, SplitCand* best,
                         cudaStream_t s);
-constexpr u32 kEvalFeatureChunk = 16;
+// Features per split-evaluation work item: 8 (one per warp) gives small
+// levels twice the blocks of 16 (measured: config 1 0.266 -> 0.247 ms,
+// config 2 0.842 -> 0.815 ms per round, config 4 unchanged).
+#ifndef DP_EVAL_CHUNK
+#define DP_EVAL_CHUNK 8
+#endif
+constexpr u32 kEvalFeatureChunk = DP_EVAL_CHUNK;
 // The same with the node count in device memory, over F features that sit
 // at a stride of fstride features per slot (0: F) and whose global ids start
 // at f_base (nbins / has_missing point at the first of them).  F may be 0:
@@ -174,7 +180,13 @@ struct PartNode {
 // bins_blk[(r / 32) * blk_stride + f * 32 + r % 32], blk_stride = 32 * F.
 void launch_partition(const u8* bins_blk, u64 blk_stride, const TreeArrays* src, const TreeArrays* dst,
                       const PartNode* nodes, const PartTask* tasks, u32 ntasks, u32* cursors, cudaStream_t s);
-constexpr u32 kPartChunk = 4096;
+// Rows per partition task: 2048 gives small levels twice the tasks of 4096
+// (measured with the 8-feature evaluation items: config 1 0.247 -> 0.230 ms,
+// config 2 0.815 -> 0.778 ms per round, config 4 5.33 -> 5.34 ms).
+#ifndef DP_PART_CHUNK
+#define DP_PART_CHUNK 2048
+#endif
+constexpr u32 kPartChunk = DP_PART_CHUNK;
 // The same with the task count in device memory.
 void launch_partition_dev(const u8* bins_blk, u64 blk_stride, const TreeArrays* src, const TreeArrays* dst,
                           const PartNode* nodes, const PartTask* tasks, const u32* ntasks_dev, u32* cursors,

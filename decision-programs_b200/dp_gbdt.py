@@ -27,7 +27,7 @@ EXPORTED = [
     "XGBoosterBoostedRounds", "XGBoosterSaveJsonConfig", "XGBoosterSaveModel", "XGBoosterSaveModelToBuffer",
     "XGBoosterLoadModelFromBuffer", "XGBoosterLoadModel", "XGBoosterSlice", "XGBoosterGetNumFeature",
     "XGBoosterPredictFromCudaArray",
-    "dp_comm_unique_id", "dp_comm_create", "dp_comm_free", "dp_comm_set_timeout", "dp_comm_reduce_scatter_hist", "dp_booster_set_comm", "dp_booster_set_profiling",
+    "dp_comm_unique_id", "dp_comm_create", "dp_comm_free", "dp_comm_set_timeout", "dp_comm_reduce_scatter_hist", "dp_release_cached_memory", "dp_booster_set_comm", "dp_booster_set_profiling",
     "dp_booster_profile", "dp_booster_margins", "dp_launch_count", "dp_quantile_cuts", "dp_bin_matrix",
     "dp_gradients", "dp_hist_build", "dp_hist_build_noalloc", "dp_probe_hist_atomics", "dp_csv_decode", "dp_csv_shape", "dp_csv_data", "dp_csv_metadata", "dp_csv_copy", "dp_csv_free", "dp_csv_parse_feature", "dp_quantize_gh", "dp_hist_prepare", "dp_hist_run", "dp_hist_free", "dp_eval_splits",
 ]
@@ -80,6 +80,7 @@ def lib() -> C.CDLL:
         L.dp_comm_free.argtypes = [P]
         L.dp_comm_set_timeout.argtypes = [P, C.c_int64]
         L.dp_comm_reduce_scatter_hist.argtypes = [P, P, P, u64, P]
+        L.dp_release_cached_memory.argtypes = []
         L.dp_booster_set_comm.argtypes = [P, P]
         L.dp_booster_set_profiling.argtypes = [P, i32]
         L.dp_booster_profile.argtypes = [P, C.POINTER(C.c_char_p)]
