@@ -334,9 +334,11 @@ def config_runs(torch, dp, device, peak_gbs: float, threads: int, cpu: bool) -> 
         d = dp.DMatrix.from_torch(x, y)
         torch.cuda.synchronize()
         dmatrix_ms = 1e3 * (time.perf_counter() - t0)
+        # the untimed run records the histogram launches' events; the timed
+        # run (identical trees) records none
         for timed in (False, True):
             b = dp.Booster(params, [d])
-            b.set_profiling(True, histograms_only=True)
+            b.set_profiling(not timed, histograms_only=True)
             ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             torch.cuda.synchronize()
             ev0.record()
@@ -345,9 +347,9 @@ def config_runs(torch, dp, device, peak_gbs: float, threads: int, cpu: bool) -> 
             ev1.record()
             torch.cuda.synchronize()
             if not timed:
+                hist = b.profile().get("histograms", {"launches": 0, "ms": 0.0, "alg_bytes": 0.0})
                 b.free()
         ms = ev0.elapsed_time(ev1)
-        hist = b.profile().get("histograms", {"launches": 0, "ms": 0.0, "alg_bytes": 0.0})
         trees = b.trees()
         b.free()
         d.free()

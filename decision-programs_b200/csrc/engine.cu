@@ -178,10 +178,23 @@ Engine::Engine(DMatrix& d, const TrainParams& p, Comm* comm) : d_(d), p_(p), com
   // 2.16 ms).  DP_HIST_WIDE=0 / 1 overrides.
   wide_ = max_bins_ > 64 && F_ > kFT && env_u64("DP_HIST_WIDE", (G_ == 1 && F_ > 2 * kFT) ? 1 : 0) != 0;
   hist_tile_ = wide_ ? kHistWideTile : kFT;
+  // Histogram tasks per SM: when the bin matrix exceeds L2, about four keep
+  // the blocks running at one time on neighbouring rows (L2 reuse of lines
+  // shared by several nodes' rows; one per SM was 4% slower over a config-4
+  // round and 50% slower for config 5 with 8 nodes).  When it fits in L2,
+  // one per SM: a quarter of the pieces' drains (config 2: 0.64 against 0.68
+  // ms per round).  DP_HIST_TASKS_PER_SM overrides.
+  {
+    int l2 = 0;
+    DP_CUDA(cudaDeviceGetAttribute(&l2, cudaDevAttrL2CacheSize, device_));
+    const bool in_l2 = u64(R_) * u64(F_) <= u64(l2) / 4 * 3;
+    hist_target_tasks_ = u32(sms_) * u32(std::max<u64>(1, env_u64("DP_HIST_TASKS_PER_SM", in_l2 ? 1 : 4)));
+  }
   // testing knobs: force the exact-count path of deep levels
   async_open_limit_ = env_u64("DP_ASYNC_OPEN_LIMIT", async_open_limit_);
   async_hist_bytes_ = env_u64("DP_ASYNC_HIST_BYTES", async_hist_bytes_);
   graphs_ = env_u64("DP_CUDA_GRAPHS", 1) != 0;
+  fold_last_ = env_u64("DP_FOLD_LAST_LEVEL", 1) != 0;
 
   // every device buffer of the engine in one allocation
   const u64 RK = std::max<u64>(R_, 1) * u64(K_);
@@ -197,6 +210,9 @@ Engine::Engine(DMatrix& d, const TrainParams& p, Comm* comm) : d_(d), p_(p), com
   plan.want(hist_counter_, 1);
   plan.want(scratch_, 1 + size_t(K_));
   plan.want(gh_totals_, 2 * size_t(K_));
+  if (K_ <= kMaxReducedClasses) plan.want(max_part_, size_t(gradient_blocks(R_)) * 2 * size_t(K_));
+  plan.want(tot_part_, size_t(quantize_round_blocks(R_, K_)) * 2 * size_t(K_));
+  plan.want(done_, 4);
   plan.want(round_dev_, 1);
   mask_words_ = (F_ + 31) / 32;
   presize(plan);
@@ -221,6 +237,8 @@ Engine::Engine(DMatrix& d, const TrainParams& p, Comm* comm) : d_(d), p_(p), com
   for (int k = 0; k < K_; ++k) base[k] = p_.base_margin(k);
   float* base_d = reinterpret_cast<float*>(scratch_.get() + 1);
   DP_CUDA(cudaMemsetAsync(scratch_.get(), 0, sizeof(u32), stream_));
+  // the last-block counters start at zero (a reused slab holds old data)
+  DP_CUDA(cudaMemsetAsync(done_.get(), 0, done_.size() * sizeof(u32), stream_));
   launch_check_labels(d_.labels(), R_, p_.objective_id(), K_, scratch_.get(), stream_);
   std::memcpy(arena_.get() + kArenaHead, base.data(), K_ * sizeof(float));
   DP_CUDA(cudaMemcpyAsync(base_d, arena_.get() + kArenaHead, K_ * sizeof(float), cudaMemcpyHostToDevice, stream_));
@@ -378,6 +396,7 @@ RoundBuffers Engine::round_buffers(int depth, u64 cap_split, u64 cap_next) const
   b.build_next = build_[n].get();
   b.triples_next = triples_[n].get();
   b.hist_tasks = hist_tasks_.get();
+  b.hist_counter = hist_counter_.get();
   b.eval_nodes = eval_nodes_.get();
   b.cands = G_ > 1 ? gathered_.get() : cand_.get();
   b.nranks = u32(G_);
@@ -402,12 +421,16 @@ RoundBuffers Engine::round_buffers(int depth, u64 cap_split, u64 cap_next) const
   return b;
 }
 
-template <class T>
-const T* Engine::download(const T* src, size_t n) {
-  std::vector<T> tmp(n);
-  T* dst = stage(tmp);
-  DP_CUDA(cudaMemcpyAsync(dst, src, n * sizeof(T), cudaMemcpyDeviceToHost, stream_));
-  return dst;
+Engine::ReadbackLayout Engine::readback_layout(u64 ids) const {
+  auto up = [](size_t v) { return (v + 255) & ~size_t(255); };
+  ReadbackLayout L;
+  L.ctr = 0;
+  L.nid = up(L.ctr + sizeof(RoundCounters));
+  L.sc = up(L.nid + size_t(K_) * sizeof(u32));
+  L.st = up(L.sc + size_t(K_) * sizeof(Scales));
+  L.nodes = up(L.st + (size_t(p_.max_depth) + 1) * sizeof(LevelStats));
+  L.bytes = L.nodes + size_t(ids) * size_t(K_) * sizeof(NodeRec);
+  return L;
 }
 
 std::vector<float> Engine::margins() const {
@@ -517,25 +540,7 @@ Engine::RoundOut Engine::enqueue_round() {
   // ---- gradients and quantiser scales
   u32* const gmax = ghmax_.get();  // [K] |g| maxima, then [K] h maxima (f32 bits)
   u32* const hmax = ghmax_.get() + K;
-  DP_CUDA(cudaMemsetAsync(gmax, 0, 2 * size_t(K) * sizeof(u32), stream_));
-  prof_.begin(stream_, "gradients", double(R) * K * (4 + 8) + double(R) * 4);
-  RowSample rs;
-  if (row_sampling()) rs = RowSample{p_.subsample, p_.seed, round_dev_.get(), row0_};
-  launch_gradients(p_.objective_id(), K, margin_.get(), d_.labels(), R, gh_[0].get(), gmax, hmax, stream_, rs);
-  prof_.end(stream_);
-  if (comm_) {
-    comm_->max_u32(gmax, 2 * size_t(K), stream_);
-  }
-  launch_scales(K, gmax, hmax, scales_.get(), stream_);
-  // (g, h) become exact int32 pairs once per round; every later pass reads them
-  launch_quantize_gh(gh_[0].get(), R, K, scales_.get(), stream_);
-  for (int k = 0; k < K; ++k) launch_iota(ridx_[0].get() + u64(k) * R, R, stream_);
-  // root totals: the quantised sums over every rank's rows
-  DP_CUDA(cudaMemsetAsync(gh_totals_.get(), 0, 2 * size_t(K) * sizeof(i64), stream_));
-  launch_gh_totals(gh_[0].get(), R, K, gh_totals_.get(), stream_);
-  if (comm_) comm_->sum_i64(gh_totals_.get(), 2 * size_t(K), stream_);
-
-  // ---- round state: K roots, open at depth 0 and built directly
+  const bool one_rank = !comm_ || G_ == 1;
   grow(ctr_, 1);
   grow(stats_, size_t(D) + 1);
   grow(next_id_, K);
@@ -544,8 +549,36 @@ Engine::RoundOut Engine::enqueue_round() {
   grow(build_[0], K);
   grow_keep(nodes_, size_t(K));
   RoundCounters* const ctr = ctr_.get();  // allocated once; never regrown
-  DP_CUDA(cudaMemsetAsync(stats_.get(), 0, (size_t(D) + 1) * sizeof(LevelStats), stream_));
-  launch_round_init(round_buffers(0, 0, 0), R, gh_totals_.get(), stream_);
+  const RoundBuffers rb0 = round_buffers(0, 0, 0);
+
+  // ---- gradients and quantiser scales.  Up to 64 classes the maxima are
+  // reduced by the gradient launch's last block (with one rank it also
+  // computes the scales); beyond, per-class atomics on zeroed maxima.
+  prof_.begin(stream_, "gradients", double(R) * K * (4 + 8) + double(R) * 4);
+  RowSample rs;
+  if (row_sampling()) rs = RowSample{p_.subsample, p_.seed, round_dev_.get(), row0_};
+  const bool reduced = K <= kMaxReducedClasses;
+  if (reduced) {
+    launch_gradients_reduced(p_.objective_id(), K, margin_.get(), d_.labels(), R, gh_[0].get(), gmax, hmax,
+                             max_part_.get(), done_.get(), one_rank ? scales_.get() : nullptr, stream_, rs);
+  } else {
+    DP_CUDA(cudaMemsetAsync(gmax, 0, 2 * size_t(K) * sizeof(u32), stream_));
+    launch_gradients(p_.objective_id(), K, margin_.get(), d_.labels(), R, gh_[0].get(), gmax, hmax, stream_, rs);
+  }
+  prof_.end(stream_);
+  if (!one_rank) comm_->max_u32(gmax, 2 * size_t(K), stream_);
+  if (!reduced || !one_rank) launch_scales(K, gmax, hmax, scales_.get(), stream_);
+  // (g, h) become exact int32 pairs once per round (every later pass reads
+  // them), the row indices the identity, and the quantised root sums are
+  // reduced by the launch's last block, which with one rank also starts the
+  // round: K roots, open at depth 0 and built directly
+  launch_quantize_round(rb0, gh_[0].get(), R, scales_.get(), ridx_[0].get(), tot_part_.get(), done_.get() + 1,
+                        gh_totals_.get(), u32(D) + 1, one_rank, stream_);
+  if (!one_rank) {
+    // root totals over every rank's rows
+    comm_->sum_i64(gh_totals_.get(), 2 * size_t(K), stream_);
+    launch_round_init(rb0, R, gh_totals_.get(), u32(D) + 1, stream_);
+  }
 
   // Host-side upper bounds of the device counts, which size the buffers:
   // open nodes of this level, node ids per tree, closed leaves.  Every open
@@ -555,6 +588,7 @@ Engine::RoundOut Engine::enqueue_round() {
   std::vector<int> pi_hist(D, -1), pi_eval(D, -1);
   int set = 0, region = 0, depth = 0;
   bool zeroed_by_children = false;  // this level's output slots were zeroed by the previous level
+  bool folded = false;              // the last level routed its rows straight into the margins
   static const char* const kLevelNames[] = {"level 0", "level 1", "level 2", "level 3", "level 4", "level 5",
                                              "level 6", "level 7", "level 8", "level 9", "level 10+"};
   for (; depth < D; ++depth) {
@@ -596,20 +630,21 @@ Engine::RoundOut Engine::enqueue_round() {
     // several ranks, each builds partial histograms of all features for its
     // rows (group-major), and a reduce-scatter leaves every rank the sums of
     // its own feature group.
-    launch_hist_tasks(rb, ftiles, hist_tile_, depth, stream_);
+    launch_hist_tasks(rb, ftiles, hist_tile_, depth, hist_target_tasks_, stream_);
     i64* hout = G_ > 1 ? send_.get() : hist;
     const u64 out_slot = G_ > 1 ? full_slot_elems_ : slot_elems_;
     if (!zeroed_by_children) launch_zero_slots(rb, hout, out_slot, G_ > 1 ? nbuild_hi : 0, stream_);
     const HistLayout lay{fg_, slot_elems_, nbuild_hi * slot_elems_};
     pi_hist[depth] = prof_.begin(stream_, "histograms", 0.0);
+    // (the task kernel zeroed the queue counter)
     if (wide_)
       launch_histograms_wide(q_->bins.get(), q_->bin_stride, F, true, tarr_[set].get(), scales_.get(),
                              hist_tasks_.get(), 0, hist_counter_.get(), hout, stream_, &ctr->n_hist_tasks,
-                             G_ > 1 ? &lay : nullptr);
+                             G_ > 1 ? &lay : nullptr, true);
     else
       launch_histograms(q_->bins.get(), q_->bin_stride, F, max_bins_, true, tarr_[set].get(), scales_.get(),
                         hist_tasks_.get(), 0, hist_counter_.get(), hout, stream_, &ctr->n_hist_tasks,
-                        G_ > 1 ? &lay : nullptr);
+                        G_ > 1 ? &lay : nullptr, true);
     prof_.end(stream_);
     if (G_ > 1) {
       prof_.begin(stream_, "exchange_hist", double(nbuild_hi * full_slot_elems_) * sizeof(i64));
@@ -634,6 +669,26 @@ Engine::RoundOut Engine::enqueue_round() {
       prof_.end(stream_);
     }
     launch_decide(rb, q_->cut.get(), q_->has_missing.get(), F, depth, D, set, stream_);
+
+    if (depth + 1 == D && fold_last_) {
+      // ---- the last level: its children are leaves and nothing is built
+      // from them, so rows do not move.  Leaf values of every closed node and
+      // of the children, the closed leaves' margin update, then each split
+      // node's rows add their child's value as they are routed.
+      leaves_hi += open_hi;
+      grow(leaf_tasks_, (RK + kLeafChunkRows - 1) / kLeafChunkRows + leaves_hi);
+      const RoundBuffers rl = round_buffers(depth, open_hi, next_hi);
+      u32* const sets[2] = {ridx_[0].get(), ridx_[1].get()};
+      launch_leaf_values(rl, scales_.get(), sp, sets, R, stream_, true);
+      prof_.begin(stream_, "leaf_update", double(R) * K * 12.0);
+      launch_leaf_update_dev(leaf_tasks_.get(), &ctr->n_leaf_tasks, margin_.get(), u32(K), stream_);
+      launch_partition_leaves(q_->bins_blk.get(), 32 * u64(F), tarr_[set].get(), part_nodes_.get(),
+                              part_tasks_.get(), &ctr->n_part_tasks, cursors_.get(), margin_.get(), u32(K), stream_);
+      prof_.end(stream_);
+      ids_hi = ids_next;  // the children's ids
+      folded = true;
+      break;
+    }
 
     // ---- partition and the children's segments
     prof_.begin(stream_, "partition", 0.0);
@@ -660,18 +715,39 @@ Engine::RoundOut Engine::enqueue_round() {
     region = 1 - region;
   }
 
-  // ---- nodes still open close as leaves; leaf values and margin update
-  grow_keep(leaves_, leaves_hi + open_hi);
-  leaves_hi += open_hi;
-  grow(leaf_tasks_, (RK + kLeafChunkRows - 1) / kLeafChunkRows + leaves_hi);
-  const RoundBuffers rb = round_buffers(depth, open_hi, open_hi);
-  launch_decide(rb, q_->cut.get(), q_->has_missing.get(), F, D, D, set, stream_);
-  u32* const sets[2] = {ridx_[0].get(), ridx_[1].get()};
-  launch_leaf_values(rb, scales_.get(), sp, sets, R, stream_);
-  prof_.begin(stream_, "leaf_update", double(R) * K * 12.0);
-  launch_leaf_update_dev(leaf_tasks_.get(), &ctr->n_leaf_tasks, margin_.get(), u32(K), stream_);
-  prof_.end(stream_);
+  if (!folded) {
+    // ---- nodes still open close as leaves; leaf values and margin update
+    grow_keep(leaves_, leaves_hi + open_hi);
+    leaves_hi += open_hi;
+    grow(leaf_tasks_, (RK + kLeafChunkRows - 1) / kLeafChunkRows + leaves_hi);
+    const RoundBuffers rb = round_buffers(depth, open_hi, open_hi);
+    launch_decide(rb, q_->cut.get(), q_->has_missing.get(), F, D, D, set, stream_);
+    u32* const sets[2] = {ridx_[0].get(), ridx_[1].get()};
+    launch_leaf_values(rb, scales_.get(), sp, sets, R, stream_);
+    prof_.begin(stream_, "leaf_update", double(R) * K * 12.0);
+    launch_leaf_update_dev(leaf_tasks_.get(), &ctr->n_leaf_tasks, margin_.get(), u32(K), stream_);
+    prof_.end(stream_);
+  }
   if (row_sampling() || col_sampling()) launch_bump_round(round_dev_.get(), stream_);
+
+  // ---- the round's results straight into pinned host memory (the host
+  // reads them after one wait)
+  {
+    const u64 ids_read = std::min<u64>(ids_hi, nodes_.size() / u64(K));
+    const ReadbackLayout L = readback_layout(ids_read);
+    readback_.reserve(L.bytes);
+    u8* host = nullptr;
+    DP_CUDA(cudaHostGetDevicePointer(reinterpret_cast<void**>(&host), readback_.get(), 0));
+    const u32* src[5] = {reinterpret_cast<const u32*>(ctr), next_id_.get(),
+                         reinterpret_cast<const u32*>(scales_.get()), reinterpret_cast<const u32*>(stats_.get()),
+                         reinterpret_cast<const u32*>(nodes_.get())};
+    u32* dst[5] = {reinterpret_cast<u32*>(host + L.ctr), reinterpret_cast<u32*>(host + L.nid),
+                   reinterpret_cast<u32*>(host + L.sc), reinterpret_cast<u32*>(host + L.st),
+                   reinterpret_cast<u32*>(host + L.nodes)};
+    const u64 words[5] = {sizeof(RoundCounters) / 4, u64(K), u64(K) * sizeof(Scales) / 4,
+                          (u64(D) + 1) * sizeof(LevelStats) / 4, ids_read * u64(K) * sizeof(NodeRec) / 4};
+    launch_copy_words(src, dst, words, 5, stream_);
+  }
 
   RoundOut out;
   out.ids_hi = ids_hi;
@@ -687,21 +763,19 @@ void Engine::finish_round(Model& m, const RoundOut& out) {
   const int D = p_.max_depth;
   const SplitParams sp = p_.split_params();
   const u64 slot_bytes = slot_elems_ * sizeof(i64);
-  RoundCounters* const ctr = ctr_.get();
   const u64 ids_read = std::min<u64>(out.ids_hi, nodes_.size() / u64(K));
   auto t_wait = std::chrono::steady_clock::now();
   sync_stream();
   prof_.host("round_wait", ms_since(t_wait));
   t_wait = std::chrono::steady_clock::now();
-  arena_off_ = kArenaHead;
-  arena_.reserve(kArenaHead + ids_read * K * sizeof(NodeRec) + sizeof(RoundCounters) + K * (sizeof(u32) + sizeof(Scales)) +
-                 (size_t(D) + 1) * sizeof(LevelStats) + 5 * 256);
-  const RoundCounters* c_h = download(ctr, 1);
-  const u32* nid_h = download(next_id_.get(), K);
-  const Scales* sc_h = download(scales_.get(), K);
-  const LevelStats* st_h = download(stats_.get(), size_t(D) + 1);
-  const NodeRec* nd_h = download(nodes_.get(), ids_read * K);
-  sync_stream();
+  const ReadbackLayout L = readback_layout(ids_read);
+  need(readback_.size() >= L.bytes, "internal error: round read-back buffer too small");
+  const u8* rbh = readback_.get();
+  const RoundCounters* c_h = reinterpret_cast<const RoundCounters*>(rbh + L.ctr);
+  const u32* nid_h = reinterpret_cast<const u32*>(rbh + L.nid);
+  const Scales* sc_h = reinterpret_cast<const Scales*>(rbh + L.sc);
+  const LevelStats* st_h = reinterpret_cast<const LevelStats*>(rbh + L.st);
+  const NodeRec* nd_h = reinterpret_cast<const NodeRec*>(rbh + L.nodes);
   const u32 ovf = c_h->overflow;
   if (ovf & kOvfLostRows) fail("partition lost rows");
   if (ovf & kOvfBadCand) fail("a split candidate from the rank exchange names no feature of the matrix");

@@ -117,8 +117,6 @@ class Engine {
   T* stage(const std::vector<T>& v);  // copies into the pinned arena
   template <class T>
   void upload(DevBuf<T>& dst, const std::vector<T>& v);
-  template <class T>
-  const T* download(const T* src, size_t n);  // into the arena; valid after sync()
   // Capacity growth between launches: `grow` drops the contents, `grow_keep`
   // keeps them; both wait for the stream first, since it may still use them.
   template <class T>
@@ -168,6 +166,12 @@ class Engine {
   DevBuf<u32> ridx_[2];
   DevBuf<TreeArrays> tarr_[2];
   DevBuf<u32> ghmax_;  // gradient and hessian maxima of the round, [2][K]
+  // per-block partials of the round-start reductions (gradient maxima when
+  // K <= 64; quantised root sums) and the last-block counters, which every
+  // launch leaves zero
+  DevBuf<u32> max_part_;
+  DevBuf<i64> tot_part_;
+  DevBuf<u32> done_;
   DevBuf<Scales> scales_;
   DevBuf<i64> hist_[2];
   DevBuf<HistTask> hist_tasks_;
@@ -175,6 +179,7 @@ class Engine {
   // 64-feature histogram tasks (k_hist_wide)
   bool wide_ = false;
   u32 hist_tile_ = kHistFeatureTile;
+  u32 hist_target_tasks_ = 4 * 148;  // histogram tasks per level, about
   DevBuf<EvalNode> eval_nodes_;
   DevBuf<SplitCand> cand_;                 // [open][nchunks_] this rank's candidates
   DevBuf<i64> send_;                       // this rank's partial histograms, group-major (G > 1)
@@ -203,6 +208,9 @@ class Engine {
   int sms_ = 148;
   // CUDA graph of a whole round (replayed while the bounds and buffers hold)
   bool graphs_ = true;  // DP_CUDA_GRAPHS=0 turns capture off
+  // The last level adds leaf values while routing rows instead of moving
+  // them (DP_FOLD_LAST_LEVEL=0: moves them and updates margins afterwards).
+  bool fold_last_ = true;
   bool capturing_ = false;
   cudaGraph_t graph_ = nullptr;
   cudaGraphExec_t graph_exec_ = nullptr;
@@ -215,6 +223,14 @@ class Engine {
   u64 async_open_limit_ = u64(1) << 16;
   u64 async_hist_bytes_ = u64(4) << 30;
 
+  // The round's results (counters, node counts, scales, level statistics,
+  // node records), written into pinned host memory by the round's last
+  // kernel; sized and laid out by readback_layout().
+  struct ReadbackLayout {
+    size_t ctr = 0, nid = 0, sc = 0, st = 0, nodes = 0, bytes = 0;
+  };
+  ReadbackLayout readback_layout(u64 ids) const;
+  PinnedBuf<u8> readback_;
   // Pinned staging: the first kArenaHead bytes hold round counters read back
   // mid-round; staged copies start after them.
   static constexpr size_t kArenaHead = 256;

@@ -657,7 +657,7 @@ __global__ void __launch_bounds__(1024) k_hist_wide(HistArgs a) {
 }
 
 template <bool QUANT>
-void launch_hist_wide_variant(const HistArgs& a, cudaStream_t s) {
+void launch_hist_wide_variant(const HistArgs& a, cudaStream_t s, bool counter_zeroed) {
   constexpr int kSmem = int(kPlaneAlignPad) + 256 * kWide * 8;
   static thread_local int configured_device = -1;
   static thread_local int grid_cap = 0;
@@ -675,12 +675,12 @@ void launch_hist_wide_variant(const HistArgs& a, cudaStream_t s) {
     configured_device = dev;
   }
   const u32 grid = (a.ntasks_dev || a.ntasks >= u32(grid_cap)) ? u32(grid_cap) : a.ntasks;
-  DP_CUDA(cudaMemsetAsync(a.counter, 0, sizeof(u32), s));
+  if (!counter_zeroed) DP_CUDA(cudaMemsetAsync(a.counter, 0, sizeof(u32), s));
   k_hist_wide<QUANT><<<grid, 1024, kSmem, s>>>(a);
 }
 
 template <int MB, int THREADS, bool QUANT>
-void launch_hist_variant(const HistArgs& a, cudaStream_t s) {
+void launch_hist_variant(const HistArgs& a, cudaStream_t s, bool counter_zeroed) {
   constexpr int kSmem = hist_smem<MB>();
   static thread_local int configured_device = -1;
   static thread_local int grid_cap = 0;
@@ -699,7 +699,7 @@ void launch_hist_variant(const HistArgs& a, cudaStream_t s) {
     configured_device = dev;
   }
   const u32 grid = (a.ntasks_dev || a.ntasks >= u32(grid_cap)) ? u32(grid_cap) : a.ntasks;
-  DP_CUDA(cudaMemsetAsync(a.counter, 0, sizeof(u32), s));
+  if (!counter_zeroed) DP_CUDA(cudaMemsetAsync(a.counter, 0, sizeof(u32), s));
   k_hist<MB, THREADS, QUANT><<<grid, THREADS, kSmem, s>>>(a);
 }
 
@@ -707,30 +707,31 @@ void launch_hist_variant(const HistArgs& a, cudaStream_t s) {
 
 void launch_histograms(const u8* bins, u64 bin_stride, u32 F, int max_bins, bool quantized_gh,
                        const TreeArrays* trees, const Scales* scales, const HistTask* tasks, u32 ntasks,
-                       u32* counter, i64* hist, cudaStream_t s, const u32* ntasks_dev, const HistLayout* layout) {
+                       u32* counter, i64* hist, cudaStream_t s, const u32* ntasks_dev, const HistLayout* layout,
+                       bool counter_zeroed) {
   if (!ntasks && !ntasks_dev) return;
   const HistLayout lay = layout ? *layout : HistLayout{F, u64(F) * 2 * kMaxBins, 0};
   need(lay.fg > 0, "histogram layout needs a positive feature group size");
   const HistArgs a{bins, bin_stride, F, ntasks, ntasks_dev, trees, scales, tasks, counter, hist, lay};
   if (max_bins <= 64) {
-    if (quantized_gh) launch_hist_variant<64, 512, true>(a, s);
-    else launch_hist_variant<64, 512, false>(a, s);
+    if (quantized_gh) launch_hist_variant<64, 512, true>(a, s, counter_zeroed);
+    else launch_hist_variant<64, 512, false>(a, s, counter_zeroed);
   } else {
-    if (quantized_gh) launch_hist_variant<256, DP_HIST_THREADS, true>(a, s);
-    else launch_hist_variant<256, DP_HIST_THREADS, false>(a, s);
+    if (quantized_gh) launch_hist_variant<256, DP_HIST_THREADS, true>(a, s, counter_zeroed);
+    else launch_hist_variant<256, DP_HIST_THREADS, false>(a, s, counter_zeroed);
   }
   after_launch("histograms");
 }
 
 void launch_histograms_wide(const u8* bins, u64 bin_stride, u32 F, bool quantized_gh, const TreeArrays* trees,
                             const Scales* scales, const HistTask* tasks, u32 ntasks, u32* counter, i64* hist,
-                            cudaStream_t s, const u32* ntasks_dev, const HistLayout* layout) {
+                            cudaStream_t s, const u32* ntasks_dev, const HistLayout* layout, bool counter_zeroed) {
   if (!ntasks && !ntasks_dev) return;
   const HistLayout lay = layout ? *layout : HistLayout{F, u64(F) * 2 * kMaxBins, 0};
   need(lay.fg > 0, "histogram layout needs a positive feature group size");
   const HistArgs a{bins, bin_stride, F, ntasks, ntasks_dev, trees, scales, tasks, counter, hist, lay};
-  if (quantized_gh) launch_hist_wide_variant<true>(a, s);
-  else launch_hist_wide_variant<false>(a, s);
+  if (quantized_gh) launch_hist_wide_variant<true>(a, s, counter_zeroed);
+  else launch_hist_wide_variant<false>(a, s, counter_zeroed);
   after_launch("histograms");
 }
 

@@ -71,13 +71,16 @@ __device__ __forceinline__ NodeRec& node_at(const RoundBuffers& b, u32 tree, u32
   return b.nodes[u64(id) * b.K + tree];
 }
 
-__global__ void k_round_init(RoundBuffers b, u64 R, const i64* __restrict__ totals) {
+// One block: the K roots (open at depth 0, built directly), the counters and
+// the level statistics of a new round.
+__device__ void round_init_block(const RoundBuffers& b, u64 R, const i64* totals, u32 nstats) {
   for (u32 k = threadIdx.x; k < b.K; k += blockDim.x) {
     b.open_cur[k] = OpenRec{k, 0u, k, 0u, 0, i64(R)};
     b.build[k] = k;
     b.next_id[k] = 1u;
     node_at(b, k, 0) = NodeRec{totals[2 * k], totals[2 * k + 1], -1, -1, -1, -1, 0, 0, 0.f, 0.f};
   }
+  for (u32 d = threadIdx.x; d < nstats; d += blockDim.x) b.stats[d] = LevelStats{};
   if (threadIdx.x == 0) {
     RoundCounters c{};
     c.n_open = b.K;
@@ -86,22 +89,102 @@ __global__ void k_round_init(RoundBuffers b, u64 R, const i64* __restrict__ tota
   }
 }
 
-// Histogram tasks of the build list: about four tasks per SM of equal row
+__global__ void k_round_init(RoundBuffers b, u64 R, const i64* __restrict__ totals, u32 nstats) {
+  round_init_block(b, R, totals, nstats);
+}
+
+constexpr int kQuantThreads = 256;
+constexpr u32 kQuantSharedSums = 128;  // classes x 2 reduced through shared memory by the last block
+
+// grid (blocks, K); see launch_quantize_round.
+__global__ void __launch_bounds__(kQuantThreads) k_quantize_round(RoundBuffers b, float2* gh, u64 R,
+                                                                  const Scales* __restrict__ sc, u32* ridx, i64* part,
+                                                                  u32* done, i64* totals, u32 nstats, int init) {
+  const u32 k = blockIdx.y;
+  const Scales s = sc[k];
+  float2* g = gh + u64(k) * R;
+  u32* rk = ridx + u64(k) * R;
+  long long sg = 0, sh = 0;
+  for (u64 i = u64(blockIdx.x) * blockDim.x + threadIdx.x; i < R; i += u64(gridDim.x) * blockDim.x) {
+    const float2 v = g[i];
+    const int2 q = make_int2(quantize(v.x, s.sg), quantize(v.y, s.sh));
+    reinterpret_cast<int2*>(g)[i] = q;
+    rk[i] = u32(i);
+    sg += q.x;
+    sh += q.y;
+  }
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    sg += __shfl_xor_sync(0xffffffffu, sg, o);
+    sh += __shfl_xor_sync(0xffffffffu, sh, o);
+  }
+  __shared__ long long wg[kQuantThreads / 32], wh[kQuantThreads / 32];
+  if (lane == 0) {
+    wg[warp] = sg;
+    wh[warp] = sh;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < kQuantThreads / 32; ++w) {
+      sg += wg[w];
+      sh += wh[w];
+    }
+    // [K][2][blocks]: row 2k + c holds every block's sum of component c
+    part[(2 * u64(k)) * gridDim.x + blockIdx.x] = sg;
+    part[(2 * u64(k) + 1) * gridDim.x + blockIdx.x] = sh;
+  }
+  if (!last_block(done, gridDim.x * gridDim.y)) return;
+  const u32 nk2 = b.K * 2;
+  if (nk2 <= kQuantSharedSums) {
+    __shared__ i64 s_red[(kQuantThreads / 32) * kQuantSharedSums];
+    reduce_rows(part, nk2, gridDim.x, s_red, totals, i64(0), [](i64 x, i64 y) { return x + y; });
+  } else {
+    for (u32 kk = warp; kk < b.K; kk += kQuantThreads / 32) {
+      long long a = 0, c = 0;
+      const i64* pk = part + 2 * u64(kk) * gridDim.x;
+      for (u32 j = lane; j < gridDim.x; j += 32) {
+        a += __ldcg(pk + j);
+        c += __ldcg(pk + gridDim.x + j);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        a += __shfl_xor_sync(0xffffffffu, a, o);
+        c += __shfl_xor_sync(0xffffffffu, c, o);
+      }
+      if (lane == 0) {
+        totals[2 * kk] = a;
+        totals[2 * kk + 1] = c;
+      }
+    }
+  }
+  if (!init) return;
+  __syncthreads();  // the totals this block wrote
+  round_init_block(b, R, totals, nstats);
+}
+
+// Pieces of a node of `count` rows: floor(count / chunk), at least one, so a
+// node below two chunks stays one piece, which alone covers its histogram
+// slot and stores it instead of adding to it (a partial piece's drain, 16384
+// int64 reductions per 32-feature tile, costs about as much as its rows at
+// a few thousand rows).
+__device__ __forceinline__ u64 hist_pieces(i64 count, u64 chunk) {
+  if (count <= 0) return 0;
+  const u64 n = u64(count) / chunk;
+  return n ? n : 1;
+}
+
+// Histogram tasks of the build list: about `target` tasks of equal row
 // counts, the feature tiles of one row range adjacent in the queue so that
 // blocks running at the same time read all sectors of the same rows.
-__global__ void __launch_bounds__(kBook) k_hist_tasks(RoundBuffers b, u32 ftiles, u32 tile, u32 nsm, int depth) {
+__global__ void __launch_bounds__(kBook) k_hist_tasks(RoundBuffers b, u32 ftiles, u32 tile, u32 target, int depth) {
   __shared__ i64 s_begin[kBook], s_count[kBook];
   __shared__ u32 s_slot[kBook], s_tree[kBook];
   const u32 nb = b.ctr->n_build;
+  if (threadIdx.x == 0) *b.hist_counter = 0u;  // the next histogram launch's queue
   u64 rows = 0, total = 0;
   for (u32 i = threadIdx.x; i < nb; i += kBook) rows += u64(b.open_cur[b.build[i]].count);
   scan_block(rows, &total);
-  // About four tasks per SM: finer pieces keep the blocks running at one
-  // time on neighbouring rows (L2 reuse of lines shared by several nodes'
-  // rows); measured on B200 against one task per SM, which halves the
-  // pieces' drains but was 8% slower over a config-4 round and 50% slower
-  // for config 5 with 8 nodes.
-  const u64 target = u64(nsm) * 4;
   u64 chunk = (total * ftiles + target - 1) / target;
   if (chunk < 2048) chunk = 2048;
   u64 base = 0;
@@ -114,11 +197,11 @@ __global__ void __launch_bounds__(kBook) k_hist_tasks(RoundBuffers b, u32 ftiles
       s_count[threadIdx.x] = o.count;
       s_slot[threadIdx.x] = o.slot;
       s_tree[threadIdx.x] = o.tree;
-      pieces = o.count > 0 ? (u64(o.count) + chunk - 1) / chunk : 0;
+      pieces = hist_pieces(o.count, chunk);
     }
     base += expand(pieces * ftiles, base, b.cap_hist_tasks, [&](int j, u64 q, u64 t) {
       const i64 cnt = s_count[j], beg0 = s_begin[j], end0 = beg0 + cnt;
-      const i64 np = (cnt + i64(chunk) - 1) / i64(chunk);
+      const i64 np = i64(hist_pieces(cnt, chunk));
       const i64 piece = (cnt + np - 1) / np;
       const i64 p = i64(q / ftiles);
       const u32 ft = u32(q % ftiles);
@@ -311,9 +394,30 @@ __global__ void k_children(RoundBuffers b, int depth, int max_depth, i64* zero, 
 }
 
 // Leaf values into the node records, then the margin-update tasks (chunks of
-// up to kLeafChunk rows of each leaf segment).
+// up to kLeafChunk rows of each leaf segment).  With split_leaves, the
+// children of this level's splits are leaves as well (the last level, whose
+// rows do not move): their values go into their records and, as f32 bits, to
+// cursors[2 s] (left) and cursors[2 s + 1] (right) of split s.
 __global__ void __launch_bounds__(kBook) k_leaf_values(RoundBuffers b, const Scales* __restrict__ scales,
-                                                       SplitParams p, const u32* ridx0, const u32* ridx1, u64 R) {
+                                                       SplitParams p, const u32* ridx0, const u32* ridx1, u64 R,
+                                                       int split_leaves) {
+  if (split_leaves) {
+    const u32 ns = b.ctr->n_split;
+    for (u32 j = threadIdx.x; j < ns; j += kBook) {
+      const OpenRec o = b.open_cur[b.split_idx[j]];
+      const NodeRec& par = node_at(b, o.tree, o.id);
+      const Scales sc = scales[o.tree];
+      const i32 child[2] = {par.left, par.right};
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        NodeRec& n = node_at(b, o.tree, u32(child[c]));
+        const float v = leaf_weight(n.gq, n.hq, sc.sg, sc.sh, p);
+        n.cond = v;
+        n.feature = 0;
+        b.cursors[2 * j + c] = __float_as_uint(v);
+      }
+    }
+  }
   __shared__ i64 s_begin[kBook], s_end[kBook];
   __shared__ const u32* s_ridx[kBook];
   __shared__ float s_value[kBook];
@@ -420,13 +524,28 @@ int sm_count() {
 
 }  // namespace
 
-void launch_round_init(const RoundBuffers& b, u64 R, const i64* gh_totals, cudaStream_t s) {
-  k_round_init<<<1, 256, 0, s>>>(b, R, gh_totals);
+void launch_round_init(const RoundBuffers& b, u64 R, const i64* gh_totals, u32 nstats, cudaStream_t s) {
+  k_round_init<<<1, 256, 0, s>>>(b, R, gh_totals, nstats);
   after_launch("round_init");
 }
 
-void launch_hist_tasks(const RoundBuffers& b, u32 ftiles, u32 tile, int depth, cudaStream_t s) {
-  k_hist_tasks<<<1, kBook, 0, s>>>(b, ftiles, tile, u32(sm_count()), depth);
+u32 quantize_round_blocks(u64 R, int K) {
+  const u64 cap = (u64(sm_count()) * 8 + u64(K) - 1) / u64(K);  // about eight blocks per SM in all
+  const u64 want = (R + kQuantThreads - 1) / kQuantThreads;
+  const u64 n = want < cap ? want : cap;
+  return u32(n ? n : 1);
+}
+
+void launch_quantize_round(const RoundBuffers& b, float2* gh, u64 R, const Scales* scales, u32* ridx, i64* part,
+                           u32* done, i64* totals, u32 nstats, bool init, cudaStream_t s) {
+  need(b.K <= 65535u, "internal error: class count exceeds the grid");
+  const dim3 grid(quantize_round_blocks(R, int(b.K)), b.K);
+  k_quantize_round<<<grid, kQuantThreads, 0, s>>>(b, gh, R, scales, ridx, part, done, totals, nstats, init ? 1 : 0);
+  after_launch("quantize_round");
+}
+
+void launch_hist_tasks(const RoundBuffers& b, u32 ftiles, u32 tile, int depth, u32 target_tasks, cudaStream_t s) {
+  k_hist_tasks<<<1, kBook, 0, s>>>(b, ftiles, tile, target_tasks ? target_tasks : 1u, depth);
   after_launch("hist_tasks");
 }
 
@@ -448,8 +567,8 @@ void launch_children(const RoundBuffers& b, int depth, int max_depth, cudaStream
 }
 
 void launch_leaf_values(const RoundBuffers& b, const Scales* scales, SplitParams p, u32* const ridx_sets[2], u64 R,
-                        cudaStream_t s) {
-  k_leaf_values<<<1, kBook, 0, s>>>(b, scales, p, ridx_sets[0], ridx_sets[1], R);
+                        cudaStream_t s, bool split_leaves) {
+  k_leaf_values<<<1, kBook, 0, s>>>(b, scales, p, ridx_sets[0], ridx_sets[1], R, split_leaves ? 1 : 0);
   after_launch("leaf_values");
 }
 

@@ -14,7 +14,7 @@ namespace dp {
 
 namespace {
 
-constexpr int kSharedClasses = 64;
+constexpr int kSharedClasses = kMaxReducedClasses;
 
 __device__ __forceinline__ u32 warp_max(u32 b) {
 #pragma unroll
@@ -24,11 +24,15 @@ __device__ __forceinline__ u32 warp_max(u32 b) {
 
 // Maxima of |g| and h per class (float bits compare as unsigned for
 // non-negative values): per-thread registers for one class, per-block shared
-// counters for up to kSharedClasses classes, then one global atomic per
-// block and class.
+// counters for up to kSharedClasses classes, then either one global atomic
+// per block and class (gmax / hmax zeroed before), or (part set) per-block
+// maxima part[block][2K] that the last block to finish reduces into gmax /
+// hmax and, with scales_out, into the scales; that block also returns *done
+// to zero, so nothing has to be zeroed before the next launch.
 __global__ void __launch_bounds__(256) k_gradients(int objective, int K, const float* __restrict__ margin,
                                                     const float* __restrict__ label, u64 R, float2* __restrict__ gh,
-                                                    u32* gmax, u32* hmax, RowSample rs) {
+                                                    u32* gmax, u32* hmax, RowSample rs, u32* part, u32* done,
+                                                    Scales* scales_out) {
   __shared__ u32 smg[kSharedClasses], smh[kSharedClasses];
   const bool sampling = rs.rate < 1.0;
   const u32 round = sampling ? *rs.round : 0u;
@@ -92,11 +96,36 @@ __global__ void __launch_bounds__(256) k_gradients(int objective, int K, const f
     if ((threadIdx.x & 31) == 0) { atomicMax(smg, lg); atomicMax(smh, lh); }
   }
   __syncthreads();
-  if (shared_max)
-    for (int k = threadIdx.x; k < K; k += blockDim.x) {
-      if (smg[k]) atomicMax(gmax + k, smg[k]);
-      if (smh[k]) atomicMax(hmax + k, smh[k]);
+  if (!part) {
+    if (shared_max)
+      for (int k = threadIdx.x; k < K; k += blockDim.x) {
+        if (smg[k]) atomicMax(gmax + k, smg[k]);
+        if (smh[k]) atomicMax(hmax + k, smh[k]);
+      }
+    return;
+  }
+  // per-block maxima ([2K][blocks]), then the last block reduces them
+  for (int k = threadIdx.x; k < K; k += blockDim.x) {
+    part[u64(k) * gridDim.x + blockIdx.x] = smg[k];
+    part[u64(K + k) * gridDim.x + blockIdx.x] = smh[k];
+  }
+  if (!last_block(done, gridDim.x)) return;
+  __shared__ u32 s_red[8 * 2 * kSharedClasses];
+  __shared__ u32 s_max[2 * kSharedClasses];
+  reduce_rows(part, u32(2 * K), gridDim.x, s_red, s_max, 0u, [](u32 x, u32 y) { return x > y ? x : y; });
+  for (int k = threadIdx.x; k < K; k += blockDim.x) {
+    smg[k] = s_max[k];
+    smh[k] = s_max[K + k];
+  }
+  __syncthreads();
+  for (int k = threadIdx.x; k < K; k += blockDim.x) {
+    gmax[k] = smg[k];
+    hmax[k] = smh[k];
+    if (scales_out) {
+      scales_out[k].sg = quant_scale(__uint_as_float(smg[k]), kGradBits);
+      scales_out[k].sh = quant_scale(__uint_as_float(smh[k]), kHessBits);
     }
+  }
 }
 
 __global__ void __launch_bounds__(256) k_quantize_gh(float2* gh, u64 R, int K, const Scales* __restrict__ sc) {
@@ -105,38 +134,6 @@ __global__ void __launch_bounds__(256) k_quantize_gh(float2* gh, u64 R, int K, c
     const Scales s = sc[i / R];
     const float2 v = gh[i];
     reinterpret_cast<int2*>(gh)[i] = make_int2(quantize(v.x, s.sg), quantize(v.y, s.sh));
-  }
-}
-
-// grid (blocks, K): block sums of tree k's int32 pairs, one atomic per block.
-__global__ void __launch_bounds__(256) k_gh_totals(const int2* __restrict__ gh, u64 R, i64* __restrict__ totals) {
-  const u32 k = blockIdx.y;
-  const int2* g = gh + u64(k) * R;
-  long long sg = 0, sh = 0;
-  for (u64 i = u64(blockIdx.x) * blockDim.x + threadIdx.x; i < R; i += u64(gridDim.x) * blockDim.x) {
-    const int2 v = g[i];
-    sg += v.x;
-    sh += v.y;
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    sg += __shfl_xor_sync(0xffffffffu, sg, o);
-    sh += __shfl_xor_sync(0xffffffffu, sh, o);
-  }
-  __shared__ long long wg[8], wh[8];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  if (lane == 0) {
-    wg[warp] = sg;
-    wh[warp] = sh;
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    for (int w = 1; w < 8; ++w) {
-      sg += wg[w];
-      sh += wh[w];
-    }
-    atomicAdd(reinterpret_cast<unsigned long long*>(totals + 2 * k), static_cast<unsigned long long>(sg));
-    atomicAdd(reinterpret_cast<unsigned long long*>(totals + 2 * k + 1), static_cast<unsigned long long>(sh));
   }
 }
 
@@ -178,10 +175,6 @@ __global__ void k_init_margins(float* __restrict__ margin, u64 n, int K, const f
     margin[i] = base[i % u64(K)];
 }
 
-__global__ void k_iota(u32* p, u64 n) {
-  for (u64 i = u64(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += u64(gridDim.x) * blockDim.x) p[i] = u32(i);
-}
-
 __global__ void k_check_finite(const float* __restrict__ x, u64 R, u32 F, u64 stride, u32* bad) {
   const u64 n = R * F;
   bool any = false;
@@ -203,6 +196,19 @@ __global__ void k_check_labels(const float* __restrict__ y, u64 R, int objective
   if (__any_sync(0xffffffffu, any) && (threadIdx.x & 31) == 0) atomicOr(bad, 1u);
 }
 
+constexpr int kCopySegs = 6;
+struct CopySegs {
+  const u32* src[kCopySegs];
+  u32* dst[kCopySegs];
+  u64 words[kCopySegs];
+};
+
+__global__ void __launch_bounds__(256) k_copy_words(CopySegs c) {
+  const u64 step = u64(gridDim.x) * blockDim.x;
+  for (int j = 0; j < kCopySegs; ++j)
+    for (u64 i = u64(blockIdx.x) * blockDim.x + threadIdx.x; i < c.words[j]; i += step) c.dst[j][i] = c.src[j][i];
+}
+
 int grid_for(u64 n, int block) {
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
@@ -218,7 +224,35 @@ void launch_gradients(int objective, int K, const float* margin, const float* la
                       u32* gmax_bits, u32* hmax_bits, cudaStream_t s, const RowSample& rs) {
   if (R == 0) return;
   need(rs.rate >= 1.0 || rs.round != nullptr, "row sampling needs the round counter");
-  k_gradients<<<grid_for(R, 256), 256, 0, s>>>(objective, K, margin, label, R, gh, gmax_bits, hmax_bits, rs);
+  k_gradients<<<grid_for(R, 256), 256, 0, s>>>(objective, K, margin, label, R, gh, gmax_bits, hmax_bits, rs,
+                                                nullptr, nullptr, nullptr);
+  after_launch("gradients");
+}
+
+u32 gradient_blocks(u64 R) { return u32(grid_for(R, 256)); }
+
+void launch_copy_words(const u32* const* src, u32* const* dst, const u64* words, int n, cudaStream_t s) {
+  need(n >= 1 && n <= kCopySegs, "internal error: copy segment count");
+  CopySegs c{};
+  u64 most = 0;
+  for (int j = 0; j < n; ++j) {
+    c.src[j] = src[j];
+    c.dst[j] = dst[j];
+    c.words[j] = words[j];
+    most = words[j] > most ? words[j] : most;
+  }
+  k_copy_words<<<grid_for(most, 256), 256, 0, s>>>(c);
+  after_launch("copy_words");
+}
+
+void launch_gradients_reduced(int objective, int K, const float* margin, const float* label, u64 R, float2* gh,
+                              u32* gmax_bits, u32* hmax_bits, u32* part, u32* done, Scales* scales, cudaStream_t s,
+                              const RowSample& rs) {
+  need(K <= kSharedClasses, "internal error: per-block gradient maxima hold at most 64 classes");
+  need(rs.rate >= 1.0 || rs.round != nullptr, "row sampling needs the round counter");
+  // one block at least (R == 0 included), so the maxima are always written
+  k_gradients<<<grid_for(R, 256), 256, 0, s>>>(objective, K, margin, label, R, gh, gmax_bits, hmax_bits, rs, part,
+                                                done, scales);
   after_launch("gradients");
 }
 
@@ -231,13 +265,6 @@ void launch_quantize_gh(float2* gh, u64 R, int K, const Scales* scales, cudaStre
   if (!R) return;
   k_quantize_gh<<<grid_for(R * u64(K), 256), 256, 0, s>>>(gh, R, K, scales);
   after_launch("quantize_gh");
-}
-
-void launch_gh_totals(const float2* gh_quantized, u64 R, int K, i64* totals, cudaStream_t s) {
-  if (!R) return;
-  const dim3 grid(grid_for(R, 256), unsigned(K));
-  k_gh_totals<<<grid, 256, 0, s>>>(reinterpret_cast<const int2*>(gh_quantized), R, totals);
-  after_launch("gh_totals");
 }
 
 void launch_leaf_update(const LeafTask* tasks, u32 ntasks, float* margin, u32 K, cudaStream_t s) {
@@ -259,12 +286,6 @@ void launch_init_margins(float* margin, u64 R, int K, const float* base, cudaStr
   if (!n) return;
   k_init_margins<<<grid_for(n, 256), 256, 0, s>>>(margin, n, K, base);
   after_launch("init_margins");
-}
-
-void launch_iota(u32* p, u64 n, cudaStream_t s) {
-  if (!n) return;
-  k_iota<<<grid_for(n, 256), 256, 0, s>>>(p, n);
-  after_launch("iota");
 }
 
 void launch_check_finite(const float* x, u64 R, u32 F, u64 stride, u32* bad, cudaStream_t s) {

@@ -144,7 +144,61 @@ __global__ void __launch_bounds__(kPartThreads) k_partition_dev(const u8* __rest
     partition_task(t, bins_blk, blk_stride, src, dst, nodes, tasks, cursors);
 }
 
+// The last level of a tree: nothing is built from the children, so rows do
+// not move; each row of a split node adds its child's leaf value (vals, f32
+// bits [2 node + side]) to its margin, the same float addition the margin
+// update makes.
+__global__ void __launch_bounds__(kPartThreads) k_partition_leaves(const u8* __restrict__ bins_blk, u64 blk_stride,
+                                                                   const TreeArrays* __restrict__ src,
+                                                                   const PartNode* __restrict__ nodes,
+                                                                   const PartTask* __restrict__ tasks,
+                                                                   const u32* __restrict__ ntasks,
+                                                                   const u32* __restrict__ vals, float* margin, u32 K) {
+  const u32 n = *ntasks;
+  for (u32 task = blockIdx.x; task < n; task += gridDim.x) {
+    const PartTask t = tasks[task];
+    const PartNode nd = nodes[t.node];
+    const u32* ridx = src[nd.tree].ridx + t.begin;
+    const float vl = __uint_as_float(vals[2 * t.node]), vr = __uint_as_float(vals[2 * t.node + 1]);
+    const u8* col = bins_blk + u64(nd.feature) * 32;
+    const u32 cnt = u32(t.end - t.begin);
+    for (u32 base = 0; base < cnt; base += kPartThreads * kIlp) {
+      u32 r[kIlp];
+#pragma unroll
+      for (int u = 0; u < kIlp; ++u) {
+        const u32 i = base + u * kPartThreads + threadIdx.x;
+        r[u] = i < cnt ? __ldg(ridx + i) : 0xffffffffu;
+      }
+      u8 b[kIlp];
+      float m[kIlp];
+#pragma unroll
+      for (int u = 0; u < kIlp; ++u) {
+        b[u] = 0;
+        m[u] = 0.f;
+        if (r[u] != 0xffffffffu) {
+          b[u] = __ldg(col + u64(r[u] >> 5) * blk_stride + (r[u] & 31u));
+          m[u] = margin[u64(r[u]) * K + nd.tree];
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kIlp; ++u)
+        if (r[u] != 0xffffffffu) margin[u64(r[u]) * K + nd.tree] = m[u] + (goes_left(b[u], nd) ? vl : vr);
+    }
+  }
+}
+
 }  // namespace
+
+void launch_partition_leaves(const u8* bins_blk, u64 blk_stride, const TreeArrays* src, const PartNode* nodes,
+                             const PartTask* tasks, const u32* ntasks_dev, const u32* vals, float* margin, u32 K,
+                             cudaStream_t s) {
+  int dev = 0, sms = 148;
+  DP_CUDA(cudaGetDevice(&dev));
+  DP_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  k_partition_leaves<<<sms * 8, kPartThreads, 0, s>>>(bins_blk, blk_stride, src, nodes, tasks, ntasks_dev, vals,
+                                                       margin, K);
+  after_launch("partition_leaves");
+}
 
 void launch_partition(const u8* bins_blk, u64 blk_stride, const TreeArrays* src, const TreeArrays* dst,
                       const PartNode* nodes, const PartTask* tasks, u32 ntasks, u32* cursors, cudaStream_t s) {

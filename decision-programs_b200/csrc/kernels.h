@@ -57,6 +57,56 @@ struct EvalNode {
   u32 small;  // slot of the built sibling
 };
 
+#ifdef __CUDACC__
+// Last-block pattern: every thread of a launch calls it once, after its
+// block's writes that the last block reads.  True in the block that finishes
+// last (the other blocks' writes are then visible to it through L2: read them
+// with __ldcg); that block also returns *done to zero for the next launch.
+__device__ __forceinline__ bool last_block(u32* done, u32 nblocks) {
+  __shared__ bool s_last;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0 && threadIdx.y == 0) {
+    s_last = atomicAdd(done, 1u) + 1u == nblocks;
+    if (s_last) atomicExch(done, 0u);  // every block has counted
+  }
+  __syncthreads();
+  if (s_last) __threadfence();
+  return s_last;
+}
+
+// Reduction by one whole block of M rows of n values each (row r at
+// src[r * n], written by other blocks: read through L2) into out[r]: warp w
+// takes columns [w n / W, (w + 1) n / W) of every row, with independent
+// loads, then one thread per row combines the W warps' results.  sh holds
+// W * M values (shared memory).
+template <class T, class Op>
+__device__ void reduce_rows(const T* src, u32 M, u32 n, T* sh, T* out, T init, Op op) {
+  const u32 W = blockDim.x >> 5, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const u32 c0 = u32(u64(n) * warp / W), c1 = u32(u64(n) * (warp + 1) / W);
+  for (u32 r = 0; r < M; ++r) {
+    const T* row = src + u64(r) * n;
+    T acc = init;
+    u32 c = c0 + lane;
+    for (; c + 96 < c1; c += 128) {
+      const T a = __ldcg(row + c), b = __ldcg(row + c + 32), d = __ldcg(row + c + 64), e = __ldcg(row + c + 96);
+      acc = op(acc, op(op(a, b), op(d, e)));
+    }
+    for (; c < c1; c += 32) acc = op(acc, __ldcg(row + c));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc = op(acc, __shfl_xor_sync(0xffffffffu, acc, o));
+    if (lane == 0) sh[warp * M + r] = acc;
+  }
+  __syncthreads();
+  for (u32 r = threadIdx.x; r < M; r += blockDim.x) {
+    T acc = init;
+    for (u32 w = 0; w < W; ++w) acc = op(acc, sh[w * M + r]);
+    out[r] = acc;
+  }
+  __syncthreads();
+}
+#endif
+
 // ---- binning (quantile cuts by exact radix selection) ---------------------
 struct CutState;  // defined in k_quantile.cu
 struct CutsDevice {
@@ -84,14 +134,28 @@ void launch_gradients(int objective, int K, const float* margin, const float* la
                       u32* gmax_bits, u32* hmax_bits, cudaStream_t s, const RowSample& rs = RowSample());
 // scales[k] from the maxima.
 void launch_scales(int K, const u32* gmax_bits, const u32* hmax_bits, Scales* scales, cudaStream_t s);
+// The same gradients for K <= 64 without atomics on zeroed maxima: each block
+// writes its maxima to part ([2K][gradient_blocks(R)] u32), and the last
+// block reduces them into gmax / hmax and, with scales set, computes the
+// scales (launch_scales' formula).  *done must be zero at the first launch;
+// every launch leaves it zero.  Launches one block even for R == 0.
+constexpr int kMaxReducedClasses = 64;
+u32 gradient_blocks(u64 R);
+void launch_gradients_reduced(int objective, int K, const float* margin, const float* label, u64 R, float2* gh,
+                              u32* gmax_bits, u32* hmax_bits, u32* part, u32* done, Scales* scales, cudaStream_t s,
+                              const RowSample& rs = RowSample{});
+// Copies n segments of 32-bit words (src[i] -> dst[i], words[i] each) in one
+// launch; dst may be pinned host memory (its device address).
+void launch_copy_words(const u32* const* src, u32* const* dst, const u64* words, int n, cudaStream_t s);
 
 // ---- histograms -------------------------------------------------------------
 // hist[slot][F][256][2] (int64) must be zeroed for every slot the tasks touch.
 // Every bin value must be < max_bins (<= 64 selects a smaller tile).  With
 // quantized_gh the (g, h) arrays hold int32 pairs (see launch_quantize_gh);
 // otherwise fp32 pairs quantised with `scales`.  `counter` is one u32 of
-// device scratch (the task queue), reset by the launcher.  Positions must be
-// below 2^31.
+// device scratch (the task queue), reset by the launcher unless
+// counter_zeroed says a kernel before it on the stream zeroed it.  Positions
+// must be below 2^31.
 // With ntasks_dev set, the task count is read from device memory (ntasks is
 // then ignored) and the grid covers every SM.
 // Output layout (element offsets; a cell is the (g, h) pair of one bin):
@@ -108,7 +172,7 @@ struct HistLayout {
 void launch_histograms(const u8* bins, u64 bin_stride, u32 F, int max_bins, bool quantized_gh,
                        const TreeArrays* trees, const Scales* scales, const HistTask* tasks, u32 ntasks,
                        u32* counter, i64* hist, cudaStream_t s, const u32* ntasks_dev = nullptr,
-                       const HistLayout* layout = nullptr);
+                       const HistLayout* layout = nullptr, bool counter_zeroed = false);
 constexpr u32 kHistFeatureTile = 32;
 // The 256-bin build over 64-feature tasks (HistTask.f0 a multiple of 64):
 // same inputs and output as launch_histograms; one block per SM, each using
@@ -116,16 +180,13 @@ constexpr u32 kHistFeatureTile = 32;
 constexpr u32 kHistWideTile = 64;
 void launch_histograms_wide(const u8* bins, u64 bin_stride, u32 F, bool quantized_gh, const TreeArrays* trees,
                             const Scales* scales, const HistTask* tasks, u32 ntasks, u32* counter, i64* hist,
-                            cudaStream_t s, const u32* ntasks_dev, const HistLayout* layout);
+                            cudaStream_t s, const u32* ntasks_dev, const HistLayout* layout,
+                            bool counter_zeroed = false);
 // Rows per histogram task for a launch over `total_rows` row-tiles (about
 // four tasks per SM; tasks tasks of one node and tile stay contiguous).
 u64 hist_chunk_rows(u64 total_rows);
 // gh[k][r] (fp32 pairs) -> int32 pairs rint(g * s_g), rint(h * s_h), in place.
 void launch_quantize_gh(float2* gh, u64 R, int K, const Scales* scales, cudaStream_t s);
-// totals[2k], totals[2k+1] += sums of the quantised g and h of tree k (int32
-// pairs from launch_quantize_gh); totals must be zeroed.  Every row falls in
-// exactly one bin of every feature, so these are each root histogram's sums.
-void launch_gh_totals(const float2* gh_quantized, u64 R, int K, i64* totals, cudaStream_t s);
 
 // ---- split evaluation --------------------------------------------------------
 // Per (node, feature chunk) candidate into cand[node][chunk]; then the best per
@@ -193,6 +254,12 @@ void launch_partition_dev(const u8* bins_blk, u64 blk_stride, const TreeArrays* 
                           cudaStream_t s);
 
 // ---- leaves -------------------------------------------------------------------
+// The last level's split nodes: each row of the tasks adds vals[2 node] (left)
+// or vals[2 node + 1] (right), f32 bits, to margin[row * K + tree]; rows do
+// not move.
+void launch_partition_leaves(const u8* bins_blk, u64 blk_stride, const TreeArrays* src, const PartNode* nodes,
+                             const PartTask* tasks, const u32* ntasks_dev, const u32* vals, float* margin, u32 K,
+                             cudaStream_t s);
 struct LeafTask {
   const u32* ridx;
   i64 begin, end;
@@ -203,7 +270,6 @@ void launch_leaf_update(const LeafTask* tasks, u32 ntasks, float* margin, u32 K,
 void launch_leaf_update_dev(const LeafTask* tasks, const u32* ntasks_dev, float* margin, u32 K, cudaStream_t s);
 
 // ---- misc ---------------------------------------------------------------------
-void launch_iota(u32* p, u64 n, cudaStream_t s);
 // margin[r][k] = base[k] for r < R.
 void launch_init_margins(float* margin, u64 R, int K, const float* base, cudaStream_t s);
 // Flags (atomicOr into bad[0]) any +-inf in x[r*stride + f].

@@ -75,6 +75,7 @@ struct RoundBuffers {
   LeafTask* leaf_tasks;    // [cap_leaf_tasks]
   RoundCounters* ctr;
   LevelStats* stats;       // [max_depth + 1]
+  u32* hist_counter;       // the histogram kernel's task queue; zeroed by k_hist_tasks
   u32 K, maxn;
   // Which child of a split is built directly (the other is parent minus it):
   // the one with fewer rows, or, when rows are sharded (by_hess), the one
@@ -85,13 +86,23 @@ struct RoundBuffers {
 };
 
 // Roots of the K trees; their totals come from gh_totals ([K][2], summed over
-// all ranks).
-void launch_round_init(const RoundBuffers& b, u64 R, const i64* gh_totals, cudaStream_t s);
+// all ranks).  Also zeroes the nstats level statistics.
+void launch_round_init(const RoundBuffers& b, u64 R, const i64* gh_totals, u32 nstats, cudaStream_t s);
+// Round start after the scales: tree k's (g, h) become int32 pairs
+// (launch_quantize_gh), its row indices 0..R-1, and the quantised sums go to
+// totals ([K][2]); with init set (one rank: no exchange of the totals) the
+// launch then also does launch_round_init's work.  part holds
+// quantize_round_blocks(R, K) * K * 2 int64; *done is zero at the first
+// launch and every launch leaves it zero.
+u32 quantize_round_blocks(u64 R, int K);
+void launch_quantize_round(const RoundBuffers& b, float2* gh, u64 R, const Scales* scales, u32* ridx, i64* part,
+                           u32* done, i64* totals, u32 nstats, bool init, cudaStream_t s);
 // Histogram tasks of the build list, and the split-evaluation inputs of every
 // open node.
 // `tile` features per task (32, or 64 for the wide histogram kernel); ftiles
-// tasks per row range.
-void launch_hist_tasks(const RoundBuffers& b, u32 ftiles, u32 tile, int depth, cudaStream_t s);
+// tasks per row range; rows split into pieces of equal size for about
+// target_tasks tasks in all (2048 rows at least).
+void launch_hist_tasks(const RoundBuffers& b, u32 ftiles, u32 tile, int depth, u32 target_tasks, cudaStream_t s);
 // Zeroes max(device n_build, min_slots) histogram slots.
 void launch_zero_slots(const RoundBuffers& b, i64* hist, u64 slot_elems, u64 min_slots, cudaStream_t s);
 // Splits (depth < max_depth, gain > 0) or closes every open node.
@@ -113,8 +124,10 @@ void launch_feature_masks(const RoundBuffers& b, u32 F, long long seed, const u3
 // *round_dev += 1 (the end of a round).
 void launch_bump_round(u32* round_dev, cudaStream_t s);
 // ridx_sets[s] is the base of the K per-tree row-index arrays of set s
-// (tree k at + k * R).
+// (tree k at + k * R).  With split_leaves, also the leaf values of the
+// children of this level's splits: into their node records and, as f32 bits,
+// into cursors[2 s], cursors[2 s + 1] for launch_partition_leaves.
 void launch_leaf_values(const RoundBuffers& b, const Scales* scales, SplitParams p, u32* const ridx_sets[2], u64 R,
-                        cudaStream_t s);
+                        cudaStream_t s, bool split_leaves = false);
 
 }  // namespace dp
