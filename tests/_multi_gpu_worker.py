@@ -31,6 +31,12 @@ def data(case: str):
         x[rng.random((R, F)) < 0.1] = np.nan
         y = (np.nan_to_num(x[:, 0]) + 0.5 * np.nan_to_num(x[:, 1]) > 0).astype(np.float32)
         return x, y, {"objective": "binary:logistic", "max_depth": 6}
+    if case == "wide":
+        # 100 features: two 64-feature histogram tiles, each spanning both
+        # ranks' feature groups
+        x = rng.standard_normal((R, 100)).astype(np.float32)
+        y = (x[:, 3] * x[:, 70] + np.sin(x[:, 99]) + 0.1 * rng.standard_normal(R)).astype(np.float32)
+        return x, y, {"objective": "reg:squarederror", "max_depth": 6}
     if case == "softprob":
         y = np.argmax(x[:, :4] + 0.3 * rng.standard_normal((R, 4)), 1).astype(np.float32)
         return x, y, {"objective": "multi:softprob", "num_class": 4, "max_depth": 5}

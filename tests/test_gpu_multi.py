@@ -26,7 +26,7 @@ def free_port() -> int:
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs at least two GPUs")
 @pytest.mark.parametrize("case,K", [("squared", 1), ("logistic_nan", 1), ("softprob", 4), ("deep_exact_host", 1),
-                                    ("sampled", 1)])
+                                    ("sampled", 1), ("wide", 1)])
 def test_sharded_ranks_match_the_oracle(orc, tmp_path, case, K):
     import _multi_gpu_worker as w
     world = min(torch.cuda.device_count(), 4)
@@ -35,6 +35,8 @@ def test_sharded_ranks_match_the_oracle(orc, tmp_path, case, K):
     if case == "deep_exact_host":
         # host matrices; levels past 3 open nodes read exact counts back first
         env.update(DP_ASYNC_OPEN_LIMIT="3", DP_ASYNC_HIST_BYTES=str(8 * 24 * 256 * 16))
+    if case == "wide":
+        env.update(DP_HIST_WIDE="1")  # the 64-feature histogram kernel with sharded rows
     cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            f"--nproc-per-node={world}", "--master-addr=127.0.0.1", f"--master-port={free_port()}",
            str(ROOT / "tests" / "_multi_gpu_worker.py"), case, str(tmp_path), str(rounds)]
