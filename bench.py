@@ -740,7 +740,12 @@ def main() -> None:
                   "frac": (sent / (ex["ms"] / 1e3) / 1e9 / peak) if ex["ms"] and peak else 0.0,
                   "note": "exchange time includes waiting for the slowest rank's histogram"}
     hist_pairs_per_s = hist.get("units", 0.0) / (hist["ms"] / 1e3) if hist["ms"] else 0.0
-    atomic_roofline = {"kernel": "k_hist", "unit": "(row, feature) pairs/s", "achieved": hist_pairs_per_s,
+    # the library's choice: 64-feature tasks on one GPU above 64 features
+    # (DP_HIST_WIDE overrides), 32-feature tasks otherwise
+    wide_env = os.environ.get("DP_HIST_WIDE", "")
+    hist_kernel = "k_hist_wide" if (wide_env == "1" or (wide_env != "0" and world == 1 and FEATURES > 64)) \
+        else "k_hist"
+    atomic_roofline = {"kernel": hist_kernel, "unit": "(row, feature) pairs/s", "achieved": hist_pairs_per_s,
                        "ceiling": ceiling.value, "frac": hist_pairs_per_s / ceiling.value if ceiling.value else 0.0,
                        "ceiling_source": "dp_probe_hist_atomics: the kernel's shared-memory update loop alone "
                                          "(two 32-bit atomics per pair, one 1024-thread block per SM), "
@@ -799,7 +804,7 @@ def main() -> None:
                    "l2": "inputs (1.28 GB bins) exceed L2"},
         "e2e": e2e,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak_gbs, "unit": "GB/s",
-                     "frac": achieved / peak_gbs, "traffic": traffic, "kernel": "k_hist",
+                     "frac": achieved / peak_gbs, "traffic": traffic, "kernel": hist_kernel,
                      "peak_source": "measured" if not peaks.get("fallback") else "fallback",
                      "launches": hist["launches"], "ms_per_launch": hist_ms_per_launch},
         "rows_features_per_s": value * FEATURES,
