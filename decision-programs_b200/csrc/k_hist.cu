@@ -247,18 +247,27 @@ __global__ void __launch_bounds__(THREADS, THREADS <= 512 ? 2 : 1) k_hist(HistAr
       __syncthreads();
       // consecutive threads take consecutive bins of one feature
       i64* out = a.hist + u64(key_slot) * a.layout.slot_stride;
-      for (int idx = threadIdx.x; idx < kCells; idx += THREADS) {
-        const int f = idx / MB, b = idx % MB;
-        const long long gs = Wg[f * kWRow + b], hs = Wh[f * kWRow + b];
-        const u32 gf = key_f0 + u32(f);
-        if (gf >= a.F) continue;
-        const u32 grp = gf / a.layout.fg, fl = gf - grp * a.layout.fg;
-        i64* cell = out + grp * a.layout.group_stride + (u64(fl) * kMaxBins + b) * 2;
-        if (key_excl) {
-          *reinterpret_cast<longlong2*>(cell) = make_longlong2(gs, hs);
-        } else if (gs | hs) {
-          atomicAdd(reinterpret_cast<unsigned long long*>(cell), static_cast<unsigned long long>(gs));
-          atomicAdd(reinterpret_cast<unsigned long long*>(cell) + 1, static_cast<unsigned long long>(hs));
+      if (key_excl) {
+        for (int idx = threadIdx.x; idx < kCells; idx += THREADS) {
+          const int f = idx / MB, b = idx % MB;
+          const u32 gf = key_f0 + u32(f);
+          if (gf >= a.F) continue;
+          const u32 grp = gf / a.layout.fg, fl = gf - grp * a.layout.fg;
+          i64* cell = out + grp * a.layout.group_stride + (u64(fl) * kMaxBins + b) * 2;
+          *reinterpret_cast<longlong2*>(cell) = make_longlong2(Wg[f * kWRow + b], Wh[f * kWRow + b]);
+        }
+      } else {
+        // g and h of a cell on neighbouring lanes: a warp's 32 reductions
+        // cover 16 whole cells, eight 32-byte sectors
+        for (int idx = threadIdx.x; idx < 2 * kCells; idx += THREADS) {
+          const int c = idx >> 1, comp = idx & 1;
+          const int f = c / MB, b = c % MB;
+          const u32 gf = key_f0 + u32(f);
+          if (gf >= a.F) continue;
+          const long long v = comp ? Wh[f * kWRow + b] : Wg[f * kWRow + b];
+          const u32 grp = gf / a.layout.fg, fl = gf - grp * a.layout.fg;
+          i64* cell = out + grp * a.layout.group_stride + (u64(fl) * kMaxBins + b) * 2 + comp;
+          if (v) atomicAdd(reinterpret_cast<unsigned long long*>(cell), static_cast<unsigned long long>(v));
         }
       }
       t_clean = true;
@@ -292,18 +301,28 @@ __global__ void __launch_bounds__(THREADS, THREADS <= 512 ? 2 : 1) k_hist(HistAr
       // (slot, tile) stores every cell (16-byte stores, no read of the line);
       // otherwise non-zero cells are added with 64-bit reductions.
       i64* out = a.hist + u64(key_slot) * a.layout.slot_stride;
-      for (int idx = threadIdx.x; idx < kCells; idx += THREADS) {
-        const u32 f = u32(idx) / u32(MB), b = u32(idx) % u32(MB);
-        const u32 gf = key_f0 + f;
-        if (gf >= a.F) continue;
-        const longlong2 v = T[f * u32(MB) + (b ^ f)];
-        const u32 grp = gf / a.layout.fg, fl = gf - grp * a.layout.fg;
-        i64* cell = out + grp * a.layout.group_stride + (u64(fl) * kMaxBins + b) * 2;
-        if (key_excl) {
-          *reinterpret_cast<longlong2*>(cell) = v;
-        } else if (v.x | v.y) {
-          atomicAdd(reinterpret_cast<unsigned long long*>(cell), static_cast<unsigned long long>(v.x));
-          atomicAdd(reinterpret_cast<unsigned long long*>(cell) + 1, static_cast<unsigned long long>(v.y));
+      if (key_excl) {
+        for (int idx = threadIdx.x; idx < kCells; idx += THREADS) {
+          const u32 f = u32(idx) / u32(MB), b = u32(idx) % u32(MB);
+          const u32 gf = key_f0 + f;
+          if (gf >= a.F) continue;
+          const u32 grp = gf / a.layout.fg, fl = gf - grp * a.layout.fg;
+          i64* cell = out + grp * a.layout.group_stride + (u64(fl) * kMaxBins + b) * 2;
+          *reinterpret_cast<longlong2*>(cell) = T[f * u32(MB) + (b ^ f)];
+        }
+      } else {
+        // g and h of a cell on neighbouring lanes: a warp's 32 reductions
+        // cover 16 whole cells, eight 32-byte sectors
+        const long long* T64 = reinterpret_cast<const long long*>(T);
+        for (int idx = threadIdx.x; idx < 2 * kCells; idx += THREADS) {
+          const u32 c = u32(idx) >> 1, comp = u32(idx) & 1u;
+          const u32 f = c / u32(MB), b = c % u32(MB);
+          const u32 gf = key_f0 + f;
+          if (gf >= a.F) continue;
+          const long long v = T64[2u * (f * u32(MB) + (b ^ f)) + comp];
+          const u32 grp = gf / a.layout.fg, fl = gf - grp * a.layout.fg;
+          i64* cell = out + grp * a.layout.group_stride + (u64(fl) * kMaxBins + b) * 2 + comp;
+          if (v) atomicAdd(reinterpret_cast<unsigned long long*>(cell), static_cast<unsigned long long>(v));
         }
       }
       __syncthreads();  // the staging area is read before it is cleared
@@ -579,18 +598,28 @@ __global__ void __launch_bounds__(1024) k_hist_wide(HistArgs a) {
           }
         }
         __syncthreads();
-        for (u32 i = threadIdx.x; i < 32u * 256u; i += THREADS) {
-          const u32 fl32 = i >> 8, b = i & 255u;
-          const u32 gf = key_f0 + 32u * hf + fl32;
-          if (gf >= a.F) continue;
-          const longlong2 v = T[fl32 * 256u + (b ^ fl32)];
-          const u32 grp = gf / a.layout.fg, fl = gf - grp * a.layout.fg;
-          i64* cell = out + grp * a.layout.group_stride + (u64(fl) * kMaxBins + b) * 2;
-          if (key_excl) {
-            *reinterpret_cast<longlong2*>(cell) = v;
-          } else if (v.x | v.y) {
-            atomicAdd(reinterpret_cast<unsigned long long*>(cell), static_cast<unsigned long long>(v.x));
-            atomicAdd(reinterpret_cast<unsigned long long*>(cell) + 1, static_cast<unsigned long long>(v.y));
+        if (key_excl) {
+          for (u32 i = threadIdx.x; i < 32u * 256u; i += THREADS) {
+            const u32 fl32 = i >> 8, b = i & 255u;
+            const u32 gf = key_f0 + 32u * hf + fl32;
+            if (gf >= a.F) continue;
+            const u32 grp = gf / a.layout.fg, fl = gf - grp * a.layout.fg;
+            i64* cell = out + grp * a.layout.group_stride + (u64(fl) * kMaxBins + b) * 2;
+            *reinterpret_cast<longlong2*>(cell) = T[fl32 * 256u + (b ^ fl32)];
+          }
+        } else {
+          // g and h of a cell on neighbouring lanes: a warp's 32 reductions
+          // cover 16 whole cells, eight 32-byte sectors
+          const long long* T64 = reinterpret_cast<const long long*>(T);
+          for (u32 i = threadIdx.x; i < 2u * 32u * 256u; i += THREADS) {
+            const u32 c = i >> 1, comp = i & 1u;
+            const u32 fl32 = c >> 8, b = c & 255u;
+            const u32 gf = key_f0 + 32u * hf + fl32;
+            if (gf >= a.F) continue;
+            const long long v = T64[2u * (fl32 * 256u + (b ^ fl32)) + comp];
+            const u32 grp = gf / a.layout.fg, fl = gf - grp * a.layout.fg;
+            i64* cell = out + grp * a.layout.group_stride + (u64(fl) * kMaxBins + b) * 2 + comp;
+            if (v) atomicAdd(reinterpret_cast<unsigned long long*>(cell), static_cast<unsigned long long>(v));
           }
         }
         __syncthreads();  // the staging area is read before it is refilled or cleared
@@ -735,11 +764,21 @@ void launch_histograms_wide(const u8* bins, u64 bin_stride, u32 F, bool quantize
   after_launch("histograms");
 }
 
-u64 hist_chunk_rows(u64 total_rows) {
+u64 hist_chunk_rows(u64 total_rows, u64 nseg) {
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const u64 target = u64(sms) * 4;  // about four tasks per SM, balanced by the task queue
+  // Tasks per SM, balanced by the task queue: about four; sixteen for 2 to 16
+  // segments, whose rows interleave in the matrix: with the queue in piece
+  // order, the pieces of one row range run together, and smaller pieces keep
+  // them within what L2 holds for each range (config 5, 8 nodes: 0.40 -> 0.45
+  // of HBM at 256 bins, 0.41 -> 0.48 at 64 bins; with one node or 1024 the
+  // extra drains cost more: 0.57 -> 0.56, 0.37 -> 0.34).  DP_HIST_TASKS_PER_SM
+  // overrides.
+  u64 per_sm = (nseg >= 2 && nseg <= 16) ? 16 : 4;
+  if (const char* v = std::getenv("DP_HIST_TASKS_PER_SM"))
+    if (*v) per_sm = std::max<u64>(1, std::strtoull(v, nullptr, 10));
+  const u64 target = u64(sms) * per_sm;
   const u64 chunk = (total_rows + target - 1) / target;
   return chunk < 2048 ? 2048 : chunk;
 }

@@ -182,9 +182,9 @@ void launch_histograms_wide(const u8* bins, u64 bin_stride, u32 F, bool quantize
                             const Scales* scales, const HistTask* tasks, u32 ntasks, u32* counter, i64* hist,
                             cudaStream_t s, const u32* ntasks_dev, const HistLayout* layout,
                             bool counter_zeroed = false);
-// Rows per histogram task for a launch over `total_rows` row-tiles (about
-// four tasks per SM; tasks tasks of one node and tile stay contiguous).
-u64 hist_chunk_rows(u64 total_rows);
+// Rows per histogram task for a launch over `total_rows` row-tiles of nseg
+// segments (about four tasks per SM, sixteen for 2 to 16 segments).
+u64 hist_chunk_rows(u64 total_rows, u64 nseg);
 // gh[k][r] (fp32 pairs) -> int32 pairs rint(g * s_g), rint(h * s_h), in place.
 void launch_quantize_gh(float2* gh, u64 R, int K, const Scales* scales, cudaStream_t s);
 
