@@ -178,17 +178,21 @@ Engine::Engine(DMatrix& d, const TrainParams& p, Comm* comm) : d_(d), p_(p), com
   // 2.16 ms).  DP_HIST_WIDE=0 / 1 overrides.
   wide_ = max_bins_ > 64 && F_ > kFT && env_u64("DP_HIST_WIDE", (G_ == 1 && F_ > 2 * kFT) ? 1 : 0) != 0;
   hist_tile_ = wide_ ? kHistWideTile : kFT;
-  // Histogram tasks per SM: when the bin matrix exceeds L2, about four keep
-  // the blocks running at one time on neighbouring rows (L2 reuse of lines
-  // shared by several nodes' rows; one per SM was 4% slower over a config-4
-  // round and 50% slower for config 5 with 8 nodes).  When it fits in L2,
-  // one per SM: a quarter of the pieces' drains (config 2: 0.64 against 0.68
-  // ms per round).  DP_HIST_TASKS_PER_SM overrides.
+  // Histogram tasks per SM: when the bin matrix exceeds L2 and rows share
+  // 128-byte lines, about four keep the blocks running at one time on
+  // neighbouring rows (L2 reuse of lines shared by several nodes' rows; one
+  // per SM was 50% slower for config 5 with 8 nodes); when rows are whole
+  // lines there is nothing to share and two halve the drains (config 4: 4.85
+  // against 4.91 ms per round with four, 5.36 with eight).  When it fits in
+  // L2, one per SM: a quarter of the pieces' drains (config 2: 0.64 against
+  // 0.73 ms per round).  DP_HIST_TASKS_PER_SM overrides.
   {
     int l2 = 0;
     DP_CUDA(cudaDeviceGetAttribute(&l2, cudaDevAttrL2CacheSize, device_));
     const bool in_l2 = u64(R_) * u64(F_) <= u64(l2) / 4 * 3;
-    hist_target_tasks_ = u32(sms_) * u32(std::max<u64>(1, env_u64("DP_HIST_TASKS_PER_SM", in_l2 ? 1 : 4)));
+    const bool whole_lines = q_->bin_stride % 128 == 0;  // no two rows share a 128-byte line
+    const u64 per_sm = in_l2 ? 1 : (whole_lines ? 2 : 4);
+    hist_target_tasks_ = u32(sms_) * u32(std::max<u64>(1, env_u64("DP_HIST_TASKS_PER_SM", per_sm)));
   }
   // testing knobs: force the exact-count path of deep levels
   async_open_limit_ = env_u64("DP_ASYNC_OPEN_LIMIT", async_open_limit_);
@@ -332,7 +336,6 @@ void Engine::presize(SlabPlan& plan) {
   const u64 Rt = std::max<u64>(q_->rows_total, 1);
   const u64 RK = std::max<u64>(R_, 1) * K;
   const u64 slot_bytes = slot_elems_ * sizeof(i64);
-  const u32 ftiles = (F_ + hist_tile_ - 1) / hist_tile_;
   // the same bounds the level loop of boost_round derives
   u64 open_hi = K, ids_hi = 1, leaves_hi = 0;
   u64 hist[2] = {0, 0}, tasks = 0, split = 0, opens[2] = {K, 0}, builds[2] = {K, 0}, send = 0;
@@ -345,7 +348,7 @@ void Engine::presize(SlabPlan& plan) {
     const u64 nbuild_hi = depth == 0 ? K : (open_hi + 1) / 2;
     const u64 next_hi = std::min<u64>(2 * open_hi, K * Rt);
     hist[depth & 1] = std::max<u64>(hist[depth & 1], std::max<u64>(open_hi, 1) * slot_elems_);
-    tasks = std::max<u64>(tasks, (nbuild_hi + 4 * u64(sms_) + 1) * ftiles);
+    tasks = std::max<u64>(tasks, hist_task_bound(nbuild_hi));
     if (G_ > 1) send = std::max<u64>(send, nbuild_hi * full_slot_elems_);
     split = std::max<u64>(split, open_hi);
     opens[(depth + 1) & 1] = std::max<u64>(opens[(depth + 1) & 1], next_hi);
@@ -606,7 +609,7 @@ Engine::RoundOut Engine::enqueue_round() {
     const u64 ids_next = std::min<u64>({ids_hi + 2 * std::min<u64>(open_hi, u64(1) << depth),
                                         (u64(1) << (depth + 2)) - 1, 2 * Rt + 1});
     grow(hist_[region], std::max<u64>(open_hi, 1) * slot_elems_);
-    grow(hist_tasks_, (nbuild_hi + 4 * u64(sms_) + 1) * ftiles);
+    grow(hist_tasks_, hist_task_bound(nbuild_hi));
     grow(eval_nodes_, open_hi);
     grow(cand_, open_hi * nchunks_);
     if (G_ > 1) {

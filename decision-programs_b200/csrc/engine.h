@@ -180,6 +180,11 @@ class Engine {
   bool wide_ = false;
   u32 hist_tile_ = kHistFeatureTile;
   u32 hist_target_tasks_ = 4 * 148;  // histogram tasks per level, about
+  // Capacity of a level's histogram task list for nbuild built nodes: pieces
+  // of at least total * tiles / target rows, at least one per node and tile.
+  u64 hist_task_bound(u64 nbuild) const {
+    return (nbuild + 1) * u64((F_ + hist_tile_ - 1) / hist_tile_) + hist_target_tasks_;
+  }
   DevBuf<EvalNode> eval_nodes_;
   DevBuf<SplitCand> cand_;                 // [open][nchunks_] this rank's candidates
   DevBuf<i64> send_;                       // this rank's partial histograms, group-major (G > 1)
