@@ -110,6 +110,13 @@ class DevBuf {
     if (n > n_) resize(n);
   }
   // Becomes a view of n elements at p (memory owned elsewhere).
+  // Owns p (n elements, from cudaMalloc) from now on.
+  void take_ownership(T* p, size_t n) {
+    release();
+    p_ = p;
+    n_ = n;
+    owned_ = true;
+  }
   void adopt(T* p, size_t n) {
     release();
     p_ = p;
@@ -156,47 +163,102 @@ class SlabPlan {
   std::vector<std::function<void(unsigned char*)>> binds_;
 };
 
-// Process-wide cache of one device slab per device, for the engines of
-// boosters that come and go on one training matrix (a hyper-parameter search
-// or out-of-fold fits create one per fit): cudaMalloc of a slab costs
-// milliseconds and cudaFree waits for the whole device.  A freed engine's slab
-// stays allocated until a later engine reuses it (it holds at least what is
-// asked for and at most twice that), another slab replaces it, or
-// release_all() (dp_release_cached_memory) frees it.
+// Process-wide cache of freed device slabs, for the matrices and engines of
+// jobs that come and go in one process (a hyper-parameter search or
+// out-of-fold fits create a booster per fit, and repeated jobs a matrix per
+// job): cudaMalloc of a slab costs milliseconds and cudaFree waits for the
+// whole device.  A freed slab stays allocated until a later request reuses it
+// (the smallest cached slab of the device that holds at least what is asked
+// for and at most twice that), the cache drops it (it keeps at most kMaxSlabs
+// slabs, and at most half of a device's memory, dropping the oldest first),
+// an allocation fails (the device's cached slabs are freed and the allocation
+// retried), or release_all() (dp_release_cached_memory) frees everything.
+// A slab is handed back only when no work on it is in flight.
 class SlabCache {
  public:
+  static constexpr size_t kMaxSlabs = 4;
+
   static DevBuf<unsigned char> take(int device, size_t bytes) {
     DevBuf<unsigned char> out;
     {
       std::lock_guard<std::mutex> lock(mu());
       auto& c = slots();
-      for (auto it = c.begin(); it != c.end(); ++it) {
-        if (it->first != device) continue;
-        if (it->second.size() >= bytes && it->second.size() <= 2 * bytes) out = std::move(it->second);
-        c.erase(it);  // a slab that does not fit is freed before the new allocation
-        break;
+      size_t best = c.size();
+      for (size_t i = 0; i < c.size(); ++i) {
+        const size_t sz = c[i].second.size();
+        if (c[i].first == device && sz >= bytes && sz <= 2 * bytes && (best == c.size() || sz < c[best].second.size()))
+          best = i;
+      }
+      if (best < c.size()) {
+        out = std::move(c[best].second);
+        c.erase(c.begin() + std::ptrdiff_t(best));
       }
     }
-    if (!out.get()) out.resize(bytes);
+    if (!out.get()) {
+      if (cudaMalloc_fits(out, bytes)) return out;
+      release_device(device);
+      out.resize(bytes);
+    }
     return out;
   }
+
   static void give(int device, DevBuf<unsigned char>&& slab) {
     if (!slab.get()) return;
+    const size_t total = device_memory(device);
     std::lock_guard<std::mutex> lock(mu());
     auto& c = slots();
-    for (auto it = c.begin(); it != c.end(); ++it)
-      if (it->first == device) {
-        c.erase(it);
-        break;
-      }
     c.emplace_back(device, std::move(slab));
+    auto device_bytes = [&] {
+      size_t n = 0;
+      for (auto& e : c)
+        if (e.first == device) n += e.second.size();
+      return n;
+    };
+    while (c.size() > kMaxSlabs || (total && device_bytes() > total / 2)) {
+      size_t drop = 0;  // the oldest (of this device when over its share)
+      if (c.size() <= kMaxSlabs)
+        while (c[drop].first != device) ++drop;
+      c.erase(c.begin() + std::ptrdiff_t(drop));
+    }
   }
+
   static void release_all() {
     std::lock_guard<std::mutex> lock(mu());
     slots().clear();
   }
 
  private:
+  // One allocation attempt; false (error state cleared) when the device is out of memory.
+  static bool cudaMalloc_fits(DevBuf<unsigned char>& out, size_t bytes) {
+    unsigned char* p = nullptr;
+    const cudaError_t e = cudaMalloc(&p, bytes);
+    if (e == cudaSuccess) {
+      out.take_ownership(p, bytes);
+      return true;
+    }
+    cudaGetLastError();
+    if (e != cudaErrorMemoryAllocation) DP_CUDA(e);
+    return false;
+  }
+  // Total memory of a device (0 if unknown), looked up once per device.
+  static size_t device_memory(int device) {
+    static std::mutex m;
+    static std::vector<size_t> known;
+    std::lock_guard<std::mutex> lock(m);
+    if (device < 0) return 0;
+    if (size_t(device) >= known.size()) known.resize(size_t(device) + 1, ~size_t(0));
+    if (known[device] == ~size_t(0)) {
+      cudaDeviceProp prop{};
+      known[device] = cudaGetDeviceProperties(&prop, device) == cudaSuccess ? prop.totalGlobalMem : 0;
+    }
+    return known[device];
+  }
+  static void release_device(int device) {
+    std::lock_guard<std::mutex> lock(mu());
+    auto& c = slots();
+    for (size_t i = c.size(); i-- > 0;)
+      if (c[i].first == device) c.erase(c.begin() + std::ptrdiff_t(i));
+  }
   static std::mutex& mu() {
     static std::mutex m;
     return m;

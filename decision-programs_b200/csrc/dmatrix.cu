@@ -18,7 +18,9 @@ DMatrix::DMatrix(const float* x, u64 rows, u32 cols, u64 stride, int device, boo
   DeviceGuard g(device_);
   if (rows_ == 0) return;
   // the counts, then one flag word for infinite values
-  prefix_counts_.resize(u64(cols_) * kPrefixBuckets + 1);
+  SlabPlan plan;
+  plan.want(prefix_counts_, u64(cols_) * kPrefixBuckets + 1);
+  plan.commit(slabs_, device_);
   u32* bad = prefix_counts_.get() + u64(cols_) * kPrefixBuckets;
   DP_CUDA(cudaMemset(prefix_counts_.get(), 0, prefix_counts_.size() * sizeof(u32)));
   launch_prefix_counts(x_, rows_, cols_, stride_, has_mv_, mv_, prefix_counts_.get(), bad, nullptr);
@@ -38,10 +40,14 @@ std::unique_ptr<DMatrix> DMatrix::from_host(const float* x, u64 rows, u32 cols, 
   d->has_mv_ = has_mv;
   d->mv_ = mv;
   DeviceGuard g(device);
-  d->owned_.resize(std::max<u64>(rows, 1) * cols);
+  {
+    SlabPlan plan;
+    plan.want(d->owned_, std::max<u64>(rows, 1) * cols);
+    if (rows > 0) plan.want(d->prefix_counts_, u64(cols) * kPrefixBuckets + 1);
+    plan.commit(d->slabs_, device);
+  }
   d->x_ = d->owned_.get();
   if (rows == 0) return d;
-  d->prefix_counts_.resize(u64(cols) * kPrefixBuckets + 1);
   u32* bad = d->prefix_counts_.get() + u64(cols) * kPrefixBuckets;
   cudaStream_t copy = nullptr, count = nullptr;
   cudaEvent_t landed = nullptr;
@@ -84,6 +90,20 @@ std::unique_ptr<DMatrix> DMatrix::from_host(const float* x, u64 rows, u32 cols, 
   return d;
 }
 
+DMatrix::~DMatrix() {
+  if (slabs_.empty() && !q_) return;
+  DeviceGuard g(device_);
+  // what cudaFree would wait for: no kernel may still read the memory when a
+  // later matrix or engine is given it
+  if (cudaDeviceSynchronize() != cudaSuccess) {
+    cudaGetLastError();
+    return;  // the device is in an error state: free normally
+  }
+  for (auto& slab : slabs_) SlabCache::give(device_, std::move(slab));
+  if (q_)
+    for (auto& slab : q_->slabs) SlabCache::give(device_, std::move(slab));
+}
+
 void DMatrix::check_bad(const u32* bad_dev) {
   u32 h = 0;
   DP_CUDA(cudaMemcpy(&h, bad_dev, sizeof h, cudaMemcpyDeviceToHost));
@@ -114,7 +134,7 @@ const Quantized& DMatrix::quantized(int max_bin, Comm* comm, cudaStream_t s) {
   plan.want(q->bins, std::max<u64>(rows_, 1) * q->bin_stride);
   plan.want(q->bins_blk, std::max<u64>((rows_ + 31) / 32, 1) * 32 * cols_);
   auto t0 = std::chrono::steady_clock::now();
-  plan.commit(q->slabs);
+  plan.commit(q->slabs, device_);
   const double ms_alloc = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
   q->rows_total = comm ? comm->sum_host_u64(rows_, s) : rows_;
   CutsDevice cd{q->cut.get(), q->nbins.get(), q->has_missing.get()};

@@ -38,6 +38,10 @@ class DMatrix {
  public:
   // Borrowed device matrix.
   DMatrix(const float* x, u64 rows, u32 cols, u64 stride, int device, bool has_mv, float mv);
+  // Waits for the device, then hands the matrix's memory to SlabCache.
+  ~DMatrix();
+  DMatrix(const DMatrix&) = delete;
+  DMatrix& operator=(const DMatrix&) = delete;
   // Host matrix copied to `device`.
   static std::unique_ptr<DMatrix> from_host(const float* x, u64 rows, u32 cols, u64 stride, int device, bool has_mv,
                                             float mv);
@@ -58,6 +62,7 @@ class DMatrix {
   DMatrix() = default;
   void check_bad(const u32* bad_dev);
   const float* x_ = nullptr;
+  std::vector<DevBuf<u8>> slabs_;  // memory of owned_ and prefix_counts_
   DevBuf<float> owned_;        // host-sourced matrix
   DevBuf<u32> prefix_counts_;  // [cols][kPrefixBuckets] this rank's rows, then a flag word
   bool prefix_valid_ = false;  // counts present and not yet consumed by a cut search

@@ -154,11 +154,11 @@ DP_API int dp_comm_set_timeout(void* comm, int64_t timeout_ms);
  * partial histograms (send holds nranks blocks), ordered on `stream`. */
 DP_API int dp_comm_reduce_scatter_hist(void* comm, const int64_t* send, int64_t* recv, uint64_t recv_n, void* stream);
 
-/* Frees the device memory kept for reuse: the library keeps the working
- * memory of the last freed booster on each device (one allocation) so that
- * the next booster trained there (a search or out-of-fold fits create one per
- * fit) does not pay for cudaMalloc and cudaFree, which wait for the device.
- * No counterpart in the reference. */
+/* Frees the device memory kept for reuse: the library keeps the memory of
+ * freed boosters and matrices (at most four allocations, at most half of a
+ * device's memory) so that the next booster or matrix there (a search or
+ * out-of-fold fits create one per fit) does not pay for cudaMalloc and
+ * cudaFree, which wait for the device.  No counterpart in the reference. */
 DP_API int dp_release_cached_memory(void);
 
 /* Per-kernel CUDA-event timings of the training rounds ({"name":{"launches",
