@@ -22,7 +22,15 @@ namespace dp {
 namespace {
 
 constexpr int kPartThreads = 256;
-constexpr int kIlp = 8;  // independent row gathers in flight per thread
+// Independent row gathers in flight per thread.  Below depth 4 every row's
+// code is its own 32-byte sector (a 64-byte DRAM fetch), and ncu shows DRAM
+// about half busy with 21 long-scoreboard stalls per issue at five blocks per
+// SM; sixteen gathers per thread (4096-row tasks, four blocks per SM) were
+// slower on B200 (config 4: 4.95 against 4.85 ms per round).
+#ifndef DP_PART_ILP
+#define DP_PART_ILP 8
+#endif
+constexpr int kIlp = DP_PART_ILP;
 constexpr int kScatterSteps = 4;  // 256-position steps whose (g, h) loads are in flight together
 constexpr int kWordsPerTask = kPartChunk / 32;
 static_assert(kPartChunk % (kPartThreads * kIlp) == 0, "task rows are whole gather rounds");
