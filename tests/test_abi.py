@@ -130,3 +130,9 @@ def test_float_format_round_trips_through_double(dp, tmp_path):
         out = json.loads(b.save_raw())["learner"]["gradient_booster"]["model"]["trees"][0]["split_conditions"][0]
         # double parse then narrow, as native/class_io.hpp:180 does; the sign of zero survives
         assert np.float32(out).view(np.uint32) == v.view(np.uint32)
+
+
+def test_release_cached_memory_with_nothing_kept(dp):
+    # nothing has been freed in this process: no allocation is kept, and the
+    # call succeeds without touching a device
+    assert dp.lib().dp_release_cached_memory() == 0
