@@ -295,6 +295,19 @@ __global__ void __launch_bounds__(kBook) k_decide(RoundBuffers b, const float* _
       atomicOr(&b.ctr->overflow, kOvfBadCand);
     const bool split = valid && depth < max_depth && in_range && bs.gain > 0.0;
     const bool leaf = valid && !split;
+    // what a split reads (the node's totals, the threshold, the feature's
+    // missing flag), loaded before the block scans so that the loads' latency
+    // overlaps the barriers
+    i64 node_gq = 0, node_hq = 0;
+    float cond = 0.f;
+    i32 missing_is_bin = 0;
+    if (split) {
+      const NodeRec& p0 = node_at(b, o.tree, o.id);
+      node_gq = p0.gq;
+      node_hq = p0.hq;
+      cond = cut[u64(bs.feature) * kMaxBins + bs.bin];
+      missing_is_bin = i32(has_missing[bs.feature]);
+    }
     u64 ns = 0, nl = 0;
     const u64 rs = split_base + scan_block(split ? 1 : 0, &ns);
     const u64 rl = leaf_base + scan_block(leaf ? 1 : 0, &nl);
@@ -314,12 +327,12 @@ __global__ void __launch_bounds__(kBook) k_decide(RoundBuffers b, const float* _
         p.feature = bs.feature;
         p.bin = bs.bin;
         p.default_left = bs.default_left;
-        p.cond = cut[u64(bs.feature) * kMaxBins + bs.bin];
+        p.cond = cond;
         p.gain = float(bs.gain);
         node_at(b, o.tree, lid) = NodeRec{bs.gl, bs.hl, -1, -1, i32(o.id), -1, 0, 0, 0.f, 0.f};
-        node_at(b, o.tree, rid) = NodeRec{p.gq - bs.gl, p.hq - bs.hl, -1, -1, i32(o.id), -1, 0, 0, 0.f, 0.f};
-        b.part_nodes[rs] = PartNode{o.tree, bs.feature, bs.bin, bs.default_left, i32(has_missing[bs.feature]), 0,
-                                    o.begin, o.begin + o.count};
+        node_at(b, o.tree, rid) = NodeRec{node_gq - bs.gl, node_hq - bs.hl, -1, -1, i32(o.id), -1, 0, 0, 0.f, 0.f};
+        b.part_nodes[rs] = PartNode{o.tree, bs.feature, bs.bin, bs.default_left, missing_is_bin, 0, o.begin,
+                                    o.begin + o.count};
         b.split_idx[rs] = i;
         b.cursors[2 * rs] = 0u;
         b.cursors[2 * rs + 1] = 0u;
