@@ -373,6 +373,7 @@ void Engine::presize(SlabPlan& plan) {
     plan.want(gathered_, split * nchunks_ * u64(G_));
   }
   plan.want(split_idx_, split);
+  plan.want(zero_list_, split);
   plan.want(part_nodes_, split);
   plan.want(cursors_, 2 * split);
   plan.want(part_tasks_, (RK + kPartChunk - 1) / kPartChunk + split);
@@ -400,6 +401,7 @@ RoundBuffers Engine::round_buffers(int depth, u64 cap_split, u64 cap_next) const
   b.triples_next = triples_[n].get();
   b.hist_tasks = hist_tasks_.get();
   b.hist_counter = hist_counter_.get();
+  b.zero_list = zero_list_.get();
   b.eval_nodes = eval_nodes_.get();
   b.cands = G_ > 1 ? gathered_.get() : cand_.get();
   b.nranks = u32(G_);
@@ -590,7 +592,6 @@ Engine::RoundOut Engine::enqueue_round() {
   u64 open_hi = u64(K), ids_hi = 1, leaves_hi = 0;
   std::vector<int> pi_hist(D, -1), pi_eval(D, -1);
   int set = 0, region = 0, depth = 0;
-  bool zeroed_by_children = false;  // this level's output slots were zeroed by the previous level
   bool folded = false;              // the last level routed its rows straight into the margins
   static const char* const kLevelNames[] = {"level 0", "level 1", "level 2", "level 3", "level 4", "level 5",
                                              "level 6", "level 7", "level 8", "level 9", "level 10+"};
@@ -617,6 +618,7 @@ Engine::RoundOut Engine::enqueue_round() {
       grow(gathered_, open_hi * nchunks_ * u64(G_));
     }
     grow(split_idx_, open_hi);
+    grow(zero_list_, open_hi);
     if (col_sampling()) grow(fmask_, open_hi * mask_words_);
     grow(part_nodes_, open_hi);
     grow(cursors_, 2 * open_hi);
@@ -635,8 +637,7 @@ Engine::RoundOut Engine::enqueue_round() {
     // its own feature group.
     launch_hist_tasks(rb, ftiles, hist_tile_, depth, hist_target_tasks_, stream_);
     i64* hout = G_ > 1 ? send_.get() : hist;
-    const u64 out_slot = G_ > 1 ? full_slot_elems_ : slot_elems_;
-    if (!zeroed_by_children) launch_zero_slots(rb, hout, out_slot, G_ > 1 ? nbuild_hi : 0, stream_);
+    launch_zero_listed(rb, hout, slot_elems_, nbuild_hi * slot_elems_, u32(G_), stream_);
     const HistLayout lay{fg_, slot_elems_, nbuild_hi * slot_elems_};
     pi_hist[depth] = prof_.begin(stream_, "histograms", 0.0);
     // (the task kernel zeroed the queue counter)
@@ -698,18 +699,7 @@ Engine::RoundOut Engine::enqueue_round() {
     launch_partition_dev(q_->bins_blk.get(), 32 * u64(F), tarr_[set].get(), tarr_[1 - set].get(), part_nodes_.get(),
                          part_tasks_.get(), &ctr->n_part_tasks, cursors_.get(), stream_);
     prof_.end(stream_);
-    // the children kernel zeroes the next level's output slots when their
-    // buffer is already large enough (so the next level does not regrow it)
-    {
-      const u64 nb_next = (next_hi + 1) / 2;
-      const bool next_async = next_hi <= async_open_limit_ && next_hi * slot_bytes <= async_hist_bytes_;
-      i64* z = G_ > 1 ? send_.get() : hist_[1 - region].get();
-      const u64 zsize = G_ > 1 ? send_.size() : hist_[1 - region].size();
-      const u64 zslot = G_ > 1 ? full_slot_elems_ : slot_elems_;
-      const bool zfit = (G_ > 1 ? nb_next : next_hi) * zslot <= zsize;
-      zeroed_by_children = depth + 1 < D && next_async && zfit;
-      launch_children(rb, depth, D, stream_, zeroed_by_children ? z : nullptr, zslot, G_ > 1 ? nb_next : 0);
-    }
+    launch_children(rb, depth, D, stream_);
 
     leaves_hi += open_hi;
     open_hi = next_hi;

@@ -196,7 +196,7 @@ class Engine {
   DevBuf<LeafTask> leaf_tasks_;
   // round state on the device (level.h)
   DevBuf<NodeRec> nodes_;
-  DevBuf<u32> next_id_, tree_first_, split_idx_;
+  DevBuf<u32> next_id_, tree_first_, split_idx_, zero_list_;
   DevBuf<OpenRec> open_[2];
   DevBuf<u32> build_[2], triples_[2];
   DevBuf<LeafRec> leaves_;

@@ -187,7 +187,7 @@ __global__ void __launch_bounds__(kBook) k_hist_tasks(RoundBuffers b, u32 ftiles
   scan_block(rows, &total);
   u64 chunk = (total * ftiles + target - 1) / target;
   if (chunk < 2048) chunk = 2048;
-  u64 base = 0;
+  u64 base = 0, zbase = 0;
   for (u32 c0 = 0; c0 < nb; c0 += kBook) {
     const u32 i = c0 + threadIdx.x;
     u64 pieces = 0;
@@ -199,6 +199,11 @@ __global__ void __launch_bounds__(kBook) k_hist_tasks(RoundBuffers b, u32 ftiles
       s_tree[threadIdx.x] = o.tree;
       pieces = hist_pieces(o.count, chunk);
     }
+    // slots that are not stored whole by one task are zeroed before the build
+    u64 nz = 0;
+    const u64 zpos = zbase + scan_block(i < nb && pieces != 1 ? 1 : 0, &nz);
+    if (i < nb && pieces != 1) b.zero_list[zpos] = s_slot[threadIdx.x];
+    zbase += nz;
     base += expand(pieces * ftiles, base, b.cap_hist_tasks, [&](int j, u64 q, u64 t) {
       const i64 cnt = s_count[j], beg0 = s_begin[j], end0 = beg0 + cnt;
       const i64 np = i64(hist_pieces(cnt, chunk));
@@ -228,18 +233,23 @@ __global__ void __launch_bounds__(kBook) k_hist_tasks(RoundBuffers b, u32 ftiles
   if (threadIdx.x == 0) {
     if (base > b.cap_hist_tasks) b.ctr->overflow |= kOvfHistTasks;
     b.ctr->n_hist_tasks = u32(base < b.cap_hist_tasks ? base : b.cap_hist_tasks);
+    b.ctr->n_zero = u32(zbase);
     b.stats[depth].rows_built = i64(total);
     b.stats[depth].n_build = nb;
     b.stats[depth].n_open = n_open;
   }
 }
 
-__global__ void k_zero_slots(const RoundCounters* __restrict__ ctr, i64* hist, u64 slot_elems, u64 min_slots) {
-  const u64 nb = ctr->n_build > min_slots ? ctr->n_build : min_slots;
-  const u64 n2 = nb * slot_elems / 2;
-  longlong2* h = reinterpret_cast<longlong2*>(hist);
-  for (u64 i = u64(blockIdx.x) * blockDim.x + threadIdx.x; i < n2; i += u64(gridDim.x) * blockDim.x)
-    h[i] = make_longlong2(0, 0);
+__global__ void k_zero_listed(const RoundCounters* __restrict__ ctr, const u32* __restrict__ list, i64* hist,
+                              u64 slot_stride, u64 group_stride, u32 groups) {
+  const u64 per = slot_stride / 2;  // 16-byte stores per slot and group
+  const u64 n = u64(ctr->n_zero) * groups * per;
+  longlong2* const h = reinterpret_cast<longlong2*>(hist);
+  for (u64 k = u64(blockIdx.x) * blockDim.x + threadIdx.x; k < n; k += u64(gridDim.x) * blockDim.x) {
+    const u64 e = k % per, sg = k / per;
+    const u64 g = sg % groups, li = sg / groups;
+    h[(g * group_stride + u64(list[li]) * slot_stride) / 2 + e] = make_longlong2(0, 0);
+  }
 }
 
 // Splits or closes every open node, in open-list order (trees contiguous,
@@ -369,17 +379,10 @@ __global__ void __launch_bounds__(kBook) k_decide(RoundBuffers b, const float* _
 // Children of every split node become the next level's open list (see
 // RoundBuffers::by_hess for which child is built directly).  Block 0 also
 // sets the next level's counts.
-__global__ void k_children(RoundBuffers b, int depth, int max_depth, i64* zero, u64 slot_elems, u64 min_slots) {
+__global__ void k_children(RoundBuffers b, int depth, int max_depth) {
   const u32 ns = b.ctr->n_split;
   const bool more = depth + 1 < max_depth;
   const bool fits = 2 * u64(ns) <= b.cap_next;
-  if (zero && more) {
-    // the next level's output slots (the parents this level read are done)
-    const u64 n2 = (ns > min_slots ? u64(ns) : min_slots) * slot_elems / 2;
-    longlong2* z = reinterpret_cast<longlong2*>(zero);
-    for (u64 k = u64(blockIdx.x) * blockDim.x + threadIdx.x; k < n2; k += u64(gridDim.x) * blockDim.x)
-      z[k] = make_longlong2(0, 0);
-  }
   if (blockIdx.x == 0 && threadIdx.x == 0) {
     b.ctr->n_open = fits ? 2 * ns : 0u;
     b.ctr->n_build = (more && fits) ? ns : 0u;
@@ -562,9 +565,12 @@ void launch_hist_tasks(const RoundBuffers& b, u32 ftiles, u32 tile, int depth, u
   after_launch("hist_tasks");
 }
 
-void launch_zero_slots(const RoundBuffers& b, i64* hist, u64 slot_elems, u64 min_slots, cudaStream_t s) {
-  k_zero_slots<<<sm_count() * 4, 256, 0, s>>>(b.ctr, hist, slot_elems, min_slots);
-  after_launch("zero_slots");
+void launch_zero_listed(const RoundBuffers& b, i64* hist, u64 slot_stride, u64 group_stride, u32 groups,
+                        cudaStream_t s) {
+  need(slot_stride % 2 == 0 && (groups <= 1 || group_stride % 2 == 0), "internal error: slot strides");
+  k_zero_listed<<<sm_count() * 4, 256, 0, s>>>(b.ctr, b.zero_list, hist, slot_stride, groups > 1 ? group_stride : 0,
+                                               groups ? groups : 1);
+  after_launch("zero_listed");
 }
 
 void launch_decide(const RoundBuffers& b, const float* cut, const u8* has_missing, u32 F, int depth, int max_depth,
@@ -573,9 +579,8 @@ void launch_decide(const RoundBuffers& b, const float* cut, const u8* has_missin
   after_launch("decide");
 }
 
-void launch_children(const RoundBuffers& b, int depth, int max_depth, cudaStream_t s, i64* zero, u64 slot_elems,
-                     u64 min_slots) {
-  k_children<<<sm_count() * (zero ? 4 : 1), 256, 0, s>>>(b, depth, max_depth, zero, slot_elems, min_slots);
+void launch_children(const RoundBuffers& b, int depth, int max_depth, cudaStream_t s) {
+  k_children<<<sm_count(), 256, 0, s>>>(b, depth, max_depth);
   after_launch("children");
 }
 

@@ -33,7 +33,9 @@ struct LeafRec {
 struct RoundCounters {
   u32 n_open, n_build, n_split, n_hist_tasks;
   u32 n_part_tasks, n_leaves, n_leaf_tasks, n_triples;
-  u32 overflow, pad[7];
+  u32 overflow;
+  u32 n_zero;              // histogram slots the next histogram launch adds into (zero_list)
+  u32 pad[6];
 };
 
 // Overflow bits.
@@ -76,6 +78,7 @@ struct RoundBuffers {
   RoundCounters* ctr;
   LevelStats* stats;       // [max_depth + 1]
   u32* hist_counter;       // the histogram kernel's task queue; zeroed by k_hist_tasks
+  u32* zero_list;          // [cap_split] slots whose sums are added by several tasks, or by none
   u32 K, maxn;
   // Which child of a split is built directly (the other is parent minus it):
   // the one with fewer rows, or, when rows are sharded (by_hess), the one
@@ -103,15 +106,17 @@ void launch_quantize_round(const RoundBuffers& b, float2* gh, u64 R, const Scale
 // tasks per row range; rows split into pieces of equal size for about
 // target_tasks tasks in all (2048 rows at least).
 void launch_hist_tasks(const RoundBuffers& b, u32 ftiles, u32 tile, int depth, u32 target_tasks, cudaStream_t s);
-// Zeroes max(device n_build, min_slots) histogram slots.
-void launch_zero_slots(const RoundBuffers& b, i64* hist, u64 slot_elems, u64 min_slots, cudaStream_t s);
+// Zeroes the slots k_hist_tasks listed (zero_list, n_zero): those of nodes
+// cut into several pieces, whose tasks add their sums, and of nodes with no
+// rows here, which no task writes; a node built by one task is stored whole.
+// Slot s of group g starts at g * group_stride + s * slot_stride (groups = 1:
+// group_stride unused) and holds slot_stride int64.
+void launch_zero_listed(const RoundBuffers& b, i64* hist, u64 slot_stride, u64 group_stride, u32 groups,
+                        cudaStream_t s);
 // Splits (depth < max_depth, gain > 0) or closes every open node.
 void launch_decide(const RoundBuffers& b, const float* cut, const u8* has_missing, u32 F, int depth, int max_depth,
                    int set, cudaStream_t s);
-// With zero set (and depth + 1 < max_depth), also zeroes max(n_split,
-// min_slots) slots of slot_elems int64 at zero: the next level's output.
-void launch_children(const RoundBuffers& b, int depth, int max_depth, cudaStream_t s, i64* zero = nullptr,
-                     u64 slot_elems = 0, u64 min_slots = 0);
+void launch_children(const RoundBuffers& b, int depth, int max_depth, cudaStream_t s);
 // Column sampling of this level: for every open node, the features that may
 // split it, as bits fmask[i * W + f / 32].  Nested exact-count selections
 // (the candidates with the smallest sample_hash, ties to the lower feature):
