@@ -334,11 +334,11 @@ def config_runs(torch, dp, device, peak_gbs: float, threads: int, cpu: bool) -> 
         d = dp.DMatrix.from_torch(x, y)
         torch.cuda.synchronize()
         dmatrix_ms = 1e3 * (time.perf_counter() - t0)
-        # the untimed run records the histogram launches' events; the timed
-        # run (identical trees) records none
+        # the untimed run records every instrumented launch's events (where
+        # a round's time goes); the timed run (identical trees) records none
         for timed in (False, True):
             b = dp.Booster(params, [d])
-            b.set_profiling(not timed, histograms_only=True)
+            b.set_profiling(not timed)
             ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             torch.cuda.synchronize()
             ev0.record()
@@ -347,7 +347,10 @@ def config_runs(torch, dp, device, peak_gbs: float, threads: int, cpu: bool) -> 
             ev1.record()
             torch.cuda.synchronize()
             if not timed:
-                hist = b.profile().get("histograms", {"launches": 0, "ms": 0.0, "alg_bytes": 0.0})
+                prof_all = b.profile()
+                hist = prof_all.get("histograms", {"launches": 0, "ms": 0.0, "alg_bytes": 0.0})
+                sections = {k: v["ms"] / rounds for k, v in prof_all.items()
+                            if isinstance(v, dict) and "ms" in v and "launches" in v}
                 b.free()
         ms = ev0.elapsed_time(ev1)
         trees = b.trees()
@@ -357,6 +360,10 @@ def config_runs(torch, dp, device, peak_gbs: float, threads: int, cpu: bool) -> 
                 "trees_per_round": K, "objective": hp["objective"], "ms_total": ms,
                 "ms_per_tree": ms / (rounds * K), "rows_trees_per_s": R * rounds * K / (ms / 1e3),
                 "dmatrix_ms": dmatrix_ms,
+                # per round, from the profiled run: the timed sections, and the
+                # rest of the round (bookkeeping kernels, launch gaps, the host)
+                "ms_per_round": {**{k: round(v, 4) for k, v in sorted(sections.items())},
+                                 "rest": round(ms / rounds - sum(sections.values()), 4)},
                 "histograms": {"launches": hist["launches"], "ms": hist["ms"],
                                "GBps": hist["alg_bytes"] / (hist["ms"] / 1e3) / 1e9 if hist["ms"] else 0.0,
                                "frac_hbm": (hist["alg_bytes"] / (hist["ms"] / 1e3) / 1e9 / peak_gbs)
@@ -721,6 +728,9 @@ def main() -> None:
     torch.cuda.synchronize()
     prof = {k: {**v, "launches_per_round": v["launches"] / breakdown_rounds, "ms_per_round": v["ms"] / breakdown_rounds}
             for k, v in b.profile().items() if isinstance(v, dict) and "ms" in v}
+    # the rest of a timed round: bookkeeping kernels (decisions, task lists,
+    # children, round start and read-back) and launch gaps
+    prof["rest"] = {"ms_per_round": ms / args.steps - sum(v["ms_per_round"] for v in prof.values())}
     host_ms = b.profile().get("host_ms")
     levels = per_level(b.profile().get("log", []))
     value = args.rows * args.steps / (ms / 1e3)
