@@ -182,8 +182,9 @@ Engine::Engine(DMatrix& d, const TrainParams& p, Comm* comm) : d_(d), p_(p), com
   // 128-byte lines, about four keep the blocks running at one time on
   // neighbouring rows (L2 reuse of lines shared by several nodes' rows; one
   // per SM was 50% slower for config 5 with 8 nodes); when rows are whole
-  // lines there is nothing to share and two halve the drains (config 4: 4.85
-  // against 4.91 ms per round with four, 5.36 with eight).  When it fits in
+  // lines there is nothing to share and fewer pieces drain less (config 4:
+  // 4.81 ms per round with three, 4.85 with two, 4.91 with four, 5.36 with
+  // eight).  When it fits in
   // L2, one per SM: a quarter of the pieces' drains (config 2: 0.64 against
   // 0.73 ms per round).  DP_HIST_TASKS_PER_SM overrides.
   {
@@ -191,7 +192,7 @@ Engine::Engine(DMatrix& d, const TrainParams& p, Comm* comm) : d_(d), p_(p), com
     DP_CUDA(cudaDeviceGetAttribute(&l2, cudaDevAttrL2CacheSize, device_));
     const bool in_l2 = u64(R_) * u64(F_) <= u64(l2) / 4 * 3;
     const bool whole_lines = q_->bin_stride % 128 == 0;  // no two rows share a 128-byte line
-    const u64 per_sm = in_l2 ? 1 : (whole_lines ? 2 : 4);
+    const u64 per_sm = in_l2 ? 1 : (whole_lines ? 3 : 4);
     hist_target_tasks_ = u32(sms_) * u32(std::max<u64>(1, env_u64("DP_HIST_TASKS_PER_SM", per_sm)));
   }
   // testing knobs: force the exact-count path of deep levels
