@@ -532,7 +532,7 @@ HistPlan* make_hist_plan(const uint8_t* bins, uint64_t bin_stride, uint32_t feat
          "invalid segment bounds (positions must be below 2^31)");
     total += dp::u64(seg_end[i] - seg_begin[i]);
   }
-  int64_t chunk = int64_t(dp::hist_chunk_rows(total * ftiles, dp::u64(nseg)));
+  int64_t chunk = int64_t(dp::hist_chunk_rows(total * ftiles, dp::u64(nseg), bin_stride % 128 == 0));
   // testing knob: longer tasks, so that tests reach the multi-window folds
   if (const char* c = std::getenv("DP_HIST_MIN_CHUNK")) chunk = std::max<int64_t>(chunk, std::atoll(c));
   // Queue order: piece index first, then segment, then feature tile.  With

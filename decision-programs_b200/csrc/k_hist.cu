@@ -764,7 +764,7 @@ void launch_histograms_wide(const u8* bins, u64 bin_stride, u32 F, bool quantize
   after_launch("histograms");
 }
 
-u64 hist_chunk_rows(u64 total_rows, u64 nseg) {
+u64 hist_chunk_rows(u64 total_rows, u64 nseg, bool whole_lines) {
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -773,9 +773,10 @@ u64 hist_chunk_rows(u64 total_rows, u64 nseg) {
   // order, the pieces of one row range run together, and smaller pieces keep
   // them within what L2 holds for each range (config 5, 8 nodes: 0.40 -> 0.45
   // of HBM at 256 bins, 0.41 -> 0.48 at 64 bins; with one node or 1024 the
-  // extra drains cost more: 0.57 -> 0.56, 0.37 -> 0.34).  DP_HIST_TASKS_PER_SM
-  // overrides.
-  u64 per_sm = (nseg >= 2 && nseg <= 16) ? 16 : 4;
+  // extra drains cost more: 0.57 -> 0.56, 0.37 -> 0.34).  Rows that are whole
+  // 128-byte lines share no line, so three, for fewer drains (10M x 128, one
+  // node: 0.529 against 0.552 ms).  DP_HIST_TASKS_PER_SM overrides.
+  u64 per_sm = whole_lines ? 3 : ((nseg >= 2 && nseg <= 16) ? 16 : 4);
   if (const char* v = std::getenv("DP_HIST_TASKS_PER_SM"))
     if (*v) per_sm = std::max<u64>(1, std::strtoull(v, nullptr, 10));
   const u64 target = u64(sms) * per_sm;

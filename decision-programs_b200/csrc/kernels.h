@@ -183,8 +183,9 @@ void launch_histograms_wide(const u8* bins, u64 bin_stride, u32 F, bool quantize
                             cudaStream_t s, const u32* ntasks_dev, const HistLayout* layout,
                             bool counter_zeroed = false);
 // Rows per histogram task for a launch over `total_rows` row-tiles of nseg
-// segments (about four tasks per SM, sixteen for 2 to 16 segments).
-u64 hist_chunk_rows(u64 total_rows, u64 nseg);
+// segments (about four tasks per SM, sixteen for 2 to 16 segments, three when
+// every row is whole 128-byte lines).
+u64 hist_chunk_rows(u64 total_rows, u64 nseg, bool whole_lines);
 // gh[k][r] (fp32 pairs) -> int32 pairs rint(g * s_g), rint(h * s_h), in place.
 void launch_quantize_gh(float2* gh, u64 R, int K, const Scales* scales, cudaStream_t s);
 

@@ -63,7 +63,7 @@ extern "C" int dp_hist_build_noalloc(const uint8_t* bins, uint64_t bin_stride, u
       total += dp::u64(seg_end[i] - seg_begin[i]);
       min_tasks += seg_end[i] > seg_begin[i] ? ftiles : 0;
     }
-    const int64_t chunk = int64_t(dp::hist_chunk_rows(total * ftiles, dp::u64(nseg)));
+    const int64_t chunk = int64_t(dp::hist_chunk_rows(total * ftiles, dp::u64(nseg), bin_stride % 128 == 0));
     dp::u64 ntasks = 0;
     for (int32_t i = 0; i < nseg; ++i) {
       const int64_t n = seg_end[i] - seg_begin[i];
