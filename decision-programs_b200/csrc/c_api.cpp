@@ -488,7 +488,7 @@ struct HistPlan {
   const uint8_t* bins = nullptr;
   uint64_t bin_stride = 0;
   uint32_t features = 0;
-  int num_bins = 256;
+  int kernel_bins = 256;         // bin budget of the 32-feature kernel launched
   bool quantized = false;
   int64_t* hist = nullptr;
   int32_t nseg = 0;
@@ -512,7 +512,6 @@ HistPlan* make_hist_plan(const uint8_t* bins, uint64_t bin_stride, uint32_t feat
   p->bins = bins;
   p->bin_stride = bin_stride;
   p->features = features;
-  p->num_bins = num_bins;
   p->quantized = quantized;
   p->hist = hist;
   p->nseg = nseg;
@@ -526,12 +525,14 @@ HistPlan* make_hist_plan(const uint8_t* bins, uint64_t bin_stride, uint32_t feat
             (wide_env && *wide_env ? std::string(wide_env) != "0" : wide_default);
   const dp::u32 tile = p->wide ? dp::kHistWideTile : dp::kHistFeatureTile;
   const dp::u32 ftiles = (features + tile - 1) / tile;
-  dp::u64 total = 0;
+  dp::u64 total = 0, filled = 0;
   for (int32_t i = 0; i < nseg; ++i) {
     need(seg_begin[i] >= 0 && seg_end[i] >= seg_begin[i] && seg_end[i] < (int64_t(1) << 31),
          "invalid segment bounds (positions must be below 2^31)");
     total += dp::u64(seg_end[i] - seg_begin[i]);
+    filled += seg_end[i] > seg_begin[i] ? 1 : 0;
   }
+  p->kernel_bins = dp::hist_kernel_bins(num_bins, filled);
   int64_t chunk = int64_t(dp::hist_chunk_rows(total * ftiles, dp::u64(nseg), bin_stride % 128 == 0));
   // testing knob: longer tasks, so that tests reach the multi-window folds
   if (const char* c = std::getenv("DP_HIST_MIN_CHUNK")) chunk = std::max<int64_t>(chunk, std::atoll(c));
@@ -578,8 +579,8 @@ void run_hist_plan(const HistPlan& p, cudaStream_t s) {
     dp::launch_histograms_wide(p.bins, p.bin_stride, p.features, p.quantized, p.trees.get(), p.scales.get(),
                                p.tasks.get(), p.ntasks, p.counter.get(), p.hist, s, nullptr, nullptr);
   else
-    dp::launch_histograms(p.bins, p.bin_stride, p.features, p.num_bins, p.quantized, p.trees.get(), p.scales.get(),
-                          p.tasks.get(), p.ntasks, p.counter.get(), p.hist, s);
+    dp::launch_histograms(p.bins, p.bin_stride, p.features, p.kernel_bins, p.quantized, p.trees.get(),
+                          p.scales.get(), p.tasks.get(), p.ntasks, p.counter.get(), p.hist, s);
 }
 
 }  // namespace

@@ -186,6 +186,18 @@ void launch_histograms_wide(const u8* bins, u64 bin_stride, u32 F, bool quantize
 // segments (about four tasks per SM, sixteen for 2 to 16 segments, three when
 // every row is whole 128-byte lines).
 u64 hist_chunk_rows(u64 total_rows, u64 nseg, bool whole_lines);
+// Bin budget of the 32-feature kernel that a kernel-level build launches when
+// its codes are below num_bins and `segments` segments hold rows.  The 64-bin
+// kernel (two 512-thread blocks per SM, int64 sums in shared memory) is the
+// faster one only from 2 to 256 segments; with one segment, or 512 and more,
+// the 256-bin kernel is.  Measured on B200, 100M x 32 rows, 64-bin codes
+// (16-bin codes the same within 1 %), 64-bin against 256-bin kernel: 1 node
+// 1.41 / 1.18 ms, 2 nodes 1.27 / 1.34, 8 nodes 1.40 / 1.50, 64 nodes 1.56 /
+// 1.62, 256 nodes 1.60 / 1.74, 512 nodes 1.80 / 1.69, 1024 nodes 2.22 / 1.88.
+// Both kernels give identical sums.
+inline int hist_kernel_bins(int num_bins, u64 segments) {
+  return (num_bins <= 64 && segments >= 2 && segments <= 256) ? num_bins : 256;
+}
 // gh[k][r] (fp32 pairs) -> int32 pairs rint(g * s_g), rint(h * s_h), in place.
 void launch_quantize_gh(float2* gh, u64 R, int K, const Scales* scales, cudaStream_t s);
 

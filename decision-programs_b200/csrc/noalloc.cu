@@ -56,12 +56,13 @@ extern "C" int dp_hist_build_noalloc(const uint8_t* bins, uint64_t bin_stride, u
     dp::need(bin_stride % 16 == 0 && bin_stride >= features,
              "bin_stride must cover the features and be a multiple of 16");
     const dp::u32 ftiles = (features + dp::kHistFeatureTile - 1) / dp::kHistFeatureTile;
-    dp::u64 total = 0, min_tasks = 0;
+    dp::u64 total = 0, min_tasks = 0, filled = 0;
     for (int32_t i = 0; i < nseg; ++i) {
       dp::need(seg_begin[i] >= 0 && seg_end[i] >= seg_begin[i] && seg_end[i] < (int64_t(1) << 31),
                "invalid segment bounds (positions must be below 2^31)");
       total += dp::u64(seg_end[i] - seg_begin[i]);
       min_tasks += seg_end[i] > seg_begin[i] ? ftiles : 0;
+      filled += seg_end[i] > seg_begin[i] ? 1 : 0;
     }
     const int64_t chunk = int64_t(dp::hist_chunk_rows(total * ftiles, dp::u64(nseg), bin_stride % 128 == 0));
     dp::u64 ntasks = 0;
@@ -122,8 +123,10 @@ extern "C" int dp_hist_build_noalloc(const uint8_t* bins, uint64_t bin_stride, u
     flush();
     const dp::u64 slot = dp::u64(features) * dp::kMaxBins * 2;
     if (nseg) dp::cuda_check(cudaMemsetAsync(hist, 0, dp::u64(nseg) * slot * sizeof(int64_t), s), "zero histograms");
-    dp::launch_histograms(bins, bin_stride, features, num_bins, false, scratch->trees, scratch->scales,
-                          scratch->tasks, dp::u32(written), &scratch->counter, hist, s);
+    // the same kernel as dp_hist_build for these segments
+    dp::launch_histograms(bins, bin_stride, features, dp::hist_kernel_bins(num_bins, filled), false,
+                          scratch->trees, scratch->scales, scratch->tasks, dp::u32(written), &scratch->counter, hist,
+                          s);
     dp::cuda_check(cudaStreamSynchronize(s), "histograms");
     return 0;
   } catch (const std::exception& e) {

@@ -125,7 +125,10 @@ def test_gradients_and_scales_match_oracle(dp, orc, objective, K):
 @pytest.mark.parametrize("F,nodes,seed,nbins,R", [(32, 1, 0, 256, 40000), (16, 3, 1, 256, 40000),
                                                  (64, 5, 2, 256, 40000), (100, 2, 3, 256, 40000),
                                                  (784, 2, 4, 256, 40000), (32, 1, 5, 64, 200000),
-                                                 (40, 4, 6, 16, 100000), (32, 2, 7, 256, 600000)])
+                                                 (40, 4, 6, 16, 100000), (32, 2, 7, 256, 600000),
+                                                 # 16- and 64-bin codes through the 256-bin kernel, which
+                                                 # builds one segment and 512 or more
+                                                 (24, 0, 8, 16, 150000), (32, 600, 9, 64, 300000)])
 def test_histograms_match_oracle(dp, orc, F, nodes, seed, nbins, R):
     rng = np.random.default_rng(seed)
     stride = (F + 15) // 16 * 16
