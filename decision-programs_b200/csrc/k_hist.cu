@@ -769,14 +769,18 @@ u64 hist_chunk_rows(u64 total_rows, u64 nseg, bool whole_lines) {
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   // Tasks per SM, balanced by the task queue: about four; sixteen for 2 to 16
-  // segments, whose rows interleave in the matrix: with the queue in piece
-  // order, the pieces of one row range run together, and smaller pieces keep
-  // them within what L2 holds for each range (config 5, 8 nodes: 0.40 -> 0.45
-  // of HBM at 256 bins, 0.41 -> 0.48 at 64 bins; with one node or 1024 the
-  // extra drains cost more: 0.57 -> 0.56, 0.37 -> 0.34).  Rows that are whole
-  // 128-byte lines share no line, so three, for fewer drains (10M x 128, one
-  // node: 0.529 against 0.552 ms).  DP_HIST_TASKS_PER_SM overrides.
-  u64 per_sm = whole_lines ? 3 : ((nseg >= 2 && nseg <= 16) ? 16 : 4);
+  // segments and eight for 17 to 256, whose rows interleave in the matrix:
+  // with the queue in piece order, the pieces of one row range run together,
+  // and smaller pieces keep them within what L2 holds for each range.  With
+  // one segment or more than 256 the extra drains cost more than that gains.
+  // Measured on B200, config 5 (100M x 32), ms at 4 / 8 / 16 tasks per SM:
+  // 256 bins, 8 nodes 1.68 / 1.55 / 1.51; 64 nodes 1.63 / 1.59 / 1.64; 256
+  // nodes 1.75 / 1.62 / 1.72; 1024 nodes 1.86 / 1.93 / 2.01 (1.86 at 2); 64
+  // bins, 64 nodes 1.56 / 1.48 / 1.46; 256 nodes 1.59 / 1.45 / 1.46; one node
+  // 0.57 of HBM at 4 against 0.56 at 16.  Rows that are whole 128-byte lines
+  // share no line, so three, for fewer drains (10M x 128, one node: 0.529
+  // against 0.552 ms).  DP_HIST_TASKS_PER_SM overrides.
+  u64 per_sm = whole_lines ? 3 : (nseg >= 2 && nseg <= 16) ? 16 : (nseg > 16 && nseg <= 256) ? 8 : 4;
   if (const char* v = std::getenv("DP_HIST_TASKS_PER_SM"))
     if (*v) per_sm = std::max<u64>(1, std::strtoull(v, nullptr, 10));
   const u64 target = u64(sms) * per_sm;

@@ -183,8 +183,8 @@ void launch_histograms_wide(const u8* bins, u64 bin_stride, u32 F, bool quantize
                             cudaStream_t s, const u32* ntasks_dev, const HistLayout* layout,
                             bool counter_zeroed = false);
 // Rows per histogram task for a launch over `total_rows` row-tiles of nseg
-// segments (about four tasks per SM, sixteen for 2 to 16 segments, three when
-// every row is whole 128-byte lines).
+// segments (about four tasks per SM, sixteen for 2 to 16 segments, eight for
+// 17 to 256, three when every row is whole 128-byte lines).
 u64 hist_chunk_rows(u64 total_rows, u64 nseg, bool whole_lines);
 // Bin budget of the 32-feature kernel that a kernel-level build launches when
 // its codes are below num_bins and `segments` segments hold rows.  The 64-bin
