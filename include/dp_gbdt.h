@@ -188,7 +188,9 @@ DP_API int dp_gradients(int objective, int num_class, const float* margin, const
                         float* gh, float* scales, void* stream);
 /* hist[nseg][F][256][2] (int64, overwritten) of position segments
  * [seg_begin[i], seg_end[i]) (host arrays) of (ridx, gh) in position order.
- * Every bin code must be < num_bins (1..256); codes at or above it are skipped. */
+ * Every bin code must be < num_bins (1..256).  num_bins and the segment count
+ * select the kernel, so a code at or above num_bins is outside the contract:
+ * it may be counted in its own bin or dropped. */
 DP_API int dp_hist_build(const uint8_t* bins, uint64_t bin_stride, uint32_t features, int32_t num_bins,
                          const float* gh, const uint32_t* ridx, const int64_t* seg_begin, const int64_t* seg_end,
                          int32_t nseg, float sg, float sh, int64_t* hist, void* stream);
