@@ -18,6 +18,9 @@ roofline histogram kernel: algorithmic bytes rows*(F + 12) + slots*F*256*16
 The reference arm (--impl reference) times the CPU oracle: the reference
 repository trains only through an external GPU library that is absent here,
 so the restatement of the same algorithm is the CPU implementation of the path.
+cpu_third_party (one GPU, rank 0): scikit-learn's HistGradientBoostingRegressor
+on a 2M-row sample of the same data, a tuned CPU library for context; it is not
+the parity oracle.
 """
 from __future__ import annotations
 
@@ -240,11 +243,56 @@ def config4_cpu_leg(torch, first_trees: list[dict]) -> dict:
     m.train_more(C4_PARITY_TREES)
     dt = time.perf_counter() - t0
     same = same_trees(first_trees, m)
-    del m, x, y
-    return {"value": ROWS * C4_PARITY_TREES / dt, "unit": "rows*trees/s", "cores": threads, "kind": "port",
-            "sample": f"the whole config-4 workload ({ROWS} rows, data {where}), the first {C4_PARITY_TREES} "
-                      f"depth-10 trees (C++ oracle, {threads} threads, {dt:.1f} s; cuts and bins built before)",
-            "trees_identical_to_oracle": same, "trees_compared": C4_PARITY_TREES}
+    del m
+    third = sklearn_leg(x, y, threads)
+    del x, y
+    out = {"value": ROWS * C4_PARITY_TREES / dt, "unit": "rows*trees/s", "cores": threads, "kind": "port",
+           "sample": f"the whole config-4 workload ({ROWS} rows, data {where}), the first {C4_PARITY_TREES} "
+                     f"depth-10 trees (C++ oracle, {threads} threads, {dt:.1f} s; cuts and bins built before)",
+           "trees_identical_to_oracle": same, "trees_compared": C4_PARITY_TREES}
+    if third is not None:
+        out["third_party"] = third
+    return out
+
+
+SKLEARN_ROWS = 2_000_000
+SKLEARN_TREES = 4
+
+
+def sklearn_leg(x, y, threads: int):
+    """A tuned third-party CPU implementation of the same algorithm, for
+    context beside the oracle: scikit-learn's HistGradientBoostingRegressor
+    (histograms with sibling subtraction, depth-wise limit 10, lambda 1, eta
+    0.3, 255 value bins) on the first SKLEARN_ROWS rows of the config-4 data.
+    Binning is excluded: the time per tree is the difference between fits of
+    1 + SKLEARN_TREES trees and of one tree.  It is not the parity oracle and
+    its trees differ (its own binning and tie rules).  None when scikit-learn
+    is not installed."""
+    try:
+        import sklearn
+        from sklearn.ensemble import HistGradientBoostingRegressor
+        from threadpoolctl import threadpool_limits
+    except ImportError:
+        return None
+    xs, ys = np.ascontiguousarray(x[:SKLEARN_ROWS]), np.ascontiguousarray(y[:SKLEARN_ROWS])
+
+    def fit(trees: int) -> float:
+        h = HistGradientBoostingRegressor(max_iter=trees, max_depth=DEPTH, max_leaf_nodes=None, max_bins=255,
+                                          learning_rate=0.3, l2_regularization=1.0, min_samples_leaf=1,
+                                          early_stopping=False)
+        t0 = time.perf_counter()
+        h.fit(xs, ys)
+        return time.perf_counter() - t0
+
+    with threadpool_limits(limits=threads):
+        t1 = fit(1)
+        tn = fit(1 + SKLEARN_TREES)
+    per_tree = max(tn - t1, 1e-9) / SKLEARN_TREES
+    return {"value": SKLEARN_ROWS / per_tree, "unit": "rows*trees/s", "cores": threads,
+            "impl": f"scikit-learn {sklearn.__version__} HistGradientBoostingRegressor",
+            "sample": f"first {SKLEARN_ROWS} rows of the config-4 data, depth-10 trees; time per tree = "
+                      f"(fit of {1 + SKLEARN_TREES} trees - fit of 1) / {SKLEARN_TREES}, binning excluded",
+            "seconds_per_tree": per_tree}
 
 
 # --------------------------------------------------------------------------- configs 1-3
@@ -838,7 +886,10 @@ def main() -> None:
     if cpu is not None:
         line["trees_identical_to_oracle"] = cpu.pop("trees_identical_to_oracle")
         line["trees_compared"] = cpu.pop("trees_compared")
+        third = cpu.pop("third_party", None)
         line["cpu_baseline"] = cpu
+        if third is not None:
+            line["cpu_third_party"] = third
     if sweep is not None:
         line["hist_sweep"] = sweep
     if configs is not None:

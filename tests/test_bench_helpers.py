@@ -40,3 +40,17 @@ def test_per_level_reads_the_launch_log():
     assert bench.per_level(log[:8]) == [{"histograms": 2.0, "eval_splits": 0.5, "partition": 0.25},
                                         {"histograms": 1.5, "exchange_hist": 0.75, "partition": 0.1,
                                          "leaf_update": 0.2}]
+
+
+def test_sklearn_leg_reports_time_per_tree(monkeypatch):
+    pytest.importorskip("sklearn")
+    import bench
+    monkeypatch.setattr(bench, "SKLEARN_ROWS", 4000)
+    monkeypatch.setattr(bench, "SKLEARN_TREES", 2)
+    rng = np.random.default_rng(3)
+    x = rng.standard_normal((6000, 8)).astype(np.float32)
+    y = (x[:, 0] + 0.1 * rng.standard_normal(6000)).astype(np.float32)
+    out = bench.sklearn_leg(x, y, 2)
+    assert out["unit"] == "rows*trees/s" and out["cores"] == 2
+    assert out["value"] > 0 and out["seconds_per_tree"] > 0
+    assert "4000 rows" in out["sample"] and out["impl"].startswith("scikit-learn")
