@@ -284,9 +284,12 @@ def sklearn_leg(x, y, threads: int):
         h.fit(xs, ys)
         return time.perf_counter() - t0
 
-    with threadpool_limits(limits=threads):
-        t1 = fit(1)
-        tn = fit(1 + SKLEARN_TREES)
+    try:
+        with threadpool_limits(limits=threads):
+            t1 = fit(1)
+            tn = fit(1 + SKLEARN_TREES)
+    except Exception as e:  # context only: never cost the bench line
+        return {"error": f"{type(e).__name__}: {e}"[:200]}
     per_tree = max(tn - t1, 1e-9) / SKLEARN_TREES
     return {"value": SKLEARN_ROWS / per_tree, "unit": "rows*trees/s", "cores": threads,
             "impl": f"scikit-learn {sklearn.__version__} HistGradientBoostingRegressor",
