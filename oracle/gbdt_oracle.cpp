@@ -382,52 +382,97 @@ void quantizer(const float* gh, uint64_t R, float* sg, float* sh, const Comm& co
 static inline int64_t qv(float v, float s) { return int64_t(std::rint(v * s)); }
 
 // Histogram of one row segment: hist[F][256][2] += (q_g, q_h).  `ghp` is in
-// position order (ghp[i] belongs to row ridx[i]).
+// position order (ghp[i] belongs to row ridx[i]).  The rows are taken in
+// blocks, and each block is added one tile of features at a time, so that the
+// tile's cells (8 features x 256 bins x 16 bytes) stay in the first-level
+// cache instead of every row touching all F features' cells.  The sums are
+// exact integers, so the order of the additions does not change them.
 static void hist_segment(const uint8_t* bins, uint64_t bstride, uint32_t F, const float* ghp, const uint32_t* ridx,
                          int64_t begin, int64_t end, float sg, float sh, int64_t* hist) {
-  for (int64_t i = begin; i < end; ++i) {
-    const uint8_t* row = bins + uint64_t(ridx[i]) * bstride;
-    const int64_t g = qv(ghp[2 * i], sg), h = qv(ghp[2 * i + 1], sh);
-    for (uint32_t f = 0; f < F; ++f) {
-      int64_t* cell = hist + (size_t(f) * 256 + row[f]) * 2;
-      cell[0] += g;
-      cell[1] += h;
+  constexpr int64_t kRowBlock = 2048;
+  constexpr uint32_t kFeatTile = 8;
+  const uint8_t* rows[kRowBlock];
+  int64_t q[2 * kRowBlock];
+  for (int64_t b0 = begin; b0 < end; b0 += kRowBlock) {
+    const int64_t n = std::min(kRowBlock, end - b0);
+    for (int64_t i = 0; i < n; ++i) {
+      rows[i] = bins + uint64_t(ridx[b0 + i]) * bstride;
+      q[2 * i] = qv(ghp[2 * (b0 + i)], sg);
+      q[2 * i + 1] = qv(ghp[2 * (b0 + i) + 1], sh);
+    }
+    for (uint32_t f0 = 0; f0 < F; f0 += kFeatTile) {
+      const uint32_t f1 = std::min(F, f0 + kFeatTile);
+      for (int64_t i = 0; i < n; ++i) {
+        const uint8_t* row = rows[i];
+        const int64_t g = q[2 * i], h = q[2 * i + 1];
+        for (uint32_t f = f0; f < f1; ++f) {
+          int64_t* cell = hist + (size_t(f) * 256 + row[f]) * 2;
+          cell[0] += g;
+          cell[1] += h;
+        }
+      }
     }
   }
 }
 
-// Histograms of several segments, threaded; out[N][F][256][2] is overwritten.
+// Histograms of several segments, threaded; outs[s] (F x 256 x 2 int64) is
+// overwritten for every segment s.  A segment of at most one chunk is built by
+// one task straight into its output; a longer one is split into chunks whose
+// sums each thread gathers in its own buffer and adds under the segment's
+// lock.  The sums are exact integers, so neither the split nor the order of
+// the merges changes them.
+void histograms_into(const uint8_t* bins, uint64_t bstride, uint32_t F, const float* ghp, const uint32_t* ridx,
+                     const int64_t* seg_begin, const int64_t* seg_end, int64_t nseg, float sg, float sh,
+                     int64_t* const* outs, int threads) {
+  const size_t hsz = size_t(F) * 256 * 2;
+  const int64_t kChunk = 1 << 15;
+  struct Task { int64_t seg, b, e; bool whole; };
+  std::vector<Task> tasks;
+  std::vector<int64_t> shared_segs;  // segments of several tasks
+  for (int64_t s = 0; s < nseg; ++s) {
+    const bool whole = seg_end[s] - seg_begin[s] <= kChunk;
+    if (!whole) shared_segs.push_back(s);
+    if (whole) tasks.push_back({s, seg_begin[s], seg_end[s], true});
+    else
+      for (int64_t b = seg_begin[s]; b < seg_end[s]; b += kChunk)
+        tasks.push_back({s, b, std::min(seg_end[s], b + kChunk), false});
+  }
+  parallel_tasks(int64_t(shared_segs.size()), threads,
+                 [&](int64_t i, int) { std::fill(outs[shared_segs[i]], outs[shared_segs[i]] + hsz, 0); });
+  threads = std::max(1, threads);
+  std::vector<std::vector<int64_t>> priv(static_cast<size_t>(threads));
+  std::vector<std::unique_ptr<std::atomic<int>>> lock(size_t(std::max<int64_t>(nseg, 0)));
+  for (auto& l : lock) l = std::make_unique<std::atomic<int>>(0);
+  parallel_tasks(int64_t(tasks.size()), threads, [&](int64_t ti, int t) {
+    const Task& tk = tasks[ti];
+    if (tk.whole) {
+      std::fill(outs[tk.seg], outs[tk.seg] + hsz, 0);
+      hist_segment(bins, bstride, F, ghp, ridx, tk.b, tk.e, sg, sh, outs[tk.seg]);
+      return;
+    }
+    std::vector<int64_t>& local = priv[size_t(t)];
+    if (local.empty()) local.assign(hsz, 0);
+    hist_segment(bins, bstride, F, ghp, ridx, tk.b, tk.e, sg, sh, local.data());
+    auto& l = *lock[size_t(tk.seg)];
+    int expected = 0;
+    while (!l.compare_exchange_weak(expected, 1)) expected = 0;
+    int64_t* dst = outs[tk.seg];
+    for (size_t j = 0; j < hsz; ++j) {
+      dst[j] += local[j];
+      local[j] = 0;
+    }
+    l.store(0);
+  });
+}
+
+// The same with out[N][F][256][2] contiguous.
 void histograms(const uint8_t* bins, uint64_t bstride, uint32_t F, const float* ghp, const uint32_t* ridx,
                 const int64_t* seg_begin, const int64_t* seg_end, int64_t nseg, float sg, float sh, int64_t* out,
                 int threads) {
   const size_t hsz = size_t(F) * 256 * 2;
-  std::fill(out, out + hsz * nseg, 0);
-  const int64_t kChunk = 1 << 15;
-  struct Task { int64_t seg, b, e; };
-  std::vector<Task> tasks;
-  for (int64_t s = 0; s < nseg; ++s)
-    for (int64_t b = seg_begin[s]; b < seg_end[s]; b += kChunk) tasks.push_back({s, b, std::min(seg_end[s], b + kChunk)});
-  if (threads <= 1 || tasks.size() <= 1) {
-    for (auto& t : tasks) hist_segment(bins, bstride, F, ghp, ridx, t.b, t.e, sg, sh, out + hsz * t.seg);
-    return;
-  }
-  // Each thread owns a private histogram per touched segment; integer sums
-  // make the merge order irrelevant.
-  std::vector<std::vector<int64_t>> priv(threads);
-  std::vector<std::vector<int64_t>> priv_seg(threads);
-  std::vector<std::unique_ptr<std::atomic<int>>> lock(nseg);
-  for (auto& l : lock) l = std::make_unique<std::atomic<int>>(0);
-  parallel_tasks(int64_t(tasks.size()), threads, [&](int64_t ti, int t) {
-    const Task& tk = tasks[ti];
-    std::vector<int64_t> local(hsz, 0);
-    hist_segment(bins, bstride, F, ghp, ridx, tk.b, tk.e, sg, sh, local.data());
-    auto& l = *lock[tk.seg];
-    int expected = 0;
-    while (!l.compare_exchange_weak(expected, 1)) expected = 0;
-    int64_t* dst = out + hsz * tk.seg;
-    for (size_t j = 0; j < hsz; ++j) dst[j] += local[j];
-    l.store(0);
-  });
+  std::vector<int64_t*> outs(size_t(std::max<int64_t>(nseg, 0)));
+  for (int64_t s = 0; s < nseg; ++s) outs[size_t(s)] = out + hsz * size_t(s);
+  histograms_into(bins, bstride, F, ghp, ridx, seg_begin, seg_end, nseg, sg, sh, outs.data(), threads);
 }
 
 struct Params {
@@ -613,31 +658,57 @@ Tree grow_tree(const uint8_t* bins, uint64_t bstride, uint32_t F, uint64_t R, co
     }
     if (split_idx.empty()) { open.clear(); break; }
     // Stable partition of every split node's segment; children get ids in order.
+    // Each segment is cut into chunks: the chunks count their left rows, a
+    // prefix over them places each chunk's left and right rows, and the
+    // chunks scatter in parallel, keeping the rows' order on each side.
     std::vector<int64_t> nleft(split_idx.size());
-    parallel_tasks(int64_t(split_idx.size()), p.threads, [&](int64_t j, int) {
-      const Open& o = open[split_idx[j]];
-      const Split& s = splits[split_idx[j]];
-      const bool hm = c.has_missing[s.feature];
-      int64_t l = o.begin, cnt = 0;
-      for (int64_t i = o.begin; i < o.begin + o.count; ++i) {
-        const uint8_t b = bins[uint64_t(ridx[i]) * bstride + s.feature];
-        const bool left = (hm && b == kMissingBin) ? bool(s.default_left) : (b <= s.bin);
-        if (left) { ridx2[l] = ridx[i]; ghp2[2 * l] = ghp[2 * i]; ghp2[2 * l + 1] = ghp[2 * i + 1]; ++l; ++cnt; }
+    {
+      const int64_t kPartChunk = 1 << 16;
+      struct PTask { size_t j; int64_t b, e, nl, lpos, rpos; };
+      std::vector<PTask> pt;
+      for (size_t j = 0; j < split_idx.size(); ++j) {
+        const Open& o = open[split_idx[j]];
+        for (int64_t b = o.begin; b < o.begin + o.count; b += kPartChunk)
+          pt.push_back({j, b, std::min(o.begin + o.count, b + kPartChunk), 0, 0, 0});
       }
-      int64_t r = l;
-      for (int64_t i = o.begin; i < o.begin + o.count; ++i) {
+      auto goes_left = [&](size_t j, int64_t i) {
+        const Split& s = splits[split_idx[j]];
         const uint8_t b = bins[uint64_t(ridx[i]) * bstride + s.feature];
-        const bool left = (hm && b == kMissingBin) ? bool(s.default_left) : (b <= s.bin);
-        if (!left) { ridx2[r] = ridx[i]; ghp2[2 * r] = ghp[2 * i]; ghp2[2 * r + 1] = ghp[2 * i + 1]; ++r; }
+        return (c.has_missing[s.feature] && b == kMissingBin) ? bool(s.default_left) : (b <= s.bin);
+      };
+      parallel_tasks(int64_t(pt.size()), p.threads, [&](int64_t k, int) {
+        PTask& t = pt[size_t(k)];
+        for (int64_t i = t.b; i < t.e; ++i) t.nl += goes_left(t.j, i) ? 1 : 0;
+      });
+      for (size_t k = 0; k < pt.size(); ++k) nleft[pt[k].j] += pt[k].nl;
+      std::vector<int64_t> lcur(split_idx.size()), rcur(split_idx.size());
+      for (size_t j = 0; j < split_idx.size(); ++j) {
+        lcur[j] = open[split_idx[j]].begin;
+        rcur[j] = open[split_idx[j]].begin + nleft[j];
       }
-      nleft[j] = cnt;
-    });
+      for (auto& t : pt) {  // chunks of a segment are consecutive, in row order
+        t.lpos = lcur[t.j];
+        t.rpos = rcur[t.j];
+        lcur[t.j] += t.nl;
+        rcur[t.j] += (t.e - t.b) - t.nl;
+      }
+      parallel_tasks(int64_t(pt.size()), p.threads, [&](int64_t k, int) {
+        const PTask& t = pt[size_t(k)];
+        int64_t l = t.lpos, r = t.rpos;
+        for (int64_t i = t.b; i < t.e; ++i) {
+          const int64_t d = goes_left(t.j, i) ? l++ : r++;
+          ridx2[d] = ridx[i];
+          ghp2[2 * d] = ghp[2 * i];
+          ghp2[2 * d + 1] = ghp[2 * i + 1];
+        }
+      });
+    }
     // Copy split segments back (rows of leaves stay where they are).
-    for (size_t j = 0; j < split_idx.size(); ++j) {
-      const Open& o = open[split_idx[j]];
+    parallel_tasks(int64_t(split_idx.size()), p.threads, [&](int64_t j, int) {
+      const Open& o = open[split_idx[size_t(j)]];
       std::copy(ridx2.begin() + o.begin, ridx2.begin() + o.begin + o.count, ridx.begin() + o.begin);
       std::copy(ghp2.begin() + 2 * o.begin, ghp2.begin() + 2 * (o.begin + o.count), ghp.begin() + 2 * o.begin);
-    }
+    });
     // Row counts over all ranks decide which child is built directly.
     std::vector<int64_t> gcnt(2 * split_idx.size());
     for (size_t j = 0; j < split_idx.size(); ++j) {
@@ -684,19 +755,32 @@ Tree grow_tree(const uint8_t* bins, uint64_t bstride, uint32_t F, uint64_t R, co
         sb.push_back(next[small_idx[k]].begin);
         se.push_back(next[small_idx[k]].begin + next[small_idx[k]].count);
       }
-      std::vector<int64_t> hs(hsz * small_idx.size());
-      histograms(bins, bstride, F, ghp.data(), ridx.data(), sb.data(), se.data(), int64_t(small_idx.size()), sg, sh,
-                 hs.data(), p.threads);
-      comm.sum(hs.data(), int64_t(hs.size()));
-      for (size_t k = 0; k < small_idx.size(); ++k)
-        next[small_idx[k]].hist.assign(hs.begin() + hsz * k, hs.begin() + hsz * (k + 1));
+      if (comm.fn) {
+        // row-sharded: the level's built histograms go through one exchange
+        std::vector<int64_t> hs(hsz * small_idx.size());
+        histograms(bins, bstride, F, ghp.data(), ridx.data(), sb.data(), se.data(), int64_t(small_idx.size()), sg,
+                   sh, hs.data(), p.threads);
+        comm.sum(hs.data(), int64_t(hs.size()));
+        for (size_t k = 0; k < small_idx.size(); ++k)
+          next[small_idx[k]].hist.assign(hs.begin() + hsz * k, hs.begin() + hsz * (k + 1));
+      } else {
+        // built straight into the children's storage
+        std::vector<int64_t*> outs(small_idx.size());
+        parallel_tasks(int64_t(small_idx.size()), p.threads, [&](int64_t k, int) {
+          next[small_idx[size_t(k)]].hist.resize(hsz);
+          outs[size_t(k)] = next[small_idx[size_t(k)]].hist.data();
+        });
+        histograms_into(bins, bstride, F, ghp.data(), ridx.data(), sb.data(), se.data(), int64_t(small_idx.size()),
+                        sg, sh, outs.data(), p.threads);
+      }
       if (p.subtract) {
-        for (size_t j = 0; j < split_idx.size(); ++j) {
+        parallel_tasks(int64_t(split_idx.size()), p.threads, [&](int64_t jj, int) {
+          const size_t j = size_t(jj);
           const Open& par = open[split_idx[j]];
-          size_t sm = small_idx[j], lg = (sm == 2 * j) ? 2 * j + 1 : 2 * j;
+          const size_t sm = small_idx[j], lg = (sm == 2 * j) ? 2 * j + 1 : 2 * j;
           next[lg].hist.resize(hsz);
           for (size_t q = 0; q < hsz; ++q) next[lg].hist[q] = par.hist[q] - next[sm].hist[q];
-        }
+        });
       }
     }
     open = std::move(next);

@@ -62,7 +62,9 @@ def test_two_gloo_ranks_grow_the_trees_of_one_rank(orc, objective, K, nan_frac):
     else:
         y = (signal + 0.1 * rng.standard_normal(R)).astype(np.float32)
     kw = dict(objective=objective, num_class=K, max_depth=5, rounds=3, threads=2)
-    with mp.Manager() as manager:
+    # the manager's server process is spawned too: forking a process that
+    # already runs threads (the oracle's, OpenMP's) can deadlock the child
+    with mp.get_context("spawn").Manager() as manager:
         out = manager.dict()
         mp.spawn(_gloo_worker.run, args=(2, free_port(), x, y, kw, out), nprocs=2, join=True)
         got = dict(out)
