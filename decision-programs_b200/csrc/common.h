@@ -11,6 +11,7 @@
 #include <utility>
 #include <stdexcept>
 #include <string>
+#include <string_view>
 #include <vector>
 
 namespace dp {
@@ -27,6 +28,23 @@ struct Error : std::runtime_error {
 };
 
 [[noreturn]] inline void fail(const std::string& msg) { throw Error(msg); }
+// Caller-supplied text quoted in an error message, as printable ASCII (other
+// bytes as \xHH), so that the message stays plain text whatever was passed.
+inline std::string printable(std::string_view s) {
+  static const char kHex[] = "0123456789abcdef";
+  std::string o;
+  for (const char ch : s) {
+    const unsigned char c = static_cast<unsigned char>(ch);
+    if (c >= 0x20 && c < 0x7f) {
+      o.push_back(ch);
+    } else {
+      o += "\\x";
+      o.push_back(kHex[c >> 4]);
+      o.push_back(kHex[c & 15]);
+    }
+  }
+  return o;
+}
 // Sets the thread-local message returned by XGBGetLastError (defined beside it).
 void set_last_error(const std::string& msg);
 inline void need(bool ok, const std::string& msg) {

@@ -10,6 +10,7 @@
 
 namespace dp::json {
 
+
 bool Value::as_bool() const {
   if (kind_ == Kind::Bool) return b_;
   if (kind_ == Kind::Number && (d_ == 0.0 || d_ == 1.0)) return d_ != 0.0;
@@ -24,7 +25,7 @@ std::int64_t Value::as_int() const {
   if (!s_.empty() && s_.find_first_of(".eE") == std::string::npos) {
     std::int64_t v = 0;
     auto r = std::from_chars(s_.data(), s_.data() + s_.size(), v);
-    need(r.ec == std::errc{} && r.ptr == s_.data() + s_.size(), "JSON integer out of range: " + s_);
+    need(r.ec == std::errc{} && r.ptr == s_.data() + s_.size(), "JSON integer out of range: " + printable(s_));
     return v;
   }
   need(std::isfinite(d_) && d_ == std::floor(d_) && std::fabs(d_) < 9.0e15, "JSON number is not an integer");
@@ -35,7 +36,7 @@ std::uint64_t Value::as_uint() const {
   if (!s_.empty() && s_.find_first_of(".eE-") == std::string::npos) {
     std::uint64_t v = 0;
     auto r = std::from_chars(s_.data(), s_.data() + s_.size(), v);
-    need(r.ec == std::errc{} && r.ptr == s_.data() + s_.size(), "JSON integer out of range: " + s_);
+    need(r.ec == std::errc{} && r.ptr == s_.data() + s_.size(), "JSON integer out of range: " + printable(s_));
     return v;
   }
   std::int64_t v = as_int();
@@ -67,7 +68,7 @@ const Value* Value::find(const std::string& key) const {
 }
 const Value& Value::at(const std::string& key) const {
   const Value* v = find(key);
-  need(v != nullptr, "missing JSON key: " + key);
+  need(v != nullptr, "missing JSON key: " + printable(key));
   return *v;
 }
 size_t Value::size() const {
@@ -236,6 +237,21 @@ class Parser {
       return a;
     }
   }
+  // The value of four hex digits at `at`.
+  unsigned hex4(size_t at) const {
+    need(at + 4 <= t_.size(), "bad JSON unicode escape");
+    unsigned v = 0;
+    for (size_t k = 0; k < 4; ++k) {
+      const char h = t_[at + k];
+      const int d = (h >= '0' && h <= '9')   ? h - '0'
+                    : (h >= 'a' && h <= 'f') ? h - 'a' + 10
+                    : (h >= 'A' && h <= 'F') ? h - 'A' + 10
+                                             : -1;
+      need(d >= 0, "bad JSON unicode escape");
+      v = v * 16 + unsigned(d);
+    }
+    return v;
+  }
   std::string str() {
     ++i_;
     std::string out;
@@ -254,13 +270,31 @@ class Parser {
         case 'r': out.push_back('\r'); break;
         case 't': out.push_back('\t'); break;
         case 'u': {
-          need(i_ + 4 <= t_.size(), "bad JSON unicode escape");
-          unsigned cp = unsigned(std::strtoul(std::string(t_.substr(i_, 4)).c_str(), nullptr, 16));
+          // four hex digits; a high surrogate must be followed by an escaped
+          // low one, and the pair is one code point; a lone surrogate is refused
+          unsigned cp = hex4(i_);
           i_ += 4;
-          if (cp < 0x80) out.push_back(char(cp));
-          else if (cp < 0x800) { out.push_back(char(0xC0 | (cp >> 6))); out.push_back(char(0x80 | (cp & 0x3F))); }
-          else {
+          if (cp >= 0xD800 && cp <= 0xDBFF) {
+            need(i_ + 2 <= t_.size() && t_[i_] == '\\' && t_[i_ + 1] == 'u', "bad JSON unicode escape");
+            const unsigned lo = hex4(i_ + 2);
+            need(lo >= 0xDC00 && lo <= 0xDFFF, "bad JSON unicode escape");
+            i_ += 6;
+            cp = 0x10000 + ((cp - 0xD800) << 10) + (lo - 0xDC00);
+          } else {
+            need(cp < 0xDC00 || cp > 0xDFFF, "bad JSON unicode escape");
+          }
+          if (cp < 0x80) {
+            out.push_back(char(cp));
+          } else if (cp < 0x800) {
+            out.push_back(char(0xC0 | (cp >> 6)));
+            out.push_back(char(0x80 | (cp & 0x3F)));
+          } else if (cp < 0x10000) {
             out.push_back(char(0xE0 | (cp >> 12)));
+            out.push_back(char(0x80 | ((cp >> 6) & 0x3F)));
+            out.push_back(char(0x80 | (cp & 0x3F)));
+          } else {
+            out.push_back(char(0xF0 | (cp >> 18)));
+            out.push_back(char(0x80 | ((cp >> 12) & 0x3F)));
             out.push_back(char(0x80 | ((cp >> 6) & 0x3F)));
             out.push_back(char(0x80 | (cp & 0x3F)));
           }
@@ -279,11 +313,11 @@ class Parser {
     while (i_ < t_.size() && ((t_[i_] >= '0' && t_[i_] <= '9') || t_[i_] == '.' || t_[i_] == 'e' ||
                               t_[i_] == 'E' || t_[i_] == '-' || t_[i_] == '+'))
       ++i_;
-    need(i_ > b, std::string("invalid JSON token near: ") + std::string(t_.substr(b, 16)));
+    need(i_ > b, std::string("invalid JSON token near: ") + printable(t_.substr(b, 16)));
     std::string text(t_.substr(b, i_ - b));
     char* end = nullptr;
     double d = std::strtod(text.c_str(), &end);
-    need(end == text.c_str() + text.size(), "invalid JSON number: " + text);
+    need(end == text.c_str() + text.size(), "invalid JSON number: " + printable(text));
     return Value::number(d, text);
   }
 };

@@ -10,6 +10,7 @@
 // successors (native/class_native_source_contract.hpp:26-33), and the
 // configuration keys learner.generic_param.device and
 // learner.gradient_booster.updater[0].name (native/class_model_train.cu:48).
+#include <algorithm>
 #include <cmath>
 #include <cstdio>
 #include <string>
@@ -30,20 +31,21 @@ double to_double(const std::string& key, const std::string& v) {
   const std::string s = unquote(v);
   char* end = nullptr;
   const double d = std::strtod(s.c_str(), &end);
-  need(!s.empty() && end == s.c_str() + s.size(), "invalid numeric value for parameter " + key + ": " + v);
+  need(!s.empty() && end == s.c_str() + s.size(),
+       "invalid numeric value for parameter " + printable(key) + ": " + printable(v));
   return d;
 }
 
 long long to_int(const std::string& key, const std::string& v) {
   const double d = to_double(key, v);
   need(std::isfinite(d) && d == std::floor(d) && std::fabs(d) < 9.0e15,
-       "parameter " + key + " must be an integer: " + v);
+       "parameter " + printable(key) + " must be an integer: " + printable(v));
   return static_cast<long long>(d);
 }
 
 void range(const std::string& key, double v, double lo, double hi, bool strict_lo = false) {
   need(std::isfinite(v) && (strict_lo ? v > lo : v >= lo) && v <= hi,
-       "parameter " + key + " is outside its supported range");
+       "parameter " + printable(key) + " is outside its supported range");
 }
 
 }  // namespace
@@ -53,7 +55,7 @@ int TrainParams::objective_id() const {
   if (objective == "binary:logistic") return kLogistic;
   if (objective == "multi:softprob") return kSoftprob;
   if (objective == "multi:softmax") return kSoftmax;
-  fail("unsupported objective: " + objective);
+  fail("unsupported objective: " + printable(objective));
 }
 
 float TrainParams::base_margin(int k) const {
@@ -71,7 +73,7 @@ void TrainParams::set(const std::string& key, const std::string& value) {
   const std::string v = unquote(value);
   if (key == "objective") {
     need(v == "reg:squarederror" || v == "binary:logistic" || v == "multi:softprob" || v == "multi:softmax",
-         "unsupported objective: " + v);
+         "unsupported objective: " + printable(v));
     objective = v;
   } else if (key == "num_class") {
     const long long n = to_int(key, v);
@@ -292,7 +294,9 @@ void model_from_json(const std::string& text, Model& m, TrainParams& p) {
   TrainParams q = p;
   q.objective = learner.at("objective").at("name").as_string();
   (void)q.objective_id();
-  q.num_class = int(dec(lmp.at("num_class")));
+  const long long num_class = dec(lmp.at("num_class"));
+  need(num_class >= 0 && num_class <= (1 << 24), "num_class is outside its supported range");
+  q.num_class = int(num_class);
   if (const auto* bs = lmp.find("base_score")) {
     json::Value b = bs->is_string() ? json::parse(bs->as_string()) : *bs;
     q.base_score.clear();
@@ -308,7 +312,9 @@ void model_from_json(const std::string& text, Model& m, TrainParams& p) {
   for (size_t i = 0; i < trees.size(); ++i) {
     const auto& tj = trees[i];
     Tree t;
-    t.klass = int(info[i].as_int());
+    const long long klass = info[i].as_int();
+    need(klass >= 0 && klass < std::max(1, q.K()), "tree_info names a class outside num_class");
+    t.klass = int(klass);
     auto ints = [&](const char* k) {
       std::vector<i32> v;
       for (const auto& x : tj.at(k).items()) v.push_back(i32(x.as_int()));
@@ -355,6 +361,12 @@ void model_from_json(const std::string& text, Model& m, TrainParams& p) {
   need(!out.iteration_indptr.empty() && out.iteration_indptr.front() == 0 &&
            size_t(out.iteration_indptr.back()) == out.trees.size(),
        "iteration_indptr does not cover the stored trees");
+  // every round's trees are [indptr[r], indptr[r + 1]) of the stored trees:
+  // slicing and prediction index the trees and their device layout with them
+  for (size_t r = 1; r < out.iteration_indptr.size(); ++r)
+    need(out.iteration_indptr[r] >= out.iteration_indptr[r - 1] &&
+             size_t(out.iteration_indptr[r]) <= out.trees.size(),
+         "iteration_indptr must be non-decreasing and within the stored trees");
   m = std::move(out);
   p = q;
 }

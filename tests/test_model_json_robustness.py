@@ -1,0 +1,148 @@
+"""Model JSON from a caller is checked before use.  XGBoosterLoadModel* runs
+inside the caller's process on bytes the caller supplies, and a loaded
+model's round index (iteration_indptr), tree classes and child ids later
+index host vectors (slicing) and device arrays (prediction), so a malformed
+model must be refused with -1 and a message at load, and no input may crash
+the parser.  Runs on the CPU: loading, saving and slicing touch no device."""
+import copy
+import ctypes as C
+import json
+import random
+
+import pytest
+
+from test_abi import _model
+
+
+def load(lib, doc):
+    buf = doc if isinstance(doc, bytes) else json.dumps(doc).encode()
+    h = C.c_void_p()
+    assert lib.XGBoosterCreate(None, 0, C.byref(h)) == 0
+    rc = lib.XGBoosterLoadModelFromBuffer(h, buf, len(buf))
+    msg = lib.XGBGetLastError().decode("ascii") if rc else ""  # messages are plain text
+    return h, rc, msg
+
+
+def edit(path, value):
+    m = _model()
+    node = m
+    for k in path[:-1]:
+        node = node[k]
+    node[path[-1]] = value
+    return m
+
+
+MODEL = ["learner", "gradient_booster", "model"]
+TREE0 = MODEL + ["trees", 0]
+
+
+@pytest.mark.parametrize("doc,needle", [
+    (edit(MODEL + ["iteration_indptr"], [0, 7, 2]), "iteration_indptr must be non-decreasing"),
+    (edit(MODEL + ["iteration_indptr"], [0, 2, 1, 2]), "iteration_indptr must be non-decreasing"),
+    (edit(MODEL + ["iteration_indptr"], [0, 3]), "iteration_indptr does not cover"),
+    (edit(MODEL + ["tree_info"], [0, 2]), "tree_info names a class outside num_class"),
+    (edit(MODEL + ["tree_info"], [-1, 0]), "tree_info names a class outside num_class"),
+    (edit(["learner", "learner_model_param", "num_class"], "-3"), "num_class is outside"),
+    (edit(["learner", "learner_model_param", "num_class"], "99999999999"), "num_class is outside"),
+    (edit(TREE0 + ["left_children"], [5, -1, -1]), "tree child index out of range"),
+    (edit(TREE0 + ["right_children"], [2, -1]), "tree node arrays differ in size"),
+    (edit(MODEL + ["tree_info"], [0]), "tree_info size differs"),
+])
+def test_malformed_models_are_refused_at_load(dp, doc, needle):
+    lib = dp.lib()
+    h, rc, msg = load(lib, doc)
+    lib.XGBoosterFree(h)
+    assert rc == -1 and needle in msg, msg
+
+
+def mutate(rng, m):
+    m = copy.deepcopy(m)
+    values = [-1, -2, 0, 1, 2, 3, 7, 2**31 - 1, 2**31, -2**31, 2**63 - 1, 1e300, -1e300, 0.5, "x", None, [], {},
+              True, "nan", "1", "-1", "99999999999"]
+    lr = m["learner"]
+    model = lr["gradient_booster"]["model"]
+    t = model["trees"][rng.randrange(len(model["trees"]))]
+    key = rng.choice(["left_children", "right_children", "split_indices", "split_conditions", "default_left",
+                      "base_weights", "sum_hessian", "loss_changes", "split_type"])
+    op = rng.randrange(6)
+    if op == 0 and isinstance(t.get(key), list) and t[key]:
+        t[key][rng.randrange(len(t[key]))] = rng.choice(values)
+    elif op == 1 and isinstance(t.get(key), list):
+        t[key] = t[key][:rng.randrange(len(t[key]) + 1)]
+    elif op == 2:
+        t[key] = rng.choice(values)
+    elif op == 3:
+        t.pop(key, None)
+    elif op == 4:
+        model[rng.choice(["tree_info", "iteration_indptr"])] = [rng.choice(values) for _ in range(rng.randrange(5))]
+    else:
+        p = lr["learner_model_param"]
+        p[rng.choice(sorted(p))] = str(rng.choice(values))
+    return m
+
+
+def test_no_input_crashes_load_save_or_slice(dp):
+    lib = dp.lib()
+    rng = random.Random(20240601)
+    good = json.dumps(_model()).encode()
+    docs = [good[:i] for i in range(0, len(good), 11)]
+    for _ in range(400):
+        b = bytearray(good)
+        for _ in range(rng.randint(1, 4)):
+            b[rng.randrange(len(b))] = rng.randrange(256)
+        docs.append(bytes(b))
+    docs += [b"[" * 200000 + b"]" * 200000, b'{"a":' * 50000 + b"1" + b"}" * 50000, b"1e999999", b'"\\ud800"']
+    docs += [mutate(rng, mutate(rng, _model()) if rng.random() < 0.3 else _model()) for _ in range(600)]
+    loaded = 0
+    for doc in docs:
+        h, rc, _ = load(lib, doc)
+        assert rc in (0, -1)
+        if rc == 0:
+            loaded += 1
+            n, p = C.c_uint64(), C.c_void_p()
+            assert lib.XGBoosterSaveModelToBuffer(h, b'{"format":"json"}', C.byref(n), C.byref(p)) in (0, -1)
+            for begin, end, step in ((0, 1, 1), (0, 0, 1), (1, 0, 1), (0, 5, 2)):
+                s = C.c_void_p()
+                if lib.XGBoosterSlice(h, begin, end, step, C.byref(s)) == 0:
+                    lib.XGBoosterFree(s)
+        lib.XGBoosterFree(h)
+    assert loaded > 0  # the harmless edits still load
+
+
+def raw_model(**subst):
+    """The test model as JSON text with `objective` replaced by raw text."""
+    text = json.dumps(_model())
+    for k, v in subst.items():
+        text = text.replace(k, v)
+    return text.encode()
+
+
+@pytest.mark.parametrize("escaped,ok", [
+    (r'"\u0072eg:squarederror"', True),                       # a BMP escape of 'r'
+    (r'"\ud83d\ude00"', False),                               # a surrogate pair: valid, unknown objective
+    (r'"\u12G4"', False),                                      # not hex
+    (r'"\ud83d"', False),                                      # lone high surrogate
+    (r'"\ude00x"', False),                                     # lone low surrogate
+])
+def test_unicode_escapes(dp, escaped, ok):
+    lib = dp.lib()
+    m = _model()
+    m["learner"]["objective"]["name"] = "reg:squarederror"
+    m["learner"]["learner_model_param"]["num_class"] = "0"
+    m["learner"]["gradient_booster"]["model"]["tree_info"] = [0, 0]
+    text = json.dumps(m).replace('"reg:squarederror"', escaped).encode()
+    h, rc, msg = load(lib, text)
+    lib.XGBoosterFree(h)
+    if ok:
+        assert rc == 0, msg
+    elif "G4" in escaped or escaped.count("\\u") == 1:
+        assert rc == -1 and "bad JSON unicode escape" in msg, msg
+    else:
+        assert rc == -1 and "objective" in msg.lower(), msg   # decoded, then refused as an objective
+
+
+def test_error_messages_quote_input_as_plain_text(dp):
+    lib = dp.lib()
+    h, rc, msg = load(lib, b'{"version": [3, 4, 1], "learner": \xff\xfe\x01}')
+    lib.XGBoosterFree(h)
+    assert rc == -1 and "\\xff\\xfe\\x01" in msg, msg
