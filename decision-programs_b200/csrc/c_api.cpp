@@ -153,6 +153,9 @@ DenseSpec dense_spec(const char* data, const char* config) {
     }
   }
   need(d.rows == 0 || a.ptr != 0, "matrix data pointer is null");
+  // every kernel addresses rows * stride elements with 64-bit byte offsets
+  need(d.stride <= (dp::u64(1) << 40), "matrix row stride out of range");
+  need(d.rows <= (dp::u64(1) << 62) / 4 / d.stride, "matrix size overflows 64-bit byte offsets");
   d.ptr = reinterpret_cast<const float*>(a.ptr);
   return d;
 }

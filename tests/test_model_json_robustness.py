@@ -3,7 +3,9 @@ inside the caller's process on bytes the caller supplies, and a loaded
 model's round index (iteration_indptr), tree classes and child ids later
 index host vectors (slicing) and device arrays (prediction), so a malformed
 model must be refused with -1 and a message at load, and no input may crash
-the parser.  Runs on the CPU: loading, saving and slicing touch no device."""
+the parser.  The same holds for the array interfaces that describe a caller's
+matrix: a malformed one is refused before any CUDA call.  Runs on the CPU:
+loading, saving and slicing touch no device."""
 import copy
 import ctypes as C
 import json
@@ -146,3 +148,34 @@ def test_error_messages_quote_input_as_plain_text(dp):
     h, rc, msg = load(lib, b'{"version": [3, 4, 1], "learner": \xff\xfe\x01}')
     lib.XGBoosterFree(h)
     assert rc == -1 and "\\xff\\xfe\\x01" in msg, msg
+
+
+def iface(**kw):
+    d = {"data": [4096, True], "shape": [10, 4], "strides": None, "typestr": "<f4", "version": 3}
+    d.update(kw)
+    return json.dumps(d).encode()
+
+
+@pytest.mark.parametrize("text,needle", [
+    (iface(typestr="<f8"), "float32"),
+    (iface(shape=[10, 4, 2]), "two-dimensional"),
+    (iface(shape=[10, 0]), "column count out of range"),
+    (iface(shape=[10, 2**31]), "column count out of range"),
+    (iface(strides=[16, 8]), "row-major"),
+    (iface(strides=[18, 4]), "row-major"),
+    (iface(strides=[2**50, 4]), "row stride out of range"),
+    (iface(shape=[2**61, 4]), "overflows"),
+    (iface(data=[0, True]), "data pointer is null"),
+    (iface(mask=[1]), "masked arrays"),
+    (b"[" + iface() + b"," + iface() + b"]", "only one array interface"),
+    (iface(data="x"), "data must be"),
+    (b'{"shape": [1, 1]}', "missing JSON key"),
+])
+def test_malformed_array_interfaces_are_refused(dp, text, needle):
+    """Checked before any CUDA call, so these run without a GPU."""
+    lib = dp.lib()
+    for create in (lib.XGDMatrixCreateFromCudaArrayInterface, lib.XGDMatrixCreateFromDense):
+        h = C.c_void_p()
+        assert create(text, b'{"missing": NaN}', C.byref(h)) == -1
+        msg = lib.XGBGetLastError().decode("ascii")
+        assert needle in msg, msg
