@@ -342,9 +342,17 @@ int XGBoosterPredictFromCudaArray(BoosterHandle handle, const char* values, cons
   q.stride = spec.stride;
   q.has_mv = spec.has_mv;
   q.mv = spec.mv;
-  if (const auto* v = c.find("type")) q.type = int(v->as_int());
-  if (const auto* v = c.find("iteration_begin")) q.it_begin = int(v->as_int());
-  if (const auto* v = c.find("iteration_end")) q.it_end = int(v->as_int());
+  // checked before narrowing, so that no value wraps into a valid-looking one
+  auto small_int = [&](const char* key, long long lo, long long hi, int dflt) {
+    const auto* v = c.find(key);
+    if (!v) return dflt;
+    const long long x = v->as_int();
+    need(x >= lo && x <= hi, std::string("prediction config ") + key + " is out of range");
+    return int(x);
+  };
+  q.type = small_int("type", 0, 1, q.type);
+  q.it_begin = small_int("iteration_begin", 0, b->model.rounds(), q.it_begin);
+  q.it_end = small_int("iteration_end", 0, b->model.rounds(), q.it_end);
   if (const auto* v = c.find("strict_shape")) q.strict_shape = v->as_bool();
   q.device = q.rows ? pointer_device(spec.ptr, false) : 0;
   {

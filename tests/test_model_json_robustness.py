@@ -179,3 +179,25 @@ def test_malformed_array_interfaces_are_refused(dp, text, needle):
         assert create(text, b'{"missing": NaN}', C.byref(h)) == -1
         msg = lib.XGBGetLastError().decode("ascii")
         assert needle in msg, msg
+
+
+@pytest.mark.parametrize("config,needle", [
+    ({"type": 2}, "type is out of range"),
+    ({"type": 2**32}, "type is out of range"),
+    ({"iteration_begin": -1}, "iteration_begin is out of range"),
+    ({"iteration_end": 2**32 + 1}, "iteration_end is out of range"),
+    ({"iteration_end": 5}, "iteration_end is out of range"),
+])
+def test_prediction_config_is_checked_before_device_work(dp, config, needle):
+    """A value that would wrap when narrowed (2^32 + 1 -> 1) is refused, not
+    read as another, valid-looking one."""
+    lib = dp.lib()
+    h, rc, _ = load(lib, _model())
+    assert rc == 0
+    shape, dims, out = C.POINTER(C.c_uint64)(), C.c_uint64(), C.POINTER(C.c_float)()
+    cfg = json.dumps(dict({"missing": float("nan")}, **config)).encode()
+    rc = lib.XGBoosterPredictFromCudaArray(h, iface(shape=[10, 2]), cfg, None, C.byref(shape), C.byref(dims),
+                                           C.byref(out))
+    msg = lib.XGBGetLastError().decode("ascii")
+    lib.XGBoosterFree(h)
+    assert rc == -1 and needle in msg, msg
