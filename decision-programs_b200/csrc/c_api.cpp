@@ -343,16 +343,17 @@ int XGBoosterPredictFromCudaArray(BoosterHandle handle, const char* values, cons
   q.has_mv = spec.has_mv;
   q.mv = spec.mv;
   // checked before narrowing, so that no value wraps into a valid-looking one
-  auto small_int = [&](const char* key, long long lo, long long hi, int dflt) {
+  auto small_int = [&](const char* key, long long lo, long long hi, int dflt, const char* what) {
     const auto* v = c.find(key);
     if (!v) return dflt;
     const long long x = v->as_int();
-    need(x >= lo && x <= hi, std::string("prediction config ") + key + " is out of range");
+    need(x >= lo && x <= hi, std::string("prediction config ") + key + " is out of range: " + what);
     return int(x);
   };
-  q.type = small_int("type", 0, 1, q.type);
-  q.it_begin = small_int("iteration_begin", 0, b->model.rounds(), q.it_begin);
-  q.it_end = small_int("iteration_end", 0, b->model.rounds(), q.it_end);
+  q.type = small_int("type", 0, 1, q.type, "only types 0 (value) and 1 (margin) are supported");
+  q.it_begin = small_int("iteration_begin", 0, b->model.rounds(), q.it_begin,
+                         "iteration range outside the model's rounds");
+  q.it_end = small_int("iteration_end", 0, b->model.rounds(), q.it_end, "iteration range outside the model's rounds");
   if (const auto* v = c.find("strict_shape")) q.strict_shape = v->as_bool();
   q.device = q.rows ? pointer_device(spec.ptr, false) : 0;
   {

@@ -186,7 +186,7 @@ def test_malformed_array_interfaces_are_refused(dp, text, needle):
     ({"type": 2**32}, "type is out of range"),
     ({"iteration_begin": -1}, "iteration_begin is out of range"),
     ({"iteration_end": 2**32 + 1}, "iteration_end is out of range"),
-    ({"iteration_end": 5}, "iteration_end is out of range"),
+    ({"iteration_end": 5}, "iteration range outside the model's rounds"),
 ])
 def test_prediction_config_is_checked_before_device_work(dp, config, needle):
     """A value that would wrap when narrowed (2^32 + 1 -> 1) is refused, not
