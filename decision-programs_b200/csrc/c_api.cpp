@@ -195,13 +195,16 @@ int XGDMatrixCreateFromDense(const char* data, const char* config, DMatrixHandle
 
 int XGDMatrixSetInfoFromInterface(DMatrixHandle handle, const char* field, const char* data) {
   DP_API_BEGIN();
-  dp::DMatrix* d = as_dmatrix(handle);
   need(field != nullptr && std::string(field) == "label", "only the \"label\" field is supported");
   const ArrayInterface a = parse_array(data);
   need(a.typestr == "<f4", "labels must be little-endian float32 (<f4)");
   need(a.shape.size() == 1 || (a.shape.size() == 2 && a.shape[1] == 1), "labels must be a vector");
-  need(a.strides.empty() || a.strides.back() == 4, "labels must be contiguous");
+  // consecutive labels 4 bytes apart: for an [n, 1] array that is the stride
+  // between rows (a column of a wider matrix is refused, not read wrongly)
+  need(a.strides.empty() || (a.strides.size() == a.shape.size() && (a.shape[0] <= 1 || a.strides[0] == 4)),
+       "labels must be contiguous");
   need(a.shape[0] == 0 || a.ptr != 0, "label pointer is null");
+  dp::DMatrix* d = as_dmatrix(handle);
   {
     dp::DeviceGuard g(d->device());
     dp::cuda_check(cudaDeviceSynchronize(), "synchronise producer");

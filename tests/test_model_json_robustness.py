@@ -201,3 +201,27 @@ def test_prediction_config_is_checked_before_device_work(dp, config, needle):
     msg = lib.XGBGetLastError().decode("ascii")
     lib.XGBoosterFree(h)
     assert rc == -1 and needle in msg, msg
+
+
+@pytest.mark.parametrize("shape,strides,needle", [
+    ([10, 1], [16, 4], "contiguous"),       # a column of a 4-wide matrix
+    ([10], [8], "contiguous"),
+    ([10], [4, 4], "contiguous"),
+    ([10, 2], None, "vector"),
+    ([10, 1, 1], None, "vector"),
+])
+def test_label_interfaces_are_checked_before_the_matrix(dp, shape, strides, needle):
+    """Label arrays are checked before the matrix handle is used (here a null
+    one), so these run without a GPU."""
+    lib = dp.lib()
+    rc = lib.XGDMatrixSetInfoFromInterface(None, b"label", iface(shape=shape, strides=strides))
+    msg = lib.XGBGetLastError().decode("ascii")
+    assert rc == -1 and needle in msg, msg
+
+
+def test_contiguous_label_interfaces_reach_the_matrix_check(dp):
+    lib = dp.lib()
+    for shape, strides in (([10], None), ([10], [4]), ([10, 1], [4, 4]), ([1, 1], [64, 4])):
+        rc = lib.XGDMatrixSetInfoFromInterface(None, b"label", iface(shape=shape, strides=strides))
+        msg = lib.XGBGetLastError().decode("ascii")
+        assert rc == -1 and "DMatrix handle is null" in msg, (shape, strides, msg)
