@@ -87,7 +87,7 @@ dp::Booster* as_booster(void* h) {
 
 std::string read_file(const char* path) {
   std::ifstream f(path, std::ios::binary);
-  need(bool(f), std::string("cannot read ") + path);
+  need(bool(f), "cannot read " + dp::printable(path));
   std::ostringstream s;
   s << f.rdbuf();
   return s.str();
@@ -224,12 +224,14 @@ int XGDMatrixSetFloatInfo(DMatrixHandle handle, const char* field, const float* 
 
 int XGDMatrixNumRow(DMatrixHandle handle, bst_ulong* out) {
   DP_API_BEGIN();
+  need(out != nullptr, "output pointer is null");
   *out = as_dmatrix(handle)->rows();
   DP_API_END();
 }
 
 int XGDMatrixNumCol(DMatrixHandle handle, bst_ulong* out) {
   DP_API_BEGIN();
+  need(out != nullptr, "output pointer is null");
   *out = as_dmatrix(handle)->cols();
   DP_API_END();
 }
@@ -277,6 +279,7 @@ int XGBoosterBoostedRounds(BoosterHandle handle, int* out) {
 
 int XGBoosterSaveJsonConfig(BoosterHandle handle, bst_ulong* out_len, const char** out) {
   DP_API_BEGIN();
+  need(out_len != nullptr && out != nullptr, "output pointers are null");
   const std::string& s = as_booster(handle)->save_config_json();
   *out_len = s.size();
   *out = s.c_str();
@@ -290,16 +293,17 @@ int XGBoosterSaveModel(BoosterHandle handle, const char* fname) {
   need(ends_with(path, ".json"), "only JSON models (a .json file name) are supported");
   const std::string& s = as_booster(handle)->save_model_json();
   std::ofstream f(path, std::ios::binary | std::ios::trunc);
-  need(bool(f), "cannot write " + path);
+  need(bool(f), "cannot write " + dp::printable(path));
   f.write(s.data(), std::streamsize(s.size()));
   f.flush();
-  need(bool(f), "cannot write " + path);
+  need(bool(f), "cannot write " + dp::printable(path));
   DP_API_END();
 }
 
 int XGBoosterSaveModelToBuffer(BoosterHandle handle, const char* config, bst_ulong* out_len, const char** out) {
   DP_API_BEGIN();
   need(config != nullptr, "config is null");
+  need(out_len != nullptr && out != nullptr, "output pointers are null");
   const dp::json::Value c = dp::json::parse(config);
   need(c.at("format").as_string() == "json", "only {\"format\":\"json\"} is supported");
   const std::string& s = as_booster(handle)->save_model_json();
@@ -374,6 +378,7 @@ int XGBoosterPredictFromCudaArray(BoosterHandle handle, const char* values, cons
 
 int XGBoosterGetNumFeature(BoosterHandle handle, bst_ulong* out) {
   DP_API_BEGIN();
+  need(out != nullptr, "output pointer is null");
   *out = bst_ulong(as_booster(handle)->model.num_feature);
   DP_API_END();
 }
@@ -442,6 +447,7 @@ int dp_booster_set_profiling(BoosterHandle handle, int on) {
 
 int dp_booster_profile(BoosterHandle handle, const char** out_json) {
   DP_API_BEGIN();
+  need(out_json != nullptr, "output pointer is null");
   dp::Booster* b = as_booster(handle);
   b->profile_buf = b->engine() ? b->engine()->profiler().json() : std::string("{}");
   *out_json = b->profile_buf.c_str();
@@ -454,6 +460,7 @@ int dp_booster_margins(BoosterHandle handle, float* out, bst_ulong len) {
   need(b->engine() != nullptr, "the booster has not been trained on a matrix");
   const std::vector<float> m = b->engine()->margins();
   need(len == m.size(), "margin buffer size differs from rows * outputs");
+  need(len == 0 || out != nullptr, "margin buffer is null");
   std::memcpy(out, m.data(), m.size() * sizeof(float));
   DP_API_END();
 }

@@ -225,3 +225,25 @@ def test_contiguous_label_interfaces_reach_the_matrix_check(dp):
         rc = lib.XGDMatrixSetInfoFromInterface(None, b"label", iface(shape=shape, strides=strides))
         msg = lib.XGBGetLastError().decode("ascii")
         assert rc == -1 and "DMatrix handle is null" in msg, (shape, strides, msg)
+
+
+def test_null_output_pointers_are_refused(dp):
+    """Where XGBoost returns an error for a null output pointer, so does this
+    library, instead of writing through it."""
+    lib = dp.lib()
+    h, rc, _ = load(lib, _model())
+    assert rc == 0
+    n, p = C.c_uint64(), C.c_void_p()
+    calls = [
+        lambda: lib.XGBoosterGetNumFeature(h, None),
+        lambda: lib.XGBoosterSaveJsonConfig(h, None, None),
+        lambda: lib.XGBoosterSaveJsonConfig(h, C.byref(n), None),
+        lambda: lib.XGBoosterSaveModelToBuffer(h, b'{"format":"json"}', None, None),
+        lambda: lib.XGBoosterSaveModelToBuffer(h, b'{"format":"json"}', C.byref(n), None),
+        lambda: lib.dp_booster_profile(h, None),
+    ]
+    for i, call in enumerate(calls):
+        assert call() == -1, i
+        assert "null" in lib.XGBGetLastError().decode("ascii"), i
+    assert lib.XGBoosterSaveModelToBuffer(h, b'{"format":"json"}', C.byref(n), C.byref(p)) == 0 and n.value > 0
+    lib.XGBoosterFree(h)
