@@ -247,3 +247,29 @@ def test_null_output_pointers_are_refused(dp):
         assert "null" in lib.XGBGetLastError().decode("ascii"), i
     assert lib.XGBoosterSaveModelToBuffer(h, b'{"format":"json"}', C.byref(n), C.byref(p)) == 0 and n.value > 0
     lib.XGBoosterFree(h)
+
+
+def test_parameters_never_crash_or_break_the_configuration(dp):
+    """Random keys and values through XGBoosterSetParam: every call returns 0
+    or -1 with a plain-text message, and the configuration document stays
+    valid JSON whatever was recorded (quotes, backslashes, control bytes)."""
+    lib = dp.lib()
+    rng = random.Random(7)
+    keys = ["objective", "num_class", "max_depth", "max_bin", "eta", "lambda", "alpha", "gamma", "min_child_weight",
+            "subsample", "colsample_bynode", "seed", "device", "tree_method", "base_score", "max_delta_step",
+            "num_parallel_tree", "nthread", "eval_metric", "", "k\"ey", "\xff"]
+    values = ["", "0", "1", "-1", "1e309", "nan", "inf", "0.5", "2", "256", "99999999999999999999", "cuda:", "cuda:0",
+              "cuda:-1", "cuda:99999999999", "cpu", "\"quoted\"", "\"", "[0.5]", "[", "hist", "multi:softprob",
+              "a\\b", "\x01", "\xff\xfe", "0x10", "1e-400", "{}"]
+    for _ in range(1500):
+        h = C.c_void_p()
+        assert lib.XGBoosterCreate(None, 0, C.byref(h)) == 0
+        for _ in range(rng.randint(1, 4)):
+            rc = lib.XGBoosterSetParam(h, rng.choice(keys).encode("latin-1"), rng.choice(values).encode("latin-1"))
+            assert rc in (0, -1)
+            if rc:
+                lib.XGBGetLastError().decode("ascii")
+        n, s = C.c_uint64(), C.c_char_p()
+        assert lib.XGBoosterSaveJsonConfig(h, C.byref(n), C.byref(s)) == 0
+        json.loads(C.string_at(s, n.value))
+        lib.XGBoosterFree(h)
