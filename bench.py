@@ -58,6 +58,19 @@ def workload_config(rows: int = ROWS) -> dict:
             "l2": "inputs (1.28 GB of bins, 5.1 GB fp32) exceed the 126 MB L2"}
 
 
+def cpu_model() -> str:
+    """The host CPU's model name (Linux /proc/cpuinfo), reported beside the
+    thread count of every CPU figure."""
+    try:
+        for line in pathlib.Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+    return platform.processor() or "unknown"
+
+
 def measured_peaks() -> dict:
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -218,7 +231,8 @@ def reference_arm(args) -> None:
         "data": "synthetic (seeded)",
         "config": workload_config(ROWS),
         "parallelism": f"CPU oracle on {threads} host threads; every step one tree over all {ROWS} rows",
-        "cpu_baseline": {"value": value, "unit": "rows*trees/s", "cores": threads, "kind": "port",
+        "cpu_baseline": {"value": value, "unit": "rows*trees/s", "cores": threads, "cpu": cpu_model(),
+                         "kind": "port",
                          "sample": f"the whole config-4 workload ({ROWS} rows x {FEATURES} features, data {where}), "
                                    f"one depth-10 tree per step, {args.steps} timed steps after {args.warmup} "
                                    f"warm-up trees (C++ oracle, {threads} threads)"},
@@ -246,7 +260,8 @@ def config4_cpu_leg(torch, first_trees: list[dict]) -> dict:
     del m
     third = sklearn_leg(x, y, threads)
     del x, y
-    out = {"value": ROWS * C4_PARITY_TREES / dt, "unit": "rows*trees/s", "cores": threads, "kind": "port",
+    out = {"value": ROWS * C4_PARITY_TREES / dt, "unit": "rows*trees/s", "cores": threads, "cpu": cpu_model(),
+           "kind": "port",
            "sample": f"the whole config-4 workload ({ROWS} rows, data {where}), the first {C4_PARITY_TREES} "
                      f"depth-10 trees (C++ oracle, {threads} threads, {dt:.1f} s; cuts and bins built before)",
            "trees_identical_to_oracle": same, "trees_compared": C4_PARITY_TREES}
@@ -291,7 +306,7 @@ def sklearn_leg(x, y, threads: int):
     except Exception as e:  # context only: never cost the bench line
         return {"error": f"{type(e).__name__}: {e}"[:200]}
     per_tree = max(tn - t1, 1e-9) / SKLEARN_TREES
-    return {"value": SKLEARN_ROWS / per_tree, "unit": "rows*trees/s", "cores": threads,
+    return {"value": SKLEARN_ROWS / per_tree, "unit": "rows*trees/s", "cores": threads, "cpu": cpu_model(),
             "impl": f"scikit-learn {sklearn.__version__} HistGradientBoostingRegressor",
             "sample": f"first {SKLEARN_ROWS} rows of the config-4 data, depth-10 trees; time per tree = "
                       f"(fit of {1 + SKLEARN_TREES} trees - fit of 1) / {SKLEARN_TREES}, binning excluded",
