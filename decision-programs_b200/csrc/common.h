@@ -4,7 +4,11 @@
 #include <cuda_runtime.h>
 #include <nvtx3/nvToolsExt.h>
 
+#include <locale.h>
+#include <stdlib.h>
+
 #include <atomic>
+#include <cstdlib>
 #include <cstdint>
 #include <functional>
 #include <mutex>
@@ -28,6 +32,13 @@ struct Error : std::runtime_error {
 };
 
 [[noreturn]] inline void fail(const std::string& msg) { throw Error(msg); }
+// strtod in the "C" locale whatever the process's LC_NUMERIC: JSON and the
+// parameter strings always write the decimal point as '.', and a caller that
+// set a locale with a decimal comma must not change how they read.
+inline double strtod_c(const char* s, char** end) {
+  static const locale_t c_numeric = newlocale(LC_NUMERIC_MASK, "C", locale_t(0));
+  return c_numeric ? strtod_l(s, end, c_numeric) : std::strtod(s, end);
+}
 // Caller-supplied text quoted in an error message, as printable ASCII (other
 // bytes as \xHH), so that the message stays plain text whatever was passed.
 inline std::string printable(std::string_view s) {

@@ -4,6 +4,7 @@
 #include <chrono>
 #include <cstdlib>
 #include <cstring>
+#include <locale>
 #include <sstream>
 
 namespace dp {
@@ -92,6 +93,7 @@ void Profiler::drop_graph() {
 }
 std::string Profiler::json() const {
   std::ostringstream o;
+  o.imbue(std::locale::classic());  // JSON numbers, whatever locale the caller set
   o << "{";
   bool first = true;
   for (const auto& kv : stats_) {

@@ -130,9 +130,9 @@ std::string format_float(float v) {
   std::string s(buf, r.ptr);
   // The shortest float repr read back through a double and narrowed must give
   // v again; otherwise use 9 significant digits, which always do.
-  if (float(std::strtod(s.c_str(), nullptr)) != v) {
-    std::snprintf(buf, sizeof buf, "%.9g", double(v));
-    s = buf;
+  if (float(strtod_c(s.c_str(), nullptr)) != v) {
+    auto r9 = std::to_chars(buf, buf + sizeof buf, double(v), std::chars_format::general, 9);
+    s.assign(buf, r9.ptr);
   }
   return s;
 }
@@ -316,7 +316,7 @@ class Parser {
     need(i_ > b, std::string("invalid JSON token near: ") + printable(t_.substr(b, 16)));
     std::string text(t_.substr(b, i_ - b));
     char* end = nullptr;
-    double d = std::strtod(text.c_str(), &end);
+    double d = strtod_c(text.c_str(), &end);
     need(end == text.c_str() + text.size(), "invalid JSON number: " + printable(text));
     return Value::number(d, text);
   }

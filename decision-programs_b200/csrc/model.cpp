@@ -30,7 +30,7 @@ std::string unquote(const std::string& v) {
 double to_double(const std::string& key, const std::string& v) {
   const std::string s = unquote(v);
   char* end = nullptr;
-  const double d = std::strtod(s.c_str(), &end);
+  const double d = strtod_c(s.c_str(), &end);
   need(!s.empty() && end == s.c_str() + s.size(),
        "invalid numeric value for parameter " + printable(key) + ": " + printable(v));
   return d;
