@@ -273,3 +273,41 @@ def test_parameters_never_crash_or_break_the_configuration(dp):
         assert lib.XGBoosterSaveJsonConfig(h, C.byref(n), C.byref(s)) == 0
         json.loads(C.string_at(s, n.value))
         lib.XGBoosterFree(h)
+
+
+def test_boundary_calls_from_many_threads(dp):
+    """Searches and out-of-fold fits may drive boosters from several threads:
+    load, save, slice and refusals run concurrently, every thread reads its
+    own error message, and every saved model is the same text."""
+    import threading
+    lib = dp.lib()
+    good = json.dumps(_model()).encode()
+    bad = good[:-5]
+    outs, errors = [], []
+
+    def work(tid):
+        try:
+            for i in range(120):
+                h = C.c_void_p()
+                assert lib.XGBoosterCreate(None, 0, C.byref(h)) == 0
+                if (i + tid) % 3 == 0:
+                    assert lib.XGBoosterLoadModelFromBuffer(h, bad, len(bad)) == -1
+                    assert "JSON" in lib.XGBGetLastError().decode("ascii")
+                assert lib.XGBoosterLoadModelFromBuffer(h, good, len(good)) == 0
+                n, p = C.c_uint64(), C.c_void_p()
+                assert lib.XGBoosterSaveModelToBuffer(h, b'{"format":"json"}', C.byref(n), C.byref(p)) == 0
+                outs.append(C.string_at(p, n.value))
+                s = C.c_void_p()
+                assert lib.XGBoosterSlice(h, 0, 1, 1, C.byref(s)) == 0
+                lib.XGBoosterFree(s)
+                lib.XGBoosterFree(h)
+        except Exception as e:  # reported below, from the main thread
+            errors.append(repr(e))
+
+    threads = [threading.Thread(target=work, args=(t,)) for t in range(8)]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join()
+    assert not errors, errors[:3]
+    assert len(outs) == 8 * 120 and len(set(outs)) == 1
