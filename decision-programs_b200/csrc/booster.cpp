@@ -88,6 +88,8 @@ const float* Booster::predict(const PredictRequest& q, const u64** shape, u64* d
   need(q.it_begin >= 0 && q.it_begin <= it_end && it_end <= rounds, "iteration range outside the model's rounds");
   need(q.rows == 0 || q.x != nullptr, "prediction input pointer is null");
   const int K = params.K();
+  // outputs are [rows][K]: with no class the transform would read an empty margin buffer
+  need(K >= 1, "num_class must be at least 1 to predict with a multi-class objective");
   DeviceGuard g(q.device);
   if (!pred_ || pred_->device != q.device) {
     pred_ = std::make_unique<PredState>();

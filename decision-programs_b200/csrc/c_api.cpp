@@ -362,6 +362,7 @@ int XGBoosterPredictFromCudaArray(BoosterHandle handle, const char* values, cons
                          "iteration range outside the model's rounds");
   q.it_end = small_int("iteration_end", 0, b->model.rounds(), q.it_end, "iteration range outside the model's rounds");
   if (const auto* v = c.find("strict_shape")) q.strict_shape = v->as_bool();
+  need(b->params.K() >= 1, "num_class must be at least 1 to predict with a multi-class objective");
   q.device = q.rows ? pointer_device(spec.ptr, false) : 0;
   {
     dp::DeviceGuard g(q.device);

@@ -311,3 +311,29 @@ def test_boundary_calls_from_many_threads(dp):
         t.join()
     assert not errors, errors[:3]
     assert len(outs) == 8 * 120 and len(set(outs)) == 1
+
+
+@pytest.mark.parametrize("source", ["param", "model"])
+def test_prediction_without_classes_is_refused_on_the_host(dp, source):
+    """multi:softprob with num_class 0 (a parameter, or a tree-less model
+    file) has outputs [rows][0]; predicting is refused before device work
+    instead of transforming an empty margin buffer."""
+    lib = dp.lib()
+    if source == "param":
+        h = C.c_void_p()
+        assert lib.XGBoosterCreate(None, 0, C.byref(h)) == 0
+        assert lib.XGBoosterSetParam(h, b"objective", b"multi:softprob") == 0
+        assert lib.XGBoosterSetParam(h, b"num_class", b"0") == 0
+    else:
+        m = _model()
+        m["learner"]["learner_model_param"]["num_class"] = "0"
+        model = m["learner"]["gradient_booster"]["model"]
+        model["trees"], model["tree_info"], model["iteration_indptr"] = [], [], [0]
+        h, rc, msg = load(lib, m)
+        assert rc == 0, msg
+    shape, dims, out = C.POINTER(C.c_uint64)(), C.c_uint64(), C.POINTER(C.c_float)()
+    rc = lib.XGBoosterPredictFromCudaArray(h, iface(shape=[10, 2]), b'{"type": 0, "missing": NaN}', None,
+                                           C.byref(shape), C.byref(dims), C.byref(out))
+    msg = lib.XGBGetLastError().decode("ascii")
+    lib.XGBoosterFree(h)
+    assert rc == -1 and "num_class must be at least 1" in msg, msg
