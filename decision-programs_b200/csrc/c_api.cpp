@@ -471,6 +471,9 @@ uint64_t dp_launch_count(void) { return dp::launch_counter().load(); }
 int dp_quantile_cuts(const float* x, uint64_t rows, uint32_t features, uint64_t row_stride, int max_bin,
                      float* cut, uint16_t* nbins, uint8_t* has_missing, void* stream) {
   DP_API_BEGIN();
+  need(rows == 0 || x != nullptr, "matrix pointer is null");
+  need(cut != nullptr && nbins != nullptr && has_missing != nullptr, "output pointer is null");
+  need(row_stride >= features, "row_stride must cover the features");
   dp::CutsDevice cd{cut, nbins, has_missing};
   dp::compute_cuts(x, rows, features, row_stride, max_bin, false, 0.f, rows, nullptr, cd,
                    static_cast<cudaStream_t>(stream));
@@ -481,6 +484,9 @@ int dp_bin_matrix(const float* x, uint64_t rows, uint32_t features, uint64_t row
                   const uint16_t* nbins, uint8_t* bins, uint64_t bin_stride, void* stream) {
   DP_API_BEGIN();
   need(bin_stride >= features && bin_stride % 16 == 0, "bin_stride must cover the features and be a multiple of 16");
+  need(rows == 0 || (x != nullptr && bins != nullptr), "matrix or bins pointer is null");
+  need(cut != nullptr && nbins != nullptr, "cuts pointer is null");
+  need(row_stride >= features, "row_stride must cover the features");
   dp::CutsDevice cd{const_cast<float*>(cut), const_cast<uint16_t*>(nbins), nullptr};
   dp::launch_bin_matrix(x, rows, features, row_stride, false, 0.f, cd, bins, bin_stride,
                         static_cast<cudaStream_t>(stream));
@@ -493,6 +499,8 @@ int dp_gradients(int objective, int num_class, const float* margin, const float*
   need(objective >= 0 && objective <= 3, "objective id must be 0..3");
   const int K = (objective >= 2) ? num_class : 1;
   need(K >= 1, "num_class must be at least 1");
+  need(rows == 0 || (margin != nullptr && label != nullptr && gh != nullptr), "margin, label or gh pointer is null");
+  need(scales != nullptr, "scales pointer is null");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   dp::DevBuf<dp::u32> mx(2 * size_t(K));
   dp::cuda_check(cudaMemsetAsync(mx.get(), 0, 2 * K * sizeof(dp::u32), s), "memset");
@@ -538,6 +546,7 @@ HistPlan* make_hist_plan(const uint8_t* bins, uint64_t bin_stride, uint32_t feat
   p->quantized = quantized;
   p->hist = hist;
   p->nseg = nseg;
+  need(nseg == 0 || hist != nullptr, "hist pointer is null");
   std::vector<dp::HistTask> tasks;
   // the training path's choice on one GPU: 256-bin matrices of more than 64
   // features use the 64-feature kernel (DP_HIST_WIDE=0 / 1 overrides above
@@ -556,6 +565,7 @@ HistPlan* make_hist_plan(const uint8_t* bins, uint64_t bin_stride, uint32_t feat
     filled += seg_end[i] > seg_begin[i] ? 1 : 0;
   }
   p->kernel_bins = dp::hist_kernel_bins(num_bins, filled);
+  need(total == 0 || (bins != nullptr && gh != nullptr && ridx != nullptr), "bins, gh or ridx pointer is null");
   int64_t chunk = int64_t(dp::hist_chunk_rows(total * ftiles, dp::u64(nseg), bin_stride % 128 == 0));
   // testing knob: longer tasks, so that tests reach the multi-window folds
   if (const char* c = std::getenv("DP_HIST_MIN_CHUNK")) chunk = std::max<int64_t>(chunk, std::atoll(c));
@@ -650,6 +660,7 @@ int dp_hist_free(void* plan) {
 
 int dp_quantize_gh(float* gh, uint64_t n, float sg, float sh, void* stream) {
   DP_API_BEGIN();
+  need(n == 0 || gh != nullptr, "gh pointer is null");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   dp::DevBuf<dp::Scales> sc(1);
   const dp::Scales h{sg, sh};
@@ -665,6 +676,9 @@ int dp_eval_splits(const int64_t* hist, int32_t nnodes, uint32_t features, const
   DP_API_BEGIN();
   need(nnodes >= 0, "invalid node count");
   if (nnodes == 0) return 0;
+  need(hist != nullptr && nbins != nullptr && has_missing != nullptr && totals != nullptr, "input pointer is null");
+  need(out_i != nullptr && out_gain != nullptr && out_left != nullptr, "output pointer is null");
+  need(features > 0, "features must be positive");
   std::vector<dp::EvalNode> en(nnodes);
   for (int32_t n = 0; n < nnodes; ++n)
     en[n] = dp::EvalNode{dp::u32(n), 0, totals[2 * n], totals[2 * n + 1], dp::kNoSlot, 0};

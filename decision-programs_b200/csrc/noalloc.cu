@@ -64,6 +64,8 @@ extern "C" int dp_hist_build_noalloc(const uint8_t* bins, uint64_t bin_stride, u
       min_tasks += seg_end[i] > seg_begin[i] ? ftiles : 0;
       filled += seg_end[i] > seg_begin[i] ? 1 : 0;
     }
+    dp::need(nseg == 0 || hist != nullptr, "hist pointer is null");
+    dp::need(total == 0 || (bins != nullptr && gh != nullptr && ridx != nullptr), "bins, gh or ridx pointer is null");
     const int64_t chunk = int64_t(dp::hist_chunk_rows(total * ftiles, dp::u64(nseg), bin_stride % 128 == 0));
     dp::u64 ntasks = 0;
     for (int32_t i = 0; i < nseg; ++i) {

@@ -337,3 +337,37 @@ def test_prediction_without_classes_is_refused_on_the_host(dp, source):
     msg = lib.XGBGetLastError().decode("ascii")
     lib.XGBoosterFree(h)
     assert rc == -1 and "num_class must be at least 1" in msg, msg
+
+
+def test_kernel_level_entry_points_refuse_null_pointers(dp):
+    """The kernel-level entry points take device pointers; a missing one is
+    refused on the host before any device work, instead of a kernel writing
+    through it."""
+    lib = dp.lib()
+    seg_b = (C.c_int64 * 1)(0)
+    seg_e = (C.c_int64 * 1)(10)
+    fake = 4096  # never dereferenced: every call below is refused first
+    out_i, gain, left = (C.c_int32 * 4)(), (C.c_double * 1)(), (C.c_int64 * 2)()
+    totals = (C.c_int64 * 2)(1, 1)
+    calls = {
+        "quantile cuts output": lambda: lib.dp_quantile_cuts(fake, 10, 2, 2, 256, None, fake, fake, None),
+        "quantile cuts input": lambda: lib.dp_quantile_cuts(None, 10, 2, 2, 256, fake, fake, fake, None),
+        "quantile cuts stride": lambda: lib.dp_quantile_cuts(fake, 10, 4, 2, 256, fake, fake, fake, None),
+        "bin matrix bins": lambda: lib.dp_bin_matrix(fake, 10, 2, 2, fake, fake, None, 16, None),
+        "bin matrix cuts": lambda: lib.dp_bin_matrix(fake, 10, 2, 2, None, fake, fake, 16, None),
+        "gradients": lambda: lib.dp_gradients(0, 1, None, fake, 10, fake, fake, None),
+        "gradient scales": lambda: lib.dp_gradients(0, 1, fake, fake, 10, fake, None, None),
+        "quantize": lambda: lib.dp_quantize_gh(None, 10, 1.0, 1.0, None),
+        "eval input": lambda: lib.dp_eval_splits(None, 1, 2, fake, fake, totals, 1.0, 1.0, 1.0, 0.0, 0.0, 1.0,
+                                                 out_i, gain, left),
+        "eval output": lambda: lib.dp_eval_splits(fake, 1, 2, fake, fake, totals, 1.0, 1.0, 1.0, 0.0, 0.0, 1.0,
+                                                  None, gain, left),
+        "no-allocation hist": lambda: lib.dp_hist_build_noalloc(fake, 16, 2, 256, fake, fake, seg_b, seg_e, 1,
+                                                                1.0, 1.0, None, None),
+        "no-allocation bins": lambda: lib.dp_hist_build_noalloc(None, 16, 2, 256, fake, fake, seg_b, seg_e, 1,
+                                                                1.0, 1.0, fake, None),
+    }
+    for name, call in calls.items():
+        assert call() == -1, name
+        msg = lib.XGBGetLastError().decode("ascii")
+        assert "null" in msg or "cover the features" in msg, (name, msg)
