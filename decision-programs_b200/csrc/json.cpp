@@ -120,20 +120,41 @@ std::string format_double(double v) {
   return std::string(buf, r.ptr);
 }
 
-std::string format_float(float v) {
-  if (std::isnan(v)) return "NaN";
-  if (std::isinf(v)) return v > 0 ? "Infinity" : "-Infinity";
+void append_float(std::string& o, float v) {
+  if (std::isnan(v)) {
+    o += "NaN";
+    return;
+  }
+  if (std::isinf(v)) {
+    o += v > 0 ? "Infinity" : "-Infinity";
+    return;
+  }
   // "-0" would read back as the integer 0; keep the sign with a float token
-  if (v == 0.0f) return std::signbit(v) ? "-0.0" : "0";
+  if (v == 0.0f) {
+    o += std::signbit(v) ? "-0.0" : "0";
+    return;
+  }
   char buf[64];
   auto r = std::to_chars(buf, buf + sizeof buf, v);
-  std::string s(buf, r.ptr);
   // The shortest float repr read back through a double and narrowed must give
-  // v again; otherwise use 9 significant digits, which always do.
-  if (float(strtod_c(s.c_str(), nullptr)) != v) {
-    auto r9 = std::to_chars(buf, buf + sizeof buf, double(v), std::chars_format::general, 9);
-    s.assign(buf, r9.ptr);
-  }
+  // v again; otherwise use 9 significant digits, which always do.  (from_chars
+  // rounds correctly and ignores the locale, as the reader must.)
+  double back = 0.0;
+  const auto pr = std::from_chars(buf, r.ptr, back);
+  if (pr.ec != std::errc{} || float(back) != v)
+    r = std::to_chars(buf, buf + sizeof buf, double(v), std::chars_format::general, 9);
+  o.append(buf, r.ptr);
+}
+
+void append_int(std::string& o, long long v) {
+  char buf[24];
+  const auto r = std::to_chars(buf, buf + sizeof buf, v);
+  o.append(buf, r.ptr);
+}
+
+std::string format_float(float v) {
+  std::string s;
+  append_float(s, v);
   return s;
 }
 

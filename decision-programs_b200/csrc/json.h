@@ -72,6 +72,9 @@ Value parse(std::string_view text);
 // (the reference parses model numbers as double, then narrows to float:
 // native/class_io.hpp:180).
 std::string format_float(float v);
+// The same texts appended to o without a temporary string (model writing).
+void append_float(std::string& o, float v);
+void append_int(std::string& o, long long v);
 std::string format_double(double v);
 std::string quote(std::string_view s);
 

@@ -13,7 +13,10 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdio>
+#include <exception>
 #include <string>
+#include <thread>
+#include <vector>
 
 #include "json.h"
 #include "model.h"
@@ -152,12 +155,14 @@ void TrainParams::set(const std::string& key, const std::string& value) {
 // ------------------------------------------------------------------ writer
 namespace {
 
-template <class T, class Fmt>
-void put_array(std::string& o, const std::vector<T>& v, Fmt fmt) {
+// [v0,v1,...], each element appended by app(o, v[i]) without a temporary
+// string: a model of depth-10 trees has millions of numbers.
+template <class T, class App>
+void put_array(std::string& o, const std::vector<T>& v, App app) {
   o.push_back('[');
   for (size_t i = 0; i < v.size(); ++i) {
     if (i) o.push_back(',');
-    o += fmt(v[i]);
+    app(o, v[i]);
   }
   o.push_back(']');
 }
@@ -192,6 +197,38 @@ std::string learner_model_param(const Model& m, const TrainParams& p) {
          "\",\"num_target\":\"1\"}";
 }
 
+// One tree's JSON object, preceded by a comma unless it is tree 0.
+void put_tree(std::string& o, const Tree& t, size_t i, int num_feature) {
+  auto f = [](std::string& s, float v) { json::append_float(s, v); };
+  auto n = [](std::string& s, i32 v) { json::append_int(s, v); };
+  if (i) o += ",";
+  o += "{\"base_weights\":";
+  put_array(o, t.base_weight, f);
+  o += ",\"categories\":[],\"categories_nodes\":[],\"categories_segments\":[],\"categories_sizes\":[]";
+  o += ",\"default_left\":";
+  put_array(o, t.default_left, [](std::string& s, u8 v) { s.push_back(v ? '1' : '0'); });
+  o += ",\"id\":";
+  json::append_int(o, long(i));
+  o += ",\"left_children\":";
+  put_array(o, t.left, n);
+  o += ",\"loss_changes\":";
+  put_array(o, t.loss_change, f);
+  o += ",\"parents\":";
+  put_array(o, t.parent, [](std::string& s, i32 v) { json::append_int(s, v < 0 ? 2147483647 : v); });
+  o += ",\"right_children\":";
+  put_array(o, t.right, n);
+  o += ",\"split_conditions\":";
+  put_array(o, t.cond, f);
+  o += ",\"split_indices\":";
+  put_array(o, t.feature, n);
+  o += ",\"split_type\":";
+  put_array(o, t.left, [](std::string& s, i32) { s.push_back('0'); });
+  o += ",\"sum_hessian\":";
+  put_array(o, t.sum_hess, f);
+  o += ",\"tree_param\":{\"num_deleted\":\"0\",\"num_feature\":\"" + istr(num_feature) + "\",\"num_nodes\":\"" +
+       istr(long(t.size())) + "\",\"size_leaf_vector\":\"1\"}}";
+}
+
 }  // namespace
 
 std::string model_to_json(const Model& m, const TrainParams& p) {
@@ -203,42 +240,41 @@ std::string model_to_json(const Model& m, const TrainParams& p) {
   o += "\"gradient_booster\":{\"model\":{\"gbtree_model_param\":{\"num_parallel_tree\":\"1\",\"num_trees\":\"" +
        istr(long(m.trees.size())) + "\"},";
   o += "\"iteration_indptr\":";
-  put_array(o, m.iteration_indptr, [](int v) { return istr(v); });
+  put_array(o, m.iteration_indptr, [](std::string& s, int v) { json::append_int(s, v); });
   o += ",\"tree_info\":[";
   for (size_t i = 0; i < m.trees.size(); ++i) {
     if (i) o += ",";
     o += istr(m.trees[i].klass);
   }
   o += "],\"trees\":[";
-  auto f = [](float v) { return json::format_float(v); };
-  auto n = [](i32 v) { return istr(v); };
-  for (size_t i = 0; i < m.trees.size(); ++i) {
-    const Tree& t = m.trees[i];
-    if (i) o += ",";
-    o += "{\"base_weights\":";
-    put_array(o, t.base_weight, f);
-    o += ",\"categories\":[],\"categories_nodes\":[],\"categories_segments\":[],\"categories_sizes\":[]";
-    o += ",\"default_left\":";
-    put_array(o, t.default_left, [](u8 v) { return std::string(v ? "1" : "0"); });
-    o += ",\"id\":" + istr(long(i));
-    o += ",\"left_children\":";
-    put_array(o, t.left, n);
-    o += ",\"loss_changes\":";
-    put_array(o, t.loss_change, f);
-    o += ",\"parents\":";
-    put_array(o, t.parent, [](i32 v) { return istr(v < 0 ? 2147483647 : v); });
-    o += ",\"right_children\":";
-    put_array(o, t.right, n);
-    o += ",\"split_conditions\":";
-    put_array(o, t.cond, f);
-    o += ",\"split_indices\":";
-    put_array(o, t.feature, n);
-    o += ",\"split_type\":";
-    put_array(o, t.left, [](i32) { return std::string("0"); });
-    o += ",\"sum_hessian\":";
-    put_array(o, t.sum_hess, f);
-    o += ",\"tree_param\":{\"num_deleted\":\"0\",\"num_feature\":\"" + istr(m.num_feature) + "\",\"num_nodes\":\"" +
-         istr(long(t.size())) + "\",\"size_leaf_vector\":\"1\"}}";
+  // Trees are formatted in parallel chunks and joined in order (the text is
+  // the same as one pass): a depth-10 model has ~2k nodes per tree and its
+  // serialisation is part of every saved model's latency.
+  const size_t T = m.trees.size();
+  const unsigned hw = std::max(1u, std::thread::hardware_concurrency());
+  const size_t parts = nodes >= 20000 ? std::min<size_t>({T, size_t(8), size_t(hw)}) : 1;
+  if (parts <= 1) {
+    for (size_t i = 0; i < T; ++i) put_tree(o, m.trees[i], i, m.num_feature);
+  } else {
+    std::vector<std::string> chunk(parts);
+    std::vector<std::exception_ptr> err(parts);
+    std::vector<std::thread> pool;
+    for (size_t q = 0; q < parts; ++q)
+      pool.emplace_back([&, q] {
+        try {
+          const size_t b = T * q / parts, e = T * (q + 1) / parts;
+          size_t n = 0;
+          for (size_t i = b; i < e; ++i) n += m.trees[i].size();
+          chunk[q].reserve(1024 + n * 96);
+          for (size_t i = b; i < e; ++i) put_tree(chunk[q], m.trees[i], i, m.num_feature);
+        } catch (...) {
+          err[q] = std::current_exception();
+        }
+      });
+    for (auto& th : pool) th.join();
+    for (auto& e : err)
+      if (e) std::rethrow_exception(e);
+    for (auto& c : chunk) o += c;
   }
   o += "]},\"name\":\"gbtree\"},";
   o += "\"learner_model_param\":" + learner_model_param(m, p) + ",";
