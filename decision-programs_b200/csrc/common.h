@@ -61,6 +61,11 @@ void set_last_error(const std::string& msg);
 inline void need(bool ok, const std::string& msg) {
   if (!ok) fail(msg);
 }
+// A literal message is turned into a string only when the check fails (the
+// parser and the model reader call this per array element).
+inline void need(bool ok, const char* msg) {
+  if (!ok) fail(msg);
+}
 
 inline void cuda_check(cudaError_t e, const char* what) {
   if (e != cudaSuccess) fail(std::string(what) + ": " + cudaGetErrorString(e));

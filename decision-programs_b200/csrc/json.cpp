@@ -25,7 +25,7 @@ std::int64_t Value::as_int() const {
   if (!s_.empty() && s_.find_first_of(".eE") == std::string::npos) {
     std::int64_t v = 0;
     auto r = std::from_chars(s_.data(), s_.data() + s_.size(), v);
-    need(r.ec == std::errc{} && r.ptr == s_.data() + s_.size(), "JSON integer out of range: " + printable(s_));
+    if (r.ec != std::errc{} || r.ptr != s_.data() + s_.size()) fail("JSON integer out of range: " + printable(s_));
     return v;
   }
   need(std::isfinite(d_) && d_ == std::floor(d_) && std::fabs(d_) < 9.0e15, "JSON number is not an integer");
@@ -36,7 +36,7 @@ std::uint64_t Value::as_uint() const {
   if (!s_.empty() && s_.find_first_of(".eE-") == std::string::npos) {
     std::uint64_t v = 0;
     auto r = std::from_chars(s_.data(), s_.data() + s_.size(), v);
-    need(r.ec == std::errc{} && r.ptr == s_.data() + s_.size(), "JSON integer out of range: " + printable(s_));
+    if (r.ec != std::errc{} || r.ptr != s_.data() + s_.size()) fail("JSON integer out of range: " + printable(s_));
     return v;
   }
   std::int64_t v = as_int();
@@ -68,7 +68,7 @@ const Value* Value::find(const std::string& key) const {
 }
 const Value& Value::at(const std::string& key) const {
   const Value* v = find(key);
-  need(v != nullptr, "missing JSON key: " + printable(key));
+  if (v == nullptr) fail("missing JSON key: " + printable(key));
   return *v;
 }
 size_t Value::size() const {
@@ -334,12 +334,21 @@ class Parser {
     while (i_ < t_.size() && ((t_[i_] >= '0' && t_[i_] <= '9') || t_[i_] == '.' || t_[i_] == 'e' ||
                               t_[i_] == 'E' || t_[i_] == '-' || t_[i_] == '+'))
       ++i_;
-    need(i_ > b, std::string("invalid JSON token near: ") + printable(t_.substr(b, 16)));
+    if (i_ <= b) fail("invalid JSON token near: " + printable(t_.substr(b, 16)));
     std::string text(t_.substr(b, i_ - b));
-    char* end = nullptr;
-    double d = strtod_c(text.c_str(), &end);
-    need(end == text.c_str() + text.size(), "invalid JSON number: " + printable(text));
-    return Value::number(d, text);
+    // from_chars reads the same syntax as strtod apart from a leading '+',
+    // and reports values beyond the double range instead of returning +-inf
+    // or 0: those (rare) tokens take strtod's reading, so both paths agree.
+    double d = 0.0;
+    const auto r = std::from_chars(text.data(), text.data() + text.size(), d);
+    if (text[0] == '+' || r.ec == std::errc::result_out_of_range) {
+      char* end = nullptr;
+      d = strtod_c(text.c_str(), &end);
+      if (end != text.c_str() + text.size()) fail("invalid JSON number: " + printable(text));
+    } else {
+      if (r.ec != std::errc{} || r.ptr != text.data() + text.size()) fail("invalid JSON number: " + printable(text));
+    }
+    return Value::number(d, std::move(text));
   }
 };
 }  // namespace
