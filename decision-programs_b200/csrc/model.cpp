@@ -15,6 +15,7 @@
 #include <cstdio>
 #include <exception>
 #include <string>
+#include <system_error>
 #include <thread>
 #include <vector>
 
@@ -258,19 +259,26 @@ std::string model_to_json(const Model& m, const TrainParams& p) {
   } else {
     std::vector<std::string> chunk(parts);
     std::vector<std::exception_ptr> err(parts);
+    auto format_chunk = [&](size_t q) {
+      try {
+        const size_t b = T * q / parts, e = T * (q + 1) / parts;
+        size_t n = 0;
+        for (size_t i = b; i < e; ++i) n += m.trees[i].size();
+        chunk[q].reserve(1024 + n * 96);
+        for (size_t i = b; i < e; ++i) put_tree(chunk[q], m.trees[i], i, m.num_feature);
+      } catch (...) {
+        err[q] = std::current_exception();
+      }
+    };
     std::vector<std::thread> pool;
-    for (size_t q = 0; q < parts; ++q)
-      pool.emplace_back([&, q] {
-        try {
-          const size_t b = T * q / parts, e = T * (q + 1) / parts;
-          size_t n = 0;
-          for (size_t i = b; i < e; ++i) n += m.trees[i].size();
-          chunk[q].reserve(1024 + n * 96);
-          for (size_t i = b; i < e; ++i) put_tree(chunk[q], m.trees[i], i, m.num_feature);
-        } catch (...) {
-          err[q] = std::current_exception();
-        }
-      });
+    pool.reserve(parts);  // so that only the thread start itself can throw below
+    size_t started = 0;
+    try {
+      for (; started < parts; ++started) pool.emplace_back(format_chunk, started);
+    } catch (const std::system_error&) {
+      // no more threads: the calling thread formats the chunks not started
+    }
+    for (size_t q = started; q < parts; ++q) format_chunk(q);
     for (auto& th : pool) th.join();
     for (auto& e : err)
       if (e) std::rethrow_exception(e);
