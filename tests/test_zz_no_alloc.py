@@ -2,7 +2,8 @@
 allocate device memory (a pre-reserved memory pool, or a path that must not
 call cudaMalloc/cudaFree).  Its result must equal dp_hist_build's, the
 allocating entry point, exactly (integer sums), on consecutive calls that
-reuse its fixed scratch array, and it must refuse work above its capacity.
+reuse its fixed scratch array, and both must equal the CPU oracle's sums;
+it must refuse work above its capacity.
 This file is collected last and depends on nothing the other tests set up."""
 import numpy as np
 import pytest
@@ -26,7 +27,8 @@ def make_case(seed, R, F, nbins, nseg):
     sg = float(np.ldexp(1.0, 17 - np.frexp(np.abs(gh[:, 0]).max())[1]))
     sh = float(np.ldexp(1.0, 18 - np.frexp(gh[:, 1].max())[1]))
     dev = {k: torch.from_numpy(v).cuda() for k, v in dict(bins=bins, gh=gh, ridx=ridx).items()}
-    return dict(stride=stride, F=F, nbins=nbins, sb=sb, se=se, sg=sg, sh=sh, dev=dev)
+    return dict(stride=stride, F=F, nbins=nbins, sb=sb, se=se, sg=sg, sh=sh, dev=dev,
+                host=dict(bins=bins, gh=gh, ridx=ridx))
 
 
 def run(dp, fn, c):
@@ -39,13 +41,18 @@ def run(dp, fn, c):
     return hist.cpu().numpy()
 
 
-def test_noalloc_histogram_equals_the_allocating_entry_point(dp):
+def test_noalloc_histogram_equals_the_allocating_entry_point(dp, orc):
     lib = dp.lib()
     a = make_case(1, 200_000, 64, 256, 3)
     b = make_case(2, 60_000, 20, 64, 6)
     want_a = run(dp, lib.dp_hist_build, a)
     want_b = run(dp, lib.dp_hist_build, b)
     assert want_a.any() and want_b.any()
+    # the reference sums, from the CPU oracle, for both entry points
+    for c, want in ((a, want_a), (b, want_b)):
+        h = c["host"]
+        np.testing.assert_array_equal(
+            want, orc.histograms(h["bins"], c["F"], h["gh"], h["ridx"], c["sb"], c["se"], c["sg"], c["sh"], threads=4))
     # two calls in a row on different shapes, then the first shape again: the
     # shared scratch must carry nothing over from the previous call
     np.testing.assert_array_equal(run(dp, lib.dp_hist_build_noalloc, a), want_a)
