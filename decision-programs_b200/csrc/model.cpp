@@ -11,6 +11,7 @@
 // configuration keys learner.generic_param.device and
 // learner.gradient_booster.updater[0].name (native/class_model_train.cu:48).
 #include <algorithm>
+#include <charconv>
 #include <cmath>
 #include <cstdio>
 #include <exception>
@@ -330,11 +331,21 @@ void model_from_json(const std::string& text, Model& m, TrainParams& p) {
   const auto& gb = learner.at("gradient_booster");
   need(gb.at("name").as_string() == "gbtree", "only gbtree models are supported");
   const auto& lmp = learner.at("learner_model_param");
+  // counts are decimal strings in XGBoost's files (plain numbers are read
+  // too); the whole string must be the integer
   auto dec = [](const json::Value& v) -> long long {
-    return v.is_string() ? std::stoll(v.as_string()) : v.as_int();
+    if (!v.is_string()) return v.as_int();
+    const std::string& t = v.as_string();
+    long long x = 0;
+    const auto r = std::from_chars(t.data(), t.data() + t.size(), x);
+    if (t.empty() || r.ec != std::errc{} || r.ptr != t.data() + t.size())
+      fail("invalid integer in learner_model_param: " + printable(t));
+    return x;
   };
   Model out;
-  out.num_feature = int(dec(lmp.at("num_feature")));
+  const long long num_feature = dec(lmp.at("num_feature"));
+  need(num_feature >= 0 && num_feature <= 0x7fffffffLL, "num_feature is outside its supported range");
+  out.num_feature = int(num_feature);
   TrainParams q = p;
   q.objective = learner.at("objective").at("name").as_string();
   (void)q.objective_id();
@@ -348,6 +359,8 @@ void model_from_json(const std::string& text, Model& m, TrainParams& p) {
       for (const auto& x : b.items()) q.base_score.push_back(float(x.as_double()));
     else
       q.base_score.push_back(float(b.as_double()));
+    need(q.base_score.size() <= 1 || q.base_score.size() == size_t(std::max(1, q.K())),
+         "base_score must have one value or one per class");
   }
   const auto& model = gb.at("model");
   const auto& trees = model.at("trees");

@@ -49,6 +49,10 @@ TREE0 = MODEL + ["trees", 0]
     (edit(TREE0 + ["left_children"], [5, -1, -1]), "tree child index out of range"),
     (edit(TREE0 + ["right_children"], [2, -1]), "tree node arrays differ in size"),
     (edit(MODEL + ["tree_info"], [0]), "tree_info size differs"),
+    (edit(["learner", "learner_model_param", "base_score"], "[0.5,0.5,0.5]"), "base_score must have one value"),
+    (edit(["learner", "learner_model_param", "num_feature"], "-1e+300"), "invalid integer"),
+    (edit(["learner", "learner_model_param", "num_feature"], "12abc"), "invalid integer"),
+    (edit(["learner", "learner_model_param", "num_feature"], "-2"), "num_feature is outside"),
 ])
 def test_malformed_models_are_refused_at_load(dp, doc, needle):
     lib = dp.lib()
@@ -102,7 +106,11 @@ def test_no_input_crashes_load_save_or_slice(dp):
         if rc == 0:
             loaded += 1
             n, p = C.c_uint64(), C.c_void_p()
-            assert lib.XGBoosterSaveModelToBuffer(h, b'{"format":"json"}', C.byref(n), C.byref(p)) in (0, -1)
+            # what loads, saves, and what the library saves, it loads again
+            assert lib.XGBoosterSaveModelToBuffer(h, b'{"format":"json"}', C.byref(n), C.byref(p)) == 0
+            h2, rc2, msg2 = load(lib, C.string_at(p, n.value))
+            lib.XGBoosterFree(h2)
+            assert rc2 == 0, msg2
             for begin, end, step in ((0, 1, 1), (0, 0, 1), (1, 0, 1), (0, 5, 2)):
                 s = C.c_void_p()
                 if lib.XGBoosterSlice(h, begin, end, step, C.byref(s)) == 0:
@@ -131,6 +139,7 @@ def test_unicode_escapes(dp, escaped, ok):
     m = _model()
     m["learner"]["objective"]["name"] = "reg:squarederror"
     m["learner"]["learner_model_param"]["num_class"] = "0"
+    m["learner"]["learner_model_param"]["base_score"] = "[0]"
     m["learner"]["gradient_booster"]["model"]["tree_info"] = [0, 0]
     text = json.dumps(m).replace('"reg:squarederror"', escaped).encode()
     h, rc, msg = load(lib, text)
@@ -327,6 +336,7 @@ def test_prediction_without_classes_is_refused_on_the_host(dp, source):
     else:
         m = _model()
         m["learner"]["learner_model_param"]["num_class"] = "0"
+        m["learner"]["learner_model_param"]["base_score"] = "[0]"
         model = m["learner"]["gradient_booster"]["model"]
         model["trees"], model["tree_info"], model["iteration_indptr"] = [], [], [0]
         h, rc, msg = load(lib, m)
