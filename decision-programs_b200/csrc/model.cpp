@@ -66,7 +66,8 @@ int TrainParams::objective_id() const {
 float TrainParams::base_margin(int k) const {
   const int oid = objective_id();
   double bs = oid == kLogistic ? 0.5 : 0.0;
-  if (!base_score.empty()) bs = base_score.size() == 1 ? base_score[0] : base_score.at(size_t(k));
+  need(base_score.size() <= 1 || size_t(k) < base_score.size(), "base_score must have one value or one per class");
+  if (!base_score.empty()) bs = base_score.size() == 1 ? base_score[0] : base_score[size_t(k)];
   if (oid == kLogistic) {
     need(bs > 0.0 && bs < 1.0, "base_score must be in (0,1) for logistic loss");
     return float(std::log(bs / (1.0 - bs)));
@@ -182,11 +183,13 @@ std::string objective_json(const TrainParams& p) {
 
 std::string base_score_string(const TrainParams& p) {
   const int K = p.K();
+  need(p.base_score.size() <= 1 || p.base_score.size() == size_t(std::max(1, K)),
+       "base_score must have one value or one per class");
   std::string s = "[";
   for (int k = 0; k < K; ++k) {
     if (k) s += ",";
     double bs = p.objective_id() == kLogistic ? 0.5 : 0.0;
-    if (!p.base_score.empty()) bs = p.base_score.size() == 1 ? p.base_score[0] : p.base_score.at(size_t(k));
+    if (!p.base_score.empty()) bs = p.base_score.size() == 1 ? p.base_score[0] : p.base_score[size_t(k)];
     s += json::format_float(float(bs));
   }
   return s + "]";

@@ -381,3 +381,20 @@ def test_kernel_level_entry_points_refuse_null_pointers(dp):
         assert call() == -1, name
         msg = lib.XGBGetLastError().decode("ascii")
         assert "null" in msg or "cover the features" in msg, (name, msg)
+
+
+def test_base_score_of_the_wrong_length_is_named(dp):
+    """base_score set as a vector must have one value per class; a mismatch
+    is reported as such when the model is saved (or trained or used)."""
+    lib = dp.lib()
+    h = C.c_void_p()
+    assert lib.XGBoosterCreate(None, 0, C.byref(h)) == 0
+    assert lib.XGBoosterSetParam(h, b"objective", b"reg:squarederror") == 0
+    assert lib.XGBoosterSetParam(h, b"base_score", b"[0.5, 0.2]") == 0
+    n, p = C.c_uint64(), C.c_void_p()
+    rc = lib.XGBoosterSaveModelToBuffer(h, b'{"format":"json"}', C.byref(n), C.byref(p))
+    msg = lib.XGBGetLastError().decode("ascii")
+    assert rc == -1 and "base_score must have one value or one per class" in msg, msg
+    assert lib.XGBoosterSetParam(h, b"base_score", b"[0.5]") == 0
+    assert lib.XGBoosterSaveModelToBuffer(h, b'{"format":"json"}', C.byref(n), C.byref(p)) == 0
+    lib.XGBoosterFree(h)
