@@ -398,3 +398,30 @@ def test_base_score_of_the_wrong_length_is_named(dp):
     assert lib.XGBoosterSetParam(h, b"base_score", b"[0.5]") == 0
     assert lib.XGBoosterSaveModelToBuffer(h, b'{"format":"json"}', C.byref(n), C.byref(p)) == 0
     lib.XGBoosterFree(h)
+
+
+def test_saved_models_reload_to_the_same_text(dp):
+    """For random objective, class and base_score settings: a model that
+    saves loads again, and saving it again gives the same text."""
+    lib = dp.lib()
+    rng = random.Random(5)
+    keys = ["objective", "num_class", "base_score", "max_depth", "eta", "seed"]
+    values = ["reg:squarederror", "binary:logistic", "multi:softprob", "multi:softmax", "0", "1", "2", "3", "0.5",
+              "[0.5]", "[0.2,0.3]", "[0.1,0.2,0.3]", "[]", "-1", "nan"]
+    saved = 0
+    for _ in range(2000):
+        h = C.c_void_p()
+        assert lib.XGBoosterCreate(None, 0, C.byref(h)) == 0
+        for _ in range(rng.randint(1, 6)):
+            lib.XGBoosterSetParam(h, rng.choice(keys).encode(), rng.choice(values).encode())
+        n, p = C.c_uint64(), C.c_void_p()
+        if lib.XGBoosterSaveModelToBuffer(h, b'{"format":"json"}', C.byref(n), C.byref(p)) == 0:
+            text = C.string_at(p, n.value)
+            h2, rc, msg = load(lib, text)
+            assert rc == 0, msg
+            assert lib.XGBoosterSaveModelToBuffer(h2, b'{"format":"json"}', C.byref(n), C.byref(p)) == 0
+            assert C.string_at(p, n.value) == text
+            lib.XGBoosterFree(h2)
+            saved += 1
+        lib.XGBoosterFree(h)
+    assert saved > 1000
