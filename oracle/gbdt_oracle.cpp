@@ -133,12 +133,42 @@ struct Cuts {
   std::vector<uint8_t> has_missing;
 };
 
+// Ascending order of non-NaN floats with -0.0 already folded into +0.0: an
+// LSD radix sort over the order-preserving 32-bit key (sign bit set for
+// positives, all bits flipped for negatives) in four 8-bit passes.  Equal
+// values have equal keys, so the result is the array std::sort gives; short
+// columns use std::sort itself.
+static void sort_floats(std::vector<float>& v) {
+  const size_t n = v.size();
+  if (n < 4096) {
+    std::sort(v.begin(), v.end());
+    return;
+  }
+  std::vector<uint32_t> a(n), b(n);
+  for (size_t i = 0; i < n; ++i) {
+    uint32_t u;
+    std::memcpy(&u, &v[i], 4);
+    a[i] = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  }
+  for (int shift = 0; shift < 32; shift += 8) {
+    size_t start[257] = {0};
+    for (size_t i = 0; i < n; ++i) ++start[((a[i] >> shift) & 255u) + 1];
+    for (int d = 0; d < 256; ++d) start[d + 1] += start[d];
+    for (size_t i = 0; i < n; ++i) b[start[(a[i] >> shift) & 255u]++] = a[i];
+    a.swap(b);
+  }
+  for (size_t i = 0; i < n; ++i) {
+    const uint32_t u = (a[i] & 0x80000000u) ? (a[i] & 0x7fffffffu) : ~a[i];
+    std::memcpy(&v[i], &u, 4);
+  }
+}
+
 // Boundaries of one column from its sorted non-missing values.
 static void column_cuts(std::vector<float>& v, int max_bin, bool has_missing, float* cut, uint16_t* nbins) {
   const int64_t n = int64_t(v.size());
   const int B = std::min(max_bin, has_missing ? 255 : 256);
   if (n == 0) { *nbins = 1; return; }
-  std::sort(v.begin(), v.end());
+  sort_floats(v);
   int64_t distinct = 1;
   for (int64_t i = 1; i < n && distinct <= B; ++i) distinct += v[i] != v[i - 1];
   int nb = 0;
